@@ -1,0 +1,267 @@
+"""Generate the golden fixtures under tests/golden/ by running the REFERENCE
+prismaquant implementation (imported read-only from a local checkout) on
+seeded inputs.
+
+    PYTHONPATH=oracle/_shim:/root/reference python tests/golden/make_golden.py
+
+Outputs:
+  small_cases.npz     inputs (bf16 bit patterns) and the reference's outputs
+                      for every hot-path function on small edge-case tensors
+  full_digests.json   SHA-256 digests of the reference's outputs on the
+                      single-Linear sweep (4096x4096 with 0.1 % x20 outliers,
+                      seed 0) and on the fused-sibling q/k/v + gate/up group
+                      (seeds 1..5), plus their MSE_W values
+
+Only this script touches the reference; the committed fixtures travel, the
+reference does not.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+
+from oracle import pq_oracle as O  # noqa: E402
+
+from prismaquant import format_registry as fr  # noqa: E402
+from prismaquant import measure_quant_cost as mqc  # noqa: E402
+from prismaquant import export_native_compressed as enc  # noqa: E402
+from prismaquant import sensitivity_probe as sp  # noqa: E402
+
+torch.set_num_threads(os.cpu_count() or 1)
+
+COST_FMTS = ["NVFP4", "MXFP8", "FP8_E4M3", "BF16"]
+
+
+def to_t(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+
+
+def bits_of(t):
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def u8_of(t):
+    return t.contiguous().view(torch.uint8).numpy().copy()
+
+
+def bf16_bits_from_f32(vals):
+    return O.f32_to_bf16_bits(np.asarray(vals, dtype=np.float32))
+
+
+def tie_case():
+    """Rows whose scaled values land exactly on codebook midpoints.
+
+    Row r: first element fixes amax so that scale is an exact power of two
+    for NVFP4 (amax = 6 * 2^-4 -> s = 2^-4) and for FP8-per-channel the row
+    amax = 448 * 2^-8; the rest are +-midpoints in that grid.
+    """
+    s = 2.0 ** -4
+    e2m1_mid = [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0]
+    rows = []
+    for sign in (1.0, -1.0):
+        row = [6.0 * s] + [sign * m * s for m in e2m1_mid] + [-0.0, 0.0] + [sign * 0.1 * s] * 6
+        rows.append(row[:16] + row[:16])
+    # e4m3 midpoints for MX / FP8 channel: grid at scale 1 (amax 448)
+    mids = [448.0, 9.0, 17.0, 0.5 + 1 / 32, 2 ** -7 + 2 ** -10, 2 ** -10, 3 * 2 ** -10,
+            -9.0, -17.0, -(2 ** -10), -(3 * 2 ** -10), 104.0, -104.0, 232.0, 464.0, -0.0]
+    rows.append(mids + [-m for m in mids])
+    rows.append([v * 2.0 ** -20 for v in mids + mids])
+    return bf16_bits_from_f32(np.array(rows, dtype=np.float32))
+
+
+def small_cases():
+    cases = {}
+    cases["rand_64x128"] = O.synthetic_weight_bits((64, 128), seed=11, outlier_frac=0.01)
+    cases["rand_33x256"] = O.synthetic_weight_bits((33, 256), seed=12, std=1.0, outlier_frac=0.003)
+    cases["ties_4x32"] = tie_case()
+    z = np.zeros((3, 64), dtype=np.float32)
+    z[1, :16] = -0.0
+    z[2, 5] = 1e-30
+    z[2, 40] = -3e-39        # bf16 subnormal
+    cases["zeros_3x64"] = bf16_bits_from_f32(z)
+    wide = np.random.default_rng(5).standard_normal((8, 96)).astype(np.float32)
+    wide *= np.float32(10.0) ** np.random.default_rng(6).integers(-30, 30, (8, 1)).astype(np.float32)
+    cases["wide_range_8x96"] = bf16_bits_from_f32(wide)
+    cases["row1_1x4096"] = O.synthetic_weight_bits((1, 4096), seed=13)
+    cases["cols16_5x16"] = O.synthetic_weight_bits((5, 16), seed=14)
+    cases["cols48_7x48"] = O.synthetic_weight_bits((7, 48), seed=15)    # MXFP8 cannot group 48
+    cases["cols8_4x8"] = O.synthetic_weight_bits((4, 8), seed=16)        # whole-row groups
+    cases["packed_4x32x64"] = O.synthetic_weight_bits((4, 32, 64), seed=17, std=0.05)
+    cases["packed_3x16x96"] = O.synthetic_weight_bits((3, 16, 96), seed=18, outlier_frac=0.01)
+    return cases
+
+
+def run_cost(bits):
+    out = {}
+    W = to_t(bits)
+    for fmt in COST_FMTS:
+        spec = fr.get_format(fmt)
+        try:
+            if W.dim() == 3:
+                What = mqc._batched_quantize(spec, W)
+            else:
+                What = spec.quantize_dequantize(W.clone())
+            err = (W - What).float()
+            out[f"cost/{fmt}/qdq"] = bits_of(What)
+            out[f"cost/{fmt}/mse"] = np.array([float(err.pow(2).mean().item())], dtype=np.float64)
+        except Exception as e:  # the reference records {"error": str(e)}
+            out[f"cost/{fmt}/error"] = np.array([str(e)])
+    return out
+
+
+def run_export(bits):
+    out = {}
+    W = to_t(bits).float()
+    if W.dim() == 2:
+        rows, cols = W.shape
+        if cols % 16 == 0:
+            wp, ws, wg = enc.quantize_dequantize_nvfp4(W)
+            out["nvfp4/packed"], out["nvfp4/scale"], out["nvfp4/global"] = u8_of(wp), u8_of(ws), wg.numpy()
+            gr = enc.compute_nvfp4_global_real(W)
+            out["nvfp4/global_real"] = np.array([gr.item()], dtype=np.float32)
+            ov = torch.tensor(float(gr.item()) * 3.0)
+            wp, ws, wg = enc.quantize_dequantize_nvfp4(W, global_real_override=ov)
+            out["nvfp4_ovr/override"] = np.array([ov.item()], dtype=np.float32)
+            out["nvfp4_ovr/packed"], out["nvfp4_ovr/scale"], out["nvfp4_ovr/global"] = u8_of(wp), u8_of(ws), wg.numpy()
+            q = enc._quantize_2d(W, "NVFP4")
+            out["q2d_nvfp4/input_global_scale"] = q["input_global_scale"].numpy()
+        if cols % 32 == 0:
+            w8, s8 = enc.quantize_dequantize_mxfp8(W)
+            out["mxfp8/weight"], out["mxfp8/scale"] = u8_of(w8), u8_of(s8)
+        wf, sf = enc.quantize_dequantize_fp8_dynamic(W)
+        out["fp8dyn/weight"], out["fp8dyn/scale"] = u8_of(wf), sf.numpy()
+    else:
+        E, M, N = W.shape
+        if N % 16 == 0:
+            wp, ws, wg = enc.quantize_dequantize_nvfp4_packed(W)
+            out["nvfp4p/packed"], out["nvfp4p/scale"], out["nvfp4p/global"] = u8_of(wp), u8_of(ws), wg.numpy()
+        if N % 32 == 0:
+            w8, s8 = enc.quantize_dequantize_mxfp8_packed(W)
+            out["mxfp8p/weight"], out["mxfp8p/scale"] = u8_of(w8), u8_of(s8)
+            g = enc._quantize_2d_group_same_shape(W, "MXFP8")
+            out["grouped_mxfp8/weight"], out["grouped_mxfp8/scale"] = u8_of(g["weight"]), u8_of(g["weight_scale"])
+        wf, sf = enc.quantize_dequantize_fp8_dynamic_packed(W)
+        out["fp8dynp/weight"], out["fp8dynp/scale"] = u8_of(wf), sf.numpy()
+    return out
+
+
+def run_fisher(bits):
+    """_GradNormCapture.backward on the tensor used as a packed-expert gradient."""
+    out = {}
+    g = to_t(bits)
+    if g.dim() == 3:
+        acc, ch = {}, {}
+        w = torch.zeros(g.shape, dtype=torch.bfloat16, requires_grad=True)
+        y = sp._GradNormCapture.apply(w, "p", acc, ch, None)
+        y.backward(g)
+        out["gradnorm/scalar"] = np.array([acc["p"]], dtype=np.float64)
+        out["gradnorm/channel"] = ch["p"].numpy()
+    return out
+
+
+def fisher_bridge():
+    """FisherAccumulator on a toy Linear with ONE token per backward: the
+    reference's ||gy^T x||^2 equals the per-token product of squared norms."""
+    torch.manual_seed(3)
+    model = torch.nn.Sequential(torch.nn.Linear(64, 48, bias=False), torch.nn.Linear(48, 32, bias=False))
+    model = model.to(torch.float32)
+    tracked = ["0", "1"]
+    acc = sp.FisherAccumulator(model, tracked, {}, hook_packed_experts=False)
+    xs, gys = {n: [] for n in tracked}, {n: [] for n in tracked}
+    mods = dict(model.named_modules())
+    hooks = []
+    for n in tracked:
+        hooks.append(mods[n].register_forward_hook(lambda m, i, o, n=n: xs[n].append(i[0].detach().clone())))
+        hooks.append(mods[n].register_full_backward_hook(lambda m, gi, go, n=n: gys[n].append(go[0].detach().clone())))
+    inputs = torch.randn(5, 1, 64)
+    for i in range(inputs.shape[0]):
+        y = model(inputs[i])
+        y.pow(2).sum().backward()
+    acc.finalize(None)
+    for h in hooks:
+        h.remove()
+    out = {}
+    for n in tracked:
+        out[f"bridge/{n}/x"] = torch.cat(xs[n]).numpy()
+        out[f"bridge/{n}/gy"] = torch.cat(gys[n]).numpy()
+        out[f"bridge/{n}/h_trace_raw"] = np.array([acc.stats[n]["h_trace_raw"]], dtype=np.float64)
+        out[f"bridge/{n}/n_tokens_seen"] = np.array([acc.stats[n]["n_tokens_seen"]], dtype=np.int64)
+    return out
+
+
+def known_answers():
+    out = {}
+    v = torch.tensor([0.25, 0.75, -0.75, 1.25, -1.25, 2.5, -2.5, 5.0, -5.0, -0.0, -0.1, 0.0, 0.5, 1.0, 6.0, -6.0, 7.0, -7.0])
+    out["ka/round_to_codebook/in"] = v.numpy()
+    out["ka/round_to_codebook/out"] = enc._round_to_codebook(v).numpy()
+    # cost-path signed-codebook RTN on a row whose amax is 6 (scale exactly 1)
+    c = torch.tensor([[0.25, 0.75, -0.75, 1.25, -1.25, 2.5, -2.5, 5.0, -5.0, -0.0, -0.1, 6.0]])
+    out["ka/cost_e2m1/in"] = c.numpy()
+    out["ka/cost_e2m1/out"] = fr._rtn_fp_codebook(c, fr._CODEBOOKS["fp4_e2m1"], 0).numpy()
+    idx = torch.tensor([[1, 2, 3, 4]])
+    out["ka/pack/out"] = enc.pack_fp4_indices(idx, 4).numpy()
+    return out
+
+
+def main():
+    arrays = {}
+    for name, bits in small_cases().items():
+        arrays[f"{name}/input"] = bits
+        for k, v in {**run_cost(bits), **run_export(bits), **run_fisher(bits)}.items():
+            arrays[f"{name}/{k}"] = v
+    arrays.update(fisher_bridge())
+    arrays.update(known_answers())
+    np.savez_compressed(HERE / "small_cases.npz", **arrays)
+
+    digests = {}
+    # single-Linear sweep: 4096x4096, N(0, 0.02^2), 0.1 % x20 outliers, seed 0
+    w0 = O.synthetic_weight_bits((4096, 4096), seed=0, outlier_frac=0.001)
+    digests["linear4096"] = full_case(w0)
+    # fused siblings: q/k/v share one NVFP4 global, gate/up share one
+    sib_shapes = {"q_proj": (4096, 4096), "k_proj": (1024, 4096), "v_proj": (1024, 4096),
+                  "gate_proj": (14336, 4096), "up_proj": (14336, 4096)}
+    sib = {n: O.synthetic_weight_bits(s, seed=i + 1) for i, (n, s) in enumerate(sib_shapes.items())}
+    groups = {"qkv": ["q_proj", "k_proj", "v_proj"], "gate_up": ["gate_proj", "up_proj"]}
+    dg = {}
+    for gname, members in groups.items():
+        joint = torch.stack([enc.compute_nvfp4_global_real(to_t(sib[m]).float()) for m in members]).max()
+        for m in members:
+            d = full_case(sib[m], joint=joint)
+            d["joint_global_real"] = float(joint.item())
+            d["seed"] = list(sib_shapes).index(m) + 1
+            dg[m] = d
+    digests["siblings"] = dg
+    with open(HERE / "full_digests.json", "w") as f:
+        json.dump(digests, f, indent=1, sort_keys=True)
+    print("wrote", HERE / "small_cases.npz", HERE / "full_digests.json")
+
+
+def full_case(bits, joint=None):
+    W = to_t(bits)
+    d = {"input": O.digest(bits), "shape": list(bits.shape)}
+    for fmt in COST_FMTS:
+        What = fr.get_format(fmt).quantize_dequantize(W.clone())
+        d[f"mse/{fmt}"] = float((W - What).float().pow(2).mean().item())
+        d[f"qdq/{fmt}"] = O.digest(bits_of(What))
+    Wf = W.float()
+    wp, ws, wg = enc.quantize_dequantize_nvfp4(Wf, global_real_override=joint)
+    d["nvfp4"] = O.digest(u8_of(wp), u8_of(ws), wg.numpy())
+    d["nvfp4_global_div"] = float(wg.item())
+    w8, s8 = enc.quantize_dequantize_mxfp8(Wf)
+    d["mxfp8"] = O.digest(u8_of(w8), u8_of(s8))
+    wf, sf = enc.quantize_dequantize_fp8_dynamic(Wf)
+    d["fp8dyn"] = O.digest(u8_of(wf), sf.numpy())
+    return d
+
+
+if __name__ == "__main__":
+    main()
