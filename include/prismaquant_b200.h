@@ -1,0 +1,171 @@
+/*
+ * prismaquant_b200 — C ABI of the B200 (sm_100a) quantization-cost kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream and returns a
+ * pq_status.  Nothing here allocates or frees device memory: the caller owns
+ * every input, output and scratch buffer.  bf16 tensors are passed as
+ * uint16_t bit patterns, fp8 (float8_e4m3fn) and E8M0 as uint8_t.
+ *
+ * Paths in the comments are relative to the prismaquant project.
+ */
+#ifndef PRISMAQUANT_B200_H
+#define PRISMAQUANT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  PQ_OK = 0,
+  PQ_ERR_NULL = 1,      /* a required pointer is NULL */
+  PQ_ERR_SHAPE = 2,     /* e.g. "NVFP4 group_size=16 ∤ cols" (export_native_compressed.py:1083-1084) */
+  PQ_ERR_ALIGN = 3,     /* a pointer is not 16-byte aligned */
+  PQ_ERR_FORMAT = 4,    /* unknown format id / empty format mask */
+  PQ_ERR_CUDA = 5,      /* a CUDA launch failed (pq_last_cuda_error() has the code) */
+  PQ_ERR_LIMIT = 6,     /* a size is beyond a stated maximum */
+  PQ_ERR_DEVICE = 7     /* a kernel's bounded wait gave up (pq_device_error()) */
+} pq_status;
+
+/* Cost-path formats (prismaquant/format_registry.py:368-376, 418-426, 457-465, 536-546). */
+typedef enum {
+  PQ_FMT_NVFP4 = 0,       /* E2M1 codebook, groups of 16, real-valued amax/6 scale */
+  PQ_FMT_MXFP8 = 1,       /* E4M3 codebook, groups of 32, E8M0 scale = 2^round(log2(amax/448)) */
+  PQ_FMT_FP8_CHANNEL = 2, /* E4M3 codebook, one amax/448 scale per row (FP8_E4M3, group_size=0) */
+  PQ_FMT_BF16 = 3,        /* passthrough: error 0 */
+  PQ_NUM_FMTS = 4
+} pq_format;
+
+#define PQ_FMT_BIT(f) (1u << (f))
+
+/* One bf16 tensor on a sweep work list: [rows, cols] row-major, contiguous.
+ * A packed-experts tensor [E, M, N] is passed as rows = E*M, cols = N.
+ * fmt_mask selects formats for THIS tensor (a format whose grouping the
+ * shape cannot take is left out by the caller and reported as an error
+ * entry, as the reference's per-format try/except does,
+ * measure_quant_cost.py:320-321, 443-444, 673-675). */
+typedef struct pq_sweep_tensor {
+  const uint16_t* w;
+  int64_t rows;
+  int64_t cols;
+  uint32_t fmt_mask;
+  uint32_t _pad;
+  /* Optional fused NVFP4 export outputs (all three or none; needs cols % 16 == 0):
+   * codes [rows, cols/2] (export_native_compressed.py:1096-1097),
+   * group amax scratch [rows, cols/16] as bf16, and the tensor's running max
+   * group amax as float bits (zero it before the first launch). */
+  uint8_t* nvfp4_codes;
+  uint16_t* nvfp4_amax;
+  uint32_t* nvfp4_tmax;
+} pq_sweep_tensor;
+
+/*
+ * Multi-format weight-error sweep.  For each tensor i and format f in its
+ * mask, ADDS sum((W - qdq_f(W))^2) to sse[4*i + f] (fp64, device; zero it
+ * first).  Replaces the per-format chain `_batched_quantize` ->
+ * `err = (W - W_hat).float()` -> `err.pow(2).mean()`
+ * (measure_quant_cost.py:532-548, 627-632; 411-414 for packed experts) with
+ * one read of W for all formats.  weight_mse = sse / (rows*cols).
+ * The reference rounds W_hat and W - W_hat to bf16 and squares in fp32;
+ * so does this (an fp32 square above FLT_MAX is inf).
+ * `tensors` is a HOST array; it is copied into the launch parameters.
+ */
+int pq_sweep_sse(const pq_sweep_tensor* tensors, int n_tensors, double* sse, void* stream);
+
+/*
+ * Cost-path quantize->dequantize of one format: w_hat = qdq_f(w) as bf16,
+ * same shape.  Replaces FormatSpec.quantize_dequantize for NVFP4 / MXFP8 /
+ * FP8_E4M3 / BF16 (format_registry.py:47-48, 194-233) and
+ * `_batched_quantize` (measure_quant_cost.py:532-548).
+ */
+int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t* w_hat, void* stream);
+
+/*
+ * NVFP4 export, pass 1: E2M1 codes (abs-codebook RTN, ties toward zero,
+ * sign from signbit; export_native_compressed.py:118-136, 226-233), the bf16
+ * amax of every 16-group, and the max group amax of each of `batch`
+ * consecutive [rows, cols] slices (atomic max into tmax[b], float bits;
+ * zero tmax first).  Codes do not depend on the global scale
+ * (export_native_compressed.py:1093-1096).
+ */
+int pq_nvfp4_codes(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols,
+                   uint8_t* codes, uint16_t* amax, uint32_t* tmax, void* stream);
+
+/*
+ * NVFP4 export, pass 2: FP8 E4M3 block scales and the on-disk global
+ * divisor for `batch` slices.  Slice b's global_real is
+ *   override[b]                      if override != NULL (clamped at 1e-12),
+ *   else max over slices c with group_of[c] == group_of[b] of
+ *        (max_c(amax)/6)/448 clamped at 1e-12      (joint fused-sibling global,
+ *        export_native_compressed.py:2090-2098; group_of == NULL: own slice)
+ * scale = e4m3((amax/6 / global_real).clamp(0, 448)), global_div[b] = 1/global_real
+ * (export_native_compressed.py:1045-1055, 1085-1102, 1105-1129).
+ * `slices` lists `n` (amax, tmax, scale, rows*cols/16) tuples as flat arrays.
+ */
+int pq_nvfp4_scales(int n, const uint16_t* const* amax, const int64_t* n_groups,
+                    const uint32_t* tmax_dev, const int32_t* group_of,
+                    const float* override_dev, uint8_t* const* scales,
+                    float* global_div_dev, void* stream);
+
+/* One-call NVFP4 export of a [batch, rows, cols] tensor with a per-slice
+ * global (batch == 1: quantize_dequantize_nvfp4; batch == E:
+ * quantize_dequantize_nvfp4_packed, export_native_compressed.py:1058-1129).
+ * override_dev may be NULL or hold `batch` floats.  scratch_amax holds
+ * batch*rows*cols/16 bf16, scratch_tmax `batch` uint32 (zeroed here). */
+int pq_nvfp4_pack(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols,
+                  const float* override_dev, uint8_t* codes, uint8_t* scales,
+                  float* global_div, uint16_t* scratch_amax, uint32_t* scratch_tmax,
+                  void* stream);
+
+/*
+ * MXFP8 export (quantize_dequantize_mxfp8[_packed], export_native_compressed.py:1135-1194):
+ * E8M0 exponent e = clamp(ceil(log2(max(amax32, 2^-127)/448)), -127, 127)
+ * (torch float32 log2 semantics), q = e4m3((w / 2^e).clamp(+-448)),
+ * scale byte = e + 127.  n_rows*cols elements, cols % 32 == 0.
+ */
+int pq_mxfp8_pack(const uint16_t* w, int64_t n_rows, int64_t cols, uint8_t* q, uint8_t* scale_e8m0,
+                  void* stream);
+
+/*
+ * FP8 per-channel export (quantize_dequantize_fp8_dynamic[_packed],
+ * export_native_compressed.py:1197-1226): s = max(row amax, 2^-127)/448,
+ * q = e4m3((w / s).clamp(+-448)); scale [n_rows] fp32.
+ */
+int pq_fp8_channel_pack(const uint16_t* w, int64_t n_rows, int64_t cols, uint8_t* q, float* scale,
+                        void* stream);
+
+/*
+ * Fisher statistics.
+ *
+ * pq_sumsq_rows: _GradNormCapture.backward (sensitivity_probe.py:451-482):
+ * total += sum(g^2) (fp64, device scalar) and, if per_row != NULL,
+ * per_row[r] += sum_n g[r, n]^2 (fp32; the [E, M] channel diagonal).
+ */
+int pq_sumsq_rows(const uint16_t* g, int64_t n_rows, int64_t cols, double* total, float* per_row,
+                  void* stream);
+
+/* pq_rownorm2: out[t] = sum_d x[t, d]^2 (fp32) for x [T, d] bf16 — the
+ * forward half of the per-token estimator that replaces the
+ * GEMM-then-square in FisherAccumulator._make_bwd (sensitivity_probe.py:1115-1152). */
+int pq_rownorm2(const uint16_t* x, int64_t T, int64_t d, float* out, void* stream);
+
+/* pq_tokennorm_dot: acc[0] += sum_t xnorm[idx(t)] * sum_d g[t, d]^2 (fp64),
+ * idx(t) = token_idx ? token_idx[t] : t.  With token_idx it serves the
+ * routed (per-expert) estimator for packed experts; acc[1] += T (tokens). */
+int pq_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm,
+                     const int64_t* token_idx, double* acc, void* stream);
+
+/* Housekeeping. */
+int pq_device_error(int* code);          /* reads and clears the device error word */
+int pq_last_cuda_error(void);
+const char* pq_status_string(int status);
+int pq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PRISMAQUANT_B200_H */

@@ -1,0 +1,288 @@
+"""ctypes binding of libprismaquant_b200.so (the C ABI in include/prismaquant_b200.h).
+
+Every function here takes CUDA torch tensors, checks dtype / device /
+contiguity, hands raw pointers plus the current CUDA stream to the library
+and returns torch tensors the caller owns.  There is no CPU path: if the
+shared library is missing or a tensor is not on a CUDA device, the call
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_NAME = "libprismaquant_b200.so"
+LIB_PATH = Path(os.environ.get("PQ_B200_LIB", Path(__file__).resolve().parent / LIB_NAME))
+
+PQ_OK, PQ_ERR_NULL, PQ_ERR_SHAPE, PQ_ERR_ALIGN, PQ_ERR_FORMAT, PQ_ERR_CUDA, PQ_ERR_LIMIT, PQ_ERR_DEVICE = range(8)
+FMT_NVFP4, FMT_MXFP8, FMT_FP8_CHANNEL, FMT_BF16 = range(4)
+FMT_IDS = {"NVFP4": FMT_NVFP4, "MXFP8": FMT_MXFP8, "FP8_E4M3": FMT_FP8_CHANNEL, "BF16": FMT_BF16}
+
+EXPORTED = [
+    "pq_sweep_sse", "pq_cost_qdq", "pq_nvfp4_codes", "pq_nvfp4_scales", "pq_nvfp4_pack",
+    "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
+    "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version",
+]
+
+
+class SweepTensor(ctypes.Structure):
+    """Mirror of pq_sweep_tensor."""
+    _fields_ = [
+        ("w", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("fmt_mask", ctypes.c_uint32),
+        ("_pad", ctypes.c_uint32),
+        ("nvfp4_codes", ctypes.c_void_p),
+        ("nvfp4_amax", ctypes.c_void_p),
+        ("nvfp4_tmax", ctypes.c_void_p),
+    ]
+
+
+_LIB = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the shared library (once).  Raises if it has not been built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m prismaquant_b200.build` "
+            "(the B200 kernels have no CPU fallback)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    P, I64, I, V = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+    sig = {
+        "pq_sweep_sse": [ctypes.POINTER(SweepTensor), I, P, V],
+        "pq_cost_qdq": [P, I64, I64, I, P, V],
+        "pq_nvfp4_codes": [P, I64, I64, I64, P, P, P, V],
+        "pq_nvfp4_scales": [I, ctypes.POINTER(P), ctypes.POINTER(I64), P, ctypes.POINTER(ctypes.c_int32), P,
+                            ctypes.POINTER(P), P, V],
+        "pq_nvfp4_pack": [P, I64, I64, I64, P, P, P, P, P, P, V],
+        "pq_mxfp8_pack": [P, I64, I64, P, P, V],
+        "pq_fp8_channel_pack": [P, I64, I64, P, P, V],
+        "pq_sumsq_rows": [P, I64, I64, P, P, V],
+        "pq_rownorm2": [P, I64, I64, P, V],
+        "pq_tokennorm_dot": [P, I64, I64, P, P, P, V],
+        "pq_device_error": [ctypes.POINTER(ctypes.c_int)],
+        "pq_last_cuda_error": [],
+        "pq_status_string": [I],
+        "pq_version": [],
+    }
+    for name, args in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_char_p if name == "pq_status_string" else ctypes.c_int
+    _LIB = lib
+    return lib
+
+
+def _check(status: int, what: str, shape_msg: str | None = None):
+    if status == PQ_OK:
+        return
+    lib = load()
+    msg = lib.pq_status_string(status).decode()
+    if status == PQ_ERR_SHAPE:
+        raise ValueError(shape_msg or f"{what}: {msg}")
+    if status == PQ_ERR_CUDA:
+        raise RuntimeError(f"{what}: {msg} (cudaError {lib.pq_last_cuda_error()})")
+    raise RuntimeError(f"{what}: {msg}")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def as_bf16_cuda(w: torch.Tensor, what: str) -> torch.Tensor:
+    """Return a contiguous CUDA bf16 view of `w`.
+
+    float32 inputs are accepted when every value is a bf16 value (the
+    reference's export path feeds `weight.float()` of bf16 weights); other
+    float32 tensors are rejected rather than rounded silently.
+    """
+    if not w.is_cuda:
+        raise RuntimeError(f"{what}: tensor is on {w.device}; the B200 kernels need a CUDA tensor")
+    if w.dtype == torch.bfloat16:
+        return w.contiguous()
+    if w.dtype == torch.float32:
+        b = w.to(torch.bfloat16)
+        if not torch.equal(b.float(), w):
+            raise NotImplementedError(
+                f"{what}: float32 input with values that are not bf16-representable is not supported")
+        return b.contiguous()
+    raise TypeError(f"{what}: unsupported dtype {w.dtype}")
+
+
+def device_error() -> int:
+    code = ctypes.c_int(0)
+    _check(load().pq_device_error(ctypes.byref(code)), "pq_device_error")
+    return code.value
+
+
+# ---------------------------------------------------------------------------
+# Cost path
+# ---------------------------------------------------------------------------
+
+def sweep_sse(weights, masks, nvfp4_outputs=None, sse: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused multi-format error sweep.  `weights` are 2-D (or 3-D packed)
+    bf16 CUDA tensors, `masks` one format bitmask each.  Returns (or adds
+    into) a [n, 4] float64 tensor of sum((W - qdq_f(W))^2).
+
+    `nvfp4_outputs`, if given, is a list (per tensor, or None) of
+    (codes u8 [rows, cols/2], amax bf16-scratch [rows, cols/16], tmax u32 [1])
+    filled in the same pass."""
+    lib = load()
+    n = len(weights)
+    if n == 0:
+        return torch.zeros(0, 4, dtype=torch.float64)
+    dev = weights[0].device
+    if sse is None:
+        sse = torch.zeros(n, 4, dtype=torch.float64, device=dev)
+    arr = (SweepTensor * n)()
+    keep = []
+    for i, (w, m) in enumerate(zip(weights, masks)):
+        if w.device != dev:
+            raise RuntimeError("sweep_sse: all tensors must be on one device")
+        if w.dtype != torch.bfloat16 or not w.is_contiguous():
+            raise TypeError("sweep_sse: weights must be contiguous bf16")
+        keep.append(w)
+        cols = w.shape[-1] if w.dim() else 1
+        rows = w.numel() // cols if cols else 0
+        arr[i].w = w.data_ptr()
+        arr[i].rows = rows
+        arr[i].cols = cols
+        arr[i].fmt_mask = int(m)
+        if nvfp4_outputs is not None and nvfp4_outputs[i] is not None:
+            codes, amax, tmax = nvfp4_outputs[i]
+            arr[i].nvfp4_codes = codes.data_ptr()
+            arr[i].nvfp4_amax = amax.data_ptr()
+            arr[i].nvfp4_tmax = tmax.data_ptr()
+    _check(lib.pq_sweep_sse(arr, n, _ptr(sse), _stream(sse)), "pq_sweep_sse")
+    return sse
+
+
+def cost_qdq(w: torch.Tensor, fmt: str) -> torch.Tensor:
+    """Cost-path quantize->dequantize (bf16 in, bf16 out, same shape)."""
+    lib = load()
+    wb = as_bf16_cuda(w, "quantize_dequantize")
+    out = torch.empty_like(wb)
+    if wb.numel() == 0:
+        return out.to(w.dtype)
+    cols = wb.shape[-1]
+    rows = wb.numel() // cols
+    fid = FMT_IDS[fmt]
+    _check(lib.pq_cost_qdq(_ptr(wb), rows, cols, fid, _ptr(out), _stream(wb)), "pq_cost_qdq",
+           f"cannot reshape rows of {cols} into groups for {fmt}")
+    return out if w.dtype == torch.bfloat16 else out.to(w.dtype)
+
+
+# ---------------------------------------------------------------------------
+# Export path
+# ---------------------------------------------------------------------------
+
+def nvfp4_codes(w: torch.Tensor, batch: int, codes: torch.Tensor, amax: torch.Tensor, tmax: torch.Tensor):
+    cols = w.shape[-1]
+    rows = w.numel() // cols // max(batch, 1)
+    _check(load().pq_nvfp4_codes(_ptr(w), batch, rows, cols, _ptr(codes), _ptr(amax), _ptr(tmax), _stream(w)),
+           "pq_nvfp4_codes", f"NVFP4 group_size=16 ∤ {cols}")
+
+
+def nvfp4_scales(amax_list, tmax: torch.Tensor | None, scales_list, global_div: torch.Tensor,
+                 group_of=None, override: torch.Tensor | None = None):
+    n = len(amax_list)
+    lib = load()
+    A = (ctypes.c_void_p * n)(*[a.data_ptr() for a in amax_list])
+    G = (ctypes.c_int64 * n)(*[a.numel() for a in amax_list])
+    S = (ctypes.c_void_p * n)(*[s.data_ptr() for s in scales_list])
+    grp = None if group_of is None else (ctypes.c_int32 * n)(*[int(g) for g in group_of])
+    _check(lib.pq_nvfp4_scales(n, A, G, _ptr(tmax), grp, _ptr(override), S, _ptr(global_div),
+                               _stream(global_div)), "pq_nvfp4_scales")
+
+
+def nvfp4_pack(w: torch.Tensor, override: torch.Tensor | None = None):
+    """NVFP4 export of [rows, cols] (one global) or [E, M, N] (per-expert globals).
+
+    Returns (weight_packed u8, weight_scale float8_e4m3fn, weight_global_scale f32)."""
+    wb = as_bf16_cuda(w, "quantize_dequantize_nvfp4")
+    if wb.dim() not in (2, 3):
+        raise ValueError(f"NVFP4 export expects a 2-D or 3-D weight, got {tuple(wb.shape)}")
+    batch = 1 if wb.dim() == 2 else wb.shape[0]
+    cols = wb.shape[-1]
+    if cols % 16:
+        raise ValueError(f"NVFP4 group_size=16 ∤ {cols}")
+    lead = wb.shape[:-1]
+    dev = wb.device
+    codes = torch.empty(*lead, cols // 2, dtype=torch.uint8, device=dev)
+    scales = torch.empty(*lead, cols // 16, dtype=torch.uint8, device=dev)
+    gdiv = torch.empty(batch, dtype=torch.float32, device=dev)
+    amax = torch.empty(*lead, cols // 16, dtype=torch.int16, device=dev)
+    tmax = torch.empty(batch, dtype=torch.int32, device=dev)
+    if override is not None:
+        override = override.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+        if override.numel() == 1 and batch > 1:
+            override = override.expand(batch).contiguous()
+    rows = wb.numel() // cols // batch
+    _check(load().pq_nvfp4_pack(_ptr(wb), batch, rows, cols, _ptr(override), _ptr(codes), _ptr(scales),
+                                _ptr(gdiv), _ptr(amax), _ptr(tmax), _stream(wb)), "pq_nvfp4_pack")
+    return codes, scales.view(torch.float8_e4m3fn), gdiv
+
+
+def mxfp8_pack(w: torch.Tensor):
+    wb = as_bf16_cuda(w, "quantize_dequantize_mxfp8")
+    cols = wb.shape[-1]
+    if cols % 32:
+        raise ValueError(f"MXFP8 group_size=32 ∤ {cols}")
+    q = torch.empty(wb.shape, dtype=torch.uint8, device=wb.device)
+    sc = torch.empty(*wb.shape[:-1], cols // 32, dtype=torch.uint8, device=wb.device)
+    _check(load().pq_mxfp8_pack(_ptr(wb), wb.numel() // cols, cols, _ptr(q), _ptr(sc), _stream(wb)),
+           "pq_mxfp8_pack")
+    return q.view(torch.float8_e4m3fn), sc
+
+
+def fp8_channel_pack(w: torch.Tensor):
+    wb = as_bf16_cuda(w, "quantize_dequantize_fp8_dynamic")
+    cols = wb.shape[-1]
+    q = torch.empty(wb.shape, dtype=torch.uint8, device=wb.device)
+    s = torch.empty(*wb.shape[:-1], 1, dtype=torch.float32, device=wb.device)
+    _check(load().pq_fp8_channel_pack(_ptr(wb), wb.numel() // cols, cols, _ptr(q), _ptr(s), _stream(wb)),
+           "pq_fp8_channel_pack")
+    return q.view(torch.float8_e4m3fn), s
+
+
+# ---------------------------------------------------------------------------
+# Fisher statistics
+# ---------------------------------------------------------------------------
+
+def sumsq_rows(g: torch.Tensor, total: torch.Tensor, per_row: torch.Tensor | None = None):
+    """total[0] += sum(g^2) (fp64); per_row (fp32, g.shape[:-1]) += row sums."""
+    gb = as_bf16_cuda(g, "sumsq_rows")
+    cols = gb.shape[-1]
+    _check(load().pq_sumsq_rows(_ptr(gb), gb.numel() // cols, cols, _ptr(total), _ptr(per_row), _stream(gb)),
+           "pq_sumsq_rows")
+
+
+def rownorm2(x: torch.Tensor) -> torch.Tensor:
+    xb = as_bf16_cuda(x, "rownorm2")
+    d = xb.shape[-1]
+    out = torch.empty(xb.numel() // d, dtype=torch.float32, device=xb.device)
+    _check(load().pq_rownorm2(_ptr(xb), out.numel(), d, _ptr(out), _stream(xb)), "pq_rownorm2")
+    return out
+
+
+def tokennorm_dot(g: torch.Tensor, xnorm: torch.Tensor, acc: torch.Tensor, token_idx: torch.Tensor | None = None):
+    """acc[0] += sum_t xnorm[idx(t)] * ||g_t||^2; acc[1] += T."""
+    gb = as_bf16_cuda(g, "tokennorm_dot")
+    d = gb.shape[-1]
+    T = gb.numel() // d
+    if token_idx is not None:
+        token_idx = token_idx.to(torch.int64).contiguous()
+    _check(load().pq_tokennorm_dot(_ptr(gb), T, d, _ptr(xnorm), _ptr(token_idx), _ptr(acc), _stream(gb)),
+           "pq_tokennorm_dot")

@@ -1,0 +1,312 @@
+// C ABI entry points (include/prismaquant_b200.h): argument validation, path
+// selection and launch batching around the kernels.  No entry point allocates
+// device memory or synchronizes the stream.
+#include <string.h>
+
+#include <vector>
+
+#include "pq_common.cuh"
+#include "pq_internal.h"
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+
+int num_sms_current() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cached[dev] = v;
+  }
+  return cached[dev];
+}
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+inline int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return PQ_OK;
+  t_last_cuda_error = (int)e;
+  return PQ_ERR_CUDA;
+}
+
+constexpr uint32_t NV = PQ_FMT_BIT(PQ_FMT_NVFP4);
+constexpr uint32_t MX = PQ_FMT_BIT(PQ_FMT_MXFP8);
+constexpr uint32_t F8 = PQ_FMT_BIT(PQ_FMT_FP8_CHANNEL);
+constexpr uint32_t ALL_FMTS = 0xFu;
+
+// Shape rules of the reference's grouping (format_registry.py:208-212): a
+// group longer than the row becomes the whole row; otherwise the row must
+// divide into groups.
+int check_groups(int64_t cols, uint32_t mask) {
+  if ((mask & NV) && cols > 16 && cols % 16) return PQ_ERR_SHAPE;
+  if ((mask & MX) && cols > 32 && cols % 32) return PQ_ERR_SHAPE;
+  return PQ_OK;
+}
+
+bool staged_ok(const uint16_t* w, int64_t cols, uint32_t mask) {
+  if (cols % 16 || cols < 16 || cols * 2 > pq::STAGE_BYTES || !aligned(w, 16)) return false;
+  if ((mask & MX) && cols % 32) return false;
+  return true;
+}
+
+int flush_staged(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, cudaStream_t stream) {
+  size_t i = 0;
+  const int sms = num_sms_current();
+  while (i < descs.size()) {
+    pq::SweepLaunch L;
+    memset(&L, 0, sizeof(L));
+    L.qdq_fmt = qfmt;
+    int64_t items = 0;
+    int n = 0;
+    for (; i < descs.size() && n < pq::MAX_SWEEP_TENSORS; ++i, ++n) {
+      pq::SweepDesc d = descs[i];
+      int64_t rpi = pq::STAGE_BYTES / (d.cols * 2);
+      if (rpi > d.rows) rpi = d.rows;
+      if (rpi < 1) rpi = 1;
+      d.rows_per_item = (int32_t)rpi;
+      L.t[n] = d;
+      L.item_prefix[n] = items;
+      items += (d.rows + rpi - 1) / rpi;
+    }
+    L.n = n;
+    L.item_prefix[n] = items;
+    if (items == 0) continue;
+    const int grid = (int)(items < sms ? items : sms);
+    const int st = cuda_status(pq::launch_sweep_staged(L, mode, grid, stream));
+    if (st) return st;
+  }
+  descs.clear();
+  return PQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pq_version(void) { return 1; }
+
+int pq_last_cuda_error(void) { return t_last_cuda_error; }
+
+const char* pq_status_string(int s) {
+  switch (s) {
+    case PQ_OK: return "ok";
+    case PQ_ERR_NULL: return "null pointer";
+    case PQ_ERR_SHAPE: return "shape not divisible by the format's group size";
+    case PQ_ERR_ALIGN: return "pointer not aligned as required";
+    case PQ_ERR_FORMAT: return "unknown format";
+    case PQ_ERR_CUDA: return "CUDA launch error";
+    case PQ_ERR_LIMIT: return "size beyond the supported maximum";
+    case PQ_ERR_DEVICE: return "a kernel's bounded wait gave up";
+    default: return "unknown status";
+  }
+}
+
+int pq_device_error(int* code) {
+  if (!code) return PQ_ERR_NULL;
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, pq::g_pq_device_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e);
+  if (v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(pq::g_pq_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  *code = v;
+  return PQ_OK;
+}
+
+int pq_sweep_sse(const pq_sweep_tensor* ts, int n, double* sse, void* stream_) {
+  if (n < 0) return PQ_ERR_SHAPE;
+  if (n == 0) return PQ_OK;
+  if (!ts || !sse) return PQ_ERR_NULL;
+  cudaStream_t stream = (cudaStream_t)stream_;
+  std::vector<pq::SweepDesc> staged;
+  // validate everything before launching anything
+  for (int i = 0; i < n; ++i) {
+    const pq_sweep_tensor& t = ts[i];
+    if (t.rows < 0 || t.cols < 1) return PQ_ERR_SHAPE;
+    if (t.fmt_mask & ~ALL_FMTS) return PQ_ERR_FORMAT;
+    if (t.rows > 0 && !t.w) return PQ_ERR_NULL;
+    const int st = check_groups(t.cols, t.fmt_mask);
+    if (st) return st;
+    const bool codes = t.nvfp4_codes || t.nvfp4_amax || t.nvfp4_tmax;
+    if (codes) {
+      if (!t.nvfp4_codes || !t.nvfp4_amax || !t.nvfp4_tmax) return PQ_ERR_NULL;
+      if (t.cols % 16) return PQ_ERR_SHAPE;
+      if (!aligned(t.w, 16) || !aligned(t.nvfp4_codes, 4) || !aligned(t.nvfp4_amax, 2) || !aligned(t.nvfp4_tmax, 4))
+        return PQ_ERR_ALIGN;
+    }
+  }
+  const int sms = num_sms_current();
+  for (int i = 0; i < n; ++i) {
+    const pq_sweep_tensor& t = ts[i];
+    const uint32_t m = t.fmt_mask & (NV | MX | F8);
+    const bool codes = t.nvfp4_codes != nullptr;
+    if (t.rows == 0) continue;
+    if (staged_ok(t.w, t.cols, m)) {
+      pq::SweepDesc d;
+      memset(&d, 0, sizeof(d));
+      d.w = t.w;
+      d.rows = t.rows;
+      d.cols = t.cols;
+      d.fmt_mask = m;
+      d.sse = sse + 4 * (int64_t)i;
+      if (codes) {
+        d.nvfp4_codes = t.nvfp4_codes;
+        d.nvfp4_amax = t.nvfp4_amax;
+        d.nvfp4_tmax = t.nvfp4_tmax;
+      }
+      if (m || codes) staged.push_back(d);
+    } else {
+      if (m) {
+        const int st = cuda_status(pq::launch_sweep_generic(t.w, t.rows, t.cols, m, sse + 4 * (int64_t)i, nullptr,
+                                                            pq::MODE_SSE, sms, stream));
+        if (st) return st;
+      }
+      if (codes) {
+        const int st = cuda_status(pq::launch_nvfp4_codes(t.w, 1, t.rows, t.cols, t.nvfp4_codes, t.nvfp4_amax,
+                                                          t.nvfp4_tmax, sms, stream));
+        if (st) return st;
+      }
+    }
+  }
+  return flush_staged(staged, pq::MODE_SSE, 0, stream);
+}
+
+int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t* w_hat, void* stream_) {
+  if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (fmt < 0 || fmt >= PQ_NUM_FMTS) return PQ_ERR_FORMAT;
+  if (rows == 0) return PQ_OK;
+  if (!w || !w_hat) return PQ_ERR_NULL;
+  cudaStream_t stream = (cudaStream_t)stream_;
+  if (fmt == PQ_FMT_BF16)
+    return cuda_status(cudaMemcpyAsync(w_hat, w, (size_t)rows * cols * 2, cudaMemcpyDeviceToDevice, stream));
+  const uint32_t m = 1u << fmt;
+  const int st = check_groups(cols, m);
+  if (st) return st;
+  if (staged_ok(w, cols, m) && aligned(w_hat, 16)) {
+    std::vector<pq::SweepDesc> v(1);
+    memset(&v[0], 0, sizeof(pq::SweepDesc));
+    v[0].w = w;
+    v[0].rows = rows;
+    v[0].cols = cols;
+    v[0].fmt_mask = m;
+    v[0].out = w_hat;
+    return flush_staged(v, pq::MODE_QDQ, fmt, stream);
+  }
+  return cuda_status(pq::launch_sweep_generic(w, rows, cols, m, nullptr, w_hat, pq::MODE_QDQ, num_sms_current(),
+                                              stream));
+}
+
+int pq_nvfp4_codes(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint8_t* codes, uint16_t* amax,
+                   uint32_t* tmax, void* stream) {
+  if (batch < 0 || rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (cols % 16) return PQ_ERR_SHAPE;
+  if (batch == 0 || rows == 0) return PQ_OK;
+  if (!w || !codes || !amax || !tmax) return PQ_ERR_NULL;
+  if (!aligned(w, 16) || !aligned(codes, 4) || !aligned(amax, 2) || !aligned(tmax, 4)) return PQ_ERR_ALIGN;
+  return cuda_status(
+      pq::launch_nvfp4_codes(w, batch, rows, cols, codes, amax, tmax, num_sms_current(), (cudaStream_t)stream));
+}
+
+int pq_nvfp4_scales(int n, const uint16_t* const* amax, const int64_t* n_groups, const uint32_t* tmax_dev,
+                    const int32_t* group_of, const float* override_dev, uint8_t* const* scales,
+                    float* global_div_dev, void* stream) {
+  if (n < 0) return PQ_ERR_SHAPE;
+  if (n == 0) return PQ_OK;
+  if (n > pq::MAX_SCALE_SLICES) return PQ_ERR_LIMIT;
+  if (!amax || !n_groups || !scales || !global_div_dev || (!tmax_dev && !override_dev)) return PQ_ERR_NULL;
+  pq::ScalesLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.n = n;
+  int64_t maxg = 0;
+  for (int i = 0; i < n; ++i) {
+    if (n_groups[i] < 0) return PQ_ERR_SHAPE;
+    if (n_groups[i] > 0 && (!amax[i] || !scales[i])) return PQ_ERR_NULL;
+    L.amax[i] = amax[i];
+    L.n_groups[i] = n_groups[i];
+    L.scales[i] = scales[i];
+    L.group_of[i] = group_of ? group_of[i] : -1;
+    if (n_groups[i] > maxg) maxg = n_groups[i];
+  }
+  L.tmax = tmax_dev;
+  L.override_ = override_dev;
+  L.global_div = global_div_dev;
+  return cuda_status(pq::launch_nvfp4_scales(L, maxg, num_sms_current(), (cudaStream_t)stream));
+}
+
+int pq_nvfp4_pack(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, const float* override_dev,
+                  uint8_t* codes, uint8_t* scales, float* global_div, uint16_t* scratch_amax,
+                  uint32_t* scratch_tmax, void* stream_) {
+  if (batch < 0 || rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (cols % 16) return PQ_ERR_SHAPE;
+  if (batch == 0) return PQ_OK;
+  if (!global_div || !scratch_tmax) return PQ_ERR_NULL;
+  cudaStream_t stream = (cudaStream_t)stream_;
+  int st = cuda_status(cudaMemsetAsync(scratch_tmax, 0, (size_t)batch * sizeof(uint32_t), stream));
+  if (st) return st;
+  st = pq_nvfp4_codes(w, batch, rows, cols, codes, scratch_amax, scratch_tmax, stream_);
+  if (st) return st;
+  const int64_t ng = rows * cols / 16;
+  for (int64_t b0 = 0; b0 < batch; b0 += pq::MAX_SCALE_SLICES) {
+    const int nb = (int)((batch - b0) < pq::MAX_SCALE_SLICES ? (batch - b0) : pq::MAX_SCALE_SLICES);
+    std::vector<const uint16_t*> am(nb);
+    std::vector<int64_t> ngs(nb, ng);
+    std::vector<uint8_t*> sc(nb);
+    for (int i = 0; i < nb; ++i) {
+      am[i] = scratch_amax + (b0 + i) * ng;
+      sc[i] = scales + (b0 + i) * ng;
+    }
+    st = pq_nvfp4_scales(nb, am.data(), ngs.data(), scratch_tmax + b0, nullptr,
+                         override_dev ? override_dev + b0 : nullptr, sc.data(), global_div + b0, stream_);
+    if (st) return st;
+  }
+  return PQ_OK;
+}
+
+int pq_mxfp8_pack(const uint16_t* w, int64_t n_rows, int64_t cols, uint8_t* q, uint8_t* scale_e8m0, void* stream) {
+  if (n_rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (cols % 32) return PQ_ERR_SHAPE;
+  if (n_rows == 0) return PQ_OK;
+  if (!w || !q || !scale_e8m0) return PQ_ERR_NULL;
+  if (!aligned(w, 16) || !aligned(q, 8)) return PQ_ERR_ALIGN;
+  return cuda_status(pq::launch_mxfp8_pack(w, n_rows * cols, q, scale_e8m0, num_sms_current(), (cudaStream_t)stream));
+}
+
+int pq_fp8_channel_pack(const uint16_t* w, int64_t n_rows, int64_t cols, uint8_t* q, float* scale, void* stream) {
+  if (n_rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (n_rows == 0) return PQ_OK;
+  if (!w || !q || !scale) return PQ_ERR_NULL;
+  if ((cols % 8) == 0 && (!aligned(w, 16) || !aligned(q, 8))) return PQ_ERR_ALIGN;
+  return cuda_status(pq::launch_fp8_channel_pack(w, n_rows, cols, q, scale, num_sms_current(), (cudaStream_t)stream));
+}
+
+int pq_sumsq_rows(const uint16_t* g, int64_t n_rows, int64_t cols, double* total, float* per_row, void* stream) {
+  if (n_rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (!total) return PQ_ERR_NULL;
+  if (n_rows == 0) return PQ_OK;
+  if (!g) return PQ_ERR_NULL;
+  return cuda_status(pq::launch_sumsq_rows(g, n_rows, cols, total, per_row, num_sms_current(), (cudaStream_t)stream));
+}
+
+int pq_rownorm2(const uint16_t* x, int64_t T, int64_t d, float* out, void* stream) {
+  if (T < 0 || d < 1) return PQ_ERR_SHAPE;
+  if (T == 0) return PQ_OK;
+  if (!x || !out) return PQ_ERR_NULL;
+  return cuda_status(pq::launch_rownorm2(x, T, d, out, num_sms_current(), (cudaStream_t)stream));
+}
+
+int pq_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm, const int64_t* token_idx,
+                     double* acc, void* stream) {
+  if (T < 0 || d < 1) return PQ_ERR_SHAPE;
+  if (!acc) return PQ_ERR_NULL;
+  if (T > 0 && (!g || !xnorm)) return PQ_ERR_NULL;
+  return cuda_status(
+      pq::launch_tokennorm_dot(g, T, d, xnorm, token_idx, acc, num_sms_current(), (cudaStream_t)stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,137 @@
+// Fisher-trace statistics as HBM-streaming reductions.
+//
+//  * sumsq_rows   — _GradNormCapture.backward (prismaquant/sensitivity_probe.py:451-482):
+//                   scalar sum of g^2 (fp64) and the per-row [E, M] channel diagonal (fp32).
+//  * rownorm2     — per-token ||x_t||^2 of a Linear's input, taken in the forward hook
+//                   so the activation itself need not be kept for the backward.
+//  * tokennorm_dot— sum_t ||x_t||^2 ||g_t||^2 in the backward hook: the per-token Fisher
+//                   estimate that replaces grad_w = gy^T x; sum(grad_w^2)
+//                   (prismaquant/sensitivity_probe.py:1115-1152), optionally over the
+//                   tokens routed to one expert (token_idx).
+//
+// One warp per row; each lane reads 16-byte vectors (8 bf16), squares are
+// summed in fp32 per 8 elements and in fp64 across them.
+#include "pq_common.cuh"
+#include "pq_internal.h"
+
+namespace pq {
+
+__device__ __forceinline__ float sq8(const uint4& v) {
+  float w[8];
+  unpack8(v, w);
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s = fmaf(w[i], w[i], s);
+  return s;
+}
+
+// Sum of squares of one bf16 row, reduced over the warp (every lane gets it).
+__device__ __forceinline__ double row_sumsq(const uint16_t* __restrict__ row, int64_t cols, int lane) {
+  double acc = 0.0;
+  if ((cols & 7) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    const int64_t n8 = cols >> 3;
+    int64_t c = lane;
+    for (; c + 32 < n8; c += 64) {  // two independent loads in flight per lane
+      const uint4 a = __ldg(rv + c), b = __ldg(rv + c + 32);
+      acc += (double)sq8(a) + (double)sq8(b);
+    }
+    for (; c < n8; c += 32) acc += (double)sq8(__ldg(rv + c));
+  } else {
+    float part = 0.0f;
+    int cnt = 0;
+    for (int64_t i = lane; i < cols; i += 32) {
+      const float x = __uint_as_float((uint32_t)__ldg(row + i) << 16);
+      part = fmaf(x, x, part);
+      if (++cnt == 8) {
+        acc += (double)part;
+        part = 0.0f;
+        cnt = 0;
+      }
+    }
+    acc += (double)part;
+  }
+  return warp_sum_d(acc);
+}
+
+__global__ void __launch_bounds__(256) sumsq_rows_kernel(const uint16_t* __restrict__ g, int64_t rows, int64_t cols,
+                                                         double* total, float* per_row) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc = 0.0;
+  for (int64_t r = gw; r < rows; r += nw) {
+    const double v = row_sumsq(g + r * cols, cols, lane);
+    if (lane == 0 && per_row != nullptr) per_row[r] += (float)v;
+    acc += v;
+  }
+  __shared__ double red[8];
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    atomicAdd(total, t);
+  }
+}
+
+__global__ void __launch_bounds__(256) rownorm2_kernel(const uint16_t* __restrict__ x, int64_t T, int64_t d,
+                                                       float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t t = gw; t < T; t += nw) {
+    const double v = row_sumsq(x + t * d, d, lane);
+    if (lane == 0) out[t] = (float)v;
+  }
+}
+
+__global__ void __launch_bounds__(256) tokennorm_dot_kernel(const uint16_t* __restrict__ g, int64_t T, int64_t d,
+                                                            const float* __restrict__ xnorm,
+                                                            const int64_t* __restrict__ token_idx, double* acc) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double a = 0.0;
+  for (int64_t t = gw; t < T; t += nw) {
+    const double gn = row_sumsq(g + t * d, d, lane);
+    const int64_t src = token_idx != nullptr ? token_idx[t] : t;
+    a += gn * (double)xnorm[src];
+  }
+  __shared__ double red[8];
+  if (lane == 0) red[warp] = a;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
+    atomicAdd(acc, s);
+    if (blockIdx.x == 0) atomicAdd(acc + 1, (double)T);
+  }
+}
+
+static inline int warp_grid(int64_t rows, int num_sms) {
+  int64_t blocks = (rows + 7) / 8;
+  const int64_t cap = (int64_t)num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+cudaError_t launch_sumsq_rows(const uint16_t* g, int64_t rows, int64_t cols, double* total, float* per_row,
+                              int num_sms, cudaStream_t stream) {
+  sumsq_rows_kernel<<<warp_grid(rows, num_sms), 256, 0, stream>>>(g, rows, cols, total, per_row);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rownorm2(const uint16_t* x, int64_t T, int64_t d, float* out, int num_sms, cudaStream_t stream) {
+  rownorm2_kernel<<<warp_grid(T, num_sms), 256, 0, stream>>>(x, T, d, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm,
+                                 const int64_t* token_idx, double* acc, int num_sms, cudaStream_t stream) {
+  tokennorm_dot_kernel<<<warp_grid(T, num_sms), 256, 0, stream>>>(g, T, d, xnorm, token_idx, acc);
+  return cudaGetLastError();
+}
+
+}  // namespace pq

@@ -1,0 +1,70 @@
+// Internal declarations shared by the prismaquant_b200 translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "prismaquant_b200.h"
+
+namespace pq {
+
+constexpr int SWEEP_THREADS = 512;
+constexpr int STAGE_BYTES = 64 * 1024;     // one work item: consecutive rows, <= 64 KiB
+constexpr int NSTAGE = 3;                  // shared-memory stages per CTA (192 KiB)
+constexpr int MAX_ROWS_PER_ITEM = STAGE_BYTES / 32;  // cols >= 16
+constexpr int MAX_SWEEP_TENSORS = 320;     // descriptors per launch (kernel parameter space)
+
+enum : int { MODE_SSE = 0, MODE_QDQ = 1 };
+
+struct SweepDesc {
+  const uint16_t* w;
+  int64_t rows;
+  int64_t cols;
+  uint32_t fmt_mask;
+  int32_t rows_per_item;
+  uint8_t* nvfp4_codes;
+  uint16_t* nvfp4_amax;
+  uint32_t* nvfp4_tmax;
+  uint16_t* out;  // QDQ output
+  double* sse;    // 4 doubles (one per pq_format)
+};
+
+struct SweepLaunch {
+  int n;
+  int qdq_fmt;
+  int64_t item_prefix[MAX_SWEEP_TENSORS + 1];
+  SweepDesc t[MAX_SWEEP_TENSORS];
+};
+
+size_t sweep_smem_bytes();
+cudaError_t launch_sweep_staged(const SweepLaunch& L, int mode, int grid, cudaStream_t stream);
+cudaError_t launch_sweep_generic(const uint16_t* w, int64_t rows, int64_t cols, uint32_t mask, double* sse,
+                                 uint16_t* out, int mode, int num_sms, cudaStream_t stream);
+
+// pq_pack.cu
+constexpr int MAX_SCALE_SLICES = 256;
+struct ScalesLaunch {
+  int n;
+  const uint16_t* amax[MAX_SCALE_SLICES];
+  int64_t n_groups[MAX_SCALE_SLICES];
+  uint8_t* scales[MAX_SCALE_SLICES];
+  int32_t group_of[MAX_SCALE_SLICES];
+  const uint32_t* tmax;
+  const float* override_;
+  float* global_div;
+};
+cudaError_t launch_nvfp4_codes(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint8_t* codes,
+                               uint16_t* amax, uint32_t* tmax, int num_sms, cudaStream_t stream);
+cudaError_t launch_nvfp4_scales(const ScalesLaunch& L, int64_t max_groups, int num_sms, cudaStream_t stream);
+cudaError_t launch_mxfp8_pack(const uint16_t* w, int64_t n_elems, uint8_t* q, uint8_t* sc, int num_sms,
+                              cudaStream_t stream);
+cudaError_t launch_fp8_channel_pack(const uint16_t* w, int64_t rows, int64_t cols, uint8_t* q, float* scale,
+                                    int num_sms, cudaStream_t stream);
+
+// pq_fisher.cu
+cudaError_t launch_sumsq_rows(const uint16_t* g, int64_t rows, int64_t cols, double* total, float* per_row,
+                              int num_sms, cudaStream_t stream);
+cudaError_t launch_rownorm2(const uint16_t* x, int64_t T, int64_t d, float* out, int num_sms, cudaStream_t stream);
+cudaError_t launch_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm,
+                                 const int64_t* token_idx, double* acc, int num_sms, cudaStream_t stream);
+
+}  // namespace pq

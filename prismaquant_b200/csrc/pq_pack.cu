@@ -1,0 +1,251 @@
+// Export packing kernels: NVFP4 (codes + E4M3 block scales + fp32 global),
+// MXFP8 (E4M3 values + E8M0 scales), FP8 per-channel (E4M3 values + fp32 row
+// scales), in the compressed-tensors layouts the reference writes
+// (prismaquant/export_native_compressed.py:1045-1226).
+//
+// All are HBM-streaming kernels: each warp instruction moves 512 contiguous
+// bytes (one 16-byte vector per lane, 8 bf16 elements), groups are formed
+// with lane shuffles, outputs are written with vector stores.
+#include "pq_common.cuh"
+#include "pq_internal.h"
+
+namespace pq {
+
+static inline int grid_for(int64_t warps_needed, int num_sms, int per_sm = 8, int threads = 256) {
+  int64_t blocks = (warps_needed * 32 + threads - 1) / threads;
+  const int64_t cap = (int64_t)num_sms * per_sm;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+// ---------------------------------------------------------------------------
+// NVFP4 pass 1: codes, group amax (bf16), per-slice max group amax.
+// Codes are independent of the global scale (export_native_compressed.py:1093-1096):
+//   in_grid = w / max(max(amax,1e-12)/6, 1e-12), abs-codebook RTN, ties -> 0.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) nvfp4_codes_kernel(const uint16_t* __restrict__ w, int64_t n_chunks,
+                                                          int64_t chunks_per_slice, uint8_t* __restrict__ codes,
+                                                          uint16_t* __restrict__ amax, uint32_t* tmax) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t cur_b = -1;
+  uint32_t cur_max = 0u;
+  for (int64_t c0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x - lane; c0 < n_chunks; c0 += stride) {
+    const int64_t c = c0 + lane;
+    const bool valid = c < n_chunks;
+    float v[8];
+    unpack8(valid ? __ldg(reinterpret_cast<const uint4*>(w) + c) : make_uint4(0, 0, 0, 0), v);
+    const float a8 = amax8(v);
+    const float a16 = fmaxf(a8, __shfl_xor_sync(FULL, a8, 1));
+    if (valid) {
+      const float s = fmaxf(__fdiv_rn(fmaxf(a16, 1e-12f), 6.0f), 1e-12f);
+      uint32_t cw = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cw |= nvfp4_code(__fdiv_rn(v[i], s)) << (4 * i);
+      reinterpret_cast<uint32_t*>(codes)[c] = cw;
+      if ((lane & 1) == 0) amax[c >> 1] = (uint16_t)(__float_as_uint(a16) >> 16);
+    }
+    // per-slice running max; flushed when the slice changes
+    const int64_t b = valid ? c / chunks_per_slice : -1;
+    const int64_t b0 = __shfl_sync(FULL, b, 0);
+    const bool uniform = __all_sync(FULL, b == b0 || b < 0);
+    if (uniform) {
+      const uint32_t m = warp_max_u(valid ? __float_as_uint(a16) : 0u);
+      if (lane == 0 && b0 >= 0) {
+        if (b0 != cur_b) {
+          if (cur_b >= 0) atomicMax(tmax + cur_b, cur_max);
+          cur_b = b0;
+          cur_max = 0u;
+        }
+        cur_max = max(cur_max, m);
+      }
+    } else if (valid) {
+      atomicMax(tmax + b, __float_as_uint(a16));
+    }
+  }
+  if (lane == 0 && cur_b >= 0) atomicMax(tmax + cur_b, cur_max);
+}
+
+cudaError_t launch_nvfp4_codes(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint8_t* codes,
+                               uint16_t* amax, uint32_t* tmax, int num_sms, cudaStream_t stream) {
+  const int64_t n_chunks = batch * rows * cols / 8;
+  const int64_t cps = rows * cols / 8;
+  nvfp4_codes_kernel<<<grid_for(n_chunks / 32 + 1, num_sms), 256, 0, stream>>>(w, n_chunks, cps, codes, amax,
+                                                                                  tmax);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// NVFP4 pass 2: E4M3 block scales and the global divisor (1/global_real).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float nvfp4_global_from_tmax(uint32_t tmax_bits) {
+  // compute_nvfp4_global_real: (max_g(max(amax,1e-12)/6) / 448).clamp_min(1e-12); the max of the
+  // rounded quotients is the quotient of the max (round-to-nearest is monotone).
+  const float sg = __fdiv_rn(fmaxf(__uint_as_float(tmax_bits), 1e-12f), 6.0f);
+  return fmaxf(__fdiv_rn(sg, 448.0f), 1e-12f);
+}
+
+__global__ void __launch_bounds__(256) nvfp4_scales_kernel(const __grid_constant__ ScalesLaunch L) {
+  const int b = blockIdx.y;
+  __shared__ float s_glob;
+  if (threadIdx.x == 0) {
+    float g;
+    if (L.override_ != nullptr) {
+      g = fmaxf(L.override_[b], 1e-12f);
+    } else {
+      g = 0.0f;
+      for (int c = 0; c < L.n; ++c)
+        if (c == b || (L.group_of[c] >= 0 && L.group_of[c] == L.group_of[b]))
+          g = fmaxf(g, nvfp4_global_from_tmax(L.tmax[c]));
+    }
+    s_glob = g;
+    if (blockIdx.x == 0) L.global_div[b] = __frcp_rn(g);
+  }
+  __syncthreads();
+  const float glob = s_glob;
+  const uint16_t* am = L.amax[b];
+  uint8_t* sc = L.scales[b];
+  const int64_t ng = L.n_groups[b];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  auto one = [&](uint32_t abits) {
+    const float sg = __fdiv_rn(fmaxf(__uint_as_float(abits << 16), 1e-12f), 6.0f);
+    const float v = fminf(fmaxf(__fdiv_rn(sg, glob), 0.0f), 448.0f);
+    return e4m3_byte(v);
+  };
+  if ((ng & 7) == 0 && (reinterpret_cast<uintptr_t>(am) & 15) == 0 && (reinterpret_cast<uintptr_t>(sc) & 7) == 0) {
+    const int64_t n8 = ng >> 3;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += stride) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(am) + i);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        lo |= one(aw[k] & 0xFFFFu) << (16 * k);
+        lo |= one(aw[k] >> 16) << (16 * k + 8);
+        hi |= one(aw[k + 2] & 0xFFFFu) << (16 * k);
+        hi |= one(aw[k + 2] >> 16) << (16 * k + 8);
+      }
+      reinterpret_cast<uint2*>(sc)[i] = make_uint2(lo, hi);
+    }
+  } else {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ng; i += stride)
+      sc[i] = (uint8_t)one(am[i]);
+  }
+}
+
+cudaError_t launch_nvfp4_scales(const ScalesLaunch& L, int64_t max_groups, int num_sms, cudaStream_t stream) {
+  int64_t bx = (max_groups / 8 + 255) / 256;
+  const int64_t cap = ((int64_t)num_sms * 8 + L.n - 1) / L.n;
+  if (bx > cap) bx = cap;
+  if (bx < 1) bx = 1;
+  dim3 grid((unsigned)bx, (unsigned)L.n);
+  nvfp4_scales_kernel<<<grid, 256, 0, stream>>>(L);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// MXFP8 (export_native_compressed.py:1138-1162): lane quads form a 32-group.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) mxfp8_pack_kernel(const uint16_t* __restrict__ w, int64_t n_chunks,
+                                                         uint8_t* __restrict__ q, uint8_t* __restrict__ sc) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t c0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x - lane; c0 < n_chunks; c0 += stride) {
+    const int64_t c = c0 + lane;
+    const bool valid = c < n_chunks;
+    float v[8];
+    unpack8(valid ? __ldg(reinterpret_cast<const uint4*>(w) + c) : make_uint4(0, 0, 0, 0), v);
+    float a = amax8(v);
+    a = fmaxf(a, __shfl_xor_sync(FULL, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(FULL, a, 2));
+    if (!valid) continue;
+    const float s = __fdiv_rn(fmaxf(a, pow2i(-127)), 448.0f);  // amax.clamp_min(2^-127) / 448
+    const int e = e8m0_ceil(s);
+    const float inv = pow2i(-e);  // w / 2^e, exact
+    uint32_t out[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int i = 0; i < 4; i += 2) {
+        const float x0 = fminf(fmaxf(__fmul_rn(v[4 * k + i], inv), -448.0f), 448.0f);
+        const float x1 = fminf(fmaxf(__fmul_rn(v[4 * k + i + 1], inv), -448.0f), 448.0f);
+        word |= e4m3x2(x0, x1) << (8 * i);
+      }
+      out[k] = word;
+    }
+    reinterpret_cast<uint2*>(q)[c] = make_uint2(out[0], out[1]);
+    if ((lane & 3) == 0) sc[c >> 2] = (uint8_t)(e + 127);
+  }
+}
+
+cudaError_t launch_mxfp8_pack(const uint16_t* w, int64_t n_elems, uint8_t* q, uint8_t* sc, int num_sms,
+                              cudaStream_t stream) {
+  const int64_t n_chunks = n_elems / 8;
+  mxfp8_pack_kernel<<<grid_for(n_chunks / 32 + 1, num_sms), 256, 0, stream>>>(w, n_chunks, q, sc);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// FP8 per-channel (export_native_compressed.py:1197-1226): warp per row, row
+// amax then w / s (IEEE division), clamp, E4M3 RNE.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) fp8_channel_kernel(const uint16_t* __restrict__ w, int64_t rows, int64_t cols,
+                                                          uint8_t* __restrict__ q, float* __restrict__ scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const bool vec = (cols & 7) == 0;
+  for (int64_t r = gw; r < rows; r += nw) {
+    const uint16_t* row = w + r * cols;
+    float a = 0.0f;
+    if (vec) {
+      const uint4* rv = reinterpret_cast<const uint4*>(row);
+      for (int64_t c = lane; c < cols / 8; c += 32) {
+        float v[8];
+        unpack8(__ldg(rv + c), v);
+        a = fmaxf(a, amax8(v));
+      }
+    } else {
+      for (int64_t i = lane; i < cols; i += 32) a = fmaxf(a, fabsf(__uint_as_float((uint32_t)__ldg(row + i) << 16)));
+    }
+    a = __uint_as_float(warp_max_u(__float_as_uint(a)));
+    const float s = __fdiv_rn(fmaxf(a, pow2i(-127)), 448.0f);
+    if (lane == 0) scale[r] = s;
+    uint8_t* qrow = q + r * cols;
+    if (vec) {
+      const uint4* rv = reinterpret_cast<const uint4*>(row);
+      for (int64_t c = lane; c < cols / 8; c += 32) {
+        float v[8];
+        unpack8(__ldg(rv + c), v);
+        uint32_t out[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int i = 0; i < 4; i += 2) {
+            const float x0 = fminf(fmaxf(__fdiv_rn(v[4 * k + i], s), -448.0f), 448.0f);
+            const float x1 = fminf(fmaxf(__fdiv_rn(v[4 * k + i + 1], s), -448.0f), 448.0f);
+            word |= e4m3x2(x0, x1) << (8 * i);
+          }
+          out[k] = word;
+        }
+        reinterpret_cast<uint2*>(qrow)[c] = make_uint2(out[0], out[1]);
+      }
+    } else {
+      for (int64_t i = lane; i < cols; i += 32) {
+        const float x = __fdiv_rn(__uint_as_float((uint32_t)__ldg(row + i) << 16), s);
+        qrow[i] = (uint8_t)e4m3_byte(fminf(fmaxf(x, -448.0f), 448.0f));
+      }
+    }
+  }
+}
+
+cudaError_t launch_fp8_channel_pack(const uint16_t* w, int64_t rows, int64_t cols, uint8_t* q, float* scale,
+                                    int num_sms, cudaStream_t stream) {
+  fp8_channel_kernel<<<grid_for(rows, num_sms), 256, 0, stream>>>(w, rows, cols, q, scale);
+  return cudaGetLastError();
+}
+
+}  // namespace pq

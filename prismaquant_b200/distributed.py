@@ -1,0 +1,67 @@
+"""Multi-GPU plumbing: one process per GPU, torch.distributed over NCCL.
+
+The reference has no distributed code; it shards the cost pass by layer regex
+into per-shard pickles merged on disk (incremental_measure_quant_cost.py:73-99,
+179-221).  Here:
+  * `partition_units` assigns whole units (Linears, expert tensors; fused
+    siblings as one unit so their joint NVFP4 global needs no communication)
+    to ranks, greedy by bytes (largest first onto the least-loaded rank);
+  * `all_gather_costs` assembles the cost table with ONE all_gather of
+    fixed-size float64 records (sse per format + element count) per unit;
+  * `all_reduce_traces` sums the per-Linear Fisher (raw trace, tokens) buffer
+    across data-parallel ranks with ONE all_reduce.
+Nothing else crosses GPUs: weights and packed outputs stay on their rank.
+"""
+from __future__ import annotations
+
+import heapq
+
+import torch
+import torch.distributed as dist
+
+
+def partition_units(sizes: list[int], world: int, group_keys: list[str | None] | None = None) -> list[int]:
+    """Rank of each unit.  Units sharing a non-None group key stay together."""
+    n = len(sizes)
+    keys = group_keys or [None] * n
+    bundles: dict[object, list[int]] = {}
+    for i, k in enumerate(keys):
+        bundles.setdefault(("g", k) if k is not None else ("u", i), []).append(i)
+    items = sorted(bundles.values(), key=lambda idx: (-sum(sizes[j] for j in idx), idx[0]))
+    heap = [(0, r) for r in range(world)]
+    rank = [0] * n
+    for idx in items:
+        load, r = heapq.heappop(heap)
+        for j in idx:
+            rank[j] = r
+        heapq.heappush(heap, (load + sum(sizes[j] for j in idx), r))
+    return rank
+
+
+def max_units_per_rank(ranks: list[int], world: int) -> int:
+    return max([ranks.count(r) for r in range(world)] + [0])
+
+
+def all_gather_costs(local_ids: torch.Tensor, local_sse: torch.Tensor, n_units: int, cap: int,
+                     group=None) -> torch.Tensor:
+    """Gather [n_local, 4] sse records from every rank into a [n_units, 4] table.
+
+    Every rank pads its records to `cap` (the largest per-rank unit count,
+    known to all ranks from the partition) and tags each with its unit id,
+    so the table is assembled by index after ONE all_gather."""
+    world = dist.get_world_size(group)
+    dev = local_sse.device
+    rec = torch.full((cap, 5), -1.0, dtype=torch.float64, device=dev)
+    rec[: local_sse.shape[0], 0] = local_ids.to(torch.float64)
+    rec[: local_sse.shape[0], 1:] = local_sse
+    out = torch.empty(world * cap, 5, dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(out, rec, group=group)
+    table = torch.zeros(n_units, 4, dtype=torch.float64, device=dev)
+    valid = out[:, 0] >= 0
+    table[out[valid, 0].long()] = out[valid, 1:]
+    return table
+
+
+def all_reduce_traces(buf: torch.Tensor, group=None) -> torch.Tensor:
+    dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+    return buf

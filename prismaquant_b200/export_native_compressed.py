@@ -1,0 +1,393 @@
+"""NVFP4 / MXFP8 / FP8 packing into compressed-tensors layouts on B200.
+
+Drop-in for the packing math of prismaquant/export_native_compressed.py:
+  compute_nvfp4_global_real (:1045-1055), quantize_dequantize_nvfp4[_packed]
+  (:1058-1129), quantize_dequantize_mxfp8[_packed] (:1135-1194),
+  quantize_dequantize_fp8_dynamic[_packed] (:1197-1226), _quantize_2d NVFP4 /
+  MXFP8 / BF16 branches (:1691-1896), _quantize_3d_packed and
+  _quantize_2d_group_same_shape (:1930-1981), the fused-sibling joint global
+  (:1577-1599, :1650-1685, :2036-2099).
+Outputs have the reference's dtypes, shapes and bytes (bit-exact).
+
+`export_nvfp4_many` and `sweep_and_export` are the batched forms: pass 1 (codes,
+group amax, tensor amax) runs over every tensor, fused with the cost sweep
+when asked, and one pass-2 launch writes every E4M3 block scale with the joint
+global of each fused-sibling group.
+"""
+from __future__ import annotations
+
+import re
+from collections import defaultdict
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from . import measure_quant_cost as mqc
+
+FLOAT_TO_E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+NVFP4_MAX = 6.0
+FP8_E4M3_MAX = 448.0
+MXFP8_E4M3_MAX = 448.0
+DEFAULT_INPUT_GLOBAL_SCALE = 1.0
+
+
+def _need_group(group_size: int, expected: int, fmt: str):
+    if group_size != expected:
+        raise NotImplementedError(f"{fmt} on B200 uses group_size={expected}, got {group_size}")
+
+
+def compute_nvfp4_global_real(weight: torch.Tensor, group_size: int = 16) -> torch.Tensor:
+    """(max over 16-groups of max(amax,1e-12)/6) / 448, clamped at 1e-12; the max of
+    the rounded per-group quotients equals the quotient of the tensor amax."""
+    _need_group(group_size, 16, "NVFP4")
+    rows, cols = weight.shape
+    if cols % group_size:
+        raise ValueError(f"NVFP4 group_size={group_size} ∤ {cols}")
+    w = _lib.as_bf16_cuda(weight, "compute_nvfp4_global_real")
+    m = w.abs().amax().float().clamp_min(1e-12)
+    return (m / NVFP4_MAX / FP8_E4M3_MAX).clamp_min(1e-12)
+
+
+def quantize_dequantize_nvfp4(weight: torch.Tensor, group_size: int = 16,
+                              global_real_override: torch.Tensor | None = None):
+    """(weight_packed u8 [rows, cols/2], weight_scale e4m3 [rows, cols/16],
+    weight_global_scale f32 [1] = 1/global_real)."""
+    _need_group(group_size, 16, "NVFP4")
+    if weight.dim() != 2:
+        raise ValueError(f"expected a 2-D weight, got {tuple(weight.shape)}")
+    if weight.shape[1] % group_size:
+        raise ValueError(f"NVFP4 group_size={group_size} ∤ {weight.shape[1]}")
+    return _lib.nvfp4_pack(weight, override=global_real_override)
+
+
+def quantize_dequantize_nvfp4_packed(packed: torch.Tensor, group_size: int = 16):
+    """Per-expert globals: (u8 [E, M, N/2], e4m3 [E, M, N/16], f32 [E])."""
+    _need_group(group_size, 16, "NVFP4")
+    if packed.dim() != 3:
+        raise ValueError(f"expected [E, M, N], got {tuple(packed.shape)}")
+    if packed.shape[2] % group_size:
+        raise ValueError(f"NVFP4 group_size={group_size} ∤ {packed.shape[2]}")
+    return _lib.nvfp4_pack(packed)
+
+
+def quantize_dequantize_mxfp8(weight: torch.Tensor, group_size: int = 32):
+    _need_group(group_size, 32, "MXFP8")
+    if weight.shape[-1] % group_size:
+        raise ValueError(f"MXFP8 group_size={group_size} ∤ {weight.shape[-1]}")
+    return _lib.mxfp8_pack(weight)
+
+
+def quantize_dequantize_mxfp8_packed(packed: torch.Tensor, group_size: int = 32):
+    _need_group(group_size, 32, "MXFP8")
+    if packed.shape[-1] % group_size:
+        raise ValueError(f"MXFP8 group_size={group_size} ∤ {packed.shape[-1]}")
+    return _lib.mxfp8_pack(packed)
+
+
+def quantize_dequantize_fp8_dynamic(weight: torch.Tensor):
+    """(fp8 [out, in], fp32 per-channel scale [out, 1])."""
+    return _lib.fp8_channel_pack(weight)
+
+
+def quantize_dequantize_fp8_dynamic_packed(packed: torch.Tensor):
+    """(fp8 [E, M, N], fp32 scale [E, M, 1])."""
+    return _lib.fp8_channel_pack(packed)
+
+
+def _canonical_export_format(fmt: str) -> str:
+    return {"NVINT2": "INT2", "NVINT3": "INT3"}.get(fmt, fmt)
+
+
+def _quantize_2d(weight: torch.Tensor, fmt: str, nvfp4_global_real_override: torch.Tensor | None = None,
+                 input_global_scale_override: float | None = None, linear_name: str | None = None,
+                 awq_enabled: bool = False, gptq_enabled: bool = False, awq_round_enabled: bool = False,
+                 scale_sweep_enabled: bool = False, cached_activations: torch.Tensor | None = None):
+    """On-disk tensors of one Linear (export_native_compressed.py:1691-1896), RTN only."""
+    fmt = _canonical_export_format(fmt)
+    if awq_enabled or gptq_enabled or awq_round_enabled or scale_sweep_enabled:
+        raise NotImplementedError("activation-aware NVFP4 passes are not on the B200 path")
+    if fmt == "NVFP4":
+        wp, ws, wg = quantize_dequantize_nvfp4(weight, 16, nvfp4_global_real_override)
+        scale = DEFAULT_INPUT_GLOBAL_SCALE if input_global_scale_override is None else input_global_scale_override
+        return {"weight_packed": wp, "weight_scale": ws, "weight_global_scale": wg,
+                "input_global_scale": torch.tensor([float(scale)], dtype=torch.float32, device=wp.device)}
+    if fmt == "MXFP8":
+        w, ws = quantize_dequantize_mxfp8(weight, 32)
+        return {"weight": w, "weight_scale": ws}
+    if fmt == "BF16":
+        return {"weight": weight.to(torch.bfloat16)}
+    raise ValueError(f"unsupported format: {fmt}")
+
+
+def _quantize_3d_packed(packed: torch.Tensor, fmt: str):
+    fmt = _canonical_export_format(fmt)
+    if fmt == "BF16":
+        return {"weight": packed.to(torch.bfloat16)}
+    if fmt == "NVFP4":
+        wp, ws, wg = quantize_dequantize_nvfp4_packed(packed, 16)
+        return {"weight_packed": wp, "weight_scale": ws, "weight_global_scale": wg}
+    if fmt == "MXFP8":
+        w, ws = quantize_dequantize_mxfp8_packed(packed, 32)
+        return {"weight": w, "weight_scale": ws}
+    raise ValueError(f"unsupported format for packed-MoE: {fmt}")
+
+
+def _quantize_2d_group_same_shape(stacked_weights: torch.Tensor, fmt: str):
+    fmt = _canonical_export_format(fmt)
+    if stacked_weights.dim() != 3:
+        raise ValueError("same-shape export grouping expects [B, out, in] weights; "
+                         f"got shape={tuple(stacked_weights.shape)}")
+    if fmt == "MXFP8":
+        w, ws = quantize_dequantize_mxfp8_packed(stacked_weights, 32)
+        return {"weight": w, "weight_scale": ws}
+    raise ValueError(f"unsupported grouped 2D export format: {fmt}")
+
+
+# ---------------------------------------------------------------------------
+# fused siblings (export_native_compressed.py:1577-1599, 2036-2099)
+# ---------------------------------------------------------------------------
+_FUSED_DENSE_PATTERNS = [
+    (re.compile(r"^(?P<pre>.+)\.self_attn\.(?P<sib>q_proj|k_proj|v_proj)$"), ("q_proj", "k_proj", "v_proj")),
+    (re.compile(r"^(?P<pre>.+)\.mlp\.(?P<sib>gate_proj|up_proj)$"), ("gate_proj", "up_proj")),
+    (re.compile(r"^(?P<pre>.+)\.mlp\.shared_expert\.(?P<sib>gate_proj|up_proj)$"), ("gate_proj", "up_proj")),
+    (re.compile(r"^(?P<pre>.+)\.linear_attn\.(?P<sib>in_proj_qkv|in_proj_z)$"), ("in_proj_qkv", "in_proj_z")),
+    (re.compile(r"^(?P<pre>.+)\.linear_attn\.(?P<sib>in_proj_a|in_proj_b)$"), ("in_proj_a", "in_proj_b")),
+]
+
+_FUSED_SIBLINGS = {
+    "q_proj": "qkv", "k_proj": "qkv", "v_proj": "qkv",
+    "gate_proj": "gate_up", "up_proj": "gate_up",
+    "in_proj_qkv": "qkvz", "in_proj_z": "qkvz",
+    "in_proj_b": "ba", "in_proj_a": "ba",
+}
+
+
+def _fused_dense_group(name: str):
+    for pat, members in _FUSED_DENSE_PATTERNS:
+        m = pat.match(name)
+        if m:
+            return (m.group("pre"), members)
+    return None
+
+
+def sibling_group_key(name: str) -> str | None:
+    """Key shared by the fused siblings of `name` (parent module + family), None if unfused."""
+    parent, _, leaf = name.rpartition(".")
+    fam = _FUSED_SIBLINGS.get(leaf)
+    return None if fam is None else f"{parent}::{fam}"
+
+
+def _compute_nvfp4_joint_global(model: nn.Module, assignment: dict[str, str]) -> dict[str, torch.Tensor]:
+    groups = defaultdict(list)
+    for qname, mod in model.named_modules():
+        if isinstance(mod, nn.Linear) and assignment.get(qname) == "NVFP4":
+            g = _fused_dense_group(qname)
+            if g is not None:
+                groups[g].append((qname, mod))
+    out = {}
+    for sib in groups.values():
+        joint = torch.stack([compute_nvfp4_global_real(m.weight.detach()) for _, m in sib]).max()
+        for q, _ in sib:
+            out[q] = joint
+    return out
+
+
+def _compute_layer_joint_nvfp4(layer_mod: nn.Module, layer_qname: str, assignment: dict[str, str],
+                               profile) -> dict[str, torch.Tensor]:
+    groups = defaultdict(list)
+    for sub, mod in layer_mod.named_modules():
+        if not isinstance(mod, nn.Linear):
+            continue
+        fam = _FUSED_SIBLINGS.get(sub.rsplit(".", 1)[-1])
+        if fam is None:
+            continue
+        parent = sub.rsplit(".", 1)[0] if "." in sub else ""
+        groups[(parent, fam)].append((sub, mod))
+    out = {}
+    for members in groups.values():
+        keyed = []
+        for sub, mod in members:
+            full = f"{layer_qname}.{sub}" if sub else layer_qname
+            rk = profile.live_to_recipe_name(full)
+            keyed.append((rk, assignment.get(rk), mod))
+        if {f for _, f, _ in keyed} != {"NVFP4"}:
+            continue
+        joint = torch.stack([compute_nvfp4_global_real(m.weight.detach()) for _, _, m in keyed]).max()
+        for rk, _, _ in keyed:
+            out[rk] = joint
+    return out
+
+
+# ---------------------------------------------------------------------------
+# batched export (+ fused cost sweep)
+# ---------------------------------------------------------------------------
+
+def _alloc_nvfp4(w: torch.Tensor):
+    lead, cols = w.shape[:-1], w.shape[-1]
+    dev = w.device
+    return (torch.empty(*lead, cols // 2, dtype=torch.uint8, device=dev),
+            torch.empty(*lead, cols // 16, dtype=torch.int16, device=dev))
+
+
+def export_nvfp4_many(weights: list[torch.Tensor], group_keys: list[str | None] | None = None,
+                      fuse_sweep_specs=None, sse: torch.Tensor | None = None):
+    """NVFP4-export many 2-D bf16 CUDA weights; tensors with the same non-None
+    group key share one joint global (fused siblings).
+
+    With `fuse_sweep_specs`, pass 1 is the fused multi-format cost sweep (one
+    read of each weight gives MSE_W for every spec AND the NVFP4 codes).
+    Returns (outputs, sse, errors): outputs[i] = (weight_packed u8,
+    weight_scale e4m3, weight_global_scale f32 [1])."""
+    n = len(weights)
+    ws = [_lib.as_bf16_cuda(w, "export_nvfp4_many") for w in weights]
+    for w in ws:
+        if w.dim() != 2 or w.shape[1] % 16:
+            raise ValueError(f"NVFP4 export needs [rows, cols%16==0], got {tuple(w.shape)}")
+    dev = ws[0].device
+    codes, amax = zip(*[_alloc_nvfp4(w) for w in ws]) if n else ((), ())
+    tmax = torch.zeros(n, dtype=torch.int32, device=dev)
+    errors = None
+    if fuse_sweep_specs is not None:
+        outs = [(c, a, tmax[i:i + 1]) for i, (c, a) in enumerate(zip(codes, amax))]
+        sse, errors = mqc.sweep_sse_async(ws, fuse_sweep_specs, nvfp4_outputs=outs, sse=sse)
+    else:
+        for i, w in enumerate(ws):
+            _lib.nvfp4_codes(w, 1, codes[i], amax[i], tmax[i:i + 1])
+    gdiv = torch.empty(n, dtype=torch.float32, device=dev)
+    scales = [torch.empty(a.shape, dtype=torch.uint8, device=dev) for a in amax]
+    ids: dict[str, int] = {}
+    grp = [-1 if (group_keys is None or k is None) else ids.setdefault(k, len(ids)) for k in
+           (group_keys or [None] * n)]
+    step = 256
+    for b0 in range(0, n, step):
+        sl = slice(b0, min(n, b0 + step))
+        sub_grp = grp[sl]
+        # a joint group must not straddle launches: fall back to own-slice scope if it would
+        if any(g >= 0 and (grp.count(g) != sub_grp.count(g)) for g in sub_grp):
+            raise ValueError("fused-sibling groups must be adjacent within 256 tensors")
+        _lib.nvfp4_scales(list(amax[sl]), tmax[sl], scales[sl], gdiv[sl], group_of=sub_grp)
+    outputs = [(codes[i], scales[i].view(torch.float8_e4m3fn), gdiv[i:i + 1]) for i in range(n)]
+    return outputs, sse, errors
+
+
+def sweep_and_export(named_weights, specs, export_nvfp4: bool = True):
+    """One pass over every weight: MSE_W for all `specs` (cost table) and,
+    if `export_nvfp4`, the NVFP4 export of every tensor with fused-sibling
+    joint globals.  Returns (cost dict {name: {fmt: weight_mse}}, {name: (packed, scale, global)})."""
+    items = list(named_weights.items()) if isinstance(named_weights, dict) else list(named_weights)
+    names = [n for n, _ in items]
+    ws = [w for _, w in items]
+    if export_nvfp4:
+        outs, sse, errors = export_nvfp4_many(ws, [sibling_group_key(n) for n in names], fuse_sweep_specs=specs)
+    else:
+        sse, errors = mqc.sweep_sse_async([_lib.as_bf16_cuda(w, "sweep") for w in ws], specs)
+        outs = None
+    host = sse.cpu().tolist()
+    costs = {}
+    for name, w, row, err in zip(names, ws, host, errors):
+        per = {}
+        for s in specs:
+            per[s.name] = {"error": err[s.name]} if s.name in err else \
+                mqc._mse_from_sse(row[mqc._KCOL[mqc._kernel_format(s)]], w.numel())
+        costs[name] = per
+    return costs, (dict(zip(names, outs)) if outs is not None else None)
+
+
+class SweepExportPlan:
+    """Cost sweep (+ NVFP4 export) of a fixed set of device-resident bf16
+    weights, planned once and run many times: the descriptor table, outputs
+    and scratch are built at construction; `run()` is a memset plus two
+    kernel launches (the fused sweep with NVFP4 codes, then the block-scale
+    pass with fused-sibling joint globals) and no host synchronisation.
+
+    After run(): `sse` [n, 4] fp64 holds sum(err^2) per (tensor, format),
+    `outputs[i]` the NVFP4 (weight_packed, weight_scale, weight_global_scale)."""
+
+    def __init__(self, named_weights, specs, export_nvfp4: bool = True):
+        import ctypes
+        items = list(named_weights.items()) if isinstance(named_weights, dict) else list(named_weights)
+        self.names = [n for n, _ in items]
+        self.weights = [_lib.as_bf16_cuda(w, "SweepExportPlan") for _, w in items]
+        self.specs = list(specs)
+        self.numel = [w.numel() for w in self.weights]
+        n = len(self.weights)
+        dev = self.weights[0].device
+        self.device = dev
+        self.sse = torch.zeros(n, 4, dtype=torch.float64, device=dev)
+        self.tmax = torch.zeros(max(n, 1), dtype=torch.int32, device=dev)
+        kf = [mqc._kernel_format(s) for s in self.specs]
+        self.errors = []
+        masks = []
+        for w in self.weights:
+            m, err = 0, {}
+            for s, k in zip(self.specs, kf):
+                e = mqc.shape_error(k, w.shape[-1])
+                if e:
+                    err[s.name] = e
+                else:
+                    m |= mqc._KBIT[k]
+            masks.append(m & 0x7)
+            self.errors.append(err)
+        self.export = export_nvfp4
+        self.codes, self.amax, self.scales = [], [], []
+        arr = (_lib.SweepTensor * n)()
+        for i, (w, m) in enumerate(zip(self.weights, masks)):
+            cols = w.shape[-1]
+            arr[i].w, arr[i].rows, arr[i].cols, arr[i].fmt_mask = w.data_ptr(), w.numel() // cols, cols, m
+            if export_nvfp4:
+                if w.dim() != 2 or cols % 16:
+                    raise ValueError(f"NVFP4 export needs [rows, cols%16==0], got {tuple(w.shape)}")
+                c, a = _alloc_nvfp4(w)
+                self.codes.append(c)
+                self.amax.append(a)
+                self.scales.append(torch.empty(a.shape, dtype=torch.uint8, device=dev))
+                arr[i].nvfp4_codes, arr[i].nvfp4_amax = c.data_ptr(), a.data_ptr()
+                arr[i].nvfp4_tmax = self.tmax.data_ptr() + 4 * i
+        self._arr = arr
+        self._n = n
+        self.gdiv = torch.empty(max(n, 1), dtype=torch.float32, device=dev)
+        if export_nvfp4:
+            ids: dict[str, int] = {}
+            grp = [(-1 if k is None else ids.setdefault(k, len(ids))) for k in map(sibling_group_key, self.names)]
+            self._scale_calls = []
+            for b0 in range(0, n, 256):
+                sl = slice(b0, min(n, b0 + 256))
+                A = (ctypes.c_void_p * (sl.stop - b0))(*[a.data_ptr() for a in self.amax[sl]])
+                G = (ctypes.c_int64 * (sl.stop - b0))(*[a.numel() for a in self.amax[sl]])
+                S = (ctypes.c_void_p * (sl.stop - b0))(*[s.data_ptr() for s in self.scales[sl]])
+                Q = (ctypes.c_int32 * (sl.stop - b0))(*grp[sl])
+                self._scale_calls.append((sl.stop - b0, A, G, S, Q, self.tmax.data_ptr() + 4 * b0,
+                                          self.gdiv.data_ptr() + 4 * b0))
+        self.outputs = [(self.codes[i], self.scales[i].view(torch.float8_e4m3fn), self.gdiv[i:i + 1])
+                        for i in range(n)] if export_nvfp4 else None
+
+    def launch_sweep(self):
+        lib = _lib.load()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib._check(lib.pq_sweep_sse(self._arr, self._n, _lib._ptr(self.sse), stream), "pq_sweep_sse")
+
+    def launch_scales(self):
+        import ctypes
+        lib = _lib.load()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        for (n, A, G, S, Q, tptr, gptr) in self._scale_calls:
+            _lib._check(lib.pq_nvfp4_scales(n, A, G, ctypes.c_void_p(tptr), Q, None, S, ctypes.c_void_p(gptr),
+                                            stream), "pq_nvfp4_scales")
+
+    def run(self):
+        self.sse.zero_()
+        if self.export:
+            self.tmax.zero_()
+        self.launch_sweep()
+        if self.export:
+            self.launch_scales()
+        return self.sse
+
+    def costs(self) -> dict:
+        host = self.sse.cpu().tolist()
+        out = {}
+        for name, n, row, err in zip(self.names, self.numel, host, self.errors):
+            out[name] = {s.name: ({"error": err[s.name]} if s.name in err else
+                                  mqc._mse_from_sse(row[mqc._KCOL[mqc._kernel_format(s)]], n)) for s in self.specs}
+        return out

@@ -1,0 +1,344 @@
+"""Per-(Linear, format) quantization cost on B200.
+
+Drop-in for the weight-error half of prismaquant/measure_quant_cost.py:
+  * `_batched_quantize(spec, stacked_w)`            (:532-548)
+  * `measure_batched_gpu(...)` / `measure_unbatched(...)` (:551-685, :266-327)
+  * `_measure_packed_experts(...)`                 (:381-449)
+  * `_accumulate_result` / `_finalize_results`     (:57-101), same cost-table schema.
+
+The new primitive is `sweep_weight_mse`: ONE kernel pass over every weight
+scores all requested formats (NVFP4, MXFP8, FP8 per channel; BF16 is 0 by
+definition) and a single device->host copy returns the whole table, where the
+reference runs a quantize + subtract + square + mean chain per (chunk,
+format) with a host sync each.  `output_mse` / `predicted_dloss` keep the
+reference's definitions: the reconstruction comes from the CUDA
+quantize-dequantize kernel, the GEMMs (`bmm`) stay library calls.
+"""
+from __future__ import annotations
+
+import math
+import re
+import time
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from . import format_registry as fr
+
+FLT_MAX = float(torch.finfo(torch.float32).max)
+_KBIT = {"NVFP4": 1 << _lib.FMT_NVFP4, "MXFP8": 1 << _lib.FMT_MXFP8, "FP8_E4M3": 1 << _lib.FMT_FP8_CHANNEL,
+         "BF16": 1 << _lib.FMT_BF16}
+_KCOL = {"NVFP4": _lib.FMT_NVFP4, "MXFP8": _lib.FMT_MXFP8, "FP8_E4M3": _lib.FMT_FP8_CHANNEL, "BF16": _lib.FMT_BF16}
+_GROUP = {"NVFP4": 16, "MXFP8": 32}
+
+
+def canonical_linear_name(name: str) -> str:
+    """measure_quant_cost.py:41-55: per-expert Linears -> packed-expert cost keys."""
+    m = re.match(r"^(.+\.mlp\.experts)\.(\d+)\.(gate_proj|up_proj|down_proj)$", name)
+    if not m:
+        return name
+    prefix, eid, proj = m.groups()
+    return f"{prefix}.gate_up_proj.{eid}" if proj in {"gate_proj", "up_proj"} else f"{prefix}.down_proj.{eid}"
+
+
+def _kernel_format(spec: fr.FormatSpec) -> str:
+    k = getattr(spec, "kernel_format", None)
+    if k is None:
+        raise NotImplementedError(f"format {spec.name} has no B200 kernel")
+    return k
+
+
+def shape_error(kfmt: str, cols: int) -> str | None:
+    """The reference reshapes rows into groups (format_registry.py:208-212); a row
+    that does not divide raises there and is recorded as {"error": ...}."""
+    g = _GROUP.get(kfmt)
+    if g is not None and cols > g and cols % g:
+        return f"shape '[-1, {cols // g}, {g}]' is invalid for a row of {cols} elements"
+    return None
+
+
+# ---------------------------------------------------------------------------
+# cost-table schema (measure_quant_cost.py:57-101)
+# ---------------------------------------------------------------------------
+
+def _accumulate_result(bucket: dict, name: str, fmt: str, weight_mse: float, output_mse: float,
+                       rel_output_mse: float, predicted_dloss: float | None = None):
+    acc = bucket.setdefault(name, {}).setdefault(fmt, {
+        "_count": 0, "_weight_mse_sum": 0.0, "_output_mse_sum": 0.0, "_rel_output_mse_sum": 0.0,
+        "_predicted_dloss_sum": 0.0, "_predicted_dloss_count": 0})
+    if "error" in acc:
+        return
+    acc["_count"] += 1
+    acc["_weight_mse_sum"] += weight_mse
+    acc["_output_mse_sum"] += output_mse
+    acc["_rel_output_mse_sum"] += rel_output_mse
+    if predicted_dloss is not None:
+        acc["_predicted_dloss_sum"] += predicted_dloss
+        acc["_predicted_dloss_count"] += 1
+
+
+def _finalize_results(bucket: dict) -> dict:
+    out = {}
+    for name, per in bucket.items():
+        out[name] = {}
+        for fmt, acc in per.items():
+            if "error" in acc:
+                out[name][fmt] = acc
+                continue
+            n = max(int(acc["_count"]), 1)
+            entry = {"weight_mse": acc["_weight_mse_sum"] / n, "output_mse": acc["_output_mse_sum"] / n,
+                     "rel_output_mse": acc["_rel_output_mse_sum"] / n}
+            if acc["_predicted_dloss_count"] > 0:
+                entry["predicted_dloss"] = acc["_predicted_dloss_sum"] / acc["_predicted_dloss_count"]
+            out[name][fmt] = entry
+    return out
+
+
+# ---------------------------------------------------------------------------
+# the fused sweep
+# ---------------------------------------------------------------------------
+
+def sweep_sse_async(weights: list[torch.Tensor], specs: list[fr.FormatSpec], nvfp4_outputs=None,
+                    sse: torch.Tensor | None = None):
+    """Launch the fused sweep; returns (sse [n, 4] fp64 on device, errors).
+
+    errors[i][spec.name] holds the reference's error text for a (tensor,
+    format) whose grouping the shape cannot take; that format is left out of
+    the tensor's mask."""
+    kf = [_kernel_format(s) for s in specs]
+    masks, errors = [], []
+    for w in weights:
+        cols = w.shape[-1]
+        m, err = 0, {}
+        for s, k in zip(specs, kf):
+            e = shape_error(k, cols)
+            if e:
+                err[s.name] = e
+            else:
+                m |= _KBIT[k]
+        masks.append(m & 0x7)
+        errors.append(err)
+    sse = _lib.sweep_sse(weights, masks, nvfp4_outputs=nvfp4_outputs, sse=sse)
+    return sse, errors
+
+
+def _mse_from_sse(sse: float, n: int) -> float:
+    if not math.isfinite(sse) or sse > FLT_MAX:
+        return float("inf") if not math.isnan(sse) else sse
+    return sse / max(n, 1)
+
+
+def sweep_weight_mse(named_weights, specs: list[fr.FormatSpec]) -> dict[str, dict[str, float | dict]]:
+    """{name: {spec.name: weight_mse | {"error": msg}}} for bf16 CUDA weights
+    ([out, in] Linears or [E, M, N] packed experts), all formats in one pass."""
+    items = list(named_weights.items()) if isinstance(named_weights, dict) else list(named_weights)
+    names = [n for n, _ in items]
+    weights = [_lib.as_bf16_cuda(w.detach(), "sweep_weight_mse") for _, w in items]
+    if not weights:
+        return {}
+    sse, errors = sweep_sse_async(weights, specs)
+    host = sse.cpu().tolist()  # the one device->host copy
+    out = {}
+    for name, w, row, err in zip(names, weights, host, errors):
+        per = {}
+        for s in specs:
+            if s.name in err:
+                per[s.name] = {"error": err[s.name]}
+            else:
+                per[s.name] = _mse_from_sse(row[_KCOL[_kernel_format(s)]], w.numel())
+        out[name] = per
+    return out
+
+
+def _batched_quantize(spec: fr.FormatSpec, stacked_w: torch.Tensor) -> torch.Tensor:
+    """measure_quant_cost.py:532-548: W_hat of a stacked [N, out, in] weight."""
+    k = _kernel_format(spec)
+    if k == "BF16":
+        return stacked_w.clone()
+    return _lib.cost_qdq(stacked_w, k)
+
+
+# ---------------------------------------------------------------------------
+# reference entry points
+# ---------------------------------------------------------------------------
+
+def _group_by_shape(model: nn.Module, target_names: set[str]):
+    groups: dict[tuple[int, int], list[tuple[str, nn.Linear]]] = {}
+    for name, mod in model.named_modules():
+        cname = canonical_linear_name(name)
+        if isinstance(mod, nn.Linear) and cname in target_names:
+            groups.setdefault((mod.in_features, mod.out_features), []).append((cname, mod))
+    return groups
+
+
+def _weight_mse_or_errors(W_list, specs):
+    """Weight MSE of each weight for each spec (one fused pass), as python floats."""
+    res = sweep_weight_mse([(str(i), w) for i, w in enumerate(W_list)], specs)
+    return [res[str(i)] for i in range(len(W_list))]
+
+
+def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], specs: list[fr.FormatSpec],
+                        device: str, dtype: torch.dtype, chunk_size: int = 256, h_detail=None) -> dict:
+    """measure_quant_cost.py:551-685 with the weight error from the fused sweep."""
+    dev = torch.device(device)
+    groups = _group_by_shape(model, target_names)
+    accum: dict = {}
+    processed, t0 = 0, time.time()
+    total = sum(len(v) for v in groups.values())
+    for (_in_f, _out_f), entries in groups.items():
+        entries = [(n, m) for n, m in entries if n in act_cache]
+        for i in range(0, len(entries), chunk_size):
+            chunk = entries[i:i + chunk_size]
+            names = [n for n, _ in chunk]
+            acts = [act_cache.load(n) for n in names]
+            rows = min(a.size(0) for a in acts)
+            W = torch.stack([m.weight.detach().to(device=dev, dtype=dtype) for _, m in chunk])
+            X = torch.stack([a[:rows].to(device=dev, dtype=dtype) for a in acts])
+            y_ref = torch.bmm(X, W.transpose(1, 2))
+            ref_energy = y_ref.float().pow(2).mean(dim=(1, 2))
+            h_stacked = None
+            if h_detail is not None and all(n in h_detail for n in names):
+                hs = [h_detail.load(n) for n in names]
+                if all(tuple(h.shape) == tuple(W.shape[1:]) for h in hs):
+                    h_stacked = torch.stack([h.to(dev).float() for h in hs])
+            wmse = _weight_mse_or_errors(list(W.unbind(0)), specs) if dtype == torch.bfloat16 else None
+            for spec in specs:
+                try:
+                    if wmse is None and _kernel_format(spec) != "BF16":
+                        raise NotImplementedError(f"B200 cost kernels take bf16 weights, got {dtype}")
+                    W_hat = _batched_quantize(spec, W)
+                    X_hat = spec.activation_quantize_dequantize(X.clone())
+                    y_q = torch.bmm(X_hat, W_hat.transpose(1, 2))
+                    out_mse = (y_ref - y_q).float().pow(2).mean(dim=(1, 2))
+                    rel = out_mse / ref_energy.clamp_min(1e-12)
+                    dl = None
+                    if h_stacked is not None:
+                        err = (W - W_hat).float()
+                        dl = (0.5 * (h_stacked * err.pow(2)).sum(dim=(1, 2))).cpu().tolist()
+                    om, rl = out_mse.cpu().tolist(), rel.cpu().tolist()
+                    for j, name in enumerate(names):
+                        wm = 0.0 if wmse is None else wmse[j][spec.name]
+                        if isinstance(wm, dict):
+                            raise ValueError(wm["error"])
+                        _accumulate_result(accum, name, spec.name, float(wm), float(om[j]), float(rl[j]),
+                                           predicted_dloss=None if dl is None else float(dl[j]))
+                except Exception as e:  # measure_quant_cost.py:673-675
+                    for name in names:
+                        accum.setdefault(name, {})[spec.name] = {"error": str(e)}
+            processed += len(chunk)
+            if processed % (chunk_size * 4) == 0 or processed == total:
+                print(f"[cost] {processed}/{total} ({time.time() - t0:.1f}s)", flush=True)
+    return _finalize_results(accum)
+
+
+def measure_unbatched(model: nn.Module, act_cache, target_names: set[str], specs: list[fr.FormatSpec],
+                      device: str, dtype: torch.dtype, h_detail=None) -> dict:
+    """measure_quant_cost.py:266-327: one Linear at a time (same numbers as batched)."""
+    accum: dict = {}
+    for name, mod in model.named_modules():
+        cname = canonical_linear_name(name)
+        if not isinstance(mod, nn.Linear) or cname not in target_names or cname not in act_cache:
+            continue
+        sub = nn.Module()
+        sub.add_module("lin", mod)
+        one = measure_batched_gpu(sub, _Renamed(act_cache, cname), {"lin"}, specs, device, dtype, 1,
+                                  _Renamed(h_detail, cname) if h_detail is not None else None)
+        for fmt, entry in one.get("lin", {}).items():
+            if "error" in entry:
+                accum.setdefault(cname, {})[fmt] = entry
+            else:
+                _accumulate_result(accum, cname, fmt, entry["weight_mse"], entry["output_mse"],
+                                   entry["rel_output_mse"], entry.get("predicted_dloss"))
+    return _finalize_results(accum)
+
+
+class _Renamed:
+    def __init__(self, index, real_name):
+        self.index, self.real = index, real_name
+
+    def __contains__(self, name):
+        return self.real in self.index
+
+    def load(self, name):
+        return self.index.load(self.real)
+
+
+_PACKED_EXPERT_PARAM_NAMES = {"gate_up_proj", "down_proj", "w1", "w2", "w3", "gate_proj", "up_proj"}
+
+
+def _is_packed_experts_module(module: nn.Module) -> bool:
+    """sensitivity_probe.py:507-530: class name contains "expert" and it owns a
+    3-D parameter with a known packed-expert name."""
+    if "expert" not in type(module).__name__.lower():
+        return False
+    return any(p.dim() == 3 and n in _PACKED_EXPERT_PARAM_NAMES for n, p in module.named_parameters(recurse=False))
+
+
+def _packed_experts_param_names(module: nn.Module) -> list[str]:
+    return sorted(n for n, p in module.named_parameters(recurse=False)
+                  if p.dim() == 3 and n in _PACKED_EXPERT_PARAM_NAMES)
+
+
+def _enumerate_packed_experts(model: nn.Module, target_names: set[str]):
+    out = []
+    for qname, mod in model.named_modules():
+        if not _is_packed_experts_module(mod):
+            continue
+        for pn in _packed_experts_param_names(mod):
+            full = f"{qname}.{pn}" if qname else pn
+            if full in target_names:
+                out.append((full, getattr(mod, pn)))
+    return out
+
+
+def _measure_packed_experts(model: nn.Module, target_names: set[str], specs: list[fr.FormatSpec], device: str,
+                            dtype: torch.dtype, accum: dict, h_detail=None) -> None:
+    """measure_quant_cost.py:381-449: weight_mse of every packed [E, M, N]
+    parameter for every spec in one fused pass (output_mse recorded as 0)."""
+    dev = torch.device(device)
+    entries = _enumerate_packed_experts(model, target_names)
+    if not entries:
+        return
+    ws = [p.detach().to(device=dev, dtype=dtype) for _, p in entries]
+    res = sweep_weight_mse([(n, w) for (n, _), w in zip(entries, ws)], specs)
+    for (name, _), w in zip(entries, ws):
+        h_em = None
+        if h_detail is not None and name in h_detail:
+            h = h_detail.load(name).to(dev).float()
+            if tuple(h.shape) == (w.size(0), w.size(1)):
+                h_em = h
+        for spec in specs:
+            v = res[name][spec.name]
+            if isinstance(v, dict):
+                accum.setdefault(name, {})[spec.name] = v
+                continue
+            dl = None
+            if h_em is not None:
+                err = (w - _batched_quantize(spec, w)).float()
+                dl = float(0.5 * (h_em * err.pow(2).mean(dim=-1)).sum().item() * err.size(-1))
+            _accumulate_result(accum, name, spec.name, float(v), 0.0, 0.0, predicted_dloss=dl)
+
+
+def measure_weight_costs(model: nn.Module, target_names: set[str], specs: list[fr.FormatSpec],
+                         device: str = "cuda", dtype: torch.dtype = torch.bfloat16) -> dict:
+    """Whole-model weight-error table in one fused pass: every target Linear
+    and packed-expert tensor, every spec.  Entries carry weight_mse (what the
+    allocator consumes when no predicted_dloss is present,
+    allocator_candidates.py:120-131) and zero output_mse / rel_output_mse."""
+    dev = torch.device(device)
+    named = []
+    for name, mod in model.named_modules():
+        cname = canonical_linear_name(name)
+        if isinstance(mod, nn.Linear) and cname in target_names:
+            named.append((cname, mod.weight.detach().to(device=dev, dtype=dtype)))
+    named += [(n, p.detach().to(device=dev, dtype=dtype)) for n, p in _enumerate_packed_experts(model, target_names)]
+    res = sweep_weight_mse(named, specs)
+    accum: dict = {}
+    for name, per in res.items():
+        for fmt, v in per.items():
+            if isinstance(v, dict):
+                accum.setdefault(name, {})[fmt] = v
+            else:
+                _accumulate_result(accum, name, fmt, float(v), 0.0, 0.0)
+    return _finalize_results(accum)

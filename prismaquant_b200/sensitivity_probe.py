@@ -1,0 +1,348 @@
+"""Fisher-trace statistics on B200.
+
+Drop-in for the hot path of prismaquant/sensitivity_probe.py:
+  * `_GradNormCapture` (:413-504): identity forward; backward reduces the
+    packed-expert weight gradient to sum(g^2) and the [E, M] channel diagonal
+    with one HBM pass (pq_sumsq_rows) into DEVICE accumulators, where the
+    reference syncs once per 1M-element chunk and copies [E, M] to the host
+    every backward.
+  * `install_packed_expert_hooks` (:555-728), same patching and metadata.
+  * `FisherAccumulator` (:959-1241) with the per-token estimator
+        h_trace_raw += sum_t ||x_t||^2 ||g_t||^2
+    — forward hook keeps ||x_t||^2 (T floats) instead of X, backward hook
+    reduces ||g_t||^2 against it — replacing grad_w = gy^T x followed by
+    sum(grad_w^2) (:1115-1152).  It equals the reference when one token flows
+    through each backward and is the per-token (diagonal-in-t) empirical
+    Fisher otherwise.  Packed experts either keep the reference's weight-grad
+    norm (`packed_estimator="grad_norm"`) or use the same per-token estimator
+    over each expert's routed tokens (`packed_estimator="per_token"`).
+All accumulators stay on the device; `finalize` does one device->host copy.
+"""
+from __future__ import annotations
+
+import re
+from collections import defaultdict
+from pathlib import Path
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+from .measure_quant_cost import _PACKED_EXPERT_PARAM_NAMES, _is_packed_experts_module, _packed_experts_param_names
+
+
+def _device_acc(store: dict, name: str, device, shape=(1,), dtype=torch.float64) -> torch.Tensor:
+    """Accumulator tensor for `name`; a prior python float in the dict is folded in."""
+    cur = store.get(name)
+    if isinstance(cur, torch.Tensor) and cur.device == device and cur.dtype == dtype and tuple(cur.shape) == tuple(shape):
+        return cur
+    t = torch.zeros(shape, dtype=dtype, device=device)
+    if isinstance(cur, torch.Tensor):
+        t += cur.to(device=device, dtype=dtype).reshape(shape)
+    elif cur is not None:
+        t += float(cur)
+    store[name] = t
+    return t
+
+
+class _GradNormCapture(torch.autograd.Function):
+    """sensitivity_probe.py:413-504.  Accumulators are device tensors: the
+    scalar one a [1] float64 (float() of it gives the reference's number), the
+    channel one [E, M] float32."""
+
+    @staticmethod
+    def forward(ctx, weight, name, scalar_accumulator, channel_accumulator, full_accumulator):
+        ctx.name = name
+        ctx.scalar_acc = scalar_accumulator
+        ctx.channel_acc = channel_accumulator
+        ctx.full_acc = full_accumulator
+        return weight
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        if grad_output is None:
+            return None, None, None, None, None
+        if ctx.full_acc is not None:
+            raise NotImplementedError("the per-weight [E, M, N] Fisher accumulator is not on the B200 path")
+        g = grad_output.detach()
+        total = _device_acc(ctx.scalar_acc, ctx.name, g.device)
+        per_row = None
+        if ctx.channel_acc is not None and g.dim() in (2, 3):
+            per_row = _device_acc(ctx.channel_acc, ctx.name, g.device, tuple(g.shape[:-1]), torch.float32)
+        _lib.sumsq_rows(g, total, per_row)
+        return None, None, None, None, None
+
+
+class _TokenNormCapture(torch.autograd.Function):
+    """Identity on a Linear's output y; backward adds sum_t xnorm[t] * ||dy_t||^2
+    (and the token count) into `acc` without touching the gradient."""
+
+    @staticmethod
+    def forward(ctx, y, xnorm, acc):
+        ctx.save_for_backward(xnorm)
+        ctx.acc = acc
+        return y.view_as(y)
+
+    @staticmethod
+    def backward(ctx, gy):
+        (xnorm,) = ctx.saved_tensors
+        _lib.tokennorm_dot(gy.detach().reshape(-1, gy.shape[-1]), xnorm, ctx.acc)
+        return gy, None, None
+
+
+_PATCH = "_prismaquant_packed_expert_patch"
+_CHANNEL = "_prismaquant_packed_expert_channel_patch"
+_FULL = "_prismaquant_packed_expert_full_patch"
+
+
+def _packed_meta(qname: str, pn: str, p: torch.Tensor) -> dict:
+    shape = tuple(p.shape)
+    return {"h_trace_raw": 0.0, "h_w2_sum_raw": 0.0, "w_max_abs": None if p.is_meta else float(p.detach().abs().max()),
+            "w_norm_sq": None if p.is_meta else float(p.detach().float().pow(2).sum()),
+            "n_params": int(p.numel()), "in_features": int(shape[2]), "out_features": int(shape[1]),
+            "num_experts": int(shape[0]), "n_tokens_seen": 0, "route_prob": None, "router_path": None,
+            "expert_id": None, "_packed_experts_module": qname, "_packed_param": pn}
+
+
+def install_packed_expert_hooks(model: nn.Module, accumulator: dict, channel_accumulator: dict | None = None,
+                                full_accumulator: dict | None = None) -> dict[str, dict]:
+    """Route every packed-experts parameter through _GradNormCapture
+    (sensitivity_probe.py:555-728); idempotent re-binding of accumulators."""
+    meta = {}
+    for qname, module in model.named_modules():
+        if not _is_packed_experts_module(module):
+            continue
+        names = _packed_experts_param_names(module)
+        for pn in names:
+            p = module._parameters.get(pn)
+            if p is not None:
+                meta[f"{qname}.{pn}" if qname else pn] = _packed_meta(qname, pn, p)
+        already = hasattr(module, _PATCH)
+        setattr(module, _PATCH, accumulator)
+        setattr(module, _CHANNEL, channel_accumulator)
+        setattr(module, _FULL, full_accumulator)
+        if already:
+            continue
+        for pn in names:
+            getattr(module, pn).requires_grad_(True)
+        original = module.forward
+        fulls = [f"{qname}.{pn}" if qname else pn for pn in names]
+
+        def patched(*args, _ns=tuple(names), _full=tuple(fulls), _orig=original, _mod=module, **kwargs):
+            acc = getattr(_mod, _PATCH, None)
+            if acc is None:
+                return _orig(*args, **kwargs)
+            ch, fu = getattr(_mod, _CHANNEL, None), getattr(_mod, _FULL, None)
+            saved = {}
+            for pn, fn in zip(_ns, _full):
+                saved[pn] = _mod._parameters.pop(pn)
+                _mod.__dict__[pn] = _GradNormCapture.apply(saved[pn], fn, acc, ch, fu)
+            try:
+                return _orig(*args, **kwargs)
+            finally:
+                for pn in _ns:
+                    _mod.__dict__.pop(pn, None)
+                    _mod._parameters[pn] = saved[pn]
+
+        module.forward = patched
+    return meta
+
+
+def install_routed_expert_hooks(model: nn.Module, accumulator: dict) -> dict[str, dict]:
+    """Per-token estimator for packed experts with gate_up_proj [E, 2I, H] /
+    down_proj [E, H, I] (HF Qwen3MoeExperts layout): the experts forward is
+    re-expressed as the same routed loop (token_idx per expert, act(gate)*up,
+    routing-weighted index_add) with ||x_t||^2 / ||dy_t||^2 captured around
+    each expert's two projections.  accumulator[name] is a [E, 2] float64
+    device tensor (trace, tokens) per packed parameter."""
+    meta = {}
+    for qname, module in model.named_modules():
+        if not _is_packed_experts_module(module):
+            continue
+        if not (hasattr(module, "gate_up_proj") and hasattr(module, "down_proj") and hasattr(module, "act_fn")):
+            continue
+        gu_name, dn_name = f"{qname}.gate_up_proj", f"{qname}.down_proj"
+        for pn in ("gate_up_proj", "down_proj"):
+            meta[f"{qname}.{pn}"] = _packed_meta(qname, pn, getattr(module, pn))
+        E = module.gate_up_proj.shape[0]
+        dev = module.gate_up_proj.device
+        acc_gu = _device_acc(accumulator, gu_name, dev, (E, 2))
+        acc_dn = _device_acc(accumulator, dn_name, dev, (E, 2))
+
+        def routed(hidden_states, top_k_index, top_k_weights, _m=module, _gu=acc_gu, _dn=acc_dn):
+            final = torch.zeros_like(hidden_states)
+            with torch.no_grad():
+                mask = F.one_hot(top_k_index, num_classes=_m.gate_up_proj.shape[0]).permute(2, 1, 0)
+                hit = torch.greater(mask.sum(dim=(-1, -2)), 0).nonzero()
+            for e in hit.flatten().tolist():
+                top_k_pos, token_idx = torch.where(mask[e])
+                x = hidden_states[token_idx]
+                gu = _TokenNormCapture.apply(F.linear(x, _m.gate_up_proj[e]), _lib.rownorm2(x.detach()), _gu[e])
+                gate, up = gu.chunk(2, dim=-1)
+                h = _m.act_fn(gate) * up
+                out = _TokenNormCapture.apply(F.linear(h, _m.down_proj[e]), _lib.rownorm2(h.detach()), _dn[e])
+                out = out * top_k_weights[token_idx, top_k_pos, None]
+                final.index_add_(0, token_idx, out.to(final.dtype))
+            return final
+
+        module.forward = routed
+    return meta
+
+
+class FisherAccumulator:
+    """sensitivity_probe.py:959-1241 with the per-token estimator and device accumulators."""
+
+    def __init__(self, model: nn.Module, tracked: list[str], expert_info: dict[str, tuple[str, str]],
+                 act_cache_dir: Path | None = None, input_rows: int = 256, hook_packed_experts: bool = True,
+                 h_detail_dir: Path | None = None, packed_estimator: str = "grad_norm"):
+        if h_detail_dir is not None:
+            raise NotImplementedError("per-weight Fisher detail needs grad_w = gy^T x (a GEMM); not on the B200 path")
+        self.stats: dict[str, dict] = {}
+        self.tracked = set(tracked)
+        self.expert_info = expert_info
+        self.cache_dir = Path(act_cache_dir) if act_cache_dir else None
+        self.input_rows = input_rows
+        self._fwd_handles, self._bwd_handles = [], []
+        self._xnorm: dict[str, torch.Tensor] = {}
+        self._input_snaps: dict[str, list[torch.Tensor]] = defaultdict(list)
+        self._rows_got: dict[str, int] = defaultdict(int)
+        self._packed_grad_acc: dict = {}
+        self._h_packed_channel: dict = {}
+        self._packed_sample_count: dict[str, torch.Tensor] = {}
+        self._names: list[str] = []
+        lin = [(n, m) for n, m in model.named_modules() if n in self.tracked and isinstance(m, nn.Linear)]
+        dev = lin[0][1].weight.device if lin else torch.device("cuda")
+        # one [n, 2] fp64 accumulator (raw trace, tokens) per tracked Linear
+        self._acc = torch.zeros(len(lin), 2, dtype=torch.float64, device=dev)
+        wstats = []
+        for i, (name, mod) in enumerate(lin):
+            self._names.append(name)
+            router, eid = expert_info.get(name, (None, None))
+            w = mod.weight.detach()
+            wstats.append(torch.stack([w.abs().max().float(), w.float().pow(2).sum()]))
+            self.stats[name] = {"h_trace_raw": 0.0, "h_w2_sum_raw": 0.0, "w_max_abs": None, "w_norm_sq": None,
+                                "n_params": int(w.numel()), "in_features": mod.in_features,
+                                "out_features": mod.out_features, "n_tokens_seen": 0, "route_prob": None,
+                                "router_path": router, "expert_id": eid}
+            self._fwd_handles.append(mod.register_forward_hook(self._make_fwd(name)))
+            self._bwd_handles.append(mod.register_full_backward_hook(self._make_bwd(name, i)))
+        if wstats:
+            host = torch.stack(wstats).cpu().tolist()   # one sync for every Linear's weight stats
+            for (name, _), (mx, n2) in zip(lin, host):
+                self.stats[name]["w_max_abs"], self.stats[name]["w_norm_sq"] = mx, n2
+        self.packed_estimator = packed_estimator
+        if hook_packed_experts:
+            if packed_estimator == "grad_norm":
+                meta = install_packed_expert_hooks(model, self._packed_grad_acc, self._h_packed_channel)
+            elif packed_estimator == "per_token":
+                meta = install_routed_expert_hooks(model, self._packed_grad_acc)
+            else:
+                raise ValueError(f"unknown packed_estimator {packed_estimator!r}")
+            for full, m in meta.items():
+                qn = m.pop("_packed_experts_module")
+                m.pop("_packed_param", None)
+                layer = ".".join(qn.split(".")[:3])
+                if any(t.startswith(layer + ".") for t in self.tracked):
+                    self.stats[full] = m
+                    mod = model.get_submodule(qn)
+                    cnt = self._packed_sample_count.setdefault(
+                        full, torch.zeros(1, dtype=torch.int64, device=dev))
+
+                    def _exp_fwd(_m, inp, _out, _c=cnt):
+                        x = inp[0] if isinstance(inp, tuple) else inp
+                        if isinstance(x, torch.Tensor):
+                            _c += x.reshape(-1, x.size(-1)).size(0)
+                    self._fwd_handles.append(mod.register_forward_hook(_exp_fwd))
+
+    def _make_fwd(self, name: str):
+        def hook(module, inp, out):
+            x = inp[0] if isinstance(inp, tuple) else inp
+            x2 = x.detach().reshape(-1, x.size(-1))
+            self._xnorm[name] = _lib.rownorm2(x2)
+            if self.cache_dir is not None:
+                need = self.input_rows - self._rows_got[name]
+                if need > 0:
+                    flat = x2
+                    if flat.size(0) > need:
+                        flat = flat.index_select(0, torch.randperm(flat.size(0), device=flat.device)[:need])
+                    self._input_snaps[name].append(flat.to("cpu"))
+                    self._rows_got[name] += flat.size(0)
+        return hook
+
+    def _make_bwd(self, name: str, idx: int):
+        def hook(module, grad_input, grad_output):
+            gy = grad_output[0]
+            xn = self._xnorm.pop(name, None)
+            if xn is None or gy is None:
+                return
+            _lib.tokennorm_dot(gy.reshape(-1, gy.size(-1)), xn, self._acc[idx])
+        return hook
+
+    @property
+    def trace_buffer(self) -> torch.Tensor:
+        """[n_linears, 2] float64 (raw trace, tokens): what a data-parallel run all-reduces."""
+        return self._acc
+
+    def finalize(self, tracker=None):
+        host = self._acc.cpu().tolist()
+        for name, (tr, tok) in zip(self._names, host):
+            self.stats[name]["h_trace_raw"] += tr
+            self.stats[name]["n_tokens_seen"] += int(round(tok))
+        for full, raw in self._packed_grad_acc.items():
+            if full not in self.stats:
+                continue
+            if isinstance(raw, torch.Tensor) and raw.dim() == 2:   # per-token routed [E, 2]
+                self.stats[full]["h_trace_raw"] += float(raw[:, 0].sum())
+                self.stats[full]["expert_trace_raw"] = raw[:, 0].cpu().tolist()
+            else:
+                self.stats[full]["h_trace_raw"] += float(raw)
+            self.stats[full]["n_tokens_seen"] = int(self._packed_sample_count.get(full, torch.zeros(1)).item())
+        if tracker is not None:
+            for s in self.stats.values():
+                if s["router_path"]:
+                    s["route_prob"] = tracker.prob(s["router_path"], s["expert_id"])
+        for s in self.stats.values():
+            tokens = max(s["n_tokens_seen"], 1)
+            rp = s["route_prob"]
+            div = tokens * rp if (rp is not None and rp > 0) else tokens
+            s["h_trace"] = s["h_trace_raw"] / div
+            s["h_w2_sum"] = s["h_w2_sum_raw"] / div
+        if self.cache_dir is not None:
+            self.cache_dir.mkdir(parents=True, exist_ok=True)
+            for name, snaps in self._input_snaps.items():
+                if snaps:
+                    X = torch.cat(snaps).to(torch.bfloat16).contiguous()
+                    torch.save({"inputs": X, "name": name},
+                               self.cache_dir / (re.sub(r"[^A-Za-z0-9_-]", "__", name) + ".pt"))
+
+    def remove_hooks(self):
+        for h in self._fwd_handles + self._bwd_handles:
+            h.remove()
+        self._fwd_handles.clear()
+        self._bwd_handles.clear()
+
+
+def probe_pass(model: nn.Module, calib: torch.Tensor, tracked: list[str], batch_size: int = 1,
+               acc: FisherAccumulator | None = None, all_reduce=None) -> FisherAccumulator:
+    """The probe loop of run_probe_pass (sensitivity_probe.py:1509-1576): per
+    batch of calibration sequences, sum-reduced next-token cross entropy and
+    one backward; the hooks accumulate on the device.  `all_reduce`, if
+    given, is called on the trace buffer before finalize (data parallel)."""
+    if acc is None:
+        acc = FisherAccumulator(model, tracked, {})
+    model.train()
+    emb = model.get_input_embeddings()
+    for i in range(0, calib.size(0), batch_size):
+        ids = calib[i:i + batch_size].to(emb.weight.device)
+        with torch.no_grad():
+            e = emb(ids)
+        e.requires_grad_(True)
+        logits = model(inputs_embeds=e).logits
+        lp = F.log_softmax(logits[:, :-1].reshape(-1, logits.size(-1)).float(), dim=-1)
+        loss = -lp.gather(1, ids[:, 1:].reshape(-1, 1)).sum()
+        loss.backward()
+        acc._xnorm.clear()
+    if all_reduce is not None:
+        all_reduce(acc.trace_buffer)
+    return acc

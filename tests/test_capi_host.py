@@ -1,0 +1,176 @@
+"""CPU-side checks of the boundary and the host logic (no GPU needed)."""
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    text = (REPO / "include" / "prismaquant_b200.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(pq_\w+)\s*\(", text, re.M)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from prismaquant_b200 import _lib
+    lib = _lib.load()
+    syms = declared_symbols()
+    assert len(syms) >= 14
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(_lib.EXPORTED) == set(syms)
+    assert lib.pq_version() >= 1
+    assert lib.pq_status_string(2) == b"shape not divisible by the format's group size"
+
+
+def test_struct_layout_matches_header():
+    from prismaquant_b200 import _lib
+    assert ctypes.sizeof(_lib.SweepTensor) == 56
+    assert _lib.SweepTensor.nvfp4_codes.offset == 32
+
+
+def test_argument_validation_without_gpu():
+    """Shape / null checks happen before any CUDA call."""
+    from prismaquant_b200 import _lib
+    lib = _lib.load()
+    assert lib.pq_mxfp8_pack(None, 4, 48, None, None, None) == _lib.PQ_ERR_SHAPE
+    assert lib.pq_nvfp4_codes(None, 1, 4, 40, None, None, None, None) == _lib.PQ_ERR_SHAPE
+    assert lib.pq_cost_qdq(None, 4, 64, 9, None, None) == _lib.PQ_ERR_FORMAT
+    assert lib.pq_sumsq_rows(None, 4, 64, None, None, None) == _lib.PQ_ERR_NULL
+    assert lib.pq_sweep_sse(None, 0, None, None) == _lib.PQ_OK
+    arr = (_lib.SweepTensor * 1)()
+    arr[0].rows, arr[0].cols, arr[0].fmt_mask = 4, 48, 1 << _lib.FMT_MXFP8
+    arr[0].w = 16
+    assert lib.pq_sweep_sse(arr, 1, ctypes.c_void_p(16), None) == _lib.PQ_ERR_SHAPE
+    arr[0].fmt_mask = 1 << 7
+    assert lib.pq_sweep_sse(arr, 1, ctypes.c_void_p(16), None) == _lib.PQ_ERR_FORMAT
+    assert lib.pq_nvfp4_scales(300, None, None, None, None, None, None, None, None) == _lib.PQ_ERR_LIMIT
+
+
+def test_cuda_calls_fail_loudly_on_cpu_tensors():
+    import torch
+    from prismaquant_b200 import format_registry as fr
+    with pytest.raises(RuntimeError):
+        fr.get_format("NVFP4").quantize_dequantize(torch.zeros(4, 16, dtype=torch.bfloat16))
+
+
+def test_e8m0_table_header_matches_oracle():
+    from oracle import pq_oracle as O
+    text = (REPO / "prismaquant_b200" / "csrc" / "pq_e8m0_tables.h").read_text()
+    def arr(name):
+        body = re.search(name + r"\[\d+\] = \{([^}]*)\}", text).group(1)
+        return [int(v) for v in body.replace("\n", " ").split(",") if v.strip()]
+    ceil_last, round_first = arr("PQ_CEIL_LAST"), arr("PQ_ROUND_FIRST")
+    t = O.e8m0()
+    assert ceil_last == [t.ceil_last[k] for k in range(-127, 128)]
+    assert round_first == [t.round_first[k] for k in range(-126, 128)]
+
+
+def test_format_registry_metadata_matches_reference_formats():
+    from prismaquant_b200 import format_registry as fr
+    shape = (128, 128)
+    assert fr.get_format("NVFP4").effective_bits_for_shape(shape) == pytest.approx(4.5)
+    assert fr.get_format("MXFP8").effective_bits_for_shape(shape) == pytest.approx(8.25)
+    assert fr.get_format("BF16").effective_bits_for_shape(shape) == pytest.approx(16.0)
+    spec = fr.get_format("FP8_E4M3")
+    assert spec.scale_count_for_shape((5, 7)) == 5
+    assert spec.memory_bytes_for_shape((5, 7)) == 5 * 7 + 5 * 4
+    with pytest.raises(KeyError):
+        fr.get_format("NOPE")
+
+
+def test_cost_schema_roundtrip():
+    from prismaquant_b200 import measure_quant_cost as mqc
+    b = {}
+    mqc._accumulate_result(b, "x", "NVFP4", 2.0, 1.0, 0.5, predicted_dloss=3.0)
+    mqc._accumulate_result(b, "x", "NVFP4", 4.0, 3.0, 1.5)
+    out = mqc._finalize_results(b)
+    assert out["x"]["NVFP4"] == {"weight_mse": 3.0, "output_mse": 2.0, "rel_output_mse": 1.0, "predicted_dloss": 3.0}
+    assert mqc.shape_error("MXFP8", 48) and mqc.shape_error("MXFP8", 16) is None
+    assert mqc.shape_error("NVFP4", 24) and mqc.shape_error("NVFP4", 8) is None
+    assert mqc.canonical_linear_name("m.mlp.experts.3.up_proj") == "m.mlp.experts.gate_up_proj.3"
+
+
+def test_cost_schema_matches_reference_validator():
+    """The cost table validates under the reference's own schema checker when it is importable."""
+    import sys
+    from tests.conftest import REFERENCE, reference_available
+    if not reference_available():
+        pytest.skip("reference checkout not present")
+    sys.path.insert(0, str(REFERENCE))
+    try:
+        from prismaquant import schemas
+    finally:
+        sys.path.remove(str(REFERENCE))
+    from prismaquant_b200 import measure_quant_cost as mqc
+    b = {}
+    mqc._accumulate_result(b, "model.layers.0.mlp.up_proj", "NVFP4", 1e-5, 0.0, 0.0)
+    table = {"costs": mqc._finalize_results(b), "formats": ["NVFP4"], "meta": {}}
+    fn = getattr(schemas, "validate_cost_payload", None)
+    if fn is None:
+        pytest.skip("reference has no cost validator")
+    fn(table)
+
+
+def test_sibling_keys_and_partition():
+    from prismaquant_b200 import export_native_compressed as enc
+    from prismaquant_b200 import distributed as D
+    from prismaquant_b200 import synthetic as S
+    assert enc.sibling_group_key("model.layers.3.self_attn.k_proj") == "model.layers.3.self_attn::qkv"
+    assert enc.sibling_group_key("model.layers.3.mlp.down_proj") is None
+    assert enc._fused_dense_group("model.layers.5.self_attn.q_proj")[0] == "model.layers.5"
+    lin = S.llama_dense_linears()
+    assert len(lin) == 32 * 7 + 1
+    assert sum(np.prod(s) for _, s in lin) == 7_504_658_432
+    sizes = [int(np.prod(s)) for _, s in lin]
+    keys = [enc.sibling_group_key(n) for n, _ in lin]
+    for world in (1, 2, 4, 8):
+        ranks = D.partition_units(sizes, world, keys)
+        loads = [sum(s for s, r in zip(sizes, ranks) if r == k) for k in range(world)]
+        assert max(loads) / (sum(sizes) / world) < 1.10
+        for k in set(x for x in keys if x):
+            assert len({r for r, kk in zip(ranks, keys) if kk == k}) == 1
+
+
+def _gloo_worker(rank, world, port, q):
+    import os
+    import torch
+    import torch.distributed as dist
+    from prismaquant_b200 import distributed as D
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n_units = 7
+        ranks = [u % world for u in range(n_units)]
+        ids = torch.tensor([u for u in range(n_units) if ranks[u] == rank])
+        sse = torch.stack([torch.arange(4, dtype=torch.float64) + 10 * u for u in ids.tolist()])
+        table = D.all_gather_costs(ids, sse, n_units, D.max_units_per_rank(ranks, world))
+        buf = torch.full((3, 2), float(rank + 1), dtype=torch.float64)
+        D.all_reduce_traces(buf)
+        q.put((rank, table.tolist(), buf.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_gather_and_reduce():
+    import multiprocessing as mp
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, table, buf in res:
+        assert table == [[10.0 * u + j for j in range(4)] for u in range(7)]
+        assert buf == [[3.0, 3.0]] * 3

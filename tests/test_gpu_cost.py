@@ -1,0 +1,103 @@
+"""Cost path on the GPU vs the reference (golden fixtures) and the oracle.
+
+Bar: quantize-dequantize reconstructions bit-exact; MSE_W within 1e-5
+relative (fp64 accumulation of fp32 squares vs the reference's fp32 mean)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import pq_oracle as O
+from prismaquant_b200 import format_registry as fr
+from prismaquant_b200 import measure_quant_cost as mqc
+from tests._helpers import assert_rel, bits_of, to_cuda_bf16
+
+pytestmark = pytest.mark.gpu
+
+CASES = ["rand_64x128", "rand_33x256", "ties_4x32", "zeros_3x64", "wide_range_8x96",
+         "row1_1x4096", "cols16_5x16", "cols48_7x48", "cols8_4x8", "packed_4x32x64", "packed_3x16x96"]
+FMTS = ["NVFP4", "MXFP8", "FP8_E4M3", "BF16"]
+
+
+@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("fmt", FMTS)
+def test_qdq_matches_reference(golden, case, fmt):
+    bits = golden[f"{case}/input"]
+    w = to_cuda_bf16(bits)
+    spec = fr.get_format(fmt)
+    key = f"{case}/cost/{fmt}"
+    if f"{key}/error" in golden:
+        with pytest.raises(ValueError):
+            spec.quantize_dequantize(w)
+        return
+    out = spec.quantize_dequantize(w) if w.dim() == 2 else mqc._batched_quantize(spec, w)
+    np.testing.assert_array_equal(bits_of(out), golden[f"{key}/qdq"])
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_fused_sweep_matches_reference(golden, case):
+    w = to_cuda_bf16(golden[f"{case}/input"])
+    specs = [fr.get_format(f) for f in FMTS]
+    res = mqc.sweep_weight_mse({"t": w}, specs)["t"]
+    for f in FMTS:
+        key = f"{case}/cost/{f}"
+        if f"{key}/error" in golden:
+            assert isinstance(res[f], dict) and "error" in res[f]
+        else:
+            assert_rel(res[f], float(golden[f"{key}/mse"][0]), 1e-5, f"{case} {f}")
+
+
+@pytest.mark.parametrize("shape,seed", [((512, 4096), 1), ((96, 14336), 2), ((4, 128, 768), 3),
+                                        ((1000, 1536), 4), ((3, 2048), 5), ((77, 48), 6), ((13, 24), 7)])
+def test_sweep_and_qdq_vs_oracle(shape, seed):
+    bits = O.synthetic_weight_bits(shape, seed=seed, outlier_frac=0.002)
+    w = to_cuda_bf16(bits)
+    specs = [fr.get_format(f) for f in FMTS]
+    res = mqc.sweep_weight_mse({"t": w}, specs)["t"]
+    for f in FMTS:
+        try:
+            ref_q = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, f))
+        except ValueError:
+            assert isinstance(res[f], dict)
+            continue
+        q = mqc._batched_quantize(fr.get_format(f), w)
+        np.testing.assert_array_equal(bits_of(q), ref_q, err_msg=f)
+        assert_rel(res[f], O.cost_mse(bits, f), 1e-5, f)
+
+
+def test_many_tensors_one_launch():
+    """Hundreds of tensors of mixed shapes in one sweep call (several launches
+    of the descriptor table) give the per-tensor oracle values."""
+    rng = np.random.default_rng(0)
+    shapes = [(int(rng.integers(1, 40)), int(rng.choice([16, 32, 64, 128, 256, 4096]))) for _ in range(400)]
+    bits = [O.synthetic_weight_bits(s, seed=100 + i) for i, s in enumerate(shapes)]
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3")]
+    res = mqc.sweep_weight_mse({str(i): to_cuda_bf16(b) for i, b in enumerate(bits)}, specs)
+    for i, b in enumerate(bits):
+        for s in specs:
+            assert_rel(res[str(i)][s.name], O.cost_mse(b, s.name), 1e-5, f"{i} {s.name} {shapes[i]}")
+
+
+def test_all_bf16_values_rtn():
+    """Every finite bf16 value, in rows whose amax fixes exact power-of-two
+    scales, goes through every format's rounding (ties, subnormals, saturation)."""
+    allv = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    f = O.bf16_bits_to_f32(allv)
+    vals = allv[np.isfinite(f) & (np.abs(f) < 1e30)]
+    vals = vals[: (vals.size // 256) * 256].reshape(-1, 256)
+    for fmt in ("NVFP4", "MXFP8", "FP8_E4M3"):
+        q = fr.get_format(fmt).quantize_dequantize(to_cuda_bf16(vals))
+        np.testing.assert_array_equal(bits_of(q), O.f32_to_bf16_bits(O.cost_qdq_f32(vals, fmt)), err_msg=fmt)
+
+
+def test_linear4096_digest(full_digests):
+    """Full single-Linear sweep (4096x4096, 0.1 % x20 outliers, seed 0) against
+    the reference's own outputs (SHA-256 of W_hat) and MSE_W."""
+    d = full_digests["linear4096"]
+    bits = O.synthetic_weight_bits((4096, 4096), seed=0, outlier_frac=0.001)
+    assert O.digest(bits) == d["input"], "synthetic generator differs on this host"
+    w = to_cuda_bf16(bits)
+    specs = [fr.get_format(f) for f in FMTS]
+    res = mqc.sweep_weight_mse({"w": w}, specs)["w"]
+    for f in FMTS:
+        assert O.digest(bits_of(fr.get_format(f).quantize_dequantize(w))) == d[f"qdq/{f}"], f
+        assert_rel(res[f], d[f"mse/{f}"], 1e-5, f)

@@ -1,0 +1,151 @@
+"""Export packing on the GPU vs the reference (golden fixtures, full-size
+digests) and the oracle.  Bar: bit-exact codes, scales and globals."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import pq_oracle as O
+from prismaquant_b200 import export_native_compressed as enc
+from prismaquant_b200 import format_registry as fr
+from prismaquant_b200 import measure_quant_cost as mqc
+from tests._helpers import assert_rel, to_cuda_bf16, u8_of
+
+pytestmark = pytest.mark.gpu
+
+CASES2D = ["rand_64x128", "rand_33x256", "ties_4x32", "zeros_3x64", "wide_range_8x96", "row1_1x4096",
+           "cols16_5x16", "cols48_7x48", "cols8_4x8"]
+
+
+def f32(t):
+    return t.detach().cpu().numpy()
+
+
+@pytest.mark.parametrize("case", CASES2D)
+def test_export_2d_matches_reference(golden, case):
+    w = to_cuda_bf16(golden[f"{case}/input"])
+    if f"{case}/nvfp4/packed" in golden:
+        p, s, g = enc.quantize_dequantize_nvfp4(w)
+        np.testing.assert_array_equal(u8_of(p), golden[f"{case}/nvfp4/packed"])
+        np.testing.assert_array_equal(u8_of(s), golden[f"{case}/nvfp4/scale"])
+        np.testing.assert_array_equal(f32(g), golden[f"{case}/nvfp4/global"])
+        assert s.dtype == torch.float8_e4m3fn and p.dtype == torch.uint8 and g.dtype == torch.float32
+        gr = enc.compute_nvfp4_global_real(w)
+        assert float(gr) == float(golden[f"{case}/nvfp4/global_real"][0])
+        ov = torch.tensor(float(golden[f"{case}/nvfp4_ovr/override"][0]))
+        p, s, g = enc.quantize_dequantize_nvfp4(w, global_real_override=ov)
+        np.testing.assert_array_equal(u8_of(p), golden[f"{case}/nvfp4_ovr/packed"])
+        np.testing.assert_array_equal(u8_of(s), golden[f"{case}/nvfp4_ovr/scale"])
+        np.testing.assert_array_equal(f32(g), golden[f"{case}/nvfp4_ovr/global"])
+        q = enc._quantize_2d(w, "NVFP4")
+        assert float(q["input_global_scale"]) == float(golden[f"{case}/q2d_nvfp4/input_global_scale"][0])
+    else:
+        with pytest.raises(ValueError):
+            enc.quantize_dequantize_nvfp4(w)
+    if f"{case}/mxfp8/weight" in golden:
+        q, sc = enc.quantize_dequantize_mxfp8(w)
+        np.testing.assert_array_equal(u8_of(q), golden[f"{case}/mxfp8/weight"])
+        np.testing.assert_array_equal(u8_of(sc), golden[f"{case}/mxfp8/scale"])
+    q, sc = enc.quantize_dequantize_fp8_dynamic(w)
+    np.testing.assert_array_equal(u8_of(q), golden[f"{case}/fp8dyn/weight"])
+    np.testing.assert_array_equal(f32(sc), golden[f"{case}/fp8dyn/scale"])
+
+
+@pytest.mark.parametrize("case", ["packed_4x32x64", "packed_3x16x96"])
+def test_export_packed_matches_reference(golden, case):
+    w = to_cuda_bf16(golden[f"{case}/input"])
+    p, s, g = enc.quantize_dequantize_nvfp4_packed(w)
+    np.testing.assert_array_equal(u8_of(p), golden[f"{case}/nvfp4p/packed"])
+    np.testing.assert_array_equal(u8_of(s), golden[f"{case}/nvfp4p/scale"])
+    np.testing.assert_array_equal(f32(g), golden[f"{case}/nvfp4p/global"])
+    q, sc = enc.quantize_dequantize_mxfp8_packed(w)
+    np.testing.assert_array_equal(u8_of(q), golden[f"{case}/mxfp8p/weight"])
+    np.testing.assert_array_equal(u8_of(sc), golden[f"{case}/mxfp8p/scale"])
+    gq = enc._quantize_2d_group_same_shape(w, "MXFP8")
+    np.testing.assert_array_equal(u8_of(gq["weight"]), golden[f"{case}/grouped_mxfp8/weight"])
+    q, sc = enc.quantize_dequantize_fp8_dynamic_packed(w)
+    np.testing.assert_array_equal(u8_of(q), golden[f"{case}/fp8dynp/weight"])
+    np.testing.assert_array_equal(f32(sc), golden[f"{case}/fp8dynp/scale"])
+
+
+@pytest.mark.parametrize("shape,seed,std", [((512, 4096), 1, 0.02), ((64, 14336), 2, 0.02), ((8, 64, 768), 3, 0.02),
+                                            ((257, 2048), 4, 1e-20), ((33, 1024), 5, 1e20)])
+def test_export_vs_oracle(shape, seed, std):
+    bits = O.synthetic_weight_bits(shape, seed=seed, std=std, outlier_frac=0.001)
+    w = to_cuda_bf16(bits)
+    wf = O.bf16_bits_to_f32(bits)
+    ref = O.nvfp4_pack(wf) if len(shape) == 2 else O.nvfp4_pack_packed(wf)
+    got = enc.quantize_dequantize_nvfp4(w) if len(shape) == 2 else enc.quantize_dequantize_nvfp4_packed(w)
+    for r, g in zip(ref, got):
+        np.testing.assert_array_equal(u8_of(g) if g.dtype != torch.float32 else f32(g), r)
+    q, sc = enc.quantize_dequantize_mxfp8(w)
+    rq, rsc = O.mxfp8_pack(wf)
+    np.testing.assert_array_equal(u8_of(q), rq)
+    np.testing.assert_array_equal(u8_of(sc), rsc)
+    q, sc = enc.quantize_dequantize_fp8_dynamic(w)
+    rq, rsc = O.fp8_dynamic_pack(wf)
+    np.testing.assert_array_equal(u8_of(q), rq)
+    np.testing.assert_array_equal(f32(sc), rsc)
+
+
+def test_linear4096_export_digests(full_digests):
+    d = full_digests["linear4096"]
+    bits = O.synthetic_weight_bits((4096, 4096), seed=0, outlier_frac=0.001)
+    w = to_cuda_bf16(bits)
+    p, s, g = enc.quantize_dequantize_nvfp4(w)
+    assert O.digest(u8_of(p), u8_of(s), f32(g)) == d["nvfp4"]
+    q, sc = enc.quantize_dequantize_mxfp8(w)
+    assert O.digest(u8_of(q), u8_of(sc)) == d["mxfp8"]
+    q, sc = enc.quantize_dequantize_fp8_dynamic(w)
+    assert O.digest(u8_of(q), f32(sc)) == d["fp8dyn"]
+
+
+def test_fused_siblings_joint_global(full_digests):
+    """q/k/v and gate/up share one NVFP4 global (max of their natural ones);
+    fused sweep + export in one pass reproduces the reference's packed bytes
+    and MSE_W for every sibling."""
+    dg = full_digests["siblings"]
+    names = list(dg)
+    prefix = {"q_proj": "model.layers.0.self_attn.", "k_proj": "model.layers.0.self_attn.",
+              "v_proj": "model.layers.0.self_attn.", "gate_proj": "model.layers.0.mlp.",
+              "up_proj": "model.layers.0.mlp."}
+    ws = {}
+    for n in names:
+        bits = O.synthetic_weight_bits(tuple(dg[n]["shape"]), seed=dg[n]["seed"])
+        assert O.digest(bits) == dg[n]["input"]
+        ws[prefix[n] + n] = to_cuda_bf16(bits)
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3", "BF16")]
+    costs, outs = enc.sweep_and_export(ws, specs)
+    for full, n in zip(ws, names):
+        p, s, g = outs[full]
+        assert O.digest(u8_of(p), u8_of(s), f32(g)) == dg[n]["nvfp4"], n
+        for f in ("NVFP4", "MXFP8", "FP8_E4M3", "BF16"):
+            assert_rel(costs[full][f], dg[n][f"mse/{f}"], 1e-5, f"{n} {f}")
+    # same bytes through the one-tensor API with the joint override
+    for full, n in zip(ws, names):
+        p, s, g = enc.quantize_dequantize_nvfp4(ws[full], global_real_override=torch.tensor(dg[n]["joint_global_real"]))
+        assert O.digest(u8_of(p), u8_of(s), f32(g)) == dg[n]["nvfp4"], n
+
+
+def test_fused_sweep_export_equals_separate():
+    bits = [O.synthetic_weight_bits(s, seed=40 + i) for i, s in enumerate([(256, 4096), (128, 14336), (96, 1024)])]
+    ws = {f"model.layers.0.mlp.x{i}": to_cuda_bf16(b) for i, b in enumerate(bits)}
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3")]
+    costs, outs = enc.sweep_and_export(ws, specs)
+    sep = mqc.sweep_weight_mse(ws, specs)
+    for k, w in ws.items():
+        for f in ("NVFP4", "MXFP8", "FP8_E4M3"):
+            assert costs[k][f] == sep[k][f]
+        p, s, g = enc.quantize_dequantize_nvfp4(w)
+        torch.testing.assert_close(outs[k][0], p, rtol=0, atol=0)
+        assert torch.equal(outs[k][1].view(torch.uint8), s.view(torch.uint8))
+        assert torch.equal(outs[k][2], g)
+
+
+def test_shape_errors_raise():
+    w = torch.zeros(4, 40, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        enc.quantize_dequantize_nvfp4(w)
+    with pytest.raises(ValueError):
+        enc.quantize_dequantize_mxfp8(w)
+    with pytest.raises(ValueError):
+        fr.get_format("MXFP8").quantize_dequantize(torch.zeros(4, 48, dtype=torch.bfloat16, device="cuda"))
