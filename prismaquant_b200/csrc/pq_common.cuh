@@ -79,13 +79,15 @@ __device__ __forceinline__ float grid_round_abs(float a, bool tie_up, float maxv
 
 // Cost-path RTN on the signed codebook with ties to the LOWER value
 // (format_registry.py:224-230): for x < 0 the lower value has the larger magnitude.
+// The codebook holds only +0.0, so a negative x that rounds to zero gives +0.0
+// (0 - r, not -r).
 __device__ __forceinline__ float rtn_e2m1_cost(float x) {
   const float r = grid_round_abs<1, 0>(fabsf(x), x < 0.0f, 6.0f);
-  return x < 0.0f ? -r : r;
+  return x < 0.0f ? __fsub_rn(0.0f, r) : r;
 }
 __device__ __forceinline__ float rtn_e4m3_cost(float x) {
   const float r = grid_round_abs<3, -6>(fabsf(x), x < 0.0f, 448.0f);
-  return x < 0.0f ? -r : r;
+  return x < 0.0f ? __fsub_rn(0.0f, r) : r;
 }
 
 // Export-path NVFP4 code: |x| rounded on {0,.5,1,1.5,2,3,4,6} with ties toward

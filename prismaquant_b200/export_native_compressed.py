@@ -46,7 +46,9 @@ def compute_nvfp4_global_real(weight: torch.Tensor, group_size: int = 16) -> tor
         raise ValueError(f"NVFP4 group_size={group_size} ∤ {cols}")
     w = _lib.as_bf16_cuda(weight, "compute_nvfp4_global_real")
     m = w.abs().amax().float().clamp_min(1e-12)
-    return (m / NVFP4_MAX / FP8_E4M3_MAX).clamp_min(1e-12)
+    # tensor / tensor is an IEEE division on CUDA (tensor / python-scalar multiplies by a reciprocal)
+    six, fp8max = torch.full_like(m, NVFP4_MAX), torch.full_like(m, FP8_E4M3_MAX)
+    return torch.div(torch.div(m, six), fp8max).clamp_min(1e-12)
 
 
 def quantize_dequantize_nvfp4(weight: torch.Tensor, group_size: int = 16,

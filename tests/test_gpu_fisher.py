@@ -36,7 +36,7 @@ def test_rownorm_and_tokennorm_vs_oracle(shape):
     acc = torch.zeros(2, dtype=torch.float64, device="cuda")
     _lib.tokennorm_dot(g, xn, acc)
     ref = float(np.dot(xn.cpu().numpy().astype(np.float64), O.rownorm2(gb)))
-    assert_rel(float(acc[0]), ref, 1e-9)
+    assert_rel(float(acc[0]), ref, 1e-6)
     assert_rel(float(acc[0]), O.tokennorm_trace(xb, gb), 1e-5)
     assert float(acc[1]) == T
 
@@ -58,7 +58,7 @@ def test_sumsq_rows_vs_oracle(shape):
     per_row = torch.zeros(shape[:-1], dtype=torch.float32, device="cuda")
     _lib.sumsq_rows(to_cuda_bf16(gb), total, per_row)
     t_ref, r_ref = O.sumsq_rows(gb)
-    assert_rel(float(total), t_ref, 1e-9)
+    assert_rel(float(total), t_ref, 1e-6)
     np.testing.assert_allclose(per_row.cpu().numpy(), r_ref, rtol=1e-6)
 
 
