@@ -53,7 +53,7 @@ bool staged_ok(const uint16_t* w, int64_t cols, uint32_t mask) {
   return true;
 }
 
-int flush_staged(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, cudaStream_t stream) {
+int launch_batch(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, uint32_t key, cudaStream_t stream) {
   size_t i = 0;
   const int sms = num_sms_current();
   while (i < descs.size()) {
@@ -65,6 +65,7 @@ int flush_staged(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, cudaStre
     for (; i < descs.size() && n < pq::MAX_SWEEP_TENSORS; ++i, ++n) {
       pq::SweepDesc d = descs[i];
       int64_t rpi = pq::STAGE_BYTES / (d.cols * 2);
+      if (mode == pq::MODE_SSE && rpi > pq::FAST_MAX_ROWS_PER_ITEM) rpi = pq::FAST_MAX_ROWS_PER_ITEM;
       if (rpi > d.rows) rpi = d.rows;
       if (rpi < 1) rpi = 1;
       d.rows_per_item = (int32_t)rpi;
@@ -76,7 +77,27 @@ int flush_staged(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, cudaStre
     L.item_prefix[n] = items;
     if (items == 0) continue;
     const int grid = (int)(items < sms ? items : sms);
-    const int st = cuda_status(pq::launch_sweep_staged(L, mode, grid, stream));
+    const int st = cuda_status(mode == pq::MODE_SSE ? pq::launch_sweep_fast(L, grid, key, stream)
+                                                    : pq::launch_sweep_staged(L, mode, grid, stream));
+    if (st) return st;
+  }
+  return PQ_OK;
+}
+
+// Launch the staged descriptors; the fast sweep kernel is specialised on the
+// format set, so descriptors are grouped by (format mask, NVFP4 codes).
+int flush_staged(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, cudaStream_t stream) {
+  if (mode != pq::MODE_SSE) {
+    const int st = launch_batch(descs, mode, qfmt, 0u, stream);
+    descs.clear();
+    return st;
+  }
+  for (uint32_t key = 1; key < 16; ++key) {
+    std::vector<pq::SweepDesc> group;
+    for (const auto& d : descs)
+      if (((d.fmt_mask & 7u) | (d.nvfp4_codes ? 8u : 0u)) == key) group.push_back(d);
+    if (group.empty()) continue;
+    const int st = launch_batch(group, mode, qfmt, key, stream);
     if (st) return st;
   }
   descs.clear();
@@ -224,11 +245,12 @@ int pq_nvfp4_scales(int n, const uint16_t* const* amax, const int64_t* n_groups,
   memset(&L, 0, sizeof(L));
   L.n = n;
   int64_t maxg = 0;
+  L.gprefix[0] = 0;
   for (int i = 0; i < n; ++i) {
     if (n_groups[i] < 0) return PQ_ERR_SHAPE;
     if (n_groups[i] > 0 && (!amax[i] || !scales[i])) return PQ_ERR_NULL;
     L.amax[i] = amax[i];
-    L.n_groups[i] = n_groups[i];
+    L.gprefix[i + 1] = L.gprefix[i] + n_groups[i];
     L.scales[i] = scales[i];
     L.group_of[i] = group_of ? group_of[i] : -1;
     if (n_groups[i] > maxg) maxg = n_groups[i];

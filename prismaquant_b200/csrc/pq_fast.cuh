@@ -1,0 +1,132 @@
+// Packed-arithmetic building blocks of the fast sweep path (sm_100a PTX).
+//
+// The fast path never computes w / s.  For a group scale s it brackets the
+// exact quotient between two round-toward-zero products with widened
+// reciprocal bounds, L = RZ(w * r_lo) and H = RZ(w * r_hi), and converts both
+// with the hardware round-to-nearest FP4 / FP8 conversions.  If the two codes
+// agree, every real number in [L, H] — the exact w / s and its float32
+// rounding included — rounds to that code and no codebook midpoint lies in
+// [L, H]; so it is also the reference's nearest-with-ties-to-lower (cost) and
+// nearest-with-ties-toward-zero (export) code.  If they differ the element is
+// within ~2^-20 (relative) of a midpoint and the unit is redone with IEEE
+// division and the exact tie rules (pq_common.cuh).
+//
+// Bracket proof sketch: r = rcp.approx(s) is within 1 ulp of 1/s (PTX ISA
+// bound); r_lo = RZ(r (1 - 2^-20)) < (1 - 2^-21)/s and r_hi = RZ(r (1 + 2^-20))
+// > (1 + 2^-21)/s, hence |L| < |w/s| (1 - 2^-21) and |H| > |w/s| (1 + 2^-22).
+// A float32 quotient equal to a midpoint m has |w/s| within m (1 +- 2^-24),
+// so |L| < m < |H| strictly and the two conversions differ.
+#pragma once
+#include "pq_common.cuh"
+
+namespace pq {
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// bf16 pair {lo, hi} (one 32-bit word) -> float32 pair
+__device__ __forceinline__ uint64_t f2_from_bf16x2(uint32_t v) {
+  return f2_pack(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint64_t f2_mul_rz(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul_rn(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// FP4 E2M1 pair, round-to-nearest-even, saturating at 6: low nibble = lo.
+__device__ __forceinline__ uint32_t cvt_e2m1x2(uint64_t x) {
+  float lo, hi;
+  f2_unpack(x, lo, hi);
+  uint16_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// FP8 E4M3 pair, round-to-nearest-even, saturating at 448: low byte = lo.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(uint64_t x) {
+  float lo, hi;
+  f2_unpack(x, lo, hi);
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Code pair -> float32 pair (exact: both formats embed in f16).
+__device__ __forceinline__ uint64_t e2m1x2_to_f2(uint32_t c) {
+  uint32_t h;
+  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u16 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h) : "h"((uint16_t)c));
+  float lo, hi;
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
+      : "=f"(lo), "=f"(hi) : "r"(h));
+  return f2_pack(lo, hi);
+}
+__device__ __forceinline__ uint64_t e4m3x2_to_f2(uint32_t c) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((uint16_t)c));
+  float lo, hi;
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
+      : "=f"(lo), "=f"(hi) : "r"(h));
+  return f2_pack(lo, hi);
+}
+// float32 pair -> bf16 pair, RNE (low half = lo).
+__device__ __forceinline__ uint32_t f2_to_bf16x2(uint64_t x) {
+  float lo, hi;
+  f2_unpack(x, lo, hi);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// max(|a|, |b|) per half (sign = sign(a) ^ sign(b)); on magnitudes it is the magnitude max.
+__device__ __forceinline__ uint32_t bf16x2_maxabs(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_minabs(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// acc += lo^2 + hi^2 of a bf16 pair (exact bf16 products, fp32 accumulate).
+__device__ __forceinline__ float sq2_acc(uint32_t e, float acc) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %1;\n\tfma.rn.f32.bf16 %0, a, a, %0;\n\tfma.rn.f32.bf16 %0, b, b, %0;\n\t}"
+      : "+f"(acc) : "r"(e));
+  return acc;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// RN(a / d) for a normal bf16 value a and d in {6, 448}, with rd = RN(1/d):
+// product plus one remainder correction (Markstein); checked exhaustively
+// against IEEE division over all normal bf16 inputs.
+__device__ __forceinline__ float div_const(float a, float d, float rd) {
+  const float q = __fmul_rn(a, rd);
+  const float r = __fmaf_rn(-q, d, a);
+  return __fmaf_rn(r, rd, q);
+}
+
+// Widened reciprocal bounds of a positive normal scale s (see header comment).
+__device__ __forceinline__ void recip_bounds(float s, float& r_lo, float& r_hi) {
+  const float r = rcp_approx(s);
+  r_lo = __fmul_rz(r, 1.0f - 9.5367431640625e-07f);   // 1 - 2^-20
+  r_hi = __fmul_rz(r, 1.0f + 9.5367431640625e-07f);   // 1 + 2^-20
+}
+
+}  // namespace pq

@@ -11,6 +11,7 @@ constexpr int SWEEP_THREADS = 512;
 constexpr int STAGE_BYTES = 64 * 1024;     // one work item: consecutive rows, <= 64 KiB
 constexpr int NSTAGE = 3;                  // shared-memory stages per CTA (192 KiB)
 constexpr int MAX_ROWS_PER_ITEM = STAGE_BYTES / 32;  // cols >= 16
+constexpr int FAST_MAX_ROWS_PER_ITEM = 256;          // fast sweep kernel: row parameters kept in shared memory
 constexpr int MAX_SWEEP_TENSORS = 320;     // descriptors per launch (kernel parameter space)
 
 enum : int { MODE_SSE = 0, MODE_QDQ = 1 };
@@ -36,6 +37,8 @@ struct SweepLaunch {
 };
 
 size_t sweep_smem_bytes();
+size_t sweep_fast_smem_bytes();
+cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cudaStream_t stream);
 cudaError_t launch_sweep_staged(const SweepLaunch& L, int mode, int grid, cudaStream_t stream);
 cudaError_t launch_sweep_generic(const uint16_t* w, int64_t rows, int64_t cols, uint32_t mask, double* sse,
                                  uint16_t* out, int mode, int num_sms, cudaStream_t stream);
@@ -45,7 +48,7 @@ constexpr int MAX_SCALE_SLICES = 256;
 struct ScalesLaunch {
   int n;
   const uint16_t* amax[MAX_SCALE_SLICES];
-  int64_t n_groups[MAX_SCALE_SLICES];
+  int64_t gprefix[MAX_SCALE_SLICES + 1];   // flat group offset of each slice
   uint8_t* scales[MAX_SCALE_SLICES];
   int32_t group_of[MAX_SCALE_SLICES];
   const uint32_t* tmax;

@@ -86,10 +86,12 @@ __device__ __forceinline__ float nvfp4_global_from_tmax(uint32_t tmax_bits) {
   return fmaxf(__fdiv_rn(sg, 448.0f), 1e-12f);
 }
 
+// One thread per 8 consecutive groups of the flattened (slice, group) space, so
+// a huge slice (lm_head) spreads over the whole grid instead of one column of
+// blocks.  Slice b covers flat groups [gprefix[b], gprefix[b+1]).
 __global__ void __launch_bounds__(256) nvfp4_scales_kernel(const __grid_constant__ ScalesLaunch L) {
-  const int b = blockIdx.y;
-  __shared__ float s_glob;
-  if (threadIdx.x == 0) {
+  __shared__ float s_glob[MAX_SCALE_SLICES];
+  for (int b = threadIdx.x; b < L.n; b += blockDim.x) {
     float g;
     if (L.override_ != nullptr) {
       g = fmaxf(L.override_[b], 1e-12f);
@@ -99,48 +101,56 @@ __global__ void __launch_bounds__(256) nvfp4_scales_kernel(const __grid_constant
         if (c == b || (L.group_of[c] >= 0 && L.group_of[c] == L.group_of[b]))
           g = fmaxf(g, nvfp4_global_from_tmax(L.tmax[c]));
     }
-    s_glob = g;
+    s_glob[b] = g;
     if (blockIdx.x == 0) L.global_div[b] = __frcp_rn(g);
   }
   __syncthreads();
-  const float glob = s_glob;
-  const uint16_t* am = L.amax[b];
-  uint8_t* sc = L.scales[b];
-  const int64_t ng = L.n_groups[b];
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  auto one = [&](uint32_t abits) {
+  auto one = [&](uint32_t abits, float glob) {
     const float sg = __fdiv_rn(fmaxf(__uint_as_float(abits << 16), 1e-12f), 6.0f);
     const float v = fminf(fmaxf(__fdiv_rn(sg, glob), 0.0f), 448.0f);
     return e4m3_byte(v);
   };
-  if ((ng & 7) == 0 && (reinterpret_cast<uintptr_t>(am) & 15) == 0 && (reinterpret_cast<uintptr_t>(sc) & 7) == 0) {
-    const int64_t n8 = ng >> 3;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += stride) {
-      const uint4 a = __ldg(reinterpret_cast<const uint4*>(am) + i);
+  const int64_t total = L.gprefix[L.n];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
+  int b = 0;
+  for (int64_t g0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; g0 < total; g0 += stride) {
+    while (b + 1 < L.n && L.gprefix[b + 1] <= g0) ++b;   // monotone per thread
+    int bb = b;
+    const float glob0 = s_glob[bb];
+    const int64_t local = g0 - L.gprefix[bb];
+    const uint16_t* am = L.amax[bb];
+    uint8_t* sc = L.scales[bb];
+    if (g0 + 8 <= L.gprefix[bb + 1] && ((reinterpret_cast<uintptr_t>(am + local) & 15) == 0) &&
+        ((reinterpret_cast<uintptr_t>(sc + local) & 7) == 0)) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(am + local));
       const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
-        lo |= one(aw[k] & 0xFFFFu) << (16 * k);
-        lo |= one(aw[k] >> 16) << (16 * k + 8);
-        hi |= one(aw[k + 2] & 0xFFFFu) << (16 * k);
-        hi |= one(aw[k + 2] >> 16) << (16 * k + 8);
+        lo |= one(aw[k] & 0xFFFFu, glob0) << (16 * k);
+        lo |= one(aw[k] >> 16, glob0) << (16 * k + 8);
+        hi |= one(aw[k + 2] & 0xFFFFu, glob0) << (16 * k);
+        hi |= one(aw[k + 2] >> 16, glob0) << (16 * k + 8);
       }
-      reinterpret_cast<uint2*>(sc)[i] = make_uint2(lo, hi);
+      *reinterpret_cast<uint2*>(sc + local) = make_uint2(lo, hi);
+    } else {
+      for (int64_t g = g0; g < g0 + 8 && g < total; ++g) {
+        while (bb + 1 < L.n && L.gprefix[bb + 1] <= g) ++bb;
+        const int64_t lg = g - L.gprefix[bb];
+        L.scales[bb][lg] = (uint8_t)one(L.amax[bb][lg], s_glob[bb]);
+      }
     }
-  } else {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ng; i += stride)
-      sc[i] = (uint8_t)one(am[i]);
   }
 }
 
 cudaError_t launch_nvfp4_scales(const ScalesLaunch& L, int64_t max_groups, int num_sms, cudaStream_t stream) {
-  int64_t bx = (max_groups / 8 + 255) / 256;
-  const int64_t cap = ((int64_t)num_sms * 8 + L.n - 1) / L.n;
-  if (bx > cap) bx = cap;
-  if (bx < 1) bx = 1;
-  dim3 grid((unsigned)bx, (unsigned)L.n);
-  nvfp4_scales_kernel<<<grid, 256, 0, stream>>>(L);
+  (void)max_groups;
+  const int64_t total = L.gprefix[L.n];
+  int64_t blocks = (total / 8 + 255) / 256;
+  const int64_t cap = (int64_t)num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  nvfp4_scales_kernel<<<(unsigned)blocks, 256, 0, stream>>>(L);
   return cudaGetLastError();
 }
 

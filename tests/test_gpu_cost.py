@@ -101,3 +101,39 @@ def test_linear4096_digest(full_digests):
     for f in FMTS:
         assert O.digest(bits_of(fr.get_format(f).quantize_dequantize(w))) == d[f"qdq/{f}"], f
         assert_rel(res[f], d[f"mse/{f}"], 1e-5, f)
+
+
+def test_fast_sweep_per_row_exact():
+    """The fast sweep path (bracketed quotients, packed conversions, SWAR MX
+    rounding) against the oracle with every finite bf16 value, one 32-element
+    row per tensor so that a single mis-rounded element shows (rel 2e-6 is
+    the fp32-partial-sum noise of 32 exact squares)."""
+    allv = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    f = O.bf16_bits_to_f32(allv)
+    vals = allv[np.isfinite(f) & (np.abs(f) < 1e30)]
+    rng = np.random.default_rng(1)
+    vals = rng.permutation(vals)
+    rows = vals[: (vals.size // 32) * 32].reshape(-1, 32)
+    # scale rows into realistic ranges: each row keeps its bf16 patterns but rows with huge spread are common
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3")]
+    named = {str(i): to_cuda_bf16(r.reshape(1, 32)) for i, r in enumerate(rows)}
+    res = mqc.sweep_weight_mse(named, specs)
+    bad = []
+    for i, r in enumerate(rows):
+        b = r.reshape(1, 32)
+        for s in specs:
+            ref = O.cost_mse(b, s.name)
+            got = res[str(i)][s.name]
+            if not (got == ref or abs(got - ref) <= 2e-6 * max(abs(ref), 1e-38)):
+                bad.append((i, s.name, got, ref))
+    assert not bad, bad[:10]
+
+
+def test_fast_sweep_gaussian_rows_exact():
+    """Same per-row check on realistic N(0, 0.02^2) rows with outliers, many tensors."""
+    bits = O.synthetic_weight_bits((3000, 32), seed=77, outlier_frac=0.01)
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3")]
+    res = mqc.sweep_weight_mse({str(i): to_cuda_bf16(bits[i:i + 1]) for i in range(bits.shape[0])}, specs)
+    for i in range(bits.shape[0]):
+        for s in specs:
+            assert_rel(res[str(i)][s.name], O.cost_mse(bits[i:i + 1], s.name), 2e-6, f"row {i} {s.name}")
