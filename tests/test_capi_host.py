@@ -174,3 +174,34 @@ def test_gloo_two_ranks_gather_and_reduce():
     for rank, table, buf in res:
         assert table == [[10.0 * u + j for j in range(4)] for u in range(7)]
         assert buf == [[3.0, 3.0]] * 3
+
+
+def test_patch_prismaquant_rebinds_reference_functions():
+    """install.patch_prismaquant rebinds the reference's hot-path functions in place (and restores them)."""
+    import sys
+    from tests.conftest import REFERENCE, reference_available
+    if not reference_available():
+        pytest.skip("reference checkout not present")
+    shim = str(Path(__file__).resolve().parent.parent / "oracle" / "_shim")
+    sys.path[:0] = [shim, str(REFERENCE)]
+    try:
+        import prismaquant.export_native_compressed as enc
+        import prismaquant.format_registry as fr
+        import prismaquant.measure_quant_cost as mqc
+        import prismaquant.sensitivity_probe as sp
+        from prismaquant_b200 import install
+        orig = (fr.REGISTRY["NVFP4"].quantize_dequantize, mqc._batched_quantize, enc.quantize_dequantize_nvfp4,
+                sp._GradNormCapture, fr.REGISTRY["INT3"].quantize_dequantize)
+        done = install.patch_prismaquant()
+        assert "measure_quant_cost._batched_quantize" in done
+        assert fr.REGISTRY["NVFP4"].quantize_dequantize is not orig[0]
+        assert enc.quantize_dequantize_nvfp4.__module__ == "prismaquant_b200.export_native_compressed"
+        assert sp._GradNormCapture.__module__ == "prismaquant_b200.sensitivity_probe"
+        assert fr.REGISTRY["INT3"].quantize_dequantize is orig[4]     # no B200 kernel: untouched
+        install.unpatch_prismaquant()
+        assert (fr.REGISTRY["NVFP4"].quantize_dequantize, mqc._batched_quantize, enc.quantize_dequantize_nvfp4,
+                sp._GradNormCapture) == orig[:4]
+    finally:
+        for p in (shim, str(REFERENCE)):
+            if p in sys.path:
+                sys.path.remove(p)
