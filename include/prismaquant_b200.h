@@ -121,6 +121,26 @@ int pq_nvfp4_pack(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols,
                   void* stream);
 
 /*
+ * NVFP4 export for callers that cannot allocate device memory.  No
+ * counterpart in the reference: it is pq_nvfp4_pack with the two scratch
+ * buffers (group amax, per-slice max) replaced by a fixed array inside the
+ * library, for programs whose device memory belongs to another allocator,
+ * plug-in hosts that forbid device allocations, and code that must not risk
+ * the device-wide synchronisation of a cudaMalloc.  The caller still passes
+ * inputs and outputs; nothing is allocated or freed.
+ *   Limits: batch <= 256 and batch*rows*cols/16 <= 8,388,608 groups
+ *   (PQ_ERR_LIMIT otherwise).  Every GPU that loads the library holds the
+ *   16 MiB + 1 KiB array until the process exits.
+ *   The first call on a device looks up the array's device address with
+ *   cudaGetSymbolAddress (that device current); make it before any stream
+ *   capture.  All calls on a device share the array: calls that overlap on
+ *   the GPU race; each call clears the per-slice maxima it uses.
+ */
+int pq_nvfp4_pack_noalloc(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols,
+                          const float* override_dev, uint8_t* codes, uint8_t* scales, float* global_div,
+                          void* stream);
+
+/*
  * MXFP8 export (quantize_dequantize_mxfp8[_packed], export_native_compressed.py:1135-1194):
  * E8M0 exponent e = clamp(ceil(log2(max(amax32, 2^-127)/448)), -127, 127)
  * (torch float32 log2 semantics), q = e4m3((w / 2^e).clamp(+-448)),

@@ -24,7 +24,7 @@ FMT_IDS = {"NVFP4": FMT_NVFP4, "MXFP8": FMT_MXFP8, "FP8_E4M3": FMT_FP8_CHANNEL, 
 EXPORTED = [
     "pq_sweep_sse", "pq_cost_qdq", "pq_nvfp4_codes", "pq_nvfp4_scales", "pq_nvfp4_pack",
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
-    "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version",
+    "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
 ]
 
 
@@ -63,6 +63,7 @@ def load() -> ctypes.CDLL:
         "pq_nvfp4_scales": [I, ctypes.POINTER(P), ctypes.POINTER(I64), P, ctypes.POINTER(ctypes.c_int32), P,
                             ctypes.POINTER(P), P, V],
         "pq_nvfp4_pack": [P, I64, I64, I64, P, P, P, P, P, P, V],
+        "pq_nvfp4_pack_noalloc": [P, I64, I64, I64, P, P, P, P, V],
         "pq_mxfp8_pack": [P, I64, I64, P, P, V],
         "pq_fp8_channel_pack": [P, I64, I64, P, P, V],
         "pq_sumsq_rows": [P, I64, I64, P, P, V],

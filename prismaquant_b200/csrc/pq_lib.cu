@@ -5,3 +5,4 @@
 #include "pq_pack.cu"
 #include "pq_fisher.cu"
 #include "pq_capi.cu"
+#include "pq_noalloc.cu"
