@@ -39,11 +39,121 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama8b", choices=["llama8b", "siblings", "linear4096", "moe30b"])
+    ap.add_argument("--workload", default="llama8b", choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b"])
+    ap.add_argument("--fisher-seqs", type=int, default=64, help="calibration sequences (split across ranks)")
+    ap.add_argument("--fisher-batch", type=int, default=4, help="sequences per backward on each rank")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     return ap.parse_args()
+
+
+def run_fisher(a, rank, world, local):
+    """Fisher-trace probe on a random-init Llama-style 1B model (16 layers, hidden 2048,
+    intermediate 8192, 16 heads, vocab 32000, bf16): calibration ids drawn uniformly from
+    [0, 32000) (64 x 2048 by default, seed 0), split across ranks (data parallel); every
+    Linear tracked with the per-token estimator; per-rank traces combined with one all_reduce.
+    One step = one backward of --fisher-batch sequences on every rank."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from prismaquant_b200 import _lib
+    from prismaquant_b200 import distributed as D
+    from prismaquant_b200 import sensitivity_probe as sp
+    from prismaquant_b200 import synthetic as S
+    from transformers import LlamaForCausalLM
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    torch.manual_seed(0)
+    cfg = S.llama_1b_config()
+    model = LlamaForCausalLM(cfg).to(device=dev, dtype=torch.bfloat16)
+    for p in model.parameters():
+        p.requires_grad_(False)
+    tracked = [n for n, m in model.named_modules() if isinstance(m, torch.nn.Linear)]
+    g = torch.Generator().manual_seed(0)
+    calib = torch.randint(0, cfg.vocab_size, (a.fisher_seqs, 2048), generator=g)
+    mine = calib[rank::world]
+    B = a.fisher_batch
+
+    # time the hook kernels with events on the launching stream
+    kev = []
+    orig_rn, orig_td = _lib.rownorm2, _lib.tokennorm_dot
+    kbytes = [0]
+
+    def timed(fn, nbytes):
+        def w(*args, **kw):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = fn(*args, **kw)
+            e1.record()
+            kev.append((e0, e1))
+            kbytes[0] += nbytes(*args)
+            return out
+        return w
+    sp._lib.rownorm2 = timed(orig_rn, lambda x: x.numel() * 2 + (x.numel() // x.shape[-1]) * 4)
+    sp._lib.tokennorm_dot = timed(orig_td, lambda g_, xn, acc, token_idx=None: g_.numel() * 2 + xn.numel() * 4)
+
+    acc = sp.FisherAccumulator(model, tracked, {})
+    model.train()
+    emb = model.get_input_embeddings()
+
+    def step(i):
+        ids = mine[(i * B) % len(mine):(i * B) % len(mine) + B].to(dev)
+        with torch.no_grad():
+            e = emb(ids)
+        e.requires_grad_(True)
+        logits = model(inputs_embeds=e).logits
+        lp = torch.nn.functional.log_softmax(logits[:, :-1].reshape(-1, logits.size(-1)).float(), dim=-1)
+        loss = -lp.gather(1, ids[:, 1:].reshape(-1, 1)).sum()
+        loss.backward()
+        acc._xnorm.clear()
+        if world > 1:
+            D.all_reduce_traces(acc.trace_buffer.clone())
+
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    kev.clear()
+    kbytes[0] = 0
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record()
+        for i in range(a.steps):
+            step(i)
+        t1.record()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    kern_ms = sum(e0.elapsed_time(e1) for e0, e1 in kev)
+    tokens = world * a.steps * B * 2048
+    hbm, peak_kind = peaks()
+    achieved = kbytes[0] / (kern_ms / 1e3) / 1e9 if kern_ms > 0 else 0.0
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Fisher probe tokens/s (fwd+bwd with per-token trace hooks)", "value": round(tokens / (ms_max / 1e3), 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(ms_max / a.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: random-init weights, uniform token ids",
+            "config": {"workload": "llama1b_fisher_probe", "seq_len": 2048, "seqs_per_step_per_rank": B,
+                       "tracked_linears": len(tracked), "parallelism": f"data-parallel x{world}, traces all-reduced"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "rownorm2 + tokennorm_dot (hook kernels)",
+                         "kernel_ms_per_step": round(kern_ms / a.steps, 4),
+                         "hook_share_of_step": round(kern_ms / ms, 4)},
+            "clocks": clk.summary(), "gpu_launches": len(kev)}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def workload_shapes(name):
@@ -56,6 +166,9 @@ def workload_shapes(name):
         return [("model.layers.0.self_attn.o_proj", (4096, 4096))], "single_linear_4096_sweep_nvfp4_export"
     if name == "moe30b":
         return S.moe_expert_params(), "qwen3_30b_a3b_packed_expert_sweep"
+    if name == "fisher1b":
+        return S.llama_dense_linears(n_layers=16, hidden=2048, inter=8192, n_heads=16, n_kv=16, head_dim=128,
+                                     vocab=32000), "llama1b_fisher_probe"
     raise ValueError(name)
 
 
@@ -155,6 +268,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.workload == "fisher1b" and a.impl == "ours":
+        return run_fisher(a, rank, world, local)
     shapes, wl_name = workload_shapes(a.workload)
     params = sum(int(__import__("math").prod(s)) for _, s in shapes)
     metric, unit = "weight GB/s scored across all formats", "GB/s"
@@ -327,7 +442,7 @@ def main():
             "hbm_frac": round(value / world / hbm, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "sweep_staged_kernel (fused sweep + NVFP4 codes)",
+                         "kernel": "sweep_fast_kernel (fused sweep + NVFP4 codes)",
                          "kernel_ms": round(kern_ms, 4), "algorithmic_bytes_per_launch": alg_bytes},
             "clocks": clk.summary(),
             "gpu_launches": a.steps * (2 if plan.export else 1),
