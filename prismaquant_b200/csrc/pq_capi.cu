@@ -64,7 +64,7 @@ int launch_batch(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, uint32_t
     int n = 0;
     for (; i < descs.size() && n < pq::MAX_SWEEP_TENSORS; ++i, ++n) {
       pq::SweepDesc d = descs[i];
-      int64_t rpi = pq::STAGE_BYTES / (d.cols * 2);
+      int64_t rpi = (mode == pq::MODE_SSE ? pq::FAST_STAGE_BYTES : pq::STAGE_BYTES) / (d.cols * 2);
       if (mode == pq::MODE_SSE && rpi > pq::FAST_MAX_ROWS_PER_ITEM) rpi = pq::FAST_MAX_ROWS_PER_ITEM;
       if (rpi > d.rows) rpi = d.rows;
       if (rpi < 1) rpi = 1;

@@ -11,7 +11,9 @@ constexpr int SWEEP_THREADS = 512;
 constexpr int STAGE_BYTES = 64 * 1024;     // one work item: consecutive rows, <= 64 KiB
 constexpr int NSTAGE = 3;                  // shared-memory stages per CTA (192 KiB)
 constexpr int MAX_ROWS_PER_ITEM = STAGE_BYTES / 32;  // cols >= 16
-constexpr int FAST_MAX_ROWS_PER_ITEM = 256;          // fast sweep kernel: row parameters kept in shared memory
+constexpr int FAST_STAGE_BYTES = 96 * 1024;  // fast sweep kernel: one work item
+constexpr int FAST_NSTAGE = 2;                // and two stages (192 KiB)
+constexpr int FAST_MAX_ROWS_PER_ITEM = 256;   // fast sweep kernel: row maxima kept in shared memory
 constexpr int MAX_SWEEP_TENSORS = 320;     // descriptors per launch (kernel parameter space)
 
 enum : int { MODE_SSE = 0, MODE_QDQ = 1 };

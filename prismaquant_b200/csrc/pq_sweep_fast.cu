@@ -24,9 +24,24 @@ namespace pq {
 constexpr int FAST_THREADS = SWEEP_THREADS;
 constexpr float RCP6 = 0.16666667163372039794921875f;        // RN(1/6)
 
+constexpr float RCP448 = 0x1.24924ap-9f;                     // RN(1/448)
+// FP8 per-channel rows whose max |w| reaches this are done entirely by the
+// exact path (a provisional fp32 square could overflow).
+constexpr float F8_EXACT_ROW_AMAX = 1.152921504606846976e18f;  // 2^60
+
 struct RowParam {
   float s, r_lo, r_hi, amax;
 };
+
+// FP8 per-channel row scale from the row's max |w| (bf16 bits): s = max(amax, 1e-8) / 448
+// (div_const is exact for every normal bf16 value and for the 1e-8 floor).
+__device__ __forceinline__ RowParam row_param(uint32_t ra_bits) {
+  RowParam p;
+  p.amax = __uint_as_float(ra_bits << 16);
+  p.s = div_const(fmaxf(p.amax, 1e-8f), 448.0f, RCP448);
+  recip_bounds(p.s, p.r_lo, p.r_hi);
+  return p;
+}
 
 // Loads unit u (16 bf16) from the stage into v[0..7]; lanes of a quarter-warp
 // alternate which 16-byte half they read first so the 128-bit loads are
@@ -97,77 +112,180 @@ __device__ __forceinline__ float f8_pair_sq(uint32_t v, uint32_t cl, uint64_t s2
   return sq2_acc(bf16x2_sub(v, rec), 0.0f);
 }
 
-// Warp-cooperative resolution of queued units (entry = unit index).  For each
-// uncertain pair (bracket codes differ) or every pair of an exact unit, adds
-// exact squared errors minus the main loop's provisional ones and rewrites
-// the export code bytes.
-__device__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0, uint8_t* codes,
-                         bool cost) {
+// Exact side of an uncertain element.  The bracket codes of |w| / s are the
+// neighbours qlo < qhi (magnitudes) with midpoint m between them, and
+// |w / s - m| <= 2^-19 m, so r = |w| - m s is exact as one FMA (|w| has 8
+// significant bits, m at most 5, s 24: r is an integer multiple of the finer
+// of ulp(|w|) and ulp(m) ulp(s) and small enough to fit in 24 bits).
+// The reference rounds q = fl(|w| / s) and compares it with m (m has a short
+// mantissa, so it is an even float32):
+//   q > m  <=>  |w| / s > m + ulp(m) / 2   <=>  r > s ulp(m) / 2        (up)
+//   q < m  <=>  |w| / s < m - ulp-(m) / 2  <=>  r < -s ulp-(m) / 2      (dn)
+// and q == m otherwise (a tie); ulp-(m) is the spacing below m, half of
+// ulp(m) when m is a power of two.  s ulp(m) / 2 is a power-of-two multiple
+// of s, exact and normal for every scale the fast path accepts.
+__device__ __forceinline__ void mid_side(float a, float qlo, float qhi, float s, bool& up, bool& dn) {
+  const float m = 0.5f * (fabsf(qlo) + fabsf(qhi));
+  const uint32_t mb = __float_as_uint(m);
+  const float t = __fmul_rn(s, __uint_as_float((mb & 0x7F800000u) - (24u << 23)));
+  const float tdn = (mb & 0x7FFFFFu) ? t : 0.5f * t;
+  const float r = __fmaf_rn(-m, s, a);
+  up = r > t;
+  dn = r < -tdn;
+}
+
+// NVFP4 pair whose bracket codes cl != ch: exact cost code (ties to the lower
+// value, so toward larger magnitude for negative w) and export code (ties
+// toward zero).
+__device__ __forceinline__ void nv_resolve_pair(uint32_t vp, uint32_t cl, uint32_t ch, float s, uint32_t& cx,
+                                                uint32_t& ce) {
+  float ql0, ql1, qh0, qh1;
+  f2_unpack(e2m1x2_to_f2(cl), ql0, ql1);
+  f2_unpack(e2m1x2_to_f2(ch), qh0, qh1);
+  const float w0 = bf16lo(vp), w1 = bf16hi(vp);
+  const uint32_t d = cl ^ ch;
+  cx = cl;
+  ce = cl;
+  if (d & 0x0Fu) {
+    bool up, dn;
+    mid_side(fabsf(w0), ql0, qh0, s, up, dn);
+    if (up || (!dn && w0 < 0.0f)) cx = (cx & 0xF0u) | (ch & 0x0Fu);
+    if (up) ce = (ce & 0xF0u) | (ch & 0x0Fu);
+  }
+  if (d & 0xF0u) {
+    bool up, dn;
+    mid_side(fabsf(w1), ql1, qh1, s, up, dn);
+    if (up || (!dn && w1 < 0.0f)) cx = (cx & 0x0Fu) | (ch & 0xF0u);
+    if (up) ce = (ce & 0x0Fu) | (ch & 0xF0u);
+  }
+}
+
+// FP8 pair (16-bit code pair, low byte = low element), cost rule.
+__device__ __forceinline__ uint32_t f8_resolve_pair(uint32_t vp, uint32_t cl, uint32_t ch, float s) {
+  float ql0, ql1, qh0, qh1;
+  f2_unpack(e4m3x2_to_f2(cl), ql0, ql1);
+  f2_unpack(e4m3x2_to_f2(ch), qh0, qh1);
+  const float w0 = bf16lo(vp), w1 = bf16hi(vp);
+  const uint32_t d = cl ^ ch;
+  uint32_t cx = cl;
+  if (d & 0x00FFu) {
+    bool up, dn;
+    mid_side(fabsf(w0), ql0, qh0, s, up, dn);
+    if (up || (!dn && w0 < 0.0f)) cx = (cx & 0xFF00u) | (ch & 0x00FFu);
+  }
+  if (d & 0xFF00u) {
+    bool up, dn;
+    mid_side(fabsf(w1), ql1, qh1, s, up, dn);
+    if (up || (!dn && w1 < 0.0f)) cx = (cx & 0x00FFu) | (ch & 0xFF00u);
+  }
+  return cx;
+}
+
+// Units outside the fast path's range (amax below the 1e-8 scale floor, or
+// large enough for an fp32 square to overflow): every element by IEEE
+// division and the exact tie rules.  The main loop contributed nothing.
+__device__ __noinline__ double nv_exact_unit(const uint32_t* vw, float a16, uint8_t* cu, bool cost) {
+  const float s = __fdiv_rn(fmaxf(a16, 1e-8f), 6.0f);
+  const float se = fmaxf(__fdiv_rn(fmaxf(a16, 1e-12f), 6.0f), 1e-12f);   // export scale
+  double delta = 0.0;
+  for (int p = 0; p < 8; ++p) {
+    const uint32_t vp = vw[p];
+    const float w0 = bf16lo(vp), w1 = bf16hi(vp);
+    if (cost) {
+      const float r0 = bf16_round(__fmul_rn(rtn_e2m1_cost(__fdiv_rn(w0, s)), s));
+      const float r1 = bf16_round(__fmul_rn(rtn_e2m1_cost(__fdiv_rn(w1, s)), s));
+      delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
+    }
+    if (cu) cu[p] = (uint8_t)(nvfp4_code(__fdiv_rn(w0, se)) | (nvfp4_code(__fdiv_rn(w1, se)) << 4));
+  }
+  return delta;
+}
+
+__device__ __noinline__ double f8_exact_unit(const uint32_t* vw, float s) {
+  double delta = 0.0;
+  for (int p = 0; p < 8; ++p) {
+    const uint32_t vp = vw[p];
+    const float w0 = bf16lo(vp), w1 = bf16hi(vp);
+    const float r0 = bf16_round(__fmul_rn(rtn_e4m3_cost(__fdiv_rn(w0, s)), s));
+    const float r1 = bf16_round(__fmul_rn(rtn_e4m3_cost(__fdiv_rn(w1, s)), s));
+    delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
+  }
+  return delta;
+}
+
+// Warp-cooperative resolution of queued units (entry = unit index): for each
+// uncertain pair, adds the exact squared errors minus the main loop's
+// provisional ones and rewrites the export code byte.
+__device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
+                                        uint8_t* codes, bool cost) {
   double delta = 0.0;
   for (int i = lane; i < cnt; i += 32) {
     const int u = (int)q[i];
     const uint4 a = st[2 * u], b = st[2 * u + 1];
     const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     const float a16 = __uint_as_float(unit_absmax(v) << 16);
-    const bool ex = exact_unit(a16);
-    const float s = __fdiv_rn(fmaxf(a16, 1e-8f), 6.0f);
+    const uint32_t* vw = reinterpret_cast<const uint32_t*>(st) + 8 * u;
+    uint8_t* cu = codes ? codes + (elem0 + 16 * (int64_t)u) / 2 : nullptr;
+    if (exact_unit(a16)) {
+      delta += nv_exact_unit(vw, a16, cu, cost);
+      continue;
+    }
+    const float s = div_const(a16, 6.0f, RCP6);
     float rlo, rhi;
     recip_bounds(s, rlo, rhi);
     const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi), s2 = f2_pack(s, s);
-    const float se = fmaxf(__fdiv_rn(fmaxf(a16, 1e-12f), 6.0f), 1e-12f);   // export scale
-    uint32_t pm = ex ? 0xFFu : 0u;
+    uint32_t pm = 0;
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
       uint32_t cl, ch;
       nv_bracket(f2_from_bf16x2(v[p]), rlo2, rhi2, cl, ch);
       pm |= (cl != ch ? 1u : 0u) << p;
     }
-    const uint32_t* vw = reinterpret_cast<const uint32_t*>(st) + 8 * u;
+    float dl = 0.0f;
     for (; pm; pm &= pm - 1) {
       const int p = __ffs(pm) - 1;
       const uint32_t vp = vw[p];
-      const float w0 = bf16lo(vp), w1 = bf16hi(vp);
-      const float r0 = bf16_round(__fmul_rn(rtn_e2m1_cost(__fdiv_rn(w0, s)), s));
-      const float r1 = bf16_round(__fmul_rn(rtn_e2m1_cost(__fdiv_rn(w1, s)), s));
-      if (cost) {
-        delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
-        if (!ex) delta -= (double)nv_pair_sq(vp, cvt_e2m1x2(f2_mul_rz(f2_from_bf16x2(vp), rlo2)), s2);
-      }
-      if (codes) {
-        const uint32_t c = nvfp4_code(__fdiv_rn(w0, se)) | (nvfp4_code(__fdiv_rn(w1, se)) << 4);
-        codes[(elem0 + 16 * (int64_t)u + 2 * p) / 2] = (uint8_t)c;
-      }
+      uint32_t cl, ch, cx, ce;
+      nv_bracket(f2_from_bf16x2(vp), rlo2, rhi2, cl, ch);
+      nv_resolve_pair(vp, cl, ch, s, cx, ce);
+      if (cost && cx != cl) dl += nv_pair_sq(vp, cx, s2) - nv_pair_sq(vp, cl, s2);
+      if (cu) cu[p] = (uint8_t)ce;
     }
+    delta += (double)dl;
   }
   return delta;
 }
 
-__device__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const RowParam* rowp, int upr,
-                           uint32_t rdiv) {
+__device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
+                                        int upr, uint32_t rdiv) {
   double delta = 0.0;
   for (int i = lane; i < cnt; i += 32) {
     const int u = (int)q[i];
     const uint4 a = st[2 * u], b = st[2 * u + 1];
     const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const bool ex = __uint_as_float(unit_absmax(v) << 16) >= 1.152921504606846976e18f;   // overflow guard
-    const RowParam rp = rowp[upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)];
+    const uint32_t* vw = reinterpret_cast<const uint32_t*>(st) + 8 * u;
+    const RowParam rp = row_param(ramax[upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)]);
+    if (rp.amax >= F8_EXACT_ROW_AMAX) {
+      delta += f8_exact_unit(vw, rp.s);
+      continue;
+    }
     const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
-    uint32_t pm = ex ? 0xFFu : 0u;
+    uint32_t pm = 0;
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
       const uint64_t w2 = f2_from_bf16x2(v[p]);
       pm |= (cvt_e4m3x2(f2_mul_rz(w2, rlo2)) != cvt_e4m3x2(f2_mul_rz(w2, rhi2)) ? 1u : 0u) << p;
     }
-    const uint32_t* vw = reinterpret_cast<const uint32_t*>(st) + 8 * u;
+    float dl = 0.0f;
     for (; pm; pm &= pm - 1) {
       const int p = __ffs(pm) - 1;
       const uint32_t vp = vw[p];
-      const float w0 = bf16lo(vp), w1 = bf16hi(vp);
-      const float r0 = bf16_round(__fmul_rn(rtn_e4m3_cost(__fdiv_rn(w0, rp.s)), rp.s));
-      const float r1 = bf16_round(__fmul_rn(rtn_e4m3_cost(__fdiv_rn(w1, rp.s)), rp.s));
-      delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
-      if (!ex) delta -= (double)f8_pair_sq(vp, cvt_e4m3x2(f2_mul_rz(f2_from_bf16x2(vp), rlo2)), s2);
+      const uint64_t w2 = f2_from_bf16x2(vp);
+      const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2, rlo2)), ch = cvt_e4m3x2(f2_mul_rz(w2, rhi2));
+      const uint32_t cx = f8_resolve_pair(vp, cl, ch, rp.s);
+      if (cx != cl) dl += f8_pair_sq(vp, cx, s2) - f8_pair_sq(vp, cl, s2);
     }
+    delta += (double)dl;
   }
   return delta;
 }
@@ -192,7 +310,7 @@ struct ItemCtx {
   uint32_t rdiv;
   uint8_t* codes_it;     // codes of the item's first element
   uint16_t* amax_it;     // group amax of the item's first group
-  const RowParam* rowp;
+  uint32_t* ramax;       // per-row max |w| (bf16 bits) of this item's rows
   int64_t elem0;
 };
 
@@ -203,9 +321,15 @@ struct Accum {
   int cnt_nv, cnt_f8;
 };
 
+__device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
+  return c.upr == 1 ? u : (int)__umulhi((uint32_t)u, c.rdiv);   // exact for u < 4096 (host-checked)
+}
+
+// Pass A over one unit: NVFP4 cost and export codes, MXFP8 cost, and (when the
+// FP8 format is on) the unit's contribution to its row maximum.
 template <bool NV, bool MX, bool F8, bool CODES>
-__device__ __forceinline__ void process_unit(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt,
-                                             uint32_t* q_nv, uint32_t* q_f8, Accum& A) {
+__device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, bool warp_rows,
+                                            uint32_t* q_nv, Accum& A) {
   const bool valid = u < c.nunits;
   const int uc = valid ? u : c.nunits - 1;
   uint32_t v[8];
@@ -213,11 +337,6 @@ __device__ __forceinline__ void process_unit(const ItemCtx& c, int u, int lane, 
   uint32_t a16b, amin = 0;
   if (MX) unit_absmax_min(v, a16b, amin); else a16b = unit_absmax(v);
   const float a16 = __uint_as_float(a16b << 16);
-  uint64_t w2[8];
-  if (NV || CODES || F8) {
-#pragma unroll
-    for (int p = 0; p < 8; ++p) w2[p] = f2_from_bf16x2(v[p]);
-  }
 
   if (NV || CODES) {
     const bool ex = exact_unit(a16);
@@ -226,18 +345,19 @@ __device__ __forceinline__ void process_unit(const ItemCtx& c, int u, int lane, 
     recip_bounds(snv, rlo, rhi);
     const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi), s2 = f2_pack(snv, snv);
     uint32_t ux = 0, cc[8];
-    float part = 0.0f;
+    float pe = 0.0f, po = 0.0f;   // two accumulation chains
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
       uint32_t ch;
-      nv_bracket(w2[p], rlo2, rhi2, cc[p], ch);
+      nv_bracket(f2_from_bf16x2(v[p]), rlo2, rhi2, cc[p], ch);
       ux |= cc[p] ^ ch;
       if (NV) {
         const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e2m1x2_to_f2(cc[p]), s2));
-        part = sq2_acc(bf16x2_sub(v[p], rec), part);
+        if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
+        else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
       }
     }
-    if (NV) A.nv += (valid && !ex) ? part : 0.0f;
+    if (NV) A.nv += (valid && !ex) ? pe + po : 0.0f;
     if (CODES) {   // lanes past the end re-store the last unit's identical bytes
       const uint32_t cw0 = __byte_perm(__byte_perm(cc[0], cc[1], 0x0040), __byte_perm(cc[2], cc[3], 0x0040), 0x5410);
       const uint32_t cw1 = __byte_perm(__byte_perm(cc[4], cc[5], 0x0040), __byte_perm(cc[6], cc[7], 0x0040), 0x5410);
@@ -267,14 +387,16 @@ __device__ __forceinline__ void process_unit(const ItemCtx& c, int u, int lane, 
     const uint32_t m448 = ((uint32_t)(e + 135) << 7) | 0x60u;   // bf16 bits of 448 * 2^e
     const uint32_t m448x2 = m448 | (m448 << 16);
     const bool ok = amin >= ((uint32_t)(e + 121) << 7);          // every |w| >= 2^(e-6): E4M3 normal range
-    float part = 0.0f;
+    float pe = 0.0f, po = 0.0f;
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
       const uint32_t neg = (v[p] >> 15) & 0x00010001u;
       const uint32_t rq = (v[p] + 0x00070007u + neg) & 0xFFF0FFF0u;   // ties to the lower value
       const uint32_t q = bf16x2_minabs(rq, m448x2);                   // saturate |q| at 448 * 2^e
-      part = sq2_acc(bf16x2_sub(v[p], q), part);
+      if (p & 1) po = sq2_acc(bf16x2_sub(v[p], q), po);
+      else pe = sq2_acc(bf16x2_sub(v[p], q), pe);
     }
+    float part = pe + po;
     if (!ok && valid) {
       Chunk8 c0, c1;
       unit_to_chunks(v, c0, c1);
@@ -284,34 +406,57 @@ __device__ __forceinline__ void process_unit(const ItemCtx& c, int u, int lane, 
     A.mx += valid ? part : 0.0f;
   }
 
-  if (F8) {
-    const RowParam rp = c.rowp[c.upr == 1 ? uc : (int)__umulhi((uint32_t)uc, c.rdiv)];
-    const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
-    const bool exf = a16 >= 1.152921504606846976e18f;
-    uint32_t ux = 0;
-    float part = 0.0f;
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2[p], rlo2));
-      const uint32_t ch = cvt_e4m3x2(f2_mul_rz(w2[p], rhi2));
-      ux |= cl ^ ch;
-      const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(cl), s2));
-      part = sq2_acc(bf16x2_sub(v[p], rec), part);
-    }
-    A.f8 += (valid && !exf) ? part : 0.0f;
-    const bool need = valid && (ux != 0 || exf);
-    const uint32_t bal = __ballot_sync(FULL, need);
-    if (bal) {
-      if (need) q_f8[A.cnt_f8 + __popc(bal & lanemask_lt)] = (uint32_t)u;
-      A.cnt_f8 += __popc(bal);
-      if (A.cnt_f8 > FAST_QCAP - 32) {
-        __syncwarp();
-        A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.rowp, c.upr, c.rdiv);
-        __syncwarp();
-        A.cnt_f8 = 0;
-      }
+  if (F8) {   // row maxima for pass B
+    const int row = row_of(c, uc);
+    if (warp_rows) {   // the warp's 32 units lie in one row, all valid or all past the end
+      const uint32_t m = warp_max_u(a16b);
+      if (lane == 0 && u - lane < c.nunits) atomicMax(&c.ramax[row], m);
+    } else if (valid) {
+      atomicMax(&c.ramax[row], a16b);
     }
   }
+}
+
+// Pass B over one unit: FP8 per-channel cost with the completed row maximum.
+__device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, uint32_t* q_f8,
+                                            Accum& A) {
+  const bool valid = u < c.nunits;
+  const int uc = valid ? u : c.nunits - 1;
+  uint32_t v[8];
+  load_unit(c.st, uc, true, lane, v);
+  const RowParam rp = row_param(c.ramax[row_of(c, uc)]);
+  const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
+  const bool exf = rp.amax >= F8_EXACT_ROW_AMAX;
+  uint32_t ux = 0;
+  float pe = 0.0f, po = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    const uint64_t w2 = f2_from_bf16x2(v[p]);
+    const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2, rlo2));
+    const uint32_t ch = cvt_e4m3x2(f2_mul_rz(w2, rhi2));
+    ux |= cl ^ ch;
+    const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(cl), s2));
+    if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
+    else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
+  }
+  A.f8 += (valid && !exf) ? pe + po : 0.0f;
+  const bool need = valid && (ux != 0 || exf);
+  const uint32_t bal = __ballot_sync(FULL, need);
+  if (bal) {
+    if (need) q_f8[A.cnt_f8 + __popc(bal & lanemask_lt)] = (uint32_t)u;
+    A.cnt_f8 += __popc(bal);
+    if (A.cnt_f8 > FAST_QCAP - 32) {
+      __syncwarp();
+      A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv);
+      __syncwarp();
+      A.cnt_f8 = 0;
+    }
+  }
+}
+
+__device__ __forceinline__ void fold(float& f, double& d) {
+  d += (double)f;
+  f = 0.0f;
 }
 
 template <bool NV, bool MX, bool F8, bool CODES>
@@ -319,12 +464,11 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int NWARPS = FAST_THREADS / 32;
   uint8_t* stages = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE_BYTES);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + NSTAGE);
-  RowParam* rowp = reinterpret_cast<RowParam*>(bars + NSTAGE + 2);
-  double* red = reinterpret_cast<double*>(rowp + FAST_MAX_ROWS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FAST_NSTAGE * FAST_STAGE_BYTES);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + FAST_NSTAGE);
+  uint32_t* ramax_buf = reinterpret_cast<uint32_t*>(bars + FAST_NSTAGE + 1);   // [2][FAST_MAX_ROWS]
+  double* red = reinterpret_cast<double*>(ramax_buf + 2 * FAST_MAX_ROWS);
   uint32_t* qbase = reinterpret_cast<uint32_t*>(red + NWARPS * 3);
-  auto row_amax = [&](int i) -> uint32_t* { return reinterpret_cast<uint32_t*>(&rowp[i].amax); };
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t* q_nv = qbase + warp * (2 * FAST_QCAP);
@@ -333,9 +477,9 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
   const int64_t n_items = L.item_prefix[L.n];
   const int64_t my_n = n_items > (int64_t)blockIdx.x ? (n_items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 
-  for (int i = tid; i < FAST_MAX_ROWS; i += FAST_THREADS) *row_amax(i) = 0u;
+  for (int i = tid; i < 2 * FAST_MAX_ROWS; i += FAST_THREADS) ramax_buf[i] = 0u;
   if (tid == 0) {
-    for (int s = 0; s < NSTAGE; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < FAST_NSTAGE; ++s) mbar_init(&bars[s], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -346,23 +490,24 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     const ItemRef it = next_item(L, (int64_t)blockIdx.x + j * gridDim.x, ti_issue);
     const SweepDesc& d = L.t[it.ti];
     const uint32_t bytes = (uint32_t)(it.nr * d.cols * 2);
-    uint64_t* bar = &bars[j % NSTAGE];
+    uint64_t* bar = &bars[j % FAST_NSTAGE];
     mbar_arrive_expect_tx(bar, bytes);
-    bulk_g2s(stages + (j % NSTAGE) * STAGE_BYTES, d.w + it.r0 * d.cols, bytes, bar);
+    bulk_g2s(stages + (j % FAST_NSTAGE) * FAST_STAGE_BYTES, d.w + it.r0 * d.cols, bytes, bar);
   };
   if (tid == 0)
-    for (int64_t j = 0; j < NSTAGE && j < my_n; ++j) issue(j);
+    for (int64_t j = 0; j < FAST_NSTAGE && j < my_n; ++j) issue(j);
 
   Accum A;
   A.nv = A.mx = A.f8 = 0.0f;
   A.dnv = A.dmx = A.df8 = 0.0;
   A.tmax = 0u;
+  A.cnt_nv = A.cnt_f8 = 0;
   int cur_t = -1, ti_proc = 0;
   auto flush_tensor = [&](int t) {   // CTA-uniform call
     const SweepDesc& d = L.t[t];
-    A.dnv += (double)A.nv;
-    A.dmx += (double)A.mx;
-    A.df8 += (double)A.f8;
+    fold(A.nv, A.dnv);
+    fold(A.mx, A.dmx);
+    fold(A.f8, A.df8);
     const double a0 = warp_sum_d(A.dnv), a1 = warp_sum_d(A.dmx), a2 = warp_sum_d(A.df8);
     if (CODES) {
       const uint32_t m = warp_max_u(A.tmax);
@@ -383,15 +528,14 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       }
     }
     __syncthreads();
-    A.nv = A.mx = A.f8 = 0.0f;
     A.dnv = A.dmx = A.df8 = 0.0;
     A.tmax = 0u;
   };
 
   int64_t j_abort = -1;
   for (int64_t j = 0; j < my_n; ++j) {
-    const int s = (int)(j % NSTAGE);
-    const uint32_t parity = (uint32_t)((j / NSTAGE) & 1);
+    const int s = (int)(j % FAST_NSTAGE);
+    const uint32_t parity = (uint32_t)((j / FAST_NSTAGE) & 1);
     const ItemRef it = next_item(L, (int64_t)blockIdx.x + j * gridDim.x, ti_proc);
     if (it.ti != cur_t) {
       if (cur_t >= 0) flush_tensor(cur_t);
@@ -404,85 +548,70 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     }
 
     ItemCtx c;
-    c.st = reinterpret_cast<const uint4*>(stages + s * STAGE_BYTES);
+    c.st = reinterpret_cast<const uint4*>(stages + s * FAST_STAGE_BYTES);
     c.upr = (int)(d.cols >> 4);
     c.nunits = (int)it.nr * c.upr;
-    c.rdiv = 0xFFFFFFFFu / (uint32_t)c.upr + 1u;   // u / upr = umulhi(u, rdiv), exact for u < 4096 (host-checked)
+    c.rdiv = 0xFFFFFFFFu / (uint32_t)c.upr + 1u;
     c.elem0 = it.r0 * d.cols;
     c.codes_it = CODES ? d.nvfp4_codes + c.elem0 / 2 : nullptr;
     c.amax_it = CODES ? d.nvfp4_amax + c.elem0 / 16 : nullptr;
-    c.rowp = rowp;
+    c.ramax = ramax_buf + (j & 1) * FAST_MAX_ROWS;
     const int iters = (c.nunits + FAST_THREADS - 1) / FAST_THREADS;
+    const bool warp_rows = (c.upr & 31) == 0;
 
+    if (NV || MX || CODES || F8) {
+#pragma unroll 1
+      for (int k = 0; k < iters; ++k) {   // not unrolled: the body stays small enough for the instruction cache
+        unit_pass_a<NV, MX, F8, CODES>(c, tid + k * FAST_THREADS, lane, lanemask_lt, warp_rows, q_nv, A);
+        if ((k & 3) == 3) {   // fp32 partials hold <= 64 squares
+          fold(A.nv, A.dnv);
+          fold(A.mx, A.dmx);
+        }
+      }
+      fold(A.nv, A.dnv);
+      fold(A.mx, A.dmx);
+    }
     if (F8) {
-      __syncthreads();   // a failed wait is visible to every thread before the stage is read
+      __syncthreads();   // row maxima complete; a failed wait is visible to every thread
       if (*abort_flag) {
         if (j_abort < 0) j_abort = j;
         break;
       }
-      const bool warp_rows = (c.upr & 31) == 0;
+      uint32_t* next = ramax_buf + ((j + 1) & 1) * FAST_MAX_ROWS;   // last read by item j-1
+      for (int i = tid; i < FAST_MAX_ROWS; i += FAST_THREADS) next[i] = 0u;
+#pragma unroll 1
       for (int k = 0; k < iters; ++k) {
-        const int u = tid + k * FAST_THREADS;
-        uint32_t v[8];
-        load_unit(c.st, min(u, c.nunits - 1), true, lane, v);
-        uint32_t a = unit_absmax(v);
-        const int row = c.upr == 1 ? u : (int)__umulhi((uint32_t)u, c.rdiv);
-        if (warp_rows) {
-          a = warp_max_u(a);
-          if (lane == 0 && u - lane < c.nunits) atomicMax(row_amax(row), a);
-        } else if (u < c.nunits) {
-          atomicMax(row_amax(row), a);
-        }
+        unit_pass_b(c, tid + k * FAST_THREADS, lane, lanemask_lt, q_f8, A);
+        if ((k & 3) == 3) fold(A.f8, A.df8);
       }
-      __syncthreads();
-      for (int i = tid; i < it.nr; i += FAST_THREADS) {
-        const float ar = __uint_as_float(*row_amax(i) << 16);
-        const float sr = __fdiv_rn(fmaxf(ar, 1e-8f), 448.0f);
-        RowParam p;
-        p.s = sr;
-        p.amax = ar;
-        recip_bounds(sr, p.r_lo, p.r_hi);
-        rowp[i] = p;
-      }
-      __syncthreads();
-    }
-
-    A.cnt_nv = A.cnt_f8 = 0;
-    for (int k = 0; k < iters; k += 4) {
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        if (k + kk < iters) process_unit<NV, MX, F8, CODES>(c, tid + (k + kk) * FAST_THREADS, lane, lanemask_lt, q_nv, q_f8, A);
-      A.dnv += (double)A.nv;   // fold fp32 partials (<= 64 squares each) into fp64
-      A.dmx += (double)A.mx;
-      A.df8 += (double)A.f8;
-      A.nv = A.mx = A.f8 = 0.0f;
+      fold(A.f8, A.df8);
     }
     __syncwarp();
     if ((NV || CODES) && A.cnt_nv)
       A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV);
-    if (F8 && A.cnt_f8) A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, rowp, c.upr, c.rdiv);
-    if (F8)
-      for (int i = tid; i < it.nr; i += FAST_THREADS) *row_amax(i) = 0u;   // ready for the next item
-    __syncthreads();   // stage s, row parameters and queues are free again
+    if (F8 && A.cnt_f8) A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv);
+    A.cnt_nv = A.cnt_f8 = 0;
+    __syncthreads();   // stage s and the queues are free again
     if (*abort_flag) {
       if (j_abort < 0) j_abort = j;
       break;
     }
-    if (tid == 0 && j + NSTAGE < my_n) {
+    if (tid == 0 && j + FAST_NSTAGE < my_n) {
       fence_proxy_async_smem();
-      issue(j + NSTAGE);
+      issue(j + FAST_NSTAGE);
     }
   }
   if (cur_t >= 0 && j_abort < 0) flush_tensor(cur_t);
   if (j_abort >= 0 && tid == 0) {
-    for (int64_t jj = j_abort; jj < j_abort + NSTAGE && jj < my_n; ++jj)
-      (void)mbar_wait_bounded(&bars[jj % NSTAGE], (uint32_t)((jj / NSTAGE) & 1), 1u << 20);
+    for (int64_t jj = j_abort; jj < j_abort + FAST_NSTAGE && jj < my_n; ++jj)
+      (void)mbar_wait_bounded(&bars[jj % FAST_NSTAGE], (uint32_t)((jj / FAST_NSTAGE) & 1), 1u << 20);
   }
 }
 
 size_t sweep_fast_smem_bytes() {
-  return (size_t)NSTAGE * STAGE_BYTES + (NSTAGE + 2) * sizeof(uint64_t) + FAST_MAX_ROWS * sizeof(RowParam) +
-         (FAST_THREADS / 32) * 3 * sizeof(double) + (FAST_THREADS / 32) * 2 * FAST_QCAP * sizeof(uint32_t);
+  return (size_t)FAST_NSTAGE * FAST_STAGE_BYTES + (FAST_NSTAGE + 1) * sizeof(uint64_t) +
+         2 * FAST_MAX_ROWS * sizeof(uint32_t) + (FAST_THREADS / 32) * 3 * sizeof(double) +
+         (FAST_THREADS / 32) * 2 * FAST_QCAP * sizeof(uint32_t);
 }
 
 template <bool NV, bool MX, bool F8, bool CODES>
