@@ -77,6 +77,12 @@ __device__ __forceinline__ uint64_t e4m3x2_to_f2(uint32_t c) {
       : "=f"(lo), "=f"(hi) : "r"(h));
   return f2_pack(lo, hi);
 }
+// One E4M3 code byte -> float32 (exact).
+__device__ __forceinline__ float e4m3x2_to_f2_lo(uint32_t c) {
+  float lo, hi;
+  f2_unpack(e4m3x2_to_f2(c & 0xFFu), lo, hi);
+  return lo;
+}
 // float32 pair -> bf16 pair, RNE (low half = lo).
 __device__ __forceinline__ uint32_t f2_to_bf16x2(uint64_t x) {
   float lo, hi;
@@ -113,13 +119,38 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return r;
 }
 
+constexpr float RCP6 = 0.16666667163372039794921875f;   // RN(1/6)
+constexpr float RCP448 = 0x1.24924ap-9f;                // RN(1/448)
+
 // RN(a / d) for a normal bf16 value a and d in {6, 448}, with rd = RN(1/d):
 // product plus one remainder correction (Markstein); checked exhaustively
-// against IEEE division over all normal bf16 inputs.
+// against IEEE division over all normal bf16 inputs and the floors 1e-8 and 1e-12.
 __device__ __forceinline__ float div_const(float a, float d, float rd) {
   const float q = __fmul_rn(a, rd);
   const float r = __fmaf_rn(-q, d, a);
   return __fmaf_rn(r, rd, q);
+}
+
+// Exact side of an uncertain quotient a / s (a, s > 0 float32).  The bracket
+// codes of a / s are the neighbours qlo < qhi (magnitudes) with midpoint m
+// between them, and |a / s - m| <= 2^-19 m, so r = a - m s is exact as one
+// FMA: m has at most 5 significant bits and s 24, so r is an integer multiple
+// of the finer of ulp(a) and ulp(m) ulp(s), and |r| <= 2^-19 a is below 2^11
+// of those units.  The reference rounds q = fl(a / s) and compares it with m
+// (m has a short mantissa, so it is an even float32):
+//   q > m  <=>  a / s > m + ulp(m) / 2   <=>  r > s ulp(m) / 2        (up)
+//   q < m  <=>  a / s < m - ulp-(m) / 2  <=>  r < -s ulp-(m) / 2      (dn)
+// and q == m otherwise (a tie); ulp-(m) is the spacing below m, half of
+// ulp(m) when m is a power of two.  s ulp(m) / 2 is a power-of-two multiple
+// of s, exact and normal for every scale the fast paths accept.
+__device__ __forceinline__ void mid_side(float a, float qlo, float qhi, float s, bool& up, bool& dn) {
+  const float m = 0.5f * (fabsf(qlo) + fabsf(qhi));
+  const uint32_t mb = __float_as_uint(m);
+  const float t = __fmul_rn(s, __uint_as_float((mb & 0x7F800000u) - (24u << 23)));
+  const float tdn = (mb & 0x7FFFFFu) ? t : 0.5f * t;
+  const float r = __fmaf_rn(-m, s, a);
+  up = r > t;
+  dn = r < -tdn;
 }
 
 // Widened reciprocal bounds of a positive normal scale s (see header comment).

@@ -7,6 +7,7 @@
 // bytes (one 16-byte vector per lane, 8 bf16 elements), groups are formed
 // with lane shuffles, outputs are written with vector stores.
 #include "pq_common.cuh"
+#include "pq_fast.cuh"
 #include "pq_internal.h"
 
 namespace pq {
@@ -86,58 +87,108 @@ __device__ __forceinline__ float nvfp4_global_from_tmax(uint32_t tmax_bits) {
   return fmaxf(__fdiv_rn(sg, 448.0f), 1e-12f);
 }
 
-// One thread per 8 consecutive groups of the flattened (slice, group) space, so
+// Block scale byte of one group: e4m3(clamp(RN(RN(max(amax, 1e-12) / 6) / glob), 0, 448)), RNE
+// (export_native_compressed.py:1099-1102), by IEEE division.
+__device__ __forceinline__ uint32_t nvfp4_scale_exact(uint32_t abits, float glob) {
+  const float sg = __fdiv_rn(fmaxf(__uint_as_float(abits << 16), 1e-12f), 6.0f);
+  return e4m3_byte(fminf(fmaxf(__fdiv_rn(sg, glob), 0.0f), 448.0f));
+}
+
+// RNE choice between adjacent E4M3 codes lo < hi (one byte) for the quotient a / s.
+__device__ __forceinline__ uint32_t e4m3_rne_pick(float a, float s, uint32_t lo, uint32_t hi) {
+  bool up, dn;
+  mid_side(a, e4m3x2_to_f2_lo(lo), e4m3x2_to_f2_lo(hi), s, up, dn);
+  return up ? hi : dn ? lo : ((lo & 1u) ? hi : lo);   // a tie goes to the even code
+}
+
+// Two groups at once (amax pair a2, low half first) without dividing: sg = a/6 by
+// div_const (exact for every normal bf16 and the 1e-12 floor), then sg/glob is
+// bracketed between RZ(sg * r_lo) and RZ(sg * r_hi) as in the fast sweep and both
+// are converted with the hardware RNE E4M3 conversion (saturating at 448, as the
+// clamp does).  Equal codes are the reference's code; where they differ (a
+// quotient within ~2^-20 of an E4M3 midpoint) mid_side decides the side exactly.
+__device__ __forceinline__ uint32_t nvfp4_scale_pair(uint32_t a2, float glob, uint64_t rlo2, uint64_t rhi2) {
+  const float sg0 = div_const(fmaxf(__uint_as_float(a2 << 16), 1e-12f), 6.0f, RCP6);
+  const float sg1 = div_const(fmaxf(__uint_as_float(a2 & 0xFFFF0000u), 1e-12f), 6.0f, RCP6);
+  const uint64_t sg2 = f2_pack(sg0, sg1);
+  const uint32_t lo = cvt_e4m3x2(f2_mul_rz(sg2, rlo2));
+  const uint32_t hi = cvt_e4m3x2(f2_mul_rz(sg2, rhi2));
+  if (lo == hi) return lo;
+  uint32_t r = lo;
+  if ((lo ^ hi) & 0x00FFu) r = (r & 0xFF00u) | e4m3_rne_pick(sg0, glob, lo & 0xFFu, hi & 0xFFu);
+  if ((lo ^ hi) & 0xFF00u) r = (r & 0x00FFu) | (e4m3_rne_pick(sg1, glob, lo >> 8, hi >> 8) << 8);
+  return r;
+}
+
+// One thread per 32 consecutive groups of the flattened (slice, group) space, so
 // a huge slice (lm_head) spreads over the whole grid instead of one column of
 // blocks.  Slice b covers flat groups [gprefix[b], gprefix[b+1]).
+constexpr int SCALE_GROUPS_PER_THREAD = 32;
+
 __global__ void __launch_bounds__(256) nvfp4_scales_kernel(const __grid_constant__ ScalesLaunch L) {
+  __shared__ float s_nat[MAX_SCALE_SLICES];
   __shared__ float s_glob[MAX_SCALE_SLICES];
+  __shared__ float s_rlo[MAX_SCALE_SLICES], s_rhi[MAX_SCALE_SLICES];
+  if (L.override_ == nullptr)
+    for (int c = threadIdx.x; c < L.n; c += blockDim.x) s_nat[c] = nvfp4_global_from_tmax(L.tmax[c]);
+  __syncthreads();
   for (int b = threadIdx.x; b < L.n; b += blockDim.x) {
     float g;
     if (L.override_ != nullptr) {
       g = fmaxf(L.override_[b], 1e-12f);
     } else {
-      g = 0.0f;
-      for (int c = 0; c < L.n; ++c)
-        if (c == b || (L.group_of[c] >= 0 && L.group_of[c] == L.group_of[b]))
-          g = fmaxf(g, nvfp4_global_from_tmax(L.tmax[c]));
+      g = s_nat[b];   // joint global of a fused-sibling group: the max of the members' globals
+      if (L.group_of[b] >= 0)
+        for (int c = 0; c < L.n; ++c)
+          if (L.group_of[c] == L.group_of[b]) g = fmaxf(g, s_nat[c]);
     }
     s_glob[b] = g;
+    // The bracket needs a normal reciprocal with room to spare; a slice whose global lies
+    // outside [1e-30, 1e30] (only reachable through an override) is marked r_lo < 0 and
+    // takes the division path.
+    if (g >= 1.0e-30f && g <= 1.0e30f) {
+      recip_bounds(g, s_rlo[b], s_rhi[b]);
+    } else {
+      s_rlo[b] = -1.0f;
+      s_rhi[b] = -1.0f;
+    }
     if (blockIdx.x == 0) L.global_div[b] = __frcp_rn(g);
   }
   __syncthreads();
-  auto one = [&](uint32_t abits, float glob) {
-    const float sg = __fdiv_rn(fmaxf(__uint_as_float(abits << 16), 1e-12f), 6.0f);
-    const float v = fminf(fmaxf(__fdiv_rn(sg, glob), 0.0f), 448.0f);
-    return e4m3_byte(v);
-  };
+  constexpr int G = SCALE_GROUPS_PER_THREAD;
   const int64_t total = L.gprefix[L.n];
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * G;
   int b = 0;
-  for (int64_t g0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; g0 < total; g0 += stride) {
+  for (int64_t g0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * G; g0 < total; g0 += stride) {
     while (b + 1 < L.n && L.gprefix[b + 1] <= g0) ++b;   // monotone per thread
     int bb = b;
-    const float glob0 = s_glob[bb];
     const int64_t local = g0 - L.gprefix[bb];
     const uint16_t* am = L.amax[bb];
     uint8_t* sc = L.scales[bb];
-    if (g0 + 8 <= L.gprefix[bb + 1] && ((reinterpret_cast<uintptr_t>(am + local) & 15) == 0) &&
-        ((reinterpret_cast<uintptr_t>(sc + local) & 7) == 0)) {
-      const uint4 a = __ldg(reinterpret_cast<const uint4*>(am + local));
-      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
-      uint32_t lo = 0, hi = 0;
+    if (g0 + G <= L.gprefix[bb + 1] && s_rlo[bb] > 0.0f && ((reinterpret_cast<uintptr_t>(am + local) & 15) == 0) &&
+        ((reinterpret_cast<uintptr_t>(sc + local) & 15) == 0)) {
+      const float glob0 = s_glob[bb];
+      const uint64_t rlo2 = f2_pack(s_rlo[bb], s_rlo[bb]), rhi2 = f2_pack(s_rhi[bb], s_rhi[bb]);
+      const uint4* src = reinterpret_cast<const uint4*>(am + local);
+      uint4 a[G / 8];
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        lo |= one(aw[k] & 0xFFFFu, glob0) << (16 * k);
-        lo |= one(aw[k] >> 16, glob0) << (16 * k + 8);
-        hi |= one(aw[k + 2] & 0xFFFFu, glob0) << (16 * k);
-        hi |= one(aw[k + 2] >> 16, glob0) << (16 * k + 8);
+      for (int i = 0; i < G / 8; ++i) a[i] = __ldg(src + i);   // all loads in flight before any arithmetic
+#pragma unroll
+      for (int h = 0; h < G / 16; ++h) {
+        const uint32_t aw[8] = {a[2 * h].x, a[2 * h].y, a[2 * h].z, a[2 * h].w,
+                                a[2 * h + 1].x, a[2 * h + 1].y, a[2 * h + 1].z, a[2 * h + 1].w};
+        uint32_t out[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          out[k] = nvfp4_scale_pair(aw[2 * k], glob0, rlo2, rhi2) |
+                   (nvfp4_scale_pair(aw[2 * k + 1], glob0, rlo2, rhi2) << 16);
+        reinterpret_cast<uint4*>(sc + local)[h] = make_uint4(out[0], out[1], out[2], out[3]);
       }
-      *reinterpret_cast<uint2*>(sc + local) = make_uint2(lo, hi);
     } else {
-      for (int64_t g = g0; g < g0 + 8 && g < total; ++g) {
+      for (int64_t g = g0; g < g0 + G && g < total; ++g) {
         while (bb + 1 < L.n && L.gprefix[bb + 1] <= g) ++bb;
         const int64_t lg = g - L.gprefix[bb];
-        L.scales[bb][lg] = (uint8_t)one(L.amax[bb][lg], s_glob[bb]);
+        L.scales[bb][lg] = (uint8_t)nvfp4_scale_exact(L.amax[bb][lg], s_glob[bb]);
       }
     }
   }
@@ -146,7 +197,7 @@ __global__ void __launch_bounds__(256) nvfp4_scales_kernel(const __grid_constant
 cudaError_t launch_nvfp4_scales(const ScalesLaunch& L, int64_t max_groups, int num_sms, cudaStream_t stream) {
   (void)max_groups;
   const int64_t total = L.gprefix[L.n];
-  int64_t blocks = (total / 8 + 255) / 256;
+  int64_t blocks = (total / SCALE_GROUPS_PER_THREAD + 255) / 256;
   const int64_t cap = (int64_t)num_sms * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;

@@ -22,9 +22,7 @@
 namespace pq {
 
 constexpr int FAST_THREADS = SWEEP_THREADS;
-constexpr float RCP6 = 0.16666667163372039794921875f;        // RN(1/6)
 
-constexpr float RCP448 = 0x1.24924ap-9f;                     // RN(1/448)
 // FP8 per-channel rows whose max |w| reaches this are done entirely by the
 // exact path (a provisional fp32 square could overflow).
 constexpr float F8_EXACT_ROW_AMAX = 1.152921504606846976e18f;  // 2^60
@@ -110,28 +108,6 @@ __device__ __forceinline__ float nv_pair_sq(uint32_t v, uint32_t cl, uint64_t s2
 __device__ __forceinline__ float f8_pair_sq(uint32_t v, uint32_t cl, uint64_t s2) {
   const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(cl), s2));
   return sq2_acc(bf16x2_sub(v, rec), 0.0f);
-}
-
-// Exact side of an uncertain element.  The bracket codes of |w| / s are the
-// neighbours qlo < qhi (magnitudes) with midpoint m between them, and
-// |w / s - m| <= 2^-19 m, so r = |w| - m s is exact as one FMA (|w| has 8
-// significant bits, m at most 5, s 24: r is an integer multiple of the finer
-// of ulp(|w|) and ulp(m) ulp(s) and small enough to fit in 24 bits).
-// The reference rounds q = fl(|w| / s) and compares it with m (m has a short
-// mantissa, so it is an even float32):
-//   q > m  <=>  |w| / s > m + ulp(m) / 2   <=>  r > s ulp(m) / 2        (up)
-//   q < m  <=>  |w| / s < m - ulp-(m) / 2  <=>  r < -s ulp-(m) / 2      (dn)
-// and q == m otherwise (a tie); ulp-(m) is the spacing below m, half of
-// ulp(m) when m is a power of two.  s ulp(m) / 2 is a power-of-two multiple
-// of s, exact and normal for every scale the fast path accepts.
-__device__ __forceinline__ void mid_side(float a, float qlo, float qhi, float s, bool& up, bool& dn) {
-  const float m = 0.5f * (fabsf(qlo) + fabsf(qhi));
-  const uint32_t mb = __float_as_uint(m);
-  const float t = __fmul_rn(s, __uint_as_float((mb & 0x7F800000u) - (24u << 23)));
-  const float tdn = (mb & 0x7FFFFFu) ? t : 0.5f * t;
-  const float r = __fmaf_rn(-m, s, a);
-  up = r > t;
-  dn = r < -tdn;
 }
 
 // NVFP4 pair whose bracket codes cl != ch: exact cost code (ties to the lower

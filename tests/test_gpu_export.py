@@ -149,3 +149,31 @@ def test_shape_errors_raise():
         enc.quantize_dequantize_mxfp8(w)
     with pytest.raises(ValueError):
         fr.get_format("MXFP8").quantize_dequantize(torch.zeros(4, 48, dtype=torch.bfloat16, device="cuda"))
+
+
+def test_nvfp4_scales_every_bf16_amax():
+    """pq_nvfp4_scales over every positive bf16 group maximum, for globals that put many quotients
+    exactly on E4M3 midpoints (1, 1/2, 7/6, ...), the 1e-12 floor (also reached from below), a
+    global outside the bracket's range, and a misaligned tail slice (scalar path)."""
+    from prismaquant_b200 import _lib
+    bits = np.arange(0, 0x7F80, dtype=np.uint16)                 # 0 .. largest finite bf16
+    amax = torch.from_numpy(bits.view(np.int16)).cuda()
+    globs = [1.0, 0.5, 3.0, 7.0 / 6.0, 1.0 / 448.0, 2.0 ** -20, 1e-12, 1e-20, 1e31, 12.25]
+    slices = [amax] * len(globs) + [amax[1:]]                    # last: 2-byte offset, scalar path
+    over = torch.tensor(globs + [0.75], dtype=torch.float32, device="cuda")
+    scales = [torch.empty(s.numel(), dtype=torch.uint8, device="cuda") for s in slices]
+    gdiv = torch.empty(len(slices), dtype=torch.float32, device="cuda")
+    _lib.nvfp4_scales(slices, None, scales, gdiv, override=over)
+    torch.cuda.synchronize()
+    a32 = O.bf16_bits_to_f32(bits)
+    s_g = (np.maximum(a32, np.float32(1e-12)) / np.float32(6.0)).astype(np.float32)
+    for i, g in enumerate(globs + [0.75]):
+        glob = np.float32(max(np.float32(g), np.float32(1e-12)))
+        want = O.f32_to_e4m3fn_bits(np.clip((s_g / glob).astype(np.float32), np.float32(0), np.float32(448)))
+        if i == len(globs):
+            want = want[1:]
+        got = scales[i].cpu().numpy()
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, (g, bad[:5], got[bad[:5]], want[bad[:5]])
+        assert gdiv[i].item() == float(np.float32(1.0) / glob)
+    assert _lib.device_error() == 0
