@@ -77,6 +77,69 @@ __device__ __forceinline__ uint64_t e4m3x2_to_f2(uint32_t c) {
       : "=f"(lo), "=f"(hi) : "r"(h));
   return f2_pack(lo, hi);
 }
+// f16 pair (one 32-bit word) -> float32 pair (exact).
+__device__ __forceinline__ uint64_t f16x2_to_f2(uint32_t h) {
+  float lo, hi;
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
+      : "=f"(lo), "=f"(hi) : "r"(h));
+  return f2_pack(lo, hi);
+}
+
+// Four NVFP4 pairs at once, codes kept in byte registers: l[2p], l[2p+1] are
+// the low-bracket products of pair p, h[] the high ones.  cw gets the four
+// low-bracket code bytes (pair p in byte p), dx = cw ^ the high-bracket
+// bytes, q[p] the f16 pair of pair p's low-bracket code.
+__device__ __forceinline__ void nv_codes4(const float (&l)[8], const float (&h)[8], uint32_t& cw, uint32_t& dx,
+                                          uint32_t (&q)[4]) {
+  asm("{\n\t.reg .b8 c0, c1, c2, c3, d0, d1, d2, d3;\n\t.reg .b32 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c0, %7, %6;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c1, %9, %8;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c2, %11, %10;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c3, %13, %12;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 d0, %15, %14;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 d1, %17, %16;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 d2, %19, %18;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 d3, %21, %20;\n\t"
+      "mov.b32 %0, {c0, c1, c2, c3};\n\t"
+      "mov.b32 t, {d0, d1, d2, d3};\n\t"
+      "xor.b32 %1, %0, t;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, c0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, c1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %4, c2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %5, c3;\n\t}"
+      : "=r"(cw), "=r"(dx), "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3])
+      : "f"(l[0]), "f"(l[1]), "f"(l[2]), "f"(l[3]), "f"(l[4]), "f"(l[5]), "f"(l[6]), "f"(l[7]),
+        "f"(h[0]), "f"(h[1]), "f"(h[2]), "f"(h[3]), "f"(h[4]), "f"(h[5]), "f"(h[6]), "f"(h[7]));
+}
+
+// Four FP8 (E4M3) pairs at once: dx is nonzero iff some pair's bracket codes
+// differ, q[p] the f16 pair of pair p's low-bracket code.
+__device__ __forceinline__ void f8_codes4(const float (&l)[8], const float (&h)[8], uint32_t& dx, uint32_t (&q)[4]) {
+  asm("{\n\t.reg .b16 c0, c1, c2, c3, d0, d1, d2, d3;\n\t.reg .b32 t0, t1, u0, u1;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 c0, %6, %5;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 c1, %8, %7;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 c2, %10, %9;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 c3, %12, %11;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 d0, %14, %13;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 d1, %16, %15;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 d2, %18, %17;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 d3, %20, %19;\n\t"
+      "mov.b32 t0, {c0, c1};\n\t"
+      "mov.b32 t1, {c2, c3};\n\t"
+      "mov.b32 u0, {d0, d1};\n\t"
+      "mov.b32 u1, {d2, d3};\n\t"
+      "xor.b32 t0, t0, u0;\n\t"
+      "xor.b32 t1, t1, u1;\n\t"
+      "or.b32 %0, t0, t1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, c0;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %2, c1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %3, c2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %4, c3;\n\t}"
+      : "=r"(dx), "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3])
+      : "f"(l[0]), "f"(l[1]), "f"(l[2]), "f"(l[3]), "f"(l[4]), "f"(l[5]), "f"(l[6]), "f"(l[7]),
+        "f"(h[0]), "f"(h[1]), "f"(h[2]), "f"(h[3]), "f"(h[4]), "f"(h[5]), "f"(h[6]), "f"(h[7]));
+}
+
 // One E4M3 code byte -> float32 (exact).
 __device__ __forceinline__ float e4m3x2_to_f2_lo(uint32_t c) {
   float lo, hi;

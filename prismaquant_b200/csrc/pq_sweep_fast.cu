@@ -189,79 +189,126 @@ __device__ __noinline__ double f8_exact_unit(const uint32_t* vw, float s) {
   return delta;
 }
 
-// Warp-cooperative resolution of queued units (entry = unit index): for each
-// uncertain pair, adds the exact squared errors minus the main loop's
-// provisional ones and rewrites the export code byte.
-__device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
-                                        uint8_t* codes, bool cost) {
-  double delta = 0.0;
-  for (int i = lane; i < cnt; i += 32) {
-    const int u = (int)q[i];
-    const uint4 a = st[2 * u], b = st[2 * u + 1];
-    const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const float a16 = __uint_as_float(unit_absmax(v) << 16);
-    const uint32_t* vw = reinterpret_cast<const uint32_t*>(st) + 8 * u;
-    uint8_t* cu = codes ? codes + (elem0 + 16 * (int64_t)u) / 2 : nullptr;
-    if (exact_unit(a16)) {
-      delta += nv_exact_unit(vw, a16, cu, cost);
-      continue;
-    }
-    const float s = div_const(a16, 6.0f, RCP6);
-    float rlo, rhi;
-    recip_bounds(s, rlo, rhi);
-    const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi), s2 = f2_pack(s, s);
-    uint32_t pm = 0;
+constexpr int FAST_TASK_CAP = 8 * 32;   // uncertain pairs of one 32-unit batch
+
+// Inclusive warp prefix sum.
+__device__ __forceinline__ int warp_incl_scan(int x, int lane) {
 #pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      uint32_t cl, ch;
-      nv_bracket(f2_from_bf16x2(v[p]), rlo2, rhi2, cl, ch);
-      pm |= (cl != ch ? 1u : 0u) << p;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(FULL, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
+}
+
+// Warp-cooperative resolution of queued units (entry = unit index), in batches
+// of 32 units: each lane finds its unit's uncertain pairs, a prefix sum packs
+// them into the warp's task list, and the whole warp resolves the list, so a
+// batch costs one round per 32 uncertain pairs instead of one per pair of its
+// busiest lane.  Each resolved pair adds its exact squared errors minus the
+// main loop's provisional ones and rewrites its export code byte.
+// Task word: pair (bits 0-2) | unit (3-14) | group amax bf16 bits (15-29).
+__device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
+                                        uint8_t* codes, bool cost, uint32_t* tasks) {
+  double delta = 0.0;
+  const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
+  for (int base = 0; base < cnt; base += 32) {   // warp-uniform
+    const int i = base + lane;
+    uint32_t pm = 0, a16b = 0;
+    int u = 0;
+    if (i < cnt) {
+      u = (int)q[i];
+      const uint4 a = st[2 * u], b = st[2 * u + 1];
+      const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      a16b = unit_absmax(v);
+      const float a16 = __uint_as_float(a16b << 16);
+      if (exact_unit(a16)) {
+        delta += nv_exact_unit(words + 8 * u, a16, codes ? codes + (elem0 + 16 * (int64_t)u) / 2 : nullptr, cost);
+      } else {
+        const float s = div_const(a16, 6.0f, RCP6);
+        float rlo, rhi;
+        recip_bounds(s, rlo, rhi);
+        const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi);
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          uint32_t cl, ch;
+          nv_bracket(f2_from_bf16x2(v[p]), rlo2, rhi2, cl, ch);
+          pm |= (cl != ch ? 1u : 0u) << p;
+        }
+      }
     }
+    const int n = __popc(pm);
+    const int incl = warp_incl_scan(n, lane);
+    const int tot = __shfl_sync(FULL, incl, 31);
+    int off = incl - n;
+    for (uint32_t m = pm; m; m &= m - 1) tasks[off++] = (uint32_t)(__ffs(m) - 1) | ((uint32_t)u << 3) | (a16b << 15);
+    __syncwarp();
     float dl = 0.0f;
-    for (; pm; pm &= pm - 1) {
-      const int p = __ffs(pm) - 1;
-      const uint32_t vp = vw[p];
+    for (int t = lane; t < tot; t += 32) {
+      const uint32_t task = tasks[t];
+      const int p = (int)(task & 7u), uu = (int)((task >> 3) & 0xFFFu);
+      const float s = div_const(__uint_as_float((task >> 15) << 16), 6.0f, RCP6);
+      float rlo, rhi;
+      recip_bounds(s, rlo, rhi);
+      const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi), s2 = f2_pack(s, s);
+      const uint32_t vp = words[8 * uu + p];
       uint32_t cl, ch, cx, ce;
       nv_bracket(f2_from_bf16x2(vp), rlo2, rhi2, cl, ch);
       nv_resolve_pair(vp, cl, ch, s, cx, ce);
       if (cost && cx != cl) dl += nv_pair_sq(vp, cx, s2) - nv_pair_sq(vp, cl, s2);
-      if (cu) cu[p] = (uint8_t)ce;
+      if (codes) codes[(elem0 + 16 * (int64_t)uu) / 2 + p] = (uint8_t)ce;
     }
     delta += (double)dl;
+    __syncwarp();
   }
   return delta;
 }
 
+// Task word: pair (bits 0-2) | unit (3-14).
 __device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
-                                        int upr, uint32_t rdiv) {
+                                        int upr, uint32_t rdiv, uint32_t* tasks) {
   double delta = 0.0;
-  for (int i = lane; i < cnt; i += 32) {
-    const int u = (int)q[i];
-    const uint4 a = st[2 * u], b = st[2 * u + 1];
-    const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const uint32_t* vw = reinterpret_cast<const uint32_t*>(st) + 8 * u;
-    const RowParam rp = row_param(ramax[upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)]);
-    if (rp.amax >= F8_EXACT_ROW_AMAX) {
-      delta += f8_exact_unit(vw, rp.s);
-      continue;
-    }
-    const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
+  const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
+  for (int base = 0; base < cnt; base += 32) {   // warp-uniform
+    const int i = base + lane;
     uint32_t pm = 0;
+    int u = 0;
+    if (i < cnt) {
+      u = (int)q[i];
+      const RowParam rp = row_param(ramax[upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)]);
+      if (rp.amax >= F8_EXACT_ROW_AMAX) {
+        delta += f8_exact_unit(words + 8 * u, rp.s);
+      } else {
+        const uint4 a = st[2 * u], b = st[2 * u + 1];
+        const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi);
 #pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      const uint64_t w2 = f2_from_bf16x2(v[p]);
-      pm |= (cvt_e4m3x2(f2_mul_rz(w2, rlo2)) != cvt_e4m3x2(f2_mul_rz(w2, rhi2)) ? 1u : 0u) << p;
+        for (int p = 0; p < 8; ++p) {
+          const uint64_t w2 = f2_from_bf16x2(v[p]);
+          pm |= (cvt_e4m3x2(f2_mul_rz(w2, rlo2)) != cvt_e4m3x2(f2_mul_rz(w2, rhi2)) ? 1u : 0u) << p;
+        }
+      }
     }
+    const int n = __popc(pm);
+    const int incl = warp_incl_scan(n, lane);
+    const int tot = __shfl_sync(FULL, incl, 31);
+    int off = incl - n;
+    for (uint32_t m = pm; m; m &= m - 1) tasks[off++] = (uint32_t)(__ffs(m) - 1) | ((uint32_t)u << 3);
+    __syncwarp();
     float dl = 0.0f;
-    for (; pm; pm &= pm - 1) {
-      const int p = __ffs(pm) - 1;
-      const uint32_t vp = vw[p];
+    for (int t = lane; t < tot; t += 32) {
+      const uint32_t task = tasks[t];
+      const int p = (int)(task & 7u), uu = (int)(task >> 3);
+      const RowParam rp = row_param(ramax[upr == 1 ? uu : (int)__umulhi((uint32_t)uu, rdiv)]);
+      const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
+      const uint32_t vp = words[8 * uu + p];
       const uint64_t w2 = f2_from_bf16x2(vp);
       const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2, rlo2)), ch = cvt_e4m3x2(f2_mul_rz(w2, rhi2));
       const uint32_t cx = f8_resolve_pair(vp, cl, ch, rp.s);
       if (cx != cl) dl += f8_pair_sq(vp, cx, s2) - f8_pair_sq(vp, cl, s2);
     }
     delta += (double)dl;
+    __syncwarp();
   }
   return delta;
 }
@@ -287,6 +334,7 @@ struct ItemCtx {
   uint8_t* codes_it;     // codes of the item's first element
   uint16_t* amax_it;     // group amax of the item's first group
   uint32_t* ramax;       // per-row max |w| (bf16 bits) of this item's rows
+  uint32_t* tasks;       // the warp's fix-up task list
   int64_t elem0;
 };
 
@@ -320,24 +368,32 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
     float rlo, rhi;
     recip_bounds(snv, rlo, rhi);
     const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi), s2 = f2_pack(snv, snv);
-    uint32_t ux = 0, cc[8];
-    float pe = 0.0f, po = 0.0f;   // two accumulation chains
+    uint32_t cw[2], dx[2], q[8];
 #pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      uint32_t ch;
-      nv_bracket(f2_from_bf16x2(v[p]), rlo2, rhi2, cc[p], ch);
-      ux |= cc[p] ^ ch;
-      if (NV) {
-        const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e2m1x2_to_f2(cc[p]), s2));
+    for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
+      float l[8], h[8];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint64_t w2 = f2_from_bf16x2(v[4 * hf + p]);
+        f2_unpack(f2_mul_rz(w2, rlo2), l[2 * p], l[2 * p + 1]);
+        f2_unpack(f2_mul_rz(w2, rhi2), h[2 * p], h[2 * p + 1]);
+      }
+      uint32_t (&qh)[4] = *reinterpret_cast<uint32_t(*)[4]>(q + 4 * hf);
+      nv_codes4(l, h, cw[hf], dx[hf], qh);
+    }
+    const uint32_t ux = dx[0] | dx[1];
+    if (NV) {
+      float pe = 0.0f, po = 0.0f;   // two accumulation chains
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
         if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
         else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
       }
+      A.nv += (valid && !ex) ? pe + po : 0.0f;
     }
-    if (NV) A.nv += (valid && !ex) ? pe + po : 0.0f;
     if (CODES) {   // lanes past the end re-store the last unit's identical bytes
-      const uint32_t cw0 = __byte_perm(__byte_perm(cc[0], cc[1], 0x0040), __byte_perm(cc[2], cc[3], 0x0040), 0x5410);
-      const uint32_t cw1 = __byte_perm(__byte_perm(cc[4], cc[5], 0x0040), __byte_perm(cc[6], cc[7], 0x0040), 0x5410);
-      reinterpret_cast<uint2*>(c.codes_it)[uc] = sw ? make_uint2(cw1, cw0) : make_uint2(cw0, cw1);
+      reinterpret_cast<uint2*>(c.codes_it)[uc] = sw ? make_uint2(cw[1], cw[0]) : make_uint2(cw[0], cw[1]);
       c.amax_it[uc] = (uint16_t)a16b;
       A.tmax = max(A.tmax, a16b);
     }
@@ -348,7 +404,7 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       A.cnt_nv += __popc(bal);
       if (A.cnt_nv > FAST_QCAP - 32) {   // flush early only when the next unit could overflow
         __syncwarp();
-        A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? c.codes_it - c.elem0 / 2 : nullptr, NV);
+        A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? c.codes_it - c.elem0 / 2 : nullptr, NV, c.tasks);
         __syncwarp();
         A.cnt_nv = 0;
       }
@@ -406,14 +462,23 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
   uint32_t ux = 0;
   float pe = 0.0f, po = 0.0f;
 #pragma unroll
-  for (int p = 0; p < 8; ++p) {
-    const uint64_t w2 = f2_from_bf16x2(v[p]);
-    const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2, rlo2));
-    const uint32_t ch = cvt_e4m3x2(f2_mul_rz(w2, rhi2));
-    ux |= cl ^ ch;
-    const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(cl), s2));
-    if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
-    else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
+  for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
+    float l[8], h[8];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint64_t w2 = f2_from_bf16x2(v[4 * hf + p]);
+      f2_unpack(f2_mul_rz(w2, rlo2), l[2 * p], l[2 * p + 1]);
+      f2_unpack(f2_mul_rz(w2, rhi2), h[2 * p], h[2 * p + 1]);
+    }
+    uint32_t dx, q[4];
+    f8_codes4(l, h, dx, q);
+    ux |= dx;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
+      if (p & 1) po = sq2_acc(bf16x2_sub(v[4 * hf + p], rec), po);
+      else pe = sq2_acc(bf16x2_sub(v[4 * hf + p], rec), pe);
+    }
   }
   A.f8 += (valid && !exf) ? pe + po : 0.0f;
   const bool need = valid && (ux != 0 || exf);
@@ -423,7 +488,7 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
     A.cnt_f8 += __popc(bal);
     if (A.cnt_f8 > FAST_QCAP - 32) {
       __syncwarp();
-      A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv);
+      A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks);
       __syncwarp();
       A.cnt_f8 = 0;
     }
@@ -449,6 +514,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t* q_nv = qbase + warp * (2 * FAST_QCAP);
   uint32_t* q_f8 = q_nv + FAST_QCAP;
+  uint32_t* tasks = qbase + NWARPS * 2 * FAST_QCAP + warp * FAST_TASK_CAP;
   const uint32_t lanemask_lt = (1u << lane) - 1u;
   const int64_t n_items = L.item_prefix[L.n];
   const int64_t my_n = n_items > (int64_t)blockIdx.x ? (n_items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
@@ -532,6 +598,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     c.codes_it = CODES ? d.nvfp4_codes + c.elem0 / 2 : nullptr;
     c.amax_it = CODES ? d.nvfp4_amax + c.elem0 / 16 : nullptr;
     c.ramax = ramax_buf + (j & 1) * FAST_MAX_ROWS;
+    c.tasks = tasks;
     const int iters = (c.nunits + FAST_THREADS - 1) / FAST_THREADS;
     const bool warp_rows = (c.upr & 31) == 0;
 
@@ -564,8 +631,8 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     }
     __syncwarp();
     if ((NV || CODES) && A.cnt_nv)
-      A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV);
-    if (F8 && A.cnt_f8) A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv);
+      A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV, c.tasks);
+    if (F8 && A.cnt_f8) A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks);
     A.cnt_nv = A.cnt_f8 = 0;
     __syncthreads();   // stage s and the queues are free again
     if (*abort_flag) {
@@ -587,7 +654,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
 size_t sweep_fast_smem_bytes() {
   return (size_t)FAST_NSTAGE * FAST_STAGE_BYTES + (FAST_NSTAGE + 1) * sizeof(uint64_t) +
          2 * FAST_MAX_ROWS * sizeof(uint32_t) + (FAST_THREADS / 32) * 3 * sizeof(double) +
-         (FAST_THREADS / 32) * 2 * FAST_QCAP * sizeof(uint32_t);
+         (FAST_THREADS / 32) * (2 * FAST_QCAP + FAST_TASK_CAP) * sizeof(uint32_t);
 }
 
 template <bool NV, bool MX, bool F8, bool CODES>
