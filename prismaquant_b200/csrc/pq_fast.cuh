@@ -30,8 +30,14 @@ __device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
 // bf16 pair {lo, hi} (one 32-bit word) -> float32 pair
+// (each half as v * 1 + (-0), one mixed-precision FMA: exact, keeps -0, and
+// runs on the FMA pipe instead of the integer shift/mask units)
 __device__ __forceinline__ uint64_t f2_from_bf16x2(uint32_t v) {
-  return f2_pack(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+  float lo, hi;
+  asm("{\n\t.reg .b16 a, b, one;\n\tmov.b32 {a, b}, %2;\n\tmov.b16 one, 0x3F80;\n\t"
+      "fma.rn.f32.bf16 %0, a, one, 0f80000000;\n\tfma.rn.f32.bf16 %1, b, one, 0f80000000;\n\t}"
+      : "=f"(lo), "=f"(hi) : "r"(v));
+  return f2_pack(lo, hi);
 }
 __device__ __forceinline__ uint64_t f2_mul_rz(uint64_t a, uint64_t b) {
   uint64_t d;

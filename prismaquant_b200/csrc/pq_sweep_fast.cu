@@ -9,9 +9,11 @@
 //    reconstruction -> bf16x2 error -> mixed-precision square-accumulate;
 //  * MXFP8 (power-of-two scale): the E4M3 rounding is an integer rounding of
 //    the bf16 bit pattern, two elements per 32-bit operation (low 4 mantissa
-//    bits, ties to the lower value), saturated at 448 * 2^e by a packed
-//    magnitude min; its exponent is a closed form of the group amax bits
-//    (e = E - 136 + (mantissa >= 31)), checked over every bf16 amax;
+//    bits), saturated at 448 * 2^e by a packed magnitude min; its exponent is
+//    a closed form of the group amax bits (e = E - 136 + (mantissa >= 31)),
+//    checked over every bf16 amax.  Only the squared error is needed, and at a
+//    tie both neighbours are 8 ulp away (also when the upper one saturates), so
+//    the magnitude is rounded half-up whatever the reference's tie rule;
 //  * a unit whose bracket is ambiguous (or that has values outside the fast
 //    path's range) recomputes that format exactly, as the first-principles
 //    kernel does.
@@ -422,8 +424,8 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
     float pe = 0.0f, po = 0.0f;
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
-      const uint32_t neg = (v[p] >> 15) & 0x00010001u;
-      const uint32_t rq = (v[p] + 0x00070007u + neg) & 0xFFF0FFF0u;   // ties to the lower value
+      // magnitude rounded half-up (a finite bf16 half never carries into its sign bit or the next half)
+      const uint32_t rq = (v[p] + 0x00080008u) & 0xFFF0FFF0u;
       const uint32_t q = bf16x2_minabs(rq, m448x2);                   // saturate |q| at 448 * 2^e
       if (p & 1) po = sq2_acc(bf16x2_sub(v[p], q), po);
       else pe = sq2_acc(bf16x2_sub(v[p], q), pe);

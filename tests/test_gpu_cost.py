@@ -137,3 +137,56 @@ def test_fast_sweep_gaussian_rows_exact():
     for i in range(bits.shape[0]):
         for s in specs:
             assert_rel(res[str(i)][s.name], O.cost_mse(bits[i:i + 1], s.name), 2e-6, f"row {i} {s.name}")
+
+
+def _tie_rows(n_rows, seed):
+    """32-element rows seeded with the values where the fast path's bracket is ambiguous:
+    NVFP4 near-ties m * fl(amax/6) for every E2M1 midpoint m, FP8 near-ties m * fl(row_max/448) for
+    E4M3 midpoints, MXFP8 bit patterns whose low 4 mantissa bits are 1000, both signs, plus
+    subnormal and signed-zero elements."""
+    rng = np.random.default_rng(seed)
+    e2m1_mid = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], dtype=np.float32)
+    e4m3 = O.e4m3_codebook()
+    e4m3 = np.unique(np.abs(e4m3[np.isfinite(e4m3)]))
+    e4m3_mid = ((e4m3[:-1] + e4m3[1:]) / 2).astype(np.float32)
+    rows = []
+    for _ in range(n_rows):
+        amax_bits = np.uint16(rng.integers(0x3C00, 0x4100))          # row/group max in [2^-7, 8)
+        amax = O.bf16_bits_to_f32(np.array([amax_bits]))[0]
+        s_nv = np.float32(amax / np.float32(6))
+        s_f8 = np.float32(amax / np.float32(448))
+        cand = np.concatenate([e2m1_mid * s_nv, rng.choice(e4m3_mid, 16) * s_f8]).astype(np.float32)
+        cb = O.f32_to_bf16_bits(cand)
+        cb = np.concatenate([cb, cb + 1, cb - 1]).astype(np.uint16)   # the near-tie value and neighbours
+        picks = rng.choice(cb, 27)
+        mx_tie = ((rng.integers(0x3800, 0x3F00, 3) & 0xFFF0) | 0x8).astype(np.uint16)
+        extra = np.array([0x0001, 0x8000], dtype=np.uint16)          # a subnormal and -0.0
+        r = np.concatenate([picks, mx_tie, extra])
+        r = r ^ (rng.integers(0, 2, r.size).astype(np.uint16) << 15)  # random signs
+        r[rng.integers(0, 16)] = amax_bits                            # each 16-group has a known max
+        r[16 + rng.integers(0, 16)] = amax_bits
+        rows.append(r[:32])
+    return np.stack(rows).astype(np.uint16)
+
+
+def test_fast_sweep_tie_rows_exact():
+    """Rows built from near-tie values: per-row MSE of every format (rel 2e-6, the fp32 partial-sum
+    noise) and the fused NVFP4 export bytes (bit-exact) against the oracle."""
+    from prismaquant_b200 import export_native_compressed as enc
+    from tests._helpers import u8_of
+    rows = _tie_rows(600, seed=5)
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3")]
+    named = {str(i): to_cuda_bf16(r.reshape(1, 32)) for i, r in enumerate(rows)}
+    costs, outs = enc.sweep_and_export(named, specs)
+    bad = []
+    for i, r in enumerate(rows):
+        b = r.reshape(1, 32)
+        for s in specs:
+            ref = O.cost_mse(b, s.name)
+            got = costs[str(i)][s.name]
+            if not (got == ref or abs(got - ref) <= 2e-6 * max(abs(ref), 1e-38)):
+                bad.append((i, s.name, got, ref))
+        p, sc, g = O.nvfp4_pack(O.bf16_bits_to_f32(b))
+        if not (np.array_equal(u8_of(outs[str(i)][0]), p) and np.array_equal(u8_of(outs[str(i)][1]), sc)):
+            bad.append((i, "export"))
+    assert not bad, bad[:10]
