@@ -210,7 +210,7 @@ __device__ __forceinline__ int warp_incl_scan(int x, int lane) {
 // busiest lane.  Each resolved pair adds its exact squared errors minus the
 // main loop's provisional ones and rewrites its export code byte.
 // Task word: pair (bits 0-2) | unit (3-14) | group amax bf16 bits (15-29).
-__device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
+__device__ __forceinline__ double nv_fixup_body(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
                                         uint8_t* codes, bool cost, uint32_t* tasks) {
   double delta = 0.0;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
@@ -267,7 +267,7 @@ __device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4*
 }
 
 // Task word: pair (bits 0-2) | unit (3-14).
-__device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
+__device__ __forceinline__ double f8_fixup_body(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
                                         int upr, uint32_t rdiv, uint32_t* tasks) {
   double delta = 0.0;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
@@ -313,6 +313,17 @@ __device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4*
     __syncwarp();
   }
   return delta;
+}
+
+// Out-of-line copies for the rare early flush inside the per-unit loops (the
+// loop bodies stay small); the end-of-item resolution inlines the bodies.
+__device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
+                                        uint8_t* codes, bool cost, uint32_t* tasks) {
+  return nv_fixup_body(q, cnt, st, lane, elem0, codes, cost, tasks);
+}
+__device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
+                                        int upr, uint32_t rdiv, uint32_t* tasks) {
+  return f8_fixup_body(q, cnt, st, lane, ramax, upr, rdiv, tasks);
 }
 
 // Tensor index of item `item`, scanning forward from the previous one (items
@@ -633,8 +644,8 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     }
     __syncwarp();
     if ((NV || CODES) && A.cnt_nv)
-      A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV, c.tasks);
-    if (F8 && A.cnt_f8) A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks);
+      A.dnv += nv_fixup_body(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV, c.tasks);
+    if (F8 && A.cnt_f8) A.df8 += f8_fixup_body(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks);
     A.cnt_nv = A.cnt_f8 = 0;
     __syncthreads();   // stage s and the queues are free again
     if (*abort_flag) {
