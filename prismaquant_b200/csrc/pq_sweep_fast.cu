@@ -210,8 +210,9 @@ __device__ __forceinline__ int warp_incl_scan(int x, int lane) {
 // busiest lane.  Each resolved pair adds its exact squared errors minus the
 // main loop's provisional ones and rewrites its export code byte.
 // Task word: pair (bits 0-2) | unit (3-14) | group amax bf16 bits (15-29).
-__device__ __forceinline__ double nv_fixup_body(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
-                                        uint8_t* codes, bool cost, uint32_t* tasks) {
+__device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
+                                               int lane, int64_t elem0, uint8_t* codes, bool cost, uint32_t* tasks) {
+  const int cnt = c0 + c1;   // entries q0[0..c0) then q1[0..c1)
   double delta = 0.0;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
   for (int base = 0; base < cnt; base += 32) {   // warp-uniform
@@ -219,7 +220,7 @@ __device__ __forceinline__ double nv_fixup_body(const uint32_t* q, int cnt, cons
     uint32_t pm = 0, a16b = 0;
     int u = 0;
     if (i < cnt) {
-      u = (int)q[i];
+      u = (int)(i < c0 ? q0[i] : q1[i - c0]);
       const uint4 a = st[2 * u], b = st[2 * u + 1];
       const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
       a16b = unit_absmax(v);
@@ -267,8 +268,10 @@ __device__ __forceinline__ double nv_fixup_body(const uint32_t* q, int cnt, cons
 }
 
 // Task word: pair (bits 0-2) | unit (3-14).
-__device__ __forceinline__ double f8_fixup_body(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
-                                        int upr, uint32_t rdiv, uint32_t* tasks) {
+__device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
+                                               int lane, const uint32_t* ramax, int upr, uint32_t rdiv,
+                                               uint32_t* tasks) {
+  const int cnt = c0 + c1;
   double delta = 0.0;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
   for (int base = 0; base < cnt; base += 32) {   // warp-uniform
@@ -276,7 +279,7 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q, int cnt, cons
     uint32_t pm = 0;
     int u = 0;
     if (i < cnt) {
-      u = (int)q[i];
+      u = (int)(i < c0 ? q0[i] : q1[i - c0]);
       const RowParam rp = row_param(ramax[upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)]);
       if (rp.amax >= F8_EXACT_ROW_AMAX) {
         delta += f8_exact_unit(words + 8 * u, rp.s);
@@ -319,11 +322,11 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q, int cnt, cons
 // loop bodies stay small); the end-of-item resolution inlines the bodies.
 __device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
                                         uint8_t* codes, bool cost, uint32_t* tasks) {
-  return nv_fixup_body(q, cnt, st, lane, elem0, codes, cost, tasks);
+  return nv_fixup_body(q, cnt, q, 0, st, lane, elem0, codes, cost, tasks);
 }
 __device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
                                         int upr, uint32_t rdiv, uint32_t* tasks) {
-  return f8_fixup_body(q, cnt, st, lane, ramax, upr, rdiv, tasks);
+  return f8_fixup_body(q, cnt, q, 0, st, lane, ramax, upr, rdiv, tasks);
 }
 
 // Tensor index of item `item`, scanning forward from the previous one (items
@@ -508,6 +511,9 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
   }
 }
 
+// Named barrier over the 64 threads of warps 2k and 2k+1 (id 1 + k; id 0 is __syncthreads).
+__device__ __forceinline__ void pair_barrier(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+
 __device__ __forceinline__ void fold(float& f, double& d) {
   d += (double)f;
   f = 0.0f;
@@ -528,6 +534,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
   uint32_t* q_nv = qbase + warp * (2 * FAST_QCAP);
   uint32_t* q_f8 = q_nv + FAST_QCAP;
   uint32_t* tasks = qbase + NWARPS * 2 * FAST_QCAP + warp * FAST_TASK_CAP;
+  volatile int* qcnt = reinterpret_cast<volatile int*>(qbase + NWARPS * (2 * FAST_QCAP + FAST_TASK_CAP));   // [NWARPS][2]
   const uint32_t lanemask_lt = (1u << lane) - 1u;
   const int64_t n_items = L.item_prefix[L.n];
   const int64_t my_n = n_items > (int64_t)blockIdx.x ? (n_items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
@@ -643,9 +650,33 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       fold(A.f8, A.df8);
     }
     __syncwarp();
-    if ((NV || CODES) && A.cnt_nv)
-      A.dnv += nv_fixup_body(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV, c.tasks);
-    if (F8 && A.cnt_f8) A.df8 += f8_fixup_body(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks);
+    if (F8 && (NV || CODES)) {
+      // Warps work in pairs: the even warp resolves both warps' NVFP4 queues, the odd warp
+      // both FP8 queues, so each drains one fuller batch instead of two small ones.  The
+      // pair barrier also orders the partner's code stores before any fix-up rewrite.
+      if (lane == 0) {
+        qcnt[2 * warp] = A.cnt_nv;
+        qcnt[2 * warp + 1] = A.cnt_f8;
+      }
+      pair_barrier(1 + (warp >> 1));
+      const int pw = warp ^ 1;
+      const uint32_t* pq = qbase + pw * (2 * FAST_QCAP);
+      if ((warp & 1) == 0) {
+        const int pc = qcnt[2 * pw];
+        if ((NV || CODES) && A.cnt_nv + pc)
+          A.dnv += nv_fixup_body(q_nv, A.cnt_nv, pq, pc, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV,
+                                 c.tasks);
+      } else {
+        const int pc = qcnt[2 * pw + 1];
+        if (A.cnt_f8 + pc) A.df8 += f8_fixup_body(q_f8, A.cnt_f8, pq + FAST_QCAP, pc, c.st, lane, c.ramax, c.upr,
+                                                  c.rdiv, c.tasks);
+      }
+    } else {
+      if ((NV || CODES) && A.cnt_nv)
+        A.dnv += nv_fixup_body(q_nv, A.cnt_nv, q_nv, 0, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV,
+                               c.tasks);
+      if (F8 && A.cnt_f8) A.df8 += f8_fixup_body(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks);
+    }
     A.cnt_nv = A.cnt_f8 = 0;
     __syncthreads();   // stage s and the queues are free again
     if (*abort_flag) {
@@ -667,7 +698,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
 size_t sweep_fast_smem_bytes() {
   return (size_t)FAST_NSTAGE * FAST_STAGE_BYTES + (FAST_NSTAGE + 1) * sizeof(uint64_t) +
          2 * FAST_MAX_ROWS * sizeof(uint32_t) + (FAST_THREADS / 32) * 3 * sizeof(double) +
-         (FAST_THREADS / 32) * (2 * FAST_QCAP + FAST_TASK_CAP) * sizeof(uint32_t);
+         (FAST_THREADS / 32) * (2 * FAST_QCAP + FAST_TASK_CAP + 2) * sizeof(uint32_t);
 }
 
 template <bool NV, bool MX, bool F8, bool CODES>
