@@ -36,7 +36,23 @@ typedef enum {
   PQ_FMT_MXFP8 = 1,       /* E4M3 codebook, groups of 32, E8M0 scale = 2^round(log2(amax/448)) */
   PQ_FMT_FP8_CHANNEL = 2, /* E4M3 codebook, one amax/448 scale per row (FP8_E4M3, group_size=0) */
   PQ_FMT_BF16 = 3,        /* passthrough: error 0 */
-  PQ_NUM_FMTS = 4
+  PQ_NUM_FMTS = 4,        /* formats of the fused sweep (pq_sweep_sse) */
+  /* The rest of the registry, served by pq_cost_qdq and pq_format_sse with exact
+   * first-principles arithmetic (codebooks format_registry.py:237-300, RTN
+   * :194-233, symmetric integer RTN :147-172): */
+  PQ_FMT_MXFP4 = 4,          /* E2M1, groups of 32, E8M0 scale (format_registry.py:391-398) */
+  PQ_FMT_MXFP6_E3M2 = 5,     /* E3M2, groups of 32, E8M0 scale (:400-407) */
+  PQ_FMT_MXFP6_E2M3 = 6,     /* E2M3, groups of 32, E8M0 scale (:409-416) */
+  PQ_FMT_MXFP8_E5M2 = 7,     /* E5M2, groups of 32, E8M0 scale (:436-443) */
+  PQ_FMT_FP8_E5M2 = 8,       /* E5M2, one amax/cmax scale per row (:466-473) */
+  PQ_FMT_NVFP3 = 9,          /* E2M0 {0, .25, .5, 1, 2}, groups of 16, real scale (:505-514) */
+  PQ_FMT_INT3 = 10,          /* symmetric INT3, groups of 16 (:483-491) */
+  PQ_FMT_INT2 = 11,          /* symmetric INT2, groups of 16 (:492-500) */
+  PQ_FMT_INT8_CHANNEL = 12,  /* symmetric INT8, one scale per row (INT8_W8A16, :516-523) */
+  PQ_FMT_INT4_G128 = 13,     /* symmetric INT4, groups of 128 (INT4_W4A16_g128, :525-533) */
+  PQ_FMT_FP8_E4M3_G128 = 14, /* E4M3, groups of 128, real scale: FP8_SOURCE as the batched cost
+                                path quantizes it (measure_quant_cost.py:516-548) */
+  PQ_NUM_FMTS_ALL = 15
 } pq_format;
 
 #define PQ_FMT_BIT(f) (1u << (f))
@@ -77,11 +93,22 @@ int pq_sweep_sse(const pq_sweep_tensor* tensors, int n_tensors, double* sse, voi
 
 /*
  * Cost-path quantize->dequantize of one format: w_hat = qdq_f(w) as bf16,
- * same shape.  Replaces FormatSpec.quantize_dequantize for NVFP4 / MXFP8 /
- * FP8_E4M3 / BF16 (format_registry.py:47-48, 194-233) and
- * `_batched_quantize` (measure_quant_cost.py:532-548).
+ * same shape.  Replaces FormatSpec.quantize_dequantize (format_registry.py:47-48,
+ * 147-233) and `_batched_quantize` (measure_quant_cost.py:532-548) for every
+ * format id of pq_format (0 .. PQ_NUM_FMTS_ALL - 1).
  */
 int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t* w_hat, void* stream);
+
+/*
+ * Sum of squared errors of one format over one bf16 tensor [rows, cols]:
+ * ADDS sum((W - qdq_fmt(W))^2) (bf16 subtraction, fp32 square) to *sse
+ * (fp64, device; zero it first).  fmt is one of PQ_FMT_MXFP4 ..
+ * PQ_NUM_FMTS_ALL - 1, or PQ_FMT_BF16 (adds nothing); NVFP4 / MXFP8 / FP8
+ * per channel go through pq_sweep_sse.  Replaces the per-format chain of
+ * measure_quant_cost.py:627-632 for the formats outside the fused sweep.
+ * No counterpart in the reference's API as a single call.
+ */
+int pq_format_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, void* stream);
 
 /*
  * NVFP4 export, pass 1: E2M1 codes (abs-codebook RTN, ties toward zero,

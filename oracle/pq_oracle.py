@@ -231,7 +231,48 @@ def e4m3_codebook() -> np.ndarray:
     return np.array(sorted(c for c in codes if abs(c) <= 448.0), dtype=F32)
 
 
-CODEBOOKS = {"fp4_e2m1": e2m1_codebook(), "fp8_e4m3": e4m3_codebook()}
+def e3m2_codebook() -> np.ndarray:
+    """format_registry.py:244-251: (1 + m/4) 2^(exp-3), exp 0..7, m 0..3 (no subnormals), and 0."""
+    codes = {0.0}
+    for exp in range(8):
+        for m in range(4):
+            v = (1 + m / 4) * 2.0 ** (exp - 3)
+            codes.update((v, -v))
+    return np.array(sorted(codes), dtype=F32)
+
+
+def e2m3_codebook() -> np.ndarray:
+    """format_registry.py:254-261: (1 + m/8) 2^(exp-1), exp 0..3, m 0..7 (no subnormals), and 0."""
+    codes = {0.0}
+    for exp in range(4):
+        for m in range(8):
+            v = (1 + m / 8) * 2.0 ** (exp - 1)
+            codes.update((v, -v))
+    return np.array(sorted(codes), dtype=F32)
+
+
+def e2m0_codebook() -> np.ndarray:
+    """format_registry.py:264-272: 2^(exp-2), exp 0..3, and 0: {0, +-.25, +-.5, +-1, +-2}."""
+    codes = {0.0}
+    for exp in range(4):
+        v = 2.0 ** (exp - 2)
+        codes.update((v, -v))
+    return np.array(sorted(codes), dtype=F32)
+
+
+def e5m2_codebook() -> np.ndarray:
+    """format_registry.py:291-300: subnormals (m/4) 2^-14 and (1 + m/4) 2^(exp-15) for exp 1..31.
+    Exponent 31 is kept as finite values, so the largest magnitude is 1.75 * 2^16 = 114688."""
+    codes = {0.0}
+    for exp in range(32):
+        for m in range(4):
+            v = (m / 4) * 2.0 ** -14 if exp == 0 else (1 + m / 4) * 2.0 ** (exp - 15)
+            codes.update((v, -v))
+    return np.array(sorted(codes), dtype=F32)
+
+
+CODEBOOKS = {"fp4_e2m1": e2m1_codebook(), "fp8_e4m3": e4m3_codebook(), "fp6_e3m2": e3m2_codebook(),
+             "fp6_e2m3": e2m3_codebook(), "fp3_e2m0": e2m0_codebook(), "fp8_e5m2": e5m2_codebook()}
 
 # (codebook, group_size, mx_scale) for the formats on the hot path,
 # format_registry.py:368-376 (NVFP4), :418-426 (MXFP8), :457-465 (FP8_E4M3).
@@ -242,7 +283,21 @@ COST_FORMATS = {
     "MXFP8_E4M3": ("fp8_e4m3", 32, True),
     "MXFP8A16": ("fp8_e4m3", 32, True),
     "FP8_E4M3": ("fp8_e4m3", 0, False),
+    # the rest of the registry: format_registry.py:391-398 (MXFP4), :400-416 (MXFP6), :436-443
+    # (MXFP8_E5M2), :466-473 (FP8_E5M2), :505-514 (NVFP3)
+    "MXFP4": ("fp4_e2m1", 32, True),
+    "MXFP6_E3M2": ("fp6_e3m2", 32, True),
+    "MXFP6_E2M3": ("fp6_e2m3", 32, True),
+    "MXFP8_E5M2": ("fp8_e5m2", 32, True),
+    "FP8_E5M2": ("fp8_e5m2", 0, False),
+    "NVFP3": ("fp3_e2m0", 16, False),
 }
+
+# Symmetric uniform-integer formats (bits, group_size): format_registry.py:483-500 (INT3, INT2),
+# :516-533 (INT8_W8A16 per channel, INT4_W4A16_g128).
+INT_FORMATS = {"INT3": (3, 16), "INT2": (2, 16), "INT8_W8A16": (8, 0), "INT4_W4A16_g128": (4, 128)}
+FORMAT_ALIASES = {"NVINT2": "INT2", "NVINT3": "INT3"}
+IDENTITY_FORMATS = ("BF16", "FP8_SOURCE")   # quantize_dequantize = clone (format_registry.py:536-576)
 
 # ---------------------------------------------------------------------------
 # Cost path: RTN quantize-dequantize + MSE_W
@@ -264,9 +319,17 @@ def cost_qdq_f32(w_bits: np.ndarray, fmt: str) -> np.ndarray:
     """Cost-path quantize->dequantize of a bf16 tensor (bit patterns),
     returning the bf16-rounded reconstruction as float32 (format_registry.py:194-233).
     """
-    if fmt == "BF16":
+    fmt = FORMAT_ALIASES.get(fmt, fmt)
+    if fmt in IDENTITY_FORMATS:
         return bf16_bits_to_f32(w_bits)
+    if fmt in INT_FORMATS:
+        return int_qdq_f32(w_bits, *INT_FORMATS[fmt])
     cb_name, group_size, mx = COST_FORMATS[fmt]
+    return codebook_qdq_f32(w_bits, cb_name, group_size, mx)
+
+
+def codebook_qdq_f32(w_bits: np.ndarray, cb_name: str, group_size: int, mx: bool) -> np.ndarray:
+    """_rtn_fp_codebook (format_registry.py:194-233) for one codebook, group size and scale mode."""
     cb = CODEBOOKS[cb_name]
     cmax = F32(np.abs(cb).max())
     w32 = bf16_bits_to_f32(w_bits)
@@ -285,6 +348,52 @@ def cost_qdq_f32(w_bits: np.ndarray, fmt: str) -> np.ndarray:
     q = np.where(choose_hi, hi, lo).astype(F32)
     rec = (q * scale).astype(F32)
     return bf16_round(rec).reshape(shape)
+
+
+# measure_quant_cost._batched_quantize (measure_quant_cost.py:516-548) dispatches on the element
+# dtype, not on the format's own quantize_dequantize: codebook families (E2M1, E3M2, E2M3, E4M3,
+# E5M2) take the format's group size and E8M0 snapping for family "mx", integer families the
+# format's bits and group, bfloat16 a clone, anything else (fp3_e2m0 = NVFP3) raises.  So
+# FP8_SOURCE (E4M3, group 128, family "fp") is an E4M3 RTN with real g128 scales there, although
+# its per-Linear quantize_dequantize is a clone.
+# fmt -> (element dtype, family, weight bits, group size), format_registry.py:368-576
+REGISTRY_DTYPES = {
+    "NVFP4": ("fp4_e2m1", "nv", 4, 16), "NVFP4A16": ("fp4_e2m1", "nv", 4, 16),
+    "MXFP4": ("fp4_e2m1", "mx", 4, 32), "MXFP6_E3M2": ("fp6_e3m2", "mx", 6, 32),
+    "MXFP6_E2M3": ("fp6_e2m3", "mx", 6, 32), "MXFP8": ("fp8_e4m3", "mx", 8, 32),
+    "MXFP8_E4M3": ("fp8_e4m3", "mx", 8, 32), "MXFP8_E5M2": ("fp8_e5m2", "mx", 8, 32),
+    "MXFP8A16": ("fp8_e4m3", "mx", 8, 32), "FP8_E4M3": ("fp8_e4m3", "fp", 8, 0),
+    "FP8_E5M2": ("fp8_e5m2", "fp", 8, 0), "INT3": ("int3", "nv", 3, 16), "INT2": ("int2", "nv", 2, 16),
+    "NVFP3": ("fp3_e2m0", "nv", 3, 16), "INT8_W8A16": ("int8", "int", 8, 0),
+    "INT4_W4A16_g128": ("int4", "int", 4, 128), "BF16": ("bfloat16", "fp", 16, 0),
+    "FP8_SOURCE": ("fp8_e4m3", "fp", 8, 128),
+}
+_BATCHED_CODEBOOKS = ("fp4_e2m1", "fp6_e3m2", "fp6_e2m3", "fp8_e4m3", "fp8_e5m2")
+
+
+def batched_qdq_f32(w_bits: np.ndarray, fmt: str) -> np.ndarray:
+    """measure_quant_cost._batched_quantize on a stacked [N, out, in] (or 2-D) bf16 tensor."""
+    elt, fam, bits, group = REGISTRY_DTYPES[FORMAT_ALIASES.get(fmt, fmt)]
+    if elt in _BATCHED_CODEBOOKS:
+        return codebook_qdq_f32(w_bits, elt, group, fam == "mx")
+    if elt.startswith("int"):
+        return int_qdq_f32(w_bits, bits, group)
+    if elt == "bfloat16":
+        return bf16_bits_to_f32(w_bits)
+    raise ValueError(f"Unknown weight_element_dtype {elt!r} for batched RTN")
+
+
+def int_qdq_f32(w_bits: np.ndarray, bits: int, group_size: int) -> np.ndarray:
+    """_rtn_uniform_int, symmetric (format_registry.py:147-172): scale = max(amax, 1e-8) / (2^(b-1) - 1),
+    q = round_half_even(w / scale) clamped to [-2^(b-1), 2^(b-1) - 1], W_hat = bf16(q * scale)."""
+    w32 = bf16_bits_to_f32(w_bits)
+    shape = w32.shape
+    w2 = _grouped(w32, group_size)
+    levels = (1 << (bits - 1)) - 1
+    amax = np.maximum(np.abs(w2).max(axis=-1, keepdims=True), F32(1e-8))
+    scale = (amax / F32(levels)).astype(F32)
+    q = np.clip(np.rint((w2 / scale).astype(F32)), -levels - 1, levels).astype(F32)
+    return bf16_round((q * scale).astype(F32)).reshape(shape)
 
 
 def cost_err_bf16(w_bits: np.ndarray, fmt: str) -> np.ndarray:

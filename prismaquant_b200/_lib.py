@@ -20,11 +20,17 @@ LIB_PATH = Path(os.environ.get("PQ_B200_LIB", Path(__file__).resolve().parent / 
 PQ_OK, PQ_ERR_NULL, PQ_ERR_SHAPE, PQ_ERR_ALIGN, PQ_ERR_FORMAT, PQ_ERR_CUDA, PQ_ERR_LIMIT, PQ_ERR_DEVICE = range(8)
 FMT_NVFP4, FMT_MXFP8, FMT_FP8_CHANNEL, FMT_BF16 = range(4)
 FMT_IDS = {"NVFP4": FMT_NVFP4, "MXFP8": FMT_MXFP8, "FP8_E4M3": FMT_FP8_CHANNEL, "BF16": FMT_BF16}
+# the rest of the registry (pq_format ids 4..14), served by the exact codebook / integer kernel
+EXT_FMT_IDS = {"MXFP4": 4, "MXFP6_E3M2": 5, "MXFP6_E2M3": 6, "MXFP8_E5M2": 7, "FP8_E5M2": 8, "NVFP3": 9,
+               "INT3": 10, "INT2": 11, "INT8_W8A16": 12, "INT4_W4A16_g128": 13, "FP8_E4M3_G128": 14}
+FMT_IDS.update(EXT_FMT_IDS)
+NUM_FMTS_ALL = 15
 
 EXPORTED = [
     "pq_sweep_sse", "pq_cost_qdq", "pq_nvfp4_codes", "pq_nvfp4_scales", "pq_nvfp4_pack",
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
+    "pq_format_sse",
 ]
 
 
@@ -59,6 +65,7 @@ def load() -> ctypes.CDLL:
     sig = {
         "pq_sweep_sse": [ctypes.POINTER(SweepTensor), I, P, V],
         "pq_cost_qdq": [P, I64, I64, I, P, V],
+        "pq_format_sse": [P, I64, I64, I, P, V],
         "pq_nvfp4_codes": [P, I64, I64, I64, P, P, P, V],
         "pq_nvfp4_scales": [I, ctypes.POINTER(P), ctypes.POINTER(I64), P, ctypes.POINTER(ctypes.c_int32), P,
                             ctypes.POINTER(P), P, V],
@@ -183,6 +190,17 @@ def cost_qdq(w: torch.Tensor, fmt: str) -> torch.Tensor:
     _check(lib.pq_cost_qdq(_ptr(wb), rows, cols, fid, _ptr(out), _stream(wb)), "pq_cost_qdq",
            f"cannot reshape rows of {cols} into groups for {fmt}")
     return out if w.dtype == torch.bfloat16 else out.to(w.dtype)
+
+
+def format_sse(w: torch.Tensor, fmt: str, sse: torch.Tensor) -> None:
+    """Adds sum((W - qdq_fmt(W))^2) into the fp64 device scalar `sse` (one of the extended
+    formats, or BF16); asynchronous on the current stream."""
+    wb = as_bf16_cuda(w, "format_sse")
+    if wb.numel() == 0:
+        return
+    cols = wb.shape[-1]
+    _check(load().pq_format_sse(_ptr(wb), wb.numel() // cols, cols, FMT_IDS[fmt], _ptr(sse), _stream(wb)),
+           "pq_format_sse", f"cannot reshape rows of {cols} into groups for {fmt}")
 
 
 # ---------------------------------------------------------------------------

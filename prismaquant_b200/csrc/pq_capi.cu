@@ -198,9 +198,26 @@ int pq_sweep_sse(const pq_sweep_tensor* ts, int n, double* sse, void* stream_) {
   return flush_staged(staged, pq::MODE_SSE, 0, stream);
 }
 
+int pq_format_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, void* stream_) {
+  if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (fmt != PQ_FMT_BF16 && !pq::xfmt_known(fmt)) return PQ_ERR_FORMAT;
+  if (fmt != PQ_FMT_BF16 && pq::xfmt_group(fmt, cols) == 0) return PQ_ERR_SHAPE;
+  if (rows == 0 || fmt == PQ_FMT_BF16) return PQ_OK;
+  if (!w || !sse) return PQ_ERR_NULL;
+  return cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse, nullptr, pq::MODE_SSE, num_sms_current(),
+                                     (cudaStream_t)stream_));
+}
+
 int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t* w_hat, void* stream_) {
   if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
-  if (fmt < 0 || fmt >= PQ_NUM_FMTS) return PQ_ERR_FORMAT;
+  if (fmt < 0 || fmt >= PQ_NUM_FMTS_ALL) return PQ_ERR_FORMAT;
+  if (pq::xfmt_known(fmt)) {
+    if (pq::xfmt_group(fmt, cols) == 0) return PQ_ERR_SHAPE;
+    if (rows == 0) return PQ_OK;
+    if (!w || !w_hat) return PQ_ERR_NULL;
+    return cuda_status(pq::launch_xfmt(w, rows, cols, fmt, nullptr, w_hat, pq::MODE_QDQ, num_sms_current(),
+                                       (cudaStream_t)stream_));
+  }
   if (rows == 0) return PQ_OK;
   if (!w || !w_hat) return PQ_ERR_NULL;
   cudaStream_t stream = (cudaStream_t)stream_;

@@ -1,0 +1,209 @@
+// Exact cost-path quantize-dequantize for the rest of the format registry
+// (MXFP4, MXFP6 E3M2/E2M3, MXFP8/FP8 E5M2, NVFP3, the symmetric INT formats,
+// and E4M3 with real per-128 scales), first-principles arithmetic:
+//
+//  * codebook formats follow _rtn_fp_codebook (format_registry.py:194-233):
+//    scale = max(amax, 1e-8) / cmax (E8M0-snapped for the MX family),
+//    x = fl(w / scale), x placed in the sorted signed codebook as
+//    torch.bucketize does (first entry >= x), the neighbour chosen only when
+//    strictly closer in float32 (ties to the lower value), W_hat = bf16(q * scale);
+//  * integer formats follow _rtn_uniform_int, symmetric (format_registry.py:147-172):
+//    scale = max(amax, 1e-8) / (2^(b-1) - 1), q = round_half_even(w / scale)
+//    clamped to [-2^(b-1), 2^(b-1) - 1], W_hat = bf16(q * scale).
+//
+// The codebooks are generated from the same definitions as the reference's
+// (format_registry.py:237-300): FP6 and FP3 have no subnormals, and the E5M2
+// codebook keeps exponent 31 as finite values (largest magnitude 114688).
+// These formats are not on the fused hot path; one warp per row is plenty.
+#include "pq_common.cuh"
+#include "pq_internal.h"
+
+namespace pq {
+
+enum CodebookId { CB_E2M1 = 0, CB_E3M2, CB_E2M3, CB_E2M0, CB_E4M3, CB_E5M2 };
+
+struct XFmt {
+  bool is_int;
+  int cb;      // codebook (is_int == false)
+  int bits;    // integer width (is_int == true)
+  int group;   // 0: one group per row
+  bool mx;     // E8M0-snapped scale
+};
+
+__host__ __device__ inline bool xfmt_known(int fmt) { return fmt >= PQ_FMT_MXFP4 && fmt < PQ_NUM_FMTS_ALL; }
+
+// format_registry.py:391-533 and measure_quant_cost.py:516-548 (FP8_SOURCE's batched form)
+__host__ __device__ inline XFmt xfmt_of(int fmt) {
+  switch (fmt) {
+    case PQ_FMT_MXFP4: return {false, CB_E2M1, 0, 32, true};
+    case PQ_FMT_MXFP6_E3M2: return {false, CB_E3M2, 0, 32, true};
+    case PQ_FMT_MXFP6_E2M3: return {false, CB_E2M3, 0, 32, true};
+    case PQ_FMT_MXFP8_E5M2: return {false, CB_E5M2, 0, 32, true};
+    case PQ_FMT_FP8_E5M2: return {false, CB_E5M2, 0, 0, false};
+    case PQ_FMT_NVFP3: return {false, CB_E2M0, 0, 16, false};
+    case PQ_FMT_INT3: return {true, 0, 3, 16, false};
+    case PQ_FMT_INT2: return {true, 0, 2, 16, false};
+    case PQ_FMT_INT8_CHANNEL: return {true, 0, 8, 0, false};
+    case PQ_FMT_INT4_G128: return {true, 0, 4, 128, false};
+    default: return {false, CB_E4M3, 0, 128, false};   // PQ_FMT_FP8_E4M3_G128
+  }
+}
+
+// Ascending non-negative magnitudes of a codebook (mags[0] = 0); returns their count.
+__device__ int codebook_magnitudes(int cb, float* mags) {
+  int n = 0;
+  mags[n++] = 0.0f;
+  switch (cb) {
+    case CB_E2M1: {
+      const float v[7] = {0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+      for (int i = 0; i < 7; ++i) mags[n++] = v[i];
+      break;
+    }
+    case CB_E3M2:   // (1 + m/4) 2^(e-3), e = 0..7
+      for (int e = 0; e < 8; ++e)
+        for (int m = 0; m < 4; ++m) mags[n++] = ldexpf(1.0f + 0.25f * m, e - 3);
+      break;
+    case CB_E2M3:   // (1 + m/8) 2^(e-1), e = 0..3
+      for (int e = 0; e < 4; ++e)
+        for (int m = 0; m < 8; ++m) mags[n++] = ldexpf(1.0f + 0.125f * m, e - 1);
+      break;
+    case CB_E2M0:   // 2^(e-2), e = 0..3
+      for (int e = 0; e < 4; ++e) mags[n++] = ldexpf(1.0f, e - 2);
+      break;
+    case CB_E4M3:   // subnormals m/8 2^-6, then (1 + m/8) 2^(e-7) up to 448
+      for (int m = 1; m < 8; ++m) mags[n++] = ldexpf(0.125f * m, -6);
+      for (int e = 1; e < 16; ++e)
+        for (int m = 0; m < 8; ++m) {
+          const float v = ldexpf(1.0f + 0.125f * m, e - 7);
+          if (v <= 448.0f) mags[n++] = v;
+        }
+      break;
+    default:        // CB_E5M2: subnormals m/4 2^-14, then (1 + m/4) 2^(e-15), e = 1..31
+      for (int m = 1; m < 4; ++m) mags[n++] = ldexpf(0.25f * m, -14);
+      for (int e = 1; e < 32; ++e)
+        for (int m = 0; m < 4; ++m) mags[n++] = ldexpf(1.0f + 0.25f * m, e - 15);
+      break;
+  }
+  return n;
+}
+
+constexpr int XCB_MAX = 256;   // signed codebook entries (E5M2: 255)
+
+// Reconstruction of one element.  cb / ncb: sorted signed codebook.
+__device__ __forceinline__ float xfmt_rec(const XFmt& f, const float* cb, int ncb, float w, float scale) {
+  const float x = __fdiv_rn(w, scale);
+  float q;
+  if (f.is_int) {
+    const float lv = (float)((1 << (f.bits - 1)) - 1);
+    q = fminf(fmaxf(rintf(x), -lv - 1.0f), lv);
+  } else {
+    int lo = 0, hi = ncb;   // first entry >= x (torch.bucketize, right=False)
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (cb[mid] < x) lo = mid + 1; else hi = mid;
+    }
+    const float a = cb[max(lo - 1, 0)], b = cb[min(lo, ncb - 1)];
+    q = fabsf(__fsub_rn(b, x)) < fabsf(__fsub_rn(x, a)) ? b : a;
+  }
+  return bf16_round(__fmul_rn(q, scale));
+}
+
+__device__ __forceinline__ float xfmt_scale(const XFmt& f, float cmax, float amax) {
+  const float a = fmaxf(amax, 1e-8f);
+  if (f.is_int) return __fdiv_rn(a, (float)((1 << (f.bits - 1)) - 1));
+  const float s = __fdiv_rn(a, cmax);
+  return f.mx ? pow2i(e8m0_round(s)) : s;   // s >= 1e-8 / 114688: normal, never clamped
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(256) xfmt_kernel(const uint16_t* __restrict__ w, int64_t rows, int64_t cols,
+                                                   int fmt, double* sse, uint16_t* out) {
+  __shared__ float cb[XCB_MAX];
+  __shared__ float mags[XCB_MAX / 2 + 1];
+  __shared__ int s_ncb;
+  __shared__ float s_cmax;
+  const XFmt f = xfmt_of(fmt);
+  if (threadIdx.x == 0) {
+    int ncb = 0;
+    float cmax = 0.0f;
+    if (!f.is_int) {
+      const int nm = codebook_magnitudes(f.cb, mags);
+      for (int k = nm - 1; k >= 1; --k) cb[ncb++] = -mags[k];
+      for (int k = 0; k < nm; ++k) cb[ncb++] = mags[k];
+      cmax = mags[nm - 1];
+    }
+    s_ncb = ncb;
+    s_cmax = cmax;
+  }
+  __syncthreads();
+  const int ncb = s_ncb;
+  const float cmax = s_cmax;
+
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t g = (f.group > 0 && f.group < cols) ? f.group : cols;
+  double acc = 0.0;
+  float part = 0.0f;
+  int nsq = 0;
+  auto emit = [&](int64_t idx, float wi, float r) {
+    if (MODE == MODE_QDQ) out[idx] = (uint16_t)(__float_as_uint(r) >> 16);
+    const float e = bf16_round(__fsub_rn(wi, r));
+    part = fmaf(e, e, part);
+    if (++nsq == 64) {   // fp32 partials hold <= 64 exact squares
+      acc += (double)part;
+      part = 0.0f;
+      nsq = 0;
+    }
+  };
+  for (int64_t r = gw; r < rows; r += nw) {
+    const uint16_t* row = w + r * cols;
+    if (g == cols) {   // one group per row: the warp reduces the row maximum
+      float ar = 0.0f;
+      for (int64_t i = lane; i < cols; i += 32) ar = fmaxf(ar, fabsf(bf16lo((uint32_t)row[i])));
+      ar = __uint_as_float(warp_max_u(__float_as_uint(ar)));
+      const float scale = xfmt_scale(f, cmax, ar);
+      for (int64_t i = lane; i < cols; i += 32) {
+        const float wi = bf16lo((uint32_t)row[i]);
+        emit(r * cols + i, wi, xfmt_rec(f, cb, ncb, wi, scale));
+      }
+    } else {           // lanes take whole groups
+      for (int64_t gi = lane; gi < cols / g; gi += 32) {
+        const uint16_t* gp = row + gi * g;
+        float a = 0.0f;
+        for (int64_t i = 0; i < g; ++i) a = fmaxf(a, fabsf(bf16lo((uint32_t)gp[i])));
+        const float scale = xfmt_scale(f, cmax, a);
+        for (int64_t i = 0; i < g; ++i) {
+          const float wi = bf16lo((uint32_t)gp[i]);
+          emit(r * cols + gi * g + i, wi, xfmt_rec(f, cb, ncb, wi, scale));
+        }
+      }
+    }
+  }
+  if (MODE == MODE_SSE) {
+    const double v = warp_sum_d(acc + (double)part);
+    if (lane == 0 && v != 0.0) atomicAdd(sse, v);
+  }
+}
+
+// Group length the format uses for rows of `cols`, or 0 if the row does not split into groups
+// (the reference's reshape raises, format_registry.py:208-212 / :151-154).
+int64_t xfmt_group(int fmt, int64_t cols) {
+  const XFmt f = xfmt_of(fmt);
+  if (f.group > 0 && f.group < cols) return cols % f.group ? 0 : f.group;
+  return cols;
+}
+
+cudaError_t launch_xfmt(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, uint16_t* out,
+                        int mode, int num_sms, cudaStream_t stream) {
+  int64_t blocks = (rows * 32 + 255) / 256;
+  if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
+  if (blocks < 1) blocks = 1;
+  if (mode == MODE_QDQ)
+    xfmt_kernel<MODE_QDQ><<<(unsigned)blocks, 256, 0, stream>>>(w, rows, cols, fmt, sse, out);
+  else
+    xfmt_kernel<MODE_SSE><<<(unsigned)blocks, 256, 0, stream>>>(w, rows, cols, fmt, sse, out);
+  return cudaGetLastError();
+}
+
+}  // namespace pq

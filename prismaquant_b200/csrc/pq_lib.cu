@@ -4,5 +4,6 @@
 #include "pq_sweep_fast.cu"
 #include "pq_pack.cu"
 #include "pq_fisher.cu"
+#include "pq_codebook.cu"
 #include "pq_capi.cu"
 #include "pq_noalloc.cu"

@@ -280,18 +280,26 @@ def sweep_and_export(named_weights, specs, export_nvfp4: bool = True):
     items = list(named_weights.items()) if isinstance(named_weights, dict) else list(named_weights)
     names = [n for n, _ in items]
     ws = [w for _, w in items]
+    # NVFP4 / MXFP8 / FP8 per channel / BF16 ride on the export's read; the rest of the registry
+    # (exact codebook / integer kernel, NVFP3's batched-path error) is a second, separate sweep
+    fused = [s for s in specs if s.kernel_format in mqc._FUSED and s.name != "FP8_SOURCE"]
+    rest = [s for s in specs if s not in fused]
     if export_nvfp4:
-        outs, sse, errors = export_nvfp4_many(ws, [sibling_group_key(n) for n in names], fuse_sweep_specs=specs)
+        outs, sse, errors = export_nvfp4_many(ws, [sibling_group_key(n) for n in names], fuse_sweep_specs=fused)
     else:
-        sse, errors = mqc.sweep_sse_async([_lib.as_bf16_cuda(w, "sweep") for w in ws], specs)
+        sse, errors = mqc.sweep_sse_async([_lib.as_bf16_cuda(w, "sweep") for w in ws], fused)
         outs = None
+    other = mqc.sweep_weight_mse(list(zip(names, ws)), rest) if rest else {}
     host = sse.cpu().tolist()
     costs = {}
     for name, w, row, err in zip(names, ws, host, errors):
         per = {}
         for s in specs:
-            per[s.name] = {"error": err[s.name]} if s.name in err else \
-                mqc._mse_from_sse(row[mqc._KCOL[mqc._kernel_format(s)]], w.numel())
+            if s in rest:
+                per[s.name] = other[name][s.name]
+            else:
+                per[s.name] = {"error": err[s.name]} if s.name in err else \
+                    mqc._mse_from_sse(row[mqc._KCOL[mqc._kernel_format(s)]], w.numel())
         costs[name] = per
     return costs, (dict(zip(names, outs)) if outs is not None else None)
 
@@ -319,6 +327,9 @@ class SweepExportPlan:
         self.sse = torch.zeros(n, 4, dtype=torch.float64, device=dev)
         self.tmax = torch.zeros(max(n, 1), dtype=torch.int32, device=dev)
         kf = [mqc._kernel_format(s) for s in self.specs]
+        if any(k not in mqc._FUSED or s.name == "FP8_SOURCE" for s, k in zip(self.specs, kf)):
+            raise ValueError("SweepExportPlan takes the fused-sweep formats (NVFP4, MXFP8, FP8_E4M3, BF16 and "
+                             "their aliases); use sweep_and_export for the rest of the registry")
         self.errors = []
         masks = []
         for w in self.weights:

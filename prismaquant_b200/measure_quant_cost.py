@@ -30,7 +30,22 @@ FLT_MAX = float(torch.finfo(torch.float32).max)
 _KBIT = {"NVFP4": 1 << _lib.FMT_NVFP4, "MXFP8": 1 << _lib.FMT_MXFP8, "FP8_E4M3": 1 << _lib.FMT_FP8_CHANNEL,
          "BF16": 1 << _lib.FMT_BF16}
 _KCOL = {"NVFP4": _lib.FMT_NVFP4, "MXFP8": _lib.FMT_MXFP8, "FP8_E4M3": _lib.FMT_FP8_CHANNEL, "BF16": _lib.FMT_BF16}
-_GROUP = {"NVFP4": 16, "MXFP8": 32}
+_GROUP = {"NVFP4": 16, "MXFP8": 32, "MXFP4": 32, "MXFP6_E3M2": 32, "MXFP6_E2M3": 32, "MXFP8_E5M2": 32,
+          "NVFP3": 16, "INT3": 16, "INT2": 16, "INT4_W4A16_g128": 128, "FP8_E4M3_G128": 128}
+_FUSED = ("NVFP4", "MXFP8", "FP8_E4M3", "BF16")   # kernel formats of the fused sweep
+
+# measure_quant_cost._batched_quantize (measure_quant_cost.py:516-548) picks the RTN by element dtype:
+# codebook dtypes with the spec's group size (E8M0-snapped for family "mx"), integer dtypes with the
+# spec's bits and group size, bfloat16 as a clone, and raises for anything else (fp3_e2m0 = NVFP3).
+# (element dtype, group size, E8M0) -> kernel format
+_BATCHED_CODEBOOK = {
+    ("fp4_e2m1", 16, False): "NVFP4", ("fp4_e2m1", 32, True): "MXFP4",
+    ("fp6_e3m2", 32, True): "MXFP6_E3M2", ("fp6_e2m3", 32, True): "MXFP6_E2M3",
+    ("fp8_e4m3", 32, True): "MXFP8", ("fp8_e4m3", 0, False): "FP8_E4M3",
+    ("fp8_e4m3", 128, False): "FP8_E4M3_G128",
+    ("fp8_e5m2", 32, True): "MXFP8_E5M2", ("fp8_e5m2", 0, False): "FP8_E5M2",
+}
+_BATCHED_INT = {(3, 16): "INT3", (2, 16): "INT2", (8, 0): "INT8_W8A16", (4, 128): "INT4_W4A16_g128"}
 
 
 def canonical_linear_name(name: str) -> str:
@@ -47,6 +62,25 @@ def _kernel_format(spec: fr.FormatSpec) -> str:
     if k is None:
         raise NotImplementedError(f"format {spec.name} has no B200 kernel")
     return k
+
+
+def batched_kernel_format(spec: fr.FormatSpec) -> str:
+    """Kernel format of the reference's batched cost path for `spec` (measure_quant_cost.py:535-548);
+    raises ValueError with the reference's message for an element dtype it does not take."""
+    elt = spec.weight_element_dtype
+    if elt in ("fp4_e2m1", "fp6_e3m2", "fp6_e2m3", "fp8_e4m3", "fp8_e5m2"):
+        key = (elt, spec.group_size, spec.family == "mx")
+        if key not in _BATCHED_CODEBOOK:
+            raise NotImplementedError(f"no B200 kernel for {elt} groups of {spec.group_size}")
+        return _BATCHED_CODEBOOK[key]
+    if elt.startswith("int"):
+        key = (spec.weight_bits, spec.group_size)
+        if key not in _BATCHED_INT:
+            raise NotImplementedError(f"no B200 kernel for INT{spec.weight_bits} groups of {spec.group_size}")
+        return _BATCHED_INT[key]
+    if elt == "bfloat16":
+        return "BF16"
+    raise ValueError(f"Unknown weight_element_dtype {elt!r} for batched RTN")
 
 
 def shape_error(kfmt: str, cols: int) -> str | None:
@@ -115,7 +149,7 @@ def sweep_sse_async(weights: list[torch.Tensor], specs: list[fr.FormatSpec], nvf
             e = shape_error(k, cols)
             if e:
                 err[s.name] = e
-            else:
+            elif k in _KBIT:
                 m |= _KBIT[k]
         masks.append(m & 0x7)
         errors.append(err)
@@ -129,31 +163,68 @@ def _mse_from_sse(sse: float, n: int) -> float:
     return sse / max(n, 1)
 
 
-def sweep_weight_mse(named_weights, specs: list[fr.FormatSpec]) -> dict[str, dict[str, float | dict]]:
+def sweep_weight_mse(named_weights, specs: list[fr.FormatSpec],
+                     per_linear: bool = False) -> dict[str, dict[str, float | dict]]:
     """{name: {spec.name: weight_mse | {"error": msg}}} for bf16 CUDA weights
-    ([out, in] Linears or [E, M, N] packed experts), all formats in one pass."""
+    ([out, in] Linears or [E, M, N] packed experts), the fused formats in one pass.
+
+    Each spec is quantized as the batched cost path does (`_batched_quantize`), or, with
+    `per_linear`, as its own quantize_dequantize does (measure_unbatched); the two differ only for
+    NVFP3 (an error in the batched path) and FP8_SOURCE (E4M3 g128 there, a clone per Linear)."""
     items = list(named_weights.items()) if isinstance(named_weights, dict) else list(named_weights)
     names = [n for n, _ in items]
     weights = [_lib.as_bf16_cuda(w.detach(), "sweep_weight_mse") for _, w in items]
     if not weights:
         return {}
-    sse, errors = sweep_sse_async(weights, specs)
-    host = sse.cpu().tolist()  # the one device->host copy
+    # the kernel format of each spec as the batched cost path quantizes it
+    kf: dict[str, str | None] = {}
+    dtype_err: dict[str, str] = {}
+    for s in specs:
+        try:
+            kf[s.name] = _kernel_format(s) if per_linear else batched_kernel_format(s)
+        except ValueError as e:
+            kf[s.name], dtype_err[s.name] = None, str(e)
+    fused = [s for s in specs if kf[s.name] in _FUSED]
+    ext = [s for s in specs if kf[s.name] is not None and kf[s.name] not in _FUSED]
+    sse, errors = sweep_sse_async(weights, [_as_kernel_spec(s, kf[s.name]) for s in fused])
+    ext_sse = torch.zeros(len(weights), max(len(ext), 1), dtype=torch.float64, device=weights[0].device)
+    for i, w in enumerate(weights):
+        for j, s in enumerate(ext):
+            e = shape_error(kf[s.name], w.shape[-1])
+            if e:
+                errors[i][s.name] = e
+            else:
+                _lib.format_sse(w, kf[s.name], ext_sse[i, j])
+    host, ext_host = sse.cpu().tolist(), ext_sse.cpu().tolist()   # the device->host copies
     out = {}
-    for name, w, row, err in zip(names, weights, host, errors):
+    for i, (name, w) in enumerate(zip(names, weights)):
         per = {}
         for s in specs:
-            if s.name in err:
-                per[s.name] = {"error": err[s.name]}
+            if s.name in dtype_err:
+                per[s.name] = {"error": dtype_err[s.name]}
+            elif s.name in errors[i]:
+                per[s.name] = {"error": errors[i][s.name]}
+            elif kf[s.name] in _FUSED:
+                per[s.name] = _mse_from_sse(host[i][_KCOL[kf[s.name]]], w.numel())
             else:
-                per[s.name] = _mse_from_sse(row[_KCOL[_kernel_format(s)]], w.numel())
+                per[s.name] = _mse_from_sse(ext_host[i][ext.index(s)], w.numel())
         out[name] = per
     return out
 
 
+def _as_kernel_spec(spec: fr.FormatSpec, kfmt: str) -> fr.FormatSpec:
+    """`spec` with kernel_format set to the batched path's kernel format (FP8_SOURCE's
+    per-Linear kernel format is a clone; its batched one is not)."""
+    if spec.kernel_format == kfmt:
+        return spec
+    import dataclasses
+    return dataclasses.replace(spec, kernel_format=kfmt)
+
+
 def _batched_quantize(spec: fr.FormatSpec, stacked_w: torch.Tensor) -> torch.Tensor:
-    """measure_quant_cost.py:532-548: W_hat of a stacked [N, out, in] weight."""
-    k = _kernel_format(spec)
+    """measure_quant_cost.py:532-548: W_hat of a stacked [N, out, in] weight, the RTN picked by the
+    spec's element dtype as the reference does (so NVFP3 raises and FP8_SOURCE is an E4M3 g128 RTN)."""
+    k = batched_kernel_format(spec)
     if k == "BF16":
         return stacked_w.clone()
     return _lib.cost_qdq(stacked_w, k)
@@ -172,15 +243,17 @@ def _group_by_shape(model: nn.Module, target_names: set[str]):
     return groups
 
 
-def _weight_mse_or_errors(W_list, specs):
+def _weight_mse_or_errors(W_list, specs, per_linear=False):
     """Weight MSE of each weight for each spec (one fused pass), as python floats."""
-    res = sweep_weight_mse([(str(i), w) for i, w in enumerate(W_list)], specs)
+    res = sweep_weight_mse([(str(i), w) for i, w in enumerate(W_list)], specs, per_linear=per_linear)
     return [res[str(i)] for i in range(len(W_list))]
 
 
 def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], specs: list[fr.FormatSpec],
-                        device: str, dtype: torch.dtype, chunk_size: int = 256, h_detail=None) -> dict:
-    """measure_quant_cost.py:551-685 with the weight error from the fused sweep."""
+                        device: str, dtype: torch.dtype, chunk_size: int = 256, h_detail=None,
+                        _per_linear: bool = False) -> dict:
+    """measure_quant_cost.py:551-685 with the weight error from the fused sweep.  `_per_linear`
+    (used by measure_unbatched) quantizes with each spec's own quantize_dequantize instead."""
     dev = torch.device(device)
     groups = _group_by_shape(model, target_names)
     accum: dict = {}
@@ -202,12 +275,13 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                 hs = [h_detail.load(n) for n in names]
                 if all(tuple(h.shape) == tuple(W.shape[1:]) for h in hs):
                     h_stacked = torch.stack([h.to(dev).float() for h in hs])
-            wmse = _weight_mse_or_errors(list(W.unbind(0)), specs) if dtype == torch.bfloat16 else None
+            wmse = (_weight_mse_or_errors(list(W.unbind(0)), specs, _per_linear) if dtype == torch.bfloat16
+                    else None)
             for spec in specs:
                 try:
-                    if wmse is None and _kernel_format(spec) != "BF16":
+                    if wmse is None and spec.weight_element_dtype != "bfloat16":
                         raise NotImplementedError(f"B200 cost kernels take bf16 weights, got {dtype}")
-                    W_hat = _batched_quantize(spec, W)
+                    W_hat = spec.quantize_dequantize(W) if _per_linear else _batched_quantize(spec, W)
                     X_hat = spec.activation_quantize_dequantize(X.clone())
                     y_q = torch.bmm(X_hat, W_hat.transpose(1, 2))
                     out_mse = (y_ref - y_q).float().pow(2).mean(dim=(1, 2))
@@ -234,7 +308,7 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
 
 def measure_unbatched(model: nn.Module, act_cache, target_names: set[str], specs: list[fr.FormatSpec],
                       device: str, dtype: torch.dtype, h_detail=None) -> dict:
-    """measure_quant_cost.py:266-327: one Linear at a time (same numbers as batched)."""
+    """measure_quant_cost.py:266-327: one Linear at a time, each spec's own quantize_dequantize."""
     accum: dict = {}
     for name, mod in model.named_modules():
         cname = canonical_linear_name(name)
@@ -243,7 +317,7 @@ def measure_unbatched(model: nn.Module, act_cache, target_names: set[str], specs
         sub = nn.Module()
         sub.add_module("lin", mod)
         one = measure_batched_gpu(sub, _Renamed(act_cache, cname), {"lin"}, specs, device, dtype, 1,
-                                  _Renamed(h_detail, cname) if h_detail is not None else None)
+                                  _Renamed(h_detail, cname) if h_detail is not None else None, _per_linear=True)
         for fmt, entry in one.get("lin", {}).items():
             if "error" in entry:
                 accum.setdefault(cname, {})[fmt] = entry

@@ -39,6 +39,9 @@ from prismaquant import sensitivity_probe as sp  # noqa: E402
 torch.set_num_threads(os.cpu_count() or 1)
 
 COST_FMTS = ["NVFP4", "MXFP8", "FP8_E4M3", "BF16"]
+# the rest of the registry (quantize_dequantize only; served by the exact codebook kernel)
+EXT_FMTS = ["MXFP4", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E5M2", "FP8_E5M2", "NVFP3", "INT3", "INT2",
+            "INT8_W8A16", "INT4_W4A16_g128", "FP8_SOURCE"]
 
 
 def to_t(bits):
@@ -97,13 +100,19 @@ def small_cases():
     cases["cols8_4x8"] = O.synthetic_weight_bits((4, 8), seed=16)        # whole-row groups
     cases["packed_4x32x64"] = O.synthetic_weight_bits((4, 32, 64), seed=17, std=0.05)
     cases["packed_3x16x96"] = O.synthetic_weight_bits((3, 16, 96), seed=18, outlier_frac=0.01)
+    # 4096 distinct finite bf16 patterns (both zeros, subnormals, the largest finite), rows of 32
+    allv = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    fin = allv[np.isfinite(O.bf16_bits_to_f32(allv))]
+    pick = np.random.default_rng(19).choice(fin, 4096 - 6, replace=False)
+    edge = np.array([0x0000, 0x8000, 0x0001, 0x8001, 0x7F7F, 0xFF7F], dtype=np.uint16)
+    cases["bf16mix_128x32"] = np.random.default_rng(20).permutation(np.concatenate([pick, edge])).reshape(128, 32)
     return cases
 
 
 def run_cost(bits):
     out = {}
     W = to_t(bits)
-    for fmt in COST_FMTS:
+    for fmt in COST_FMTS + EXT_FMTS:
         spec = fr.get_format(fmt)
         try:
             if W.dim() == 3:

@@ -38,7 +38,13 @@ def test_argument_validation_without_gpu():
     lib = _lib.load()
     assert lib.pq_mxfp8_pack(None, 4, 48, None, None, None) == _lib.PQ_ERR_SHAPE
     assert lib.pq_nvfp4_codes(None, 1, 4, 40, None, None, None, None) == _lib.PQ_ERR_SHAPE
-    assert lib.pq_cost_qdq(None, 4, 64, 9, None, None) == _lib.PQ_ERR_FORMAT
+    assert lib.pq_cost_qdq(None, 4, 64, _lib.NUM_FMTS_ALL, None, None) == _lib.PQ_ERR_FORMAT
+    assert lib.pq_cost_qdq(None, 4, 40, _lib.FMT_IDS["INT3"], None, None) == _lib.PQ_ERR_SHAPE    # 16 does not divide 40
+    assert lib.pq_cost_qdq(None, 4, 8, _lib.FMT_IDS["INT4_W4A16_g128"], None, None) == _lib.PQ_ERR_NULL  # whole-row group
+    assert lib.pq_format_sse(None, 4, 40, _lib.FMT_IDS["MXFP4"], None, None) == _lib.PQ_ERR_SHAPE
+    assert lib.pq_format_sse(None, 4, 64, _lib.FMT_NVFP4, None, None) == _lib.PQ_ERR_FORMAT        # fused: pq_sweep_sse
+    assert lib.pq_format_sse(None, 4, 64, _lib.FMT_BF16, None, None) == _lib.PQ_OK
+    assert lib.pq_format_sse(None, 4, 64, _lib.FMT_IDS["NVFP3"], None, None) == _lib.PQ_ERR_NULL
     assert lib.pq_sumsq_rows(None, 4, 64, None, None, None) == _lib.PQ_ERR_NULL
     assert lib.pq_sweep_sse(None, 0, None, None) == _lib.PQ_OK
     arr = (_lib.SweepTensor * 1)()
@@ -197,10 +203,70 @@ def test_patch_prismaquant_rebinds_reference_functions():
         assert fr.REGISTRY["NVFP4"].quantize_dequantize is not orig[0]
         assert enc.quantize_dequantize_nvfp4.__module__ == "prismaquant_b200.export_native_compressed"
         assert sp._GradNormCapture.__module__ == "prismaquant_b200.sensitivity_probe"
-        assert fr.REGISTRY["INT3"].quantize_dequantize is orig[4]     # no B200 kernel: untouched
+        assert fr.REGISTRY["INT3"].quantize_dequantize is not orig[4]  # the exact codebook / integer kernel
         install.unpatch_prismaquant()
         assert (fr.REGISTRY["NVFP4"].quantize_dequantize, mqc._batched_quantize, enc.quantize_dequantize_nvfp4,
                 sp._GradNormCapture) == orig[:4]
+    finally:
+        for p in (shim, str(REFERENCE)):
+            if p in sys.path:
+                sys.path.remove(p)
+
+
+def test_batched_dispatch_matches_oracle():
+    """_batched_quantize picks the RTN by element dtype (measure_quant_cost.py:516-548), as the oracle's
+    restatement does: NVFP3 raises, FP8_SOURCE is an E4M3 RTN with real groups of 128."""
+    from oracle import pq_oracle as O
+    from prismaquant_b200 import format_registry as fr
+    from prismaquant_b200 import measure_quant_cost as mqc
+    kernel = {"NVFP4": ("fp4_e2m1", 16, False), "MXFP4": ("fp4_e2m1", 32, True),
+              "MXFP6_E3M2": ("fp6_e3m2", 32, True), "MXFP6_E2M3": ("fp6_e2m3", 32, True),
+              "MXFP8": ("fp8_e4m3", 32, True), "FP8_E4M3": ("fp8_e4m3", 0, False),
+              "FP8_E4M3_G128": ("fp8_e4m3", 128, False), "MXFP8_E5M2": ("fp8_e5m2", 32, True),
+              "FP8_E5M2": ("fp8_e5m2", 0, False)}
+    assert set(fr.REGISTRY) == set(O.REGISTRY_DTYPES)
+    for name in fr.REGISTRY:
+        spec = fr.get_format(name)
+        elt, fam, bits, group = O.REGISTRY_DTYPES[name]
+        assert (spec.weight_element_dtype, spec.family, spec.weight_bits, spec.group_size) == (elt, fam, bits, group)
+        if elt == "fp3_e2m0":
+            with pytest.raises(ValueError, match="Unknown weight_element_dtype"):
+                mqc.batched_kernel_format(spec)
+            continue
+        k = mqc.batched_kernel_format(spec)
+        if elt.startswith("int"):
+            assert k == name
+        elif elt == "bfloat16":
+            assert k == "BF16"
+        else:
+            assert kernel[k] == (elt, group, fam == "mx")
+
+
+def test_registry_matches_reference_registry():
+    """Every format, alias and metadata field of the reference's REGISTRY (format_registry.py:368-576)."""
+    import sys
+    from tests.conftest import REFERENCE, reference_available
+    if not reference_available():
+        pytest.skip("reference checkout not present")
+    from prismaquant_b200 import format_registry as ours
+    shim = str(Path(__file__).resolve().parent.parent / "oracle" / "_shim")
+    sys.path[:0] = [shim, str(REFERENCE)]
+    try:
+        import prismaquant.format_registry as ref
+        assert set(ref.REGISTRY) == set(ours.REGISTRY)
+        assert ref.FORMAT_ALIASES == ours.FORMAT_ALIASES
+        fields = ("weight_bits", "group_size", "scale_bits", "scale_dtype_name", "weight_element_dtype",
+                  "scale_block_shape", "act_bits", "act_dtype_name", "act_group_size", "family", "min_capability_sm")
+        for name, r in ref.REGISTRY.items():
+            o = ours.get_format(name)
+            for f in fields:
+                assert getattr(o, f) == getattr(r, f), (name, f)
+            assert o.effective_bits == pytest.approx(r.effective_bits), name
+            assert o.autoround_config() == r.autoround_config(), name
+            for shape in ((4096, 4096), (7, 96), (3, 64, 256), (100,)):
+                assert o.scale_count_for_shape(shape) == r.scale_count_for_shape(shape), (name, shape)
+                assert o.memory_bytes_for_shape(shape) == r.memory_bytes_for_shape(shape), (name, shape)
+        assert [s.name for s in ours.list_formats()] == [s.name for s in ref.list_formats()]
     finally:
         for p in (shim, str(REFERENCE)):
             if p in sys.path:

@@ -1,0 +1,112 @@
+"""The rest of the format registry on the GPU (exact codebook / integer kernel):
+MXFP4, MXFP6 E3M2/E2M3, MXFP8/FP8 E5M2, NVFP3, INT2/INT3, INT8_W8A16,
+INT4_W4A16_g128 and FP8_SOURCE, against the reference's outputs (golden
+fixtures) and the oracle.  Bar: bit-exact W_hat, MSE_W within 1e-5."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import pq_oracle as O
+from prismaquant_b200 import format_registry as fr
+from prismaquant_b200 import measure_quant_cost as mqc
+from tests._helpers import bits_of, to_cuda_bf16
+
+pytestmark = pytest.mark.gpu
+
+EXT_FMTS = ["MXFP4", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E5M2", "FP8_E5M2", "NVFP3", "INT3", "INT2",
+            "INT8_W8A16", "INT4_W4A16_g128", "FP8_SOURCE"]
+CASES = ["rand_64x128", "rand_33x256", "ties_4x32", "zeros_3x64", "wide_range_8x96", "row1_1x4096",
+         "cols16_5x16", "cols48_7x48", "cols8_4x8", "packed_4x32x64", "packed_3x16x96", "bf16mix_128x32"]
+
+
+@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("fmt", EXT_FMTS)
+def test_qdq_matches_reference(golden, case, fmt):
+    """2-D inputs through the spec's quantize_dequantize, packed 3-D ones through _batched_quantize,
+    as the fixtures were made."""
+    bits = golden[f"{case}/input"]
+    key = f"{case}/cost/{fmt}"
+    w = to_cuda_bf16(bits)
+    spec = fr.get_format(fmt)
+    run = (lambda: mqc._batched_quantize(spec, w)) if bits.ndim == 3 else (lambda: spec.quantize_dequantize(w))
+    if f"{key}/error" in golden:
+        with pytest.raises(ValueError):
+            run()
+        return
+    np.testing.assert_array_equal(bits_of(run()), golden[f"{key}/qdq"])
+
+
+def _all_bf16_rows(cols):
+    allv = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    fin = allv[np.isfinite(O.bf16_bits_to_f32(allv))]
+    fin = np.random.default_rng(cols).permutation(fin)
+    return fin[: (fin.size // cols) * cols].reshape(-1, cols)
+
+
+@pytest.mark.parametrize("fmt", EXT_FMTS + ["FP8_E4M3_G128"])
+@pytest.mark.parametrize("cols", [32, 256])
+def test_qdq_every_bf16_value_matches_oracle(fmt, cols):
+    """Every finite bf16 value, randomly grouped, through the kernel and the oracle."""
+    from prismaquant_b200 import _lib
+    bits = _all_bf16_rows(cols)
+    got = bits_of(_lib.cost_qdq(to_cuda_bf16(bits), fmt)) if fmt != "FP8_SOURCE" else \
+        bits_of(fr.get_format(fmt).quantize_dequantize(to_cuda_bf16(bits)))
+    if fmt == "FP8_E4M3_G128":
+        want = O.f32_to_bf16_bits(O.codebook_qdq_f32(bits, "fp8_e4m3", 128, False))
+    else:
+        want = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt))
+    bad = np.nonzero(got != want)
+    assert bad[0].size == 0, (fmt, got[bad][:5], want[bad][:5], bits[bad][:5])
+
+
+def _oracle_mse(bits, fmt, per_linear):
+    rec = O.cost_qdq_f32(bits, fmt) if per_linear else O.batched_qdq_f32(bits, fmt)
+    err = O.bf16_round((O.bf16_bits_to_f32(bits) - rec).astype(np.float32))
+    with np.errstate(over="ignore"):
+        sq = (err * err).astype(np.float32).astype(np.float64)
+    return float(sq.sum()) / bits.size
+
+
+@pytest.mark.parametrize("per_linear", [False, True])
+def test_sweep_weight_mse_matches_oracle(per_linear):
+    """MSE_W of every registry format over Linears and packed experts, in the batched path's
+    semantics (NVFP3 an error, FP8_SOURCE an E4M3 g128 RTN) and in the per-Linear ones."""
+    shapes = {"a.q_proj": (96, 256), "b.o_proj": (40, 512), "c.experts.gate_up_proj": (4, 32, 384),
+              "d.small": (6, 48)}
+    bits = {n: O.synthetic_weight_bits(s, seed=31 + i, outlier_frac=0.01) for i, (n, s) in enumerate(shapes.items())}
+    specs = [fr.get_format(f) for f in sorted(fr.REGISTRY)]
+    res = mqc.sweep_weight_mse({n: to_cuda_bf16(b) for n, b in bits.items()}, specs, per_linear=per_linear)
+    for n, b in bits.items():
+        for s in specs:
+            got = res[n][s.name]
+            try:
+                want = _oracle_mse(b, s.name, per_linear)
+            except ValueError as e:
+                assert isinstance(got, dict) and "error" in got, (n, s.name, got)
+                if "Unknown weight_element_dtype" in str(e):
+                    assert got["error"] == str(e)
+                continue
+            assert not isinstance(got, dict), (n, s.name, got)
+            assert got == pytest.approx(want, rel=1e-5, abs=1e-30), (n, s.name)
+
+
+def test_activation_quantizers():
+    """MX / FP8-E5M2 formats quantize activations with the same RTN as weights; the integer and
+    NVFP3 formats leave them alone; FP8_SOURCE clones (format_registry.py:391-576)."""
+    x = to_cuda_bf16(O.synthetic_weight_bits((64, 256), seed=3, std=1.0))
+    for f in ("MXFP4", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E5M2", "FP8_E5M2"):
+        s = fr.get_format(f)
+        assert torch.equal(s.activation_quantize_dequantize(x), s.quantize_dequantize(x))
+    for f in ("INT3", "INT2", "NVFP3", "INT8_W8A16", "INT4_W4A16_g128"):
+        assert fr.get_format(f).activation_quantize_dequantize(x) is x
+    y = fr.get_format("FP8_SOURCE").activation_quantize_dequantize(x)
+    assert torch.equal(y, x) and y is not x
+
+
+def test_shape_errors_raise():
+    w = torch.zeros(4, 40, dtype=torch.bfloat16, device="cuda")
+    for f in ("MXFP4", "INT3", "NVFP3"):
+        with pytest.raises(ValueError):
+            fr.get_format(f).quantize_dequantize(w)
+    res = mqc.sweep_weight_mse({"w": w}, [fr.get_format("INT3"), fr.get_format("FP8_E5M2")])
+    assert "error" in res["w"]["INT3"] and res["w"]["FP8_E5M2"] == 0.0

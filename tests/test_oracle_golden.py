@@ -7,23 +7,33 @@ from oracle import pq_oracle as O
 
 CASES = ["rand_64x128", "rand_33x256", "ties_4x32", "zeros_3x64", "wide_range_8x96",
          "row1_1x4096", "cols16_5x16", "cols48_7x48", "cols8_4x8", "packed_4x32x64",
-         "packed_3x16x96"]
+         "packed_3x16x96", "bf16mix_128x32"]
 COST_FMTS = ["NVFP4", "MXFP8", "FP8_E4M3", "BF16"]
+EXT_FMTS = ["MXFP4", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E5M2", "FP8_E5M2", "NVFP3", "INT3", "INT2",
+            "INT8_W8A16", "INT4_W4A16_g128", "FP8_SOURCE"]
 
 
 @pytest.mark.parametrize("case", CASES)
-@pytest.mark.parametrize("fmt", COST_FMTS)
+@pytest.mark.parametrize("fmt", COST_FMTS + EXT_FMTS)
 def test_cost_path_matches_reference(golden, case, fmt):
     bits = golden[f"{case}/input"]
     key = f"{case}/cost/{fmt}"
+    # the fixtures ran quantize_dequantize on 2-D inputs and _batched_quantize on packed 3-D ones
+    qdq = O.batched_qdq_f32 if bits.ndim == 3 else O.cost_qdq_f32
     if f"{key}/error" in golden:
         with pytest.raises(ValueError):
-            O.cost_qdq_f32(bits, fmt)
+            qdq(bits, fmt)
         return
-    got = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt))
-    np.testing.assert_array_equal(got, golden[f"{key}/qdq"])
+    rec = qdq(bits, fmt)
+    np.testing.assert_array_equal(O.f32_to_bf16_bits(rec), golden[f"{key}/qdq"])
     ref_mse = float(golden[f"{key}/mse"][0])
-    mse = O.cost_mse(bits, fmt)
+    w = O.bf16_bits_to_f32(bits)
+    err = O.bf16_round((w - rec).astype(np.float32))
+    with np.errstate(over="ignore"):
+        sq = (err * err).astype(np.float32).astype(np.float64)
+    mse = float(sq.sum()) / max(bits.size, 1)
+    if bits.ndim == 2:
+        assert mse == pytest.approx(O.cost_mse(bits, fmt), rel=1e-12, abs=1e-300)
     assert mse == pytest.approx(ref_mse, rel=1e-5, abs=1e-30)
 
 
@@ -137,3 +147,14 @@ def test_full_linear_digest_oracle(full_digests):
     assert O.digest(*O.nvfp4_pack(wf)) == d["nvfp4"]
     assert O.digest(*O.mxfp8_pack(wf)) == d["mxfp8"]
     assert O.digest(*O.fp8_dynamic_pack(wf)) == d["fp8dyn"]
+
+
+def test_extended_codebooks_match_reference_definitions():
+    """Codebook sizes and extremes as the reference defines them (format_registry.py:237-300):
+    FP6 and FP3 have no subnormals, and E5M2 keeps exponent 31 as finite values."""
+    sizes = {k: (v.size, float(v.max()), float(v[v > 0].min())) for k, v in O.CODEBOOKS.items()}
+    assert sizes["fp6_e3m2"] == (65, 28.0, 0.125)
+    assert sizes["fp6_e2m3"] == (65, 7.5, 0.5)
+    assert sizes["fp3_e2m0"] == (9, 2.0, 0.25)
+    assert sizes["fp8_e5m2"] == (255, 114688.0, 2.0 ** -16)
+    assert O.FORMAT_ALIASES == {"NVINT2": "INT2", "NVINT3": "INT3"}
