@@ -111,6 +111,19 @@ int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t
 int pq_format_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, void* stream);
 
 /*
+ * H-weighted squared error of one format over one bf16 tensor [rows, cols]:
+ * ADDS sum(h * (W - qdq_fmt(W))^2) to *sse (fp64, device), the square taken
+ * in fp32 and then weighted.  h is fp32, one weight per element [rows, cols]
+ * (h_per_row = 0) or one per row [rows] (h_per_row = 1).  Any format id
+ * except that PQ_FMT_BF16 adds nothing.  predicted_dloss is half of it:
+ * dense Linears with the per-weight Fisher diagonal
+ * (measure_quant_cost.py:638-640), packed experts with the per-channel [E, M]
+ * one, rows = E*M (:430-437, whose mean over N times N is this sum).
+ */
+int pq_weighted_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, const float* h, int h_per_row,
+                    double* sse, void* stream);
+
+/*
  * NVFP4 export, pass 1: E2M1 codes (abs-codebook RTN, ties toward zero,
  * sign from signbit; export_native_compressed.py:118-136, 226-233), the bf16
  * amax of every 16-group, and the max group amax of each of `batch`

@@ -30,7 +30,7 @@ EXPORTED = [
     "pq_sweep_sse", "pq_cost_qdq", "pq_nvfp4_codes", "pq_nvfp4_scales", "pq_nvfp4_pack",
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
-    "pq_format_sse",
+    "pq_format_sse", "pq_weighted_sse",
 ]
 
 
@@ -66,6 +66,7 @@ def load() -> ctypes.CDLL:
         "pq_sweep_sse": [ctypes.POINTER(SweepTensor), I, P, V],
         "pq_cost_qdq": [P, I64, I64, I, P, V],
         "pq_format_sse": [P, I64, I64, I, P, V],
+        "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
         "pq_nvfp4_codes": [P, I64, I64, I64, P, P, P, V],
         "pq_nvfp4_scales": [I, ctypes.POINTER(P), ctypes.POINTER(I64), P, ctypes.POINTER(ctypes.c_int32), P,
                             ctypes.POINTER(P), P, V],
@@ -201,6 +202,24 @@ def format_sse(w: torch.Tensor, fmt: str, sse: torch.Tensor) -> None:
     cols = wb.shape[-1]
     _check(load().pq_format_sse(_ptr(wb), wb.numel() // cols, cols, FMT_IDS[fmt], _ptr(sse), _stream(wb)),
            "pq_format_sse", f"cannot reshape rows of {cols} into groups for {fmt}")
+
+
+def weighted_sse(w: torch.Tensor, fmt: str, h: torch.Tensor, sse: torch.Tensor, per_row: bool = False) -> None:
+    """Adds sum(h * (W - qdq_fmt(W))^2) into the fp64 device scalar `sse`; h is fp32 with W's
+    shape, or (per_row) one weight per row of W viewed as [numel / cols, cols]."""
+    wb = as_bf16_cuda(w, "weighted_sse")
+    if wb.numel() == 0:
+        return
+    cols = wb.shape[-1]
+    rows = wb.numel() // cols
+    hh = h.detach()
+    if hh.device != wb.device or hh.dtype != torch.float32:
+        raise TypeError("weighted_sse: h must be float32 on the weight's device")
+    hh = hh.contiguous()
+    if hh.numel() != (rows if per_row else rows * cols):
+        raise ValueError(f"weighted_sse: h has {hh.numel()} values for a [{rows}, {cols}] weight")
+    _check(load().pq_weighted_sse(_ptr(wb), rows, cols, FMT_IDS[fmt], _ptr(hh), int(per_row), _ptr(sse),
+                                  _stream(wb)), "pq_weighted_sse", f"cannot reshape rows of {cols} into groups for {fmt}")
 
 
 # ---------------------------------------------------------------------------

@@ -208,6 +208,17 @@ int pq_format_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double
                                      (cudaStream_t)stream_));
 }
 
+int pq_weighted_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, const float* h, int h_per_row,
+                    double* sse, void* stream_) {
+  if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (fmt != PQ_FMT_BF16 && !pq::xfmt_scorable(fmt)) return PQ_ERR_FORMAT;
+  if (fmt != PQ_FMT_BF16 && pq::xfmt_group(fmt, cols) == 0) return PQ_ERR_SHAPE;
+  if (rows == 0 || fmt == PQ_FMT_BF16) return PQ_OK;
+  if (!w || !h || !sse) return PQ_ERR_NULL;
+  return cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse, nullptr, pq::MODE_SSE, num_sms_current(),
+                                     (cudaStream_t)stream_, h, h_per_row ? 2 : 1));
+}
+
 int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t* w_hat, void* stream_) {
   if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
   if (fmt < 0 || fmt >= PQ_NUM_FMTS_ALL) return PQ_ERR_FORMAT;

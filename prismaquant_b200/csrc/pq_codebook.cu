@@ -15,6 +15,8 @@
 // (format_registry.py:237-300): FP6 and FP3 have no subnormals, and the E5M2
 // codebook keeps exponent 31 as finite values (largest magnitude 114688).
 // These formats are not on the fused hot path; one warp per row is plenty.
+// The same kernel (which can also describe NVFP4, MXFP8 and FP8 per channel)
+// computes the H-weighted error sum behind predicted_dloss.
 #include "pq_common.cuh"
 #include "pq_internal.h"
 
@@ -31,10 +33,17 @@ struct XFmt {
 };
 
 __host__ __device__ inline bool xfmt_known(int fmt) { return fmt >= PQ_FMT_MXFP4 && fmt < PQ_NUM_FMTS_ALL; }
+// Formats this kernel can score (the fused-sweep ones too, for the weighted sum).
+__host__ __device__ inline bool xfmt_scorable(int fmt) {
+  return fmt == PQ_FMT_NVFP4 || fmt == PQ_FMT_MXFP8 || fmt == PQ_FMT_FP8_CHANNEL || xfmt_known(fmt);
+}
 
 // format_registry.py:391-533 and measure_quant_cost.py:516-548 (FP8_SOURCE's batched form)
 __host__ __device__ inline XFmt xfmt_of(int fmt) {
   switch (fmt) {
+    case PQ_FMT_NVFP4: return {false, CB_E2M1, 0, 16, false};
+    case PQ_FMT_MXFP8: return {false, CB_E4M3, 0, 32, true};
+    case PQ_FMT_FP8_CHANNEL: return {false, CB_E4M3, 0, 0, false};
     case PQ_FMT_MXFP4: return {false, CB_E2M1, 0, 32, true};
     case PQ_FMT_MXFP6_E3M2: return {false, CB_E3M2, 0, 32, true};
     case PQ_FMT_MXFP6_E2M3: return {false, CB_E2M3, 0, 32, true};
@@ -115,9 +124,11 @@ __device__ __forceinline__ float xfmt_scale(const XFmt& f, float cmax, float ama
   return f.mx ? pow2i(e8m0_round(s)) : s;   // s >= 1e-8 / 114688: normal, never clamped
 }
 
+// h_mode: 0 unweighted, 1 one weight per element ([rows, cols]), 2 one weight per row.
 template <int MODE>
 __global__ void __launch_bounds__(256) xfmt_kernel(const uint16_t* __restrict__ w, int64_t rows, int64_t cols,
-                                                   int fmt, double* sse, uint16_t* out) {
+                                                   int fmt, double* sse, uint16_t* out, const float* __restrict__ h,
+                                                   int h_mode) {
   __shared__ float cb[XCB_MAX];
   __shared__ float mags[XCB_MAX / 2 + 1];
   __shared__ int s_ncb;
@@ -149,7 +160,9 @@ __global__ void __launch_bounds__(256) xfmt_kernel(const uint16_t* __restrict__ 
   auto emit = [&](int64_t idx, float wi, float r) {
     if (MODE == MODE_QDQ) out[idx] = (uint16_t)(__float_as_uint(r) >> 16);
     const float e = bf16_round(__fsub_rn(wi, r));
-    part = fmaf(e, e, part);
+    const float e2 = __fmul_rn(e, e);   // the reference squares in fp32, then weights
+    part = h_mode == 0 ? __fadd_rn(part, e2)
+                       : fmaf(h_mode == 1 ? __ldg(h + idx) : __ldg(h + idx / cols), e2, part);
     if (++nsq == 64) {   // fp32 partials hold <= 64 exact squares
       acc += (double)part;
       part = 0.0f;
@@ -195,14 +208,14 @@ int64_t xfmt_group(int fmt, int64_t cols) {
 }
 
 cudaError_t launch_xfmt(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, uint16_t* out,
-                        int mode, int num_sms, cudaStream_t stream) {
+                        int mode, int num_sms, cudaStream_t stream, const float* h, int h_mode) {
   int64_t blocks = (rows * 32 + 255) / 256;
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;
   if (mode == MODE_QDQ)
-    xfmt_kernel<MODE_QDQ><<<(unsigned)blocks, 256, 0, stream>>>(w, rows, cols, fmt, sse, out);
+    xfmt_kernel<MODE_QDQ><<<(unsigned)blocks, 256, 0, stream>>>(w, rows, cols, fmt, sse, out, h, h_mode);
   else
-    xfmt_kernel<MODE_SSE><<<(unsigned)blocks, 256, 0, stream>>>(w, rows, cols, fmt, sse, out);
+    xfmt_kernel<MODE_SSE><<<(unsigned)blocks, 256, 0, stream>>>(w, rows, cols, fmt, sse, out, h, h_mode);
   return cudaGetLastError();
 }
 

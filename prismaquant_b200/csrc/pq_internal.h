@@ -42,7 +42,7 @@ size_t sweep_smem_bytes();
 size_t sweep_fast_smem_bytes();
 int64_t xfmt_group(int fmt, int64_t cols);
 cudaError_t launch_xfmt(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, uint16_t* out,
-                        int mode, int num_sms, cudaStream_t stream);
+                        int mode, int num_sms, cudaStream_t stream, const float* h = nullptr, int h_mode = 0);
 cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cudaStream_t stream);
 cudaError_t launch_sweep_staged(const SweepLaunch& L, int mode, int grid, cudaStream_t stream);
 cudaError_t launch_sweep_generic(const uint16_t* w, int64_t rows, int64_t cols, uint32_t mask, double* sse,

@@ -243,6 +243,18 @@ def _group_by_shape(model: nn.Module, target_names: set[str]):
     return groups
 
 
+def _predicted_dloss(W: torch.Tensor, spec: fr.FormatSpec, h: torch.Tensor, per_row: bool,
+                     per_linear: bool) -> list[float]:
+    """0.5 * sum(h * err^2) for each W[n] of a stacked weight, on the exact kernel (one D2H).
+    h[n] has W[n]'s shape, or (per_row) one value per row of W[n]."""
+    k = _kernel_format(spec) if per_linear else batched_kernel_format(spec)
+    out = torch.zeros(W.size(0), dtype=torch.float64, device=W.device)
+    if k != "BF16":
+        for n in range(W.size(0)):
+            _lib.weighted_sse(W[n], k, h[n].float(), out[n], per_row=per_row)
+    return (0.5 * out).cpu().tolist()
+
+
 def _weight_mse_or_errors(W_list, specs, per_linear=False):
     """Weight MSE of each weight for each spec (one fused pass), as python floats."""
     res = sweep_weight_mse([(str(i), w) for i, w in enumerate(W_list)], specs, per_linear=per_linear)
@@ -287,9 +299,8 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                     out_mse = (y_ref - y_q).float().pow(2).mean(dim=(1, 2))
                     rel = out_mse / ref_energy.clamp_min(1e-12)
                     dl = None
-                    if h_stacked is not None:
-                        err = (W - W_hat).float()
-                        dl = (0.5 * (h_stacked * err.pow(2)).sum(dim=(1, 2))).cpu().tolist()
+                    if h_stacked is not None:   # 0.5 * sum(H * err^2) per Linear (measure_quant_cost.py:638-640)
+                        dl = _predicted_dloss(W, spec, h_stacked, per_row=False, per_linear=_per_linear)
                     om, rl = out_mse.cpu().tolist(), rel.cpu().tolist()
                     for j, name in enumerate(names):
                         wm = 0.0 if wmse is None else wmse[j][spec.name]
@@ -388,9 +399,8 @@ def _measure_packed_experts(model: nn.Module, target_names: set[str], specs: lis
                 accum.setdefault(name, {})[spec.name] = v
                 continue
             dl = None
-            if h_em is not None:
-                err = (w - _batched_quantize(spec, w)).float()
-                dl = float(0.5 * (h_em * err.pow(2).mean(dim=-1)).sum().item() * err.size(-1))
+            if h_em is not None:   # 0.5 * N * sum(H_em * mean_n err^2) (measure_quant_cost.py:430-437)
+                dl = _predicted_dloss(w.unsqueeze(0), spec, h_em.unsqueeze(0), per_row=True, per_linear=False)[0]
             _accumulate_result(accum, name, spec.name, float(v), 0.0, 0.0, predicted_dloss=dl)
 
 

@@ -7,6 +7,9 @@ seeded inputs.
 Outputs:
   small_cases.npz     inputs (bf16 bit patterns) and the reference's outputs
                       for every hot-path function on small edge-case tensors
+  cost_pipeline.json  the reference's cost tables (measure_batched_gpu, measure_unbatched,
+                      _measure_packed_experts, with per-weight / per-channel H) for a
+                      toy model rebuilt from seeds by the GPU tests
   full_digests.json   SHA-256 digests of the reference's outputs on the
                       single-Linear sweep (4096x4096 with 0.1 % x20 outliers,
                       seed 0) and on the fused-sibling q/k/v + gate/up group
@@ -221,6 +224,12 @@ def known_answers():
     return out
 
 
+def cost_pipeline():
+    """The reference's cost tables for the toy model of tests/golden/pipeline_model.py."""
+    from tests.golden.pipeline_model import run_cost_pipeline
+    return run_cost_pipeline(mqc, fr, "cpu")
+
+
 def main():
     arrays = {}
     for name, bits in small_cases().items():
@@ -251,6 +260,8 @@ def main():
     digests["siblings"] = dg
     with open(HERE / "full_digests.json", "w") as f:
         json.dump(digests, f, indent=1, sort_keys=True)
+    with open(HERE / "cost_pipeline.json", "w") as f:
+        json.dump(cost_pipeline(), f, indent=1, sort_keys=True)
     print("wrote", HERE / "small_cases.npz", HERE / "full_digests.json")
 
 

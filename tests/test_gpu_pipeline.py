@@ -1,0 +1,80 @@
+"""The cost-table entry points end to end on the GPU, against the reference's own tables
+(tests/golden/cost_pipeline.json, made by running the reference's measure_batched_gpu,
+measure_unbatched and _measure_packed_experts on the same toy model): every registry format,
+with per-weight and per-channel Fisher diagonals (predicted_dloss) and the error entries.
+
+weight_mse and predicted_dloss come from the bit-exact quantizers and must match within 1e-5.
+output_mse compares bf16 bmm results computed on different devices (CPU for the fixture, cuBLAS
+here), whose bf16 roundings differ, so it is held to the same order of magnitude only."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import pq_oracle as O
+from prismaquant_b200 import format_registry as fr
+from prismaquant_b200 import measure_quant_cost as mqc
+from tests._helpers import to_cuda_bf16
+from tests.golden.pipeline_model import run_cost_pipeline
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "cost_pipeline.json"
+
+
+@pytest.fixture(scope="module")
+def pipeline():
+    return run_cost_pipeline(mqc, fr, "cuda"), json.loads(GOLDEN.read_text())
+
+
+@pytest.mark.parametrize("entry", ["batched", "unbatched", "packed"])
+def test_cost_tables_match_reference(pipeline, entry):
+    got, want = pipeline[0][entry], pipeline[1][entry]
+    assert set(got) == set(want)
+    for name in want:
+        assert set(got[name]) == set(want[name]), name
+        for fmt, w in want[name].items():
+            g = got[name][fmt]
+            if "error" in w:
+                assert "error" in g, (entry, name, fmt, g)
+                continue
+            assert "error" not in g, (entry, name, fmt, g)
+            for k in ("weight_mse", "predicted_dloss"):
+                assert g[k] == pytest.approx(w[k], rel=1e-5, abs=1e-30), (entry, name, fmt, k)
+            for k in ("output_mse", "rel_output_mse"):
+                if w[k] == 0.0:
+                    assert g[k] == 0.0, (entry, name, fmt, k)
+                else:
+                    assert 0.2 < g[k] / w[k] < 5.0, (entry, name, fmt, k, g[k], w[k])
+
+
+def _oracle_weighted(bits, fmt, h, per_row, batched):
+    rec = O.batched_qdq_f32(bits, fmt) if batched else O.cost_qdq_f32(bits, fmt)
+    w = O.bf16_bits_to_f32(bits)
+    err = O.bf16_round((w - rec).astype(np.float32)).reshape(-1, bits.shape[-1])
+    sq = (err * err).astype(np.float32).astype(np.float64)
+    hh = np.asarray(h, dtype=np.float64)
+    return float((sq.sum(axis=1) * hh.reshape(-1)).sum() if per_row else (sq * hh.reshape(sq.shape)).sum())
+
+
+@pytest.mark.parametrize("fmt", ["NVFP4", "MXFP8", "FP8_E4M3", "MXFP4", "MXFP6_E2M3", "FP8_E5M2", "NVFP3", "INT3",
+                                 "INT4_W4A16_g128", "FP8_E4M3_G128"])
+@pytest.mark.parametrize("per_row", [False, True])
+def test_weighted_sse_matches_oracle(fmt, per_row):
+    """pq_weighted_sse: sum(h * err^2) with h per element or per row, against the oracle (1e-5)."""
+    from prismaquant_b200 import _lib
+    bits = O.synthetic_weight_bits((96, 256), seed=17, outlier_frac=0.01)
+    rng = np.random.default_rng(3)
+    h = rng.random(96 if per_row else (96, 256), dtype=np.float32) * np.float32(4.0)
+    out = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.weighted_sse(to_cuda_bf16(bits), fmt, torch.from_numpy(h).cuda(), out, per_row=per_row)
+    if fmt == "FP8_E4M3_G128":
+        rec = O.codebook_qdq_f32(bits, "fp8_e4m3", 128, False)
+        err = O.bf16_round((O.bf16_bits_to_f32(bits) - rec).astype(np.float32))
+        sq = (err * err).astype(np.float32).astype(np.float64)
+        want = float((sq.sum(axis=1) * h).sum() if per_row else (sq * h).sum())
+    else:
+        want = _oracle_weighted(bits, fmt, h, per_row, batched=False)
+    assert out.item() == pytest.approx(want, rel=1e-5)
