@@ -380,14 +380,14 @@ def main():
     except Exception:
         pass
 
-    # end to end through the public API with host buffers: H2D of the weights
-    # from pinned memory, the sweep + export, D2H of the cost table and the packed outputs
+    # end to end through the public API with host buffers: the weights start in pinned host
+    # memory; StreamingSweepExport overlaps their H2D copy, the sweep + export and the D2H copy of
+    # the packed outputs chunk by chunk; the cost table comes back at the end
     e2e = None
     if not a.no_e2e:
         host = {n: w.cpu().pin_memory() for n, w in weights.items()}
-        outs_host = None
-        h2d = sum(t.numel() * 2 for t in host.values())
-        d2h = 0
+        streamer = enc.StreamingSweepExport(host, specs, export_nvfp4=plan.export, device=dev)
+        h2d, d2h = streamer.h2d_bytes, streamer.d2h_bytes
         es = []
         for i in range(a.e2e_steps + 1):
             torch.cuda.synchronize()
@@ -395,25 +395,14 @@ def main():
                 dist.barrier()
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s0.record()
-            for (n, hw), dw in zip(host.items(), plan.weights):
-                dw.copy_(hw, non_blocking=True)
-            step(False)
-            table = plan.sse.cpu()
-            if plan.export:
-                if outs_host is None:
-                    outs_host = [(torch.empty_like(c, device="cpu").pin_memory(),
-                                  torch.empty(s.shape, dtype=torch.uint8).pin_memory()) for c, s in
-                                 zip(plan.codes, plan.scales)]
-                    d2h = sum(c.numel() + s.numel() for c, s in outs_host) + 4 * n_units
-                for (hc, hs), c, s in zip(outs_host, plan.codes, plan.scales):
-                    hc.copy_(c, non_blocking=True)
-                    hs.copy_(s, non_blocking=True)
-                gd = plan.gdiv.cpu()
+            streamer.run()
+            table = streamer.sse_host()
             s1.record()
             torch.cuda.synchronize()
             if i > 0:
                 es.append(s0.elapsed_time(s1))
         d2h += table.numel() * 8
+        del streamer
         e_ms = torch.tensor([statistics.mean(es)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)

@@ -404,3 +404,96 @@ class SweepExportPlan:
             out[name] = {s.name: ({"error": err[s.name]} if s.name in err else
                                   mqc._mse_from_sse(row[mqc._KCOL[mqc._kernel_format(s)]], n)) for s in self.specs}
         return out
+
+
+class StreamingSweepExport:
+    """Cost sweep + NVFP4 export of HOST-resident bf16 weights with the transfers overlapped.
+
+    The weights are split into chunks of whole fused-sibling groups (about `chunk_bytes` each).
+    Chunk c's host->device copy runs on one copy stream while chunk c-1 is swept and exported on
+    the compute stream and chunk c-2's packed outputs go device->host on another copy stream, so a
+    run costs about max(H2D, D2H) of the link instead of their sum.  Each chunk is a
+    SweepExportPlan, so the numbers and bytes are those of the resident path.
+
+    `run()` returns nothing and does not synchronise the host; `costs()` (one device->host read
+    of the cost tables) and `host_outputs` are valid once the current stream has passed `run()`'s
+    work.  host_outputs[name] = (weight_packed u8, weight_scale float8_e4m3fn, weight_global_scale
+    f32 [1]) in pinned host memory."""
+
+    def __init__(self, named_host_weights, specs, export_nvfp4: bool = True, chunk_bytes: int = 512 << 20,
+                 device=None):
+        items = list(named_host_weights.items()) if isinstance(named_host_weights, dict) else \
+            list(named_host_weights)
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.specs = list(specs)
+        self.export = export_nvfp4
+        self.names = [n for n, _ in items]
+        host = {}
+        for n, w in items:
+            if w.device.type != "cpu" or w.dtype != torch.bfloat16:
+                raise TypeError(f"{n}: StreamingSweepExport takes bf16 host tensors")
+            w = w.contiguous()
+            host[n] = w if w.is_pinned() else w.pin_memory()
+        self.host_weights = host
+        # chunks of whole sibling groups, in first-appearance order
+        groups: dict[str, list[str]] = {}
+        for n in self.names:
+            groups.setdefault(sibling_group_key(n) or f"\0{n}", []).append(n)
+        self.chunks: list[list[str]] = [[]]
+        size = 0
+        for members in groups.values():
+            if self.chunks[-1] and size >= chunk_bytes:
+                self.chunks.append([])
+                size = 0
+            self.chunks[-1].extend(members)
+            size += sum(host[m].numel() * 2 for m in members)
+        self.dev_weights = {n: torch.empty(host[n].shape, dtype=torch.bfloat16, device=dev) for n in self.names}
+        self.plans = [SweepExportPlan([(n, self.dev_weights[n]) for n in c], specs, export_nvfp4) for c in self.chunks]
+        self.host_outputs = {}
+        if export_nvfp4:
+            for plan in self.plans:
+                for i, n in enumerate(plan.names):
+                    c, s, g = plan.outputs[i]
+                    self.host_outputs[n] = (torch.empty(c.shape, dtype=torch.uint8).pin_memory(),
+                                            torch.empty(s.shape, dtype=torch.uint8).pin_memory(),
+                                            torch.empty(1, dtype=torch.float32).pin_memory())
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.h2d_bytes = sum(w.numel() * 2 for w in host.values())
+        self.d2h_bytes = sum(c.numel() + s.numel() + 4 for c, s, _ in self.host_outputs.values())
+
+    def run(self):
+        comp = torch.cuda.current_stream(self.device)
+        self.h2d.wait_stream(comp)    # the previous run's readers of the device weights are done
+        self.d2h.wait_stream(comp)
+        for chunk, plan in zip(self.chunks, self.plans):
+            with torch.cuda.stream(self.h2d):
+                for n in chunk:
+                    self.dev_weights[n].copy_(self.host_weights[n], non_blocking=True)
+            comp.wait_stream(self.h2d)
+            plan.run()
+            if self.export:
+                self.d2h.wait_stream(comp)
+                with torch.cuda.stream(self.d2h):
+                    for i, n in enumerate(plan.names):
+                        hc, hs, hg = self.host_outputs[n]
+                        c, s, g = plan.outputs[i]
+                        hc.copy_(c, non_blocking=True)
+                        hs.copy_(s.view(torch.uint8), non_blocking=True)
+                        hg.copy_(g, non_blocking=True)
+        comp.wait_stream(self.d2h)
+
+    def costs(self) -> dict:
+        out = {}
+        for plan in self.plans:
+            out.update(plan.costs())
+        return out
+
+    def sse_host(self) -> torch.Tensor:
+        """All chunks' [n, 4] error sums in one device->host copy (synchronising)."""
+        return torch.cat([p.sse for p in self.plans]).cpu()
+
+    def outputs(self) -> dict:
+        """{name: (weight_packed, weight_scale as float8_e4m3fn, weight_global_scale)} on the host."""
+        return {n: (c, s.view(torch.float8_e4m3fn), g) for n, (c, s, g) in self.host_outputs.items()}

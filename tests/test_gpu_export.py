@@ -177,3 +177,32 @@ def test_nvfp4_scales_every_bf16_amax():
         assert bad.size == 0, (g, bad[:5], got[bad[:5]], want[bad[:5]])
         assert gdiv[i].item() == float(np.float32(1.0) / glob)
     assert _lib.device_error() == 0
+
+
+def test_streaming_sweep_export_equals_resident():
+    """StreamingSweepExport (host weights, chunked H2D / sweep + export / D2H on three streams)
+    gives the resident plan's cost table and packed bytes, fused-sibling joint globals included,
+    on two consecutive runs."""
+    shapes = {"model.layers.0.self_attn.q_proj": (256, 512), "model.layers.0.self_attn.k_proj": (64, 512),
+              "model.layers.0.self_attn.v_proj": (64, 512), "model.layers.0.self_attn.o_proj": (512, 256),
+              "model.layers.0.mlp.gate_proj": (384, 512), "model.layers.0.mlp.up_proj": (384, 512),
+              "model.layers.0.mlp.down_proj": (512, 384), "lm_head": (1000, 512)}
+    host = {n: torch.from_numpy(O.synthetic_weight_bits(s, seed=60 + i, outlier_frac=0.01).view(np.int16))
+            .view(torch.bfloat16) for i, (n, s) in enumerate(shapes.items())}
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3", "BF16")]
+    st = enc.StreamingSweepExport(host, specs, chunk_bytes=200_000)   # several chunks, groups kept whole
+    assert len(st.chunks) > 3
+    plan = enc.SweepExportPlan({n: h.cuda() for n, h in host.items()}, specs)
+    plan.run()
+    want_costs = plan.costs()
+    for _ in range(2):
+        st.run()
+        torch.cuda.synchronize()
+        assert st.costs() == want_costs
+        outs = st.outputs()
+        for i, n in enumerate(plan.names):
+            c, s, g = plan.outputs[i]
+            hc, hs, hg = outs[n]
+            assert torch.equal(hc, c.cpu())
+            assert torch.equal(hs.view(torch.uint8), s.view(torch.uint8).cpu())
+            assert torch.equal(hg, g.cpu())
