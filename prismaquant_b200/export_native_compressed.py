@@ -460,6 +460,7 @@ class StreamingSweepExport:
                                             torch.empty(1, dtype=torch.float32).pin_memory())
         self.h2d = torch.cuda.Stream(dev)
         self.d2h = torch.cuda.Stream(dev)
+        self._chunk_done = [torch.cuda.Event() for _ in self.chunks]   # chunk's outputs are on the host
         self.h2d_bytes = sum(w.numel() * 2 for w in host.values())
         self.d2h_bytes = sum(c.numel() + s.numel() + 4 for c, s, _ in self.host_outputs.values())
 
@@ -482,6 +483,7 @@ class StreamingSweepExport:
                         hc.copy_(c, non_blocking=True)
                         hs.copy_(s.view(torch.uint8), non_blocking=True)
                         hg.copy_(g, non_blocking=True)
+                    self._chunk_done[self.plans.index(plan)].record(self.d2h)
         comp.wait_stream(self.d2h)
 
     def costs(self) -> dict:
@@ -493,6 +495,41 @@ class StreamingSweepExport:
     def sse_host(self) -> torch.Tensor:
         """All chunks' [n, 4] error sums in one device->host copy (synchronising)."""
         return torch.cat([p.sse for p in self.plans]).cpu()
+
+    def export_to(self, writer, input_global_scale: float = DEFAULT_INPUT_GLOBAL_SCALE) -> None:
+        """run(), then hand every tensor's NVFP4 entries to `writer.add_tensors` (an
+        IncrementalSafetensorsWriter) chunk by chunk as each chunk's outputs reach the host, from a
+        background thread, so the disk writes of one chunk overlap the GPU work and transfers of the
+        next.  Keys are `{name}.weight_packed / .weight_scale / .weight_global_scale /
+        .input_global_scale` as _quantize_2d emits them (export_native_compressed.py:1844-1865), so
+        names are module prefixes.  Returns once everything is written; the caller finalizes."""
+        import threading
+        if not self.export:
+            raise ValueError("export_to needs export_nvfp4=True")
+        igs = torch.tensor([float(input_global_scale)], dtype=torch.float32)
+        failure: list[BaseException] = []
+
+        def writer_loop():
+            try:
+                for chunk, done in zip(self.chunks, self._chunk_done):
+                    done.synchronize()
+                    entries = {}
+                    for n in chunk:
+                        hc, hs, hg = self.host_outputs[n]
+                        entries[f"{n}.weight_packed"] = hc
+                        entries[f"{n}.weight_scale"] = hs.view(torch.float8_e4m3fn)
+                        entries[f"{n}.weight_global_scale"] = hg
+                        entries[f"{n}.input_global_scale"] = igs.clone()
+                    writer.add_tensors(entries)
+            except BaseException as e:   # re-raised on the caller's thread
+                failure.append(e)
+
+        self.run()
+        t = threading.Thread(target=writer_loop, name="pq-safetensors-writer")
+        t.start()
+        t.join()
+        if failure:
+            raise failure[0]
 
     def outputs(self) -> dict:
         """{name: (weight_packed, weight_scale as float8_e4m3fn, weight_global_scale)} on the host."""

@@ -271,3 +271,78 @@ def test_registry_matches_reference_registry():
         for p in (shim, str(REFERENCE)):
             if p in sys.path:
                 sys.path.remove(p)
+
+
+def test_safetensors_serializer_matches_safetensors():
+    """Our serializer writes the same bytes as safetensors.torch.save_file (every dtype, scalars,
+    empty tensors, with and without metadata)."""
+    import tempfile
+
+    import torch
+    from safetensors.torch import save_file as st_save
+    from prismaquant_b200 import safetensors_io as S
+    g = torch.Generator().manual_seed(0)
+    dts = [torch.bool, torch.uint8, torch.int8, torch.float8_e5m2, torch.float8_e4m3fn, torch.int16, torch.float16,
+           torch.bfloat16, torch.int32, torch.float32, torch.float64, torch.int64]
+    t = {}
+    for i, d in enumerate(dts):
+        x = torch.randn(3, 5 + i, generator=g) * 10
+        t[f"model.layers.{i}.w{'xyz'[i % 3]}"] = x > 0 if d == torch.bool else x.to(d)
+    t["scalar"] = torch.tensor(3.0)
+    t["empty"] = torch.zeros(0, 4)
+    with tempfile.TemporaryDirectory() as d:
+        for md in (None, {"format": "pt"}):
+            S.save_file(t, f"{d}/ours.safetensors", metadata=md)
+            st_save(t, f"{d}/theirs.safetensors", metadata=md)
+            assert Path(f"{d}/ours.safetensors").read_bytes() == Path(f"{d}/theirs.safetensors").read_bytes()
+
+
+def _tree_bytes(root):
+    return {p.name: p.read_bytes() for p in sorted(Path(root).iterdir())}
+
+
+def test_sharded_writers_match_reference():
+    """write_sharded_safetensors and IncrementalSafetensorsWriter write the same files (names,
+    bytes, index) as the reference's (export_native_compressed.py:3977-4131)."""
+    import sys
+    import tempfile
+
+    import torch
+    from tests.conftest import REFERENCE, reference_available
+    if not reference_available():
+        pytest.skip("reference checkout not present")
+    from prismaquant_b200 import safetensors_io as S
+    shim = str(Path(__file__).resolve().parent.parent / "oracle" / "_shim")
+    sys.path[:0] = [shim, str(REFERENCE)]
+    try:
+        import prismaquant.export_native_compressed as ref
+        g = torch.Generator().manual_seed(1)
+        tensors = {}
+        for i in range(12):
+            rows = 40 + 17 * i
+            tensors[f"model.layers.{i}.mlp.down_proj.weight_packed"] = torch.randint(0, 255, (rows, 64), dtype=torch.uint8,
+                                                                                      generator=g)
+            tensors[f"model.layers.{i}.mlp.down_proj.weight_scale"] = (torch.rand(rows, 8, generator=g) * 100).to(
+                torch.float8_e4m3fn)
+            tensors[f"model.layers.{i}.mlp.down_proj.weight_global_scale"] = torch.rand(1, generator=g)
+            tensors[f"model.layers.{i}.self_attn.o_proj.weight"] = torch.randn(32, 48, generator=g).to(torch.bfloat16)
+        for shard in (10_000, 30_000, 10_000_000):
+            with tempfile.TemporaryDirectory() as a, tempfile.TemporaryDirectory() as b:
+                S.write_sharded_safetensors(tensors, Path(a), shard)
+                ref.write_sharded_safetensors(tensors, Path(b), shard)
+                assert _tree_bytes(a) == _tree_bytes(b)
+            with tempfile.TemporaryDirectory() as a, tempfile.TemporaryDirectory() as b:
+                wa, wb = S.IncrementalSafetensorsWriter(Path(a), shard), ref.IncrementalSafetensorsWriter(Path(b), shard)
+                keys = sorted(tensors)
+                for k0 in range(0, len(keys), 7):   # batches as an export would emit them
+                    batch = {k: tensors[k] for k in keys[k0:k0 + 7]}
+                    wa.add_tensors(batch)
+                    wb.add_tensors(batch)
+                wa.finalize()
+                wb.finalize()
+                assert _tree_bytes(a) == _tree_bytes(b)
+                assert wa.weight_map == wb.weight_map
+    finally:
+        for p in (shim, str(REFERENCE)):
+            if p in sys.path:
+                sys.path.remove(p)

@@ -206,3 +206,41 @@ def test_streaming_sweep_export_equals_resident():
             assert torch.equal(hc, c.cpu())
             assert torch.equal(hs.view(torch.uint8), s.view(torch.uint8).cpu())
             assert torch.equal(hg, g.cpu())
+
+
+def test_streaming_export_to_safetensors():
+    """export_to streams every chunk's NVFP4 entries into IncrementalSafetensorsWriter shards while
+    later chunks are on the GPU; the checkpoint on disk holds the resident path's bytes under the
+    reference's keys."""
+    import tempfile
+    from pathlib import Path
+
+    from safetensors.torch import load_file
+    from prismaquant_b200 import safetensors_io as S
+    shapes = {"model.layers.0.self_attn.q_proj": (256, 512), "model.layers.0.self_attn.k_proj": (64, 512),
+              "model.layers.0.self_attn.v_proj": (64, 512), "model.layers.0.mlp.gate_proj": (384, 512),
+              "model.layers.0.mlp.up_proj": (384, 512), "model.layers.0.mlp.down_proj": (512, 384)}
+    host = {n: torch.from_numpy(O.synthetic_weight_bits(s, seed=80 + i).view(np.int16)).view(torch.bfloat16)
+            for i, (n, s) in enumerate(shapes.items())}
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3")]
+    st = enc.StreamingSweepExport(host, specs, chunk_bytes=300_000)
+    costs, packed = enc.sweep_and_export({n: h.cuda() for n, h in host.items()}, specs)
+    with tempfile.TemporaryDirectory() as d:
+        w = S.IncrementalSafetensorsWriter(Path(d), shard_bytes=150_000)
+        st.export_to(w)
+        w.finalize()
+        assert st.costs() == costs
+        files = sorted(p.name for p in Path(d).iterdir())
+        assert "model.safetensors.index.json" in files and len(files) > 2
+        loaded = {}
+        for f in files:
+            if f.endswith(".safetensors"):
+                loaded.update(load_file(str(Path(d) / f)))
+        assert set(loaded) == {f"{n}.{k}" for n in shapes for k in
+                               ("weight_packed", "weight_scale", "weight_global_scale", "input_global_scale")}
+        for n in shapes:
+            p, s, g = packed[n]
+            assert torch.equal(loaded[f"{n}.weight_packed"], p.cpu())
+            assert torch.equal(loaded[f"{n}.weight_scale"].view(torch.uint8), s.view(torch.uint8).cpu())
+            assert torch.equal(loaded[f"{n}.weight_global_scale"], g.cpu())
+            assert loaded[f"{n}.input_global_scale"].tolist() == [1.0]
