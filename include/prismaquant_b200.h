@@ -124,6 +124,23 @@ int pq_weighted_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, cons
                     double* sse, void* stream);
 
 /*
+ * Output error of a quantized Linear, on the tensor cores:
+ *   y_ref = bf16(X W^T), y_q = bf16(X_hat W_hat^T)  (bf16 operands, fp32 accumulate)
+ * ADDS sum(bf16(y_ref - y_q)^2) to err_sse[b] and sum(y_ref^2) to ref_sse[b]
+ * (fp64, device; zero them first; either may be NULL) for each of `batch`
+ * stacked Linears: x, x_hat are [batch, rows, k], w, w_hat [batch, out, k],
+ * bf16, contiguous, 16-byte aligned, k a multiple of 8.  output_mse and
+ * ref_energy are these sums over rows*out (measure_quant_cost.py:599-605,
+ * 630-635, whose two bmm's and the difference this replaces, without writing
+ * either product).  y_ref / y_q (fp32 [batch, rows, out], may be NULL)
+ * receive the unrounded accumulators.  PQ_ERR_DEVICE if an MMA completion
+ * wait gave up.
+ */
+int pq_output_sse(const uint16_t* x, const uint16_t* w, const uint16_t* x_hat, const uint16_t* w_hat, int64_t batch,
+                  int64_t rows, int64_t out, int64_t k, double* err_sse, double* ref_sse, float* y_ref, float* y_q,
+                  void* stream);
+
+/*
  * NVFP4 export, pass 1: E2M1 codes (abs-codebook RTN, ties toward zero,
  * sign from signbit; export_native_compressed.py:118-136, 226-233), the bf16
  * amax of every 16-group, and the max group amax of each of `batch`

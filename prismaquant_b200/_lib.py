@@ -30,7 +30,7 @@ EXPORTED = [
     "pq_sweep_sse", "pq_cost_qdq", "pq_nvfp4_codes", "pq_nvfp4_scales", "pq_nvfp4_pack",
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
-    "pq_format_sse", "pq_weighted_sse",
+    "pq_format_sse", "pq_weighted_sse", "pq_output_sse",
 ]
 
 
@@ -67,6 +67,7 @@ def load() -> ctypes.CDLL:
         "pq_cost_qdq": [P, I64, I64, I, P, V],
         "pq_format_sse": [P, I64, I64, I, P, V],
         "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
+        "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
         "pq_nvfp4_codes": [P, I64, I64, I64, P, P, P, V],
         "pq_nvfp4_scales": [I, ctypes.POINTER(P), ctypes.POINTER(I64), P, ctypes.POINTER(ctypes.c_int32), P,
                             ctypes.POINTER(P), P, V],
@@ -220,6 +221,37 @@ def weighted_sse(w: torch.Tensor, fmt: str, h: torch.Tensor, sse: torch.Tensor, 
         raise ValueError(f"weighted_sse: h has {hh.numel()} values for a [{rows}, {cols}] weight")
     _check(load().pq_weighted_sse(_ptr(wb), rows, cols, FMT_IDS[fmt], _ptr(hh), int(per_row), _ptr(sse),
                                   _stream(wb)), "pq_weighted_sse", f"cannot reshape rows of {cols} into groups for {fmt}")
+
+
+def output_sse(x: torch.Tensor, w: torch.Tensor, x_hat: torch.Tensor, w_hat: torch.Tensor,
+               err_sse: torch.Tensor | None, ref_sse: torch.Tensor | None,
+               y_ref: torch.Tensor | None = None, y_q: torch.Tensor | None = None) -> None:
+    """Adds, per stacked Linear b, sum(bf16(y_ref - y_q)^2) into err_sse[b] and sum(y_ref^2) into
+    ref_sse[b] (fp64 [batch] on the device), y_ref = bf16(X W^T), y_q = bf16(X_hat W_hat^T)
+    computed on the tensor cores.  x, x_hat: [batch, rows, k] (or [rows, k]); w, w_hat:
+    [batch, out, k] (or [out, k]); k a multiple of 8.  y_ref / y_q (fp32 [batch, rows, out])
+    optionally receive the unrounded accumulators."""
+    xs = [as_bf16_cuda(t, "output_sse") for t in (x, w, x_hat, w_hat)]
+    squeeze = xs[0].dim() == 2
+    if squeeze:
+        xs = [t.unsqueeze(0) for t in xs]
+    xb, wb, xqb, wqb = xs
+    if any(t.dim() != 3 for t in xs) or xb.shape != xqb.shape or wb.shape != wqb.shape or \
+            xb.shape[0] != wb.shape[0] or xb.shape[2] != wb.shape[2]:
+        raise ValueError(f"output_sse: shapes {[tuple(t.shape) for t in (x, w, x_hat, w_hat)]} do not match")
+    batch, rows, k = xb.shape
+    out = wb.shape[1]
+    for name, t in (("err_sse", err_sse), ("ref_sse", ref_sse)):
+        if t is not None and (t.dtype != torch.float64 or t.device != xb.device or t.numel() != batch
+                              or not t.is_contiguous()):
+            raise TypeError(f"output_sse: {name} must be a contiguous float64 [{batch}] tensor on the device")
+    for name, t in (("y_ref", y_ref), ("y_q", y_q)):
+        if t is not None and (t.dtype != torch.float32 or t.device != xb.device or t.numel() != batch * rows * out
+                              or not t.is_contiguous()):
+            raise TypeError(f"output_sse: {name} must be a contiguous float32 [{batch}, {rows}, {out}] tensor")
+    _check(load().pq_output_sse(_ptr(xb), _ptr(wb), _ptr(xqb), _ptr(wqb), batch, rows, out, k, _ptr(err_sse),
+                                _ptr(ref_sse), _ptr(y_ref), _ptr(y_q), _stream(xb)),
+           "pq_output_sse", f"k = {k} must be a multiple of 8")
 
 
 # ---------------------------------------------------------------------------

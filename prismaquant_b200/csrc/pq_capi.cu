@@ -219,6 +219,18 @@ int pq_weighted_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, cons
                                      (cudaStream_t)stream_, h, h_per_row ? 2 : 1));
 }
 
+int pq_output_sse(const uint16_t* x, const uint16_t* w, const uint16_t* x_hat, const uint16_t* w_hat, int64_t batch,
+                  int64_t rows, int64_t out, int64_t k, double* err_sse, double* ref_sse, float* y_ref, float* y_q,
+                  void* stream_) {
+  if (batch < 0 || rows < 0 || out < 0 || k < 1 || (k & 7)) return PQ_ERR_SHAPE;
+  if (batch > 65535 || (rows + 127) / 128 > 65535 || (out + 127) / 128 > 0x7fffffff) return PQ_ERR_LIMIT;
+  if (batch == 0 || rows == 0 || out == 0) return PQ_OK;
+  if (!x || !w || !x_hat || !w_hat) return PQ_ERR_NULL;
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(x_hat, 16) || !aligned(w_hat, 16)) return PQ_ERR_ALIGN;
+  return cuda_status(pq::launch_outerr(x, w, x_hat, w_hat, batch, rows, out, k, err_sse, ref_sse, y_ref, y_q,
+                                       (cudaStream_t)stream_));
+}
+
 int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t* w_hat, void* stream_) {
   if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
   if (fmt < 0 || fmt >= PQ_NUM_FMTS_ALL) return PQ_ERR_FORMAT;

@@ -44,6 +44,9 @@ int64_t xfmt_group(int fmt, int64_t cols);
 cudaError_t launch_xfmt(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, uint16_t* out,
                         int mode, int num_sms, cudaStream_t stream, const float* h = nullptr, int h_mode = 0);
 cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cudaStream_t stream);
+cudaError_t launch_outerr(const uint16_t* x, const uint16_t* w, const uint16_t* xq, const uint16_t* wq, int64_t batch,
+                          int64_t rows, int64_t out, int64_t K, double* err_sum, double* ref_energy, float* d_ref,
+                          float* d_q, cudaStream_t stream);
 cudaError_t launch_sweep_staged(const SweepLaunch& L, int mode, int grid, cudaStream_t stream);
 cudaError_t launch_sweep_generic(const uint16_t* w, int64_t rows, int64_t cols, uint32_t mask, double* sse,
                                  uint16_t* out, int mode, int num_sms, cudaStream_t stream);

@@ -5,5 +5,6 @@
 #include "pq_pack.cu"
 #include "pq_fisher.cu"
 #include "pq_codebook.cu"
+#include "pq_outerr.cu"
 #include "pq_capi.cu"
 #include "pq_noalloc.cu"

@@ -280,8 +280,13 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
             rows = min(a.size(0) for a in acts)
             W = torch.stack([m.weight.detach().to(device=dev, dtype=dtype) for _, m in chunk])
             X = torch.stack([a[:rows].to(device=dev, dtype=dtype) for a in acts])
-            y_ref = torch.bmm(X, W.transpose(1, 2))
-            ref_energy = y_ref.float().pow(2).mean(dim=(1, 2))
+            # tensor-core output error (pq_output_sse) for bf16 operands with k % 8 == 0; the two
+            # bmm's otherwise
+            fused_out = dtype == torch.bfloat16 and X.shape[-1] % 8 == 0 and rows > 0 and W.shape[1] > 0
+            ref_energy = None
+            if not fused_out:
+                y_ref = torch.bmm(X, W.transpose(1, 2))
+                ref_energy = y_ref.float().pow(2).mean(dim=(1, 2))
             h_stacked = None
             if h_detail is not None and all(n in h_detail for n in names):
                 hs = [h_detail.load(n) for n in names]
@@ -295,8 +300,17 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                         raise NotImplementedError(f"B200 cost kernels take bf16 weights, got {dtype}")
                     W_hat = spec.quantize_dequantize(W) if _per_linear else _batched_quantize(spec, W)
                     X_hat = spec.activation_quantize_dequantize(X.clone())
-                    y_q = torch.bmm(X_hat, W_hat.transpose(1, 2))
-                    out_mse = (y_ref - y_q).float().pow(2).mean(dim=(1, 2))
+                    if fused_out:
+                        n_out = rows * W.shape[1]
+                        err = torch.zeros(W.shape[0], dtype=torch.float64, device=dev)
+                        ref = torch.zeros_like(err) if ref_energy is None else None
+                        _lib.output_sse(X, W, X_hat, W_hat, err, ref)
+                        if ref is not None:
+                            ref_energy = ref / n_out
+                        out_mse = err / n_out
+                    else:
+                        y_q = torch.bmm(X_hat, W_hat.transpose(1, 2))
+                        out_mse = (y_ref - y_q).float().pow(2).mean(dim=(1, 2))
                     rel = out_mse / ref_energy.clamp_min(1e-12)
                     dl = None
                     if h_stacked is not None:   # 0.5 * sum(H * err^2) per Linear (measure_quant_cost.py:638-640)
