@@ -141,6 +141,20 @@ int pq_output_sse(const uint16_t* x, const uint16_t* w, const uint16_t* x_hat, c
                   void* stream);
 
 /*
+ * The reference's split of the same computation (measure_quant_cost.py:599-600
+ * once per chunk, :630-635 per format), each a single tensor-core GEMM:
+ * pq_output_ref computes y_ref = bf16(X W^T), stores it (bf16 [batch, rows,
+ * out], 16-byte aligned; may be NULL) and ADDS sum(y_ref^2) to ref_sse[b];
+ * pq_output_err computes y_q = bf16(X_hat W_hat^T) and ADDS
+ * sum(bf16(y_ref - y_q)^2) to err_sse[b], reading y_ref from memory.  Same
+ * operand rules as pq_output_sse.
+ */
+int pq_output_ref(const uint16_t* x, const uint16_t* w, int64_t batch, int64_t rows, int64_t out, int64_t k,
+                  uint16_t* y_ref, double* ref_sse, void* stream);
+int pq_output_err(const uint16_t* x_hat, const uint16_t* w_hat, const uint16_t* y_ref, int64_t batch, int64_t rows,
+                  int64_t out, int64_t k, double* err_sse, void* stream);
+
+/*
  * NVFP4 export, pass 1: E2M1 codes (abs-codebook RTN, ties toward zero,
  * sign from signbit; export_native_compressed.py:118-136, 226-233), the bf16
  * amax of every 16-group, and the max group amax of each of `batch`

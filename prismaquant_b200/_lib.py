@@ -30,7 +30,7 @@ EXPORTED = [
     "pq_sweep_sse", "pq_cost_qdq", "pq_nvfp4_codes", "pq_nvfp4_scales", "pq_nvfp4_pack",
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
-    "pq_format_sse", "pq_weighted_sse", "pq_output_sse",
+    "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err",
 ]
 
 
@@ -68,6 +68,8 @@ def load() -> ctypes.CDLL:
         "pq_format_sse": [P, I64, I64, I, P, V],
         "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
         "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
+        "pq_output_ref": [P, P, I64, I64, I64, I64, P, P, V],
+        "pq_output_err": [P, P, P, I64, I64, I64, I64, P, V],
         "pq_nvfp4_codes": [P, I64, I64, I64, P, P, P, V],
         "pq_nvfp4_scales": [I, ctypes.POINTER(P), ctypes.POINTER(I64), P, ctypes.POINTER(ctypes.c_int32), P,
                             ctypes.POINTER(P), P, V],
@@ -252,6 +254,49 @@ def output_sse(x: torch.Tensor, w: torch.Tensor, x_hat: torch.Tensor, w_hat: tor
     _check(load().pq_output_sse(_ptr(xb), _ptr(wb), _ptr(xqb), _ptr(wqb), batch, rows, out, k, _ptr(err_sse),
                                 _ptr(ref_sse), _ptr(y_ref), _ptr(y_q), _stream(xb)),
            "pq_output_sse", f"k = {k} must be a multiple of 8")
+
+
+def _outerr_operands(x: torch.Tensor, w: torch.Tensor, what: str):
+    xb, wb = as_bf16_cuda(x, what), as_bf16_cuda(w, what)
+    if xb.dim() == 2:
+        xb, wb = xb.unsqueeze(0), wb.unsqueeze(0)
+    if xb.dim() != 3 or wb.dim() != 3 or xb.shape[0] != wb.shape[0] or xb.shape[2] != wb.shape[2]:
+        raise ValueError(f"{what}: shapes {tuple(x.shape)} and {tuple(w.shape)} do not match")
+    return xb, wb
+
+
+def _check_sums(t, batch, dev, what):
+    if t is not None and (t.dtype != torch.float64 or t.device != dev or t.numel() != batch or not t.is_contiguous()):
+        raise TypeError(f"{what} must be a contiguous float64 [{batch}] tensor on the device")
+
+
+def output_ref(x: torch.Tensor, w: torch.Tensor, ref_sse: torch.Tensor | None,
+               y_ref: torch.Tensor | None = None) -> None:
+    """y_ref = bf16(X W^T) on the tensor cores: written into `y_ref` (bf16 [batch, rows, out], may be
+    None) and sum(y_ref^2) added into ref_sse[b] (fp64 [batch] on the device)."""
+    xb, wb = _outerr_operands(x, w, "output_ref")
+    batch, rows, k = xb.shape
+    out = wb.shape[1]
+    _check_sums(ref_sse, batch, xb.device, "output_ref: ref_sse")
+    if y_ref is not None and (y_ref.dtype != torch.bfloat16 or y_ref.device != xb.device or
+                              y_ref.numel() != batch * rows * out or not y_ref.is_contiguous()):
+        raise TypeError(f"output_ref: y_ref must be a contiguous bfloat16 [{batch}, {rows}, {out}] tensor")
+    _check(load().pq_output_ref(_ptr(xb), _ptr(wb), batch, rows, out, k, _ptr(y_ref), _ptr(ref_sse), _stream(xb)),
+           "pq_output_ref", f"k = {k} must be a multiple of 8")
+
+
+def output_err(x_hat: torch.Tensor, w_hat: torch.Tensor, y_ref: torch.Tensor, err_sse: torch.Tensor) -> None:
+    """Adds sum(bf16(y_ref - bf16(X_hat W_hat^T))^2) into err_sse[b]; y_ref is the bf16 output of
+    output_ref for the same shapes."""
+    xb, wb = _outerr_operands(x_hat, w_hat, "output_err")
+    batch, rows, k = xb.shape
+    out = wb.shape[1]
+    _check_sums(err_sse, batch, xb.device, "output_err: err_sse")
+    if y_ref.dtype != torch.bfloat16 or y_ref.device != xb.device or y_ref.numel() != batch * rows * out or \
+            not y_ref.is_contiguous():
+        raise TypeError(f"output_err: y_ref must be a contiguous bfloat16 [{batch}, {rows}, {out}] tensor")
+    _check(load().pq_output_err(_ptr(xb), _ptr(wb), _ptr(y_ref), batch, rows, out, k, _ptr(err_sse), _stream(xb)),
+           "pq_output_err", f"k = {k} must be a multiple of 8")
 
 
 # ---------------------------------------------------------------------------

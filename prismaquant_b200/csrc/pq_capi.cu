@@ -219,16 +219,44 @@ int pq_weighted_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, cons
                                      (cudaStream_t)stream_, h, h_per_row ? 2 : 1));
 }
 
+// Shapes the output-error kernels take: k % 8 == 0 (16-byte tensor-map strides), grid limits.
+static int outerr_shape(int64_t batch, int64_t rows, int64_t out, int64_t k) {
+  if (batch < 0 || rows < 0 || out < 0 || k < 1 || (k & 7)) return PQ_ERR_SHAPE;
+  if (batch > 65535 || (rows + 127) / 128 > 0x7fffffff || (out + 127) / 128 > 65535 || k > (int64_t)1 << 31)
+    return PQ_ERR_LIMIT;
+  return PQ_OK;
+}
+
 int pq_output_sse(const uint16_t* x, const uint16_t* w, const uint16_t* x_hat, const uint16_t* w_hat, int64_t batch,
                   int64_t rows, int64_t out, int64_t k, double* err_sse, double* ref_sse, float* y_ref, float* y_q,
                   void* stream_) {
-  if (batch < 0 || rows < 0 || out < 0 || k < 1 || (k & 7)) return PQ_ERR_SHAPE;
-  if (batch > 65535 || (rows + 127) / 128 > 65535 || (out + 127) / 128 > 0x7fffffff) return PQ_ERR_LIMIT;
+  const int st = outerr_shape(batch, rows, out, k);
+  if (st) return st;
   if (batch == 0 || rows == 0 || out == 0) return PQ_OK;
   if (!x || !w || !x_hat || !w_hat) return PQ_ERR_NULL;
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(x_hat, 16) || !aligned(w_hat, 16)) return PQ_ERR_ALIGN;
   return cuda_status(pq::launch_outerr(x, w, x_hat, w_hat, batch, rows, out, k, err_sse, ref_sse, y_ref, y_q,
                                        (cudaStream_t)stream_));
+}
+
+int pq_output_ref(const uint16_t* x, const uint16_t* w, int64_t batch, int64_t rows, int64_t out, int64_t k,
+                  uint16_t* y_ref, double* ref_sse, void* stream_) {
+  const int st = outerr_shape(batch, rows, out, k);
+  if (st) return st;
+  if (batch == 0 || rows == 0 || out == 0) return PQ_OK;
+  if (!x || !w) return PQ_ERR_NULL;
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y_ref, 16)) return PQ_ERR_ALIGN;
+  return cuda_status(pq::launch_outerr_ref(x, w, batch, rows, out, k, y_ref, ref_sse, (cudaStream_t)stream_));
+}
+
+int pq_output_err(const uint16_t* x_hat, const uint16_t* w_hat, const uint16_t* y_ref, int64_t batch, int64_t rows,
+                  int64_t out, int64_t k, double* err_sse, void* stream_) {
+  const int st = outerr_shape(batch, rows, out, k);
+  if (st) return st;
+  if (batch == 0 || rows == 0 || out == 0) return PQ_OK;
+  if (!x_hat || !w_hat || !y_ref) return PQ_ERR_NULL;
+  if (!aligned(x_hat, 16) || !aligned(w_hat, 16) || !aligned(y_ref, 16)) return PQ_ERR_ALIGN;
+  return cuda_status(pq::launch_outerr_err(x_hat, w_hat, y_ref, batch, rows, out, k, err_sse, (cudaStream_t)stream_));
 }
 
 int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t* w_hat, void* stream_) {

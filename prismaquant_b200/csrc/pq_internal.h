@@ -47,6 +47,10 @@ cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cuda
 cudaError_t launch_outerr(const uint16_t* x, const uint16_t* w, const uint16_t* xq, const uint16_t* wq, int64_t batch,
                           int64_t rows, int64_t out, int64_t K, double* err_sum, double* ref_energy, float* d_ref,
                           float* d_q, cudaStream_t stream);
+cudaError_t launch_outerr_ref(const uint16_t* x, const uint16_t* w, int64_t batch, int64_t rows, int64_t out,
+                              int64_t K, uint16_t* y_ref, double* ref_energy, cudaStream_t stream);
+cudaError_t launch_outerr_err(const uint16_t* xq, const uint16_t* wq, const uint16_t* y_ref, int64_t batch,
+                              int64_t rows, int64_t out, int64_t K, double* err_sum, cudaStream_t stream);
 cudaError_t launch_sweep_staged(const SweepLaunch& L, int mode, int grid, cudaStream_t stream);
 cudaError_t launch_sweep_generic(const uint16_t* w, int64_t rows, int64_t cols, uint32_t mask, double* sse,
                                  uint16_t* out, int mode, int num_sms, cudaStream_t stream);

@@ -1,60 +1,92 @@
 // Output error of a quantized Linear on the tcgen05 tensor cores.
 //
-// measure_quant_cost.py:599-605, 630-635 computes, per Linear and format,
-//   y_ref = bf16(X W^T),  y_q = bf16(X_hat W_hat^T)      (bf16 bmm, fp32 accumulate)
+// measure_quant_cost.py:599-605, 630-635 computes, per chunk of same-shape Linears,
+//   y_ref = bf16(X W^T)  once,  and per format  y_q = bf16(X_hat W_hat^T)
 //   output_mse = mean(bf16(y_ref - y_q)^2),  ref_energy = mean(y_ref^2)
-// This kernel computes both products for one 128x128 output tile per CTA with
-// tcgen05.mma (BF16 x BF16 -> FP32) into two TMEM accumulators and reduces the
-// error and the energy in the epilogue, so neither y_ref nor y_q is written.
+// with bf16 bmm's (fp32 accumulate).  Three kernel modes cover it:
+//   OE_REF   X W^T          -> writes bf16 y_ref (optional), adds sum(y_ref^2)
+//   OE_ERR   X_hat W_hat^T  -> reads bf16 y_ref, adds sum(bf16(y_ref - y_q)^2)
+//   OE_DUAL  both products in one pass (two accumulators), adds both sums; y_ref never stored
 //
-//  * Operand tiles (128 rows x 64 K, bf16) are staged in shared memory in the
-//    canonical K-major 128-byte-swizzle layout (8-row groups of 1024 B, the
-//    16-byte chunk c of row r at chunk c ^ (r % 8)), by ordinary 16-byte loads;
-//  * one thread issues the MMAs (4 x K=16 per operand pair and K step) and
-//    commits them to an mbarrier; every wait is bounded and a timeout sets the
-//    device error word and skips the remaining MMAs;
-//  * TMEM: 256 columns per CTA (reference accumulator in [0,128), quantized in
-//    [128,256)), allocated and freed by warp 0 on every path; at most two CTAs
-//    per SM (96 KB of shared memory each), so the 512 columns always suffice.
+// One CTA computes a 128 x BN output tile (BN = 256 for one product, 128 per product in
+// OE_DUAL) of one batch entry:
+//  * TMA (3-D tensor maps [batch, rows, k], 128-byte swizzle, zero fill past the edges) loads
+//    64-wide K slices of the operands into an NSTAGE ring of shared-memory stages, in the
+//    canonical K-major SW128 layout the MMA descriptors name;
+//  * thread 0 produces (waits for a free stage, arms its full barrier, issues the loads);
+//    thread 32 issues the MMAs (4 x K=16 per stage and product) and commits each stage back to
+//    its empty barrier, then the whole tile to the accumulator barrier;
+//  * all four warps then read the fp32 accumulators from TMEM (warp w owns lanes 32w..32w+31,
+//    i.e. tile rows) and reduce the bf16 error / energy; sums go to fp64 atomics.
+// Every wait is bounded: a timeout sets the device error word and the abort flag, the roles
+// stop issuing, outstanding loads and MMAs are waited for (bounded) and TMEM is freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "pq_common.cuh"
 #include "pq_internal.h"
 
 namespace pq {
 
-constexpr int OE_M = 128, OE_N = 128, OE_K = 64, OE_THREADS = 128;
+enum { OE_REF = 0, OE_ERR = 1, OE_DUAL = 2 };
+constexpr int OE_BM = 128, OE_BK = 64, OE_THREADS = 128;
 constexpr uint32_t OE_TMEM_COLS = 256;
-constexpr int OE_TILE_BYTES = OE_M * OE_K * 2;            // 16 KB, A and B tiles alike (M == N)
-constexpr int OE_SMEM_BYTES = 96 * 1024;                  // 1 KB alignment slack + 4 tiles + barrier, padded
-                                                          // so that at most 2 CTAs share an SM
 
-// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12 = 1),
-// both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t OE_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(OE_N >> 3) << 17) |
-                              ((uint32_t)(OE_M >> 4) << 24);
+template <int MODE>
+struct OeCfg {
+  static constexpr bool DUAL = MODE == OE_DUAL;
+  static constexpr int BN = DUAL ? 128 : 256;               // columns per product
+  static constexpr int A_BYTES = OE_BM * OE_BK * 2;         // 16 KB
+  static constexpr int B_BYTES = BN * OE_BK * 2;            // 16 / 32 KB
+  static constexpr int PAIR_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = (DUAL ? 2 : 1) * PAIR_BYTES;   // 64 / 48 KB
+  static constexpr int NSTAGE = DUAL ? 3 : 4;
+  static constexpr int SMEM = 1024 + NSTAGE * STAGE_BYTES + 256;    // align slack, stages, barriers
+  // kind::f16 instruction descriptor: D f32 (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12 = 1),
+  // both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24.
+  static constexpr uint32_t IDESC =
+      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(OE_BM >> 4) << 24);
+};
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+struct OeArgs {
+  int64_t rows, out, k;
+  double* err_sum;      // [batch] (ERR, DUAL)
+  double* ref_sum;      // [batch] (REF, DUAL)
+  uint16_t* y_ref;      // bf16 [batch, rows, out]: REF writes it (may be null), ERR reads it
+  float* d_ref;         // DUAL: fp32 accumulators (may be null)
+  float* d_q;
+};
 
-// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile starting at `saddr`:
-// start address >> 4 (bits 0-13), leading byte offset 16 B (>> 4 = 1, bits 16-29), stride byte
-// offset 1024 B between 8-row groups (>> 4, bits 32-45), version 1 (bits 46-47), swizzle 128B
-// (value 2, bits 61-63).
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile starting at `saddr`
+// (1024-byte aligned atoms): start >> 4 (bits 0-13), leading byte offset 16 B (>> 4 = 1, bits
+// 16-29), stride byte offset 1024 B between 8-row groups (>> 4, bits 32-45), version 1 (bits
+// 46-47), layout SWIZZLE_128B (2, bits 61-63).  Advancing K by 16 bf16 adds 32 bytes to start.
 __device__ __forceinline__ uint64_t oe_desc(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-__device__ __forceinline__ void oe_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, bool accumulate) {
-  const uint32_t acc = accumulate ? 1u : 0u;
+__device__ __forceinline__ void oe_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
       :
-      : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(OE_IDESC), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+      : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
+// arrives on `bar` once every tcgen05 operation this thread issued before it has completed
 __device__ __forceinline__ void oe_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+__device__ __forceinline__ void oe_tma_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void oe_ld16(uint32_t taddr, float (&v)[16]) {
@@ -70,55 +102,84 @@ __device__ __forceinline__ void oe_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Rows [r0, r0 + 128) x K [k0, k0 + 64) of a row-major [nrows, K] bf16 matrix into a swizzled
-// tile (zeros outside the matrix).  K % 8 == 0 and 16-byte-aligned rows (host-checked).
-__device__ __forceinline__ void oe_stage(uint8_t* tile, const uint16_t* __restrict__ g, int64_t nrows, int64_t K,
-                                         int64_t r0, int64_t k0, int tid) {
-  for (int i = tid; i < OE_M * 8; i += OE_THREADS) {
-    const int r = i >> 3, c = i & 7;
-    const int64_t gr = r0 + r, gk = k0 + 8 * c;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (gr < nrows && gk < K) v = __ldg(reinterpret_cast<const uint4*>(g + gr * K + gk));
-    *reinterpret_cast<uint4*>(tile + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = v;
+// 16 bf16 values of y_ref at [row, col0 .. col0+15] (zeros past `out`), as floats
+__device__ __forceinline__ void oe_load_yref(const uint16_t* __restrict__ y, int64_t row_off, int64_t col0,
+                                             int64_t out, bool vec, float (&a)[16]) {
+  if (vec) {
+    const uint4 u0 = __ldcs(reinterpret_cast<const uint4*>(y + row_off + col0));
+    const uint4 u1 = __ldcs(reinterpret_cast<const uint4*>(y + row_off + col0 + 8));
+    const uint32_t u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      a[2 * i] = __uint_as_float(u[i] << 16);
+      a[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      a[i] = col0 + i < out ? __uint_as_float((uint32_t)y[row_off + col0 + i] << 16) : 0.0f;
   }
 }
 
+// 16 values already rounded to bf16 (low 16 bits zero) into y_ref[row, col0 ..]
+__device__ __forceinline__ void oe_store_yref(uint16_t* __restrict__ y, int64_t row_off, int64_t col0, int64_t out,
+                                              bool vec, const float (&a)[16]) {
+  if (vec) {
+    uint32_t u[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) u[i] = (__float_as_uint(a[2 * i]) >> 16) | (__float_as_uint(a[2 * i + 1]) & 0xFFFF0000u);
+    *reinterpret_cast<uint4*>(y + row_off + col0) = make_uint4(u[0], u[1], u[2], u[3]);
+    *reinterpret_cast<uint4*>(y + row_off + col0 + 8) = make_uint4(u[4], u[5], u[6], u[7]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (col0 + i < out) y[row_off + col0 + i] = (uint16_t)(__float_as_uint(a[i]) >> 16);
+  }
+}
+
+// Bounded wait that also gives up as soon as another role has set the abort flag; a timeout
+// records the device error (as mbar_wait_bounded does).
+__device__ __forceinline__ bool oe_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  atomicExch(&g_pq_device_error, ERR_MBAR_TIMEOUT);
+  return false;
+}
+
+template <int MODE>
 __global__ void __launch_bounds__(OE_THREADS, 1)
-    outerr_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const uint16_t* __restrict__ xq,
-                  const uint16_t* __restrict__ wq, int64_t rows, int64_t out, int64_t K, double* err_sum,
-                  double* ref_energy, float* d_ref, float* d_q) {
-  // batch entry blockIdx.z: its own X/X_hat [rows, K], W/W_hat [out, K], sums and fp32 outputs
-  const int64_t bz = blockIdx.z;
-  x += bz * rows * K;
-  xq += bz * rows * K;
-  w += bz * out * K;
-  wq += bz * out * K;
-  if (err_sum) err_sum += bz;
-  if (ref_energy) ref_energy += bz;
-  if (d_ref) d_ref += bz * rows * out;
-  if (d_q) d_q += bz * rows * out;
+    outerr_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                  const __grid_constant__ CUtensorMap taq, const __grid_constant__ CUtensorMap tbq, OeArgs p) {
+  using C = OeCfg<MODE>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // swizzle atoms are 1024-byte aligned: round the window up (1 KB of slack is allocated)
-  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  uint8_t* sA = smem;                          // X tile
-  uint8_t* sB = smem + OE_TILE_BYTES;          // W tile
-  uint8_t* sAq = smem + 2 * OE_TILE_BYTES;     // X_hat tile
-  uint8_t* sBq = smem + 3 * OE_TILE_BYTES;     // W_hat tile
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 4 * OE_TILE_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
-  volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // 1024-aligned atoms
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NSTAGE * C::STAGE_BYTES);
+  uint64_t* empty = full + C::NSTAGE;
+  uint64_t* acc_full = empty + C::NSTAGE;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* consumed = abort_flag + 1;   // stages the MMA thread has waited for
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t m0 = (int64_t)blockIdx.y * OE_M, n0 = (int64_t)blockIdx.x * OE_N;
+  const int bz = blockIdx.z;
+  const int m0 = blockIdx.x * OE_BM, n0 = blockIdx.y * C::BN;   // M fastest: CTAs sharing a W tile run together
+  const int nk = (int)((p.k + OE_BK - 1) / OE_BK);
 
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(OE_TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(bar, 1);
-    *failed = 0;
+    for (int s = 0; s < C::NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    *consumed = 0;
     fence_mbar_init();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -126,57 +187,129 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  uint32_t phase = 0;
-  const int64_t nk = (K + OE_K - 1) / OE_K;
-  for (int64_t kb = 0; kb < nk; ++kb) {
-    oe_stage(sA, x, rows, K, m0, kb * OE_K, tid);
-    oe_stage(sB, w, out, K, n0, kb * OE_K, tid);
-    oe_stage(sAq, xq, rows, K, m0, kb * OE_K, tid);
-    oe_stage(sBq, wq, out, K, n0, kb * OE_K, tid);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> tensor core reads
-    __syncthreads();
-    if (tid == 0 && !*failed) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  // ERR: this thread's row of the y_ref tile (BN bf16 = BN/8 x 16 B) is fetched into registers
+  // now, so that the loads overlap the main loop instead of the epilogue
+  const int64_t my_row = (int64_t)m0 + 32 * warp + lane;
+  const int64_t my_row_off = ((int64_t)bz * p.rows + my_row) * p.out;
+  const bool full_row = my_row < p.rows && (int64_t)n0 + C::BN <= p.out && (p.out & 7) == 0;
+  uint4 ya[MODE == OE_ERR ? C::BN / 8 : 1];
+  if (MODE == OE_ERR && full_row) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.y_ref + my_row_off + n0);
 #pragma unroll
-      for (int kk = 0; kk < OE_K / 16; ++kk) {   // K = 16 per MMA: +32 bytes along the swizzled row
-        const bool acc = kb > 0 || kk > 0;
-        oe_mma(tmem, oe_desc(smem_addr(sA) + 32 * kk), oe_desc(smem_addr(sB) + 32 * kk), acc);
-        oe_mma(tmem + 128, oe_desc(smem_addr(sAq) + 32 * kk), oe_desc(smem_addr(sBq) + 32 * kk), acc);
-      }
-      oe_commit(bar);
-    }
-    // the stage is rewritten next iteration: wait for the MMAs that read it
-    if (!*failed && !mbar_wait_bounded(bar, phase)) *failed = 1;
-    phase ^= 1;
-    __syncthreads();
-    if (*failed) break;
+    for (int i = 0; i < C::BN / 8; ++i) ya[i] = __ldcs(src + i);
   }
-  if (*failed && tid == 0) {
-    // MMAs that may still be in flight read the stage and write TMEM: wait (bounded) before freeing
-    (void)mbar_wait_bounded(bar, phase ^ 1u, 1u << 22);
-  }
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
-  if (!*failed) {
-    // warp w reads TMEM lanes (= tile rows) 32w .. 32w + 31, 16 columns at a time
-    const int64_t row = m0 + 32 * warp + lane;
+  int produced = 0;
+  if (tid == 0) {
+    // ---- producer ----
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % C::NSTAGE, use = kb / C::NSTAGE;
+      if (use > 0 && !oe_wait(&empty[s], (uint32_t)((use - 1) & 1), abort_flag)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (*abort_flag) break;
+      uint8_t* st = smem + s * C::STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
+      oe_tma_3d(st, &ta, kb * OE_BK, m0, bz, &full[s]);
+      oe_tma_3d(st + C::A_BYTES, &tb, kb * OE_BK, n0, bz, &full[s]);
+      if (C::DUAL) {
+        oe_tma_3d(st + C::PAIR_BYTES, &taq, kb * OE_BK, m0, bz, &full[s]);
+        oe_tma_3d(st + C::PAIR_BYTES + C::A_BYTES, &tbq, kb * OE_BK, n0, bz, &full[s]);
+      }
+      produced = kb + 1;
+    }
+  } else if (tid == 32) {
+    // ---- MMA issuer ----
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % C::NSTAGE, use = kb / C::NSTAGE;
+      if (!oe_wait(&full[s], (uint32_t)(use & 1), abort_flag)) {
+        *abort_flag = 1;
+        break;
+      }
+      *consumed = kb + 1;
+      if (*abort_flag) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+#pragma unroll
+      for (int kk = 0; kk < OE_BK / 16; ++kk) {
+        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+        oe_mma(tmem, oe_desc(sa + 32 * kk), oe_desc(sa + C::A_BYTES + 32 * kk), C::IDESC, acc);
+        if (C::DUAL)
+          oe_mma(tmem + 128, oe_desc(sa + C::PAIR_BYTES + 32 * kk),
+                 oe_desc(sa + C::PAIR_BYTES + C::A_BYTES + 32 * kk), C::IDESC, acc);
+      }
+      oe_commit(&empty[s]);   // the stage is free once these MMAs have read it
+    }
+    oe_commit(acc_full);       // also the drain: arrives after every MMA issued above
+  }
+  __syncwarp();
+
+  // ---- epilogue: all four warps ----
+  if (!mbar_wait_bounded(acc_full, 0)) *abort_flag = 1;
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  __syncthreads();   // every thread sees the same abort flag
+  if (!*abort_flag) {
+    const int64_t row = (int64_t)m0 + 32 * warp + lane;
+    const bool row_ok = row < p.rows;
+    const int64_t row_off = ((int64_t)bz * p.rows + row) * p.out;
+    const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
     float es = 0.0f, rs = 0.0f;
     double esum = 0.0, rsum = 0.0;
-    for (int j = 0; j < OE_N / 16; ++j) {
-      float vr[16], vq[16];
-      const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16) + 16 * j;
-      oe_ld16(lane_base, vr);
-      oe_ld16(lane_base + 128, vq);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const float a = bf16_round(vr[e]), b = bf16_round(vq[e]);   // bf16 bmm outputs
-        const float d = bf16_round(__fsub_rn(a, b));                 // bf16 subtraction
-        es = __fadd_rn(es, __fmul_rn(d, d));
-        rs = __fadd_rn(rs, __fmul_rn(a, a));
-        const int64_t col = n0 + 16 * j + e;
-        if (row < rows && col < out) {
-          if (d_ref) d_ref[row * out + col] = vr[e];
-          if (d_q) d_q[row * out + col] = vq[e];
+    for (int j = 0; j < C::BN / 16; ++j) {
+      const int64_t col0 = (int64_t)n0 + 16 * j;
+      const bool vec = row_ok && col0 + 16 <= p.out && (p.out & 7) == 0;
+      float v[16];
+      oe_ld16(tbase + 16 * j, v);
+      if (MODE == OE_REF) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          v[e] = bf16_round(v[e]);
+          rs = __fadd_rn(rs, __fmul_rn(v[e], v[e]));
+        }
+        if (p.y_ref && row_ok) oe_store_yref(p.y_ref, row_off, col0, p.out, vec, v);
+      } else if (MODE == OE_ERR) {
+        float a[16];
+        if (full_row) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 u = ya[2 * j + (i >> 1)];
+            const uint32_t lo = (i & 1) ? u.z : u.x, hi = (i & 1) ? u.w : u.y;
+            a[4 * i] = __uint_as_float(lo << 16);
+            a[4 * i + 1] = __uint_as_float(lo & 0xFFFF0000u);
+            a[4 * i + 2] = __uint_as_float(hi << 16);
+            a[4 * i + 3] = __uint_as_float(hi & 0xFFFF0000u);
+          }
+        } else if (row_ok) {
+          oe_load_yref(p.y_ref, row_off, col0, p.out, vec, a);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) a[e] = 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float d = bf16_round(__fsub_rn(a[e], bf16_round(v[e])));   // bf16 y_ref - bf16 y_q
+          es = __fadd_rn(es, __fmul_rn(d, d));
+        }
+      } else {
+        float q[16];
+        oe_ld16(tbase + 128 + 16 * j, q);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float a = bf16_round(v[e]);
+          const float d = bf16_round(__fsub_rn(a, bf16_round(q[e])));
+          es = __fadd_rn(es, __fmul_rn(d, d));
+          rs = __fadd_rn(rs, __fmul_rn(a, a));
+        }
+        if (row_ok && (p.d_ref || p.d_q)) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (col0 + e < p.out) {
+              if (p.d_ref) p.d_ref[row_off + col0 + e] = v[e];
+              if (p.d_q) p.d_q[row_off + col0 + e] = q[e];
+            }
+          }
         }
       }
       if ((j & 3) == 3) {   // fp32 partials of <= 64 squares
@@ -188,11 +321,18 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
     esum = warp_sum_d(esum + (double)es);
     rsum = warp_sum_d(rsum + (double)rs);
     if (lane == 0) {
-      if (err_sum) atomicAdd(err_sum, esum);
-      if (ref_energy) atomicAdd(ref_energy, rsum);
+      if (MODE != OE_REF && p.err_sum) atomicAdd(p.err_sum + bz, esum);
+      if (MODE != OE_ERR && p.ref_sum) atomicAdd(p.ref_sum + bz, rsum);
     }
   }
+
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (tid == 0 && *abort_flag) {
+    // loads armed but never waited for by the MMA thread still write this CTA's shared memory
+    for (int j = *consumed; j < produced; ++j)
+      (void)mbar_wait_bounded(&full[j % C::NSTAGE], (uint32_t)((j / C::NSTAGE) & 1), 1u << 20);
+  }
   __syncthreads();
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -200,15 +340,71 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Host side: tensor maps and launches
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 oe_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// bf16 [batch, rows, k] (k % 8 == 0, 16-byte aligned base), box 64 (k) x box_rows x 1, SW128
+static bool oe_tmap(CUtensorMap* m, const uint16_t* base, int64_t batch, int64_t rows, int64_t k, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = oe_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)k, (cuuint64_t)rows, (cuuint64_t)batch};
+  const cuuint64_t strides[2] = {(cuuint64_t)k * 2, (cuuint64_t)rows * (cuuint64_t)k * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)OE_BK, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MODE>
+static cudaError_t oe_launch(const uint16_t* a, const uint16_t* b, const uint16_t* aq, const uint16_t* bq,
+                             int64_t batch, const OeArgs& args, cudaStream_t stream) {
+  using C = OeCfg<MODE>;
+  CUtensorMap ta, tb, taq, tbq;
+  if (!oe_tmap(&ta, a, batch, args.rows, args.k, OE_BM) || !oe_tmap(&tb, b, batch, args.out, args.k, C::BN))
+    return cudaErrorInvalidValue;
+  taq = ta;
+  tbq = tb;
+  if (C::DUAL && (!oe_tmap(&taq, aq, batch, args.rows, args.k, OE_BM) ||
+                  !oe_tmap(&tbq, bq, batch, args.out, args.k, C::BN)))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(outerr_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((args.rows + OE_BM - 1) / OE_BM), (unsigned)((args.out + C::BN - 1) / C::BN),
+                  (unsigned)batch);
+  outerr_kernel<MODE><<<grid, OE_THREADS, C::SMEM, stream>>>(ta, tb, taq, tbq, args);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_outerr(const uint16_t* x, const uint16_t* w, const uint16_t* xq, const uint16_t* wq, int64_t batch,
                           int64_t rows, int64_t out, int64_t K, double* err_sum, double* ref_energy, float* d_ref,
                           float* d_q, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(outerr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, OE_SMEM_BYTES);
-  if (e != cudaSuccess) return e;
-  const dim3 grid((unsigned)((out + OE_N - 1) / OE_N), (unsigned)((rows + OE_M - 1) / OE_M), (unsigned)batch);
-  outerr_kernel<<<grid, OE_THREADS, OE_SMEM_BYTES, stream>>>(x, w, xq, wq, rows, out, K, err_sum, ref_energy, d_ref,
-                                                              d_q);
-  return cudaGetLastError();
+  const OeArgs a{rows, out, K, err_sum, ref_energy, nullptr, d_ref, d_q};
+  return oe_launch<OE_DUAL>(x, w, xq, wq, batch, a, stream);
+}
+
+cudaError_t launch_outerr_ref(const uint16_t* x, const uint16_t* w, int64_t batch, int64_t rows, int64_t out,
+                              int64_t K, uint16_t* y_ref, double* ref_energy, cudaStream_t stream) {
+  const OeArgs a{rows, out, K, nullptr, ref_energy, y_ref, nullptr, nullptr};
+  return oe_launch<OE_REF>(x, w, nullptr, nullptr, batch, a, stream);
+}
+
+cudaError_t launch_outerr_err(const uint16_t* xq, const uint16_t* wq, const uint16_t* y_ref, int64_t batch,
+                              int64_t rows, int64_t out, int64_t K, double* err_sum, cudaStream_t stream) {
+  const OeArgs a{rows, out, K, err_sum, nullptr, const_cast<uint16_t*>(y_ref), nullptr, nullptr};
+  return oe_launch<OE_ERR>(xq, wq, nullptr, nullptr, batch, a, stream);
 }
 
 }  // namespace pq

@@ -12,7 +12,9 @@ definition) and a single device->host copy returns the whole table, where the
 reference runs a quantize + subtract + square + mean chain per (chunk,
 format) with a host sync each.  `output_mse` / `predicted_dloss` keep the
 reference's definitions: the reconstruction comes from the CUDA
-quantize-dequantize kernel, the GEMMs (`bmm`) stay library calls.
+quantize-dequantize kernel, and the two products with the error between them
+run on the tensor cores (`pq_output_ref` once per chunk, `pq_output_err` per
+format), so neither bf16 output of the format is written to memory.
 """
 from __future__ import annotations
 
@@ -280,11 +282,17 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
             rows = min(a.size(0) for a in acts)
             W = torch.stack([m.weight.detach().to(device=dev, dtype=dtype) for _, m in chunk])
             X = torch.stack([a[:rows].to(device=dev, dtype=dtype) for a in acts])
-            # tensor-core output error (pq_output_sse) for bf16 operands with k % 8 == 0; the two
-            # bmm's otherwise
+            # tensor cores with fused epilogues for bf16 operands with k % 8 == 0: y_ref (bf16) and
+            # its energy once per chunk (pq_output_ref), then one GEMM per format whose epilogue
+            # reduces the error against it (pq_output_err); the bmm's otherwise
             fused_out = dtype == torch.bfloat16 and X.shape[-1] % 8 == 0 and rows > 0 and W.shape[1] > 0
-            ref_energy = None
-            if not fused_out:
+            n_out = rows * W.shape[1]
+            if fused_out:
+                y_ref = torch.empty(W.shape[0], rows, W.shape[1], dtype=torch.bfloat16, device=dev)
+                ref = torch.zeros(W.shape[0], dtype=torch.float64, device=dev)
+                _lib.output_ref(X, W, ref, y_ref)
+                ref_energy = ref / n_out
+            else:
                 y_ref = torch.bmm(X, W.transpose(1, 2))
                 ref_energy = y_ref.float().pow(2).mean(dim=(1, 2))
             h_stacked = None
@@ -301,12 +309,8 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                     W_hat = spec.quantize_dequantize(W) if _per_linear else _batched_quantize(spec, W)
                     X_hat = spec.activation_quantize_dequantize(X.clone())
                     if fused_out:
-                        n_out = rows * W.shape[1]
                         err = torch.zeros(W.shape[0], dtype=torch.float64, device=dev)
-                        ref = torch.zeros_like(err) if ref_energy is None else None
-                        _lib.output_sse(X, W, X_hat, W_hat, err, ref)
-                        if ref is not None:
-                            ref_energy = ref / n_out
+                        _lib.output_err(X_hat, W_hat, y_ref, err)
                         out_mse = err / n_out
                     else:
                         y_q = torch.bmm(X_hat, W_hat.transpose(1, 2))

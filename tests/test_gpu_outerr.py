@@ -112,3 +112,54 @@ def test_validation():
     _lib.output_sse(e, torch.zeros(0, 5, 16, dtype=torch.bfloat16, device="cuda"), e,
                     torch.zeros(0, 5, 16, dtype=torch.bfloat16, device="cuda"), None, None)
     assert _lib.device_error() == 0
+
+
+def _ref_err(x, w, xq, wq):
+    from prismaquant_b200 import _lib
+    b, m, _ = x.shape
+    n = w.shape[1]
+    y = torch.empty(b, m, n, dtype=torch.bfloat16, device="cuda")
+    ref = torch.zeros(b, dtype=torch.float64, device="cuda")
+    err = torch.zeros_like(ref)
+    _lib.output_ref(x, w, ref, y)
+    _lib.output_err(xq, wq, y, err)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    return y, ref, err
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_ref_and_err_modes_match_dual(shape):
+    """The split kernels (y_ref stored once, one GEMM per format) against the one-pass dual kernel
+    and against an fp64 product of the same operands."""
+    x, w, xq, wq = _operands(*shape, seed=29)
+    y, ref, err = _ref_err(x, w, xq, wq)
+    derr, dref, yr, _ = _run(x, w, xq, wq)
+    want = torch.bmm(x.double(), w.double().transpose(1, 2))
+    bound = torch.bmm(x.double().abs(), w.double().abs().transpose(1, 2)) * ((x.shape[-1] / 16 + 4) * 2.0 ** -23)
+    # y_ref is bf16 of an fp32 accumulator within the bound: half a bf16 ulp more at most
+    assert ((y.double() - want).abs() <= bound + want.abs() * 2.0 ** -8 + 1e-30).all()
+    # the two kernels accumulate each output the same way; equal after rounding to bf16
+    assert torch.equal(y, yr.to(torch.bfloat16))
+    torch.testing.assert_close(ref, dref, rtol=4e-6, atol=0)
+    torch.testing.assert_close(err, derr, rtol=4e-6, atol=0)
+
+
+def test_err_mode_of_the_reference_operands_is_zero():
+    x, w, _, _ = _operands(3, 300, 520, 200, seed=41)
+    _, ref, err = _ref_err(x, w, x, w)
+    assert (err == 0).all() and (ref > 0).all()
+
+
+def test_ref_mode_without_output_and_validation():
+    from prismaquant_b200 import _lib
+    x, w, _, _ = _operands(2, 64, 96, 40, seed=43)
+    y, ref, _ = _ref_err(x, w, x, w)
+    ref2 = torch.zeros_like(ref)
+    _lib.output_ref(x, w, ref2, None)
+    torch.cuda.synchronize()
+    assert torch.equal(ref, ref2)
+    with pytest.raises(TypeError):
+        _lib.output_err(x, w, y.float(), ref2)
+    with pytest.raises(ValueError):
+        _lib.output_ref(x[:, :, :36], w[:, :, :36], ref2)    # k = 36 is not a multiple of 8
