@@ -39,7 +39,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama8b", choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b"])
+    ap.add_argument("--workload", default="llama8b",
+                    choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b", "outerr8b"])
     ap.add_argument("--fisher-seqs", type=int, default=64, help="calibration sequences (split across ranks)")
     ap.add_argument("--fisher-batch", type=int, default=4, help="sequences per backward on each rank")
     ap.add_argument("--no-e2e", action="store_true")
@@ -151,6 +152,141 @@ def run_fisher(a, rank, world, local):
                          "kernel_ms_per_step": round(kern_ms / a.steps, 4),
                          "hook_share_of_step": round(kern_ms / ms, 4)},
             "clocks": clk.summary(), "gpu_launches": len(kev)}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+OUTERR_GROUPS = [  # one Llama-8B decoder layer's Linears stacked by shape: (name, batch, out, in)
+    ("q_proj+o_proj", 2, 4096, 4096), ("k_proj+v_proj", 2, 1024, 4096),
+    ("gate_proj+up_proj", 2, 14336, 4096), ("down_proj", 1, 4096, 14336)]
+OUTERR_ROWS = 256          # cached activation rows per Linear (the probe's input_rows)
+OUTERR_FORMATS = ("NVFP4", "MXFP8", "FP8_E4M3")
+
+
+def run_outerr(a, rank, world, local):
+    """Output-error pass of the cost table (measure_quant_cost.py:599-605, 630-635) over one
+    Llama-8B decoder layer, its Linears stacked by shape as measure_batched_gpu stacks them, with
+    256 cached activation rows each (N(0,1) activations, N(0, 0.02^2) weights, rank-seeded).  One
+    step = per shape group y_ref and its energy once (pq_output_ref) and the output error of
+    NVFP4, MXFP8 and FP8-per-channel (pq_output_err on the formats' W_hat / X_hat, made before
+    the timed region).  The reference's torch chain on the same tensors (bmm y_ref once, then per
+    format bmm + (y_ref - y_q).float().pow(2).mean) is timed right after and reported beside it.
+    Replicas when world > 1 (each rank its own layer; max-rank time)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from prismaquant_b200 import _lib
+    from prismaquant_b200 import format_registry as fr
+    from prismaquant_b200 import measure_quant_cost as mqc
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    groups = []
+    flops = 0
+    hbm_bytes = 0
+    for name, b, out, k in OUTERR_GROUPS:
+        W = (torch.randn(b, out, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        X = torch.randn(b, OUTERR_ROWS, k, device=dev, generator=g).to(torch.bfloat16)
+        fmts = []
+        for f in OUTERR_FORMATS:
+            spec = fr.get_format(f)
+            fmts.append((f, mqc._batched_quantize(spec, W), spec.activation_quantize_dequantize(X.clone())))
+        y = torch.empty(b, OUTERR_ROWS, out, dtype=torch.bfloat16, device=dev)
+        groups.append((name, W, X, fmts, y))
+        flops += 2 * b * OUTERR_ROWS * out * k * (1 + len(fmts))
+        # algorithmic bytes: W, X, y_ref written once; per format W_hat, X_hat, y_ref read
+        hbm_bytes += (W.numel() + X.numel() + y.numel()) * 2 + len(fmts) * (W.numel() + X.numel() + y.numel()) * 2
+    sums = torch.zeros(len(groups), 1 + len(OUTERR_FORMATS), 8, dtype=torch.float64, device=dev)
+    launches = [0]
+
+    def ours():
+        for gi, (_, W, X, fmts, y) in enumerate(groups):
+            b = W.shape[0]
+            _lib.output_ref(X, W, sums[gi, 0, :b], y)
+            for fi, (_, Wh, Xh) in enumerate(fmts):
+                _lib.output_err(Xh, Wh, y, sums[gi, 1 + fi, :b])
+            launches[0] += 1 + len(fmts)
+
+    def torch_chain():
+        res = []
+        for _, W, X, fmts, _ in groups:
+            y_ref = torch.bmm(X, W.transpose(1, 2))
+            res.append(y_ref.float().pow(2).mean(dim=(1, 2)))
+            for _, Wh, Xh in fmts:
+                res.append((y_ref - torch.bmm(Xh, Wh.transpose(1, 2))).float().pow(2).mean(dim=(1, 2)))
+        return res
+
+    def timed(fn, steps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(a.warmup):
+        ours()
+    launches[0] = 0
+    with ClockSampler(local) as clk:
+        ms = timed(ours, a.steps)
+    n_launch = launches[0]
+    if _lib.device_error() != 0:
+        raise RuntimeError("output-error kernels reported a device error")
+    # parity with the torch chain on the same tensors (summation order and bf16 rounding of
+    # differently ordered fp32 sums differ: 2e-2 relative on the error, 1e-3 on the energy)
+    sums.zero_()
+    ours()
+    ref_res = torch_chain()
+    got = []
+    for gi, (_, W, _, fmts, _) in enumerate(groups):
+        b = W.shape[0]
+        n_out = OUTERR_ROWS * W.shape[1]
+        got += [sums[gi, j, :b] / n_out for j in range(1 + len(fmts))]
+    worst = max(float(((x - r.double()).abs() / r.double().abs().clamp_min(1e-30)).max()) for x, r in zip(got, ref_res))
+    for _ in range(a.warmup):
+        torch_chain()
+    ms_torch = timed(torch_chain, a.steps)
+    peak = None
+    peak_kind = "fallback"
+    try:
+        peak = float(json.loads(PEAKS.read_text())["bf16_tflops"])
+        peak_kind = "measured (burst)"
+    except Exception:
+        peak = 1590.0
+    hbm, _ = peaks()
+    tflops = flops * a.steps / (ms / 1e3) / 1e12 * world
+    per_gpu = flops / (ms / a.steps / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            "metric": "output-error TFLOP/s (y_ref once + 3 formats, fused error epilogue)",
+            "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
+            "data": "synthetic: N(0,1) activations, N(0,0.02^2) weights",
+            "config": {"workload": "llama8b_layer_output_error", "rows": OUTERR_ROWS,
+                       "groups": [f"{n} [{b},{o},{k}]" for n, b, o, k in OUTERR_GROUPS],
+                       "formats": list(OUTERR_FORMATS), "l2": "operands per step 1.8 GB > L2, no flush"},
+            "roofline": {"bound": "tensor", "achieved": round(per_gpu, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
+                         "hbm_achieved_gbs": round(hbm_bytes / (ms / a.steps / 1e3) / 1e9, 1), "hbm_peak_gbs": hbm,
+                         "hbm_bound_ms": round(hbm_bytes / hbm / 1e6, 4),
+                         "tensor_bound_ms": round(flops / peak / 1e9, 4),
+                         "kernel": "outerr_kernel (tcgen05 cta_group::2, TMA ring)"},
+            "torch_chain": {"ms_per_step": round(ms_torch / a.steps, 4),
+                            "speedup": round(ms_torch / ms, 3), "max_rel_diff": worst},
+            "clocks": clk.summary(), "gpu_launches": n_launch}), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -270,6 +406,13 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.workload == "fisher1b" and a.impl == "ours":
         return run_fisher(a, rank, world, local)
+    if a.workload == "outerr8b":
+        if a.impl == "ours":
+            return run_outerr(a, rank, world, local)
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the output-error workload's reference arm is the "
+                              "torch bmm chain, timed on the GPU beside ours (torch_chain in its line)"}), flush=True)
+        return
     shapes, wl_name = workload_shapes(a.workload)
     params = sum(int(__import__("math").prod(s)) for _, s in shapes)
     metric, unit = "weight GB/s scored across all formats", "GB/s"

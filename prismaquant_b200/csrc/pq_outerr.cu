@@ -32,20 +32,23 @@ enum { OE_REF = 0, OE_ERR = 1, OE_DUAL = 2 };
 constexpr int OE_BM = 128, OE_BK = 64, OE_THREADS = 128;
 constexpr uint32_t OE_TMEM_COLS = 256;
 
-template <int MODE>
+template <int MODE, bool PAIR>
 struct OeCfg {
   static constexpr bool DUAL = MODE == OE_DUAL;
-  static constexpr int BN = DUAL ? 128 : 256;               // columns per product
+  static_assert(!(DUAL && PAIR), "the dual-product mode runs on single CTAs");
+  static constexpr int BN = DUAL ? 128 : 256;               // output columns per product
+  static constexpr int MMA_M = PAIR ? 2 * OE_BM : OE_BM;    // rows of one MMA (a CTA pair: 256)
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;         // rows of the B tile this CTA holds
   static constexpr int A_BYTES = OE_BM * OE_BK * 2;         // 16 KB
-  static constexpr int B_BYTES = BN * OE_BK * 2;            // 16 / 32 KB
+  static constexpr int B_BYTES = B_ROWS * OE_BK * 2;        // 16 / 32 KB
   static constexpr int PAIR_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGE_BYTES = (DUAL ? 2 : 1) * PAIR_BYTES;   // 64 / 48 KB
-  static constexpr int NSTAGE = DUAL ? 3 : 4;
+  static constexpr int STAGE_BYTES = (DUAL ? 2 : 1) * PAIR_BYTES;   // 64 / 48 / 32 KB
+  static constexpr int NSTAGE = DUAL ? 3 : (PAIR ? 6 : 4);
   static constexpr int SMEM = 1024 + NSTAGE * STAGE_BYTES + 256;    // align slack, stages, barriers
   // kind::f16 instruction descriptor: D f32 (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12 = 1),
   // both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24.
   static constexpr uint32_t IDESC =
-      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(OE_BM >> 4) << 24);
+      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(MMA_M >> 4) << 24);
 };
 
 struct OeArgs {
@@ -79,6 +82,65 @@ __device__ __forceinline__ void oe_mma(uint32_t tmem_d, uint64_t adesc, uint64_t
 __device__ __forceinline__ void oe_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// ---- CTA-pair forms (cta_group::2: one MMA of M = 256 over two SMs; each CTA holds its 128 rows
+// of A, half of the B tile's rows, and its 128 rows of the accumulator in its own TMEM) ----
+__device__ __forceinline__ void oe_mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}\n"
+      :
+      : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+        "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+// arrives on the barrier at `bar`'s offset in both CTAs of the pair once the MMAs issued so far
+// have completed
+__device__ __forceinline__ void oe_commit_pair(uint64_t* bar, uint16_t pair_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(pair_mask)
+      : "memory");
+}
+
+__device__ __forceinline__ float4 oe_ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
+// tile load into this CTA's shared memory whose completion is counted on the barrier at cluster
+// address `bar_cluster` (the leader CTA's)
+__device__ __forceinline__ void oe_tma_3d_pair(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                               uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t oe_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the variable at `saddr` (a shared::cta address) in CTA `rank`
+__device__ __forceinline__ uint32_t oe_mapa(uint32_t saddr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+  return d;
+}
+
+__device__ __forceinline__ void oe_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void oe_tma_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
@@ -148,11 +210,31 @@ __device__ __forceinline__ bool oe_wait(uint64_t* bar, uint32_t parity, volatile
   return false;
 }
 
+// Epilogue arithmetic of one output value: `v` the fp32 accumulator, `a` the bf16 y_ref (ERR).
 template <int MODE>
+__device__ __forceinline__ float oe_value(float v, float a, float& es, float& rs) {
+  if (MODE == OE_REF) {
+    const float r = bf16_round(v);
+    rs = __fadd_rn(rs, __fmul_rn(r, r));
+    return r;
+  }
+  const float d = bf16_round(__fsub_rn(a, bf16_round(v)));   // bf16 y_ref - bf16 y_q
+  es = __fadd_rn(es, __fmul_rn(d, d));
+  return d;
+}
+
+// Grid: x = CTA (pairs of x for PAIR), y = output-column tile x S K-splits, z = batch entry.
+// Cluster (PAIR ? 2 : 1, S, 1): cluster rank = pair rank + 2 * split.  With S > 1 each split runs
+// its share of the K stages, stages its fp32 partial from TMEM in its own shared memory, and after
+// a cluster barrier split t sums column slice t of the tile over all S partials (distributed
+// shared memory, fixed order) and runs the epilogue on that slice.
+template <int MODE, bool PAIR, int S>
 __global__ void __launch_bounds__(OE_THREADS, 1)
     outerr_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                   const __grid_constant__ CUtensorMap taq, const __grid_constant__ CUtensorMap tbq, OeArgs p) {
-  using C = OeCfg<MODE>;
+  using C = OeCfg<MODE, PAIR>;
+  static_assert(S == 1 || (PAIR && (S == 2 || S == 4)), "K splits run on CTA pairs, 2 or 4 of them");
+  constexpr int SLICE = C::BN / S;               // epilogue columns per split
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // 1024-aligned atoms
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NSTAGE * C::STAGE_BYTES);
@@ -164,13 +246,30 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bz = blockIdx.z;
-  const int m0 = blockIdx.x * OE_BM, n0 = blockIdx.y * C::BN;   // M fastest: CTAs sharing a W tile run together
-  const int nk = (int)((p.k + OE_BK - 1) / OE_BK);
+  // PAIR: the two CTAs of a pair share one 256 x BN tile: pair rank r holds rows 128r.. of it and
+  // B rows BN/2 * r ..; the pair's leader (even cluster rank) issues the MMAs.  M is the fastest
+  // grid dimension, so the CTAs that read one W tile run together.
+  const uint32_t crank = (PAIR || S > 1) ? oe_cluster_rank() : 0u;
+  const uint32_t prank = PAIR ? (crank & 1u) : 0u;
+  const uint32_t leader = crank & ~1u;
+  const int split = (int)(blockIdx.y % S);
+  const int m0 = PAIR ? (int)(blockIdx.x >> 1) * (2 * OE_BM) + (int)prank * OE_BM : (int)blockIdx.x * OE_BM;
+  const int n0 = (int)(blockIdx.y / S) * C::BN;
+  const int nb0 = n0 + (int)prank * C::B_ROWS;
+  const int nk_all = (int)((p.k + OE_BK - 1) / OE_BK);
+  const int kb0 = split * nk_all / S;
+  const int nk = (split + 1) * nk_all / S - kb0;   // >= 1: the host keeps S <= nk_all
 
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(OE_TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(OE_TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(OE_TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   if (tid == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
@@ -183,48 +282,69 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
     fence_mbar_init();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
+  if (PAIR || S > 1)
+    oe_cluster_sync();   // every CTA's barriers exist before another signals them
+  else
+    __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  const uint32_t peer_abort = PAIR ? oe_mapa(smem_u32((const void*)abort_flag), crank ^ 1u) : 0u;
+  auto set_abort = [&]() {
+    *abort_flag = 1;
+    if (PAIR) asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1u) : "memory");
+  };
 
-  // ERR: this thread's row of the y_ref tile (BN bf16 = BN/8 x 16 B) is fetched into registers
-  // now, so that the loads overlap the main loop instead of the epilogue
+  // ERR: this thread's row of its epilogue columns of y_ref (SLICE bf16 = SLICE/8 x 16 B) is
+  // fetched into registers now, so that the loads overlap the main loop instead of the epilogue
   const int64_t my_row = (int64_t)m0 + 32 * warp + lane;
+  const bool row_ok = my_row < p.rows;
   const int64_t my_row_off = ((int64_t)bz * p.rows + my_row) * p.out;
-  const bool full_row = my_row < p.rows && (int64_t)n0 + C::BN <= p.out && (p.out & 7) == 0;
-  uint4 ya[MODE == OE_ERR ? C::BN / 8 : 1];
+  const int c0 = n0 + split * SLICE;               // first epilogue column
+  const bool full_row = row_ok && (int64_t)c0 + SLICE <= p.out && (p.out & 7) == 0;
+  uint4 ya[MODE == OE_ERR ? SLICE / 8 : 1];
   if (MODE == OE_ERR && full_row) {
-    const uint4* src = reinterpret_cast<const uint4*>(p.y_ref + my_row_off + n0);
+    const uint4* src = reinterpret_cast<const uint4*>(p.y_ref + my_row_off + c0);
 #pragma unroll
-    for (int i = 0; i < C::BN / 8; ++i) ya[i] = __ldcs(src + i);
+    for (int i = 0; i < SLICE / 8; ++i) ya[i] = __ldcs(src + i);
   }
 
   int produced = 0;
   if (tid == 0) {
-    // ---- producer ----
+    // ---- producer (each CTA loads its own operand rows) ----
+    const uint32_t leader_full0 = PAIR ? oe_mapa(smem_u32(&full[0]), leader) : 0u;
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % C::NSTAGE, use = kb / C::NSTAGE;
+      const int kc = (kb0 + kb) * OE_BK;
       if (use > 0 && !oe_wait(&empty[s], (uint32_t)((use - 1) & 1), abort_flag)) {
-        *abort_flag = 1;
+        set_abort();
         break;
       }
       if (*abort_flag) break;
       uint8_t* st = smem + s * C::STAGE_BYTES;
-      mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
-      oe_tma_3d(st, &ta, kb * OE_BK, m0, bz, &full[s]);
-      oe_tma_3d(st + C::A_BYTES, &tb, kb * OE_BK, n0, bz, &full[s]);
-      if (C::DUAL) {
-        oe_tma_3d(st + C::PAIR_BYTES, &taq, kb * OE_BK, m0, bz, &full[s]);
-        oe_tma_3d(st + C::PAIR_BYTES + C::A_BYTES, &tbq, kb * OE_BK, n0, bz, &full[s]);
+      if (PAIR) {
+        // the leader's full barrier counts the bytes of both CTAs' loads
+        if (prank == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * C::STAGE_BYTES));
+        const uint32_t fb = leader_full0 + 8u * (uint32_t)s;
+        oe_tma_3d_pair(st, &ta, kc, m0, bz, fb);
+        oe_tma_3d_pair(st + C::A_BYTES, &tb, kc, nb0, bz, fb);
+      } else {
+        mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
+        oe_tma_3d(st, &ta, kc, m0, bz, &full[s]);
+        oe_tma_3d(st + C::A_BYTES, &tb, kc, n0, bz, &full[s]);
+        if (C::DUAL) {
+          oe_tma_3d(st + C::PAIR_BYTES, &taq, kc, m0, bz, &full[s]);
+          oe_tma_3d(st + C::PAIR_BYTES + C::A_BYTES, &tbq, kc, n0, bz, &full[s]);
+        }
       }
       produced = kb + 1;
     }
-  } else if (tid == 32) {
-    // ---- MMA issuer ----
+  } else if (tid == 32 && prank == 0) {
+    // ---- MMA issuer (the pair leader's) ----
+    const uint16_t pair_mask = (uint16_t)(3u << leader);
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % C::NSTAGE, use = kb / C::NSTAGE;
       if (!oe_wait(&full[s], (uint32_t)(use & 1), abort_flag)) {
-        *abort_flag = 1;
+        set_abort();
         break;
       }
       *consumed = kb + 1;
@@ -234,28 +354,127 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
 #pragma unroll
       for (int kk = 0; kk < OE_BK / 16; ++kk) {
         const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-        oe_mma(tmem, oe_desc(sa + 32 * kk), oe_desc(sa + C::A_BYTES + 32 * kk), C::IDESC, acc);
-        if (C::DUAL)
-          oe_mma(tmem + 128, oe_desc(sa + C::PAIR_BYTES + 32 * kk),
-                 oe_desc(sa + C::PAIR_BYTES + C::A_BYTES + 32 * kk), C::IDESC, acc);
+        if (PAIR) {
+          oe_mma_pair(tmem, oe_desc(sa + 32 * kk), oe_desc(sa + C::A_BYTES + 32 * kk), C::IDESC, acc);
+        } else {
+          oe_mma(tmem, oe_desc(sa + 32 * kk), oe_desc(sa + C::A_BYTES + 32 * kk), C::IDESC, acc);
+          if (C::DUAL)
+            oe_mma(tmem + 128, oe_desc(sa + C::PAIR_BYTES + 32 * kk),
+                   oe_desc(sa + C::PAIR_BYTES + C::A_BYTES + 32 * kk), C::IDESC, acc);
+        }
       }
-      oe_commit(&empty[s]);   // the stage is free once these MMAs have read it
+      // the stage is free (in both CTAs of a pair) once these MMAs have read it
+      if (PAIR)
+        oe_commit_pair(&empty[s], pair_mask);
+      else
+        oe_commit(&empty[s]);
     }
-    oe_commit(acc_full);       // also the drain: arrives after every MMA issued above
+    // also the drain: arrives after every MMA issued above
+    if (PAIR)
+      oe_commit_pair(acc_full, pair_mask);
+    else
+      oe_commit(acc_full);
   }
   __syncwarp();
 
-  // ---- epilogue: all four warps ----
+  // ---- epilogue: all four warps of each CTA, on its own TMEM rows ----
   if (!mbar_wait_bounded(acc_full, 0)) *abort_flag = 1;
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   __syncthreads();   // every thread sees the same abort flag
-  if (!*abort_flag) {
-    const int64_t row = (int64_t)m0 + 32 * warp + lane;
-    const bool row_ok = row < p.rows;
-    const int64_t row_off = ((int64_t)bz * p.rows + row) * p.out;
-    const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
-    float es = 0.0f, rs = 0.0f;
-    double esum = 0.0, rsum = 0.0;
+  const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
+  const int trow = 32 * warp + lane;               // row within the CTA's 128
+  float es = 0.0f, rs = 0.0f;
+  double esum = 0.0, rsum = 0.0;
+  if (S > 1) {
+    // stage this split's fp32 partial (128 rows x BN) into the now idle stage ring: row r at
+    // r * 4 * BN bytes, 16-byte chunk c at chunk c ^ (r % 8) (conflict-free for thread = row)
+    static_assert(OE_BM * C::BN * 4 <= C::NSTAGE * C::STAGE_BYTES, "partial tile fits the stage ring");
+    if (!*abort_flag) {
+      float* prow = reinterpret_cast<float*>(smem + (size_t)trow * 4 * C::BN);
+#pragma unroll 1
+      for (int j = 0; j < C::BN / 16; ++j) {
+        float v[16];
+        oe_ld16(tbase + 16 * j, v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = 4 * j + q;
+          *reinterpret_cast<float4*>(prow + 4 * (c ^ (trow & 7))) =
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+      }
+    }
+    // every TMEM read of this CTA is done and every partial staged before any partner reads
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    oe_cluster_sync();
+    int any_abort = *abort_flag;
+    if (!any_abort) {
+      uint32_t part[S];
+#pragma unroll
+      for (int t = 0; t < S; ++t) part[t] = oe_mapa(smem_u32(smem + (size_t)trow * 4 * C::BN), prank + 2u * t);
+      constexpr int NCH = SLICE / 4;               // 4-column chunks of this split's slice
+      constexpr int CB = 4;                        // chunks whose S partials are loaded at once
+      static_assert(NCH % CB == 0, "slice is a whole number of load batches");
+#pragma unroll
+      for (int cb = 0; cb < NCH; cb += CB) {
+        float4 pv[CB][S];
+#pragma unroll
+        for (int q = 0; q < CB; ++q) {
+          const uint32_t off = 16u * (uint32_t)((split * NCH + cb + q) ^ (trow & 7));
+#pragma unroll
+          for (int t = 0; t < S; ++t) pv[q][t] = oe_ld_dsmem_f4(part[t] + off);
+        }
+#pragma unroll
+        for (int q = 0; q < CB; ++q) {
+        const int cl = cb + q;
+        float4 acc = pv[q][0];
+#pragma unroll
+        for (int t = 1; t < S; ++t) {   // fixed order: split 0, 1, ..
+          acc.x = __fadd_rn(acc.x, pv[q][t].x);
+          acc.y = __fadd_rn(acc.y, pv[q][t].y);
+          acc.z = __fadd_rn(acc.z, pv[q][t].z);
+          acc.w = __fadd_rn(acc.w, pv[q][t].w);
+        }
+        const float v4[4] = {acc.x, acc.y, acc.z, acc.w};
+        const int64_t col0 = (int64_t)c0 + 4 * cl;
+        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (MODE == OE_ERR) {
+          if (full_row) {
+            const uint4 u = ya[cl >> 1];
+            const uint32_t lo = (cl & 1) ? u.z : u.x, hi = (cl & 1) ? u.w : u.y;
+            a4[0] = __uint_as_float(lo << 16);
+            a4[1] = __uint_as_float(lo & 0xFFFF0000u);
+            a4[2] = __uint_as_float(hi << 16);
+            a4[3] = __uint_as_float(hi & 0xFFFF0000u);
+          } else if (row_ok) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              a4[e] = col0 + e < p.out ? __uint_as_float((uint32_t)p.y_ref[my_row_off + col0 + e] << 16) : 0.0f;
+          }
+        }
+        float r4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) r4[e] = oe_value<MODE>(v4[e], a4[e], es, rs);
+        if (MODE == OE_REF && p.y_ref && row_ok) {
+          if (full_row) {
+            const uint32_t lo = (__float_as_uint(r4[0]) >> 16) | (__float_as_uint(r4[1]) & 0xFFFF0000u);
+            const uint32_t hi = (__float_as_uint(r4[2]) >> 16) | (__float_as_uint(r4[3]) & 0xFFFF0000u);
+            *reinterpret_cast<uint2*>(p.y_ref + my_row_off + col0) = make_uint2(lo, hi);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (col0 + e < p.out) p.y_ref[my_row_off + col0 + e] = (uint16_t)(__float_as_uint(r4[e]) >> 16);
+          }
+        }
+        if ((cl & 15) == 15) {   // fp32 partials of <= 64 squares
+          esum += (double)es;
+          rsum += (double)rs;
+          es = rs = 0.0f;
+        }
+        }
+      }
+    }
+  } else if (!*abort_flag) {
+    const int64_t row_off = my_row_off;
 #pragma unroll
     for (int j = 0; j < C::BN / 16; ++j) {
       const int64_t col0 = (int64_t)n0 + 16 * j;
@@ -264,10 +483,7 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
       oe_ld16(tbase + 16 * j, v);
       if (MODE == OE_REF) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          v[e] = bf16_round(v[e]);
-          rs = __fadd_rn(rs, __fmul_rn(v[e], v[e]));
-        }
+        for (int e = 0; e < 16; ++e) v[e] = oe_value<OE_REF>(v[e], 0.0f, es, rs);
         if (p.y_ref && row_ok) oe_store_yref(p.y_ref, row_off, col0, p.out, vec, v);
       } else if (MODE == OE_ERR) {
         float a[16];
@@ -288,10 +504,7 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
           for (int e = 0; e < 16; ++e) a[e] = 0.0f;
         }
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float d = bf16_round(__fsub_rn(a[e], bf16_round(v[e])));   // bf16 y_ref - bf16 y_q
-          es = __fadd_rn(es, __fmul_rn(d, d));
-        }
+        for (int e = 0; e < 16; ++e) (void)oe_value<OE_ERR>(v[e], a[e], es, rs);
       } else {
         float q[16];
         oe_ld16(tbase + 128 + 16 * j, q);
@@ -318,6 +531,8 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
         es = rs = 0.0f;
       }
     }
+  }
+  if (!*abort_flag) {
     esum = warp_sum_d(esum + (double)es);
     rsum = warp_sum_d(rsum + (double)rs);
     if (lane == 0) {
@@ -328,15 +543,22 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (tid == 0 && *abort_flag) {
-    // loads armed but never waited for by the MMA thread still write this CTA's shared memory
+  if (tid == 0 && prank == 0 && *abort_flag) {
+    // loads armed but never waited for by the MMA thread still write shared memory (in a pair,
+    // the leader's full barrier also counts the other CTA's loads of the same stage)
     for (int j = *consumed; j < produced; ++j)
       (void)mbar_wait_bounded(&full[j % C::NSTAGE], (uint32_t)((j / C::NSTAGE) & 1), 1u << 20);
   }
-  __syncthreads();
+  if (PAIR || S > 1)
+    oe_cluster_sync();   // no CTA frees the pair's TMEM or exits while a partner still reads it
+  else
+    __syncthreads();
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(OE_TMEM_COLS));
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(OE_TMEM_COLS));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(OE_TMEM_COLS));
   }
 }
 
@@ -368,43 +590,115 @@ static bool oe_tmap(CUtensorMap* m, const uint16_t* base, int64_t batch, int64_t
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+template <int MODE, bool PAIR, int S>
+static cudaError_t oe_launch_s(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& taq,
+                               const CUtensorMap& tbq, int64_t batch, int64_t mtiles, const OeArgs& args,
+                               cudaStream_t stream) {
+  using C = OeCfg<MODE, PAIR>;
+  cudaError_t e =
+      cudaFuncSetAttribute(outerr_kernel<MODE, PAIR, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)mtiles, (unsigned)(((args.out + C::BN - 1) / C::BN) * S), (unsigned)batch);
+  cfg.blockDim = dim3(OE_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[0].val.clusterDim.y = S;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, outerr_kernel<MODE, PAIR, S>, ta, tb, taq, tbq, args);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+// Clusters of outerr_kernel<MODE, true, S> (2 x S CTAs) the device holds at once (cached).
+template <int MODE, int S>
+static int oe_max_clusters() {
+  static int cached = -1;
+  if (cached < 0) {
+    using C = OeCfg<MODE, true>;
+    int n = 0;
+    if (cudaFuncSetAttribute(outerr_kernel<MODE, true, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) ==
+        cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, S, 1);
+      cfg.blockDim = dim3(OE_THREADS, 1, 1);
+      cfg.dynamicSmemBytes = C::SMEM;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = S;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, outerr_kernel<MODE, true, S>, &cfg) != cudaSuccess) n = 0;
+    }
+    (void)cudaGetLastError();
+    cached = n;
+  }
+  return cached;
+}
+
+// K splits for a launch of `units` CTA pairs (one cluster each) over nk 64-wide K stages: the
+// largest of 4, 2 that still fits every cluster on the device at once and gives every SM at most
+// about one CTA, with at least two stages per split; 1 when the tiles alone fill the device.
 template <int MODE>
+static int oe_splits(int64_t units, int64_t nk) {
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t room = sms + sms / 8;
+  if (nk >= 8 && 8 * units <= room && units <= oe_max_clusters<MODE, 4>()) return 4;
+  if (nk >= 4 && 4 * units <= room && units <= oe_max_clusters<MODE, 2>()) return 2;
+  return 1;
+}
+
+template <int MODE, bool PAIR>
 static cudaError_t oe_launch(const uint16_t* a, const uint16_t* b, const uint16_t* aq, const uint16_t* bq,
                              int64_t batch, const OeArgs& args, cudaStream_t stream) {
-  using C = OeCfg<MODE>;
+  using C = OeCfg<MODE, PAIR>;
   CUtensorMap ta, tb, taq, tbq;
-  if (!oe_tmap(&ta, a, batch, args.rows, args.k, OE_BM) || !oe_tmap(&tb, b, batch, args.out, args.k, C::BN))
+  if (!oe_tmap(&ta, a, batch, args.rows, args.k, OE_BM) || !oe_tmap(&tb, b, batch, args.out, args.k, C::B_ROWS))
     return cudaErrorInvalidValue;
   taq = ta;
   tbq = tb;
   if (C::DUAL && (!oe_tmap(&taq, aq, batch, args.rows, args.k, OE_BM) ||
-                  !oe_tmap(&tbq, bq, batch, args.out, args.k, C::BN)))
+                  !oe_tmap(&tbq, bq, batch, args.out, args.k, C::B_ROWS)))
     return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(outerr_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  if (e != cudaSuccess) return e;
-  const dim3 grid((unsigned)((args.rows + OE_BM - 1) / OE_BM), (unsigned)((args.out + C::BN - 1) / C::BN),
-                  (unsigned)batch);
-  outerr_kernel<MODE><<<grid, OE_THREADS, C::SMEM, stream>>>(ta, tb, taq, tbq, args);
-  return cudaGetLastError();
+  const int64_t mtiles = PAIR ? 2 * ((args.rows + 2 * OE_BM - 1) / (2 * OE_BM)) : (args.rows + OE_BM - 1) / OE_BM;
+  if constexpr (!PAIR) {
+    return oe_launch_s<MODE, false, 1>(ta, tb, taq, tbq, batch, mtiles, args, stream);
+  } else {
+    const int64_t units = (mtiles / 2) * ((args.out + C::BN - 1) / C::BN) * batch;
+    switch (oe_splits<MODE>(units, (args.k + OE_BK - 1) / OE_BK)) {
+      case 4: return oe_launch_s<MODE, true, 4>(ta, tb, taq, tbq, batch, mtiles, args, stream);
+      case 2: return oe_launch_s<MODE, true, 2>(ta, tb, taq, tbq, batch, mtiles, args, stream);
+      default: return oe_launch_s<MODE, true, 1>(ta, tb, taq, tbq, batch, mtiles, args, stream);
+    }
+  }
 }
 
 cudaError_t launch_outerr(const uint16_t* x, const uint16_t* w, const uint16_t* xq, const uint16_t* wq, int64_t batch,
                           int64_t rows, int64_t out, int64_t K, double* err_sum, double* ref_energy, float* d_ref,
                           float* d_q, cudaStream_t stream) {
   const OeArgs a{rows, out, K, err_sum, ref_energy, nullptr, d_ref, d_q};
-  return oe_launch<OE_DUAL>(x, w, xq, wq, batch, a, stream);
+  return oe_launch<OE_DUAL, false>(x, w, xq, wq, batch, a, stream);
 }
 
 cudaError_t launch_outerr_ref(const uint16_t* x, const uint16_t* w, int64_t batch, int64_t rows, int64_t out,
                               int64_t K, uint16_t* y_ref, double* ref_energy, cudaStream_t stream) {
   const OeArgs a{rows, out, K, nullptr, ref_energy, y_ref, nullptr, nullptr};
-  return oe_launch<OE_REF>(x, w, nullptr, nullptr, batch, a, stream);
+  return oe_launch<OE_REF, true>(x, w, nullptr, nullptr, batch, a, stream);
 }
 
 cudaError_t launch_outerr_err(const uint16_t* xq, const uint16_t* wq, const uint16_t* y_ref, int64_t batch,
                               int64_t rows, int64_t out, int64_t K, double* err_sum, cudaStream_t stream) {
   const OeArgs a{rows, out, K, err_sum, nullptr, const_cast<uint16_t*>(y_ref), nullptr, nullptr};
-  return oe_launch<OE_ERR>(xq, wq, nullptr, nullptr, batch, a, stream);
+  return oe_launch<OE_ERR, true>(xq, wq, nullptr, nullptr, batch, a, stream);
 }
 
 }  // namespace pq
