@@ -43,6 +43,8 @@ def parse():
                     choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b", "outerr8b"])
     ap.add_argument("--fisher-seqs", type=int, default=64, help="calibration sequences (split across ranks)")
     ap.add_argument("--fisher-batch", type=int, default=4, help="sequences per backward on each rank")
+    ap.add_argument("--outerr-layers", type=int, default=32,
+                    help="decoder layers whose Linears the output-error workload stacks by shape")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -157,7 +159,7 @@ def run_fisher(a, rank, world, local):
         dist.destroy_process_group()
 
 
-OUTERR_GROUPS = [  # one Llama-8B decoder layer's Linears stacked by shape: (name, batch, out, in)
+OUTERR_GROUPS = [  # a Llama-8B decoder layer's Linears by shape: (name, per layer, out, in)
     ("q_proj+o_proj", 2, 4096, 4096), ("k_proj+v_proj", 2, 1024, 4096),
     ("gate_proj+up_proj", 2, 14336, 4096), ("down_proj", 1, 4096, 14336)]
 OUTERR_ROWS = 256          # cached activation rows per Linear (the probe's input_rows)
@@ -165,10 +167,12 @@ OUTERR_FORMATS = ("NVFP4", "MXFP8", "FP8_E4M3")
 
 
 def run_outerr(a, rank, world, local):
-    """Output-error pass of the cost table (measure_quant_cost.py:599-605, 630-635) over one
-    Llama-8B decoder layer, its Linears stacked by shape as measure_batched_gpu stacks them, with
-    256 cached activation rows each (N(0,1) activations, N(0, 0.02^2) weights, rank-seeded).  One
-    step = per shape group y_ref and its energy once (pq_output_ref) and the output error of
+    """Output-error pass of the cost table (measure_quant_cost.py:599-605, 630-635) over the
+    Linears of --outerr-layers Llama-8B decoder layers (default 32: the whole model but lm_head),
+    stacked by shape as measure_batched_gpu stacks them (its chunk_size of 256 holds each group
+    whole), with 256 cached activation rows each (N(0,1) activations, N(0, 0.02^2) weights,
+    rank-seeded).  One step = per shape group y_ref and its energy once (pq_output_ref) and the
+    output error of
     NVFP4, MXFP8 and FP8-per-channel (pq_output_err on the formats' W_hat / X_hat, made before
     the timed region).  The reference's torch chain on the same tensors (bmm y_ref once, then per
     format bmm + (y_ref - y_q).float().pow(2).mean) is timed right after and reported beside it.
@@ -189,8 +193,11 @@ def run_outerr(a, rank, world, local):
     groups = []
     flops = 0
     hbm_bytes = 0
-    for name, b, out, k in OUTERR_GROUPS:
-        W = (torch.randn(b, out, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    for name, per_layer, out, k in OUTERR_GROUPS:
+        b = per_layer * a.outerr_layers
+        W = torch.empty(b, out, k, dtype=torch.bfloat16, device=dev)
+        for i in range(b):   # one Linear at a time keeps the fp32 temporary small
+            W[i] = (torch.randn(out, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         X = torch.randn(b, OUTERR_ROWS, k, device=dev, generator=g).to(torch.bfloat16)
         fmts = []
         for f in OUTERR_FORMATS:
@@ -201,7 +208,8 @@ def run_outerr(a, rank, world, local):
         flops += 2 * b * OUTERR_ROWS * out * k * (1 + len(fmts))
         # algorithmic bytes: W, X, y_ref written once; per format W_hat, X_hat, y_ref read
         hbm_bytes += (W.numel() + X.numel() + y.numel()) * 2 + len(fmts) * (W.numel() + X.numel() + y.numel()) * 2
-    sums = torch.zeros(len(groups), 1 + len(OUTERR_FORMATS), 8, dtype=torch.float64, device=dev)
+    sums = torch.zeros(len(groups), 1 + len(OUTERR_FORMATS), max(gr[1].shape[0] for gr in groups),
+                       dtype=torch.float64, device=dev)
     launches = [0]
 
     def ours():
@@ -275,9 +283,10 @@ def run_outerr(a, rank, world, local):
             "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
             "data": "synthetic: N(0,1) activations, N(0,0.02^2) weights",
-            "config": {"workload": "llama8b_layer_output_error", "rows": OUTERR_ROWS,
-                       "groups": [f"{n} [{b},{o},{k}]" for n, b, o, k in OUTERR_GROUPS],
-                       "formats": list(OUTERR_FORMATS), "l2": "operands per step 1.8 GB > L2, no flush"},
+            "config": {"workload": f"llama8b_output_error_{a.outerr_layers}_layers", "rows": OUTERR_ROWS,
+                       "groups": [f"{n} [{b * a.outerr_layers},{o},{k}]" for n, b, o, k in OUTERR_GROUPS],
+                       "formats": list(OUTERR_FORMATS),
+                       "l2": f"operands per step {hbm_bytes / 1e9:.1f} GB > L2, no flush"},
             "roofline": {"bound": "tensor", "achieved": round(per_gpu, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
                          "hbm_achieved_gbs": round(hbm_bytes / (ms / a.steps / 1e3) / 1e9, 1), "hbm_peak_gbs": hbm,
