@@ -51,6 +51,16 @@ struct OeCfg {
       (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(MMA_M >> 4) << 24);
 };
 
+// Stage ring of one launch: CTA pairs without K splits keep 3 stages (98 KB), so two CTAs share
+// an SM and one's prologue and epilogue overlap the other's main loop; K-split launches keep 6
+// (their fp32 partial tile, 128 KB, is staged in the ring) and so run one CTA per SM.
+template <int MODE, bool PAIR, int S>
+struct OeRing {
+  using C = OeCfg<MODE, PAIR>;
+  static constexpr int NSTAGE = (PAIR && S == 1) ? 3 : C::NSTAGE;
+  static constexpr int SMEM = 1024 + NSTAGE * C::STAGE_BYTES + 256;
+};
+
 struct OeArgs {
   int64_t rows, out, k;
   double* err_sum;      // [batch] (ERR, DUAL)
@@ -233,13 +243,14 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
     outerr_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                   const __grid_constant__ CUtensorMap taq, const __grid_constant__ CUtensorMap tbq, OeArgs p) {
   using C = OeCfg<MODE, PAIR>;
+  constexpr int NSTAGE = OeRing<MODE, PAIR, S>::NSTAGE;
   static_assert(S == 1 || (PAIR && (S == 2 || S == 4)), "K splits run on CTA pairs, 2 or 4 of them");
   constexpr int SLICE = C::BN / S;               // epilogue columns per split
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // 1024-aligned atoms
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NSTAGE * C::STAGE_BYTES);
-  uint64_t* empty = full + C::NSTAGE;
-  uint64_t* acc_full = empty + C::NSTAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * C::STAGE_BYTES);
+  uint64_t* empty = full + NSTAGE;
+  uint64_t* acc_full = empty + NSTAGE;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* consumed = abort_flag + 1;   // stages the MMA thread has waited for
@@ -272,7 +283,7 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
     }
   }
   if (tid == 0) {
-    for (int s = 0; s < C::NSTAGE; ++s) {
+    for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -313,7 +324,7 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
     // ---- producer (each CTA loads its own operand rows) ----
     const uint32_t leader_full0 = PAIR ? oe_mapa(smem_u32(&full[0]), leader) : 0u;
     for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % C::NSTAGE, use = kb / C::NSTAGE;
+      const int s = kb % NSTAGE, use = kb / NSTAGE;
       const int kc = (kb0 + kb) * OE_BK;
       if (use > 0 && !oe_wait(&empty[s], (uint32_t)((use - 1) & 1), abort_flag)) {
         set_abort();
@@ -342,7 +353,7 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
     // ---- MMA issuer (the pair leader's) ----
     const uint16_t pair_mask = (uint16_t)(3u << leader);
     for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % C::NSTAGE, use = kb / C::NSTAGE;
+      const int s = kb % NSTAGE, use = kb / NSTAGE;
       if (!oe_wait(&full[s], (uint32_t)(use & 1), abort_flag)) {
         set_abort();
         break;
@@ -388,7 +399,7 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
   if (S > 1) {
     // stage this split's fp32 partial (128 rows x BN) into the now idle stage ring: row r at
     // r * 4 * BN bytes, 16-byte chunk c at chunk c ^ (r % 8) (conflict-free for thread = row)
-    static_assert(OE_BM * C::BN * 4 <= C::NSTAGE * C::STAGE_BYTES, "partial tile fits the stage ring");
+    static_assert(S == 1 || OE_BM * C::BN * 4 <= NSTAGE * C::STAGE_BYTES, "partial tile fits the stage ring");
     if (!*abort_flag) {
       float* prow = reinterpret_cast<float*>(smem + (size_t)trow * 4 * C::BN);
 #pragma unroll 1
@@ -547,7 +558,7 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
     // loads armed but never waited for by the MMA thread still write shared memory (in a pair,
     // the leader's full barrier also counts the other CTA's loads of the same stage)
     for (int j = *consumed; j < produced; ++j)
-      (void)mbar_wait_bounded(&full[j % C::NSTAGE], (uint32_t)((j / C::NSTAGE) & 1), 1u << 20);
+      (void)mbar_wait_bounded(&full[j % NSTAGE], (uint32_t)((j / NSTAGE) & 1), 1u << 20);
   }
   if (PAIR || S > 1)
     oe_cluster_sync();   // no CTA frees the pair's TMEM or exits while a partner still reads it
@@ -596,12 +607,13 @@ static cudaError_t oe_launch_s(const CUtensorMap& ta, const CUtensorMap& tb, con
                                cudaStream_t stream) {
   using C = OeCfg<MODE, PAIR>;
   cudaError_t e =
-      cudaFuncSetAttribute(outerr_kernel<MODE, PAIR, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+      cudaFuncSetAttribute(outerr_kernel<MODE, PAIR, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           OeRing<MODE, PAIR, S>::SMEM);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)mtiles, (unsigned)(((args.out + C::BN - 1) / C::BN) * S), (unsigned)batch);
   cfg.blockDim = dim3(OE_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.dynamicSmemBytes = OeRing<MODE, PAIR, S>::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -622,12 +634,13 @@ static int oe_max_clusters() {
   if (cached < 0) {
     using C = OeCfg<MODE, true>;
     int n = 0;
-    if (cudaFuncSetAttribute(outerr_kernel<MODE, true, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) ==
+    if (cudaFuncSetAttribute(outerr_kernel<MODE, true, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             OeRing<MODE, true, S>::SMEM) ==
         cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2, S, 1);
       cfg.blockDim = dim3(OE_THREADS, 1, 1);
-      cfg.dynamicSmemBytes = C::SMEM;
+      cfg.dynamicSmemBytes = OeRing<MODE, true, S>::SMEM;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 2;
