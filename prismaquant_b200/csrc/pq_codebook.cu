@@ -199,6 +199,173 @@ __global__ void __launch_bounds__(256) xfmt_kernel(const uint16_t* __restrict__ 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Coalesced kernel for rows of a multiple of 8 elements (16-byte aligned): each lane takes 8
+// consecutive elements with one 16-byte load; the lanes of a 16/32/128-group reduce its maximum
+// with shuffles (row-wise formats: the warp, over the row).  The rounding is closed-form:
+// the codebook RTN above (bucketize, then the strictly closer neighbour) is the nearest codebook
+// value with ties to the lower signed value, saturated at the largest magnitude, because the
+// reference's two float32 differences are exact wherever they can decide (adjacent entries are
+// within a factor of two, Sterbenz), so grid_round_abs gives the same point.  The FP6 / FP3
+// codebooks have no subnormals: below their smallest normal 2^EMIN they hold only 0, with the
+// tie at 2^(EMIN-1).  MX scales are powers of two, so w / scale is the exact product
+// w * 2^-e.
+// ---------------------------------------------------------------------------
+enum XKind { XK_E2M1 = 0, XK_E3M2, XK_E2M3, XK_E2M0, XK_E4M3, XK_E5M2, XK_INT };
+
+template <int KIND> struct XK;
+template <> struct XK<XK_E2M1> { static constexpr int M = 1, EMIN = 0; static constexpr bool SUB = true; static constexpr float MAXV = 6.0f; };
+template <> struct XK<XK_E3M2> { static constexpr int M = 2, EMIN = -3; static constexpr bool SUB = false; static constexpr float MAXV = 28.0f; };
+template <> struct XK<XK_E2M3> { static constexpr int M = 3, EMIN = -1; static constexpr bool SUB = false; static constexpr float MAXV = 7.5f; };
+template <> struct XK<XK_E2M0> { static constexpr int M = 0, EMIN = -2; static constexpr bool SUB = false; static constexpr float MAXV = 2.0f; };
+template <> struct XK<XK_E4M3> { static constexpr int M = 3, EMIN = -6; static constexpr bool SUB = true; static constexpr float MAXV = 448.0f; };
+template <> struct XK<XK_E5M2> { static constexpr int M = 2, EMIN = -14; static constexpr bool SUB = true; static constexpr float MAXV = 114688.0f; };
+
+__host__ __device__ inline int xkind_of(const XFmt& f) {
+  if (f.is_int) return XK_INT;
+  switch (f.cb) {
+    case CB_E2M1: return XK_E2M1;
+    case CB_E3M2: return XK_E3M2;
+    case CB_E2M3: return XK_E2M3;
+    case CB_E2M0: return XK_E2M0;
+    case CB_E4M3: return XK_E4M3;
+    default: return XK_E5M2;
+  }
+}
+
+// Cost-path RTN of x on the format's grid (codebook: ties to the lower value, +0.0 for a
+// negative x that rounds to zero; integer: round half even, then clamp).
+template <int KIND>
+__device__ __forceinline__ float xk_round(float x, int bits) {
+  if constexpr (KIND == XK_INT) {
+    const float lv = (float)((1 << (bits - 1)) - 1);
+    return fminf(fmaxf(rintf(x), -lv - 1.0f), lv);
+  } else {
+    using K = XK<KIND>;
+    const float a = fabsf(x);
+    const bool neg = x < 0.0f;
+    float r = grid_round_abs<K::M, K::EMIN>(a, neg, K::MAXV);
+    if constexpr (!K::SUB) {
+      const float lo = K::EMIN >= 0 ? (float)(1 << K::EMIN) : 1.0f / (float)(1 << -K::EMIN);
+      const float half = 0.5f * lo;
+      const float rs = (a > half || (a == half && neg)) ? lo : 0.0f;
+      r = a < lo ? rs : r;
+    }
+    return neg ? __fsub_rn(0.0f, r) : r;
+  }
+}
+
+template <int MODE, int KIND>
+__global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__ w, int64_t rows, int64_t cols,
+                                                    int fmt, double* sse, uint16_t* out,
+                                                    const float* __restrict__ h, int h_mode) {
+  const XFmt f = xfmt_of(fmt);
+  const float cmax = KIND == XK_INT ? 0.0f : XK<(KIND == XK_INT ? XK_E2M1 : KIND)>::MAXV;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const bool grouped = f.group > 0 && f.group < cols;
+  double acc = 0.0;
+
+  // scale of a group with maximum a, and the factor x = w * inv or w / scale
+  auto scale_of = [&](float a, float& inv) {
+    const float s = xfmt_scale(f, cmax, a);
+    inv = (!f.is_int && f.mx) ? __frcp_rn(s) : 0.0f;   // exact: s is a power of two
+    return s;
+  };
+  // 8 elements at flat index idx (row r): reconstruction, error, optional W_hat store
+  auto do8 = [&](const float (&wv)[8], int64_t idx, int64_t r, float scale, float inv) {
+    float hv[8];
+    if (h_mode == 1) {
+      const float4 h0 = __ldg(reinterpret_cast<const float4*>(h + idx));
+      const float4 h1 = __ldg(reinterpret_cast<const float4*>(h + idx + 4));
+      hv[0] = h0.x; hv[1] = h0.y; hv[2] = h0.z; hv[3] = h0.w;
+      hv[4] = h1.x; hv[5] = h1.y; hv[6] = h1.z; hv[7] = h1.w;
+    } else {
+      const float hr = h_mode == 2 ? __ldg(h + r) : 1.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hv[i] = hr;
+    }
+    float part = 0.0f;
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = inv != 0.0f ? __fmul_rn(wv[i], inv) : __fdiv_rn(wv[i], scale);
+      const float q = xk_round<KIND>(x, f.bits);
+      const float rec = bf16_round(__fmul_rn(q, scale));
+      const float e = bf16_round(__fsub_rn(wv[i], rec));
+      const float e2 = __fmul_rn(e, e);   // the reference squares in fp32, then weights
+      part = h_mode == 0 ? __fadd_rn(part, e2) : fmaf(hv[i], e2, part);
+      if (MODE == MODE_QDQ) {
+        const uint32_t b = __float_as_uint(rec) >> 16;
+        o[i >> 1] = (i & 1) ? (o[i >> 1] | (b << 16)) : b;
+      }
+    }
+    if (MODE == MODE_QDQ) *reinterpret_cast<uint4*>(out + idx) = make_uint4(o[0], o[1], o[2], o[3]);
+    acc += (double)part;   // fp32 partials of 8 exact squares
+  };
+
+  if (grouped) {
+    // warps take 256-element chunks of rows; a group (16/32/128 | 256) lies in one chunk
+    const int64_t cpr = (cols + 255) / 256;
+    const int gl = (int)(f.group >> 3);   // lanes per group: 2, 4 or 16
+    for (int64_t c = gw; c < rows * cpr; c += nw) {
+      const int64_t r = c / cpr;
+      const int64_t col = (c - r * cpr) * 256 + lane * 8;
+      const bool valid = col < cols;      // cols % group == 0: a group is all valid or all not
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (valid) u = __ldg(reinterpret_cast<const uint4*>(w + r * cols + col));
+      float wv[8];
+      unpack8(u, wv);
+      float a = amax8(wv);
+      for (int o = 1; o < gl; o <<= 1) a = fmaxf(a, __shfl_xor_sync(FULL, a, o));
+      float inv;
+      const float scale = scale_of(a, inv);
+      if (valid) do8(wv, r * cols + col, r, scale, inv);
+    }
+  } else {
+    // one scale per row: the warp reduces the row maximum, then scores the row
+    for (int64_t r = gw; r < rows; r += nw) {
+      const uint16_t* row = w + r * cols;
+      float a = 0.0f;
+      for (int64_t col = lane * 8; col < cols; col += 256) {
+        float wv[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(row + col)), wv);
+        a = fmaxf(a, amax8(wv));
+      }
+      a = __uint_as_float(warp_max_u(__float_as_uint(a)));
+      float inv;
+      const float scale = scale_of(a, inv);
+      for (int64_t col = lane * 8; col < cols; col += 256) {
+        float wv[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(row + col)), wv);
+        do8(wv, r * cols + col, r, scale, inv);
+      }
+    }
+  }
+  if (MODE == MODE_SSE) {
+    const double v = warp_sum_d(acc);
+    if (lane == 0 && v != 0.0) atomicAdd(sse, v);
+  }
+}
+
+template <int MODE>
+static void launch_xfmt2_mode(int kind, unsigned blocks, const uint16_t* w, int64_t rows, int64_t cols, int fmt,
+                              double* sse, uint16_t* out, const float* h, int h_mode, cudaStream_t stream) {
+  switch (kind) {
+#define PQ_XK_CASE(K) \
+    case K: xfmt2_kernel<MODE, K><<<blocks, 256, 0, stream>>>(w, rows, cols, fmt, sse, out, h, h_mode); break;
+    PQ_XK_CASE(XK_E2M1)
+    PQ_XK_CASE(XK_E3M2)
+    PQ_XK_CASE(XK_E2M3)
+    PQ_XK_CASE(XK_E2M0)
+    PQ_XK_CASE(XK_E4M3)
+    PQ_XK_CASE(XK_E5M2)
+    default: xfmt2_kernel<MODE, XK_INT><<<blocks, 256, 0, stream>>>(w, rows, cols, fmt, sse, out, h, h_mode); break;
+#undef PQ_XK_CASE
+  }
+}
+
 // Group length the format uses for rows of `cols`, or 0 if the row does not split into groups
 // (the reference's reshape raises, format_registry.py:208-212 / :151-154).
 int64_t xfmt_group(int fmt, int64_t cols) {
@@ -209,6 +376,19 @@ int64_t xfmt_group(int fmt, int64_t cols) {
 
 cudaError_t launch_xfmt(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, uint16_t* out,
                         int mode, int num_sms, cudaStream_t stream, const float* h, int h_mode) {
+  const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (cols % 8 == 0 && al16(w) && (mode != MODE_QDQ || al16(out)) && (h_mode != 1 || al16(h))) {
+    const XFmt f = xfmt_of(fmt);
+    const int64_t work = (f.group > 0 && f.group < cols) ? rows * ((cols + 255) / 256) : rows;   // warp tasks
+    int64_t blocks2 = (work + 7) / 8;
+    if (blocks2 > (int64_t)num_sms * 8) blocks2 = (int64_t)num_sms * 8;
+    if (blocks2 < 1) blocks2 = 1;
+    if (mode == MODE_QDQ)
+      launch_xfmt2_mode<MODE_QDQ>(xkind_of(f), (unsigned)blocks2, w, rows, cols, fmt, sse, out, h, h_mode, stream);
+    else
+      launch_xfmt2_mode<MODE_SSE>(xkind_of(f), (unsigned)blocks2, w, rows, cols, fmt, sse, out, h, h_mode, stream);
+    return cudaGetLastError();
+  }
   int64_t blocks = (rows * 32 + 255) / 256;
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;

@@ -110,3 +110,42 @@ def test_shape_errors_raise():
             fr.get_format(f).quantize_dequantize(w)
     res = mqc.sweep_weight_mse({"w": w}, [fr.get_format("INT3"), fr.get_format("FP8_E5M2")])
     assert "error" in res["w"]["INT3"] and res["w"]["FP8_E5M2"] == 0.0
+
+
+@pytest.mark.parametrize("fmt", ["FP8_E5M2", "INT8_W8A16", "FP8_E4M3"])
+@pytest.mark.parametrize("cols", [12, 20, 36])
+def test_rows_off_the_16_byte_grid_match_oracle(fmt, cols):
+    """Row-wise formats on rows that are not a multiple of 8 elements take the scalar kernel;
+    W_hat must still match the oracle bit for bit."""
+    from prismaquant_b200 import _lib
+    bits = O.synthetic_weight_bits((33, cols), seed=cols, outlier_frac=0.02)
+    if fmt == "FP8_E4M3":   # the exact codebook path scores it for the weighted sum
+        h = torch.ones(33 * cols, dtype=torch.float32, device="cuda")
+        out = torch.zeros((), dtype=torch.float64, device="cuda")
+        _lib.weighted_sse(to_cuda_bf16(bits), fmt, h, out)
+        err = O.bf16_round((O.bf16_bits_to_f32(bits) - O.cost_qdq_f32(bits, fmt)).astype(np.float32))
+        assert out.item() == pytest.approx(float((err * err).astype(np.float32).astype(np.float64).sum()), rel=1e-5)
+        return
+    got = bits_of(_lib.cost_qdq(to_cuda_bf16(bits), fmt))
+    np.testing.assert_array_equal(got, O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt)))
+
+
+@pytest.mark.parametrize("fmt", EXT_FMTS[:-1] + ["FP8_E4M3_G128"])
+def test_misaligned_view_takes_the_scalar_kernel_with_equal_results(fmt):
+    """A contiguous view 2 bytes off a 16-byte boundary cannot use 16-byte loads; both kernels
+    must give the same W_hat and the same error sum."""
+    from prismaquant_b200 import _lib
+    bits = O.synthetic_weight_bits((64, 256), seed=5, outlier_frac=0.01)
+    w = to_cuda_bf16(bits)
+    buf = torch.empty(w.numel() + 1, dtype=torch.bfloat16, device="cuda")
+    buf[1:].copy_(w.reshape(-1))
+    wm = buf[1:].view(64, 256)
+    assert wm.data_ptr() % 16 != 0 and wm.is_contiguous()
+    a = bits_of(_lib.cost_qdq(w, fmt))
+    b = bits_of(_lib.cost_qdq(wm, fmt))
+    np.testing.assert_array_equal(a, b)
+    s1 = torch.zeros((), dtype=torch.float64, device="cuda")
+    s2 = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.format_sse(w, fmt, s1)
+    _lib.format_sse(wm, fmt, s2)
+    assert s1.item() == pytest.approx(s2.item(), rel=1e-6)   # fp32 partials of 8 vs 64 squares
