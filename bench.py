@@ -40,7 +40,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama8b",
-                    choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b", "outerr8b"])
+                    choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b", "outerr8b", "kernels"])
     ap.add_argument("--fisher-seqs", type=int, default=64, help="calibration sequences (split across ranks)")
     ap.add_argument("--fisher-batch", type=int, default=4, help="sequences per backward on each rank")
     ap.add_argument("--outerr-layers", type=int, default=32,
@@ -301,6 +301,94 @@ def run_outerr(a, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_kernels(a, local):
+    """Per-kernel table: every library kernel timed alone (CUDA events, back-to-back calls after
+    warm-up) on inputs larger than L2, with its algorithmic bytes per call and the fraction of the
+    measured HBM bandwidth (TFLOP/s of the measured bf16 peak for the output-error GEMM).
+    Weights: one [32768, 4096] bf16 tensor (268 MB), N(0, 0.02^2); H: fp32 of the same shape;
+    activations / gradients: [65536, 4096] bf16."""
+    import torch
+
+    from prismaquant_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(7)
+    R, C = 32768, 4096
+    n = R * C
+    W = (torch.randn(R, C, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    H = torch.rand(R, C, device=dev, generator=g)
+    X = torch.randn(65536, C, device=dev, generator=g).to(torch.bfloat16)
+    xnorm = _lib.rownorm2(X)
+    acc2 = torch.zeros(2, dtype=torch.float64, device=dev)
+    sse = torch.zeros(1, 4, dtype=torch.float64, device=dev)
+    s0 = torch.zeros((), dtype=torch.float64, device=dev)
+    codes = torch.empty(R, C // 2, dtype=torch.uint8, device=dev)
+    amax = torch.empty(R, C // 16, dtype=torch.int16, device=dev)
+    tmax = torch.zeros(1, dtype=torch.int32, device=dev)
+    Xo = torch.randn(16, 256, C, device=dev, generator=g).to(torch.bfloat16)
+    Wo = (torch.randn(16, 4096, C, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    Yo = torch.empty(16, 256, 4096, dtype=torch.bfloat16, device=dev)
+    eo = torch.zeros(16, dtype=torch.float64, device=dev)
+    _lib.output_ref(Xo, Wo, eo, Yo)
+    hbm, _ = peaks()
+    try:
+        tf_peak = float(json.loads(PEAKS.read_text())["bf16_tflops"])
+    except Exception:
+        tf_peak = 1590.0
+    gb = lambda b: b / 1e9
+    table = [   # name, call, algorithmic bytes (or FLOP for the GEMM), unit
+        ("sweep_fast_kernel: NVFP4+MXFP8+FP8-channel MSE_W", lambda: _lib.sweep_sse([W], [7], sse=sse), 2 * n, "GB/s"),
+        ("sweep_fast_kernel + NVFP4 codes (export pass 1)",
+         lambda: _lib.sweep_sse([W], [15], nvfp4_outputs=[(codes, amax, tmax)], sse=sse), 2.625 * n, "GB/s"),
+        ("nvfp4_pack (codes + E4M3 scales + global)", lambda: _lib.nvfp4_pack(W), (2 + 0.5 + 1 / 16 + 0.25) * n, "GB/s"),
+        ("mxfp8_pack", lambda: _lib.mxfp8_pack(W), (2 + 1 + 1 / 32) * n, "GB/s"),
+        ("fp8_channel_pack", lambda: _lib.fp8_channel_pack(W), 3 * n, "GB/s"),
+        ("cost_qdq NVFP4 (W_hat)", lambda: _lib.cost_qdq(W, "NVFP4"), 4 * n, "GB/s"),
+        ("cost_qdq MXFP8 (W_hat)", lambda: _lib.cost_qdq(W, "MXFP8"), 4 * n, "GB/s"),
+        ("cost_qdq FP8_E4M3 (W_hat)", lambda: _lib.cost_qdq(W, "FP8_E4M3"), 4 * n, "GB/s"),
+    ]
+    for f in ("MXFP4", "MXFP6_E3M2", "FP8_E5M2", "NVFP3", "INT4_W4A16_g128"):
+        table.append((f"xfmt2_kernel format_sse {f}", (lambda f=f: _lib.format_sse(W, f, s0)), 2 * n, "GB/s"))
+    table += [
+        ("xfmt2_kernel weighted_sse NVFP4 (predicted_dloss)", lambda: _lib.weighted_sse(W, "NVFP4", H, s0), 6 * n, "GB/s"),
+        ("rownorm2 (Fisher forward hook)", lambda: _lib.rownorm2(X), X.numel() * 2 + X.shape[0] * 4, "GB/s"),
+        ("tokennorm_dot (Fisher backward hook)", lambda: _lib.tokennorm_dot(X, xnorm, acc2), X.numel() * 2 + X.shape[0] * 4,
+         "GB/s"),
+        ("outerr_kernel ERR [16, 256, 4096] x [16, 4096, 4096]", lambda: _lib.output_err(Xo, Wo, Yo, eo),
+         2 * 16 * 256 * 4096 * C, "TFLOP/s"),
+    ]
+    rows = []
+    with ClockSampler(local) as clk:
+        for name, fn, work, unit in table:
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / a.steps
+            if unit == "GB/s":
+                v = gb(work) / (ms / 1e3)
+                rows.append({"kernel": name, "ms": round(ms, 4), "bytes": int(work), "GB/s": round(v, 1),
+                             "frac_hbm": round(v / hbm, 4)})
+            else:
+                v = work / (ms / 1e3) / 1e12
+                rows.append({"kernel": name, "ms": round(ms, 4), "flop": int(work), "TFLOP/s": round(v, 1),
+                             "frac_bf16": round(v / tf_peak, 4)})
+    if _lib.device_error() != 0:
+        raise RuntimeError("a kernel reported a device error")
+    print(json.dumps({"metric": "per-kernel throughput (each kernel alone)", "unit": "GB/s | TFLOP/s",
+                      "steps": a.steps, "data": "synthetic: N(0,0.02^2) weights, N(0,1) activations",
+                      "config": {"workload": "kernel_table", "weight": [R, C], "activations": list(X.shape),
+                                 "l2": "every input > 126 MB L2, no flush"},
+                      "peaks": {"hbm_gbs": hbm, "bf16_tflops": tf_peak}, "kernels": rows,
+                      "clocks": clk.summary()}), flush=True)
+
+
 def workload_shapes(name):
     from prismaquant_b200 import synthetic as S
     if name == "llama8b":
@@ -415,6 +503,12 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.workload == "fisher1b" and a.impl == "ours":
         return run_fisher(a, rank, world, local)
+    if a.workload == "kernels":
+        if a.impl == "ours" and rank == 0:
+            run_kernels(a, local)
+        elif a.impl == "reference" and rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the kernel table has no reference arm"}))
+        return
     if a.workload == "outerr8b":
         if a.impl == "ours":
             return run_outerr(a, rank, world, local)
