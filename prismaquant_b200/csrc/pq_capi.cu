@@ -277,7 +277,7 @@ int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t
   const uint32_t m = 1u << fmt;
   const int st = check_groups(cols, m);
   if (st) return st;
-  if (staged_ok(w, cols, m) && aligned(w_hat, 16)) {
+  if (staged_ok(w, cols, m) && aligned(w_hat, 16)) {   // the fast sweep kernel's W_hat mode
     std::vector<pq::SweepDesc> v(1);
     memset(&v[0], 0, sizeof(pq::SweepDesc));
     v[0].w = w;
@@ -285,7 +285,7 @@ int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t
     v[0].cols = cols;
     v[0].fmt_mask = m;
     v[0].out = w_hat;
-    return flush_staged(v, pq::MODE_QDQ, fmt, stream);
+    return launch_batch(v, pq::MODE_SSE, 0, m | 16u, stream);
   }
   return cuda_status(pq::launch_sweep_generic(w, rows, cols, m, nullptr, w_hat, pq::MODE_QDQ, num_sms_current(),
                                               stream));

@@ -103,6 +103,27 @@ __device__ __forceinline__ void nv_bracket(uint64_t w2, uint64_t rlo2, uint64_t 
   cl = cvt_e2m1x2(f2_mul_rz(w2, rlo2));
   ch = cvt_e2m1x2(f2_mul_rz(w2, rhi2));
 }
+// bf16 pair with each -0.0 replaced by +0.0: the cost codebook holds only +0.0, so a value that
+// rounds to zero reconstructs as +0.0 whatever its sign.
+__device__ __forceinline__ uint32_t bf16x2_plus_zero(uint32_t r) {
+  const uint32_t nz = ((r & 0x7FFF7FFFu) + 0x7FFF7FFFu) & 0x80008000u;   // bit 15 / 31 set iff |half| != 0
+  return r & (nz | 0x7FFF7FFFu);
+}
+__device__ __forceinline__ uint32_t nv_pair_rec(uint32_t cl, uint64_t s2) {
+  return bf16x2_plus_zero(f2_to_bf16x2(f2_mul_rn(e2m1x2_to_f2(cl), s2)));
+}
+__device__ __forceinline__ uint32_t f8_pair_rec(uint32_t cl, uint64_t s2) {
+  return bf16x2_plus_zero(f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(cl), s2)));
+}
+// W_hat words of unit u (16 elements = 8 bf16 pairs) from the pairs as load_unit ordered them
+// (swapped 16-byte halves when sw).
+__device__ __forceinline__ void store_unit_words(uint32_t* out_words, int u, bool sw, const uint32_t (&r)[8]) {
+  uint4* o = reinterpret_cast<uint4*>(out_words + 8 * (int64_t)u);
+  const uint4 lo = make_uint4(r[0], r[1], r[2], r[3]), hi = make_uint4(r[4], r[5], r[6], r[7]);
+  o[0] = sw ? hi : lo;
+  o[1] = sw ? lo : hi;
+}
+
 __device__ __forceinline__ float nv_pair_sq(uint32_t v, uint32_t cl, uint64_t s2) {
   const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e2m1x2_to_f2(cl), s2));
   return sq2_acc(bf16x2_sub(v, rec), 0.0f);
@@ -162,24 +183,25 @@ __device__ __forceinline__ uint32_t f8_resolve_pair(uint32_t vp, uint32_t cl, ui
 // Units outside the fast path's range (amax below the 1e-8 scale floor, or
 // large enough for an fp32 square to overflow): every element by IEEE
 // division and the exact tie rules.  The main loop contributed nothing.
-__device__ __noinline__ double nv_exact_unit(const uint32_t* vw, float a16, uint8_t* cu, bool cost) {
+__device__ __noinline__ double nv_exact_unit(const uint32_t* vw, float a16, uint8_t* cu, bool cost, uint32_t* ou) {
   const float s = __fdiv_rn(fmaxf(a16, 1e-8f), 6.0f);
   const float se = fmaxf(__fdiv_rn(fmaxf(a16, 1e-12f), 6.0f), 1e-12f);   // export scale
   double delta = 0.0;
   for (int p = 0; p < 8; ++p) {
     const uint32_t vp = vw[p];
     const float w0 = bf16lo(vp), w1 = bf16hi(vp);
-    if (cost) {
+    if (cost || ou) {
       const float r0 = bf16_round(__fmul_rn(rtn_e2m1_cost(__fdiv_rn(w0, s)), s));
       const float r1 = bf16_round(__fmul_rn(rtn_e2m1_cost(__fdiv_rn(w1, s)), s));
-      delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
+      if (cost) delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
+      if (ou) ou[p] = (__float_as_uint(r0) >> 16) | (__float_as_uint(r1) & 0xFFFF0000u);
     }
     if (cu) cu[p] = (uint8_t)(nvfp4_code(__fdiv_rn(w0, se)) | (nvfp4_code(__fdiv_rn(w1, se)) << 4));
   }
   return delta;
 }
 
-__device__ __noinline__ double f8_exact_unit(const uint32_t* vw, float s) {
+__device__ __noinline__ double f8_exact_unit(const uint32_t* vw, float s, uint32_t* ou) {
   double delta = 0.0;
   for (int p = 0; p < 8; ++p) {
     const uint32_t vp = vw[p];
@@ -187,6 +209,7 @@ __device__ __noinline__ double f8_exact_unit(const uint32_t* vw, float s) {
     const float r0 = bf16_round(__fmul_rn(rtn_e4m3_cost(__fdiv_rn(w0, s)), s));
     const float r1 = bf16_round(__fmul_rn(rtn_e4m3_cost(__fdiv_rn(w1, s)), s));
     delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
+    if (ou) ou[p] = (__float_as_uint(r0) >> 16) | (__float_as_uint(r1) & 0xFFFF0000u);
   }
   return delta;
 }
@@ -211,7 +234,8 @@ __device__ __forceinline__ int warp_incl_scan(int x, int lane) {
 // main loop's provisional ones and rewrites its export code byte.
 // Task word: pair (bits 0-2) | unit (3-14) | group amax bf16 bits (15-29).
 __device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
-                                               int lane, int64_t elem0, uint8_t* codes, bool cost, uint32_t* tasks) {
+                                               int lane, int64_t elem0, uint8_t* codes, bool cost, uint32_t* tasks,
+                                               uint32_t* outw) {
   const int cnt = c0 + c1;   // entries q0[0..c0) then q1[0..c1)
   double delta = 0.0;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
@@ -226,7 +250,8 @@ __device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, cons
       a16b = unit_absmax(v);
       const float a16 = __uint_as_float(a16b << 16);
       if (exact_unit(a16)) {
-        delta += nv_exact_unit(words + 8 * u, a16, codes ? codes + (elem0 + 16 * (int64_t)u) / 2 : nullptr, cost);
+        delta += nv_exact_unit(words + 8 * u, a16, codes ? codes + (elem0 + 16 * (int64_t)u) / 2 : nullptr, cost,
+                               outw ? outw + (elem0 + 16 * (int64_t)u) / 2 : nullptr);
       } else {
         const float s = div_const(a16, 6.0f, RCP6);
         float rlo, rhi;
@@ -259,6 +284,7 @@ __device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, cons
       nv_bracket(f2_from_bf16x2(vp), rlo2, rhi2, cl, ch);
       nv_resolve_pair(vp, cl, ch, s, cx, ce);
       if (cost && cx != cl) dl += nv_pair_sq(vp, cx, s2) - nv_pair_sq(vp, cl, s2);
+      if (outw && cx != cl) outw[(elem0 + 16 * (int64_t)uu) / 2 + p] = nv_pair_rec(cx, s2);
       if (codes) codes[(elem0 + 16 * (int64_t)uu) / 2 + p] = (uint8_t)ce;
     }
     delta += (double)dl;
@@ -270,7 +296,7 @@ __device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, cons
 // Task word: pair (bits 0-2) | unit (3-14).
 __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
                                                int lane, const uint32_t* ramax, int upr, uint32_t rdiv,
-                                               uint32_t* tasks) {
+                                               uint32_t* tasks, int64_t elem0, uint32_t* outw) {
   const int cnt = c0 + c1;
   double delta = 0.0;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
@@ -282,7 +308,7 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, cons
       u = (int)(i < c0 ? q0[i] : q1[i - c0]);
       const RowParam rp = row_param(ramax[upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)]);
       if (rp.amax >= F8_EXACT_ROW_AMAX) {
-        delta += f8_exact_unit(words + 8 * u, rp.s);
+        delta += f8_exact_unit(words + 8 * u, rp.s, outw ? outw + (elem0 + 16 * (int64_t)u) / 2 : nullptr);
       } else {
         const uint4 a = st[2 * u], b = st[2 * u + 1];
         const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -311,6 +337,7 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, cons
       const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2, rlo2)), ch = cvt_e4m3x2(f2_mul_rz(w2, rhi2));
       const uint32_t cx = f8_resolve_pair(vp, cl, ch, rp.s);
       if (cx != cl) dl += f8_pair_sq(vp, cx, s2) - f8_pair_sq(vp, cl, s2);
+      if (outw && cx != cl) outw[(elem0 + 16 * (int64_t)uu) / 2 + p] = f8_pair_rec(cx, s2);
     }
     delta += (double)dl;
     __syncwarp();
@@ -321,12 +348,12 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, cons
 // Out-of-line copies for the rare early flush inside the per-unit loops (the
 // loop bodies stay small); the end-of-item resolution inlines the bodies.
 __device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
-                                        uint8_t* codes, bool cost, uint32_t* tasks) {
-  return nv_fixup_body(q, cnt, q, 0, st, lane, elem0, codes, cost, tasks);
+                                        uint8_t* codes, bool cost, uint32_t* tasks, uint32_t* outw) {
+  return nv_fixup_body(q, cnt, q, 0, st, lane, elem0, codes, cost, tasks, outw);
 }
 __device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
-                                        int upr, uint32_t rdiv, uint32_t* tasks) {
-  return f8_fixup_body(q, cnt, q, 0, st, lane, ramax, upr, rdiv, tasks);
+                                        int upr, uint32_t rdiv, uint32_t* tasks, int64_t elem0, uint32_t* outw) {
+  return f8_fixup_body(q, cnt, q, 0, st, lane, ramax, upr, rdiv, tasks, elem0, outw);
 }
 
 // Tensor index of item `item`, scanning forward from the previous one (items
@@ -352,6 +379,7 @@ struct ItemCtx {
   uint32_t* ramax;       // per-row max |w| (bf16 bits) of this item's rows
   uint32_t* tasks;       // the warp's fix-up task list
   int64_t elem0;
+  uint32_t* outw;        // W_hat of the tensor as bf16 pairs (single-format W_hat launches), else null
 };
 
 struct Accum {
@@ -367,7 +395,7 @@ __device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
 
 // Pass A over one unit: NVFP4 cost and export codes, MXFP8 cost, and (when the
 // FP8 format is on) the unit's contribution to its row maximum.
-template <bool NV, bool MX, bool F8, bool CODES>
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT>
 __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, bool warp_rows,
                                             uint32_t* q_nv, Accum& A) {
   const bool valid = u < c.nunits;
@@ -400,13 +428,19 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
     const uint32_t ux = dx[0] | dx[1];
     if (NV) {
       float pe = 0.0f, po = 0.0f;   // two accumulation chains
+      uint32_t recw[8];
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
         const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
-        if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
+        if (OUT) recw[p] = bf16x2_plus_zero(rec);
+        else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
         else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
       }
-      A.nv += (valid && !ex) ? pe + po : 0.0f;
+      if (OUT) {   // uncertain pairs and exact-path units are rewritten by the fix-ups
+        if (valid) store_unit_words(c.outw + c.elem0 / 2, uc, sw, recw);
+      } else {
+        A.nv += (valid && !ex) ? pe + po : 0.0f;
+      }
     }
     if (CODES) {   // lanes past the end re-store the last unit's identical bytes
       reinterpret_cast<uint2*>(c.codes_it)[uc] = sw ? make_uint2(cw[1], cw[0]) : make_uint2(cw[0], cw[1]);
@@ -420,7 +454,8 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       A.cnt_nv += __popc(bal);
       if (A.cnt_nv > FAST_QCAP - 32) {   // flush early only when the next unit could overflow
         __syncwarp();
-        A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? c.codes_it - c.elem0 / 2 : nullptr, NV, c.tasks);
+        A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? c.codes_it - c.elem0 / 2 : nullptr, NV && !OUT,
+                          c.tasks, c.outw);
         __syncwarp();
         A.cnt_nv = 0;
       }
@@ -436,12 +471,18 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
     const uint32_t m448x2 = m448 | (m448 << 16);
     const bool ok = amin >= ((uint32_t)(e + 121) << 7);          // every |w| >= 2^(e-6): E4M3 normal range
     float pe = 0.0f, po = 0.0f;
+    uint32_t recw[8];
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
-      // magnitude rounded half-up (a finite bf16 half never carries into its sign bit or the next half)
-      const uint32_t rq = (v[p] + 0x00080008u) & 0xFFF0FFF0u;
+      // the magnitude rounded to 3 mantissa bits (a finite bf16 half never carries into its sign
+      // bit or the next half).  The cost needs only the nearest value: a tie's two neighbours
+      // are equally far, so half-up will do.  W_hat needs the reference's tie rule, to the lower
+      // value: toward zero for w > 0, away from zero for w < 0.
+      const uint32_t rq = OUT ? ((v[p] + 0x00070007u + ((v[p] >> 15) & 0x00010001u)) & 0xFFF0FFF0u)
+                              : ((v[p] + 0x00080008u) & 0xFFF0FFF0u);
       const uint32_t q = bf16x2_minabs(rq, m448x2);                   // saturate |q| at 448 * 2^e
-      if (p & 1) po = sq2_acc(bf16x2_sub(v[p], q), po);
+      if (OUT) recw[p] = bf16x2_plus_zero(q);
+      else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], q), po);
       else pe = sq2_acc(bf16x2_sub(v[p], q), pe);
     }
     float part = pe + po;
@@ -449,9 +490,22 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       Chunk8 c0, c1;
       unit_to_chunks(v, c0, c1);
       uint32_t rec[8];
-      part = mxfp8_cost8(c0, a32, rec) + mxfp8_cost8(c1, a32, rec);
+      if (OUT) {
+        (void)mxfp8_cost8(c0, a32, rec);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) recw[i] = rec[2 * i] | (rec[2 * i + 1] << 16);
+        (void)mxfp8_cost8(c1, a32, rec);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) recw[4 + i] = rec[2 * i] | (rec[2 * i + 1] << 16);
+      } else {
+        part = mxfp8_cost8(c0, a32, rec) + mxfp8_cost8(c1, a32, rec);
+      }
     }
-    A.mx += valid ? part : 0.0f;
+    if (OUT) {
+      if (valid) store_unit_words(c.outw + c.elem0 / 2, uc, sw, recw);
+    } else {
+      A.mx += valid ? part : 0.0f;
+    }
   }
 
   if (F8) {   // row maxima for pass B
@@ -466,17 +520,19 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
 }
 
 // Pass B over one unit: FP8 per-channel cost with the completed row maximum.
+template <bool OUT>
 __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, uint32_t* q_f8,
                                             Accum& A) {
   const bool valid = u < c.nunits;
   const int uc = valid ? u : c.nunits - 1;
   uint32_t v[8];
-  load_unit(c.st, uc, true, lane, v);
+  const bool sw = load_unit(c.st, uc, true, lane, v);
   const RowParam rp = row_param(c.ramax[row_of(c, uc)]);
   const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
   const bool exf = rp.amax >= F8_EXACT_ROW_AMAX;
   uint32_t ux = 0;
   float pe = 0.0f, po = 0.0f;
+  uint32_t recw[8];
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
     float l[8], h[8];
@@ -492,11 +548,16 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
-      if (p & 1) po = sq2_acc(bf16x2_sub(v[4 * hf + p], rec), po);
+      if (OUT) recw[4 * hf + p] = bf16x2_plus_zero(rec);
+      else if (p & 1) po = sq2_acc(bf16x2_sub(v[4 * hf + p], rec), po);
       else pe = sq2_acc(bf16x2_sub(v[4 * hf + p], rec), pe);
     }
   }
-  A.f8 += (valid && !exf) ? pe + po : 0.0f;
+  if (OUT) {   // uncertain pairs and exact-path rows are rewritten by the fix-ups
+    if (valid) store_unit_words(c.outw + c.elem0 / 2, uc, sw, recw);
+  } else {
+    A.f8 += (valid && !exf) ? pe + po : 0.0f;
+  }
   const bool need = valid && (ux != 0 || exf);
   const uint32_t bal = __ballot_sync(FULL, need);
   if (bal) {
@@ -504,7 +565,7 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
     A.cnt_f8 += __popc(bal);
     if (A.cnt_f8 > FAST_QCAP - 32) {
       __syncwarp();
-      A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks);
+      A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0, c.outw);
       __syncwarp();
       A.cnt_f8 = 0;
     }
@@ -519,7 +580,7 @@ __device__ __forceinline__ void fold(float& f, double& d) {
   f = 0.0f;
 }
 
-template <bool NV, bool MX, bool F8, bool CODES>
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT>
 __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __grid_constant__ SweepLaunch L) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int NWARPS = FAST_THREADS / 32;
@@ -586,7 +647,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       for (int f = 0; f < 3; ++f) {
         double x = lane < NWARPS ? red[lane * 3 + f] : 0.0;
         x = warp_sum_d(x);
-        if (lane == 0 && (d.fmt_mask & (1u << f))) atomicAdd(d.sse + f, x);
+        if (!OUT && lane == 0 && (d.fmt_mask & (1u << f))) atomicAdd(d.sse + f, x);
       }
     }
     __syncthreads();
@@ -619,13 +680,14 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     c.amax_it = CODES ? d.nvfp4_amax + c.elem0 / 16 : nullptr;
     c.ramax = ramax_buf + (j & 1) * FAST_MAX_ROWS;
     c.tasks = tasks;
+    c.outw = OUT ? reinterpret_cast<uint32_t*>(d.out) : nullptr;
     const int iters = (c.nunits + FAST_THREADS - 1) / FAST_THREADS;
     const bool warp_rows = (c.upr & 31) == 0;
 
     if (NV || MX || CODES || F8) {
 #pragma unroll 1
       for (int k = 0; k < iters; ++k) {   // not unrolled: the body stays small enough for the instruction cache
-        unit_pass_a<NV, MX, F8, CODES>(c, tid + k * FAST_THREADS, lane, lanemask_lt, warp_rows, q_nv, A);
+        unit_pass_a<NV, MX, F8, CODES, OUT>(c, tid + k * FAST_THREADS, lane, lanemask_lt, warp_rows, q_nv, A);
         if ((k & 3) == 3) {   // fp32 partials hold <= 64 squares
           fold(A.nv, A.dnv);
           fold(A.mx, A.dmx);
@@ -644,7 +706,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       for (int i = tid; i < FAST_MAX_ROWS; i += FAST_THREADS) next[i] = 0u;
 #pragma unroll 1
       for (int k = 0; k < iters; ++k) {
-        unit_pass_b(c, tid + k * FAST_THREADS, lane, lanemask_lt, q_f8, A);
+        unit_pass_b<OUT>(c, tid + k * FAST_THREADS, lane, lanemask_lt, q_f8, A);
         if ((k & 3) == 3) fold(A.f8, A.df8);
       }
       fold(A.f8, A.df8);
@@ -664,18 +726,19 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       if ((warp & 1) == 0) {
         const int pc = qcnt[2 * pw];
         if ((NV || CODES) && A.cnt_nv + pc)
-          A.dnv += nv_fixup_body(q_nv, A.cnt_nv, pq, pc, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV,
-                                 c.tasks);
+          A.dnv += nv_fixup_body(q_nv, A.cnt_nv, pq, pc, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
+                                 NV && !OUT, c.tasks, c.outw);
       } else {
         const int pc = qcnt[2 * pw + 1];
         if (A.cnt_f8 + pc) A.df8 += f8_fixup_body(q_f8, A.cnt_f8, pq + FAST_QCAP, pc, c.st, lane, c.ramax, c.upr,
-                                                  c.rdiv, c.tasks);
+                                                  c.rdiv, c.tasks, c.elem0, c.outw);
       }
     } else {
       if ((NV || CODES) && A.cnt_nv)
-        A.dnv += nv_fixup_body(q_nv, A.cnt_nv, q_nv, 0, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr, NV,
-                               c.tasks);
-      if (F8 && A.cnt_f8) A.df8 += f8_fixup_body(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks);
+        A.dnv += nv_fixup_body(q_nv, A.cnt_nv, q_nv, 0, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
+                               NV && !OUT, c.tasks, c.outw);
+      if (F8 && A.cnt_f8)
+        A.df8 += f8_fixup_body(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0, c.outw);
     }
     A.cnt_nv = A.cnt_f8 = 0;
     __syncthreads();   // stage s and the queues are free again
@@ -701,19 +764,23 @@ size_t sweep_fast_smem_bytes() {
          (FAST_THREADS / 32) * (2 * FAST_QCAP + FAST_TASK_CAP + 2) * sizeof(uint32_t);
 }
 
-template <bool NV, bool MX, bool F8, bool CODES>
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT = false>
 static cudaError_t launch_fast_t(const SweepLaunch& L, int grid, cudaStream_t stream) {
   const size_t smem = sweep_fast_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(sweep_fast_kernel<NV, MX, F8, CODES>,
+  cudaError_t e = cudaFuncSetAttribute(sweep_fast_kernel<NV, MX, F8, CODES, OUT>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  sweep_fast_kernel<NV, MX, F8, CODES><<<grid, FAST_THREADS, smem, stream>>>(L);
+  sweep_fast_kernel<NV, MX, F8, CODES, OUT><<<grid, FAST_THREADS, smem, stream>>>(L);
   return cudaGetLastError();
 }
 
-// All descriptors of L share the flag set `key` (format mask bits 0-2, bit 3 = NVFP4 codes).
+// All descriptors of L share the flag set `key` (format mask bits 0-2, bit 3 = NVFP4 codes, bit 4 =
+// W_hat of the one format in the mask into each descriptor's `out`, no error sums).
 cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cudaStream_t stream) {
-  switch (key & 15u) {
+  switch (key & 31u) {
+    case 16 | 1: return launch_fast_t<true, false, false, false, true>(L, grid, stream);
+    case 16 | 2: return launch_fast_t<false, true, false, false, true>(L, grid, stream);
+    case 16 | 4: return launch_fast_t<false, false, true, false, true>(L, grid, stream);
 #define PQ_CASE(K) \
   case K: return launch_fast_t<(K & 1) != 0, (K & 2) != 0, (K & 4) != 0, (K & 8) != 0>(L, grid, stream);
     PQ_CASE(1) PQ_CASE(2) PQ_CASE(3) PQ_CASE(4) PQ_CASE(5) PQ_CASE(6) PQ_CASE(7)

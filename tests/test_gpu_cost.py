@@ -190,3 +190,14 @@ def test_fast_sweep_tie_rows_exact():
         if not (np.array_equal(u8_of(outs[str(i)][0]), p) and np.array_equal(u8_of(outs[str(i)][1]), sc)):
             bad.append((i, "export"))
     assert not bad, bad[:10]
+
+
+@pytest.mark.parametrize("fmt", ["NVFP4", "MXFP8", "FP8_E4M3"])
+def test_qdq_tie_rows_exact(fmt):
+    """W_hat of rows built from near-tie values (the fast kernel's uncertain pairs, rewritten by
+    its fix-ups) and of rows with out-of-range maxima (its exact path), bit-exact with the oracle."""
+    rows = _tie_rows(600, seed=7)
+    tiny = (O.synthetic_weight_bits((8, 32), seed=9) & np.uint16(0x807F)) | np.uint16(0x0100)   # |w| ~ 1e-37
+    bits = np.concatenate([rows, tiny]).astype(np.uint16)
+    q = fr.get_format(fmt).quantize_dequantize(to_cuda_bf16(bits))
+    np.testing.assert_array_equal(bits_of(q), O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt)), err_msg=fmt)
