@@ -298,6 +298,20 @@ int pq_nvfp4_codes(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols,
   if (batch == 0 || rows == 0) return PQ_OK;
   if (!w || !codes || !amax || !tmax) return PQ_ERR_NULL;
   if (!aligned(w, 16) || !aligned(codes, 4) || !aligned(amax, 2) || !aligned(tmax, 4)) return PQ_ERR_ALIGN;
+  if (staged_ok(w, cols, NV) && aligned(codes, 8)) {
+    // the fast sweep kernel's codes-only form (the fused export's pass 1), one descriptor per slice
+    std::vector<pq::SweepDesc> v((size_t)batch);
+    for (int64_t b = 0; b < batch; ++b) {
+      memset(&v[b], 0, sizeof(pq::SweepDesc));
+      v[b].w = w + b * rows * cols;
+      v[b].rows = rows;
+      v[b].cols = cols;
+      v[b].nvfp4_codes = codes + b * rows * cols / 2;
+      v[b].nvfp4_amax = amax + b * rows * cols / 16;
+      v[b].nvfp4_tmax = tmax + b;
+    }
+    return launch_batch(v, pq::MODE_SSE, 0, 8u, (cudaStream_t)stream);
+  }
   return cuda_status(
       pq::launch_nvfp4_codes(w, batch, rows, cols, codes, amax, tmax, num_sms_current(), (cudaStream_t)stream));
 }
