@@ -208,43 +208,55 @@ cudaError_t launch_nvfp4_scales(const ScalesLaunch& L, int64_t max_groups, int n
 // ---------------------------------------------------------------------------
 // MXFP8 (export_native_compressed.py:1138-1162): lane quads form a 32-group.
 // ---------------------------------------------------------------------------
+// A warp takes MX_UNROLL x 32 consecutive 8-element chunks per pass and issues all its loads first
+// (more bytes in flight per thread); four lanes form a 32-group.
+constexpr int MX_UNROLL = 4;
 __global__ void __launch_bounds__(256) mxfp8_pack_kernel(const uint16_t* __restrict__ w, int64_t n_chunks,
                                                          uint8_t* __restrict__ q, uint8_t* __restrict__ sc) {
   const int lane = threadIdx.x & 31;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t c0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x - lane; c0 < n_chunks; c0 += stride) {
-    const int64_t c = c0 + lane;
-    const bool valid = c < n_chunks;
-    float v[8];
-    unpack8(valid ? __ldg(reinterpret_cast<const uint4*>(w) + c) : make_uint4(0, 0, 0, 0), v);
-    float a = amax8(v);
-    a = fmaxf(a, __shfl_xor_sync(FULL, a, 1));
-    a = fmaxf(a, __shfl_xor_sync(FULL, a, 2));
-    if (!valid) continue;
-    const float s = __fdiv_rn(fmaxf(a, pow2i(-127)), 448.0f);  // amax.clamp_min(2^-127) / 448
-    const int e = e8m0_ceil(s);
-    const float inv = pow2i(-e);  // w / 2^e, exact
-    uint32_t out[2];
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t base = gw * (32 * MX_UNROLL); base < n_chunks; base += nw * (32 * MX_UNROLL)) {
+    uint4 u[MX_UNROLL];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int i = 0; i < 4; i += 2) {
-        const float x0 = fminf(fmaxf(__fmul_rn(v[4 * k + i], inv), -448.0f), 448.0f);
-        const float x1 = fminf(fmaxf(__fmul_rn(v[4 * k + i + 1], inv), -448.0f), 448.0f);
-        word |= e4m3x2(x0, x1) << (8 * i);
-      }
-      out[k] = word;
+    for (int j = 0; j < MX_UNROLL; ++j) {
+      const int64_t c = base + 32 * j + lane;
+      u[j] = c < n_chunks ? __ldg(reinterpret_cast<const uint4*>(w) + c) : make_uint4(0, 0, 0, 0);
     }
-    reinterpret_cast<uint2*>(q)[c] = make_uint2(out[0], out[1]);
-    if ((lane & 3) == 0) sc[c >> 2] = (uint8_t)(e + 127);
+#pragma unroll
+    for (int j = 0; j < MX_UNROLL; ++j) {
+      const int64_t c = base + 32 * j + lane;
+      float v[8];
+      unpack8(u[j], v);
+      float a = amax8(v);
+      a = fmaxf(a, __shfl_xor_sync(FULL, a, 1));
+      a = fmaxf(a, __shfl_xor_sync(FULL, a, 2));
+      if (c >= n_chunks) continue;
+      const float s = __fdiv_rn(fmaxf(a, pow2i(-127)), 448.0f);  // amax.clamp_min(2^-127) / 448
+      const int e = e8m0_ceil(s);
+      const float inv = pow2i(-e);  // w / 2^e, exact
+      uint32_t out[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i += 2) {
+          const float x0 = fminf(fmaxf(__fmul_rn(v[4 * k + i], inv), -448.0f), 448.0f);
+          const float x1 = fminf(fmaxf(__fmul_rn(v[4 * k + i + 1], inv), -448.0f), 448.0f);
+          word |= e4m3x2(x0, x1) << (8 * i);
+        }
+        out[k] = word;
+      }
+      reinterpret_cast<uint2*>(q)[c] = make_uint2(out[0], out[1]);
+      if ((lane & 3) == 0) sc[c >> 2] = (uint8_t)(e + 127);
+    }
   }
 }
 
 cudaError_t launch_mxfp8_pack(const uint16_t* w, int64_t n_elems, uint8_t* q, uint8_t* sc, int num_sms,
                               cudaStream_t stream) {
   const int64_t n_chunks = n_elems / 8;
-  mxfp8_pack_kernel<<<grid_for(n_chunks / 32 + 1, num_sms), 256, 0, stream>>>(w, n_chunks, q, sc);
+  mxfp8_pack_kernel<<<grid_for(n_chunks / (32 * MX_UNROLL) + 1, num_sms), 256, 0, stream>>>(w, n_chunks, q, sc);
   return cudaGetLastError();
 }
 
