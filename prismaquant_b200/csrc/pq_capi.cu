@@ -1,6 +1,7 @@
 // C ABI entry points (include/prismaquant_b200.h): argument validation, path
 // selection and launch batching around the kernels.  No entry point allocates
 // device memory or synchronizes the stream.
+#include <atomic>
 #include <string.h>
 
 #include <vector>
@@ -13,16 +14,16 @@ namespace {
 thread_local int t_last_cuda_error = 0;
 
 int num_sms_current() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];   // per device; host threads may race to fill a slot with one value
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int v = 0;
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
-    cached[dev] = v;
+    cached[dev].store(v, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return v;
 }
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }

@@ -577,14 +577,14 @@ __global__ void __launch_bounds__(OE_THREADS, 1)
 // Host side: tensor maps and launches
 // ---------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 oe_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {   // thread-safe one-time initialisation
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+  }();
   return fn;
 }
 
@@ -630,9 +630,7 @@ static cudaError_t oe_launch_s(const CUtensorMap& ta, const CUtensorMap& tb, con
 // Clusters of outerr_kernel<MODE, true, S> (2 x S CTAs) the device holds at once (cached).
 template <int MODE, int S>
 static int oe_max_clusters() {
-  static int cached = -1;
-  if (cached < 0) {
-    using C = OeCfg<MODE, true>;
+  static const int cached = [] {   // thread-safe one-time initialisation (one device model per process)
     int n = 0;
     if (cudaFuncSetAttribute(outerr_kernel<MODE, true, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              OeRing<MODE, true, S>::SMEM) ==
@@ -651,8 +649,8 @@ static int oe_max_clusters() {
       if (cudaOccupancyMaxActiveClusters(&n, outerr_kernel<MODE, true, S>, &cfg) != cudaSuccess) n = 0;
     }
     (void)cudaGetLastError();
-    cached = n;
-  }
+    return n;
+  }();
   return cached;
 }
 
