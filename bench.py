@@ -40,7 +40,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama8b",
-                    choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b", "outerr8b", "kernels"])
+                    choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b", "outerr8b", "kernels",
+                             "costtable8b"])
     ap.add_argument("--fisher-seqs", type=int, default=64, help="calibration sequences (split across ranks)")
     ap.add_argument("--fisher-batch", type=int, default=4, help="sequences per backward on each rank")
     ap.add_argument("--outerr-layers", type=int, default=32,
@@ -389,6 +390,86 @@ def run_kernels(a, local):
                       "clocks": clk.summary()}), flush=True)
 
 
+def run_costtable(a, local):
+    """The reference's cost-table entry point end to end: measure_quant_cost.measure_batched_gpu
+    (measure_quant_cost.py:551-685) on a random-init Llama-8B-shaped model (the 224 decoder
+    Linears of 32 layers, N(0, 0.02^2) bf16 weights) with 256 cached activation rows per Linear
+    (N(0,1); one tensor per input width, shared), for NVFP4, MXFP8 and FP8 per channel: weight_mse
+    from the fused sweep, W_hat per format, the activation quantizers and output_mse /
+    rel_output_mse from the tensor-core output-error kernels, with the reference's cost-table
+    schema as the result.  One step = one full call (its host syncs included)."""
+    import contextlib
+    import io
+
+    import torch
+    import torch.nn as nn
+
+    from prismaquant_b200 import _lib
+    from prismaquant_b200 import format_registry as fr
+    from prismaquant_b200 import measure_quant_cost as mqc
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    model = nn.Module()
+    layers = nn.ModuleList()
+    shapes = {"self_attn": {"q_proj": (4096, 4096), "k_proj": (4096, 1024), "v_proj": (4096, 1024),
+                            "o_proj": (4096, 4096)},
+              "mlp": {"gate_proj": (4096, 14336), "up_proj": (4096, 14336), "down_proj": (14336, 4096)}}
+    with torch.no_grad():
+        for _ in range(32):
+            layer = nn.Module()
+            for block, projs in shapes.items():
+                mod = nn.Module()
+                for pn, (fin, fout) in projs.items():
+                    lin = nn.Linear(fin, fout, bias=False, device=dev, dtype=torch.bfloat16)
+                    lin.weight.normal_(0.0, 0.02)
+                    setattr(mod, pn, lin)
+                setattr(layer, block, mod)
+            layers.append(layer)
+    model.layers = layers
+    names = {n for n, m in model.named_modules() if isinstance(m, nn.Linear)}
+    params = sum(m.weight.numel() for m in model.modules() if isinstance(m, nn.Linear))
+    acts_by_width = {w_: torch.randn(256, w_, device=dev).to(torch.bfloat16) for w_ in (4096, 14336)}
+    in_of = {n: m.in_features for n, m in model.named_modules() if isinstance(m, nn.Linear)}
+
+    class Acts:
+        def __contains__(self, n):
+            return n in in_of
+
+        def load(self, n):
+            return acts_by_width[in_of[n]]
+
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3")]
+    run = lambda: mqc.measure_batched_gpu(model, Acts(), names, specs, "cuda", torch.bfloat16)
+    with contextlib.redirect_stdout(io.StringIO()):
+        for _ in range(max(1, a.warmup)):
+            table = run()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clk:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.steps):
+                table = run()
+            e1.record()
+            torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    if _lib.device_error() != 0:
+        raise RuntimeError("a kernel reported a device error")
+    assert len(table) == len(names) and all("error" not in v for e in table.values() for v in e.values())
+    sample = table["layers.0.mlp.down_proj"]
+    print(json.dumps({
+        "metric": "cost table: measure_batched_gpu over an 8B model (weight_mse + output_mse, 3 formats)",
+        "value": round(params * 2 / (ms / 1e3) / 1e9, 1), "unit": "GB/s (bf16 weights per second)",
+        "n_gpus": 1, "steps": a.steps, "warmup": max(1, a.warmup), "ms_per_step": round(ms, 2),
+        "higher_is_better": True, "data": "synthetic: N(0,0.02^2) weights, N(0,1) activations",
+        "config": {"workload": "llama8b_cost_table", "linears": len(names), "params": params, "rows": 256,
+                   "formats": [s_.name for s_ in specs], "chunk_size": 256},
+        "sample_entry": {"layers.0.mlp.down_proj": {f: {k: float(f"{v:.6g}") for k, v in e.items()}
+                                                    for f, e in sample.items()}},
+        "clocks": clk.summary()}), flush=True)
+
+
 def workload_shapes(name):
     from prismaquant_b200 import synthetic as S
     if name == "llama8b":
@@ -503,6 +584,13 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.workload == "fisher1b" and a.impl == "ours":
         return run_fisher(a, rank, world, local)
+    if a.workload == "costtable8b":
+        if a.impl == "ours" and rank == 0:
+            run_costtable(a, local)
+        elif a.impl == "reference" and rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the cost-table workload has no reference arm on "
+                              "the GPU box (the reference is Python and does not travel)"}))
+        return
     if a.workload == "kernels":
         if a.impl == "ours" and rank == 0:
             run_kernels(a, local)
