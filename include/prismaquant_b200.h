@@ -100,6 +100,18 @@ int pq_sweep_sse(const pq_sweep_tensor* tensors, int n_tensors, double* sse, voi
 int pq_cost_qdq(const uint16_t* w, int64_t rows, int64_t cols, int fmt, uint16_t* w_hat, void* stream);
 
 /*
+ * W_hat of several of the fused formats from one read of W: fmt_mask is a
+ * subset of PQ_FMT_BIT(PQ_FMT_NVFP4) | PQ_FMT_BIT(PQ_FMT_MXFP8) |
+ * PQ_FMT_BIT(PQ_FMT_FP8_CHANNEL), and w_hat holds popcount(fmt_mask) bf16
+ * slices of rows*cols, one per format in the mask, in that order.  Each slice
+ * equals pq_cost_qdq of its format.  No counterpart in the reference's API as
+ * a single call; it serves measure_batched_gpu's per-format W_hat
+ * (measure_quant_cost.py:628-630).
+ */
+int pq_cost_qdq_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_t fmt_mask, uint16_t* w_hat,
+                      void* stream);
+
+/*
  * Sum of squared errors of one format over one bf16 tensor [rows, cols]:
  * ADDS sum((W - qdq_fmt(W))^2) (bf16 subtraction, fp32 square) to *sse
  * (fp64, device; zero it first).  fmt is one of PQ_FMT_MXFP4 ..

@@ -30,7 +30,7 @@ EXPORTED = [
     "pq_sweep_sse", "pq_cost_qdq", "pq_nvfp4_codes", "pq_nvfp4_scales", "pq_nvfp4_pack",
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
-    "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err",
+    "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
 ]
 
 
@@ -65,6 +65,7 @@ def load() -> ctypes.CDLL:
     sig = {
         "pq_sweep_sse": [ctypes.POINTER(SweepTensor), I, P, V],
         "pq_cost_qdq": [P, I64, I64, I, P, V],
+        "pq_cost_qdq_fused": [P, I64, I64, ctypes.c_uint32, P, V],
         "pq_format_sse": [P, I64, I64, I, P, V],
         "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
         "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
@@ -194,6 +195,25 @@ def cost_qdq(w: torch.Tensor, fmt: str) -> torch.Tensor:
     _check(lib.pq_cost_qdq(_ptr(wb), rows, cols, fid, _ptr(out), _stream(wb)), "pq_cost_qdq",
            f"cannot reshape rows of {cols} into groups for {fmt}")
     return out if w.dtype == torch.bfloat16 else out.to(w.dtype)
+
+
+FUSED_FMTS = ("NVFP4", "MXFP8", "FP8_E4M3")
+
+
+def cost_qdq_fused(w: torch.Tensor, fmts) -> dict:
+    """Cost-path W_hat of several of NVFP4 / MXFP8 / FP8_E4M3 (per channel) from one read of W:
+    {fmt: bf16 tensor of w's shape}, each equal to cost_qdq(w, fmt)."""
+    wb = as_bf16_cuda(w, "quantize_dequantize")
+    want = [f for f in FUSED_FMTS if f in set(fmts)]
+    if len(want) != len(set(fmts)):
+        raise ValueError(f"cost_qdq_fused: formats must be among {FUSED_FMTS}, got {list(fmts)}")
+    out = torch.empty((len(want),) + tuple(wb.shape), dtype=torch.bfloat16, device=wb.device)
+    if wb.numel():
+        cols = wb.shape[-1] if wb.dim() else 1
+        mask = sum(1 << FMT_IDS[f] for f in want)
+        _check(load().pq_cost_qdq_fused(_ptr(wb), wb.numel() // cols, cols, mask, _ptr(out), _stream(wb)),
+               "pq_cost_qdq_fused", f"cannot reshape rows of {cols} into groups for {want}")
+    return {f: out[i] for i, f in enumerate(want)}
 
 
 def format_sse(w: torch.Tensor, fmt: str, sse: torch.Tensor) -> None:

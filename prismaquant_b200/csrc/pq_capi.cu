@@ -228,6 +228,35 @@ static int outerr_shape(int64_t batch, int64_t rows, int64_t out, int64_t k) {
   return PQ_OK;
 }
 
+int pq_cost_qdq_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_t fmt_mask, uint16_t* w_hat,
+                      void* stream_) {
+  if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  const uint32_t fused = NV | MX | F8;
+  if (fmt_mask == 0 || (fmt_mask & ~fused)) return PQ_ERR_FORMAT;
+  const int st0 = check_groups(cols, fmt_mask);
+  if (st0) return st0;
+  if (rows == 0) return PQ_OK;
+  if (!w || !w_hat) return PQ_ERR_NULL;
+  if (staged_ok(w, cols, fmt_mask) && aligned(w_hat, 16)) {   // one read of W for every format
+    std::vector<pq::SweepDesc> v(1);
+    memset(&v[0], 0, sizeof(pq::SweepDesc));
+    v[0].w = w;
+    v[0].rows = rows;
+    v[0].cols = cols;
+    v[0].fmt_mask = fmt_mask;
+    v[0].out = w_hat;
+    return launch_batch(v, pq::MODE_SSE, 0, fmt_mask | 16u, (cudaStream_t)stream_);
+  }
+  int slot = 0;   // other shapes: one W_hat at a time, same slices
+  for (int f = 0; f < 3; ++f) {
+    if (!(fmt_mask & (1u << f))) continue;
+    const int st = pq_cost_qdq(w, rows, cols, f, w_hat + (int64_t)slot * rows * cols, stream_);
+    if (st) return st;
+    ++slot;
+  }
+  return PQ_OK;
+}
+
 int pq_output_sse(const uint16_t* x, const uint16_t* w, const uint16_t* x_hat, const uint16_t* w_hat, int64_t batch,
                   int64_t rows, int64_t out, int64_t k, double* err_sse, double* ref_sse, float* y_ref, float* y_q,
                   void* stream_) {

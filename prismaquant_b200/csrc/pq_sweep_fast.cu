@@ -379,7 +379,11 @@ struct ItemCtx {
   uint32_t* ramax;       // per-row max |w| (bf16 bits) of this item's rows
   uint32_t* tasks;       // the warp's fix-up task list
   int64_t elem0;
-  uint32_t* outw;        // W_hat of the tensor as bf16 pairs (single-format W_hat launches), else null
+  // W_hat launches: each format's W_hat of the tensor as bf16 pairs, one slice per format present,
+  // in format order (NVFP4, MXFP8, FP8 per channel); null otherwise
+  uint32_t* outw;        // NVFP4
+  uint32_t* outw_mx;     // MXFP8
+  uint32_t* outw_f8;     // FP8 per channel
 };
 
 struct Accum {
@@ -502,7 +506,7 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       }
     }
     if (OUT) {
-      if (valid) store_unit_words(c.outw + c.elem0 / 2, uc, sw, recw);
+      if (valid) store_unit_words(c.outw_mx + c.elem0 / 2, uc, sw, recw);
     } else {
       A.mx += valid ? part : 0.0f;
     }
@@ -554,7 +558,7 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
     }
   }
   if (OUT) {   // uncertain pairs and exact-path rows are rewritten by the fix-ups
-    if (valid) store_unit_words(c.outw + c.elem0 / 2, uc, sw, recw);
+    if (valid) store_unit_words(c.outw_f8 + c.elem0 / 2, uc, sw, recw);
   } else {
     A.f8 += (valid && !exf) ? pe + po : 0.0f;
   }
@@ -565,7 +569,7 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
     A.cnt_f8 += __popc(bal);
     if (A.cnt_f8 > FAST_QCAP - 32) {
       __syncwarp();
-      A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0, c.outw);
+      A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0, c.outw_f8);
       __syncwarp();
       A.cnt_f8 = 0;
     }
@@ -680,7 +684,13 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     c.amax_it = CODES ? d.nvfp4_amax + c.elem0 / 16 : nullptr;
     c.ramax = ramax_buf + (j & 1) * FAST_MAX_ROWS;
     c.tasks = tasks;
-    c.outw = OUT ? reinterpret_cast<uint32_t*>(d.out) : nullptr;
+    {
+      const int64_t slot = d.rows * d.cols / 2;   // words of one W_hat
+      uint32_t* base = OUT ? reinterpret_cast<uint32_t*>(d.out) : nullptr;
+      c.outw = (OUT && NV) ? base : nullptr;
+      c.outw_mx = (OUT && MX) ? base + (NV ? slot : 0) : nullptr;
+      c.outw_f8 = (OUT && F8) ? base + ((NV ? 1 : 0) + (MX ? 1 : 0)) * slot : nullptr;
+    }
     const int iters = (c.nunits + FAST_THREADS - 1) / FAST_THREADS;
     const bool warp_rows = (c.upr & 31) == 0;
 
@@ -731,14 +741,15 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       } else {
         const int pc = qcnt[2 * pw + 1];
         if (A.cnt_f8 + pc) A.df8 += f8_fixup_body(q_f8, A.cnt_f8, pq + FAST_QCAP, pc, c.st, lane, c.ramax, c.upr,
-                                                  c.rdiv, c.tasks, c.elem0, c.outw);
+                                                  c.rdiv, c.tasks, c.elem0, c.outw_f8);
       }
     } else {
       if ((NV || CODES) && A.cnt_nv)
         A.dnv += nv_fixup_body(q_nv, A.cnt_nv, q_nv, 0, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
                                NV && !OUT, c.tasks, c.outw);
       if (F8 && A.cnt_f8)
-        A.df8 += f8_fixup_body(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0, c.outw);
+        A.df8 += f8_fixup_body(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0,
+                               c.outw_f8);
     }
     A.cnt_nv = A.cnt_f8 = 0;
     __syncthreads();   // stage s and the queues are free again
@@ -775,12 +786,17 @@ static cudaError_t launch_fast_t(const SweepLaunch& L, int grid, cudaStream_t st
 }
 
 // All descriptors of L share the flag set `key` (format mask bits 0-2, bit 3 = NVFP4 codes, bit 4 =
-// W_hat of the one format in the mask into each descriptor's `out`, no error sums).
+// W_hat of each format in the mask into each descriptor's `out`, one slice per format in format
+// order, no error sums).
 cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cudaStream_t stream) {
   switch (key & 31u) {
     case 16 | 1: return launch_fast_t<true, false, false, false, true>(L, grid, stream);
     case 16 | 2: return launch_fast_t<false, true, false, false, true>(L, grid, stream);
+    case 16 | 3: return launch_fast_t<true, true, false, false, true>(L, grid, stream);
     case 16 | 4: return launch_fast_t<false, false, true, false, true>(L, grid, stream);
+    case 16 | 5: return launch_fast_t<true, false, true, false, true>(L, grid, stream);
+    case 16 | 6: return launch_fast_t<false, true, true, false, true>(L, grid, stream);
+    case 16 | 7: return launch_fast_t<true, true, true, false, true>(L, grid, stream);
 #define PQ_CASE(K) \
   case K: return launch_fast_t<(K & 1) != 0, (K & 2) != 0, (K & 4) != 0, (K & 8) != 0>(L, grid, stream);
     PQ_CASE(1) PQ_CASE(2) PQ_CASE(3) PQ_CASE(4) PQ_CASE(5) PQ_CASE(6) PQ_CASE(7)

@@ -236,6 +236,31 @@ def _batched_quantize(spec: fr.FormatSpec, stacked_w: torch.Tensor) -> torch.Ten
 # reference entry points
 # ---------------------------------------------------------------------------
 
+def _fused_w_hats(W: torch.Tensor, specs) -> dict:
+    """W_hat of every spec whose batched RTN is NVFP4, MXFP8 or FP8 per channel, from one read of
+    the stacked weight (pq_cost_qdq_fused) when two or more of them are asked for and the extra
+    slices fit in a quarter of the free device memory; {} otherwise, or on a shape error (the
+    per-format path then reports each format's own error)."""
+    by_kernel: dict[str, list[str]] = {}
+    for spec in specs:
+        try:
+            k = batched_kernel_format(spec)
+        except Exception:
+            continue
+        if k in _lib.FUSED_FMTS:
+            by_kernel.setdefault(k, []).append(spec.name)
+    if len(by_kernel) < 2:
+        return {}
+    free, _ = torch.cuda.mem_get_info(W.device)
+    if W.numel() * 2 * len(by_kernel) > free // 4:
+        return {}
+    try:
+        hats = _lib.cost_qdq_fused(W, list(by_kernel))
+    except ValueError:
+        return {}
+    return {name: hats[k] for k, names in by_kernel.items() for name in names}
+
+
 def _group_by_shape(model: nn.Module, target_names: set[str]):
     groups: dict[tuple[int, int], list[tuple[str, nn.Linear]]] = {}
     for name, mod in model.named_modules():
@@ -302,11 +327,14 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                     h_stacked = torch.stack([h.to(dev).float() for h in hs])
             wmse = (_weight_mse_or_errors(list(W.unbind(0)), specs, _per_linear) if dtype == torch.bfloat16
                     else None)
+            w_hat_pre = _fused_w_hats(W, specs) if dtype == torch.bfloat16 and not _per_linear else {}
             for spec in specs:
                 try:
                     if wmse is None and spec.weight_element_dtype != "bfloat16":
                         raise NotImplementedError(f"B200 cost kernels take bf16 weights, got {dtype}")
-                    W_hat = spec.quantize_dequantize(W) if _per_linear else _batched_quantize(spec, W)
+                    W_hat = w_hat_pre.get(spec.name)
+                    if W_hat is None:
+                        W_hat = spec.quantize_dequantize(W) if _per_linear else _batched_quantize(spec, W)
                     X_hat = spec.activation_quantize_dequantize(X.clone())
                     if fused_out:
                         err = torch.zeros(W.shape[0], dtype=torch.float64, device=dev)

@@ -201,3 +201,28 @@ def test_qdq_tie_rows_exact(fmt):
     bits = np.concatenate([rows, tiny]).astype(np.uint16)
     q = fr.get_format(fmt).quantize_dequantize(to_cuda_bf16(bits))
     np.testing.assert_array_equal(bits_of(q), O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt)), err_msg=fmt)
+
+
+@pytest.mark.parametrize("fmts", [("NVFP4", "MXFP8", "FP8_E4M3"), ("NVFP4", "FP8_E4M3"), ("MXFP8", "FP8_E4M3"),
+                                  ("NVFP4", "MXFP8")])
+@pytest.mark.parametrize("shape", [(512, 4096), (4, 128, 768), (600, 32), (7, 48)])
+def test_fused_w_hat_equals_single_format(fmts, shape):
+    """W_hat of several formats from one read (one slice per format) equals each format's own W_hat
+    and the oracle, including the near-tie rows that the fix-ups rewrite; odd shapes take the
+    per-format path."""
+    from prismaquant_b200 import _lib
+    bits = _tie_rows(600, seed=11)[:, :32] if shape == (600, 32) else \
+        O.synthetic_weight_bits(shape, seed=sum(shape), outlier_frac=0.002)
+    w = to_cuda_bf16(bits)
+    if "MXFP8" in fmts and shape[-1] % 32 and shape[-1] > 32:   # MXFP8 cannot group the row
+        with pytest.raises(ValueError):
+            _lib.cost_qdq_fused(w, fmts)
+        return
+    got = _lib.cost_qdq_fused(w, fmts)
+    for f in fmts:
+        try:
+            want = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, f))
+        except ValueError:   # MXFP8 cannot group 48 columns
+            continue
+        np.testing.assert_array_equal(bits_of(got[f]), want, err_msg=f)
+        np.testing.assert_array_equal(bits_of(got[f]), bits_of(_lib.cost_qdq(w, f)), err_msg=f)
