@@ -161,6 +161,17 @@ int pq_output_sse(const uint16_t* x, const uint16_t* w, const uint16_t* x_hat, c
  * sum(bf16(y_ref - y_q)^2) to err_sse[b], reading y_ref from memory.  Same
  * operand rules as pq_output_sse.
  */
+/*
+ * Per-weight Fisher diagonal of one backward of one Linear, on the tensor
+ * cores (sensitivity_probe.py:1114-1152):
+ *   grad_w = bf16(gy^T x)          gy [t, m] output gradients, x [t, n] inputs (bf16)
+ *   g2 = bf16(grad_w^2);  h[m, n] += g2 (fp32, updated in place)
+ *   sums[0] += sum(g2);  sums[1] += sum(bf16(g2 * bf16(w^2)))   (fp64; w [m, n] bf16, may be NULL)
+ * m and n multiples of 8, pointers 16-byte aligned.  grad_w itself is never stored.
+ */
+int pq_grad_sq_acc(const uint16_t* gy, const uint16_t* x, const uint16_t* w, int64_t t, int64_t m, int64_t n,
+                   float* h, double* sums, void* stream);
+
 int pq_output_ref(const uint16_t* x, const uint16_t* w, int64_t batch, int64_t rows, int64_t out, int64_t k,
                   uint16_t* y_ref, double* ref_sse, void* stream);
 int pq_output_err(const uint16_t* x_hat, const uint16_t* w_hat, const uint16_t* y_ref, int64_t batch, int64_t rows,

@@ -31,6 +31,7 @@ EXPORTED = [
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
+    "pq_grad_sq_acc",
 ]
 
 
@@ -71,6 +72,7 @@ def load() -> ctypes.CDLL:
         "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
         "pq_output_ref": [P, P, I64, I64, I64, I64, P, P, V],
         "pq_output_err": [P, P, P, I64, I64, I64, I64, P, V],
+        "pq_grad_sq_acc": [P, P, P, I64, I64, I64, P, P, V],
         "pq_nvfp4_codes": [P, I64, I64, I64, P, P, P, V],
         "pq_nvfp4_scales": [I, ctypes.POINTER(P), ctypes.POINTER(I64), P, ctypes.POINTER(ctypes.c_int32), P,
                             ctypes.POINTER(P), P, V],
@@ -317,6 +319,26 @@ def output_err(x_hat: torch.Tensor, w_hat: torch.Tensor, y_ref: torch.Tensor, er
         raise TypeError(f"output_err: y_ref must be a contiguous bfloat16 [{batch}, {rows}, {out}] tensor")
     _check(load().pq_output_err(_ptr(xb), _ptr(wb), _ptr(y_ref), batch, rows, out, k, _ptr(err_sse), _stream(xb)),
            "pq_output_err", f"k = {k} must be a multiple of 8")
+
+
+def grad_sq_acc(gy: torch.Tensor, x: torch.Tensor, h: torch.Tensor, sums: torch.Tensor,
+                w: torch.Tensor | None = None) -> None:
+    """One backward's per-weight Fisher diagonal on the tensor cores: with grad_w = bf16(gy^T x)
+    (gy [t, m], x [t, n]) and g2 = bf16(grad_w^2), h (fp32 [m, n]) += g2, sums[0] += sum(g2) and,
+    given the bf16 weight w [m, n], sums[1] += sum(bf16(g2 * bf16(w^2)))."""
+    gb, xb = as_bf16_cuda(gy, "grad_sq_acc"), as_bf16_cuda(x, "grad_sq_acc")
+    gb, xb = gb.reshape(-1, gb.shape[-1]), xb.reshape(-1, xb.shape[-1])
+    t, m = gb.shape
+    n = xb.shape[1]
+    if xb.shape[0] != t or tuple(h.shape) != (m, n) or h.dtype != torch.float32 or not h.is_contiguous():
+        raise ValueError(f"grad_sq_acc: gy {tuple(gy.shape)}, x {tuple(x.shape)}, h {tuple(h.shape)} do not match")
+    if sums.dtype != torch.float64 or sums.numel() < 2 or not sums.is_contiguous():
+        raise TypeError("grad_sq_acc: sums must be a contiguous float64 tensor of 2")
+    wb = None if w is None else as_bf16_cuda(w, "grad_sq_acc")
+    if wb is not None and tuple(wb.shape) != (m, n):
+        raise ValueError(f"grad_sq_acc: w {tuple(wb.shape)} is not [{m}, {n}]")
+    _check(load().pq_grad_sq_acc(_ptr(gb), _ptr(xb), _ptr(wb), t, m, n, _ptr(h), _ptr(sums), _stream(gb)),
+           "pq_grad_sq_acc", f"grad_w [{m}, {n}]: both sides must be multiples of 8")
 
 
 # ---------------------------------------------------------------------------

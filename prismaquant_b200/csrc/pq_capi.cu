@@ -257,6 +257,16 @@ int pq_cost_qdq_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_t fm
   return PQ_OK;
 }
 
+int pq_grad_sq_acc(const uint16_t* gy, const uint16_t* x, const uint16_t* w, int64_t t, int64_t m, int64_t n,
+                   float* h, double* sums, void* stream_) {
+  if (t < 0 || m < 0 || n < 0 || (m & 7) || (n & 7)) return PQ_ERR_SHAPE;
+  if (t > 0x7fffffff || (m + 255) / 256 > 0x3fffffff || (n + 255) / 256 > 65535) return PQ_ERR_LIMIT;
+  if (t == 0 || m == 0 || n == 0) return PQ_OK;
+  if (!gy || !x || !h || !sums) return PQ_ERR_NULL;
+  if (!aligned(gy, 16) || !aligned(x, 16) || !aligned(h, 16) || !aligned(w, 16)) return PQ_ERR_ALIGN;
+  return cuda_status(pq::launch_gradsq(gy, x, w, t, m, n, h, sums, (cudaStream_t)stream_));
+}
+
 int pq_output_sse(const uint16_t* x, const uint16_t* w, const uint16_t* x_hat, const uint16_t* w_hat, int64_t batch,
                   int64_t rows, int64_t out, int64_t k, double* err_sse, double* ref_sse, float* y_ref, float* y_q,
                   void* stream_) {

@@ -49,6 +49,8 @@ cudaError_t launch_outerr(const uint16_t* x, const uint16_t* w, const uint16_t* 
                           float* d_q, cudaStream_t stream);
 cudaError_t launch_outerr_ref(const uint16_t* x, const uint16_t* w, int64_t batch, int64_t rows, int64_t out,
                               int64_t K, uint16_t* y_ref, double* ref_energy, cudaStream_t stream);
+cudaError_t launch_gradsq(const uint16_t* gy, const uint16_t* x, const uint16_t* w, int64_t t, int64_t m, int64_t n,
+                          float* h, double* sums, cudaStream_t stream);
 cudaError_t launch_outerr_err(const uint16_t* xq, const uint16_t* wq, const uint16_t* y_ref, int64_t batch,
                               int64_t rows, int64_t out, int64_t K, double* err_sum, cudaStream_t stream);
 cudaError_t launch_sweep_staged(const SweepLaunch& L, int mode, int grid, cudaStream_t stream);

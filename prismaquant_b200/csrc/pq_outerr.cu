@@ -693,6 +693,252 @@ static cudaError_t oe_launch(const uint16_t* a, const uint16_t* b, const uint16_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Per-weight Fisher diagonal (sensitivity_probe.py:1114-1152): for one backward of one Linear,
+//   grad_w = bf16(gy^T x)  (gy [T, M] output gradients, x [T, N] inputs, K = T tokens)
+//   g2 = bf16(grad_w^2);  h[M, N] += g2 (fp32);  sums[0] += sum(g2);  sums[1] += sum(bf16(g2 * bf16(w^2)))
+// on CTA pairs: both operands are M/N-contiguous, so they are loaded as they lie (64 x 64 TMA
+// boxes, 128-byte swizzle) and described to the MMA as MN-major tiles; the epilogue reads the
+// accumulators from TMEM and updates h in place (each h tile belongs to one CTA).
+// ---------------------------------------------------------------------------
+constexpr int GS_NSTAGE = 3;                          // 32 KB stages, two CTAs per SM
+constexpr int GS_STAGE_BYTES = 2 * 16384;             // A (128 M x 64 K) + B (128 N x 64 K) per CTA
+constexpr int GS_SMEM = 1024 + GS_NSTAGE * GS_STAGE_BYTES + 256;
+// kind::f16: D f32, A and B bf16, both MN-major (bits 15, 16 = 1), N = 256, M = 256 (pair)
+constexpr uint32_t GS_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
+                              ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+struct GsArgs {
+  int64_t m, n, t;      // grad_w is [m, n]; t tokens
+  float* h;             // [m, n] fp32, updated in place
+  const uint16_t* w;    // [m, n] bf16 weight (may be null: no w^2 sum)
+  double* sums;         // [2]
+};
+
+// Shared-memory descriptor of an MN-major, 128-byte-swizzled tile: atoms of 8 K-rows x 128 bytes
+// (64 M/N elements); the next 64 M/N elements 8192 bytes on (leading byte offset, >> 4 = 512), the
+// next 8 K-rows 1024 bytes on (stride byte offset, >> 4 = 64); version 1, SWIZZLE_128B.
+__device__ __forceinline__ uint64_t gs_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(8192 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void gs_tma_2d_pair(void* dst, const CUtensorMap* map, int c0, int c1, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(OE_THREADS, 1)
+    gradsq_kernel(const __grid_constant__ CUtensorMap tg, const __grid_constant__ CUtensorMap tx, GsArgs p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GS_NSTAGE * GS_STAGE_BYTES);
+  uint64_t* empty = full + GS_NSTAGE;
+  uint64_t* acc_full = empty + GS_NSTAGE;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* consumed = abort_flag + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t crank = oe_cluster_rank();
+  const uint32_t prank = crank & 1u;
+  const uint32_t leader = crank & ~1u;
+  const int m0 = (int)(blockIdx.x >> 1) * 256 + (int)prank * 128;   // this CTA's 128 rows of grad_w
+  const int n0 = (int)blockIdx.y * 256;                              // the tile's 256 columns
+  const int nb0 = n0 + (int)prank * 128;                             // this CTA's half of B
+  const int nk = (int)((p.t + OE_BK - 1) / OE_BK);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(OE_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < GS_NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    *consumed = 0;
+    fence_mbar_init();
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  oe_cluster_sync();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t peer_abort = oe_mapa(smem_u32((const void*)abort_flag), crank ^ 1u);
+  auto set_abort = [&]() {
+    *abort_flag = 1;
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1u) : "memory");
+  };
+
+  int produced = 0;
+  if (tid == 0) {
+    // ---- producer: this CTA's A (gy, 128 rows of M) and half of B (x, 128 of N), 64 tokens a stage
+    const uint32_t leader_full0 = oe_mapa(smem_u32(&full[0]), leader);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % GS_NSTAGE, use = kb / GS_NSTAGE;
+      if (use > 0 && !oe_wait(&empty[s], (uint32_t)((use - 1) & 1), abort_flag)) {
+        set_abort();
+        break;
+      }
+      if (*abort_flag) break;
+      uint8_t* st = smem + s * GS_STAGE_BYTES;
+      if (prank == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * GS_STAGE_BYTES));
+      const uint32_t fb = leader_full0 + 8u * (uint32_t)s;
+      const int t0 = kb * OE_BK;
+      gs_tma_2d_pair(st, &tg, m0, t0, fb);
+      gs_tma_2d_pair(st + 8192, &tg, m0 + 64, t0, fb);
+      gs_tma_2d_pair(st + 16384, &tx, nb0, t0, fb);
+      gs_tma_2d_pair(st + 16384 + 8192, &tx, nb0 + 64, t0, fb);
+      produced = kb + 1;
+    }
+  } else if (tid == 32 && prank == 0) {
+    // ---- MMA issuer (the pair leader's): K = 16 tokens per MMA = two 8-row groups = 2048 bytes
+    const uint16_t pair_mask = (uint16_t)(3u << leader);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % GS_NSTAGE, use = kb / GS_NSTAGE;
+      if (!oe_wait(&full[s], (uint32_t)(use & 1), abort_flag)) {
+        set_abort();
+        break;
+      }
+      *consumed = kb + 1;
+      if (*abort_flag) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t sa = smem_u32(smem + s * GS_STAGE_BYTES);
+#pragma unroll
+      for (int kk = 0; kk < OE_BK / 16; ++kk)
+        oe_mma_pair(tmem, gs_desc(sa + 2048 * kk), gs_desc(sa + 16384 + 2048 * kk), GS_IDESC,
+                    (kb > 0 || kk > 0) ? 1u : 0u);
+      oe_commit_pair(&empty[s], pair_mask);
+    }
+    oe_commit_pair(acc_full, pair_mask);
+  }
+  __syncwarp();
+
+  // ---- epilogue: row m of grad_w per thread (TMEM lane), 256 columns, h updated in place
+  if (!mbar_wait_bounded(acc_full, 0)) *abort_flag = 1;
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (!*abort_flag) {
+    const int64_t m = (int64_t)m0 + 32 * warp + lane;
+    const bool row_ok = m < p.m;
+    const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
+    float ts = 0.0f, ws = 0.0f;
+    double tsum = 0.0, wsum = 0.0;
+#pragma unroll 1
+    for (int jb = 0; jb < 16; jb += 4) {   // 64 columns at a time: h and w loads issued first
+      float4 hv[16];
+      uint4 wv[8];
+      const int64_t cb = (int64_t)n0 + 16 * jb;
+      const bool vec = row_ok && cb + 64 <= p.n;
+      if (vec) {
+        const float4* hp = reinterpret_cast<const float4*>(p.h + m * p.n + cb);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) hv[i] = hp[i];
+        if (p.w) {
+          const uint4* wp = reinterpret_cast<const uint4*>(p.w + m * p.n + cb);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) wv[i] = __ldg(wp + i);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) wv[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        float v[16];
+        oe_ld16(tbase + 16 * (jb + jj), v);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int64_t col = cb + 16 * jj + e;
+          const float g = bf16_round(v[e]);                      // grad_w, bf16
+          const float g2 = bf16_round(__fmul_rn(g, g));           // grad_w.pow(2), bf16
+          float wf = 0.0f;
+          if (vec) {
+            const uint32_t u = (&wv[0].x)[(16 * jj + e) >> 1];
+            wf = __uint_as_float(((16 * jj + e) & 1) ? (u & 0xFFFF0000u) : (u << 16));
+            float* hc = &(&hv[0].x)[16 * jj + e];
+            *hc = __fadd_rn(*hc, g2);
+          } else if (row_ok && col < p.n) {
+            if (p.w) wf = __uint_as_float((uint32_t)p.w[m * p.n + col] << 16);
+            p.h[m * p.n + col] = __fadd_rn(p.h[m * p.n + col], g2);
+          }
+          ts = __fadd_rn(ts, g2);
+          ws = __fadd_rn(ws, bf16_round(__fmul_rn(g2, bf16_round(__fmul_rn(wf, wf)))));
+        }
+        tsum += (double)ts;   // fp32 partials of 16 values
+        wsum += (double)ws;
+        ts = ws = 0.0f;
+      }
+      if (vec) {
+        float4* hp = reinterpret_cast<float4*>(p.h + m * p.n + cb);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) hp[i] = hv[i];
+      }
+    }
+    tsum = warp_sum_d(tsum);
+    wsum = warp_sum_d(wsum);
+    if (lane == 0) {
+      atomicAdd(p.sums, tsum);
+      if (p.w) atomicAdd(p.sums + 1, wsum);
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (tid == 0 && prank == 0 && *abort_flag) {
+    for (int j = *consumed; j < produced; ++j)
+      (void)mbar_wait_bounded(&full[j % GS_NSTAGE], (uint32_t)((j / GS_NSTAGE) & 1), 1u << 20);
+  }
+  oe_cluster_sync();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(OE_TMEM_COLS));
+  }
+}
+
+// bf16 [rows, cols] (cols % 8 == 0, 16-byte aligned base), box 64 (cols) x 64 (rows), SW128
+static bool gs_tmap(CUtensorMap* map, const uint16_t* base, int64_t rows, int64_t cols) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = oe_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {64, 64};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_gradsq(const uint16_t* gy, const uint16_t* x, const uint16_t* w, int64_t t, int64_t m, int64_t n,
+                          float* h, double* sums, cudaStream_t stream) {
+  CUtensorMap tg, tx;
+  if (!gs_tmap(&tg, gy, t, m) || !gs_tmap(&tx, x, t, n)) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(gradsq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GS_SMEM);
+  if (e != cudaSuccess) return e;
+  const GsArgs args{m, n, t, h, w, sums};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * ((m + 255) / 256)), (unsigned)((n + 255) / 256), 1);
+  cfg.blockDim = dim3(OE_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = GS_SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, gradsq_kernel, tg, tx, args);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 cudaError_t launch_outerr(const uint16_t* x, const uint16_t* w, const uint16_t* xq, const uint16_t* wq, int64_t batch,
                           int64_t rows, int64_t out, int64_t K, double* err_sum, double* ref_energy, float* d_ref,
                           float* d_q, cudaStream_t stream) {
