@@ -191,13 +191,22 @@ def install_routed_expert_hooks(model: nn.Module, accumulator: dict) -> dict[str
 
 
 class FisherAccumulator:
-    """sensitivity_probe.py:959-1241 with the per-token estimator and device accumulators."""
+    """sensitivity_probe.py:959-1241 with the per-token estimator and device accumulators.
+
+    With `h_detail_dir`, every backward of a tracked Linear also forms the reference's per-weight
+    Fisher diagonal on the tensor cores (pq_grad_sq_acc: grad_w = bf16(gy^T x), h_full +=
+    bf16(grad_w^2)), so the Linear's stats are the reference's exact ones (h_trace_raw = the sum
+    over backwards of bf16(sum grad_w^2), h_w2_sum_raw likewise with bf16(w^2)) rather than the
+    per-token estimate, and finalize writes the reference's h_detail files (sensitivity_probe.py:
+    1114-1152, 1200-1235) for measure_quant_cost's predicted_dloss."""
 
     def __init__(self, model: nn.Module, tracked: list[str], expert_info: dict[str, tuple[str, str]],
                  act_cache_dir: Path | None = None, input_rows: int = 256, hook_packed_experts: bool = True,
                  h_detail_dir: Path | None = None, packed_estimator: str = "grad_norm"):
-        if h_detail_dir is not None:
-            raise NotImplementedError("per-weight Fisher detail needs grad_w = gy^T x (a GEMM); not on the B200 path")
+        self.h_detail_dir = Path(h_detail_dir) if h_detail_dir else None
+        self._detail = self.h_detail_dir is not None
+        self._saved_inputs: dict[str, torch.Tensor] = {}
+        self._h_full: dict[str, torch.Tensor] = {}
         self.stats: dict[str, dict] = {}
         self.tracked = set(tracked)
         self.expert_info = expert_info
@@ -215,6 +224,14 @@ class FisherAccumulator:
         dev = lin[0][1].weight.device if lin else torch.device("cuda")
         # one [n, 2] fp64 accumulator (raw trace, tokens) per tracked Linear
         self._acc = torch.zeros(len(lin), 2, dtype=torch.float64, device=dev)
+        if self._detail:
+            odd = [n for n, m in lin if m.in_features % 8 or m.out_features % 8]
+            if odd:
+                raise NotImplementedError(f"per-weight Fisher detail needs in/out features that are multiples of 8: {odd}")
+            # (trace, w^2 sum) per Linear, each backward's sums rounded to bf16 as the reference's
+            # .sum() of a bf16 tensor returns them; and one scratch pair per backward
+            self._exact = torch.zeros(len(lin), 2, dtype=torch.float64, device=dev)
+            self._call_sums = torch.zeros(2, dtype=torch.float64, device=dev)
         wstats = []
         for i, (name, mod) in enumerate(lin):
             self._names.append(name)
@@ -226,7 +243,7 @@ class FisherAccumulator:
                                 "out_features": mod.out_features, "n_tokens_seen": 0, "route_prob": None,
                                 "router_path": router, "expert_id": eid}
             self._fwd_handles.append(mod.register_forward_hook(self._make_fwd(name)))
-            self._bwd_handles.append(mod.register_full_backward_hook(self._make_bwd(name, i)))
+            self._bwd_handles.append(mod.register_full_backward_hook(self._make_bwd(name, i, mod)))
         if wstats:
             host = torch.stack(wstats).cpu().tolist()   # one sync for every Linear's weight stats
             for (name, _), (mx, n2) in zip(lin, host):
@@ -259,7 +276,10 @@ class FisherAccumulator:
         def hook(module, inp, out):
             x = inp[0] if isinstance(inp, tuple) else inp
             x2 = x.detach().reshape(-1, x.size(-1))
-            self._xnorm[name] = _lib.rownorm2(x2)
+            if self._detail:
+                self._saved_inputs[name] = x2   # the reference's saved input (:1094)
+            else:
+                self._xnorm[name] = _lib.rownorm2(x2)
             if self.cache_dir is not None:
                 need = self.input_rows - self._rows_got[name]
                 if need > 0:
@@ -270,9 +290,25 @@ class FisherAccumulator:
                     self._rows_got[name] += flat.size(0)
         return hook
 
-    def _make_bwd(self, name: str, idx: int):
+    def _make_bwd(self, name: str, idx: int, mod: nn.Linear):
         def hook(module, grad_input, grad_output):
             gy = grad_output[0]
+            if self._detail:
+                x2 = self._saved_inputs.pop(name, None)
+                if x2 is None or gy is None:
+                    return
+                gy2 = gy.reshape(-1, gy.size(-1))
+                h = self._h_full.get(name)
+                if h is None:
+                    h = self._h_full[name] = torch.zeros(mod.out_features, mod.in_features, dtype=torch.float32,
+                                                         device=gy2.device)
+                w = mod.weight
+                wd = w.detach() if (w is not None and not w.is_meta) else None
+                self._call_sums.zero_()
+                _lib.grad_sq_acc(gy2, x2, h, self._call_sums, wd)
+                self._exact[idx] += self._call_sums.float().to(torch.bfloat16).double()
+                self._acc[idx, 1] += gy2.size(0)
+                return
             xn = self._xnorm.pop(name, None)
             if xn is None or gy is None:
                 return
@@ -286,8 +322,13 @@ class FisherAccumulator:
 
     def finalize(self, tracker=None):
         host = self._acc.cpu().tolist()
-        for name, (tr, tok) in zip(self._names, host):
-            self.stats[name]["h_trace_raw"] += tr
+        exact = self._exact.cpu().tolist() if self._detail else [None] * len(host)
+        for name, (tr, tok), ex in zip(self._names, host, exact):
+            if ex is not None:   # the reference's exact statistics
+                self.stats[name]["h_trace_raw"] += ex[0]
+                self.stats[name]["h_w2_sum_raw"] += ex[1]
+            else:
+                self.stats[name]["h_trace_raw"] += tr
             self.stats[name]["n_tokens_seen"] += int(round(tok))
         for full, raw in self._packed_grad_acc.items():
             if full not in self.stats:
@@ -315,6 +356,28 @@ class FisherAccumulator:
                     X = torch.cat(snaps).to(torch.bfloat16).contiguous()
                     torch.save({"inputs": X, "name": name},
                                self.cache_dir / (re.sub(r"[^A-Za-z0-9_-]", "__", name) + ".pt"))
+        if self.h_detail_dir is not None:   # sensitivity_probe.py:1200-1235, the same files and keys
+            self.h_detail_dir.mkdir(parents=True, exist_ok=True)
+            sub = re.compile(r"[^A-Za-z0-9_-]")
+            for name, acc in self._h_full.items():
+                if name not in self.stats:
+                    continue
+                tokens = max(self.stats[name]["n_tokens_seen"], 1)
+                rp = self.stats[name].get("route_prob")
+                h = acc.to(torch.float32).cpu() / (tokens * rp if (rp is not None and rp > 0) else tokens)
+                fname = sub.sub("__", name) + ".pt"
+                torch.save({"h_diag": h, "name": name, "kind": "linear", "shape": list(h.shape)},
+                           self.h_detail_dir / fname)
+                self.stats[name]["h_detail_path"] = fname
+            for full_name, ch in self._h_packed_channel.items():
+                if full_name not in self.stats:
+                    continue
+                tokens = max(self.stats[full_name]["n_tokens_seen"], 1)
+                h = ch.to(torch.float32).cpu() / tokens
+                fname = sub.sub("__", full_name) + ".pt"
+                torch.save({"h_diag": h, "name": full_name, "kind": "packed", "shape": list(h.shape)},
+                           self.h_detail_dir / fname)
+                self.stats[full_name]["h_detail_path"] = fname
 
     def remove_hooks(self):
         for h in self._fwd_handles + self._bwd_handles:
@@ -343,6 +406,7 @@ def probe_pass(model: nn.Module, calib: torch.Tensor, tracked: list[str], batch_
         loss = -lp.gather(1, ids[:, 1:].reshape(-1, 1)).sum()
         loss.backward()
         acc._xnorm.clear()
+        acc._saved_inputs.clear()
     if all_reduce is not None:
         all_reduce(acc.trace_buffer)
     return acc

@@ -210,6 +210,46 @@ def fisher_bridge():
     return out
 
 
+def fisher_detail():
+    """FisherAccumulator with h_detail_dir on a toy bf16 model, several tokens per backward: each
+    backward's inputs and output gradients, the h_diag files the reference writes and its exact
+    stats (h_trace_raw = sum of bf16(grad_w)^2, h_w2_sum_raw, n_tokens_seen)."""
+    import tempfile
+    torch.manual_seed(5)
+    model = torch.nn.Sequential(torch.nn.Linear(64, 48, bias=False), torch.nn.Linear(48, 32, bias=False))
+    model = model.to(torch.bfloat16)
+    tracked = ["0", "1"]
+    out = {}
+    with tempfile.TemporaryDirectory() as d:
+        acc = sp.FisherAccumulator(model, tracked, {}, hook_packed_experts=False, h_detail_dir=Path(d))
+        xs, gys = {n: [] for n in tracked}, {n: [] for n in tracked}
+        mods = dict(model.named_modules())
+        hooks = []
+        for n in tracked:
+            hooks.append(mods[n].register_forward_hook(lambda m, i, o, n=n: xs[n].append(i[0].detach().clone())))
+            hooks.append(mods[n].register_full_backward_hook(
+                lambda m, gi, go, n=n: gys[n].append(go[0].detach().clone())))
+        inputs = torch.randn(5, 16, 64).to(torch.bfloat16)
+        for i in range(inputs.shape[0]):
+            y = model(inputs[i])
+            y.float().pow(2).sum().backward()
+        acc.finalize(None)
+        for h in hooks:
+            h.remove()
+        for n in tracked:
+            blob = torch.load(Path(d) / (n + ".pt"), weights_only=False)
+            out[f"detail/{n}/x"] = torch.stack(xs[n]).view(torch.int16).numpy()
+            out[f"detail/{n}/gy"] = torch.stack(gys[n]).view(torch.int16).numpy()
+            out[f"detail/{n}/w"] = mods[n].weight.detach().view(torch.int16).numpy()
+            out[f"detail/{n}/h_diag"] = blob["h_diag"].numpy()
+            out[f"detail/{n}/kind"] = np.array([blob["kind"]])
+            for k in ("h_trace_raw", "h_w2_sum_raw"):
+                out[f"detail/{n}/{k}"] = np.array([acc.stats[n][k]], dtype=np.float64)
+            out[f"detail/{n}/n_tokens_seen"] = np.array([acc.stats[n]["n_tokens_seen"]], dtype=np.int64)
+            out[f"detail/{n}/h_detail_path"] = np.array([acc.stats[n]["h_detail_path"]])
+    return out
+
+
 def known_answers():
     out = {}
     v = torch.tensor([0.25, 0.75, -0.75, 1.25, -1.25, 2.5, -2.5, 5.0, -5.0, -0.0, -0.1, 0.0, 0.5, 1.0, 6.0, -6.0, 7.0, -7.0])
@@ -231,6 +271,9 @@ def cost_pipeline():
 
 
 def main():
+    if "fisher_detail" in sys.argv[1:]:   # only the per-weight Fisher fixture
+        np.savez_compressed(HERE / "fisher_detail.npz", **fisher_detail())
+        return
     arrays = {}
     for name, bits in small_cases().items():
         arrays[f"{name}/input"] = bits

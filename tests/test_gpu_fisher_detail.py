@@ -76,3 +76,85 @@ def test_validation():
     h = torch.zeros(12, 16, dtype=torch.float32, device="cuda")
     with pytest.raises(ValueError):
         _lib.grad_sq_acc(gy, x, h, torch.zeros(2, dtype=torch.float64, device="cuda"))   # m = 12
+
+
+from pathlib import Path   # noqa: E402
+
+import numpy as np   # noqa: E402
+
+DETAIL = Path(__file__).resolve().parent / "golden" / "fisher_detail.npz"
+
+
+def _t(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).view(torch.bfloat16).cuda()
+
+
+@pytest.mark.parametrize("n", ["0", "1"])
+def test_kernel_against_reference_fixture(n):
+    """Each recorded backward of the reference's FisherAccumulator (tests/golden/fisher_detail.npz)
+    through pq_grad_sq_acc, its sums rounded to bf16 per backward as the reference's .sum() of a
+    bf16 tensor: h_diag and the exact stats against the reference's own outputs.  The reference
+    ran on the CPU (its bf16 GEMM accumulates in another order), so a few grad_w roundings differ."""
+    from prismaquant_b200 import _lib
+    d = np.load(DETAIL)
+    x, gy, w = _t(d[f"detail/{n}/x"]), _t(d[f"detail/{n}/gy"]), _t(d[f"detail/{n}/w"])
+    h = torch.zeros(w.shape, dtype=torch.float32, device="cuda")
+    trace = w2 = 0.0
+    for c in range(x.shape[0]):
+        s = torch.zeros(2, dtype=torch.float64, device="cuda")
+        _lib.grad_sq_acc(gy[c], x[c], h, s, w)
+        trace += s.float().to(torch.bfloat16).double()[0].item()
+        w2 += s.float().to(torch.bfloat16).double()[1].item()
+    tokens = int(d[f"detail/{n}/n_tokens_seen"][0])
+    got = (h.cpu() / tokens).numpy()
+    want = d[f"detail/{n}/h_diag"]
+    assert (got == want).mean() >= 0.9
+    np.testing.assert_allclose(got, want, rtol=2.0 ** -5, atol=1e-6 * float(np.abs(want).max()))
+    assert trace == pytest.approx(float(d[f"detail/{n}/h_trace_raw"][0]), rel=2.0 ** -7)
+    assert w2 == pytest.approx(float(d[f"detail/{n}/h_w2_sum_raw"][0]), rel=2.0 ** -7)
+
+
+def test_accumulator_writes_the_reference_detail_files(tmp_path):
+    """FisherAccumulator(h_detail_dir=...) on the fixture's toy model on the GPU: the reference's
+    file names and keys, stats with h_detail_path and the exact trace, and values equal to the
+    reference's algorithm run in torch on the same GPU activations."""
+    from prismaquant_b200 import sensitivity_probe as sp
+    d = np.load(DETAIL)
+    model = torch.nn.Sequential(torch.nn.Linear(64, 48, bias=False), torch.nn.Linear(48, 32, bias=False))
+    model = model.to(device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        for n in ("0", "1"):
+            model.get_submodule(n).weight.copy_(_t(d[f"detail/{n}/w"]))
+    tracked = ["0", "1"]
+    acc = sp.FisherAccumulator(model, tracked, {}, hook_packed_experts=False, h_detail_dir=tmp_path)
+    xs, gys = {n: [] for n in tracked}, {n: [] for n in tracked}
+    hooks = []
+    for n in tracked:
+        m = model.get_submodule(n)
+        hooks.append(m.register_forward_hook(lambda mm, i, o, n=n: xs[n].append(i[0].detach().clone())))
+        hooks.append(m.register_full_backward_hook(lambda mm, gi, go, n=n: gys[n].append(go[0].detach().clone())))
+    inputs = _t(d["detail/0/x"])
+    for c in range(inputs.shape[0]):
+        model(inputs[c]).float().pow(2).sum().backward()
+    acc.finalize(None)
+    for h in hooks:
+        h.remove()
+    for n in tracked:
+        blob = torch.load(tmp_path / f"{n}.pt", weights_only=False)
+        assert set(blob) == {"h_diag", "name", "kind", "shape"} and blob["kind"] == "linear" and blob["name"] == n
+        assert acc.stats[n]["h_detail_path"] == f"{n}.pt" and acc.stats[n]["n_tokens_seen"] == 80
+        # the reference's algorithm (sensitivity_probe.py:1120-1141) in torch on the same activations
+        h_ref = torch.zeros(blob["shape"], dtype=torch.float32, device="cuda")
+        tr = w2 = 0.0
+        wd = model.get_submodule(n).weight.detach()
+        for x, gy in zip(xs[n], gys[n]):
+            g2 = (gy.reshape(-1, gy.shape[-1]).t() @ x.reshape(-1, x.shape[-1])).pow(2)
+            h_ref += g2.float()
+            tr += float(g2.sum())
+            w2 += float((g2 * wd.pow(2)).sum())
+        got, want = blob["h_diag"].numpy(), (h_ref.cpu() / 80).numpy()
+        assert (got == want).mean() >= 0.9
+        np.testing.assert_allclose(got, want, rtol=2.0 ** -5, atol=1e-6 * float(np.abs(want).max()))
+        assert acc.stats[n]["h_trace_raw"] == pytest.approx(tr, rel=2.0 ** -7)
+        assert acc.stats[n]["h_w2_sum_raw"] == pytest.approx(w2, rel=2.0 ** -7)
+        assert acc.stats[n]["h_trace"] == pytest.approx(acc.stats[n]["h_trace_raw"] / 80)
