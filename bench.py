@@ -44,6 +44,8 @@ def parse():
                              "costtable8b"])
     ap.add_argument("--fisher-seqs", type=int, default=64, help="calibration sequences (split across ranks)")
     ap.add_argument("--fisher-batch", type=int, default=4, help="sequences per backward on each rank")
+    ap.add_argument("--fisher-detail", action="store_true",
+                    help="per-weight Fisher diagonal (h_detail) on the tensor cores, the reference's exact stats")
     ap.add_argument("--outerr-layers", type=int, default=32,
                     help="decoder layers whose Linears the output-error workload stacks by shape")
     ap.add_argument("--no-e2e", action="store_true")
@@ -100,8 +102,14 @@ def run_fisher(a, rank, world, local):
         return w
     sp._lib.rownorm2 = timed(orig_rn, lambda x: x.numel() * 2 + (x.numel() // x.shape[-1]) * 4)
     sp._lib.tokennorm_dot = timed(orig_td, lambda g_, xn, acc, token_idx=None: g_.numel() * 2 + xn.numel() * 4)
+    detail_dir = None
+    if a.fisher_detail:   # the tensor-core per-weight diagonal: work counted in FLOP (2 t m n)
+        import tempfile
+        detail_dir = tempfile.mkdtemp(prefix="pq_hdetail_")
+        orig_gs = _lib.grad_sq_acc
+        sp._lib.grad_sq_acc = timed(orig_gs, lambda gy, x, h, sums, w=None: 2 * gy.shape[0] * gy.shape[1] * x.shape[1])
 
-    acc = sp.FisherAccumulator(model, tracked, {})
+    acc = sp.FisherAccumulator(model, tracked, {}, h_detail_dir=detail_dir)
     model.train()
     emb = model.get_input_embeddings()
 
@@ -115,6 +123,7 @@ def run_fisher(a, rank, world, local):
         loss = -lp.gather(1, ids[:, 1:].reshape(-1, 1)).sum()
         loss.backward()
         acc._xnorm.clear()
+        acc._saved_inputs.clear()
         if world > 1:
             D.all_reduce_traces(acc.trace_buffer.clone())
 
@@ -141,19 +150,30 @@ def run_fisher(a, rank, world, local):
     tokens = world * a.steps * B * 2048
     hbm, peak_kind = peaks()
     achieved = kbytes[0] / (kern_ms / 1e3) / 1e9 if kern_ms > 0 else 0.0
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+            "kernel": "rownorm2 + tokennorm_dot (hook kernels)",
+            "kernel_ms_per_step": round(kern_ms / a.steps, 4), "hook_share_of_step": round(kern_ms / ms, 4)}
+    if a.fisher_detail:
+        try:
+            tf_peak = float(json.loads(PEAKS.read_text())["bf16_tflops"])
+        except Exception:
+            tf_peak = 1590.0
+        tf = kbytes[0] / (kern_ms / 1e3) / 1e12 if kern_ms > 0 else 0.0
+        roof = {"bound": "tensor", "achieved": round(tf, 1), "peak": tf_peak, "unit": "TFLOP/s",
+                "frac": round(tf / tf_peak, 4), "traffic": None, "peak_kind": "measured (burst)",
+                "kernel": "gradsq_kernel (per-weight Fisher diagonal, tcgen05)",
+                "kernel_ms_per_step": round(kern_ms / a.steps, 4), "hook_share_of_step": round(kern_ms / ms, 4)}
     if rank == 0:
         print(json.dumps({
             "metric": "Fisher probe tokens/s (fwd+bwd with per-token trace hooks)", "value": round(tokens / (ms_max / 1e3), 1),
             "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": round(ms_max / a.steps, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic: random-init weights, uniform token ids",
-            "config": {"workload": "llama1b_fisher_probe", "seq_len": 2048, "seqs_per_step_per_rank": B,
-                       "tracked_linears": len(tracked), "parallelism": f"data-parallel x{world}, traces all-reduced"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
-                         "kernel": "rownorm2 + tokennorm_dot (hook kernels)",
-                         "kernel_ms_per_step": round(kern_ms / a.steps, 4),
-                         "hook_share_of_step": round(kern_ms / ms, 4)},
+            "config": {"workload": "llama1b_fisher_probe" + ("_h_detail" if a.fisher_detail else ""),
+                       "seq_len": 2048, "seqs_per_step_per_rank": B, "tracked_linears": len(tracked),
+                       "parallelism": f"data-parallel x{world}, traces all-reduced"},
+            "roofline": roof,
             "clocks": clk.summary(), "gpu_launches": len(kev)}), flush=True)
     if world > 1:
         dist.barrier()
