@@ -65,3 +65,26 @@ def all_gather_costs(local_ids: torch.Tensor, local_sse: torch.Tensor, n_units: 
 def all_reduce_traces(buf: torch.Tensor, group=None) -> torch.Tensor:
     dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
     return buf
+
+
+def all_reduce_fisher(acc, group=None):
+    """Sum, in place over the ranks of a data-parallel probe, everything a FisherAccumulator holds
+    before finalize: the (trace, tokens) buffer; with h_detail_dir also the exact (trace, w^2)
+    sums and each per-weight diagonal; and the packed-expert accumulators.  Tensors are reduced in
+    sorted name order, so every rank issues the same collectives.  Afterwards every rank's
+    finalize gives the same stats; call it with file output on one rank only."""
+    dist.all_reduce(acc._acc, op=dist.ReduceOp.SUM, group=group)
+    if getattr(acc, "_detail", False):
+        dist.all_reduce(acc._exact, op=dist.ReduceOp.SUM, group=group)
+        for name in sorted(acc._h_full):
+            dist.all_reduce(acc._h_full[name], op=dist.ReduceOp.SUM, group=group)
+    for store in (acc._packed_grad_acc, acc._h_packed_channel, acc._packed_sample_count):
+        for name in sorted(store):
+            v = store[name]
+            if isinstance(v, torch.Tensor):
+                dist.all_reduce(v, op=dist.ReduceOp.SUM, group=group)
+            else:   # a Python float (scalar grad-norm accumulator)
+                t = torch.tensor([float(v)], dtype=torch.float64, device=acc._acc.device)
+                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+                store[name] = float(t.item())
+    return acc

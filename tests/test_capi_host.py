@@ -161,6 +161,62 @@ def _gloo_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _gloo_fisher_worker(rank, world, port, q, detail_dir):
+    import os
+    import torch
+    import torch.distributed as dist
+    from prismaquant_b200 import distributed as D
+    from prismaquant_b200 import sensitivity_probe as sp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        model = torch.nn.Sequential(torch.nn.Linear(16, 8, bias=False), torch.nn.Linear(8, 24, bias=False))
+        acc = sp.FisherAccumulator(model, ["0", "1"], {}, hook_packed_experts=False,
+                                   h_detail_dir=detail_dir if rank == 0 else detail_dir + f"_{rank}")
+        # what each rank's backwards would have left: rank-dependent values
+        acc._acc += torch.tensor([[0.0, 10.0], [0.0, 10.0]], dtype=torch.float64) * (rank + 1)
+        acc._exact += torch.tensor([[1.0, 0.5], [2.0, 0.25]], dtype=torch.float64) * (rank + 1)
+        acc._h_full["0"] = torch.full((8, 16), float(rank + 1))
+        acc._h_full["1"] = torch.full((24, 8), 2.0 * (rank + 1))
+        D.all_reduce_fisher(acc)
+        if rank == 0:
+            acc.finalize(None)
+            blob = torch.load(os.path.join(detail_dir, "0.pt"), weights_only=False)
+            q.put((rank, acc.stats["0"]["h_trace_raw"], acc.stats["1"]["h_w2_sum_raw"], acc.stats["0"]["n_tokens_seen"],
+                   float(blob["h_diag"][0, 0]), acc.stats["1"]["h_detail_path"]))
+        else:
+            q.put((rank, float(acc._exact[0, 0]), float(acc._h_full["1"][0, 0]), None, None, None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_fisher_detail_reduce(tmp_path):
+    """all_reduce_fisher on two gloo ranks: the exact sums, tokens and per-weight diagonals add up,
+    and rank 0's finalize writes the reference's h_detail files from the summed values."""
+    import multiprocessing as mp
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    d = str(tmp_path / "hd")
+    procs = [ctx.Process(target=_gloo_fisher_worker, args=(r, 2, port, q, d)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    r0, r1 = res
+    assert r0[1:4] == (3.0, 0.75, 30)            # trace 1+2, w^2 sum 0.25*(1+2), tokens 10+20
+    assert r0[4] == pytest.approx(3.0 / 30)      # h_diag = summed h_full / summed tokens
+    assert r0[5] == "1.pt"
+    assert r1[1:3] == (3.0, 6.0)
+
+
 def test_gloo_two_ranks_gather_and_reduce():
     import multiprocessing as mp
     import socket
