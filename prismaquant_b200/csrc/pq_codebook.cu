@@ -17,6 +17,7 @@
 // These formats are not on the fused hot path; one warp per row is plenty.
 // The same kernel (which can also describe NVFP4, MXFP8 and FP8 per channel)
 // computes the H-weighted error sum behind predicted_dloss.
+#include <type_traits>
 #include "pq_common.cuh"
 #include "pq_internal.h"
 
@@ -255,6 +256,57 @@ __device__ __forceinline__ float xk_round(float x, int bits) {
   }
 }
 
+// MX reconstruction of 8 elements without the generic rounding, for a group scale 2^es with
+// |es| <= 100 and no NaN among the 8 (w holds their bf16 bits, wv their values):
+//  - |w| >= 2^(EMIN+es) (the format's normal range): the grid point is w rounded to M mantissa
+//    bits, ties to the lower signed value (up in magnitude for a negative w), saturated at
+//    MAXV 2^es — integer arithmetic on the bf16 magnitudes, two per word (a magnitude plus the
+//    rounding increment stays below 0x10000, so no carry crosses into the other half);
+//  - |w| < 2^(EMIN+es): t = |w| + 2^(EMIN+es) lies in the binade of 2^(EMIN+es), and t rounded
+//    to MS mantissa bits (MS = M with subnormals, 0 without: then only 0 and 2^EMIN) minus
+//    2^(EMIN+es) is the grid point.  The sum is exact wherever it can reach a rounding
+//    boundary (|w| >= 2^(EMIN+es-4) there); a smaller |w| rounds to 0 either way.
+// Every grid point times 2^es is a bf16, so this is bf16(q 2^es) of the generic rule, with +0 for
+// a negative w that rounds to zero.
+template <int KIND>
+__device__ __forceinline__ void mx_rec8(const uint4& u, const float (&wv)[8], int es, float (&rec)[8]) {
+  using K = XK<KIND>;
+  constexpr int MS = K::SUB ? K::M : 0;
+  constexpr uint32_t DROP = 7 - K::M;
+  constexpr uint32_t HALF = ((1u << (DROP - 1)) - 1u) * 0x00010001u;
+  constexpr uint32_t MASK = ((0xFFFFu >> DROP) << DROP) * 0x00010001u;
+  constexpr uint32_t HALF32 = (1u << (22 - MS)) - 1u;
+  constexpr uint32_t MASK32 = ~((1u << (23 - MS)) - 1u);
+  const float cw = pow2i(K::EMIN + es);
+  const uint32_t satb = (__float_as_uint(K::MAXV) >> 16) + ((uint32_t)es << 7);
+  const uint32_t sat2 = (satb & 0xFFFFu) * 0x00010001u;
+  const uint32_t words[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t v = words[p];
+    const uint32_t neg = (v >> 15) & 0x00010001u;
+    const uint32_t m = __vminu2(((v & 0x7FFF7FFFu) + HALF + neg) & MASK, sat2);
+    const float big[2] = {__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u)};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = 2 * p + h;
+      const float a = fabsf(wv[i]);
+      const uint32_t ng = (v >> (15 + 16 * h)) & 1u;
+      const float t = __fadd_rn(a, cw);
+      const float small = __fsub_rn(__uint_as_float((__float_as_uint(t) + HALF32 + ng) & MASK32), cw);
+      const float mag = a < cw ? small : big[h];
+      rec[i] = ng ? __fsub_rn(0.0f, mag) : mag;
+    }
+  }
+}
+
+// NaN among 8 bf16 values: a magnitude above 0x7F80 in some half
+__device__ __forceinline__ bool has_nan8(const uint4& u) {
+  const uint32_t t = (((u.x & 0x7FFF7FFFu) + 0x007F007Fu) | ((u.y & 0x7FFF7FFFu) + 0x007F007Fu) |
+                      ((u.z & 0x7FFF7FFFu) + 0x007F007Fu) | ((u.w & 0x7FFF7FFFu) + 0x007F007Fu));
+  return (t & 0x80008000u) != 0u;
+}
+
 template <int MODE, int KIND>
 __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__ w, int64_t rows, int64_t cols,
                                                     int fmt, double* sse, uint16_t* out,
@@ -265,6 +317,7 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const bool grouped = f.group > 0 && f.group < cols;
+  constexpr bool MXK = KIND != XK_INT && KIND != XK_E2M0;   // kinds some MX format uses
   double acc = 0.0;
 
   // scale of a group with maximum a, and the factor x = w * inv or w / scale
@@ -274,7 +327,10 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
     return s;
   };
   // 8 elements at flat index idx (row r): reconstruction, error, optional W_hat store
-  auto do8 = [&](const float (&wv)[8], int64_t idx, int64_t r, float scale, float inv) {
+  // fast: MX group in range, reconstructions by mx_rec8, whose errors w - rec are bf16 already
+  auto do8 = [&](const uint4& u, const float (&wv)[8], int64_t idx, int64_t r, float scale, float inv,
+                 auto fast) {
+    constexpr bool FAST = decltype(fast)::value;
     float hv[8];
     if (h_mode == 1) {
       const float4 h0 = __ldg(reinterpret_cast<const float4*>(h + idx));
@@ -288,12 +344,20 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
     }
     float part = 0.0f;
     uint32_t o[4];
+    float recv[8];
+    if constexpr (FAST && KIND != XK_INT) {
+      mx_rec8<(KIND == XK_INT ? XK_E2M1 : KIND)>(u, wv, (int)(__float_as_uint(scale) >> 23) - 127, recv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = inv != 0.0f ? __fmul_rn(wv[i], inv) : __fdiv_rn(wv[i], scale);
+        recv[i] = bf16_round(__fmul_rn(xk_round<KIND>(x, f.bits), scale));
+      }
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float x = inv != 0.0f ? __fmul_rn(wv[i], inv) : __fdiv_rn(wv[i], scale);
-      const float q = xk_round<KIND>(x, f.bits);
-      const float rec = bf16_round(__fmul_rn(q, scale));
-      const float e = bf16_round(__fsub_rn(wv[i], rec));
+      const float rec = recv[i];
+      const float e = FAST ? __fsub_rn(wv[i], rec) : bf16_round(__fsub_rn(wv[i], rec));
       const float e2 = __fmul_rn(e, e);   // the reference squares in fp32, then weights
       part = h_mode == 0 ? __fadd_rn(part, e2) : fmaf(hv[i], e2, part);
       if (MODE == MODE_QDQ) {
@@ -321,7 +385,13 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
       for (int o = 1; o < gl; o <<= 1) a = fmaxf(a, __shfl_xor_sync(FULL, a, o));
       float inv;
       const float scale = scale_of(a, inv);
-      if (valid) do8(wv, r * cols + col, r, scale, inv);
+      if (valid) {
+        // an MX group in range with no NaN among the lane's 8 takes the integer reconstruction
+        if (MXK && f.mx && scale >= 0x1p-100f && scale <= 0x1p100f && !has_nan8(u))
+          do8(u, wv, r * cols + col, r, scale, inv, std::true_type{});
+        else
+          do8(u, wv, r * cols + col, r, scale, inv, std::false_type{});
+      }
     }
   } else {
     // one scale per row: the warp reduces the row maximum, then scores the row
@@ -338,8 +408,9 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
       const float scale = scale_of(a, inv);
       for (int64_t col = lane * 8; col < cols; col += 256) {
         float wv[8];
-        unpack8(__ldg(reinterpret_cast<const uint4*>(row + col)), wv);
-        do8(wv, r * cols + col, r, scale, inv);
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + col));
+        unpack8(u, wv);
+        do8(u, wv, r * cols + col, r, scale, inv, std::false_type{});
       }
     }
   }

@@ -106,7 +106,11 @@ __device__ __forceinline__ int e8m0_round(float s) {
   const uint32_t u = __float_as_uint(s);
   const int k = (int)(u >> 23) - 127;
   const int m = (int)(u & 0x7FFFFFu);
-  const int e = m >= PQ_ROUND_FIRST[k + 126] ? k + 1 : k;
+  // the thresholds of all binades lie in [PQ_ROUND_FIRST_MIN, PQ_ROUND_FIRST_MAX]: outside that
+  // window the mantissa decides alone, and the per-lane indexed table read (which serializes
+  // over the distinct binades of a warp) is skipped
+  int e = m >= PQ_ROUND_FIRST_MAX ? k + 1 : k;
+  if (m >= PQ_ROUND_FIRST_MIN && m < PQ_ROUND_FIRST_MAX) e = m >= PQ_ROUND_FIRST[k + 126] ? k + 1 : k;
   return max(-127, min(127, e));
 }
 
@@ -118,6 +122,8 @@ __device__ __forceinline__ int e8m0_ceil(float s) {
   const int m = (int)(u & 0x7FFFFFu);
   if (be > 0) {
     const int k = be - 127;
+    if (m <= PQ_CEIL_LAST_MIN) return k;                      // as e8m0_round: the table only
+    if (m > PQ_CEIL_LAST_MAX) return min(127, k + 1);         // inside the thresholds' window
     return min(127, m <= PQ_CEIL_LAST[k + 127] ? k : k + 1);
   }
   if (m >= (1 << 22)) return (m - (1 << 22)) <= PQ_CEIL_LAST[0] ? -127 : -126;
