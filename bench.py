@@ -344,6 +344,7 @@ def run_kernels(a, local):
     acc2 = torch.zeros(2, dtype=torch.float64, device=dev)
     sse = torch.zeros(1, 4, dtype=torch.float64, device=dev)
     s0 = torch.zeros((), dtype=torch.float64, device=dev)
+    s3 = torch.zeros(3, dtype=torch.float64, device=dev)
     codes = torch.empty(R, C // 2, dtype=torch.uint8, device=dev)
     amax = torch.empty(R, C // 16, dtype=torch.int16, device=dev)
     tmax = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -373,6 +374,8 @@ def run_kernels(a, local):
         table.append((f"xfmt2_kernel format_sse {f}", (lambda f=f: _lib.format_sse(W, f, s0)), 2 * n, "GB/s"))
     table += [
         ("xfmt2_kernel weighted_sse NVFP4 (predicted_dloss)", lambda: _lib.weighted_sse(W, "NVFP4", H, s0), 6 * n, "GB/s"),
+        ("sweep_fast_kernel weighted NVFP4+MXFP8+FP8-channel (predicted_dloss)",
+         lambda: _lib.weighted_sse_fused(W, _lib.FUSED_FMTS, H, s3), 6 * n, "GB/s"),
         ("rownorm2 (Fisher forward hook)", lambda: _lib.rownorm2(X), X.numel() * 2 + X.shape[0] * 4, "GB/s"),
         ("tokennorm_dot (Fisher backward hook)", lambda: _lib.tokennorm_dot(X, xnorm, acc2), X.numel() * 2 + X.shape[0] * 4,
          "GB/s"),

@@ -136,6 +136,19 @@ int pq_weighted_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, cons
                     double* sse, void* stream);
 
 /*
+ * pq_weighted_sse for several of the fused formats from one read of W and H:
+ * fmt_mask is a subset of PQ_FMT_BIT(PQ_FMT_NVFP4) | PQ_FMT_BIT(PQ_FMT_MXFP8) |
+ * PQ_FMT_BIT(PQ_FMT_FP8_CHANNEL), and sse[f] receives what pq_weighted_sse of
+ * format f would add, for each f in the mask (the other entries are left
+ * alone).  h as for pq_weighted_sse (16-byte aligned for the one-read path).
+ * No counterpart in the reference's API as a single call; it serves
+ * measure_batched_gpu's per-format predicted_dloss
+ * (measure_quant_cost.py:638-640).
+ */
+int pq_weighted_sse_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_t fmt_mask, const float* h,
+                          int h_per_row, double* sse, void* stream);
+
+/*
  * Output error of a quantized Linear, on the tensor cores:
  *   y_ref = bf16(X W^T), y_q = bf16(X_hat W_hat^T)  (bf16 operands, fp32 accumulate)
  * ADDS sum(bf16(y_ref - y_q)^2) to err_sse[b] and sum(y_ref^2) to ref_sse[b]

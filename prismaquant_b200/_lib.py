@@ -31,7 +31,7 @@ EXPORTED = [
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
-    "pq_grad_sq_acc",
+    "pq_weighted_sse_fused", "pq_grad_sq_acc",
 ]
 
 
@@ -67,6 +67,7 @@ def load() -> ctypes.CDLL:
         "pq_sweep_sse": [ctypes.POINTER(SweepTensor), I, P, V],
         "pq_cost_qdq": [P, I64, I64, I, P, V],
         "pq_cost_qdq_fused": [P, I64, I64, ctypes.c_uint32, P, V],
+        "pq_weighted_sse_fused": [P, I64, I64, ctypes.c_uint32, P, I, P, V],
         "pq_format_sse": [P, I64, I64, I, P, V],
         "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
         "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
@@ -245,6 +246,35 @@ def weighted_sse(w: torch.Tensor, fmt: str, h: torch.Tensor, sse: torch.Tensor, 
         raise ValueError(f"weighted_sse: h has {hh.numel()} values for a [{rows}, {cols}] weight")
     _check(load().pq_weighted_sse(_ptr(wb), rows, cols, FMT_IDS[fmt], _ptr(hh), int(per_row), _ptr(sse),
                                   _stream(wb)), "pq_weighted_sse", f"cannot reshape rows of {cols} into groups for {fmt}")
+
+
+def weighted_sse_fused(w: torch.Tensor, fmts, h: torch.Tensor, sse: torch.Tensor | None = None,
+                       per_row: bool = False) -> torch.Tensor:
+    """weighted_sse of several of NVFP4 / MXFP8 / FP8_E4M3 (per channel) from one read of W and h:
+    adds each format's sum into sse[FMT_IDS[fmt]] of the fp64 device vector `sse` (3 entries; a
+    new zero vector when None) and returns it."""
+    wb = as_bf16_cuda(w, "weighted_sse")
+    want = [f for f in FUSED_FMTS if f in set(fmts)]
+    if len(want) != len(set(fmts)) or not want:
+        raise ValueError(f"weighted_sse_fused: formats must be among {FUSED_FMTS}, got {list(fmts)}")
+    if sse is None:
+        sse = torch.zeros(3, dtype=torch.float64, device=wb.device)
+    _check_sums(sse, 3, wb.device, "weighted_sse_fused")
+    if wb.numel() == 0:
+        return sse
+    cols = wb.shape[-1]
+    rows = wb.numel() // cols
+    hh = h.detach()
+    if hh.device != wb.device or hh.dtype != torch.float32:
+        raise TypeError("weighted_sse_fused: h must be float32 on the weight's device")
+    hh = hh.contiguous()
+    if hh.numel() != (rows if per_row else rows * cols):
+        raise ValueError(f"weighted_sse_fused: h has {hh.numel()} values for a [{rows}, {cols}] weight")
+    mask = sum(1 << FMT_IDS[f] for f in want)
+    _check(load().pq_weighted_sse_fused(_ptr(wb), rows, cols, mask, _ptr(hh), int(per_row), _ptr(sse),
+                                        _stream(wb)),
+           "pq_weighted_sse_fused", f"cannot reshape rows of {cols} into groups for {want}")
+    return sse
 
 
 def output_sse(x: torch.Tensor, w: torch.Tensor, x_hat: torch.Tensor, w_hat: torch.Tensor,

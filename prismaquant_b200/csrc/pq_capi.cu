@@ -220,6 +220,34 @@ int pq_weighted_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, cons
                                      (cudaStream_t)stream_, h, h_per_row ? 2 : 1));
 }
 
+int pq_weighted_sse_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_t fmt_mask, const float* h,
+                          int h_per_row, double* sse, void* stream_) {
+  if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (fmt_mask == 0 || (fmt_mask & ~(NV | MX | F8))) return PQ_ERR_FORMAT;
+  const int st0 = check_groups(cols, fmt_mask);
+  if (st0) return st0;
+  if (rows == 0) return PQ_OK;
+  if (!w || !h || !sse) return PQ_ERR_NULL;
+  if (staged_ok(w, cols, fmt_mask) && (h_per_row || aligned(h, 16))) {   // one read of W and H
+    std::vector<pq::SweepDesc> v(1);
+    memset(&v[0], 0, sizeof(pq::SweepDesc));
+    v[0].w = w;
+    v[0].rows = rows;
+    v[0].cols = cols;
+    v[0].fmt_mask = fmt_mask;
+    v[0].sse = sse;
+    v[0].h = h;
+    v[0].h_per_row = h_per_row ? 1 : 0;
+    return launch_batch(v, pq::MODE_SSE, 0, fmt_mask | 32u, (cudaStream_t)stream_);
+  }
+  for (int f = 0; f < 3; ++f) {   // other shapes: one format at a time
+    if (!(fmt_mask & (1u << f))) continue;
+    const int st = pq_weighted_sse(w, rows, cols, f, h, h_per_row, sse + f, stream_);
+    if (st) return st;
+  }
+  return PQ_OK;
+}
+
 // Shapes the output-error kernels take: k % 8 == 0 (16-byte tensor-map strides), grid limits.
 static int outerr_shape(int64_t batch, int64_t rows, int64_t out, int64_t k) {
   if (batch < 0 || rows < 0 || out < 0 || k < 1 || (k & 7)) return PQ_ERR_SHAPE;

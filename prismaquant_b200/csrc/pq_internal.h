@@ -29,6 +29,8 @@ struct SweepDesc {
   uint32_t* nvfp4_tmax;
   uint16_t* out;  // QDQ output
   double* sse;    // 4 doubles (one per pq_format)
+  const float* h;     // weighted sums (fast sweep, key bit 32): H per element, or per row
+  int32_t h_per_row;
 };
 
 struct SweepLaunch {
@@ -37,6 +39,7 @@ struct SweepLaunch {
   int64_t item_prefix[MAX_SWEEP_TENSORS + 1];
   SweepDesc t[MAX_SWEEP_TENSORS];
 };
+static_assert(sizeof(SweepLaunch) <= 32764, "a SweepLaunch is passed as one kernel parameter block");
 
 size_t sweep_smem_bytes();
 size_t sweep_fast_smem_bytes();

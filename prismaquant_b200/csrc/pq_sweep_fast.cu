@@ -133,6 +133,35 @@ __device__ __forceinline__ float f8_pair_sq(uint32_t v, uint32_t cl, uint64_t s2
   return sq2_acc(bf16x2_sub(v, rec), 0.0f);
 }
 
+// Weighted sums (predicted_dloss, measure_quant_cost.py:638-640: sum(H * err^2) with err the
+// bf16 difference): H of the item's elements, one value per element or one per row.
+struct HRef {
+  const float* el;    // per element, from the item's first element (null: per row)
+  const float* row;   // per row, from the item's first row
+  int upr;
+  uint32_t rdiv;
+  // H of element k (0..15, element order) of unit u
+  __device__ __forceinline__ float at(int u, int k) const {
+    return el ? __ldg(el + 16 * (int64_t)u + k)
+              : __ldg(row + (upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)));
+  }
+};
+
+// acc + h_lo e_lo^2 + h_hi e_hi^2 for a bf16 error pair (exact squares)
+__device__ __forceinline__ float wsq2_acc(uint32_t e, float hlo, float hhi, float acc) {
+  const float lo = __uint_as_float(e << 16), hi = __uint_as_float(e & 0xFFFF0000u);
+  acc = __fmaf_rn(hlo, __fmul_rn(lo, lo), acc);
+  return __fmaf_rn(hhi, __fmul_rn(hi, hi), acc);
+}
+__device__ __forceinline__ float nv_pair_wsq(uint32_t v, uint32_t cl, uint64_t s2, float h0, float h1) {
+  const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e2m1x2_to_f2(cl), s2));
+  return wsq2_acc(bf16x2_sub(v, rec), h0, h1, 0.0f);
+}
+__device__ __forceinline__ float f8_pair_wsq(uint32_t v, uint32_t cl, uint64_t s2, float h0, float h1) {
+  const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(cl), s2));
+  return wsq2_acc(bf16x2_sub(v, rec), h0, h1, 0.0f);
+}
+
 // NVFP4 pair whose bracket codes cl != ch: exact cost code (ties to the lower
 // value, so toward larger magnitude for negative w) and export code (ties
 // toward zero).
@@ -183,7 +212,9 @@ __device__ __forceinline__ uint32_t f8_resolve_pair(uint32_t vp, uint32_t cl, ui
 // Units outside the fast path's range (amax below the 1e-8 scale floor, or
 // large enough for an fp32 square to overflow): every element by IEEE
 // division and the exact tie rules.  The main loop contributed nothing.
-__device__ __noinline__ double nv_exact_unit(const uint32_t* vw, float a16, uint8_t* cu, bool cost, uint32_t* ou) {
+// H (weighted sums): the unit's weights, u its index; null for plain sums.
+__device__ __noinline__ double nv_exact_unit(const uint32_t* vw, float a16, uint8_t* cu, bool cost, uint32_t* ou,
+                                            const HRef* H = nullptr, int u = 0) {
   const float s = __fdiv_rn(fmaxf(a16, 1e-8f), 6.0f);
   const float se = fmaxf(__fdiv_rn(fmaxf(a16, 1e-12f), 6.0f), 1e-12f);   // export scale
   double delta = 0.0;
@@ -193,7 +224,12 @@ __device__ __noinline__ double nv_exact_unit(const uint32_t* vw, float a16, uint
     if (cost || ou) {
       const float r0 = bf16_round(__fmul_rn(rtn_e2m1_cost(__fdiv_rn(w0, s)), s));
       const float r1 = bf16_round(__fmul_rn(rtn_e2m1_cost(__fdiv_rn(w1, s)), s));
-      if (cost) delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
+      if (cost && H) {
+        delta += (double)__fmaf_rn(H->at(u, 2 * p), sq_exact_err(w0, r0),
+                                   __fmul_rn(H->at(u, 2 * p + 1), sq_exact_err(w1, r1)));
+      } else if (cost) {
+        delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
+      }
       if (ou) ou[p] = (__float_as_uint(r0) >> 16) | (__float_as_uint(r1) & 0xFFFF0000u);
     }
     if (cu) cu[p] = (uint8_t)(nvfp4_code(__fdiv_rn(w0, se)) | (nvfp4_code(__fdiv_rn(w1, se)) << 4));
@@ -201,14 +237,19 @@ __device__ __noinline__ double nv_exact_unit(const uint32_t* vw, float a16, uint
   return delta;
 }
 
-__device__ __noinline__ double f8_exact_unit(const uint32_t* vw, float s, uint32_t* ou) {
+__device__ __noinline__ double f8_exact_unit(const uint32_t* vw, float s, uint32_t* ou, const HRef* H = nullptr,
+                                            int u = 0) {
   double delta = 0.0;
   for (int p = 0; p < 8; ++p) {
     const uint32_t vp = vw[p];
     const float w0 = bf16lo(vp), w1 = bf16hi(vp);
     const float r0 = bf16_round(__fmul_rn(rtn_e4m3_cost(__fdiv_rn(w0, s)), s));
     const float r1 = bf16_round(__fmul_rn(rtn_e4m3_cost(__fdiv_rn(w1, s)), s));
-    delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
+    if (H)
+      delta += (double)__fmaf_rn(H->at(u, 2 * p), sq_exact_err(w0, r0),
+                                 __fmul_rn(H->at(u, 2 * p + 1), sq_exact_err(w1, r1)));
+    else
+      delta += (double)(sq_exact_err(w0, r0) + sq_exact_err(w1, r1));
     if (ou) ou[p] = (__float_as_uint(r0) >> 16) | (__float_as_uint(r1) & 0xFFFF0000u);
   }
   return delta;
@@ -233,9 +274,11 @@ __device__ __forceinline__ int warp_incl_scan(int x, int lane) {
 // busiest lane.  Each resolved pair adds its exact squared errors minus the
 // main loop's provisional ones and rewrites its export code byte.
 // Task word: pair (bits 0-2) | unit (3-14) | group amax bf16 bits (15-29).
+// HW: weighted sums, H the item's weights.
+template <bool HW = false>
 __device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
                                                int lane, int64_t elem0, uint8_t* codes, bool cost, uint32_t* tasks,
-                                               uint32_t* outw) {
+                                               uint32_t* outw, HRef H = HRef{}) {
   const int cnt = c0 + c1;   // entries q0[0..c0) then q1[0..c1)
   double delta = 0.0;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
@@ -251,7 +294,7 @@ __device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, cons
       const float a16 = __uint_as_float(a16b << 16);
       if (exact_unit(a16)) {
         delta += nv_exact_unit(words + 8 * u, a16, codes ? codes + (elem0 + 16 * (int64_t)u) / 2 : nullptr, cost,
-                               outw ? outw + (elem0 + 16 * (int64_t)u) / 2 : nullptr);
+                               outw ? outw + (elem0 + 16 * (int64_t)u) / 2 : nullptr, HW ? &H : nullptr, u);
       } else {
         const float s = div_const(a16, 6.0f, RCP6);
         float rlo, rhi;
@@ -283,7 +326,12 @@ __device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, cons
       uint32_t cl, ch, cx, ce;
       nv_bracket(f2_from_bf16x2(vp), rlo2, rhi2, cl, ch);
       nv_resolve_pair(vp, cl, ch, s, cx, ce);
-      if (cost && cx != cl) dl += nv_pair_sq(vp, cx, s2) - nv_pair_sq(vp, cl, s2);
+      if (HW && cost && cx != cl) {
+        const float h0 = H.at(uu, 2 * p), h1 = H.at(uu, 2 * p + 1);
+        dl += nv_pair_wsq(vp, cx, s2, h0, h1) - nv_pair_wsq(vp, cl, s2, h0, h1);
+      } else if (cost && cx != cl) {
+        dl += nv_pair_sq(vp, cx, s2) - nv_pair_sq(vp, cl, s2);
+      }
       if (outw && cx != cl) outw[(elem0 + 16 * (int64_t)uu) / 2 + p] = nv_pair_rec(cx, s2);
       if (codes) codes[(elem0 + 16 * (int64_t)uu) / 2 + p] = (uint8_t)ce;
     }
@@ -294,9 +342,10 @@ __device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, cons
 }
 
 // Task word: pair (bits 0-2) | unit (3-14).
+template <bool HW = false>
 __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
                                                int lane, const uint32_t* ramax, int upr, uint32_t rdiv,
-                                               uint32_t* tasks, int64_t elem0, uint32_t* outw) {
+                                               uint32_t* tasks, int64_t elem0, uint32_t* outw, HRef H = HRef{}) {
   const int cnt = c0 + c1;
   double delta = 0.0;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
@@ -308,7 +357,8 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, cons
       u = (int)(i < c0 ? q0[i] : q1[i - c0]);
       const RowParam rp = row_param(ramax[upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)]);
       if (rp.amax >= F8_EXACT_ROW_AMAX) {
-        delta += f8_exact_unit(words + 8 * u, rp.s, outw ? outw + (elem0 + 16 * (int64_t)u) / 2 : nullptr);
+        delta += f8_exact_unit(words + 8 * u, rp.s, outw ? outw + (elem0 + 16 * (int64_t)u) / 2 : nullptr,
+                               HW ? &H : nullptr, u);
       } else {
         const uint4 a = st[2 * u], b = st[2 * u + 1];
         const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -336,7 +386,12 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, cons
       const uint64_t w2 = f2_from_bf16x2(vp);
       const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2, rlo2)), ch = cvt_e4m3x2(f2_mul_rz(w2, rhi2));
       const uint32_t cx = f8_resolve_pair(vp, cl, ch, rp.s);
-      if (cx != cl) dl += f8_pair_sq(vp, cx, s2) - f8_pair_sq(vp, cl, s2);
+      if (HW && cx != cl) {
+        const float h0 = H.at(uu, 2 * p), h1 = H.at(uu, 2 * p + 1);
+        dl += f8_pair_wsq(vp, cx, s2, h0, h1) - f8_pair_wsq(vp, cl, s2, h0, h1);
+      } else if (cx != cl) {
+        dl += f8_pair_sq(vp, cx, s2) - f8_pair_sq(vp, cl, s2);
+      }
       if (outw && cx != cl) outw[(elem0 + 16 * (int64_t)uu) / 2 + p] = f8_pair_rec(cx, s2);
     }
     delta += (double)dl;
@@ -347,13 +402,16 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, cons
 
 // Out-of-line copies for the rare early flush inside the per-unit loops (the
 // loop bodies stay small); the end-of-item resolution inlines the bodies.
+template <bool HW>
 __device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
-                                        uint8_t* codes, bool cost, uint32_t* tasks, uint32_t* outw) {
-  return nv_fixup_body(q, cnt, q, 0, st, lane, elem0, codes, cost, tasks, outw);
+                                        uint8_t* codes, bool cost, uint32_t* tasks, uint32_t* outw, HRef H) {
+  return nv_fixup_body<HW>(q, cnt, q, 0, st, lane, elem0, codes, cost, tasks, outw, H);
 }
+template <bool HW>
 __device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
-                                        int upr, uint32_t rdiv, uint32_t* tasks, int64_t elem0, uint32_t* outw) {
-  return f8_fixup_body(q, cnt, q, 0, st, lane, ramax, upr, rdiv, tasks, elem0, outw);
+                                        int upr, uint32_t rdiv, uint32_t* tasks, int64_t elem0, uint32_t* outw,
+                                        HRef H) {
+  return f8_fixup_body<HW>(q, cnt, q, 0, st, lane, ramax, upr, rdiv, tasks, elem0, outw, H);
 }
 
 // Tensor index of item `item`, scanning forward from the previous one (items
@@ -384,7 +442,23 @@ struct ItemCtx {
   uint32_t* outw;        // NVFP4
   uint32_t* outw_mx;     // MXFP8
   uint32_t* outw_f8;     // FP8 per channel
+  HRef h;                // weighted launches: the item's H
 };
+
+// H of unit u's 16 elements in load_unit's order (16-byte halves swapped when sw)
+__device__ __forceinline__ void load_unit_h(const HRef& H, int u, bool sw, float (&h)[16]) {
+  if (H.el) {
+    const float4* p = reinterpret_cast<const float4*>(H.el + 16 * (int64_t)u);
+    const float4 a = __ldg(p + (sw ? 2 : 0)), b = __ldg(p + (sw ? 3 : 1));
+    const float4 c = __ldg(p + (sw ? 0 : 2)), d = __ldg(p + (sw ? 1 : 3));
+    h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w; h[4] = b.x; h[5] = b.y; h[6] = b.z; h[7] = b.w;
+    h[8] = c.x; h[9] = c.y; h[10] = c.z; h[11] = c.w; h[12] = d.x; h[13] = d.y; h[14] = d.z; h[15] = d.w;
+  } else {
+    const float x = H.at(u, 0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) h[i] = x;
+  }
+}
 
 struct Accum {
   float nv, mx, f8;
@@ -399,13 +473,16 @@ __device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
 
 // Pass A over one unit: NVFP4 cost and export codes, MXFP8 cost, and (when the
 // FP8 format is on) the unit's contribution to its row maximum.
-template <bool NV, bool MX, bool F8, bool CODES, bool OUT>
+// HW: sums weighted by H (per element or per row).
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW>
 __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, bool warp_rows,
                                             uint32_t* q_nv, Accum& A) {
   const bool valid = u < c.nunits;
   const int uc = valid ? u : c.nunits - 1;
   uint32_t v[8];
   const bool sw = load_unit(c.st, uc, true, lane, v);
+  float hv[16];
+  if (HW && (NV || MX)) load_unit_h(c.h, uc, sw, hv);
   uint32_t a16b, amin = 0;
   if (MX) unit_absmax_min(v, a16b, amin); else a16b = unit_absmax(v);
   const float a16 = __uint_as_float(a16b << 16);
@@ -437,6 +514,8 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       for (int p = 0; p < 8; ++p) {
         const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
         if (OUT) recw[p] = bf16x2_plus_zero(rec);
+        else if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[p], rec), hv[2 * p], hv[2 * p + 1], po);
+        else if (HW) pe = wsq2_acc(bf16x2_sub(v[p], rec), hv[2 * p], hv[2 * p + 1], pe);
         else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
         else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
       }
@@ -458,8 +537,8 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       A.cnt_nv += __popc(bal);
       if (A.cnt_nv > FAST_QCAP - 32) {   // flush early only when the next unit could overflow
         __syncwarp();
-        A.dnv += nv_fixup(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? c.codes_it - c.elem0 / 2 : nullptr, NV && !OUT,
-                          c.tasks, c.outw);
+        A.dnv += nv_fixup<HW>(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? c.codes_it - c.elem0 / 2 : nullptr,
+                              NV && !OUT, c.tasks, c.outw, c.h);
         __syncwarp();
         A.cnt_nv = 0;
       }
@@ -486,6 +565,8 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
                               : ((v[p] + 0x00080008u) & 0xFFF0FFF0u);
       const uint32_t q = bf16x2_minabs(rq, m448x2);                   // saturate |q| at 448 * 2^e
       if (OUT) recw[p] = bf16x2_plus_zero(q);
+      else if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[p], q), hv[2 * p], hv[2 * p + 1], po);
+      else if (HW) pe = wsq2_acc(bf16x2_sub(v[p], q), hv[2 * p], hv[2 * p + 1], pe);
       else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], q), po);
       else pe = sq2_acc(bf16x2_sub(v[p], q), pe);
     }
@@ -494,13 +575,18 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       Chunk8 c0, c1;
       unit_to_chunks(v, c0, c1);
       uint32_t rec[8];
-      if (OUT) {
+      if (OUT || HW) {
         (void)mxfp8_cost8(c0, a32, rec);
 #pragma unroll
         for (int i = 0; i < 4; ++i) recw[i] = rec[2 * i] | (rec[2 * i + 1] << 16);
         (void)mxfp8_cost8(c1, a32, rec);
 #pragma unroll
         for (int i = 0; i < 4; ++i) recw[4 + i] = rec[2 * i] | (rec[2 * i + 1] << 16);
+        if (HW) {
+          part = 0.0f;
+#pragma unroll
+          for (int p = 0; p < 8; ++p) part = wsq2_acc(bf16x2_sub(v[p], recw[p]), hv[2 * p], hv[2 * p + 1], part);
+        }
       } else {
         part = mxfp8_cost8(c0, a32, rec) + mxfp8_cost8(c1, a32, rec);
       }
@@ -524,13 +610,15 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
 }
 
 // Pass B over one unit: FP8 per-channel cost with the completed row maximum.
-template <bool OUT>
+template <bool OUT, bool HW>
 __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, uint32_t* q_f8,
                                             Accum& A) {
   const bool valid = u < c.nunits;
   const int uc = valid ? u : c.nunits - 1;
   uint32_t v[8];
   const bool sw = load_unit(c.st, uc, true, lane, v);
+  float hv[16];
+  if (HW) load_unit_h(c.h, uc, sw, hv);
   const RowParam rp = row_param(c.ramax[row_of(c, uc)]);
   const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
   const bool exf = rp.amax >= F8_EXACT_ROW_AMAX;
@@ -552,9 +640,12 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
-      if (OUT) recw[4 * hf + p] = bf16x2_plus_zero(rec);
-      else if (p & 1) po = sq2_acc(bf16x2_sub(v[4 * hf + p], rec), po);
-      else pe = sq2_acc(bf16x2_sub(v[4 * hf + p], rec), pe);
+      const int pp = 4 * hf + p;
+      if (OUT) recw[pp] = bf16x2_plus_zero(rec);
+      else if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], po);
+      else if (HW) pe = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], pe);
+      else if (p & 1) po = sq2_acc(bf16x2_sub(v[pp], rec), po);
+      else pe = sq2_acc(bf16x2_sub(v[pp], rec), pe);
     }
   }
   if (OUT) {   // uncertain pairs and exact-path rows are rewritten by the fix-ups
@@ -569,7 +660,7 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
     A.cnt_f8 += __popc(bal);
     if (A.cnt_f8 > FAST_QCAP - 32) {
       __syncwarp();
-      A.df8 += f8_fixup(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0, c.outw_f8);
+      A.df8 += f8_fixup<HW>(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0, c.outw_f8, c.h);
       __syncwarp();
       A.cnt_f8 = 0;
     }
@@ -584,7 +675,7 @@ __device__ __forceinline__ void fold(float& f, double& d) {
   f = 0.0f;
 }
 
-template <bool NV, bool MX, bool F8, bool CODES, bool OUT>
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW>
 __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __grid_constant__ SweepLaunch L) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int NWARPS = FAST_THREADS / 32;
@@ -684,6 +775,10 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     c.amax_it = CODES ? d.nvfp4_amax + c.elem0 / 16 : nullptr;
     c.ramax = ramax_buf + (j & 1) * FAST_MAX_ROWS;
     c.tasks = tasks;
+    c.h.el = (HW && !d.h_per_row) ? d.h + c.elem0 : nullptr;
+    c.h.row = (HW && d.h_per_row) ? d.h + it.r0 : nullptr;
+    c.h.upr = c.upr;
+    c.h.rdiv = c.rdiv;
     {
       const int64_t slot = d.rows * d.cols / 2;   // words of one W_hat
       uint32_t* base = OUT ? reinterpret_cast<uint32_t*>(d.out) : nullptr;
@@ -697,7 +792,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     if (NV || MX || CODES || F8) {
 #pragma unroll 1
       for (int k = 0; k < iters; ++k) {   // not unrolled: the body stays small enough for the instruction cache
-        unit_pass_a<NV, MX, F8, CODES, OUT>(c, tid + k * FAST_THREADS, lane, lanemask_lt, warp_rows, q_nv, A);
+        unit_pass_a<NV, MX, F8, CODES, OUT, HW>(c, tid + k * FAST_THREADS, lane, lanemask_lt, warp_rows, q_nv, A);
         if ((k & 3) == 3) {   // fp32 partials hold <= 64 squares
           fold(A.nv, A.dnv);
           fold(A.mx, A.dmx);
@@ -716,7 +811,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       for (int i = tid; i < FAST_MAX_ROWS; i += FAST_THREADS) next[i] = 0u;
 #pragma unroll 1
       for (int k = 0; k < iters; ++k) {
-        unit_pass_b<OUT>(c, tid + k * FAST_THREADS, lane, lanemask_lt, q_f8, A);
+        unit_pass_b<OUT, HW>(c, tid + k * FAST_THREADS, lane, lanemask_lt, q_f8, A);
         if ((k & 3) == 3) fold(A.f8, A.df8);
       }
       fold(A.f8, A.df8);
@@ -736,20 +831,20 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       if ((warp & 1) == 0) {
         const int pc = qcnt[2 * pw];
         if ((NV || CODES) && A.cnt_nv + pc)
-          A.dnv += nv_fixup_body(q_nv, A.cnt_nv, pq, pc, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
-                                 NV && !OUT, c.tasks, c.outw);
+          A.dnv += nv_fixup_body<HW>(q_nv, A.cnt_nv, pq, pc, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
+                                     NV && !OUT, c.tasks, c.outw, c.h);
       } else {
         const int pc = qcnt[2 * pw + 1];
-        if (A.cnt_f8 + pc) A.df8 += f8_fixup_body(q_f8, A.cnt_f8, pq + FAST_QCAP, pc, c.st, lane, c.ramax, c.upr,
-                                                  c.rdiv, c.tasks, c.elem0, c.outw_f8);
+        if (A.cnt_f8 + pc) A.df8 += f8_fixup_body<HW>(q_f8, A.cnt_f8, pq + FAST_QCAP, pc, c.st, lane, c.ramax, c.upr,
+                                                      c.rdiv, c.tasks, c.elem0, c.outw_f8, c.h);
       }
     } else {
       if ((NV || CODES) && A.cnt_nv)
-        A.dnv += nv_fixup_body(q_nv, A.cnt_nv, q_nv, 0, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
-                               NV && !OUT, c.tasks, c.outw);
+        A.dnv += nv_fixup_body<HW>(q_nv, A.cnt_nv, q_nv, 0, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
+                                   NV && !OUT, c.tasks, c.outw, c.h);
       if (F8 && A.cnt_f8)
-        A.df8 += f8_fixup_body(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0,
-                               c.outw_f8);
+        A.df8 += f8_fixup_body<HW>(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0,
+                                   c.outw_f8, c.h);
     }
     A.cnt_nv = A.cnt_f8 = 0;
     __syncthreads();   // stage s and the queues are free again
@@ -775,21 +870,28 @@ size_t sweep_fast_smem_bytes() {
          (FAST_THREADS / 32) * (2 * FAST_QCAP + FAST_TASK_CAP + 2) * sizeof(uint32_t);
 }
 
-template <bool NV, bool MX, bool F8, bool CODES, bool OUT = false>
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT = false, bool HW = false>
 static cudaError_t launch_fast_t(const SweepLaunch& L, int grid, cudaStream_t stream) {
   const size_t smem = sweep_fast_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(sweep_fast_kernel<NV, MX, F8, CODES, OUT>,
+  cudaError_t e = cudaFuncSetAttribute(sweep_fast_kernel<NV, MX, F8, CODES, OUT, HW>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  sweep_fast_kernel<NV, MX, F8, CODES, OUT><<<grid, FAST_THREADS, smem, stream>>>(L);
+  sweep_fast_kernel<NV, MX, F8, CODES, OUT, HW><<<grid, FAST_THREADS, smem, stream>>>(L);
   return cudaGetLastError();
 }
 
 // All descriptors of L share the flag set `key` (format mask bits 0-2, bit 3 = NVFP4 codes, bit 4 =
 // W_hat of each format in the mask into each descriptor's `out`, one slice per format in format
-// order, no error sums).
+// order, no error sums; bit 5 = error sums weighted by each descriptor's `h`).
 cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cudaStream_t stream) {
-  switch (key & 31u) {
+  switch (key & 63u) {
+    case 32 | 1: return launch_fast_t<true, false, false, false, false, true>(L, grid, stream);
+    case 32 | 2: return launch_fast_t<false, true, false, false, false, true>(L, grid, stream);
+    case 32 | 3: return launch_fast_t<true, true, false, false, false, true>(L, grid, stream);
+    case 32 | 4: return launch_fast_t<false, false, true, false, false, true>(L, grid, stream);
+    case 32 | 5: return launch_fast_t<true, false, true, false, false, true>(L, grid, stream);
+    case 32 | 6: return launch_fast_t<false, true, true, false, false, true>(L, grid, stream);
+    case 32 | 7: return launch_fast_t<true, true, true, false, false, true>(L, grid, stream);
     case 16 | 1: return launch_fast_t<true, false, false, false, true>(L, grid, stream);
     case 16 | 2: return launch_fast_t<false, true, false, false, true>(L, grid, stream);
     case 16 | 3: return launch_fast_t<true, true, false, false, true>(L, grid, stream);

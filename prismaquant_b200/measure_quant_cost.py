@@ -261,6 +261,31 @@ def _fused_w_hats(W: torch.Tensor, specs) -> dict:
     return {name: hats[k] for k, names in by_kernel.items() for name in names}
 
 
+def _fused_predicted_dloss(W: torch.Tensor, specs, h: torch.Tensor, per_row: bool = False) -> dict:
+    """predicted_dloss of every spec whose batched RTN is NVFP4, MXFP8 or FP8 per channel, from one
+    read of each W[n] and h[n] (pq_weighted_sse_fused) when two or more of them are asked for:
+    {spec name: [0.5 * sum(h[n] * err^2) for each n]}; {} otherwise, or on a shape error (the
+    per-format path then reports each format's own error)."""
+    by_kernel: dict[str, list[str]] = {}
+    for spec in specs:
+        try:
+            k = batched_kernel_format(spec)
+        except Exception:
+            continue
+        if k in _lib.FUSED_FMTS:
+            by_kernel.setdefault(k, []).append(spec.name)
+    if len(by_kernel) < 2:
+        return {}
+    out = torch.zeros(W.size(0), 3, dtype=torch.float64, device=W.device)
+    try:
+        for n in range(W.size(0)):
+            _lib.weighted_sse_fused(W[n], list(by_kernel), h[n].float(), out[n], per_row=per_row)
+    except ValueError:
+        return {}
+    vals = (0.5 * out).cpu()
+    return {name: vals[:, _lib.FMT_IDS[k]].tolist() for k, names in by_kernel.items() for name in names}
+
+
 def _group_by_shape(model: nn.Module, target_names: set[str]):
     groups: dict[tuple[int, int], list[tuple[str, nn.Linear]]] = {}
     for name, mod in model.named_modules():
@@ -328,6 +353,8 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
             wmse = (_weight_mse_or_errors(list(W.unbind(0)), specs, _per_linear) if dtype == torch.bfloat16
                     else None)
             w_hat_pre = _fused_w_hats(W, specs) if dtype == torch.bfloat16 and not _per_linear else {}
+            dl_pre = (_fused_predicted_dloss(W, specs, h_stacked)
+                      if h_stacked is not None and dtype == torch.bfloat16 and not _per_linear else {})
             for spec in specs:
                 try:
                     if wmse is None and spec.weight_element_dtype != "bfloat16":
@@ -346,7 +373,9 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                     rel = out_mse / ref_energy.clamp_min(1e-12)
                     dl = None
                     if h_stacked is not None:   # 0.5 * sum(H * err^2) per Linear (measure_quant_cost.py:638-640)
-                        dl = _predicted_dloss(W, spec, h_stacked, per_row=False, per_linear=_per_linear)
+                        dl = dl_pre.get(spec.name)
+                        if dl is None:
+                            dl = _predicted_dloss(W, spec, h_stacked, per_row=False, per_linear=_per_linear)
                     om, rl = out_mse.cpu().tolist(), rel.cpu().tolist()
                     for j, name in enumerate(names):
                         wm = 0.0 if wmse is None else wmse[j][spec.name]
@@ -439,6 +468,8 @@ def _measure_packed_experts(model: nn.Module, target_names: set[str], specs: lis
             h = h_detail.load(name).to(dev).float()
             if tuple(h.shape) == (w.size(0), w.size(1)):
                 h_em = h
+        dl_pre = (_fused_predicted_dloss(w.unsqueeze(0), specs, h_em.unsqueeze(0), per_row=True)
+                  if h_em is not None and dtype == torch.bfloat16 else {})
         for spec in specs:
             v = res[name][spec.name]
             if isinstance(v, dict):
@@ -446,7 +477,8 @@ def _measure_packed_experts(model: nn.Module, target_names: set[str], specs: lis
                 continue
             dl = None
             if h_em is not None:   # 0.5 * N * sum(H_em * mean_n err^2) (measure_quant_cost.py:430-437)
-                dl = _predicted_dloss(w.unsqueeze(0), spec, h_em.unsqueeze(0), per_row=True, per_linear=False)[0]
+                dl = dl_pre[spec.name][0] if spec.name in dl_pre else \
+                    _predicted_dloss(w.unsqueeze(0), spec, h_em.unsqueeze(0), per_row=True, per_linear=False)[0]
             _accumulate_result(accum, name, spec.name, float(v), 0.0, 0.0, predicted_dloss=dl)
 
 

@@ -78,3 +78,60 @@ def test_weighted_sse_matches_oracle(fmt, per_row):
     else:
         want = _oracle_weighted(bits, fmt, h, per_row, batched=False)
     assert out.item() == pytest.approx(want, rel=1e-5)
+
+
+def _fused_cases():
+    from tests.test_gpu_cost import _tie_rows
+    ties = _tie_rows(800, seed=21)                                            # fix-ups of every format
+    tiny = (O.synthetic_weight_bits((8, 32), seed=5) & np.uint16(0x807F)) | np.uint16(0x0100)   # amax < 1e-8
+    huge = O.synthetic_weight_bits((4, 32), seed=6)
+    huge[:, 3] = np.uint16(0x5F80)                                           # 2^64: exact units and FP8 rows
+    return {
+        "ties_tiny_huge_836x32": np.concatenate([ties, tiny, huge]).astype(np.uint16),
+        "dense_300x4096": O.synthetic_weight_bits((300, 4096), seed=8, outlier_frac=0.002),
+        "rows_of_96_2x700x96": O.synthetic_weight_bits((2, 700, 96), seed=9),   # several rows per warp
+        "odd_cols_40x48": O.synthetic_weight_bits((40, 48), seed=10),          # no MXFP8 grouping
+        "narrow_12x8": O.synthetic_weight_bits((12, 8), seed=11),              # rows under one group
+    }
+
+
+@pytest.mark.parametrize("case", list(_fused_cases()))
+@pytest.mark.parametrize("fmts", [("NVFP4", "MXFP8", "FP8_E4M3"), ("NVFP4", "FP8_E4M3"), ("MXFP8",), ("FP8_E4M3",)])
+@pytest.mark.parametrize("per_row", [False, True])
+def test_weighted_sse_fused_matches_oracle(case, fmts, per_row):
+    """pq_weighted_sse_fused: every format's sum(h * err^2) from one read of W and h, against the
+    oracle (1e-5) and against pq_weighted_sse of the format alone (fp32 partial regrouping only);
+    shapes the one-read kernel does not take go format by format; MXFP8 on rows it cannot group
+    raises."""
+    from prismaquant_b200 import _lib
+    bits = _fused_cases()[case]
+    rows, cols = bits.size // bits.shape[-1], bits.shape[-1]
+    rng = np.random.default_rng(rows + cols)
+    h = rng.random(rows if per_row else (rows, cols), dtype=np.float32) * np.float32(4.0)
+    w, hc = to_cuda_bf16(bits), torch.from_numpy(h).cuda()
+    if "MXFP8" in fmts and cols > 32 and cols % 32:
+        with pytest.raises(ValueError):
+            _lib.weighted_sse_fused(w, fmts, hc, per_row=per_row)
+        return
+    got = _lib.weighted_sse_fused(w, fmts, hc, per_row=per_row).cpu().numpy()
+    for f in _lib.FUSED_FMTS:
+        v = got[_lib.FMT_IDS[f]]
+        if f not in fmts:
+            assert v == 0.0, f
+            continue
+        want = _oracle_weighted(bits.reshape(rows, cols), f, h, per_row, batched=False)
+        assert v == pytest.approx(want, rel=1e-5, abs=1e-30), (case, f)
+        one = torch.zeros((), dtype=torch.float64, device="cuda")
+        _lib.weighted_sse(w, f, hc, one, per_row=per_row)
+        assert v == pytest.approx(one.item(), rel=1e-6, abs=1e-30), (case, f)
+
+
+def test_weighted_sse_fused_rejects_other_formats():
+    from prismaquant_b200 import _lib
+    w = to_cuda_bf16(O.synthetic_weight_bits((4, 64), seed=1))
+    h = torch.ones(4, 64, device="cuda")
+    for fmts in [("MXFP4",), ("NVFP4", "BF16"), ()]:
+        with pytest.raises(ValueError):
+            _lib.weighted_sse_fused(w, fmts, h)
+    with pytest.raises(ValueError):
+        _lib.weighted_sse_fused(w, ("NVFP4",), torch.ones(5, device="cuda"), per_row=True)
