@@ -112,6 +112,19 @@ int pq_cost_qdq_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_t fm
                       void* stream);
 
 /*
+ * pq_cost_qdq_fused and the error sums of the same formats from one read of a
+ * stacked weight w [batch, rows, cols]: w_hat holds popcount(fmt_mask) bf16
+ * slices of batch*rows*cols, one per format in the mask in format order (each
+ * equal to pq_cost_qdq of its format), and sse [batch, 4] (fp64, device)
+ * receives, in column f of each row b, what pq_sweep_sse would add for
+ * format f of w[b].  No counterpart in the reference's API as a single call;
+ * it serves measure_batched_gpu, which needs both weight_mse and W_hat of each
+ * format for every Linear of a chunk (measure_quant_cost.py:628-632).
+ */
+int pq_cost_qdq_fused_sse(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint32_t fmt_mask,
+                          uint16_t* w_hat, double* sse, void* stream);
+
+/*
  * Sum of squared errors of one format over one bf16 tensor [rows, cols]:
  * ADDS sum((W - qdq_fmt(W))^2) (bf16 subtraction, fp32 square) to *sse
  * (fp64, device; zero it first).  fmt is one of PQ_FMT_MXFP4 ..

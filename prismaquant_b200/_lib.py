@@ -31,7 +31,7 @@ EXPORTED = [
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
-    "pq_weighted_sse_fused", "pq_grad_sq_acc",
+    "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_grad_sq_acc",
 ]
 
 
@@ -68,6 +68,7 @@ def load() -> ctypes.CDLL:
         "pq_cost_qdq": [P, I64, I64, I, P, V],
         "pq_cost_qdq_fused": [P, I64, I64, ctypes.c_uint32, P, V],
         "pq_weighted_sse_fused": [P, I64, I64, ctypes.c_uint32, P, I, P, V],
+        "pq_cost_qdq_fused_sse": [P, I64, I64, I64, ctypes.c_uint32, P, P, V],
         "pq_format_sse": [P, I64, I64, I, P, V],
         "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
         "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
@@ -217,6 +218,28 @@ def cost_qdq_fused(w: torch.Tensor, fmts) -> dict:
         _check(load().pq_cost_qdq_fused(_ptr(wb), wb.numel() // cols, cols, mask, _ptr(out), _stream(wb)),
                "pq_cost_qdq_fused", f"cannot reshape rows of {cols} into groups for {want}")
     return {f: out[i] for i, f in enumerate(want)}
+
+
+def cost_qdq_fused_sse(w: torch.Tensor, fmts) -> tuple[dict, torch.Tensor]:
+    """cost_qdq_fused of a stacked weight [batch, rows, cols] (a 2-D weight is batch 1) together
+    with each w[b]'s error sums, from one read of w: ({fmt: bf16 tensor of w's shape},
+    fp64 [batch, 4] device tensor whose column FMT_IDS[fmt] holds sum((w[b] - W_hat)^2))."""
+    wb = as_bf16_cuda(w, "quantize_dequantize")
+    want = [f for f in FUSED_FMTS if f in set(fmts)]
+    if len(want) != len(set(fmts)) or not want:
+        raise ValueError(f"cost_qdq_fused_sse: formats must be among {FUSED_FMTS}, got {list(fmts)}")
+    if wb.dim() not in (2, 3):
+        raise ValueError(f"cost_qdq_fused_sse: expected a [rows, cols] or [batch, rows, cols] weight, got "
+                         f"{tuple(wb.shape)}")
+    w3 = wb.unsqueeze(0) if wb.dim() == 2 else wb
+    batch, rows, cols = w3.shape
+    out = torch.empty((len(want),) + tuple(wb.shape), dtype=torch.bfloat16, device=wb.device)
+    sse = torch.zeros(batch, 4, dtype=torch.float64, device=wb.device)
+    if w3.numel():
+        mask = sum(1 << FMT_IDS[f] for f in want)
+        _check(load().pq_cost_qdq_fused_sse(_ptr(w3), batch, rows, cols, mask, _ptr(out), _ptr(sse), _stream(wb)),
+               "pq_cost_qdq_fused_sse", f"cannot reshape rows of {cols} into groups for {want}")
+    return {f: out[i] for i, f in enumerate(want)}, sse
 
 
 def format_sse(w: torch.Tensor, fmt: str, sse: torch.Tensor) -> None:

@@ -54,13 +54,16 @@ bool staged_ok(const uint16_t* w, int64_t cols, uint32_t mask) {
   return true;
 }
 
-int launch_batch(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, uint32_t key, cudaStream_t stream) {
+// out_slice: W_hat launches, elements between format slices (0: each descriptor's rows*cols).
+int launch_batch(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, uint32_t key, cudaStream_t stream,
+                 int64_t out_slice = 0) {
   size_t i = 0;
   const int sms = num_sms_current();
   while (i < descs.size()) {
     pq::SweepLaunch L;
     memset(&L, 0, sizeof(L));
     L.qdq_fmt = qfmt;
+    L.out_slice = out_slice;
     int64_t items = 0;
     int n = 0;
     for (; i < descs.size() && n < pq::MAX_SWEEP_TENSORS; ++i, ++n) {
@@ -283,6 +286,44 @@ int pq_cost_qdq_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_t fm
     ++slot;
   }
   return PQ_OK;
+}
+
+int pq_cost_qdq_fused_sse(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint32_t fmt_mask,
+                          uint16_t* w_hat, double* sse, void* stream_) {
+  if (batch < 0 || rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (fmt_mask == 0 || (fmt_mask & ~(NV | MX | F8))) return PQ_ERR_FORMAT;
+  const int st0 = check_groups(cols, fmt_mask);
+  if (st0) return st0;
+  if (batch == 0 || rows == 0) return PQ_OK;
+  if (!w || !w_hat || !sse) return PQ_ERR_NULL;
+  if (batch > 0x7fffffff) return PQ_ERR_LIMIT;
+  const int64_t per = rows * cols;
+  cudaStream_t stream = (cudaStream_t)stream_;
+  if (staged_ok(w, cols, fmt_mask) && aligned(w_hat, 16)) {   // one read of W: W_hat and the sums
+    std::vector<pq::SweepDesc> v((size_t)batch);
+    for (int64_t b = 0; b < batch; ++b) {
+      memset(&v[b], 0, sizeof(pq::SweepDesc));
+      v[b].w = w + b * per;
+      v[b].rows = rows;
+      v[b].cols = cols;
+      v[b].fmt_mask = fmt_mask;
+      v[b].out = w_hat + b * per;
+      v[b].sse = sse + 4 * b;
+    }
+    return launch_batch(v, pq::MODE_SSE, 0, fmt_mask | 16u | 64u, stream, batch * per);
+  }
+  // other shapes: the W_hat slices as pq_cost_qdq_fused writes them, the sums as pq_sweep_sse adds them
+  const int st = pq_cost_qdq_fused(w, batch * rows, cols, fmt_mask, w_hat, stream_);
+  if (st) return st;
+  std::vector<pq_sweep_tensor> ts((size_t)batch);
+  for (int64_t b = 0; b < batch; ++b) {
+    memset(&ts[b], 0, sizeof(pq_sweep_tensor));
+    ts[b].w = w + b * per;
+    ts[b].rows = rows;
+    ts[b].cols = cols;
+    ts[b].fmt_mask = fmt_mask;
+  }
+  return pq_sweep_sse(ts.data(), (int)batch, sse, stream_);
 }
 
 int pq_grad_sq_acc(const uint16_t* gy, const uint16_t* x, const uint16_t* w, int64_t t, int64_t m, int64_t n,

@@ -36,6 +36,7 @@ struct SweepDesc {
 struct SweepLaunch {
   int n;
   int qdq_fmt;
+  int64_t out_slice;   // W_hat launches: elements between format slices (0: each descriptor's rows*cols)
   int64_t item_prefix[MAX_SWEEP_TENSORS + 1];
   SweepDesc t[MAX_SWEEP_TENSORS];
 };

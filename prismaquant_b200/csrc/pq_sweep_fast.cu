@@ -473,8 +473,8 @@ __device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
 
 // Pass A over one unit: NVFP4 cost and export codes, MXFP8 cost, and (when the
 // FP8 format is on) the unit's contribution to its row maximum.
-// HW: sums weighted by H (per element or per row).
-template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW>
+// HW: sums weighted by H (per element or per row).  OSSE (with OUT): the error sums as well.
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW, bool OSSE>
 __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, bool warp_rows,
                                             uint32_t* q_nv, Accum& A) {
   const bool valid = u < c.nunits;
@@ -514,16 +514,16 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       for (int p = 0; p < 8; ++p) {
         const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
         if (OUT) recw[p] = bf16x2_plus_zero(rec);
-        else if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[p], rec), hv[2 * p], hv[2 * p + 1], po);
+        if (OUT && !OSSE) continue;
+        if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[p], rec), hv[2 * p], hv[2 * p + 1], po);
         else if (HW) pe = wsq2_acc(bf16x2_sub(v[p], rec), hv[2 * p], hv[2 * p + 1], pe);
         else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
         else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
       }
       if (OUT) {   // uncertain pairs and exact-path units are rewritten by the fix-ups
         if (valid) store_unit_words(c.outw + c.elem0 / 2, uc, sw, recw);
-      } else {
-        A.nv += (valid && !ex) ? pe + po : 0.0f;
       }
+      if (!OUT || OSSE) A.nv += (valid && !ex) ? pe + po : 0.0f;
     }
     if (CODES) {   // lanes past the end re-store the last unit's identical bytes
       reinterpret_cast<uint2*>(c.codes_it)[uc] = sw ? make_uint2(cw[1], cw[0]) : make_uint2(cw[0], cw[1]);
@@ -538,7 +538,7 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       if (A.cnt_nv > FAST_QCAP - 32) {   // flush early only when the next unit could overflow
         __syncwarp();
         A.dnv += nv_fixup<HW>(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? c.codes_it - c.elem0 / 2 : nullptr,
-                              NV && !OUT, c.tasks, c.outw, c.h);
+                              NV && (!OUT || OSSE), c.tasks, c.outw, c.h);
         __syncwarp();
         A.cnt_nv = 0;
       }
@@ -565,7 +565,8 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
                               : ((v[p] + 0x00080008u) & 0xFFF0FFF0u);
       const uint32_t q = bf16x2_minabs(rq, m448x2);                   // saturate |q| at 448 * 2^e
       if (OUT) recw[p] = bf16x2_plus_zero(q);
-      else if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[p], q), hv[2 * p], hv[2 * p + 1], po);
+      if (OUT && !OSSE) continue;
+      if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[p], q), hv[2 * p], hv[2 * p + 1], po);
       else if (HW) pe = wsq2_acc(bf16x2_sub(v[p], q), hv[2 * p], hv[2 * p + 1], pe);
       else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], q), po);
       else pe = sq2_acc(bf16x2_sub(v[p], q), pe);
@@ -576,12 +577,13 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       unit_to_chunks(v, c0, c1);
       uint32_t rec[8];
       if (OUT || HW) {
-        (void)mxfp8_cost8(c0, a32, rec);
+        const float p0 = mxfp8_cost8(c0, a32, rec);
 #pragma unroll
         for (int i = 0; i < 4; ++i) recw[i] = rec[2 * i] | (rec[2 * i + 1] << 16);
-        (void)mxfp8_cost8(c1, a32, rec);
+        const float p1 = mxfp8_cost8(c1, a32, rec);
 #pragma unroll
         for (int i = 0; i < 4; ++i) recw[4 + i] = rec[2 * i] | (rec[2 * i + 1] << 16);
+        if (OSSE) part = p0 + p1;
         if (HW) {
           part = 0.0f;
 #pragma unroll
@@ -593,9 +595,8 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
     }
     if (OUT) {
       if (valid) store_unit_words(c.outw_mx + c.elem0 / 2, uc, sw, recw);
-    } else {
-      A.mx += valid ? part : 0.0f;
     }
+    if (!OUT || OSSE) A.mx += valid ? part : 0.0f;
   }
 
   if (F8) {   // row maxima for pass B
@@ -610,7 +611,7 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
 }
 
 // Pass B over one unit: FP8 per-channel cost with the completed row maximum.
-template <bool OUT, bool HW>
+template <bool OUT, bool HW, bool OSSE>
 __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, uint32_t* q_f8,
                                             Accum& A) {
   const bool valid = u < c.nunits;
@@ -642,7 +643,8 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
       const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
       const int pp = 4 * hf + p;
       if (OUT) recw[pp] = bf16x2_plus_zero(rec);
-      else if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], po);
+      if (OUT && !OSSE) continue;
+      if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], po);
       else if (HW) pe = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], pe);
       else if (p & 1) po = sq2_acc(bf16x2_sub(v[pp], rec), po);
       else pe = sq2_acc(bf16x2_sub(v[pp], rec), pe);
@@ -650,9 +652,8 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
   }
   if (OUT) {   // uncertain pairs and exact-path rows are rewritten by the fix-ups
     if (valid) store_unit_words(c.outw_f8 + c.elem0 / 2, uc, sw, recw);
-  } else {
-    A.f8 += (valid && !exf) ? pe + po : 0.0f;
   }
+  if (!OUT || OSSE) A.f8 += (valid && !exf) ? pe + po : 0.0f;
   const bool need = valid && (ux != 0 || exf);
   const uint32_t bal = __ballot_sync(FULL, need);
   if (bal) {
@@ -675,7 +676,7 @@ __device__ __forceinline__ void fold(float& f, double& d) {
   f = 0.0f;
 }
 
-template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW>
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW, bool OSSE>
 __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __grid_constant__ SweepLaunch L) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int NWARPS = FAST_THREADS / 32;
@@ -742,7 +743,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       for (int f = 0; f < 3; ++f) {
         double x = lane < NWARPS ? red[lane * 3 + f] : 0.0;
         x = warp_sum_d(x);
-        if (!OUT && lane == 0 && (d.fmt_mask & (1u << f))) atomicAdd(d.sse + f, x);
+        if ((!OUT || OSSE) && lane == 0 && (d.fmt_mask & (1u << f))) atomicAdd(d.sse + f, x);
       }
     }
     __syncthreads();
@@ -780,7 +781,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     c.h.upr = c.upr;
     c.h.rdiv = c.rdiv;
     {
-      const int64_t slot = d.rows * d.cols / 2;   // words of one W_hat
+      const int64_t slot = (L.out_slice > 0 ? L.out_slice : d.rows * d.cols) / 2;   // words between slices
       uint32_t* base = OUT ? reinterpret_cast<uint32_t*>(d.out) : nullptr;
       c.outw = (OUT && NV) ? base : nullptr;
       c.outw_mx = (OUT && MX) ? base + (NV ? slot : 0) : nullptr;
@@ -792,7 +793,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     if (NV || MX || CODES || F8) {
 #pragma unroll 1
       for (int k = 0; k < iters; ++k) {   // not unrolled: the body stays small enough for the instruction cache
-        unit_pass_a<NV, MX, F8, CODES, OUT, HW>(c, tid + k * FAST_THREADS, lane, lanemask_lt, warp_rows, q_nv, A);
+        unit_pass_a<NV, MX, F8, CODES, OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, lanemask_lt, warp_rows, q_nv, A);
         if ((k & 3) == 3) {   // fp32 partials hold <= 64 squares
           fold(A.nv, A.dnv);
           fold(A.mx, A.dmx);
@@ -811,7 +812,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       for (int i = tid; i < FAST_MAX_ROWS; i += FAST_THREADS) next[i] = 0u;
 #pragma unroll 1
       for (int k = 0; k < iters; ++k) {
-        unit_pass_b<OUT, HW>(c, tid + k * FAST_THREADS, lane, lanemask_lt, q_f8, A);
+        unit_pass_b<OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, lanemask_lt, q_f8, A);
         if ((k & 3) == 3) fold(A.f8, A.df8);
       }
       fold(A.f8, A.df8);
@@ -832,7 +833,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
         const int pc = qcnt[2 * pw];
         if ((NV || CODES) && A.cnt_nv + pc)
           A.dnv += nv_fixup_body<HW>(q_nv, A.cnt_nv, pq, pc, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
-                                     NV && !OUT, c.tasks, c.outw, c.h);
+                                     NV && (!OUT || OSSE), c.tasks, c.outw, c.h);
       } else {
         const int pc = qcnt[2 * pw + 1];
         if (A.cnt_f8 + pc) A.df8 += f8_fixup_body<HW>(q_f8, A.cnt_f8, pq + FAST_QCAP, pc, c.st, lane, c.ramax, c.upr,
@@ -841,7 +842,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     } else {
       if ((NV || CODES) && A.cnt_nv)
         A.dnv += nv_fixup_body<HW>(q_nv, A.cnt_nv, q_nv, 0, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
-                                   NV && !OUT, c.tasks, c.outw, c.h);
+                                   NV && (!OUT || OSSE), c.tasks, c.outw, c.h);
       if (F8 && A.cnt_f8)
         A.df8 += f8_fixup_body<HW>(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0,
                                    c.outw_f8, c.h);
@@ -870,21 +871,29 @@ size_t sweep_fast_smem_bytes() {
          (FAST_THREADS / 32) * (2 * FAST_QCAP + FAST_TASK_CAP + 2) * sizeof(uint32_t);
 }
 
-template <bool NV, bool MX, bool F8, bool CODES, bool OUT = false, bool HW = false>
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT = false, bool HW = false, bool OSSE = false>
 static cudaError_t launch_fast_t(const SweepLaunch& L, int grid, cudaStream_t stream) {
   const size_t smem = sweep_fast_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(sweep_fast_kernel<NV, MX, F8, CODES, OUT, HW>,
+  cudaError_t e = cudaFuncSetAttribute(sweep_fast_kernel<NV, MX, F8, CODES, OUT, HW, OSSE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  sweep_fast_kernel<NV, MX, F8, CODES, OUT, HW><<<grid, FAST_THREADS, smem, stream>>>(L);
+  sweep_fast_kernel<NV, MX, F8, CODES, OUT, HW, OSSE><<<grid, FAST_THREADS, smem, stream>>>(L);
   return cudaGetLastError();
 }
 
 // All descriptors of L share the flag set `key` (format mask bits 0-2, bit 3 = NVFP4 codes, bit 4 =
 // W_hat of each format in the mask into each descriptor's `out`, one slice per format in format
-// order, no error sums; bit 5 = error sums weighted by each descriptor's `h`).
+// order, no error sums; bit 5 = error sums weighted by each descriptor's `h`; bit 6 with bit 4 =
+// W_hat and the plain error sums together).
 cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cudaStream_t stream) {
-  switch (key & 63u) {
+  switch (key & 127u) {
+    case 80 | 1: return launch_fast_t<true, false, false, false, true, false, true>(L, grid, stream);
+    case 80 | 2: return launch_fast_t<false, true, false, false, true, false, true>(L, grid, stream);
+    case 80 | 3: return launch_fast_t<true, true, false, false, true, false, true>(L, grid, stream);
+    case 80 | 4: return launch_fast_t<false, false, true, false, true, false, true>(L, grid, stream);
+    case 80 | 5: return launch_fast_t<true, false, true, false, true, false, true>(L, grid, stream);
+    case 80 | 6: return launch_fast_t<false, true, true, false, true, false, true>(L, grid, stream);
+    case 80 | 7: return launch_fast_t<true, true, true, false, true, false, true>(L, grid, stream);
     case 32 | 1: return launch_fast_t<true, false, false, false, false, true>(L, grid, stream);
     case 32 | 2: return launch_fast_t<false, true, false, false, false, true>(L, grid, stream);
     case 32 | 3: return launch_fast_t<true, true, false, false, false, true>(L, grid, stream);

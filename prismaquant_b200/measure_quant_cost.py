@@ -236,11 +236,13 @@ def _batched_quantize(spec: fr.FormatSpec, stacked_w: torch.Tensor) -> torch.Ten
 # reference entry points
 # ---------------------------------------------------------------------------
 
-def _fused_w_hats(W: torch.Tensor, specs) -> dict:
+def _fused_w_hats(W: torch.Tensor, specs, with_mse: bool = False):
     """W_hat of every spec whose batched RTN is NVFP4, MXFP8 or FP8 per channel, from one read of
     the stacked weight (pq_cost_qdq_fused) when two or more of them are asked for and the extra
     slices fit in a quarter of the free device memory; {} otherwise, or on a shape error (the
-    per-format path then reports each format's own error)."""
+    per-format path then reports each format's own error).  with_mse: the same read also gives
+    each W[n]'s weight_mse for those specs (pq_cost_qdq_fused_sse), returned as a second dict
+    {spec name: [weight_mse of W[n] for each n]} ({} when the first one is)."""
     by_kernel: dict[str, list[str]] = {}
     for spec in specs:
         try:
@@ -249,16 +251,27 @@ def _fused_w_hats(W: torch.Tensor, specs) -> dict:
             continue
         if k in _lib.FUSED_FMTS:
             by_kernel.setdefault(k, []).append(spec.name)
+    none = ({}, {}) if with_mse else {}
     if len(by_kernel) < 2:
-        return {}
+        return none
     free, _ = torch.cuda.mem_get_info(W.device)
     if W.numel() * 2 * len(by_kernel) > free // 4:
-        return {}
+        return none
     try:
-        hats = _lib.cost_qdq_fused(W, list(by_kernel))
+        if with_mse:
+            hats, sse = _lib.cost_qdq_fused_sse(W, list(by_kernel))
+        else:
+            hats = _lib.cost_qdq_fused(W, list(by_kernel))
     except ValueError:
-        return {}
-    return {name: hats[k] for k, names in by_kernel.items() for name in names}
+        return none
+    out = {name: hats[k] for k, names in by_kernel.items() for name in names}
+    if not with_mse:
+        return out
+    per = W[0].numel() if W.dim() == 3 else W.numel()
+    host = sse.cpu().tolist()
+    mse = {name: [_mse_from_sse(row[_KCOL[k]], per) for row in host] for k, names in by_kernel.items()
+           for name in names}
+    return out, mse
 
 
 def _fused_predicted_dloss(W: torch.Tensor, specs, h: torch.Tensor, per_row: bool = False) -> dict:
@@ -350,9 +363,17 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                 hs = [h_detail.load(n) for n in names]
                 if all(tuple(h.shape) == tuple(W.shape[1:]) for h in hs):
                     h_stacked = torch.stack([h.to(dev).float() for h in hs])
-            wmse = (_weight_mse_or_errors(list(W.unbind(0)), specs, _per_linear) if dtype == torch.bfloat16
-                    else None)
-            w_hat_pre = _fused_w_hats(W, specs) if dtype == torch.bfloat16 and not _per_linear else {}
+            # W_hat and weight_mse of the fused formats from one read of W; the sweep for the rest
+            w_hat_pre, mse_pre = (_fused_w_hats(W, specs, with_mse=True)
+                                  if dtype == torch.bfloat16 and not _per_linear else ({}, {}))
+            wmse = None
+            if dtype == torch.bfloat16:
+                rest = [s for s in specs if s.name not in mse_pre]
+                wmse = (_weight_mse_or_errors(list(W.unbind(0)), rest, _per_linear) if rest
+                        else [{} for _ in names])
+                for j, per in enumerate(wmse):
+                    for sname, vals in mse_pre.items():
+                        per[sname] = vals[j]
             dl_pre = (_fused_predicted_dloss(W, specs, h_stacked)
                       if h_stacked is not None and dtype == torch.bfloat16 and not _per_linear else {})
             for spec in specs:

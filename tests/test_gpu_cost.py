@@ -226,3 +226,51 @@ def test_fused_w_hat_equals_single_format(fmts, shape):
             continue
         np.testing.assert_array_equal(bits_of(got[f]), want, err_msg=f)
         np.testing.assert_array_equal(bits_of(got[f]), bits_of(_lib.cost_qdq(w, f)), err_msg=f)
+
+
+def _stacked_case(name):
+    if name == "ties_2x600x32":
+        return _tie_rows(1200, seed=13).reshape(2, 600, 32)
+    if name == "exact_units_3x64x64":   # tiny groups, an FP8 row at 2^64, ordinary rows
+        b = O.synthetic_weight_bits((3, 64, 64), seed=14)
+        b[0, :8] = (b[0, :8] & np.uint16(0x807F)) | np.uint16(0x0100)
+        b[1, 5, 9] = np.uint16(0x5F80)
+        return b
+    shape = {"dense_3x512x4096": (3, 512, 4096), "rows_of_96_4x128x96": (4, 128, 96),
+             "narrow_2x10x8": (2, 10, 8), "odd_1x7x48": (1, 7, 48)}[name]
+    return O.synthetic_weight_bits(shape, seed=sum(shape), outlier_frac=0.002)
+
+
+@pytest.mark.parametrize("case", ["dense_3x512x4096", "ties_2x600x32", "exact_units_3x64x64", "rows_of_96_4x128x96",
+                                  "narrow_2x10x8", "odd_1x7x48"])
+@pytest.mark.parametrize("fmts", [("NVFP4", "MXFP8", "FP8_E4M3"), ("NVFP4", "FP8_E4M3"), ("MXFP8",)])
+def test_fused_w_hat_with_sums(case, fmts):
+    """pq_cost_qdq_fused_sse: the W_hat slices of a stacked weight equal each format's own W_hat bit
+    for bit, and each W[b]'s sums equal pq_sweep_sse of W[b] (same arithmetic; only the fp64
+    atomics may add in another order) and the oracle (1e-5); rows the one-read kernel does not
+    take go through the per-format path; MXFP8 on rows it cannot group raises."""
+    from prismaquant_b200 import _lib
+    bits = _stacked_case(case)
+    w = to_cuda_bf16(bits)
+    batch, cols = bits.shape[0], bits.shape[-1]
+    if "MXFP8" in fmts and cols > 32 and cols % 32:
+        with pytest.raises(ValueError):
+            _lib.cost_qdq_fused_sse(w, fmts)
+        return
+    hats, sse = _lib.cost_qdq_fused_sse(w, fmts)
+    mask = sum(1 << _lib.FMT_IDS[f] for f in fmts)
+    ref = _lib.sweep_sse([w[b] for b in range(batch)], [mask] * batch).cpu().numpy()
+    got = sse.cpu().numpy()
+    for f in fmts:
+        np.testing.assert_array_equal(bits_of(hats[f]), bits_of(_lib.cost_qdq(w, f)), err_msg=f"{case} {f}")
+        col = _lib.FMT_IDS[f]
+        for b in range(batch):
+            assert got[b, col] == pytest.approx(ref[b, col], rel=1e-12, abs=1e-30), (case, f, b)
+            rec = O.cost_qdq_f32(bits[b], f)
+            err = O.bf16_round((O.bf16_bits_to_f32(bits[b]) - rec).astype(np.float32))
+            with np.errstate(over="ignore"):
+                want = float((err * err).astype(np.float32).astype(np.float64).sum())
+            assert got[b, col] == pytest.approx(want, rel=1e-5, abs=1e-30), (case, f, b)
+    for f in _lib.FUSED_FMTS:
+        if f not in fmts:
+            assert (got[:, _lib.FMT_IDS[f]] == 0).all(), f
