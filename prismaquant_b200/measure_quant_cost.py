@@ -241,8 +241,9 @@ def _fused_w_hats(W: torch.Tensor, specs, with_mse: bool = False):
     the stacked weight (pq_cost_qdq_fused) when two or more of them are asked for and the extra
     slices fit in a quarter of the free device memory; {} otherwise, or on a shape error (the
     per-format path then reports each format's own error).  with_mse: the same read also gives
-    each W[n]'s weight_mse for those specs (pq_cost_qdq_fused_sse), returned as a second dict
-    {spec name: [weight_mse of W[n] for each n]} ({} when the first one is)."""
+    each W[n]'s squared-error sum for those specs (pq_cost_qdq_fused_sse), returned as a second
+    dict {spec name: (fp64 device tensor [N] of sums, elements per W[n])} ({} when the first one
+    is); weight_mse is sum / elements."""
     by_kernel: dict[str, list[str]] = {}
     for spec in specs:
         try:
@@ -268,9 +269,7 @@ def _fused_w_hats(W: torch.Tensor, specs, with_mse: bool = False):
     if not with_mse:
         return out
     per = W[0].numel() if W.dim() == 3 else W.numel()
-    host = sse.cpu().tolist()
-    mse = {name: [_mse_from_sse(row[_KCOL[k]], per) for row in host] for k, names in by_kernel.items()
-           for name in names}
+    mse = {name: (sse[:, _KCOL[k]], per) for k, names in by_kernel.items() for name in names}
     return out, mse
 
 
@@ -336,6 +335,15 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
     accum: dict = {}
     processed, t0 = 0, time.time()
     total = sum(len(v) for v in groups.values())
+    # Results stay on the device until the end and come back in one copy (the GPU never waits for
+    # the host in between); entries are replayed in processing order, errors included.
+    pending: list = []
+    dev_parts: list = []
+
+    def stash(t: torch.Tensor) -> int:
+        dev_parts.append(t.detach().reshape(-1).to(torch.float64))
+        return len(dev_parts) - 1
+
     for (_in_f, _out_f), entries in groups.items():
         entries = [(n, m) for n, m in entries if n in act_cache]
         for i in range(0, len(entries), chunk_size):
@@ -367,13 +375,11 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
             w_hat_pre, mse_pre = (_fused_w_hats(W, specs, with_mse=True)
                                   if dtype == torch.bfloat16 and not _per_linear else ({}, {}))
             wmse = None
+            mse_dev = {sname: (stash(t), per) for sname, (t, per) in mse_pre.items()}
             if dtype == torch.bfloat16:
                 rest = [s for s in specs if s.name not in mse_pre]
                 wmse = (_weight_mse_or_errors(list(W.unbind(0)), rest, _per_linear) if rest
                         else [{} for _ in names])
-                for j, per in enumerate(wmse):
-                    for sname, vals in mse_pre.items():
-                        per[sname] = vals[j]
             dl_pre = (_fused_predicted_dloss(W, specs, h_stacked)
                       if h_stacked is not None and dtype == torch.bfloat16 and not _per_linear else {})
             for spec in specs:
@@ -397,19 +403,38 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                         dl = dl_pre.get(spec.name)
                         if dl is None:
                             dl = _predicted_dloss(W, spec, h_stacked, per_row=False, per_linear=_per_linear)
-                    om, rl = out_mse.cpu().tolist(), rel.cpu().tolist()
-                    for j, name in enumerate(names):
-                        wm = 0.0 if wmse is None else wmse[j][spec.name]
-                        if isinstance(wm, dict):
-                            raise ValueError(wm["error"])
-                        _accumulate_result(accum, name, spec.name, float(wm), float(om[j]), float(rl[j]),
-                                           predicted_dloss=None if dl is None else float(dl[j]))
+                    if spec.name in mse_dev:
+                        wm = mse_dev[spec.name]
+                    else:
+                        wm = [0.0 if wmse is None else wmse[j][spec.name] for j in range(len(names))]
+                        for v in wm:
+                            if isinstance(v, dict):
+                                raise ValueError(v["error"])
+                    pending.append((names, spec.name, wm, stash(out_mse), stash(rel), dl))
                 except Exception as e:  # measure_quant_cost.py:673-675
-                    for name in names:
-                        accum.setdefault(name, {})[spec.name] = {"error": str(e)}
+                    pending.append((names, spec.name, str(e)))
             processed += len(chunk)
             if processed % (chunk_size * 4) == 0 or processed == total:
                 print(f"[cost] {processed}/{total} ({time.time() - t0:.1f}s)", flush=True)
+    host = torch.cat(dev_parts).cpu() if dev_parts else None   # the one device->host copy
+    offs = [0]
+    for t in dev_parts:
+        offs.append(offs[-1] + t.numel())
+    part = lambda i: host[offs[i]:offs[i + 1]].tolist()
+    for rec in pending:
+        if len(rec) == 3:
+            names, sname, msg = rec
+            for name in names:
+                accum.setdefault(name, {})[sname] = {"error": msg}
+            continue
+        names, sname, wm, i_om, i_rl, dl = rec
+        if isinstance(wm, tuple):   # device sums of the fused formats
+            sums, per = part(wm[0]), wm[1]
+            wm = [_mse_from_sse(v, per) for v in sums]
+        om, rl = part(i_om), part(i_rl)
+        for j, name in enumerate(names):
+            _accumulate_result(accum, name, sname, float(wm[j]), float(om[j]), float(rl[j]),
+                               predicted_dloss=None if dl is None else float(dl[j]))
     return _finalize_results(accum)
 
 
