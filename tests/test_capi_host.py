@@ -54,6 +54,17 @@ def test_argument_validation_without_gpu():
     arr[0].fmt_mask = 1 << 7
     assert lib.pq_sweep_sse(arr, 1, ctypes.c_void_p(16), None) == _lib.PQ_ERR_FORMAT
     assert lib.pq_nvfp4_scales(300, None, None, None, None, None, None, None, None) == _lib.PQ_ERR_LIMIT
+    mx, nv = 1 << _lib.FMT_MXFP8, 1 << _lib.FMT_NVFP4
+    assert lib.pq_weighted_sse_fused(None, 4, 64, 0, None, 0, None, None) == _lib.PQ_ERR_FORMAT
+    assert lib.pq_weighted_sse_fused(None, 4, 64, 1 << _lib.FMT_BF16, None, 0, None, None) == _lib.PQ_ERR_FORMAT
+    assert lib.pq_weighted_sse_fused(None, 4, 48, mx, None, 0, None, None) == _lib.PQ_ERR_SHAPE
+    assert lib.pq_weighted_sse_fused(None, 0, 64, nv | mx, None, 0, None, None) == _lib.PQ_OK
+    assert lib.pq_weighted_sse_fused(None, 4, 64, nv | mx, None, 1, None, None) == _lib.PQ_ERR_NULL
+    assert lib.pq_cost_qdq_fused_sse(None, -1, 4, 64, nv, None, None, None) == _lib.PQ_ERR_SHAPE
+    assert lib.pq_cost_qdq_fused_sse(None, 2, 4, 64, 0, None, None, None) == _lib.PQ_ERR_FORMAT
+    assert lib.pq_cost_qdq_fused_sse(None, 2, 4, 48, nv | mx, None, None, None) == _lib.PQ_ERR_SHAPE
+    assert lib.pq_cost_qdq_fused_sse(None, 0, 4, 64, nv | mx, None, None, None) == _lib.PQ_OK
+    assert lib.pq_cost_qdq_fused_sse(None, 2, 4, 64, nv | mx, None, None, None) == _lib.PQ_ERR_NULL
 
 
 def test_cuda_calls_fail_loudly_on_cpu_tensors():
