@@ -236,14 +236,13 @@ def _batched_quantize(spec: fr.FormatSpec, stacked_w: torch.Tensor) -> torch.Ten
 # reference entry points
 # ---------------------------------------------------------------------------
 
-def _fused_w_hats(W: torch.Tensor, specs, with_mse: bool = False):
-    """W_hat of every spec whose batched RTN is NVFP4, MXFP8 or FP8 per channel, from one read of
-    the stacked weight (pq_cost_qdq_fused) when two or more of them are asked for and the extra
-    slices fit in a quarter of the free device memory; {} otherwise, or on a shape error (the
-    per-format path then reports each format's own error).  with_mse: the same read also gives
-    each W[n]'s squared-error sum for those specs (pq_cost_qdq_fused_sse), returned as a second
-    dict {spec name: (fp64 device tensor [N] of sums, elements per W[n])} ({} when the first one
-    is); weight_mse is sum / elements."""
+def _fused_w_hats(W: torch.Tensor, specs):
+    """W_hat of every spec whose batched RTN is NVFP4, MXFP8 or FP8 per channel, and each W[n]'s
+    squared-error sum for those specs, from one read of the stacked weight (pq_cost_qdq_fused_sse)
+    when two or more of them are asked for and the extra slices fit in a quarter of the free
+    device memory: ({spec name: W_hat}, {spec name: (fp64 device tensor [N] of sums, elements per
+    W[n])}); weight_mse is sum / elements.  ({}, {}) otherwise, or on a shape error (the
+    per-format path then reports each format's own error)."""
     by_kernel: dict[str, list[str]] = {}
     for spec in specs:
         try:
@@ -252,23 +251,17 @@ def _fused_w_hats(W: torch.Tensor, specs, with_mse: bool = False):
             continue
         if k in _lib.FUSED_FMTS:
             by_kernel.setdefault(k, []).append(spec.name)
-    none = ({}, {}) if with_mse else {}
     if len(by_kernel) < 2:
-        return none
+        return {}, {}
     free, _ = torch.cuda.mem_get_info(W.device)
     if W.numel() * 2 * len(by_kernel) > free // 4:
-        return none
+        return {}, {}
     try:
-        if with_mse:
-            hats, sse = _lib.cost_qdq_fused_sse(W, list(by_kernel))
-        else:
-            hats = _lib.cost_qdq_fused(W, list(by_kernel))
+        hats, sse = _lib.cost_qdq_fused_sse(W, list(by_kernel))
     except ValueError:
-        return none
-    out = {name: hats[k] for k, names in by_kernel.items() for name in names}
-    if not with_mse:
-        return out
+        return {}, {}
     per = W[0].numel() if W.dim() == 3 else W.numel()
+    out = {name: hats[k] for k, names in by_kernel.items() for name in names}
     mse = {name: (sse[:, _KCOL[k]], per) for k, names in by_kernel.items() for name in names}
     return out, mse
 
@@ -372,7 +365,7 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                 if all(tuple(h.shape) == tuple(W.shape[1:]) for h in hs):
                     h_stacked = torch.stack([h.to(dev).float() for h in hs])
             # W_hat and weight_mse of the fused formats from one read of W; the sweep for the rest
-            w_hat_pre, mse_pre = (_fused_w_hats(W, specs, with_mse=True)
+            w_hat_pre, mse_pre = (_fused_w_hats(W, specs)
                                   if dtype == torch.bfloat16 and not _per_linear else ({}, {}))
             wmse = None
             mse_dev = {sname: (stash(t), per) for sname, (t, per) in mse_pre.items()}
