@@ -380,6 +380,8 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                     if wmse is None and spec.weight_element_dtype != "bfloat16":
                         raise NotImplementedError(f"B200 cost kernels take bf16 weights, got {dtype}")
                     W_hat = w_hat_pre.get(spec.name)
+                    if W_hat is None and not _per_linear and batched_kernel_format(spec) == "BF16":
+                        W_hat = W   # the reference's clone (measure_quant_cost.py:544-545) is only read here
                     if W_hat is None:
                         W_hat = spec.quantize_dequantize(W) if _per_linear else _batched_quantize(spec, W)
                     X_hat = spec.activation_quantize_dequantize(X.clone())
