@@ -162,6 +162,17 @@ int pq_weighted_sse_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_
                           int h_per_row, double* sse, void* stream);
 
 /*
+ * pq_weighted_sse_fused of each w[b] of a stacked weight [batch, rows, cols]
+ * with its own weights h[b] ([rows, cols], or [rows] with h_per_row = 1), in
+ * one launch: sse [batch, 3] (fp64, device), row b receiving what
+ * pq_weighted_sse_fused(w[b], ..., h[b], ...) would add.  No counterpart in
+ * the reference's API as a single call; it serves measure_batched_gpu's
+ * per-Linear predicted_dloss of a chunk (measure_quant_cost.py:638-640).
+ */
+int pq_weighted_sse_fused_batch(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint32_t fmt_mask,
+                                const float* h, int h_per_row, double* sse, void* stream);
+
+/*
  * Output error of a quantized Linear, on the tensor cores:
  *   y_ref = bf16(X W^T), y_q = bf16(X_hat W_hat^T)  (bf16 operands, fp32 accumulate)
  * ADDS sum(bf16(y_ref - y_q)^2) to err_sse[b] and sum(y_ref^2) to ref_sse[b]

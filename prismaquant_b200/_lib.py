@@ -31,7 +31,7 @@ EXPORTED = [
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
-    "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_grad_sq_acc",
+    "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_weighted_sse_fused_batch", "pq_grad_sq_acc",
 ]
 
 
@@ -69,6 +69,7 @@ def load() -> ctypes.CDLL:
         "pq_cost_qdq_fused": [P, I64, I64, ctypes.c_uint32, P, V],
         "pq_weighted_sse_fused": [P, I64, I64, ctypes.c_uint32, P, I, P, V],
         "pq_cost_qdq_fused_sse": [P, I64, I64, I64, ctypes.c_uint32, P, P, V],
+        "pq_weighted_sse_fused_batch": [P, I64, I64, I64, ctypes.c_uint32, P, I, P, V],
         "pq_format_sse": [P, I64, I64, I, P, V],
         "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
         "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
@@ -297,6 +298,32 @@ def weighted_sse_fused(w: torch.Tensor, fmts, h: torch.Tensor, sse: torch.Tensor
     _check(load().pq_weighted_sse_fused(_ptr(wb), rows, cols, mask, _ptr(hh), int(per_row), _ptr(sse),
                                         _stream(wb)),
            "pq_weighted_sse_fused", f"cannot reshape rows of {cols} into groups for {want}")
+    return sse
+
+
+def weighted_sse_fused_batch(w: torch.Tensor, fmts, h: torch.Tensor, per_row: bool = False) -> torch.Tensor:
+    """weighted_sse_fused of each w[b] of a stacked [batch, rows, cols] weight with its own h[b]
+    ([rows, cols], or [rows] when per_row), in one launch: a new fp64 [batch, 3] device tensor
+    whose column FMT_IDS[fmt] holds w[b]'s sum(h[b] * err^2)."""
+    wb = as_bf16_cuda(w, "weighted_sse")
+    want = [f for f in FUSED_FMTS if f in set(fmts)]
+    if len(want) != len(set(fmts)) or not want:
+        raise ValueError(f"weighted_sse_fused_batch: formats must be among {FUSED_FMTS}, got {list(fmts)}")
+    if wb.dim() != 3:
+        raise ValueError(f"weighted_sse_fused_batch: expected a [batch, rows, cols] weight, got {tuple(wb.shape)}")
+    batch, rows, cols = wb.shape
+    hh = h.detach()
+    if hh.device != wb.device or hh.dtype != torch.float32:
+        raise TypeError("weighted_sse_fused_batch: h must be float32 on the weight's device")
+    hh = hh.contiguous()
+    if hh.numel() != batch * (rows if per_row else rows * cols):
+        raise ValueError(f"weighted_sse_fused_batch: h has {hh.numel()} values for a {tuple(wb.shape)} weight")
+    sse = torch.zeros(batch, 3, dtype=torch.float64, device=wb.device)
+    if wb.numel():
+        mask = sum(1 << FMT_IDS[f] for f in want)
+        _check(load().pq_weighted_sse_fused_batch(_ptr(wb), batch, rows, cols, mask, _ptr(hh), int(per_row),
+                                                  _ptr(sse), _stream(wb)),
+               "pq_weighted_sse_fused_batch", f"cannot reshape rows of {cols} into groups for {want}")
     return sse
 
 

@@ -251,6 +251,37 @@ int pq_weighted_sse_fused(const uint16_t* w, int64_t rows, int64_t cols, uint32_
   return PQ_OK;
 }
 
+int pq_weighted_sse_fused_batch(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint32_t fmt_mask,
+                                const float* h, int h_per_row, double* sse, void* stream_) {
+  if (batch < 0 || rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (fmt_mask == 0 || (fmt_mask & ~(NV | MX | F8))) return PQ_ERR_FORMAT;
+  const int st0 = check_groups(cols, fmt_mask);
+  if (st0) return st0;
+  if (batch == 0 || rows == 0) return PQ_OK;
+  if (!w || !h || !sse) return PQ_ERR_NULL;
+  const int64_t per = rows * cols, hper = h_per_row ? rows : per;
+  if (staged_ok(w, cols, fmt_mask) && (h_per_row || aligned(h, 16))) {   // one launch for the batch
+    std::vector<pq::SweepDesc> v((size_t)batch);
+    for (int64_t b = 0; b < batch; ++b) {
+      memset(&v[b], 0, sizeof(pq::SweepDesc));
+      v[b].w = w + b * per;
+      v[b].rows = rows;
+      v[b].cols = cols;
+      v[b].fmt_mask = fmt_mask;
+      v[b].sse = sse + 3 * b;
+      v[b].h = h + b * hper;
+      v[b].h_per_row = h_per_row ? 1 : 0;
+    }
+    return launch_batch(v, pq::MODE_SSE, 0, fmt_mask | 32u, (cudaStream_t)stream_);
+  }
+  for (int64_t b = 0; b < batch; ++b) {   // other shapes: one tensor at a time
+    const int st = pq_weighted_sse_fused(w + b * per, rows, cols, fmt_mask, h + b * hper, h_per_row, sse + 3 * b,
+                                         stream_);
+    if (st) return st;
+  }
+  return PQ_OK;
+}
+
 // Shapes the output-error kernels take: k % 8 == 0 (16-byte tensor-map strides), grid limits.
 static int outerr_shape(int64_t batch, int64_t rows, int64_t out, int64_t k) {
   if (batch < 0 || rows < 0 || out < 0 || k < 1 || (k & 7)) return PQ_ERR_SHAPE;

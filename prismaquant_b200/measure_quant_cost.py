@@ -268,7 +268,8 @@ def _fused_w_hats(W: torch.Tensor, specs):
 
 def _fused_predicted_dloss(W: torch.Tensor, specs, h: torch.Tensor, per_row: bool = False) -> dict:
     """predicted_dloss of every spec whose batched RTN is NVFP4, MXFP8 or FP8 per channel, from one
-    read of each W[n] and h[n] (pq_weighted_sse_fused) when two or more of them are asked for:
+    read of each W[n] and h[n], all in one launch (pq_weighted_sse_fused_batch), when two or more
+    of them are asked for:
     {spec name: [0.5 * sum(h[n] * err^2) for each n]}; {} otherwise, or on a shape error (the
     per-format path then reports each format's own error)."""
     by_kernel: dict[str, list[str]] = {}
@@ -281,10 +282,9 @@ def _fused_predicted_dloss(W: torch.Tensor, specs, h: torch.Tensor, per_row: boo
             by_kernel.setdefault(k, []).append(spec.name)
     if len(by_kernel) < 2:
         return {}
-    out = torch.zeros(W.size(0), 3, dtype=torch.float64, device=W.device)
     try:
-        for n in range(W.size(0)):
-            _lib.weighted_sse_fused(W[n], list(by_kernel), h[n].float(), out[n], per_row=per_row)
+        W3 = W if W.dim() == 3 else W.reshape(W.size(0), -1, W.shape[-1])   # packed [1, E, M, N] -> [1, E*M, N]
+        out = _lib.weighted_sse_fused_batch(W3, list(by_kernel), h.float(), per_row=per_row)
     except ValueError:
         return {}
     vals = (0.5 * out).cpu()

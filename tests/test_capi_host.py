@@ -65,6 +65,10 @@ def test_argument_validation_without_gpu():
     assert lib.pq_cost_qdq_fused_sse(None, 2, 4, 48, nv | mx, None, None, None) == _lib.PQ_ERR_SHAPE
     assert lib.pq_cost_qdq_fused_sse(None, 0, 4, 64, nv | mx, None, None, None) == _lib.PQ_OK
     assert lib.pq_cost_qdq_fused_sse(None, 2, 4, 64, nv | mx, None, None, None) == _lib.PQ_ERR_NULL
+    assert lib.pq_weighted_sse_fused_batch(None, 2, 4, 48, mx, None, 0, None, None) == _lib.PQ_ERR_SHAPE
+    assert lib.pq_weighted_sse_fused_batch(None, 2, 4, 64, 1 << 3, None, 0, None, None) == _lib.PQ_ERR_FORMAT
+    assert lib.pq_weighted_sse_fused_batch(None, 0, 4, 64, nv, None, 0, None, None) == _lib.PQ_OK
+    assert lib.pq_weighted_sse_fused_batch(None, 2, 4, 64, nv, None, 0, None, None) == _lib.PQ_ERR_NULL
 
 
 def test_cuda_calls_fail_loudly_on_cpu_tensors():

@@ -135,3 +135,22 @@ def test_weighted_sse_fused_rejects_other_formats():
             _lib.weighted_sse_fused(w, fmts, h)
     with pytest.raises(ValueError):
         _lib.weighted_sse_fused(w, ("NVFP4",), torch.ones(5, device="cuda"), per_row=True)
+
+
+@pytest.mark.parametrize("shape", [(5, 300, 256), (3, 64, 96), (2, 10, 8)])
+@pytest.mark.parametrize("per_row", [False, True])
+def test_weighted_sse_fused_batch_matches_single(shape, per_row):
+    """pq_weighted_sse_fused_batch: one launch over a stacked weight gives each w[b] the sums of
+    pq_weighted_sse_fused(w[b], h[b]) (the same arithmetic: only the fp64 atomics may add in another
+    order); rows the one-read kernel does not take go tensor by tensor."""
+    from prismaquant_b200 import _lib
+    bits = O.synthetic_weight_bits(shape, seed=sum(shape), outlier_frac=0.002)
+    rng = np.random.default_rng(7)
+    b, rows, cols = shape
+    h = rng.random((b, rows) if per_row else shape, dtype=np.float32) * np.float32(4.0)
+    w, hc = to_cuda_bf16(bits), torch.from_numpy(h).cuda()
+    fmts = ("NVFP4", "FP8_E4M3") if cols % 32 and cols > 32 else _lib.FUSED_FMTS
+    got = _lib.weighted_sse_fused_batch(w, fmts, hc, per_row=per_row).cpu().numpy()
+    for i in range(b):
+        one = _lib.weighted_sse_fused(w[i], fmts, hc[i], per_row=per_row).cpu().numpy()
+        np.testing.assert_allclose(got[i], one, rtol=1e-12, atol=1e-30, err_msg=f"{shape} {i}")
