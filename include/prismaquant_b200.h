@@ -125,6 +125,19 @@ int pq_cost_qdq_fused_sse(const uint16_t* w, int64_t batch, int64_t rows, int64_
                           uint16_t* w_hat, double* sse, void* stream);
 
 /*
+ * pq_cost_qdq_fused_sse for weights that are not stacked: ws holds batch device
+ * pointers (a host array) to [rows, cols] bf16 weights.  w_hat holds
+ * popcount(fmt_mask) + 1 slices of batch*rows*cols: the formats' W_hat as in
+ * pq_cost_qdq_fused_sse, then the weights themselves stacked, written in the
+ * same read (the stacked weight the other cost-table steps take).  No
+ * counterpart in the reference's API as a single call; it replaces the
+ * reference's torch.stack of a chunk's weights (measure_quant_cost.py:595-597)
+ * together with the W_hat and weight_mse of each format.
+ */
+int pq_cost_qdq_fused_sse_list(const uint16_t* const* ws, int64_t batch, int64_t rows, int64_t cols,
+                               uint32_t fmt_mask, uint16_t* w_hat, double* sse, void* stream);
+
+/*
  * Sum of squared errors of one format over one bf16 tensor [rows, cols]:
  * ADDS sum((W - qdq_fmt(W))^2) (bf16 subtraction, fp32 square) to *sse
  * (fp64, device; zero it first).  fmt is one of PQ_FMT_MXFP4 ..

@@ -31,7 +31,8 @@ EXPORTED = [
     "pq_mxfp8_pack", "pq_fp8_channel_pack", "pq_sumsq_rows", "pq_rownorm2", "pq_tokennorm_dot",
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
-    "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_weighted_sse_fused_batch", "pq_grad_sq_acc",
+    "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_weighted_sse_fused_batch",
+    "pq_cost_qdq_fused_sse_list", "pq_grad_sq_acc",
 ]
 
 
@@ -70,6 +71,7 @@ def load() -> ctypes.CDLL:
         "pq_weighted_sse_fused": [P, I64, I64, ctypes.c_uint32, P, I, P, V],
         "pq_cost_qdq_fused_sse": [P, I64, I64, I64, ctypes.c_uint32, P, P, V],
         "pq_weighted_sse_fused_batch": [P, I64, I64, I64, ctypes.c_uint32, P, I, P, V],
+        "pq_cost_qdq_fused_sse_list": [P, I64, I64, I64, ctypes.c_uint32, P, P, V],
         "pq_format_sse": [P, I64, I64, I, P, V],
         "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
         "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
@@ -241,6 +243,27 @@ def cost_qdq_fused_sse(w: torch.Tensor, fmts) -> tuple[dict, torch.Tensor]:
         _check(load().pq_cost_qdq_fused_sse(_ptr(w3), batch, rows, cols, mask, _ptr(out), _ptr(sse), _stream(wb)),
                "pq_cost_qdq_fused_sse", f"cannot reshape rows of {cols} into groups for {want}")
     return {f: out[i] for i, f in enumerate(want)}, sse
+
+
+def cost_qdq_fused_sse_list(ws, fmts) -> tuple[dict, torch.Tensor, torch.Tensor]:
+    """cost_qdq_fused_sse for a list of same-shape [rows, cols] bf16 CUDA weights that are not
+    stacked: ({fmt: W_hat [batch, rows, cols]}, the weights stacked [batch, rows, cols], fp64
+    [batch, 4] sums), all from one read of each weight."""
+    want = [f for f in FUSED_FMTS if f in set(fmts)]
+    if len(want) != len(set(fmts)) or not want:
+        raise ValueError(f"cost_qdq_fused_sse_list: formats must be among {FUSED_FMTS}, got {list(fmts)}")
+    wl = [as_bf16_cuda(w, "quantize_dequantize") for w in ws]
+    if not wl or any(w.dim() != 2 or w.shape != wl[0].shape or w.device != wl[0].device for w in wl):
+        raise ValueError("cost_qdq_fused_sse_list: expected same-shape [rows, cols] weights on one device")
+    batch, (rows, cols) = len(wl), wl[0].shape
+    out = torch.empty((len(want) + 1, batch, rows, cols), dtype=torch.bfloat16, device=wl[0].device)
+    sse = torch.zeros(batch, 4, dtype=torch.float64, device=wl[0].device)
+    if out.numel():
+        ptrs = (ctypes.c_void_p * batch)(*[w.data_ptr() for w in wl])
+        mask = sum(1 << FMT_IDS[f] for f in want)
+        _check(load().pq_cost_qdq_fused_sse_list(ptrs, batch, rows, cols, mask, _ptr(out), _ptr(sse), _stream(wl[0])),
+               "pq_cost_qdq_fused_sse_list", f"cannot reshape rows of {cols} into groups for {want}")
+    return {f: out[i] for i, f in enumerate(want)}, out[len(want)], sse
 
 
 def format_sse(w: torch.Tensor, fmt: str, sse: torch.Tensor) -> None:

@@ -55,8 +55,9 @@ bool staged_ok(const uint16_t* w, int64_t cols, uint32_t mask) {
 }
 
 // out_slice: W_hat launches, elements between format slices (0: each descriptor's rows*cols).
+// copy_slice: W_hat launches, also store each weight as the slice after the formats.
 int launch_batch(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, uint32_t key, cudaStream_t stream,
-                 int64_t out_slice = 0) {
+                 int64_t out_slice = 0, int copy_slice = 0) {
   size_t i = 0;
   const int sms = num_sms_current();
   while (i < descs.size()) {
@@ -64,6 +65,7 @@ int launch_batch(std::vector<pq::SweepDesc>& descs, int mode, int qfmt, uint32_t
     memset(&L, 0, sizeof(L));
     L.qdq_fmt = qfmt;
     L.out_slice = out_slice;
+    L.copy_slice = copy_slice;
     int64_t items = 0;
     int n = 0;
     for (; i < descs.size() && n < pq::MAX_SWEEP_TENSORS; ++i, ++n) {
@@ -355,6 +357,46 @@ int pq_cost_qdq_fused_sse(const uint16_t* w, int64_t batch, int64_t rows, int64_
     ts[b].fmt_mask = fmt_mask;
   }
   return pq_sweep_sse(ts.data(), (int)batch, sse, stream_);
+}
+
+int pq_cost_qdq_fused_sse_list(const uint16_t* const* ws, int64_t batch, int64_t rows, int64_t cols,
+                               uint32_t fmt_mask, uint16_t* w_hat, double* sse, void* stream_) {
+  if (batch < 0 || rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (fmt_mask == 0 || (fmt_mask & ~(NV | MX | F8))) return PQ_ERR_FORMAT;
+  const int st0 = check_groups(cols, fmt_mask);
+  if (st0) return st0;
+  if (batch == 0 || rows == 0) return PQ_OK;
+  if (!ws || !w_hat || !sse) return PQ_ERR_NULL;
+  if (batch > 0x7fffffff) return PQ_ERR_LIMIT;
+  bool staged = aligned(w_hat, 16);
+  for (int64_t b = 0; b < batch; ++b) {
+    if (!ws[b]) return PQ_ERR_NULL;
+    staged = staged && staged_ok(ws[b], cols, fmt_mask);
+  }
+  const int64_t per = rows * cols;
+  const int nf = __builtin_popcount(fmt_mask);
+  uint16_t* copy = w_hat + (int64_t)nf * batch * per;   // the stacked weight, after the format slices
+  cudaStream_t stream = (cudaStream_t)stream_;
+  if (staged) {   // one read of each weight: W_hat, the sums and the stacked copy
+    std::vector<pq::SweepDesc> v((size_t)batch);
+    for (int64_t b = 0; b < batch; ++b) {
+      memset(&v[b], 0, sizeof(pq::SweepDesc));
+      v[b].w = ws[b];
+      v[b].rows = rows;
+      v[b].cols = cols;
+      v[b].fmt_mask = fmt_mask;
+      v[b].out = w_hat + b * per;
+      v[b].sse = sse + 4 * b;
+    }
+    return launch_batch(v, pq::MODE_SSE, 0, fmt_mask | 16u | 64u, stream, batch * per, 1);
+  }
+  // other shapes or alignments: stack the weights into the copy slice, then work on the copy
+  for (int64_t b = 0; b < batch; ++b) {
+    const int st = cuda_status(cudaMemcpyAsync(copy + b * per, ws[b], (size_t)per * 2, cudaMemcpyDeviceToDevice,
+                                               stream));
+    if (st) return st;
+  }
+  return pq_cost_qdq_fused_sse(copy, batch, rows, cols, fmt_mask, w_hat, sse, stream_);
 }
 
 int pq_grad_sq_acc(const uint16_t* gy, const uint16_t* x, const uint16_t* w, int64_t t, int64_t m, int64_t n,

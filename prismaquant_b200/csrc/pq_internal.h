@@ -36,6 +36,8 @@ struct SweepDesc {
 struct SweepLaunch {
   int n;
   int qdq_fmt;
+  int copy_slice;      // W_hat launches: also store the weight itself, as the slice after the formats'
+  int pad_;
   int64_t out_slice;   // W_hat launches: elements between format slices (0: each descriptor's rows*cols)
   int64_t item_prefix[MAX_SWEEP_TENSORS + 1];
   SweepDesc t[MAX_SWEEP_TENSORS];

@@ -442,6 +442,7 @@ struct ItemCtx {
   uint32_t* outw;        // NVFP4
   uint32_t* outw_mx;     // MXFP8
   uint32_t* outw_f8;     // FP8 per channel
+  uint32_t* outw_copy;   // the weight itself (copy_slice launches), after the format slices
   HRef h;                // weighted launches: the item's H
 };
 
@@ -481,6 +482,7 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
   const int uc = valid ? u : c.nunits - 1;
   uint32_t v[8];
   const bool sw = load_unit(c.st, uc, true, lane, v);
+  if (OUT && c.outw_copy && valid) store_unit_words(c.outw_copy + c.elem0 / 2, uc, sw, v);
   float hv[16];
   if (HW && (NV || MX)) load_unit_h(c.h, uc, sw, hv);
   uint32_t a16b, amin = 0;
@@ -786,6 +788,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       c.outw = (OUT && NV) ? base : nullptr;
       c.outw_mx = (OUT && MX) ? base + (NV ? slot : 0) : nullptr;
       c.outw_f8 = (OUT && F8) ? base + ((NV ? 1 : 0) + (MX ? 1 : 0)) * slot : nullptr;
+      c.outw_copy = (OUT && L.copy_slice) ? base + ((NV ? 1 : 0) + (MX ? 1 : 0) + (F8 ? 1 : 0)) * slot : nullptr;
     }
     const int iters = (c.nunits + FAST_THREADS - 1) / FAST_THREADS;
     const bool warp_rows = (c.upr & 31) == 0;

@@ -266,6 +266,38 @@ def _fused_w_hats(W: torch.Tensor, specs):
     return out, mse
 
 
+def _fused_w_hats_list(ws, specs, dev: torch.device):
+    """_fused_w_hats for a chunk's weights as they are (bf16, contiguous, on `dev`, one shape),
+    without stacking them first: the same read also writes the stacked weight
+    (pq_cost_qdq_fused_sse_list).  Returns (W_hat dict, sums dict, stacked weight), or
+    ({}, {}, None) when the chunk does not qualify; the caller then stacks as the reference does."""
+    by_kernel: dict[str, list[str]] = {}
+    for spec in specs:
+        try:
+            k = batched_kernel_format(spec)
+        except Exception:
+            continue
+        if k in _lib.FUSED_FMTS:
+            by_kernel.setdefault(k, []).append(spec.name)
+    if len(by_kernel) < 2 or not ws:
+        return {}, {}, None
+    shape = ws[0].shape
+    if any(w.device != dev or w.dtype != torch.bfloat16 or w.dim() != 2 or w.shape != shape or
+           not w.is_contiguous() for w in ws):
+        return {}, {}, None
+    free, _ = torch.cuda.mem_get_info(dev)
+    if len(ws) * ws[0].numel() * 2 * (len(by_kernel) + 1) > free // 4:
+        return {}, {}, None
+    try:
+        hats, W, sse = _lib.cost_qdq_fused_sse_list(ws, list(by_kernel))
+    except ValueError:
+        return {}, {}, None
+    per = ws[0].numel()
+    out = {name: hats[k] for k, names in by_kernel.items() for name in names}
+    mse = {name: (sse[:, _KCOL[k]], per) for k, names in by_kernel.items() for name in names}
+    return out, mse, W
+
+
 def _fused_predicted_dloss(W: torch.Tensor, specs, h: torch.Tensor, per_row: bool = False) -> dict:
     """predicted_dloss of every spec whose batched RTN is NVFP4, MXFP8 or FP8 per channel, from one
     read of each W[n] and h[n], all in one launch (pq_weighted_sse_fused_batch), when two or more
@@ -344,7 +376,15 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
             names = [n for n, _ in chunk]
             acts = [act_cache.load(n) for n in names]
             rows = min(a.size(0) for a in acts)
-            W = torch.stack([m.weight.detach().to(device=dev, dtype=dtype) for _, m in chunk])
+            # W_hat and weight_mse of the fused formats from one read of each weight, which also
+            # stacks the weights; the reference's stack (measure_quant_cost.py:595-597) otherwise
+            w_hat_pre, mse_pre, W = ({}, {}, None)
+            if dtype == torch.bfloat16 and not _per_linear:
+                w_hat_pre, mse_pre, W = _fused_w_hats_list([m.weight.detach() for _, m in chunk], specs, dev)
+            if W is None:
+                W = torch.stack([m.weight.detach().to(device=dev, dtype=dtype) for _, m in chunk])
+                if dtype == torch.bfloat16 and not _per_linear:
+                    w_hat_pre, mse_pre = _fused_w_hats(W, specs)
             X = torch.stack([a[:rows].to(device=dev, dtype=dtype) for a in acts])
             # tensor cores with fused epilogues for bf16 operands with k % 8 == 0: y_ref (bf16) and
             # its energy once per chunk (pq_output_ref), then one GEMM per format whose epilogue
@@ -364,9 +404,6 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
                 hs = [h_detail.load(n) for n in names]
                 if all(tuple(h.shape) == tuple(W.shape[1:]) for h in hs):
                     h_stacked = torch.stack([h.to(dev).float() for h in hs])
-            # W_hat and weight_mse of the fused formats from one read of W; the sweep for the rest
-            w_hat_pre, mse_pre = (_fused_w_hats(W, specs)
-                                  if dtype == torch.bfloat16 and not _per_linear else ({}, {}))
             wmse = None
             mse_dev = {sname: (stash(t), per) for sname, (t, per) in mse_pre.items()}
             if dtype == torch.bfloat16:

@@ -274,3 +274,22 @@ def test_fused_w_hat_with_sums(case, fmts):
     for f in _lib.FUSED_FMTS:
         if f not in fmts:
             assert (got[:, _lib.FMT_IDS[f]] == 0).all(), f
+
+
+@pytest.mark.parametrize("shape", [(3, 512, 4096), (4, 128, 96), (2, 10, 8)])
+def test_fused_w_hat_with_sums_from_separate_weights(shape):
+    """pq_cost_qdq_fused_sse_list: weights in separate allocations give the stacked entry point's
+    W_hat slices bit for bit, their stacked copy equals torch.stack, and the sums agree (only the
+    fp64 atomics may add in another order); rows the one-read kernel does not take are stacked
+    first and go through the stacked entry point."""
+    from prismaquant_b200 import _lib
+    bits = O.synthetic_weight_bits(shape, seed=sum(shape) + 1, outlier_frac=0.002)
+    ws = [to_cuda_bf16(bits[b].copy()) for b in range(shape[0])]   # one allocation each
+    fmts = _lib.FUSED_FMTS
+    hats, W, sse = _lib.cost_qdq_fused_sse_list(ws, fmts)
+    stacked = torch.stack(ws)
+    assert torch.equal(W, stacked)
+    want_hats, want_sse = _lib.cost_qdq_fused_sse(stacked, fmts)
+    for f in fmts:
+        np.testing.assert_array_equal(bits_of(hats[f]), bits_of(want_hats[f]), err_msg=f"{shape} {f}")
+    np.testing.assert_allclose(sse.cpu().numpy(), want_sse.cpu().numpy(), rtol=1e-12, atol=1e-30)
