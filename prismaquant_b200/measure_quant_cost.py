@@ -282,6 +282,8 @@ def _fused_w_hats_list(ws, specs, dev: torch.device):
     if len(by_kernel) < 2 or not ws:
         return {}, {}, None
     shape = ws[0].shape
+    if dev.type == "cuda" and dev.index is None:   # "cuda" names the current device
+        dev = torch.device("cuda", torch.cuda.current_device())
     if any(w.device != dev or w.dtype != torch.bfloat16 or w.dim() != 2 or w.shape != shape or
            not w.is_contiguous() for w in ws):
         return {}, {}, None

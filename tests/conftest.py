@@ -8,7 +8,9 @@ REPO = Path(__file__).resolve().parent.parent
 if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 
-REFERENCE = Path(os.environ.get("PQ_REFERENCE_DIR", "/root/reference"))
+# A local checkout of the reference project, for the CPU tests that import it: $PQ_REFERENCE_DIR,
+# else a checkout named "reference" beside this repository.  Absent on GPU hosts (those tests skip).
+REFERENCE = Path(os.environ["PQ_REFERENCE_DIR"]) if os.environ.get("PQ_REFERENCE_DIR") else REPO.parent / "reference"
 
 
 def pytest_configure(config):

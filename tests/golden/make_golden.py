@@ -2,7 +2,7 @@
 prismaquant implementation (imported read-only from a local checkout) on
 seeded inputs.
 
-    PYTHONPATH=oracle/_shim:/root/reference python tests/golden/make_golden.py
+    PYTHONPATH=oracle/_shim:<reference checkout> python tests/golden/make_golden.py
 
 Outputs:
   small_cases.npz     inputs (bf16 bit patterns) and the reference's outputs

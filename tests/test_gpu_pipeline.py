@@ -154,3 +154,30 @@ def test_weighted_sse_fused_batch_matches_single(shape, per_row):
     for i in range(b):
         one = _lib.weighted_sse_fused(w[i], fmts, hc[i], per_row=per_row).cpu().numpy()
         np.testing.assert_allclose(got[i], one, rtol=1e-12, atol=1e-30, err_msg=f"{shape} {i}")
+
+
+def test_batched_gpu_takes_list_entry_with_plain_cuda_device(monkeypatch):
+    """measure_batched_gpu(..., "cuda", bf16): callers name the device "cuda" (no index); the
+    weights live on cuda:<current>, and the chunk must still take the one-read list entry point
+    (pq_cost_qdq_fused_sse_list) instead of stacking in torch first."""
+    from prismaquant_b200 import _lib
+    from tests.golden.pipeline_model import PIPE_LINEARS, Index, build_pipeline_model, pipeline_inputs, to_t
+    calls = []
+    orig = _lib.cost_qdq_fused_sse_list
+
+    def counted(*a, **kw):
+        calls.append(1)
+        return orig(*a, **kw)
+
+    monkeypatch.setattr(_lib, "cost_qdq_fused_sse_list", counted)
+    ws, acts, _ = pipeline_inputs()
+    model = build_pipeline_model(ws, device="cuda")
+    act = Index({n: to_t(a) for n, a in acts.items()})
+    specs = [fr.get_format(n) for n in ("NVFP4", "MXFP8", "FP8_E4M3", "BF16")]
+    got = mqc.measure_batched_gpu(model, act, set(PIPE_LINEARS), specs, "cuda", torch.bfloat16, chunk_size=2)
+    assert calls, "the list entry point was not reached with device='cuda'"
+    ref = mqc.measure_batched_gpu(model, act, set(PIPE_LINEARS), specs, torch.device("cuda", 0), torch.bfloat16,
+                                  chunk_size=2)
+    for name in got:
+        for fmt in got[name]:
+            assert got[name][fmt]["weight_mse"] == ref[name][fmt]["weight_mse"]
