@@ -277,8 +277,11 @@ int pq_nvfp4_pack(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols,
  *   16 MiB + 1 KiB array until the process exits.
  *   The first call on a device looks up the array's device address with
  *   cudaGetSymbolAddress (that device current); make it before any stream
- *   capture.  All calls on a device share the array: calls that overlap on
- *   the GPU race; each call clears the per-slice maxima it uses.
+ *   capture.  The address is kept for the process's lifetime, so the entry
+ *   point must not be used on a device after a cudaDeviceReset of it.  All
+ *   calls on a device share the array: calls that overlap on the GPU race;
+ *   each call clears the per-slice maxima it uses.  It runs the same codes
+ *   and scales passes as pq_nvfp4_pack, so bytes and speed are the same.
  */
 int pq_nvfp4_pack_noalloc(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols,
                           const float* override_dev, uint8_t* codes, uint8_t* scales, float* global_div,

@@ -18,7 +18,10 @@
 //    GPU (different streams, or several host threads) race on the array.
 //  * The first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
-//    before any stream capture on that device.
+//    before any stream capture on that device.  The address is kept for the
+//    life of the process: do not call this entry point on a device after a
+//    cudaDeviceReset (or any re-creation of its primary context) in the same
+//    process, since the kept address would then be stale.
 //
 // This file is part of the single translation unit pq_lib.cu and uses the
 // launchers and helpers of pq_pack.cu / pq_capi.cu unchanged.
@@ -73,12 +76,14 @@ extern "C" int pq_nvfp4_pack_noalloc(const uint16_t* w, int64_t batch, int64_t r
                                      void* stream_) {
   if (batch < 0 || rows < 0 || cols < 1) return PQ_ERR_SHAPE;
   if (cols % 16) return PQ_ERR_SHAPE;
-  if (batch == 0 || rows == 0) return PQ_OK;
+  if (batch == 0) return PQ_OK;
   if (batch > pq::NOALLOC_MAX_SLICES) return PQ_ERR_LIMIT;
-  const int64_t per_slice = rows * (cols / 16);
-  if (per_slice > pq::NOALLOC_MAX_GROUPS / batch) return PQ_ERR_LIMIT;
-  if (!w || !codes || !scales || !global_div) return PQ_ERR_NULL;
-  if (!aligned(w, 16) || !aligned(codes, 4)) return PQ_ERR_ALIGN;
+  const int64_t groups_per_row = cols / 16;
+  // compared by division, so that no product of the caller's sizes can overflow
+  if (rows > pq::NOALLOC_MAX_GROUPS / groups_per_row / batch) return PQ_ERR_LIMIT;
+  const int64_t per_slice = rows * groups_per_row;
+  if (!global_div) return PQ_ERR_NULL;
+  if (rows > 0 && (!w || !codes || !scales)) return PQ_ERR_NULL;
   uint16_t* amax = nullptr;
   uint32_t* tmax = nullptr;
   int st = pq::noalloc_scratch(&amax, &tmax);
@@ -87,21 +92,18 @@ extern "C" int pq_nvfp4_pack_noalloc(const uint16_t* w, int64_t batch, int64_t r
   // the per-slice maxima must start at zero; the group amax is rewritten in full
   st = cuda_status(cudaMemsetAsync(tmax, 0, (size_t)batch * sizeof(uint32_t), stream));
   if (st) return st;
-  const int sms = num_sms_current();
-  st = cuda_status(pq::launch_nvfp4_codes(w, batch, rows, cols, codes, amax, tmax, sms, stream));
+  // the codes pass of pq_nvfp4_pack, unchanged (the fast sweep kernel's codes-only form where the
+  // shape and alignment allow it); with rows == 0 it does nothing and the scale pass still writes
+  // each slice's global, as pq_nvfp4_pack does
+  st = pq_nvfp4_codes(w, batch, rows, cols, codes, amax, tmax, stream_);
   if (st) return st;
-  pq::ScalesLaunch L;
-  memset(&L, 0, sizeof(L));
-  L.n = (int)batch;
-  L.gprefix[0] = 0;
+  const uint16_t* am[pq::NOALLOC_MAX_SLICES];
+  int64_t ngs[pq::NOALLOC_MAX_SLICES];
+  uint8_t* sc[pq::NOALLOC_MAX_SLICES];
   for (int b = 0; b < (int)batch; ++b) {
-    L.amax[b] = amax + b * per_slice;
-    L.scales[b] = scales + b * per_slice;
-    L.gprefix[b + 1] = L.gprefix[b] + per_slice;
-    L.group_of[b] = -1;
+    am[b] = amax + b * per_slice;
+    ngs[b] = per_slice;
+    sc[b] = scales ? scales + b * per_slice : nullptr;
   }
-  L.tmax = tmax;
-  L.override_ = override_dev;
-  L.global_div = global_div;
-  return cuda_status(pq::launch_nvfp4_scales(L, per_slice, sms, stream));
+  return pq_nvfp4_scales((int)batch, am, ngs, tmax, nullptr, override_dev, sc, global_div, stream_);
 }

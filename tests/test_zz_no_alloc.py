@@ -81,3 +81,33 @@ def test_noalloc_rejects_sizes_beyond_its_array():
     # 8,388,608 groups is the limit: 2 x 4096 x 65,552 bf16 is above it; 257 slices is above 256
     assert lib.pq_nvfp4_pack_noalloc(None, 2, 65552, 4096, None, None, None, None, None) == _lib.PQ_ERR_LIMIT
     assert lib.pq_nvfp4_pack_noalloc(None, 257, 16, 16, None, None, None, None, None) == _lib.PQ_ERR_LIMIT
+
+
+def test_noalloc_at_its_exact_limit_and_with_empty_slices():
+    """At exactly 8,388,608 groups (the array's size: 2 slices of 4096 x 16384) and with rows == 0
+    (no groups at all: each slice's global still comes from the override, or from a zero maximum),
+    the entry point gives pq_nvfp4_pack's bytes."""
+    w = _w((2, 4096, 16384), seed=5, std=0.02)
+    got = _pack_noalloc(w, 2, None)
+    want = _pack_with_scratch(w, 2, None)
+    for g, r in zip(got, want):
+        assert torch.equal(g, r)
+    lib = _lib.load()
+    for ov in (None, torch.tensor([2e-3, 5e-4, 1e-3], dtype=torch.float32, device="cuda")):
+        e = torch.empty(0, dtype=torch.bfloat16, device="cuda")
+        g_na = torch.full((3,), -1.0, dtype=torch.float32, device="cuda")
+        g_sc = torch.full((3,), -2.0, dtype=torch.float32, device="cuda")
+        s = torch.cuda.current_stream().cuda_stream
+        assert lib.pq_nvfp4_pack_noalloc(_ptr(e), 3, 0, 64, _ptr(ov), None, None, _ptr(g_na), s) == _lib.PQ_OK
+        tm = torch.empty(3, dtype=torch.int32, device="cuda")
+        assert lib.pq_nvfp4_pack(_ptr(e), 3, 0, 64, _ptr(ov), None, None, _ptr(g_sc), None, _ptr(tm), s) == \
+            _lib.PQ_OK
+        torch.cuda.synchronize()
+        assert torch.equal(g_na, g_sc)
+    assert _lib.device_error() == 0
+
+
+def test_noalloc_limit_checks_do_not_overflow():
+    lib = _lib.load()
+    # rows * cols / 16 would overflow int64 if formed before the check
+    assert lib.pq_nvfp4_pack_noalloc(None, 1, 2 ** 62, 2 ** 20, None, None, None, None, None) == _lib.PQ_ERR_LIMIT
