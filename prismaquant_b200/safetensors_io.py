@@ -2,7 +2,8 @@
 
 Drop-in for the reference's writers (export_native_compressed.py:3977-4076
 `IncrementalSafetensorsWriter`, :4078-4131 `write_sharded_safetensors`): the same
-shard boundaries, file names, index JSON and bytes on disk.  The file layout is
+shard boundaries, file names, index JSON and bytes on disk, from a layout planner
+(`even_shard_runs`, `shard_file_names`) and a writer of this module's own.  The file layout is
 safetensors': an 8-byte little-endian header length, a compact JSON header
 (`__metadata__` first, then one entry per tensor in data order) padded with
 spaces to a multiple of 8 bytes, then the tensors' bytes back to back.  Data
@@ -16,7 +17,6 @@ while the GPU is still producing later chunks (`StreamingSweepExport.export_to`)
 from __future__ import annotations
 
 import json
-import math
 import os
 import struct
 from pathlib import Path
@@ -64,94 +64,126 @@ def save_file(tensors: dict[str, torch.Tensor], path, metadata: dict[str, str] |
             f.write(_bytes_of(tensors[k]))
 
 
+# ---------------------------------------------------------------------------
+# shard layout: which tensors go to which file, and the files' names and index
+# ---------------------------------------------------------------------------
+#
+# The on-disk result must be what the reference's writers produce
+# (export_native_compressed.py:3977-4131), because its loaders and tools read these
+# checkpoints.  The rules that fix it:
+#   * names are laid out in sorted order;
+#   * one-shot writes aim every shard at the same size, total / ceil(total / budget), and
+#     a shard is closed before the tensor that would take it past that size;
+#   * streamed writes close a shard before a tensor that would take it past the budget, and
+#     also right after a tensor that brings it to the budget or beyond;
+#   * a single shard is `model.safetensors` with no index; n > 1 shards are
+#     `model-<i>-of-<n>.safetensors` (five-digit, 1-based) plus
+#     `model.safetensors.index.json` = {"metadata": {"total_size": bytes}, "weight_map":
+#     {tensor: file}} written with two-space indentation;
+#   * every file carries the metadata {"format": "pt"}.
+
+_INDEX_NAME = "model.safetensors.index.json"
+_FILE_META = {"format": "pt"}
+
+
+def _nbytes(t: torch.Tensor) -> int:
+    return int(t.numel() * t.element_size())
+
+
+def shard_file_names(n_shards: int) -> list[str]:
+    """Final file name of each of `n_shards` shards."""
+    if n_shards == 1:
+        return ["model.safetensors"]
+    return ["model-%05d-of-%05d.safetensors" % (i, n_shards) for i in range(1, n_shards + 1)]
+
+
+def even_shard_runs(sizes: list[int], shard_bytes: int) -> list[tuple[int, int]]:
+    """[start, stop) runs of the (already ordered) sizes for a one-shot write: each run is closed
+    before the element that would take it past the common target size."""
+    total = sum(sizes)
+    n_target = max(1, -(-total // shard_bytes))
+    target = -(-total // n_target)
+    runs: list[tuple[int, int]] = []
+    start, fill = 0, 0
+    for i, n in enumerate(sizes):
+        if i > start and fill + n > target:
+            runs.append((start, i))
+            start, fill = i, 0
+        fill += n
+    runs.append((start, len(sizes)))
+    return runs
+
+
+def _write_index(out_dir: Path, files: list[str], keys_per_file: list[list[str]], total: int) -> None:
+    wmap = {}
+    for fname, keys in zip(files, keys_per_file):
+        wmap.update(dict.fromkeys(keys, fname))
+    (out_dir / _INDEX_NAME).write_text(json.dumps({"metadata": {"total_size": total}, "weight_map": wmap}, indent=2))
+
+
 def write_sharded_safetensors(tensors: dict[str, torch.Tensor], out_dir: Path, shard_bytes: int) -> None:
-    """export_native_compressed.py:4078-4131: near-equal shards of the sorted keys; one file
-    is `model.safetensors`, several are `model-0000i-of-0000n.safetensors` plus the index."""
+    """Write `tensors` as near-equal shards of at most about `shard_bytes` each (drop-in for
+    export_native_compressed.py:4078-4131; the layout rules are above)."""
     out_dir = Path(out_dir)
-    keys = sorted(tensors)
-    sizes = {k: tensors[k].numel() * tensors[k].element_size() for k in keys}
-    total = sum(sizes.values())
-    n_shards = max(1, math.ceil(total / shard_bytes))
-    target = math.ceil(total / n_shards)
-    shards: list[list[str]] = [[]]
-    cur = 0
-    for k in keys:
-        if cur + sizes[k] > target and shards[-1]:
-            shards.append([])
-            cur = 0
-        shards[-1].append(k)
-        cur += sizes[k]
-    if len(shards) == 1:
-        save_file({k: tensors[k] for k in shards[0]}, out_dir / "model.safetensors", metadata={"format": "pt"})
-        return
-    weight_map: dict[str, str] = {}
-    n = len(shards)
-    for i, shard_keys in enumerate(shards):
-        name = f"model-{i + 1:05d}-of-{n:05d}.safetensors"
-        save_file({k: tensors[k] for k in shard_keys}, out_dir / name, metadata={"format": "pt"})
-        for k in shard_keys:
-            weight_map[k] = name
-    with open(out_dir / "model.safetensors.index.json", "w") as f:
-        json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=2)
+    order = sorted(tensors)
+    runs = even_shard_runs([_nbytes(tensors[k]) for k in order], shard_bytes)
+    files = shard_file_names(len(runs))
+    groups = [order[a:b] for a, b in runs]
+    for fname, keys in zip(files, groups):
+        save_file({k: tensors[k] for k in keys}, out_dir / fname, metadata=_FILE_META)
+    if len(files) > 1:
+        _write_index(out_dir, files, groups, sum(_nbytes(t) for t in tensors.values()))
 
 
 class IncrementalSafetensorsWriter:
-    """export_native_compressed.py:3977-4076: keeps one shard resident, flushes it to a temporary
-    file once adding the next tensor would pass `shard_bytes` (a single tensor at or above the
-    budget is flushed on its own), and on finalize renames the shards to their final names and
-    writes the index (none for a single shard)."""
+    """Streamed checkpoint writer (drop-in for export_native_compressed.py:3977-4076).
+
+    Tensors arrive in batches (`add_tensors`, each batch taken in name order).  The open shard
+    is held in memory and spilled to a hidden temporary file whenever the streaming rule above
+    closes it; `finalize` gives the spilled files their final names (which depend on how many
+    there are) and writes the index.  `weight_map` is {tensor name: final file} after finalize."""
 
     def __init__(self, out_dir: Path, shard_bytes: int):
         self.out_dir = Path(out_dir)
-        self.shard_bytes = int(shard_bytes)
-        self.current: dict[str, torch.Tensor] = {}
-        self.current_size = 0
-        self.total_size = 0
-        self.tmp_shards: list[tuple[Path, list[str]]] = []
-        self.weight_map: dict[str, str] = {}
-        self.seen_keys: set[str] = set()
         self.out_dir.mkdir(parents=True, exist_ok=True)
+        self.shard_bytes = int(shard_bytes)
+        self.weight_map: dict[str, str] = {}
+        self._open: list[tuple[str, torch.Tensor]] = []
+        self._open_bytes = 0
+        self._spilled: list[tuple[Path, list[str]]] = []   # (temporary file, its tensor names)
+        self._written: set[str] = set()
+        self._total = 0
 
     def add_tensors(self, tensors: dict[str, torch.Tensor]) -> None:
-        for key in sorted(tensors):
-            if key in self.seen_keys:
-                raise RuntimeError(f"duplicate tensor key emitted during export: {key}")
-            t = tensors[key]
-            size = int(t.numel() * t.element_size())
-            if self.current and self.current_size + size > self.shard_bytes:
-                self._flush_current()
-            self.current[key] = t
-            self.current_size += size
-            self.total_size += size
-            self.seen_keys.add(key)
-            if self.current_size >= self.shard_bytes:
-                self._flush_current()
+        for name in sorted(tensors):
+            if name in self._written:
+                raise RuntimeError(f"tensor {name!r} was already added to this checkpoint")
+            t = tensors[name]
+            n = _nbytes(t)
+            if self._open and self._open_bytes + n > self.shard_bytes:
+                self._spill()
+            self._open.append((name, t))
+            self._open_bytes += n
+            self._total += n
+            self._written.add(name)
+            if self._open_bytes >= self.shard_bytes:
+                self._spill()
 
-    def _flush_current(self) -> None:
-        if not self.current:
+    def _spill(self) -> None:
+        if not self._open:
             return
-        idx = len(self.tmp_shards) + 1
-        tmp = self.out_dir / f".model-{idx:05d}.safetensors.tmp"
-        save_file(self.current, tmp, metadata={"format": "pt"})
-        self.tmp_shards.append((tmp, list(self.current.keys())))
-        self.current = {}
-        self.current_size = 0
+        tmp = self.out_dir / f".pq-shard-{len(self._spilled):05d}.partial"
+        save_file(dict(self._open), tmp, metadata=_FILE_META)
+        self._spilled.append((tmp, [name for name, _ in self._open]))
+        self._open, self._open_bytes = [], 0
 
     def finalize(self) -> None:
-        self._flush_current()
-        if not self.tmp_shards:
-            raise RuntimeError("no tensors were written")
-        if len(self.tmp_shards) == 1:
-            tmp, keys = self.tmp_shards[0]
-            os.replace(tmp, self.out_dir / "model.safetensors")
-            for k in keys:
-                self.weight_map[k] = "model.safetensors"
-            return
-        n = len(self.tmp_shards)
-        for i, (tmp, keys) in enumerate(self.tmp_shards, start=1):
-            name = f"model-{i:05d}-of-{n:05d}.safetensors"
-            os.replace(tmp, self.out_dir / name)
-            for k in keys:
-                self.weight_map[k] = name
-        with open(self.out_dir / "model.safetensors.index.json", "w") as f:
-            json.dump({"metadata": {"total_size": self.total_size}, "weight_map": self.weight_map}, f, indent=2)
+        self._spill()
+        if not self._spilled:
+            raise RuntimeError("finalize() on a checkpoint with no tensors")
+        files = shard_file_names(len(self._spilled))
+        for fname, (tmp, keys) in zip(files, self._spilled):
+            os.replace(tmp, self.out_dir / fname)
+            self.weight_map.update(dict.fromkeys(keys, fname))
+        if len(files) > 1:
+            _write_index(self.out_dir, files, [keys for _, keys in self._spilled], self._total)
