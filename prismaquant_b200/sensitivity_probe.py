@@ -202,9 +202,19 @@ class FisherAccumulator:
 
     def __init__(self, model: nn.Module, tracked: list[str], expert_info: dict[str, tuple[str, str]],
                  act_cache_dir: Path | None = None, input_rows: int = 256, hook_packed_experts: bool = True,
-                 h_detail_dir: Path | None = None, packed_estimator: str = "grad_norm"):
+                 h_detail_dir: Path | None = None, packed_estimator: str = "grad_norm",
+                 estimator: str | None = None):
+        """`estimator` picks the dense Linears' statistic: "exact" is the reference's own (each
+        backward forms grad_w on the tensor cores and keeps the per-weight diagonal on the device;
+        the files are written only with `h_detail_dir`), "per_token" the per-token estimate.  The
+        default is "exact" with `h_detail_dir` and "per_token" without."""
         self.h_detail_dir = Path(h_detail_dir) if h_detail_dir else None
-        self._detail = self.h_detail_dir is not None
+        if estimator is None:
+            estimator = "exact" if self.h_detail_dir is not None else "per_token"
+        if estimator not in ("exact", "per_token"):
+            raise ValueError(f"unknown estimator {estimator!r}")
+        self.estimator = estimator
+        self._detail = estimator == "exact"
         self._saved_inputs: dict[str, torch.Tensor] = {}
         self._h_full: dict[str, torch.Tensor] = {}
         self.stats: dict[str, dict] = {}
@@ -409,4 +419,138 @@ def probe_pass(model: nn.Module, calib: torch.Tensor, tracked: list[str], batch_
         acc._saved_inputs.clear()
     if all_reduce is not None:
         all_reduce(acc.trace_buffer)
+    return acc
+
+
+def make_layer_fisher_hooks(saved_inputs: dict, acc_stats: dict, acc_h_full: dict | None):
+    """Drop-in for the per-layer hook pair of the production probe's whole-batch backward
+    (incremental_probe.py:1222-1262, `make_fwd` / `make_bwd`): returns (make_fwd, make_bwd) with
+    the same closures' contract, computed on the tensor cores.
+
+      make_fwd(name)          forward hook: keeps the Linear's input in `saved_inputs[name]`
+      make_bwd(name, module)  backward hook: pops it and, with grad_w = bf16(gy^T x) and
+                              g2 = bf16(grad_w^2) formed by pq_grad_sq_acc (never stored),
+                              adds bf16(sum g2) to acc_stats[name]["h_trace_raw"],
+                              bf16(sum bf16(g2 * bf16(w^2))) to "h_w2_sum_raw", the row count to
+                              "n_tokens_seen", and, when `acc_h_full` is a dict, g2 into
+                              acc_h_full[name] (fp32 [out, in], created on the host as the
+                              reference does, or used where the caller put it).
+
+    The activation-snapshot side of the reference's forward hook is the caller's (it is not on
+    the Fisher path); chain it before this one if it is needed."""
+    scratch: dict[tuple, torch.Tensor] = {}
+
+    def make_fwd(name: str):
+        def hook(module, inp, out):
+            x = inp[0] if isinstance(inp, tuple) else inp
+            saved_inputs[name] = x.detach()
+        return hook
+
+    def make_bwd(name: str, mod_ref: nn.Module):
+        def hook(module, grad_input, grad_output):
+            gy = grad_output[0]
+            x = saved_inputs.pop(name, None)
+            if x is None or gy is None:
+                return
+            gy2 = gy.reshape(-1, gy.size(-1))
+            x2 = x.reshape(-1, x.size(-1))
+            m, n = gy2.size(1), x2.size(1)
+            key = (gy2.device, m, n)
+            h = scratch.get(key)
+            if h is None:
+                h = scratch[key] = torch.empty(m, n, dtype=torch.float32, device=gy2.device)
+            h.zero_()
+            sums = torch.zeros(2, dtype=torch.float64, device=gy2.device)
+            w = getattr(mod_ref, "weight", None)
+            wd = w.detach() if (w is not None and not w.is_meta) else None
+            _lib.grad_sq_acc(gy2, x2, h, sums, wd)
+            if acc_h_full is not None:
+                acc = acc_h_full.get(name)
+                if acc is None:
+                    acc = acc_h_full[name] = torch.zeros(m, n, dtype=torch.float32, device="cpu")
+                acc.add_(h.to(acc.device))
+            s = sums.float().to(torch.bfloat16).double().cpu().tolist()   # .sum() of a bf16 tensor is bf16
+            st = acc_stats[name]
+            st["h_trace_raw"] += s[0]
+            if wd is not None:
+                st["h_w2_sum_raw"] += s[1]
+            st["n_tokens_seen"] += x2.size(0)
+        return hook
+
+    return make_fwd, make_bwd
+
+
+def run_probe_pass(model: nn.Module, tokenizer, calib: torch.Tensor, model_name: str, dataset_name: str,
+                   seqlen: int, dtype_name: str, requested_device: str, load_device_map, exec_device,
+                   linear_include: str, linear_exclude: str, importance_weighting: bool,
+                   activation_cache_dir: str | None, output_path: str, h_detail_dir: str | None = None,
+                   *, expert_info: dict | None = None, tracker=None, top_k: int | None = None,
+                   estimator: str = "exact") -> FisherAccumulator:
+    """sensitivity_probe.py:1456-1590 with the same arguments and the same pickle: every Linear
+    matching `linear_include` and not `linear_exclude` is tracked; one sequence per backward under
+    the sum-reduced next-token cross entropy (optionally importance-weighted per token, weights
+    clamped to [0.25, 4] around their mean); the statistics come from this package's
+    FisherAccumulator (`estimator="exact"`: the reference's own numbers, on the tensor cores).
+
+    Router bookkeeping of ModuleList MoE models (the reference's discover_moe_structure /
+    RouterTracker) is model-structure code outside this path: pass `expert_info`, `tracker` (an
+    object with .prob(router, expert), .counts, .total_tokens and .remove_hooks()) and `top_k`
+    to have route_prob filled in; a dense model needs none of them."""
+    import pickle
+    import time
+
+    inc, exc = re.compile(linear_include), re.compile(linear_exclude)
+    tracked = [n for n, m in model.named_modules() if isinstance(m, nn.Linear) and inc.search(n) and not exc.search(n)]
+    print(f"[probe] tracking {len(tracked)} Linear layers", flush=True)
+    expert_info = {k: v for k, v in (expert_info or {}).items() if k in tracked}
+    cache_dir = Path(activation_cache_dir) if activation_cache_dir else None
+    acc = FisherAccumulator(model, tracked, expert_info, cache_dir,
+                            h_detail_dir=Path(h_detail_dir) if h_detail_dir else None, estimator=estimator)
+    model.train()
+    emb = model.get_input_embeddings()
+    t_fwd = t_bwd = 0.0
+    for i in range(calib.size(0)):
+        ids = calib[i:i + 1].to(exec_device)
+        t0 = time.time()
+        with torch.no_grad():
+            e = emb(ids)
+        e.requires_grad_(True)
+        logits = model(inputs_embeds=e).logits
+        t_fwd += time.time() - t0
+        t0 = time.time()
+        lp = F.log_softmax(logits[..., :-1, :].reshape(-1, logits.size(-1)), dim=-1)
+        nll = -lp.gather(1, ids[..., 1:].reshape(-1, 1)).squeeze(1)
+        if importance_weighting:
+            with torch.no_grad():
+                tok = F.cross_entropy(logits.detach()[..., :-1, :].reshape(-1, logits.size(-1)),
+                                      ids[..., 1:].reshape(-1), reduction="none")
+                wts = (tok / max(float(tok.mean().item()), 1e-6)).clamp(0.25, 4.0)
+            loss = (nll * wts).sum()
+        else:
+            loss = nll.sum()
+        loss.backward()
+        t_bwd += time.time() - t0
+        if (i + 1) % 4 == 0 or i == 0:
+            print(f"[probe] sample {i + 1}/{calib.size(0)} loss={float(loss.detach()) / max(nll.numel(), 1):.3f} "
+                  f"fwd_avg={t_fwd / (i + 1):.2f}s bwd_avg={t_bwd / (i + 1):.2f}s", flush=True)
+        acc._saved_inputs.clear()
+        acc._xnorm.clear()
+    acc.finalize(tracker)
+    acc.remove_hooks()
+    if tracker is not None:
+        tracker.remove_hooks()
+    out = Path(output_path)
+    out.parent.mkdir(parents=True, exist_ok=True)
+    with open(out, "wb") as f:
+        pickle.dump({"stats": acc.stats,
+                     "router_counts": dict(tracker.counts) if tracker else {},
+                     "router_totals": dict(tracker.total_tokens) if tracker else {},
+                     "expert_info": expert_info,
+                     "meta": {"model": model_name, "dataset": dataset_name, "nsamples": calib.size(0),
+                              "seqlen": seqlen, "dtype": dtype_name, "device_map": str(load_device_map),
+                              "execution_device": str(exec_device), "top_k": top_k if top_k is not None else 2,
+                              "importance_weighting": importance_weighting,
+                              "activation_cache_dir": str(cache_dir) if cache_dir else None,
+                              "linear_include": linear_include, "linear_exclude": linear_exclude}}, f)
+    print(f"[probe] wrote {out}", flush=True)
     return acc

@@ -417,3 +417,82 @@ def test_sharded_writers_match_reference():
         for p in (shim, str(REFERENCE)):
             if p in sys.path:
                 sys.path.remove(p)
+
+
+def test_patch_reaches_production_entry_points():
+    """patch_prismaquant also rebinds the cost and probe entry points, in the reference's own modules
+    and in the production modules that imported them by name (incremental_measure_quant_cost.py:53-62,
+    incremental_probe.py:55-67); the installed FisherAccumulator defaults to the exact statistics;
+    unpatch restores every name in every namespace."""
+    import inspect
+    import sys
+    from tests.conftest import REFERENCE, reference_available
+    if not reference_available():
+        pytest.skip("reference checkout not present")
+    shim = str(Path(__file__).resolve().parent.parent / "oracle" / "_shim")
+    sys.path[:0] = [shim, str(REFERENCE)]
+    try:
+        import prismaquant.incremental_measure_quant_cost as imqc
+        import prismaquant.incremental_probe as ip
+        import prismaquant.measure_quant_cost as mqc
+        import prismaquant.sensitivity_probe as sp
+        from prismaquant_b200 import install
+        from prismaquant_b200 import measure_quant_cost as our_mqc
+        from prismaquant_b200 import sensitivity_probe as our_sp
+        where = {mqc: install._COST_NAMES, imqc: install._COST_NAMES, sp: install._PROBE_NAMES,
+                 ip: install._PROBE_NAMES}
+        before = {(m, n): getattr(m, n) for m, names in where.items() for n in names}
+        done = install.patch_prismaquant()
+        for m, names in where.items():
+            short = m.__name__.rsplit(".", 1)[1]
+            for n in names:
+                assert f"{short}.{n}" in done, (short, n)
+                got = getattr(m, n)
+                assert got is not before[(m, n)]
+                if n in install._COST_NAMES:
+                    assert got.__prismaquant_b200__ is getattr(our_mqc, n)
+                elif n == "FisherAccumulator":
+                    assert issubclass(got, our_sp.FisherAccumulator)
+                else:
+                    assert got is getattr(our_sp, n)
+        # the production namespaces hold the very objects the reference modules hold
+        assert imqc.measure_batched_gpu is mqc.measure_batched_gpu and ip.FisherAccumulator is sp.FisherAccumulator
+        assert inspect.signature(sp.FisherAccumulator.__init__).parameters["h_detail_dir"].default is None
+        install.unpatch_prismaquant()
+        for (m, n), v in before.items():
+            assert getattr(m, n) is v, (m.__name__, n)
+        install.patch_prismaquant(fisher="per_token")
+        install.unpatch_prismaquant()
+        with pytest.raises(ValueError):
+            install.patch_prismaquant(fisher="bogus")
+    finally:
+        for p in (shim, str(REFERENCE)):
+            if p in sys.path:
+                sys.path.remove(p)
+
+
+def test_installed_cost_entry_keeps_reference_path_off_cuda():
+    """The rebound measure_* functions hand a non-CUDA call (the reference's CPU mode) back to the
+    reference's own function with the caller's arguments untouched."""
+    from prismaquant_b200 import format_registry as our_fr
+    from prismaquant_b200 import install
+
+    calls = []
+
+    def theirs(model, act_cache, target_names, specs, device, dtype, chunk_size=256, h_detail=None):
+        calls.append(("theirs", device, chunk_size))
+        return "ref"
+
+    def ours(**kw):
+        calls.append(("ours", kw["device"], kw["chunk_size"], [s.name for s in kw["specs"]]))
+        return "b200"
+
+    class Spec:
+        def __init__(self, name):
+            self.name = name
+
+    w = install._cost_wrapper(ours, theirs, our_fr)
+    assert w(None, None, set(), [Spec("NVFP4")], "cpu", None) == "ref"
+    assert w(None, None, set(), [Spec("NVFP4"), Spec("MXFP8")], "cuda", None, chunk_size=8) == "b200"
+    assert calls[-1] == ("ours", "cuda", 8, ["NVFP4", "MXFP8"])
+    assert w(None, None, set(), [Spec("MY_CUSTOM_FORMAT")], "cuda:0", None) == "ref"

@@ -158,3 +158,79 @@ def test_accumulator_writes_the_reference_detail_files(tmp_path):
         assert acc.stats[n]["h_trace_raw"] == pytest.approx(tr, rel=2.0 ** -7)
         assert acc.stats[n]["h_w2_sum_raw"] == pytest.approx(w2, rel=2.0 ** -7)
         assert acc.stats[n]["h_trace"] == pytest.approx(acc.stats[n]["h_trace_raw"] / 80)
+
+
+@pytest.mark.parametrize("n", ["0", "1"])
+def test_production_layer_hooks_against_reference_fixture(n):
+    """make_layer_fisher_hooks (the production probe's whole-batch hook pair,
+    incremental_probe.py:1222-1262) on the fixture's recorded backwards: the reference's stats and
+    its fp32 host accumulator of grad_w^2, within the same one-bf16-ulp allowance as above."""
+    from prismaquant_b200 import sensitivity_probe as sp
+    d = np.load(DETAIL)
+    x, gy, w = _t(d[f"detail/{n}/x"]), _t(d[f"detail/{n}/gy"]), _t(d[f"detail/{n}/w"])
+    lin = torch.nn.Linear(w.shape[1], w.shape[0], bias=False, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    saved, h_full = {}, {}
+    stats = {n: {"h_trace_raw": 0.0, "h_w2_sum_raw": 0.0, "n_tokens_seen": 0}}
+    make_fwd, make_bwd = sp.make_layer_fisher_hooks(saved, stats, h_full)
+    fwd, bwd = make_fwd(n), make_bwd(n, lin)
+    for c in range(x.shape[0]):
+        fwd(lin, (x[c],), None)
+        bwd(lin, None, (gy[c],))
+    assert not saved
+    st = stats[n]
+    assert st["n_tokens_seen"] == int(d[f"detail/{n}/n_tokens_seen"][0])
+    assert st["h_trace_raw"] == pytest.approx(float(d[f"detail/{n}/h_trace_raw"][0]), rel=2.0 ** -7)
+    assert st["h_w2_sum_raw"] == pytest.approx(float(d[f"detail/{n}/h_w2_sum_raw"][0]), rel=2.0 ** -7)
+    assert h_full[n].device.type == "cpu" and h_full[n].dtype == torch.float32
+    got = (h_full[n] / st["n_tokens_seen"]).numpy()
+    want = d[f"detail/{n}/h_diag"]
+    assert (got == want).mean() >= 0.9
+    np.testing.assert_allclose(got, want, rtol=2.0 ** -5, atol=1e-6 * float(np.abs(want).max()))
+
+
+def test_run_probe_pass_reference_signature_and_pickle(tmp_path):
+    """run_probe_pass with the reference's arguments (sensitivity_probe.py:1456-1472) on a small
+    random-init bf16 Llama: one sequence per backward, the exact statistics from the tensor cores,
+    the reference's pickle keys; each Linear's h_trace_raw equals the reference's algorithm
+    (bf16 gy^T x per backward, squared, summed) run in torch on the same GPU activations."""
+    import pickle
+
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from prismaquant_b200 import sensitivity_probe as sp
+    cfg = LlamaConfig(vocab_size=256, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=64,
+                      tie_word_embeddings=False)
+    torch.manual_seed(0)
+    model = LlamaForCausalLM(cfg).cuda().to(torch.bfloat16)
+    for p in model.parameters():
+        p.requires_grad_(False)
+    calib = torch.randint(0, 256, (3, 32), generator=torch.Generator().manual_seed(1))
+    # record what the reference's hook would see, with plain hooks beside ours
+    names = [n for n, m in model.named_modules() if isinstance(m, torch.nn.Linear) and "mlp" in n]
+    xs, gys, hooks = {n: [] for n in names}, {n: [] for n in names}, []
+    for n in names:
+        m = model.get_submodule(n)
+        hooks.append(m.register_forward_hook(lambda mm, i, o, n=n: xs[n].append(i[0].detach().clone())))
+        hooks.append(m.register_full_backward_hook(lambda mm, gi, go, n=n: gys[n].append(go[0].detach().clone())))
+    out = tmp_path / "probe.pkl"
+    acc = sp.run_probe_pass(model, None, calib, "toy", "synthetic", 32, "bfloat16", "cuda", "cuda",
+                            torch.device("cuda"), r"mlp\.", r"^$", False, None, str(out))
+    for h in hooks:
+        h.remove()
+    blob = pickle.loads(out.read_bytes())
+    assert set(blob) == {"stats", "router_counts", "router_totals", "expert_info", "meta"}
+    assert blob["meta"]["nsamples"] == 3 and blob["meta"]["linear_include"] == r"mlp\."
+    assert set(blob["stats"]) == set(names)
+    for n in names:
+        tr = 0.0
+        for x, gy in zip(xs[n], gys[n]):
+            g2 = (gy.reshape(-1, gy.shape[-1]).t() @ x.reshape(-1, x.shape[-1])).pow(2)
+            tr += float(g2.sum())
+        st = blob["stats"][n]
+        assert st["n_tokens_seen"] == 3 * 32
+        assert st["h_trace_raw"] == pytest.approx(tr, rel=2.0 ** -6), n
+        assert st["h_trace"] == pytest.approx(st["h_trace_raw"] / 96)
+    assert acc.estimator == "exact"
