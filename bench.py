@@ -8,8 +8,11 @@ to NVFP4 (codes, E4M3 block scales, fused-sibling joint globals), then the
 cost table is all-gathered across ranks.  Default workload: Llama-style 8B
 dense (32 layers, hidden 4096, intermediate 14336, 32/8 heads of 128,
 lm_head 128256 x 4096; 7.50e9 Linear params, 15.01 GB bf16) with random
-N(0, 0.02^2) weights.  Multi-GPU is weak scaling: each rank sweeps its own
-model instance (rank-seeded weights), units all ranks processed / max-rank time.
+N(0, 0.02^2) weights.  Multi-GPU is strong scaling by default: the one model's
+units (Linears, expert tensors; fused siblings together) are split across the
+ranks by bytes, each rank sweeps and exports its shard, and one all-gather
+assembles the cost table; value = model bytes / max-rank time.  `--scaling weak`
+gives each rank its own model instance instead.
 
 metric "weight GB/s scored" = bf16 weight bytes swept per second (all formats
 from one read); inputs (15 GB/rank) are far larger than L2, so no flush is needed.
@@ -48,6 +51,9 @@ def parse():
                     help="per-weight Fisher diagonal (h_detail) on the tensor cores, the reference's exact stats")
     ap.add_argument("--outerr-layers", type=int, default=32,
                     help="decoder layers whose Linears the output-error workload stacks by shape")
+    ap.add_argument("--scaling", default="auto", choices=["auto", "strong", "weak"],
+                    help="N > 1: strong = one model sharded across the ranks by whole units (fused siblings "
+                         "kept together), weak = one model instance per rank; auto = strong")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -598,6 +604,56 @@ def make_pool():
 
 # ---------------------------------------------------------------------------
 
+def result_digest(plan, mine, table, n_units, world, strong, dev):
+    """A checksum of the run's outputs, outside the timed region: per unit an integer checksum of
+    its NVFP4 codes, block scales and global (64-bit word sums, exact and order-free), gathered in
+    unit order and hashed; and the cost table's weight MSE averaged over all weights per format.
+    The codes digest is the same at every N of a strong-scaling run (the same model)."""
+    import hashlib
+
+    import torch
+    import torch.distributed as dist
+    n_local = len(mine)
+    cs = torch.zeros(max(n_local, 1), 3, dtype=torch.int64, device=dev)
+    if plan.export:
+        for j, (c, sc, g) in enumerate(plan.outputs):
+            for k, t in enumerate((c, sc.view(torch.uint8), g.view(torch.uint8))):
+                b = t.reshape(-1)
+                pad = (-b.numel()) % 8
+                if pad:
+                    b = torch.cat([b, torch.zeros(pad, dtype=torch.uint8, device=dev)])
+                v = b.view(torch.int64)
+                cs[j, k] = v.sum() + (v * 0x9E3779B97F4A7C1).sum()
+    numel = float(sum(plan.numel))
+    if world > 1:
+        caps = torch.tensor([n_local], device=dev)
+        dist.all_reduce(caps, op=dist.ReduceOp.MAX)
+        cap = max(1, int(caps.item()))
+        rec = torch.full((cap, 4), -1, dtype=torch.int64, device=dev)
+        rec[:n_local, 0] = torch.tensor(mine, device=dev)
+        rec[:n_local, 1:] = cs[:n_local]
+        out = torch.empty(world * cap, 4, dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(out, rec)
+        out = out.cpu()
+        if not strong:   # one instance per rank: rank r's units follow rank r-1's
+            out[:, 0] += torch.arange(world).repeat_interleave(cap) * n_units * (out[:, 0] >= 0)
+        rows = sorted((int(r[0]), r[1:].tolist()) for r in out if r[0] >= 0)
+        total = torch.tensor([numel], dtype=torch.float64, device=dev)
+        dist.all_reduce(total)
+        numel = float(total.item())
+    else:
+        rows = list(zip(mine, cs[:n_local].cpu().tolist()))
+    h = hashlib.sha256()
+    for uid, vals in rows:
+        h.update(int(uid).to_bytes(8, "little", signed=True))
+        for v in vals:
+            h.update(int(v).to_bytes(8, "little", signed=True))
+    sse = table.double().sum(dim=0).cpu().tolist()
+    return {"nvfp4_export_sha256_16": h.hexdigest()[:16] if plan.export else None,
+            "mean_weight_mse": {f: float("%.7g" % (sse[i] / numel)) for i, f in
+                                enumerate(("NVFP4", "MXFP8", "FP8_E4M3", "BF16"))}}
+
+
 def main():
     a = parse()
     if a.warmup < 3:
@@ -648,7 +704,7 @@ def main():
         line = {"impl": "reference", "metric": metric, "value": round(v, 4), "unit": unit, "n_gpus": a.gpus,
                 "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(1e3 * statistics.median(dts), 2),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic", "config": {"workload": wl_name, "params_per_rank": params,
+                "data": "synthetic", "config": {"workload": wl_name, "model_params": params,
                                                 "sample": "one 4096x4096 Linear per step"},
                 "cpu_baseline": {"value": round(v, 4), "unit": unit, "cores": cores, "kind": "port",
                                  "sample": "one 4096x4096 bf16 Linear per step: NVFP4/MXFP8/FP8 cost + NVFP4 pack, "
@@ -675,14 +731,27 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3", "BF16")]
-    weights = S.cuda_weights(shapes, dev, base_seed=1_000_003 * rank)
-    plan = enc.SweepExportPlan(weights, specs, export_nvfp4=a.workload != "moe30b")
+    strong = world > 1 and a.scaling in ("auto", "strong")
     n_units = len(shapes)
+    if strong:   # one model: this rank's units only, the same per-name seeds at every N
+        sizes = [int(__import__("math").prod(sh)) for _, sh in shapes]
+        owner = D.partition_units(sizes, world, [enc.sibling_group_key(n) for n, _ in shapes])
+        mine = [i for i in range(n_units) if owner[i] == rank]
+        cap = D.max_units_per_rank(owner, world)
+        weights = S.cuda_weights([shapes[i] for i in mine], dev, base_seed=0)
+        my_params = sum(sizes[i] for i in mine)
+    else:
+        mine = list(range(n_units))
+        weights = S.cuda_weights(shapes, dev, base_seed=1_000_003 * rank)
+        my_params = params
+    plan = enc.SweepExportPlan(weights, specs, export_nvfp4=a.workload != "moe30b")
+    my_ids = torch.tensor(mine, dtype=torch.int64, device=dev)
 
     def gather():
+        if strong:
+            return D.all_gather_costs(my_ids, plan.sse, n_units, cap)
         if world > 1:
-            ids = torch.arange(n_units, device=dev) + rank * n_units
-            return D.all_gather_costs(ids, plan.sse, n_units * world, n_units)
+            return D.all_gather_costs(my_ids + rank * n_units, plan.sse, n_units * world, n_units)
         return plan.sse
 
     sweep_ms = []
@@ -724,11 +793,13 @@ def main():
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
     kern_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in sweep_ms)
-    bytes_w = 2.0 * params
-    value = world * bytes_w * a.steps / (ms_max / 1e3) / 1e9
+    bytes_w = 2.0 * params                       # one model
+    job_bytes = bytes_w if strong else world * bytes_w
+    value = job_bytes * a.steps / (ms_max / 1e3) / 1e9
+    digest = result_digest(plan, mine, gather(), n_units, world, strong, dev)
 
     # dominant kernel roofline: fused sweep + NVFP4 codes; reads 2 B/param, writes 0.5 B/param of codes
-    alg_bytes = params * (2.0 + (0.5 if plan.export else 0.0))
+    alg_bytes = my_params * (2.0 + (0.5 if plan.export else 0.0))
     achieved = alg_bytes / (kern_ms / 1e3) / 1e9
     traffic = None
     try:
@@ -763,7 +834,7 @@ def main():
         e_ms = torch.tensor([statistics.mean(es)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-        e2e = {"value": round(world * bytes_w / (float(e_ms.item()) / 1e3) / 1e9, 3), "unit": unit,
+        e2e = {"value": round(job_bytes / (float(e_ms.item()) / 1e3) / 1e9, 3), "unit": unit,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": a.e2e_steps}
 
     cpu = None
@@ -779,13 +850,17 @@ def main():
         line = {
             "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: random-init N(0, 0.02^2) bf16 weights of the named shapes, generated on the device",
-            "config": {"workload": wl_name, "params_per_rank": params, "tensors_per_rank": n_units,
+            "config": {"workload": wl_name, "model_params": params, "tensors": n_units,
+                       "rank0_params": my_params, "rank0_tensors": len(mine),
                        "formats": ["NVFP4", "MXFP8", "FP8_E4M3", "BF16"], "nvfp4_export": plan.export,
                        "l2": "inputs (2 B/param per rank) far larger than the 126 MB L2; no flush",
-                       "parallelism": f"unit-sharded x{world} (weak), cost table all-gathered"},
+                       "parallelism": (f"one model, units sharded by bytes x{world} (strong), cost table "
+                                       f"all-gathered" if strong else
+                                       f"one model instance per rank x{world} (weak), cost table all-gathered")},
             "hbm_frac": round(value / world / hbm, 4),
+            "digest": digest,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "sweep_fast_kernel (fused sweep + NVFP4 codes)",

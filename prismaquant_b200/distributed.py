@@ -56,10 +56,12 @@ def all_gather_costs(local_ids: torch.Tensor, local_sse: torch.Tensor, n_units: 
     rec[: local_sse.shape[0], 1:] = local_sse
     out = torch.empty(world * cap, 5, dtype=torch.float64, device=dev)
     dist.all_gather_into_tensor(out, rec, group=group)
-    table = torch.zeros(n_units, 4, dtype=torch.float64, device=dev)
-    valid = out[:, 0] >= 0
-    table[out[valid, 0].long()] = out[valid, 1:]
-    return table
+    # scatter by id without a device->host sync: padding rows (id -1) land in a spare last row
+    ids = out[:, 0].long()
+    ids = torch.where(ids >= 0, ids, torch.full_like(ids, n_units))
+    table = torch.zeros(n_units + 1, 4, dtype=torch.float64, device=dev)
+    table.index_copy_(0, ids, out[:, 1:])
+    return table[:n_units]
 
 
 def all_reduce_traces(buf: torch.Tensor, group=None) -> torch.Tensor:
