@@ -327,6 +327,16 @@ int pq_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm
 
 /* Housekeeping. */
 int pq_device_error(int* code);          /* reads and clears the device error word */
+
+/* Failure-detection hook (no counterpart in the reference): the iteration
+ * limit of the sweep kernels' waits for a work item's bulk copy, on the
+ * current device.  A kernel whose wait runs out records ERR_MBAR_TIMEOUT (1)
+ * in the device error word, waits with a fixed limit for the copies it has
+ * issued, and returns; pq_device_error() then reports it.  0 makes every such
+ * wait give up at once (tests); pq_default_wait_limit() restores the default.
+ * Synchronous with respect to the host; not for use while sweeps are running. */
+int pq_set_wait_limit(uint32_t iterations);
+uint32_t pq_default_wait_limit(void);
 int pq_last_cuda_error(void);
 const char* pq_status_string(int status);
 int pq_version(void);

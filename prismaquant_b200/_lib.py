@@ -32,7 +32,7 @@ EXPORTED = [
     "pq_device_error", "pq_last_cuda_error", "pq_status_string", "pq_version", "pq_nvfp4_pack_noalloc",
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
     "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_weighted_sse_fused_batch",
-    "pq_cost_qdq_fused_sse_list", "pq_grad_sq_acc",
+    "pq_cost_qdq_fused_sse_list", "pq_grad_sq_acc", "pq_set_wait_limit", "pq_default_wait_limit",
 ]
 
 
@@ -89,6 +89,8 @@ def load() -> ctypes.CDLL:
         "pq_rownorm2": [P, I64, I64, P, V],
         "pq_tokennorm_dot": [P, I64, I64, P, P, P, V],
         "pq_device_error": [ctypes.POINTER(ctypes.c_int)],
+        "pq_set_wait_limit": [ctypes.c_uint32],
+        "pq_default_wait_limit": [],
         "pq_last_cuda_error": [],
         "pq_status_string": [I],
         "pq_version": [],
@@ -96,7 +98,8 @@ def load() -> ctypes.CDLL:
     for name, args in sig.items():
         fn = getattr(lib, name)
         fn.argtypes = args
-        fn.restype = ctypes.c_char_p if name == "pq_status_string" else ctypes.c_int
+        fn.restype = (ctypes.c_char_p if name == "pq_status_string" else
+                      ctypes.c_uint32 if name == "pq_default_wait_limit" else ctypes.c_int)
     _LIB = lib
     return lib
 
@@ -145,6 +148,23 @@ def device_error() -> int:
     code = ctypes.c_int(0)
     _check(load().pq_device_error(ctypes.byref(code)), "pq_device_error")
     return code.value
+
+
+def raise_on_device_error(what: str) -> None:
+    """Raise if a kernel's bounded wait gave up since the last check (reads and clears the
+    device error word; a host synchronisation point)."""
+    code = device_error()
+    if code:
+        raise RuntimeError(f"{what}: a kernel's bounded wait gave up (device error {code}); its results are "
+                           "incomplete")
+
+
+def set_wait_limit(iterations: int | None) -> None:
+    """Iteration limit of the sweep kernels' stage waits (None: the default).  A test hook for
+    the failure-detection path: 0 makes those waits give up at once."""
+    lib = load()
+    n = lib.pq_default_wait_limit() if iterations is None else int(iterations)
+    _check(lib.pq_set_wait_limit(n), "pq_set_wait_limit")
 
 
 # ---------------------------------------------------------------------------

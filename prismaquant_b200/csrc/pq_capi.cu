@@ -146,6 +146,12 @@ int pq_device_error(int* code) {
   return PQ_OK;
 }
 
+int pq_set_wait_limit(uint32_t iterations) {
+  return cuda_status(cudaMemcpyToSymbol(pq::g_pq_wait_limit, &iterations, sizeof(uint32_t)));
+}
+
+uint32_t pq_default_wait_limit(void) { return pq::DEFAULT_WAIT_LIMIT; }
+
 int pq_sweep_sse(const pq_sweep_tensor* ts, int n, double* sse, void* stream_) {
   if (n < 0) return PQ_ERR_SHAPE;
   if (n == 0) return PQ_OK;

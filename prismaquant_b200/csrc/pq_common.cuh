@@ -192,6 +192,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// Iteration limit of the sweep kernels' stage waits (the waits for a work item's bulk copy).
+// pq_set_wait_limit changes it so that a test can make those waits run out on purpose: the
+// kernel then records ERR_MBAR_TIMEOUT, waits (with the fixed limit) for the copies it has
+// issued, and returns, leaving the context usable.
+constexpr uint32_t DEFAULT_WAIT_LIMIT = 1u << 24;
+__device__ uint32_t g_pq_wait_limit = DEFAULT_WAIT_LIMIT;
+
+__device__ __forceinline__ bool mbar_wait_stage(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_bounded(bar, parity, *(volatile uint32_t*)&g_pq_wait_limit);
+}
+
 // ---------------------------------------------------------------------------
 // Reductions
 // ---------------------------------------------------------------------------

@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(SWEEP_THREADS, 1) sweep_staged_kernel(const __
     const ItemRef it = find_item(L, (int64_t)blockIdx.x + j * gridDim.x);
     const SweepDesc& d = L.t[it.ti];
 
-    if (!mbar_wait_bounded(&bars[s], parity)) *abort_flag = 1;
+    if (!mbar_wait_stage(&bars[s], parity)) *abort_flag = 1;
     __syncthreads();
     if (*abort_flag) {
       j_abort = j;

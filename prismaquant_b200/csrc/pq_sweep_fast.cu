@@ -763,7 +763,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       cur_t = it.ti;
     }
     const SweepDesc& d = L.t[it.ti];
-    if (!mbar_wait_bounded(&bars[s], parity)) {
+    if (!mbar_wait_stage(&bars[s], parity)) {
       *abort_flag = 1;
       j_abort = j;
     }

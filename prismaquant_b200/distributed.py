@@ -90,3 +90,53 @@ def all_reduce_fisher(acc, group=None):
                 dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
                 store[name] = float(t.item())
     return acc
+
+
+class RankLeft(RuntimeError):
+    """A peer rank announced that it left the job."""
+
+
+class RankTimeout(RuntimeError):
+    """A peer rank did not reach a step within the monitor's timeout."""
+
+
+class StepMonitor:
+    """Host-side liveness between steps, over a key-value store (the process group's
+    TCPStore, or any object with set / check).  A rank calls `arrive(step)` when it reaches a
+    step, `check(step)` before that step's launches and collectives, and `leave()` when it stops
+    taking part (only between steps: none of its kernels or collectives in flight).  `check`
+    returns once every rank has reached `step`, raises RankLeft when a peer has left, and
+    RankTimeout when a peer is still missing after `timeout` seconds, so the survivors find out
+    on the host instead of blocking in their next collective."""
+
+    def __init__(self, store, rank: int, world: int, timeout: float = 10.0, prefix: str = "pq_steps",
+                 poll: float = 0.01):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout, self.prefix, self.poll = float(timeout), prefix, float(poll)
+
+    def _key(self, kind: str, rank: int, step: int | None = None) -> str:
+        return f"{self.prefix}/{kind}/{rank}" + ("" if step is None else f"/{step}")
+
+    def arrive(self, step: int) -> None:
+        self.store.set(self._key("step", self.rank, step), b"1")
+
+    def leave(self) -> None:
+        self.store.set(self._key("left", self.rank), b"1")
+
+    def check(self, step: int) -> None:
+        import time
+        deadline = time.monotonic() + self.timeout
+        pending = [r for r in range(self.world) if r != self.rank]
+        while pending:
+            still = []
+            for r in pending:
+                if self.store.check([self._key("step", r, step)]):
+                    continue
+                if self.store.check([self._key("left", r)]):
+                    raise RankLeft(f"rank {r} left the job before step {step}")
+                still.append(r)
+            pending = still
+            if pending:
+                if time.monotonic() > deadline:
+                    raise RankTimeout(f"rank(s) {pending} did not reach step {step} within {self.timeout:.1f} s")
+                time.sleep(self.poll)

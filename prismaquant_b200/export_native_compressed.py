@@ -399,6 +399,7 @@ class SweepExportPlan:
 
     def costs(self) -> dict:
         host = self.sse.cpu().tolist()
+        _lib.raise_on_device_error("SweepExportPlan")
         out = {}
         for name, n, row, err in zip(self.names, self.numel, host, self.errors):
             out[name] = {s.name: ({"error": err[s.name]} if s.name in err else

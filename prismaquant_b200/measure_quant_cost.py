@@ -198,6 +198,7 @@ def sweep_weight_mse(named_weights, specs: list[fr.FormatSpec],
             else:
                 _lib.format_sse(w, kf[s.name], ext_sse[i, j])
     host, ext_host = sse.cpu().tolist(), ext_sse.cpu().tolist()   # the device->host copies
+    _lib.raise_on_device_error("sweep_weight_mse")
     out = {}
     for i, (name, w) in enumerate(zip(names, weights)):
         per = {}
@@ -451,6 +452,7 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
             if processed % (chunk_size * 4) == 0 or processed == total:
                 print(f"[cost] {processed}/{total} ({time.time() - t0:.1f}s)", flush=True)
     host = torch.cat(dev_parts).cpu() if dev_parts else None   # the one device->host copy
+    _lib.raise_on_device_error("measure_batched_gpu")
     offs = [0]
     for t in dev_parts:
         offs.append(offs[-1] + t.numel())

@@ -11,7 +11,7 @@ REPO = Path(__file__).resolve().parent.parent
 
 def declared_symbols():
     text = (REPO / "include" / "prismaquant_b200.h").read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(pq_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|uint32_t|const char\*)\s+(pq_\w+)\s*\(", text, re.M)))
 
 
 def test_library_loads_and_exports_every_declared_symbol():
