@@ -314,6 +314,14 @@ int pq_fp8_channel_pack(const uint16_t* w, int64_t n_rows, int64_t cols, uint8_t
 int pq_sumsq_rows(const uint16_t* g, int64_t n_rows, int64_t cols, double* total, float* per_row,
                   void* stream);
 
+/* pq_sumsq_rows_full: pq_sumsq_rows plus the per-weight accumulator of
+ * _GradNormCapture's full_accumulator (sensitivity_probe.py:486-503):
+ * h_full[i] += fp32(g[i])^2 (fp32, one IEEE add per element, bit-exact with the
+ * reference's `cur.add_(g.float().pow(2))`), from the same read of g.
+ * h_full has n_rows*cols floats. */
+int pq_sumsq_rows_full(const uint16_t* g, int64_t n_rows, int64_t cols, double* total, float* per_row,
+                       float* h_full, void* stream);
+
 /* pq_rownorm2: out[t] = sum_d x[t, d]^2 (fp32) for x [T, d] bf16 — the
  * forward half of the per-token estimator that replaces the
  * GEMM-then-square in FisherAccumulator._make_bwd (sensitivity_probe.py:1115-1152). */

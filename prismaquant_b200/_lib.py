@@ -33,6 +33,7 @@ EXPORTED = [
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
     "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_weighted_sse_fused_batch",
     "pq_cost_qdq_fused_sse_list", "pq_grad_sq_acc", "pq_set_wait_limit", "pq_default_wait_limit",
+    "pq_sumsq_rows_full",
 ]
 
 
@@ -86,6 +87,7 @@ def load() -> ctypes.CDLL:
         "pq_mxfp8_pack": [P, I64, I64, P, P, V],
         "pq_fp8_channel_pack": [P, I64, I64, P, P, V],
         "pq_sumsq_rows": [P, I64, I64, P, P, V],
+        "pq_sumsq_rows_full": [P, I64, I64, P, P, P, V],
         "pq_rownorm2": [P, I64, I64, P, V],
         "pq_tokennorm_dot": [P, I64, I64, P, P, P, V],
         "pq_device_error": [ctypes.POINTER(ctypes.c_int)],
@@ -547,6 +549,18 @@ def sumsq_rows(g: torch.Tensor, total: torch.Tensor, per_row: torch.Tensor | Non
     cols = gb.shape[-1]
     _check(load().pq_sumsq_rows(_ptr(gb), gb.numel() // cols, cols, _ptr(total), _ptr(per_row), _stream(gb)),
            "pq_sumsq_rows")
+
+
+def sumsq_rows_full(g: torch.Tensor, total: torch.Tensor, per_row: torch.Tensor | None, h_full: torch.Tensor):
+    """sumsq_rows plus h_full (fp32, g's shape, on g's device) += g.float()^2, one read of g."""
+    gb = as_bf16_cuda(g, "sumsq_rows_full")
+    cols = gb.shape[-1]
+    if (h_full.dtype != torch.float32 or not h_full.is_contiguous() or h_full.numel() != gb.numel()
+            or h_full.device != gb.device):
+        raise ValueError(f"sumsq_rows_full: h_full must be a contiguous float32 tensor of {tuple(gb.shape)} on "
+                         f"{gb.device}")
+    _check(load().pq_sumsq_rows_full(_ptr(gb), gb.numel() // cols, cols, _ptr(total), _ptr(per_row), _ptr(h_full),
+                                     _stream(gb)), "pq_sumsq_rows_full")
 
 
 def rownorm2(x: torch.Tensor) -> torch.Tensor:

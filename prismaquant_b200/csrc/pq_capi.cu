@@ -585,6 +585,16 @@ int pq_sumsq_rows(const uint16_t* g, int64_t n_rows, int64_t cols, double* total
   return cuda_status(pq::launch_sumsq_rows(g, n_rows, cols, total, per_row, num_sms_current(), (cudaStream_t)stream));
 }
 
+int pq_sumsq_rows_full(const uint16_t* g, int64_t n_rows, int64_t cols, double* total, float* per_row,
+                       float* h_full, void* stream) {
+  if (n_rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (!total || !h_full) return PQ_ERR_NULL;
+  if (n_rows == 0) return PQ_OK;
+  if (!g) return PQ_ERR_NULL;
+  return cuda_status(
+      pq::launch_sumsq_rows_full(g, n_rows, cols, total, per_row, h_full, num_sms_current(), (cudaStream_t)stream));
+}
+
 int pq_rownorm2(const uint16_t* x, int64_t T, int64_t d, float* out, void* stream) {
   if (T < 0 || d < 1) return PQ_ERR_SHAPE;
   if (T == 0) return PQ_OK;

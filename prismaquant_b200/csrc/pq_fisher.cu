@@ -75,6 +75,73 @@ __global__ void __launch_bounds__(256) sumsq_rows_kernel(const uint16_t* __restr
   }
 }
 
+// sumsq_rows with the per-weight [E, M, N] accumulator of _GradNormCapture
+// (sensitivity_probe.py:486-503): h[i] += fp32(g[i])^2 in fp32 (each square is exact, each add
+// one IEEE rounding, as the reference's `cur.add_(g.float().pow(2))`), in the same read of g.
+__device__ __forceinline__ double row_sumsq_acc(const uint16_t* __restrict__ row, float* __restrict__ hrow,
+                                                int64_t cols, int lane) {
+  double acc = 0.0;
+  if ((cols & 7) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(hrow) & 15) == 0) {
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    float4* hv = reinterpret_cast<float4*>(hrow);
+    const int64_t n8 = cols >> 3;
+    for (int64_t c = lane; c < n8; c += 32) {
+      float w[8];
+      unpack8(__ldg(rv + c), w);
+      float4 h0 = hv[2 * c], h1 = hv[2 * c + 1];
+      float s = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s = fmaf(w[i], w[i], s);
+      h0.x = __fadd_rn(h0.x, __fmul_rn(w[0], w[0])); h0.y = __fadd_rn(h0.y, __fmul_rn(w[1], w[1]));
+      h0.z = __fadd_rn(h0.z, __fmul_rn(w[2], w[2])); h0.w = __fadd_rn(h0.w, __fmul_rn(w[3], w[3]));
+      h1.x = __fadd_rn(h1.x, __fmul_rn(w[4], w[4])); h1.y = __fadd_rn(h1.y, __fmul_rn(w[5], w[5]));
+      h1.z = __fadd_rn(h1.z, __fmul_rn(w[6], w[6])); h1.w = __fadd_rn(h1.w, __fmul_rn(w[7], w[7]));
+      hv[2 * c] = h0;
+      hv[2 * c + 1] = h1;
+      acc += (double)s;
+    }
+  } else {
+    float part = 0.0f;
+    int cnt = 0;
+    for (int64_t i = lane; i < cols; i += 32) {
+      const float x = __uint_as_float((uint32_t)__ldg(row + i) << 16);
+      const float x2 = __fmul_rn(x, x);
+      hrow[i] = __fadd_rn(hrow[i], x2);
+      part = __fadd_rn(part, x2);
+      if (++cnt == 8) {
+        acc += (double)part;
+        part = 0.0f;
+        cnt = 0;
+      }
+    }
+    acc += (double)part;
+  }
+  return warp_sum_d(acc);
+}
+
+__global__ void __launch_bounds__(256) sumsq_rows_full_kernel(const uint16_t* __restrict__ g, int64_t rows,
+                                                              int64_t cols, double* total, float* per_row,
+                                                              float* __restrict__ h) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc = 0.0;
+  for (int64_t r = gw; r < rows; r += nw) {
+    const double v = row_sumsq_acc(g + r * cols, h + r * cols, cols, lane);
+    if (lane == 0 && per_row != nullptr) per_row[r] += (float)v;
+    acc += v;
+  }
+  __shared__ double red[8];
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    atomicAdd(total, t);
+  }
+}
+
 __global__ void __launch_bounds__(256) rownorm2_kernel(const uint16_t* __restrict__ x, int64_t T, int64_t d,
                                                        float* __restrict__ out) {
   const int lane = threadIdx.x & 31;
@@ -120,6 +187,12 @@ static inline int warp_grid(int64_t rows, int num_sms) {
 cudaError_t launch_sumsq_rows(const uint16_t* g, int64_t rows, int64_t cols, double* total, float* per_row,
                               int num_sms, cudaStream_t stream) {
   sumsq_rows_kernel<<<warp_grid(rows, num_sms), 256, 0, stream>>>(g, rows, cols, total, per_row);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sumsq_rows_full(const uint16_t* g, int64_t rows, int64_t cols, double* total, float* per_row,
+                                   float* h, int num_sms, cudaStream_t stream) {
+  sumsq_rows_full_kernel<<<warp_grid(rows, num_sms), 256, 0, stream>>>(g, rows, cols, total, per_row, h);
   return cudaGetLastError();
 }
 

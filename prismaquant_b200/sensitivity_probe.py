@@ -63,14 +63,26 @@ class _GradNormCapture(torch.autograd.Function):
     def backward(ctx, grad_output):
         if grad_output is None:
             return None, None, None, None, None
-        if ctx.full_acc is not None:
-            raise NotImplementedError("the per-weight [E, M, N] Fisher accumulator is not on the B200 path")
         g = grad_output.detach()
         total = _device_acc(ctx.scalar_acc, ctx.name, g.device)
         per_row = None
         if ctx.channel_acc is not None and g.dim() in (2, 3):
             per_row = _device_acc(ctx.channel_acc, ctx.name, g.device, tuple(g.shape[:-1]), torch.float32)
-        _lib.sumsq_rows(g, total, per_row)
+        if ctx.full_acc is not None and g.dim() >= 2:
+            # the per-weight [E, M, N] accumulator (sensitivity_probe.py:486-503), kept on the
+            # device (the reference streams each backward's gradient to a host copy); a
+            # caller-provided tensor elsewhere is updated from a device copy
+            cur = ctx.full_acc.get(ctx.name)
+            if cur is None:
+                cur = ctx.full_acc[ctx.name] = torch.zeros(g.shape, dtype=torch.float32, device=g.device)
+            if cur.device == g.device and cur.is_contiguous():
+                _lib.sumsq_rows_full(g, total, per_row, cur)
+            else:
+                tmp = cur.to(g.device).contiguous()
+                _lib.sumsq_rows_full(g, total, per_row, tmp)
+                cur.copy_(tmp)
+        else:
+            _lib.sumsq_rows(g, total, per_row)
         return None, None, None, None, None
 
 

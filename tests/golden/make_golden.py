@@ -14,6 +14,13 @@ Outputs:
                       single-Linear sweep (4096x4096 with 0.1 % x20 outliers,
                       seed 0) and on the fused-sibling q/k/v + gate/up group
                       (seeds 1..5), plus their MSE_W values
+  config_digests.json (`configs`) the same for one full-shape Llama-8B decoder
+                      layer + lm_head rows 0-4095, and one Qwen3-30B-A3B-like
+                      MoE layer through _measure_packed_experts, the batched
+                      W_hat and the packed NVFP4 export
+  fisher_bridge_bf16.npz (`fisher_bridge`) FisherAccumulator at one token per
+                      backward on bf16-valued inputs and gradients
+  fisher_detail.npz   (`fisher_detail`) FisherAccumulator with h_detail_dir
 
 Only this script touches the reference; the committed fixtures travel, the
 reference does not.
@@ -270,9 +277,113 @@ def cost_pipeline():
     return run_cost_pipeline(mqc, fr, "cpu")
 
 
+def fisher_bridge_bf16():
+    """FisherAccumulator (fp32 model, ONE token per backward) on inputs and output gradients that
+    are all bf16 values, so the B200 per-token kernels can take the very same numbers: then the
+    reference's ||gy^T x||_F^2 (fp32 GEMM, square, sum) equals sum_t ||x_t||^2 ||g_t||^2 up to fp32
+    rounding.  Two Linears, each fed its own input and output gradient (no chain rule between
+    them, so every recorded gradient stays a bf16 value)."""
+    torch.manual_seed(7)
+    model = torch.nn.ModuleDict({"0": torch.nn.Linear(64, 48, bias=False), "1": torch.nn.Linear(48, 32, bias=False)})
+    tracked = ["0", "1"]
+    acc = sp.FisherAccumulator(model, tracked, {}, hook_packed_experts=False)
+    bf = lambda t: t.to(torch.bfloat16).float()   # noqa: E731
+    xs = {"0": bf(torch.randn(6, 1, 64)), "1": bf(torch.randn(6, 1, 48) * 3)}
+    gs = {"0": bf(torch.randn(6, 1, 48) * 0.01), "1": bf(torch.randn(6, 1, 32) * 0.1)}
+    for i in range(6):
+        ys = [model[n](xs[n][i].clone().requires_grad_(True)) for n in tracked]
+        torch.autograd.backward(ys, [gs[n][i] for n in tracked])
+    acc.finalize(None)
+    out = {}
+    for n in tracked:
+        out[f"bridge16/{n}/x"] = xs[n].reshape(6, -1).to(torch.bfloat16).view(torch.int16).numpy()
+        out[f"bridge16/{n}/gy"] = gs[n].reshape(6, -1).to(torch.bfloat16).view(torch.int16).numpy()
+        out[f"bridge16/{n}/w"] = model[n].weight.detach().to(torch.bfloat16).view(torch.int16).numpy()
+        out[f"bridge16/{n}/h_trace_raw"] = np.array([acc.stats[n]["h_trace_raw"]], dtype=np.float64)
+        out[f"bridge16/{n}/n_tokens_seen"] = np.array([acc.stats[n]["n_tokens_seen"]], dtype=np.int64)
+    return out
+
+
+def name_seed(name: str) -> int:
+    """Per-tensor seed of the full-shape configuration fixtures (the GPU tests derive the same)."""
+    import hashlib
+    return int.from_bytes(hashlib.sha256(name.encode()).digest()[:6], "little")
+
+
+# Llama-8B decoder layer (config 2: hidden 4096, intermediate 14336, 32 / 8 heads of 128) and the
+# first 4096 rows of lm_head [128256, 4096]
+LLAMA8B_LAYER = {"model.layers.0.self_attn.q_proj": (4096, 4096), "model.layers.0.self_attn.k_proj": (1024, 4096),
+                 "model.layers.0.self_attn.v_proj": (1024, 4096), "model.layers.0.self_attn.o_proj": (4096, 4096),
+                 "model.layers.0.mlp.gate_proj": (14336, 4096), "model.layers.0.mlp.up_proj": (14336, 4096),
+                 "model.layers.0.mlp.down_proj": (4096, 14336), "lm_head": (4096, 4096)}
+LLAMA8B_SIBLINGS = {"qkv": ["model.layers.0.self_attn.q_proj", "model.layers.0.self_attn.k_proj",
+                            "model.layers.0.self_attn.v_proj"],
+                    "gate_up": ["model.layers.0.mlp.gate_proj", "model.layers.0.mlp.up_proj"]}
+# one Qwen3-30B-A3B-like MoE layer (config 3): 128 experts, hidden 2048, expert intermediate 768
+MOE_LAYER = {"model.layers.0.mlp.experts.gate_up_proj": (128, 1536, 2048),
+             "model.layers.0.mlp.experts.down_proj": (128, 2048, 768)}
+
+
+class _PackedExperts(torch.nn.Module):   # class name holds "expert"; owns packed 3-D parameters
+    def __init__(self, params):
+        super().__init__()
+        for n, t in params.items():
+            self.register_parameter(n, torch.nn.Parameter(t, requires_grad=False))
+
+
+def config_fixtures():
+    """The reference on one full-shape config-2 decoder layer (+ lm_head rows) and one config-3
+    MoE layer: per tensor the MSE_W of each cost format and SHA-256 digests of W_hat, of the NVFP4
+    export (fused-sibling joint globals for q/k/v and gate/up) and of the MXFP8 / FP8 exports;
+    for the packed experts, _measure_packed_experts' table, the batched W_hat and the per-expert
+    NVFP4 export."""
+    out = {"llama8b_layer": {}, "moe30b_layer": {}}
+    joint = {}
+    for members in LLAMA8B_SIBLINGS.values():
+        g = torch.stack([enc.compute_nvfp4_global_real(
+            to_t(O.synthetic_weight_bits(LLAMA8B_LAYER[m], seed=name_seed(m))).float()) for m in members]).max()
+        for m in members:
+            joint[m] = g
+    for name, shape in LLAMA8B_LAYER.items():
+        bits = O.synthetic_weight_bits(shape, seed=name_seed(name))
+        d = full_case(bits, joint=joint.get(name))
+        d["seed"] = name_seed(name)
+        if name in joint:
+            d["joint_global_real"] = float(joint[name].item())
+        out["llama8b_layer"][name] = d
+        print("[config2]", name, flush=True)
+    model = torch.nn.Module()
+    model.add_module("experts", _PackedExperts({n.rsplit(".", 1)[1]: to_t(O.synthetic_weight_bits(s, seed=name_seed(n)))
+                                                 for n, s in MOE_LAYER.items()}))
+    specs = [fr.get_format(f) for f in COST_FMTS]
+    accum = {}
+    mqc._measure_packed_experts(model, {"experts.gate_up_proj", "experts.down_proj"}, specs, "cpu", torch.bfloat16,
+                                accum)
+    table = mqc._finalize_results(accum)
+    for name, shape in MOE_LAYER.items():
+        pn = name.rsplit(".", 1)[1]
+        W = getattr(model.experts, pn).detach()
+        d = {"seed": name_seed(name), "shape": list(shape), "input": O.digest(bits_of(W)),
+             "table": table["experts." + pn]}
+        for fmt in COST_FMTS:
+            d[f"qdq/{fmt}"] = O.digest(bits_of(mqc._batched_quantize(fr.get_format(fmt), W)))
+        wp, ws, wg = enc.quantize_dequantize_nvfp4_packed(W.float())
+        d["nvfp4_packed"] = O.digest(u8_of(wp), u8_of(ws), wg.numpy())
+        out["moe30b_layer"][name] = d
+        print("[config3]", name, flush=True)
+    return out
+
+
 def main():
     if "fisher_detail" in sys.argv[1:]:   # only the per-weight Fisher fixture
         np.savez_compressed(HERE / "fisher_detail.npz", **fisher_detail())
+        return
+    if "fisher_bridge" in sys.argv[1:]:   # only the bf16-valued Fisher bridge
+        np.savez_compressed(HERE / "fisher_bridge_bf16.npz", **fisher_bridge_bf16())
+        return
+    if "configs" in sys.argv[1:]:         # only the full-shape config-2 / config-3 fixtures
+        with open(HERE / "config_digests.json", "w") as f:
+            json.dump(config_fixtures(), f, indent=1, sort_keys=True)
         return
     arrays = {}
     for name, bits in small_cases().items():

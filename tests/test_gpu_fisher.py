@@ -97,21 +97,6 @@ def test_fisher_accumulator_per_token_vs_oracle():
     acc.remove_hooks()
 
 
-def test_fisher_bridge_one_token_matches_reference(golden):
-    """At one token per backward the per-token estimator IS the reference's
-    ||gy^T x||_F^2 (FisherAccumulator._make_bwd); the recorded x / gy of the
-    reference run give its h_trace_raw."""
-    for lin in ("0", "1"):
-        x = golden[f"bridge/{lin}/x"]
-        gy = golden[f"bridge/{lin}/gy"]
-        xb, gb = O.f32_to_bf16_bits(x), O.f32_to_bf16_bits(gy)
-        if not (np.array_equal(O.bf16_bits_to_f32(xb), x) and np.array_equal(O.bf16_bits_to_f32(gb), gy)):
-            # fp32 recordings: evaluate the estimator on the GPU in fp32 via its definition
-            xn = torch.from_numpy(x).cuda().double().pow(2).sum(-1)
-            gn = torch.from_numpy(gy).cuda().double().pow(2).sum(-1)
-            assert_rel(float((xn * gn).sum()), float(golden[f"bridge/{lin}/h_trace_raw"][0]), 1e-5)
-
-
 def _explicit_routed_traces(blk, x):
     """Independent statement of the routed per-token estimator: the experts
     loop of HF Qwen3MoeExperts.forward written out with retained per-expert
@@ -165,3 +150,156 @@ def test_routed_expert_estimator_vs_explicit_autograd():
     assert_rel(float(acc["experts.gate_up_proj"][:, 0].sum()), tg, 1e-5, "gate_up")
     assert_rel(float(acc["experts.down_proj"][:, 0].sum()), td, 1e-5, "down")
     assert float(acc["experts.down_proj"][:, 1].sum()) == 50 * 2
+
+
+@pytest.mark.parametrize("shape", [(4, 96, 64), (3, 16, 100), (2, 40)])
+def test_gradnorm_capture_full_accumulator(shape):
+    """_GradNormCapture with all three accumulators (sensitivity_probe.py:451-503): the [E, M, N]
+    accumulator is h += g.float()^2 in fp32, bit-exact with the reference's add, over two
+    backwards; the scalar and channel sums as before."""
+    gs = [to_cuda_bf16(O.synthetic_weight_bits(shape, seed=40 + k, std=0.01)) for k in range(2)]
+    acc, ch, full = {}, {}, {}
+    for g in gs:
+        w = torch.zeros(shape, dtype=torch.bfloat16, device="cuda", requires_grad=True)
+        sp._GradNormCapture.apply(w, "p", acc, ch, full).backward(g)
+        assert w.grad is None
+    want = torch.zeros(shape, dtype=torch.float32)
+    for g in gs:
+        want.add_(g.cpu().float().pow(2))          # the reference's CPU accumulation
+    assert torch.equal(full["p"].cpu(), want)
+    tot = sum(float(g.double().pow(2).sum()) for g in gs)
+    assert_rel(float(acc["p"]), tot, 1e-6)
+    if len(shape) >= 2:
+        np.testing.assert_allclose(ch["p"].cpu().numpy(), sum(g.float().pow(2).sum(-1) for g in gs).cpu().numpy(),
+                                   rtol=1e-5)
+
+
+class _PackedExpertsToy(nn.Module):   # class name holds "expert"; owns packed gate_up_proj / down_proj
+    def __init__(self, E=4, H=64, I=32):
+        super().__init__()
+        self.gate_up_proj = nn.Parameter(torch.randn(E, 2 * I, H) * 0.05)
+        self.down_proj = nn.Parameter(torch.randn(E, H, I) * 0.05)
+
+    def forward(self, x):   # every expert sees every token (dense mixture), enough for the hooks
+        h = torch.einsum("th,emh->etm", x, self.gate_up_proj)
+        g, u = h.chunk(2, dim=-1)
+        return torch.einsum("eti,ehi->th", torch.nn.functional.silu(g) * u, self.down_proj)
+
+
+class _MoEToy(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.model = nn.Module()
+        self.model.layers = nn.ModuleList([nn.Module()])
+        self.model.layers[0].mlp = nn.Module()
+        self.model.layers[0].mlp.experts = _PackedExpertsToy()
+        self.model.layers[0].mlp.up = nn.Linear(64, 64, bias=False)
+
+    def forward(self, x):
+        return self.model.layers[0].mlp.experts(self.model.layers[0].mlp.up(x))
+
+
+def _packed_grads(model, xs):
+    """The packed parameters' plain autograd gradients for each backward (the reference's g)."""
+    ex = model.model.layers[0].mlp.experts
+    out = []
+    for x in xs:
+        ex.zero_grad(set_to_none=True)
+        model(x).float().pow(2).sum().backward()
+        out.append({n: getattr(ex, n).grad.detach().clone() for n in ("gate_up_proj", "down_proj")})
+    return out
+
+
+def test_install_packed_expert_hooks_through_a_packed_module():
+    """install_packed_expert_hooks on a module that owns packed experts (sensitivity_probe.py:555-728):
+    the forward is unchanged, no .grad is kept on the packed leaves, and the scalar / channel / full
+    accumulators equal sum(g^2) / sum_n g^2 / g^2 of the plain autograd gradients."""
+    torch.manual_seed(0)
+    model = _MoEToy().cuda().to(torch.bfloat16)
+    xs = [torch.randn(37, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    ref_out = model(xs[0]).detach()
+    grads = _packed_grads(model, xs)
+    ex = model.model.layers[0].mlp.experts
+    ex.zero_grad(set_to_none=True)
+    scalar, chan, full = {}, {}, {}
+    meta = sp.install_packed_expert_hooks(model, scalar, chan, full)
+    q = "model.layers.0.mlp.experts"
+    assert set(meta) == {f"{q}.gate_up_proj", f"{q}.down_proj"}
+    assert meta[f"{q}.gate_up_proj"]["num_experts"] == 4 and meta[f"{q}.down_proj"]["in_features"] == 32
+    torch.testing.assert_close(model(xs[0]).detach(), ref_out, rtol=0, atol=0)
+    ex.zero_grad(set_to_none=True)
+    for x in xs:
+        model(x).float().pow(2).sum().backward()
+    assert ex.gate_up_proj.grad is None and ex.down_proj.grad is None
+    for pn in ("gate_up_proj", "down_proj"):
+        name = f"{q}.{pn}"
+        g = [gr[pn] for gr in grads]
+        assert_rel(float(scalar[name]), sum(float(t.double().pow(2).sum()) for t in g), 1e-5, pn)
+        np.testing.assert_allclose(chan[name].cpu().numpy(), sum(t.float().pow(2).sum(-1) for t in g).cpu().numpy(),
+                                   rtol=1e-5)
+        want = torch.zeros_like(full[name])
+        for t in g:
+            want.add_(t.float().pow(2))
+        assert torch.equal(full[name], want)
+
+
+def test_fisher_accumulator_hooks_packed_experts():
+    """FisherAccumulator(hook_packed_experts=True) on a model with packed experts: the packed
+    parameters get stats entries with the reference's schema, h_trace_raw = sum over backwards of
+    sum(g^2), tokens counted by the experts' forward hook, and the tracked Linear its own stats."""
+    torch.manual_seed(1)
+    model = _MoEToy().cuda().to(torch.bfloat16)
+    xs = [torch.randn(21, 64, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    grads = _packed_grads(model, xs)
+    model.model.layers[0].mlp.experts.zero_grad(set_to_none=True)
+    acc = sp.FisherAccumulator(model, ["model.layers.0.mlp.up"], {}, hook_packed_experts=True)
+    for x in xs:
+        model(x).float().pow(2).sum().backward()
+    acc.finalize(None)
+    q = "model.layers.0.mlp.experts"
+    for pn in ("gate_up_proj", "down_proj"):
+        st = acc.stats[f"{q}.{pn}"]
+        assert {"h_trace_raw", "h_w2_sum_raw", "n_params", "num_experts", "n_tokens_seen", "h_trace"} <= set(st)
+        assert_rel(st["h_trace_raw"], sum(float(gr[pn].double().pow(2).sum()) for gr in grads), 1e-5, pn)
+        assert st["n_tokens_seen"] == 3 * 21
+        assert st["h_trace"] == pytest.approx(st["h_trace_raw"] / 63)
+    assert acc.stats["model.layers.0.mlp.up"]["n_tokens_seen"] == 63
+    acc.remove_hooks()
+
+
+BRIDGE = __import__("pathlib").Path(__file__).resolve().parent / "golden" / "fisher_bridge_bf16.npz"
+
+
+@pytest.mark.parametrize("n", ["0", "1"])
+def test_fisher_bridge_kernels_match_reference(n):
+    """At one token per backward the reference's ||gy^T x||_F^2 is the per-token product of squared
+    norms.  The reference ran FisherAccumulator on bf16-valued inputs and output gradients
+    (tests/golden/fisher_bridge_bf16.npz); the same numbers go through this package's
+    FisherAccumulator on the GPU (its hooks call pq_rownorm2 and pq_tokennorm_dot), and its
+    h_trace_raw must match the reference's within 1e-5."""
+    d = np.load(BRIDGE)
+    x = torch.from_numpy(d[f"bridge16/{n}/x"]).view(torch.bfloat16).cuda()
+    gy = torch.from_numpy(d[f"bridge16/{n}/gy"]).view(torch.bfloat16).cuda()
+    w = torch.from_numpy(d[f"bridge16/{n}/w"]).view(torch.bfloat16).cuda()
+    lin = nn.Linear(w.shape[1], w.shape[0], bias=False, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    model = nn.ModuleDict({n: lin})
+    calls = []
+    orig = _lib.tokennorm_dot
+
+    def counted(*a, **k):
+        calls.append(1)
+        return orig(*a, **k)
+    sp._lib.tokennorm_dot = counted
+    try:
+        acc = sp.FisherAccumulator(model, [n], {}, hook_packed_experts=False, estimator="per_token")
+        for t in range(x.shape[0]):
+            xi = x[t:t + 1].clone().requires_grad_(True)
+            lin(xi).backward(gy[t:t + 1])
+        acc.finalize(None)
+    finally:
+        sp._lib.tokennorm_dot = orig
+    assert len(calls) == x.shape[0]
+    assert acc.stats[n]["n_tokens_seen"] == int(d[f"bridge16/{n}/n_tokens_seen"][0])
+    assert_rel(acc.stats[n]["h_trace_raw"], float(d[f"bridge16/{n}/h_trace_raw"][0]), 1e-5, n)
