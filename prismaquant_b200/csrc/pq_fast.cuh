@@ -50,6 +50,19 @@ __device__ __forceinline__ uint64_t f2_mul_rn(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint64_t f2_fma_rn(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// per-element minimum of two float32 pairs
+__device__ __forceinline__ uint64_t f2_min(uint64_t a, uint64_t b) {
+  float a0, a1, b0, b1;
+  f2_unpack(a, a0, a1);
+  f2_unpack(b, b0, b1);
+  return f2_pack(fminf(a0, b0), fminf(a1, b1));
+}
+
 // FP4 E2M1 pair, round-to-nearest-even, saturating at 6: low nibble = lo.
 __device__ __forceinline__ uint32_t cvt_e2m1x2(uint64_t x) {
   float lo, hi;
@@ -116,6 +129,51 @@ __device__ __forceinline__ void nv_codes4(const float (&l)[8], const float (&h)[
       : "=r"(cw), "=r"(dx), "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3])
       : "f"(l[0]), "f"(l[1]), "f"(l[2]), "f"(l[3]), "f"(l[4]), "f"(l[5]), "f"(l[6]), "f"(l[7]),
         "f"(h[0]), "f"(h[1]), "f"(h[2]), "f"(h[3]), "f"(h[4]), "f"(h[5]), "f"(h[6]), "f"(h[7]));
+}
+
+// Four NVFP4 pairs of biased cost products c (pair p = c[2p], c[2p+1]): q[p] the f16 pair of the
+// pair's E2M1 codes.
+__device__ __forceinline__ void nv_cost4(const float (&c)[8], uint32_t (&q)[4]) {
+  asm("{\n\t.reg .b8 c0, c1, c2, c3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c0, %5, %4;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c1, %7, %6;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c2, %9, %8;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c3, %11, %10;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, c0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, c1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, c2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, c3;\n\t}"
+      : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3])
+      : "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]), "f"(c[4]), "f"(c[5]), "f"(c[6]), "f"(c[7]));
+}
+
+// Four NVFP4 pairs of export products l: the four code bytes (pair p in byte p).
+__device__ __forceinline__ uint32_t nv_export4(const float (&l)[8]) {
+  uint32_t cw;
+  asm("{\n\t.reg .b8 c0, c1, c2, c3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c3, %8, %7;\n\t"
+      "mov.b32 %0, {c0, c1, c2, c3};\n\t}"
+      : "=r"(cw)
+      : "f"(l[0]), "f"(l[1]), "f"(l[2]), "f"(l[3]), "f"(l[4]), "f"(l[5]), "f"(l[6]), "f"(l[7]));
+  return cw;
+}
+
+// Four FP8 (E4M3) pairs of products x: q[p] the f16 pair of pair p's codes.
+__device__ __forceinline__ void f8_codes_q4(const float (&x)[8], uint32_t (&q)[4]) {
+  asm("{\n\t.reg .b16 c0, c1, c2, c3;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 c0, %5, %4;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 c1, %7, %6;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 c2, %9, %8;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 c3, %11, %10;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, c0;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, c1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %2, c2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %3, c3;\n\t}"
+      : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3])
+      : "f"(x[0]), "f"(x[1]), "f"(x[2]), "f"(x[3]), "f"(x[4]), "f"(x[5]), "f"(x[6]), "f"(x[7]));
 }
 
 // Four FP8 (E4M3) pairs at once: dx is nonzero iff some pair's bracket codes

@@ -4,8 +4,25 @@
 //
 //  * a thread owns a 16-element NVFP4 group ("unit", two 16-byte shared
 //    loads); MXFP8 32-groups are lane pairs (one shuffle);
-//  * NVFP4 / FP8-per-channel: bracketed quotient -> hardware FP4 / FP8
-//    conversion -> exact f16 decode -> f32x2 product with the scale -> bf16x2
+//  * NVFP4 cost: the code of fma(w, r, -2^-18) with r = rcp.approx(s), one
+//    hardware conversion per pair.  w and the group max a have 8-bit
+//    significands, so w / (a / 6) is either exactly an E2M1 midpoint or at
+//    least ~2^-11 (relative) away from every midpoint; at an exact midpoint
+//    the reference's fl32(w / s) IS the midpoint (a / 6 is exact unless the
+//    midpoint is 0.75, and there the scale's rounding moves the quotient by
+//    at most half an ulp of 0.75), so its nearest-with-ties-to-lower code is
+//    "the code below", which the absolute bias toward -inf gives.  The NVFP4
+//    export code (ties toward zero) is the code of RZ(w r_lo), r_lo just
+//    below 1/s.  Both rules are checked against the reference rule on every
+//    pair of bf16 values (tests/test_fast_rules.py);
+//  * FP8 per channel: the code of min(RZ(w r_lo), RZ(w r_hi)), the bracket
+//    product below the quotient, the same tie rule.  It is exact except in
+//    rows where |a - 448 s| = 3 * 64 ulp(s) and s's significand is below 1.5
+//    (and rows whose max is below the 1e-8 floor): there the quotient of an
+//    exact tie can round off the midpoint.  Those rows also convert both
+//    brackets; a unit with a pair whose brackets differ is queued and
+//    resolved exactly at the end of the item (division-free, mid_side);
+//  * then exact f16 decode -> f32x2 product with the scale -> bf16x2
 //    reconstruction -> bf16x2 error -> mixed-precision square-accumulate;
 //  * MXFP8 (power-of-two scale): the E4M3 rounding is an integer rounding of
 //    the bf16 bit pattern, two elements per 32-bit operation (low 4 mantissa
@@ -14,10 +31,8 @@
 //    checked over every bf16 amax.  Only the squared error is needed, and at a
 //    tie both neighbours are 8 ulp away (also when the upper one saturates), so
 //    the magnitude is rounded half-up whatever the reference's tie rule;
-//  * a unit whose bracket is ambiguous (or that has values outside the fast
-//    path's range) recomputes that format exactly, as the first-principles
-//    kernel does.
-// The fused NVFP4 export codes are the FP4 conversion codes of the bracket.
+//  * a unit or row outside the fast path's range is done by the exact path
+//    (IEEE division, the reference's tie rules).
 #include "pq_fast.cuh"
 #include "pq_internal.h"
 
@@ -31,15 +46,23 @@ constexpr float F8_EXACT_ROW_AMAX = 1.152921504606846976e18f;  // 2^60
 
 struct RowParam {
   float s, r_lo, r_hi, amax;
+  bool flag;   // the lower-bracket rule may differ from the reference here: resolve exactly
 };
 
 // FP8 per-channel row scale from the row's max |w| (bf16 bits): s = max(amax, 1e-8) / 448
-// (div_const is exact for every normal bf16 value and for the 1e-8 floor).
+// (div_const is exact for every normal bf16 value and for the 1e-8 floor).  flag: the row's max
+// is below the floor (s is not amax / 448), or d = amax - 448 s (exact as one FMA: a multiple of
+// 64 ulp(s) of at most 3 of them) is 3 x 64 ulp(s) and s's significand is below 1.5, the only
+// rows where an exact midpoint's fl32 quotient can round off the midpoint.
 __device__ __forceinline__ RowParam row_param(uint32_t ra_bits) {
   RowParam p;
   p.amax = __uint_as_float(ra_bits << 16);
   p.s = div_const(fmaxf(p.amax, 1e-8f), 448.0f, RCP448);
   recip_bounds(p.s, p.r_lo, p.r_hi);
+  const uint32_t sb = __float_as_uint(p.s);
+  const float ulp = __uint_as_float((sb & 0x7F800000u) - (23u << 23));
+  const float d = __fmaf_rn(-448.0f, p.s, p.amax);
+  p.flag = p.amax < 1e-8f || (fabsf(d) >= 160.0f * ulp && (sb & 0x7FFFFFu) < 0x400000u);
   return p;
 }
 
@@ -85,7 +108,11 @@ __device__ __forceinline__ void unit_to_chunks(const uint32_t (&v)[8], Chunk8& c
   unpack8(make_uint4(v[4], v[5], v[6], v[7]), c1.w);
 }
 
-constexpr int FAST_QCAP = 64;            // queued uncertain units per warp and format
+constexpr int FAST_QCAP = 64;            // queued FP8 units per warp
+// NVFP4 cost products are biased by this (absolute, in units of the scaled value |w / s| <= 6):
+// below 2^-13 x 0.25, the smallest distance of a non-midpoint quotient from a midpoint, and
+// above the products' own error at a midpoint (tests/test_fast_rules.py checks every bf16 pair)
+constexpr float NV_COST_BIAS = 3.814697265625e-06f;   // 2^-18
 constexpr int FAST_MAX_ROWS = FAST_MAX_ROWS_PER_ITEM;
 
 __device__ __forceinline__ float sq_exact_err(float w, float r) {
@@ -160,32 +187,6 @@ __device__ __forceinline__ float nv_pair_wsq(uint32_t v, uint32_t cl, uint64_t s
 __device__ __forceinline__ float f8_pair_wsq(uint32_t v, uint32_t cl, uint64_t s2, float h0, float h1) {
   const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(cl), s2));
   return wsq2_acc(bf16x2_sub(v, rec), h0, h1, 0.0f);
-}
-
-// NVFP4 pair whose bracket codes cl != ch: exact cost code (ties to the lower
-// value, so toward larger magnitude for negative w) and export code (ties
-// toward zero).
-__device__ __forceinline__ void nv_resolve_pair(uint32_t vp, uint32_t cl, uint32_t ch, float s, uint32_t& cx,
-                                                uint32_t& ce) {
-  float ql0, ql1, qh0, qh1;
-  f2_unpack(e2m1x2_to_f2(cl), ql0, ql1);
-  f2_unpack(e2m1x2_to_f2(ch), qh0, qh1);
-  const float w0 = bf16lo(vp), w1 = bf16hi(vp);
-  const uint32_t d = cl ^ ch;
-  cx = cl;
-  ce = cl;
-  if (d & 0x0Fu) {
-    bool up, dn;
-    mid_side(fabsf(w0), ql0, qh0, s, up, dn);
-    if (up || (!dn && w0 < 0.0f)) cx = (cx & 0xF0u) | (ch & 0x0Fu);
-    if (up) ce = (ce & 0xF0u) | (ch & 0x0Fu);
-  }
-  if (d & 0xF0u) {
-    bool up, dn;
-    mid_side(fabsf(w1), ql1, qh1, s, up, dn);
-    if (up || (!dn && w1 < 0.0f)) cx = (cx & 0x0Fu) | (ch & 0xF0u);
-    if (up) ce = (ce & 0x0Fu) | (ch & 0xF0u);
-  }
 }
 
 // FP8 pair (16-bit code pair, low byte = low element), cost rule.
@@ -267,80 +268,12 @@ __device__ __forceinline__ int warp_incl_scan(int x, int lane) {
   return x;
 }
 
-// Warp-cooperative resolution of queued units (entry = unit index), in batches
-// of 32 units: each lane finds its unit's uncertain pairs, a prefix sum packs
-// them into the warp's task list, and the whole warp resolves the list, so a
-// batch costs one round per 32 uncertain pairs instead of one per pair of its
-// busiest lane.  Each resolved pair adds its exact squared errors minus the
-// main loop's provisional ones and rewrites its export code byte.
-// Task word: pair (bits 0-2) | unit (3-14) | group amax bf16 bits (15-29).
-// HW: weighted sums, H the item's weights.
-template <bool HW = false>
-__device__ __forceinline__ double nv_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
-                                               int lane, int64_t elem0, uint8_t* codes, bool cost, uint32_t* tasks,
-                                               uint32_t* outw, HRef H = HRef{}) {
-  const int cnt = c0 + c1;   // entries q0[0..c0) then q1[0..c1)
-  double delta = 0.0;
-  const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
-  for (int base = 0; base < cnt; base += 32) {   // warp-uniform
-    const int i = base + lane;
-    uint32_t pm = 0, a16b = 0;
-    int u = 0;
-    if (i < cnt) {
-      u = (int)(i < c0 ? q0[i] : q1[i - c0]);
-      const uint4 a = st[2 * u], b = st[2 * u + 1];
-      const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-      a16b = unit_absmax(v);
-      const float a16 = __uint_as_float(a16b << 16);
-      if (exact_unit(a16)) {
-        delta += nv_exact_unit(words + 8 * u, a16, codes ? codes + (elem0 + 16 * (int64_t)u) / 2 : nullptr, cost,
-                               outw ? outw + (elem0 + 16 * (int64_t)u) / 2 : nullptr, HW ? &H : nullptr, u);
-      } else {
-        const float s = div_const(a16, 6.0f, RCP6);
-        float rlo, rhi;
-        recip_bounds(s, rlo, rhi);
-        const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi);
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          uint32_t cl, ch;
-          nv_bracket(f2_from_bf16x2(v[p]), rlo2, rhi2, cl, ch);
-          pm |= (cl != ch ? 1u : 0u) << p;
-        }
-      }
-    }
-    const int n = __popc(pm);
-    const int incl = warp_incl_scan(n, lane);
-    const int tot = __shfl_sync(FULL, incl, 31);
-    int off = incl - n;
-    for (uint32_t m = pm; m; m &= m - 1) tasks[off++] = (uint32_t)(__ffs(m) - 1) | ((uint32_t)u << 3) | (a16b << 15);
-    __syncwarp();
-    float dl = 0.0f;
-    for (int t = lane; t < tot; t += 32) {
-      const uint32_t task = tasks[t];
-      const int p = (int)(task & 7u), uu = (int)((task >> 3) & 0xFFFu);
-      const float s = div_const(__uint_as_float((task >> 15) << 16), 6.0f, RCP6);
-      float rlo, rhi;
-      recip_bounds(s, rlo, rhi);
-      const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi), s2 = f2_pack(s, s);
-      const uint32_t vp = words[8 * uu + p];
-      uint32_t cl, ch, cx, ce;
-      nv_bracket(f2_from_bf16x2(vp), rlo2, rhi2, cl, ch);
-      nv_resolve_pair(vp, cl, ch, s, cx, ce);
-      if (HW && cost && cx != cl) {
-        const float h0 = H.at(uu, 2 * p), h1 = H.at(uu, 2 * p + 1);
-        dl += nv_pair_wsq(vp, cx, s2, h0, h1) - nv_pair_wsq(vp, cl, s2, h0, h1);
-      } else if (cost && cx != cl) {
-        dl += nv_pair_sq(vp, cx, s2) - nv_pair_sq(vp, cl, s2);
-      }
-      if (outw && cx != cl) outw[(elem0 + 16 * (int64_t)uu) / 2 + p] = nv_pair_rec(cx, s2);
-      if (codes) codes[(elem0 + 16 * (int64_t)uu) / 2 + p] = (uint8_t)ce;
-    }
-    delta += (double)dl;
-    __syncwarp();
-  }
-  return delta;
-}
-
+// Warp-cooperative resolution of queued FP8 units (entry = unit index), in batches of 32 units:
+// each lane finds its unit's pairs whose two bracket codes differ, a prefix sum packs them into
+// the warp's task list, and the whole warp resolves the list, so a batch costs one round per 32
+// pairs instead of one per pair of its busiest lane.  Each resolved pair adds its exact squared
+// errors minus those of the main loop's provisional code (the lower bracket's) and, in W_hat
+// launches, rewrites its reconstruction.
 // Task word: pair (bits 0-2) | unit (3-14).
 template <bool HW = false>
 __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
@@ -384,15 +317,17 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, cons
       const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
       const uint32_t vp = words[8 * uu + p];
       const uint64_t w2 = f2_from_bf16x2(vp);
-      const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2, rlo2)), ch = cvt_e4m3x2(f2_mul_rz(w2, rhi2));
+      const uint64_t lo = f2_mul_rz(w2, rlo2), hi = f2_mul_rz(w2, rhi2);
+      const uint32_t cl = cvt_e4m3x2(lo), ch = cvt_e4m3x2(hi);
+      const uint32_t cp = cvt_e4m3x2(f2_min(lo, hi));   // the main loop's code
       const uint32_t cx = f8_resolve_pair(vp, cl, ch, rp.s);
-      if (HW && cx != cl) {
+      if (HW && cx != cp) {
         const float h0 = H.at(uu, 2 * p), h1 = H.at(uu, 2 * p + 1);
-        dl += f8_pair_wsq(vp, cx, s2, h0, h1) - f8_pair_wsq(vp, cl, s2, h0, h1);
-      } else if (cx != cl) {
-        dl += f8_pair_sq(vp, cx, s2) - f8_pair_sq(vp, cl, s2);
+        dl += f8_pair_wsq(vp, cx, s2, h0, h1) - f8_pair_wsq(vp, cp, s2, h0, h1);
+      } else if (cx != cp) {
+        dl += f8_pair_sq(vp, cx, s2) - f8_pair_sq(vp, cp, s2);
       }
-      if (outw && cx != cl) outw[(elem0 + 16 * (int64_t)uu) / 2 + p] = f8_pair_rec(cx, s2);
+      if (outw && cx != cp) outw[(elem0 + 16 * (int64_t)uu) / 2 + p] = f8_pair_rec(cx, s2);
     }
     delta += (double)dl;
     __syncwarp();
@@ -400,13 +335,8 @@ __device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, cons
   return delta;
 }
 
-// Out-of-line copies for the rare early flush inside the per-unit loops (the
-// loop bodies stay small); the end-of-item resolution inlines the bodies.
-template <bool HW>
-__device__ __noinline__ double nv_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, int64_t elem0,
-                                        uint8_t* codes, bool cost, uint32_t* tasks, uint32_t* outw, HRef H) {
-  return nv_fixup_body<HW>(q, cnt, q, 0, st, lane, elem0, codes, cost, tasks, outw, H);
-}
+// Out-of-line copy for the rare early flush inside the per-unit loop (the loop body stays small);
+// the end-of-item resolution inlines the body.
 template <bool HW>
 __device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
                                         int upr, uint32_t rdiv, uint32_t* tasks, int64_t elem0, uint32_t* outw,
@@ -465,7 +395,7 @@ struct Accum {
   float nv, mx, f8;
   double dnv, dmx, df8;
   uint32_t tmax;
-  int cnt_nv, cnt_f8;
+  int cnt_f8;
 };
 
 __device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
@@ -476,8 +406,7 @@ __device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
 // FP8 format is on) the unit's contribution to its row maximum.
 // HW: sums weighted by H (per element or per row).  OSSE (with OUT): the error sums as well.
 template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW, bool OSSE>
-__device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, bool warp_rows,
-                                            uint32_t* q_nv, Accum& A) {
+__device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, bool warp_rows, Accum& A) {
   const bool valid = u < c.nunits;
   const int uc = valid ? u : c.nunits - 1;
   uint32_t v[8];
@@ -492,23 +421,23 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
   if (NV || CODES) {
     const bool ex = exact_unit(a16);
     const float snv = div_const(fmaxf(a16, 1e-8f), 6.0f, RCP6);
-    float rlo, rhi;
-    recip_bounds(snv, rlo, rhi);
-    const uint64_t rlo2 = f2_pack(rlo, rlo), rhi2 = f2_pack(rhi, rhi), s2 = f2_pack(snv, snv);
-    uint32_t cw[2], dx[2], q[8];
+    const float r = rcp_approx(snv);
+    const float rlo = __fmul_rz(r, 1.0f - 9.5367431640625e-07f);   // 1 - 2^-20
+    const uint64_t r2 = f2_pack(r, r), rlo2 = f2_pack(rlo, rlo), s2 = f2_pack(snv, snv);
+    const uint64_t nb2 = f2_pack(-NV_COST_BIAS, -NV_COST_BIAS);
+    uint32_t cw[2], q[8];
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
-      float l[8], h[8];
+      float cc[8], l[8];
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         const uint64_t w2 = f2_from_bf16x2(v[4 * hf + p]);
-        f2_unpack(f2_mul_rz(w2, rlo2), l[2 * p], l[2 * p + 1]);
-        f2_unpack(f2_mul_rz(w2, rhi2), h[2 * p], h[2 * p + 1]);
+        if (NV) f2_unpack(f2_fma_rn(w2, r2, nb2), cc[2 * p], cc[2 * p + 1]);
+        if (CODES) f2_unpack(f2_mul_rz(w2, rlo2), l[2 * p], l[2 * p + 1]);
       }
-      uint32_t (&qh)[4] = *reinterpret_cast<uint32_t(*)[4]>(q + 4 * hf);
-      nv_codes4(l, h, cw[hf], dx[hf], qh);
+      if (NV) nv_cost4(cc, *reinterpret_cast<uint32_t(*)[4]>(q + 4 * hf));
+      if (CODES) cw[hf] = nv_export4(l);
     }
-    const uint32_t ux = dx[0] | dx[1];
     if (NV) {
       float pe = 0.0f, po = 0.0f;   // two accumulation chains
       uint32_t recw[8];
@@ -522,7 +451,7 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
         else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
         else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
       }
-      if (OUT) {   // uncertain pairs and exact-path units are rewritten by the fix-ups
+      if (OUT) {   // exact-path units are rewritten below
         if (valid) store_unit_words(c.outw + c.elem0 / 2, uc, sw, recw);
       }
       if (!OUT || OSSE) A.nv += (valid && !ex) ? pe + po : 0.0f;
@@ -532,18 +461,10 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
       c.amax_it[uc] = (uint16_t)a16b;
       A.tmax = max(A.tmax, a16b);
     }
-    const bool need = valid && (ux != 0 || ex);
-    const uint32_t bal = __ballot_sync(FULL, need);
-    if (bal) {
-      if (need) q_nv[A.cnt_nv + __popc(bal & lanemask_lt)] = (uint32_t)u;
-      A.cnt_nv += __popc(bal);
-      if (A.cnt_nv > FAST_QCAP - 32) {   // flush early only when the next unit could overflow
-        __syncwarp();
-        A.dnv += nv_fixup<HW>(q_nv, A.cnt_nv, c.st, lane, c.elem0, CODES ? c.codes_it - c.elem0 / 2 : nullptr,
-                              NV && (!OUT || OSSE), c.tasks, c.outw, c.h);
-        __syncwarp();
-        A.cnt_nv = 0;
-      }
+    if (ex && valid) {   // rare: amax below the 1e-8 floor or near fp32 overflow; overwrites the unit
+      A.dnv += nv_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, a16,
+                             CODES ? c.codes_it + 8 * (int64_t)uc : nullptr, NV && (!OUT || OSSE),
+                             (OUT && NV) ? c.outw + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
     }
   }
 
@@ -612,7 +533,9 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, u
   }
 }
 
-// Pass B over one unit: FP8 per-channel cost with the completed row maximum.
+// Pass B over one unit: FP8 per-channel cost with the completed row maximum.  The code is the
+// lower bracket's; in flagged rows (row_param) both brackets are converted too, and a unit with a
+// pair whose brackets differ is queued for the exact resolution.
 template <bool OUT, bool HW, bool OSSE>
 __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, uint32_t* q_f8,
                                             Accum& A) {
@@ -630,16 +553,22 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
   uint32_t recw[8];
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
-    float l[8], h[8];
+    float l[8], h[8], x[8];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const uint64_t w2 = f2_from_bf16x2(v[4 * hf + p]);
       f2_unpack(f2_mul_rz(w2, rlo2), l[2 * p], l[2 * p + 1]);
       f2_unpack(f2_mul_rz(w2, rhi2), h[2 * p], h[2 * p + 1]);
+      x[2 * p] = fminf(l[2 * p], h[2 * p]);
+      x[2 * p + 1] = fminf(l[2 * p + 1], h[2 * p + 1]);
     }
-    uint32_t dx, q[4];
-    f8_codes4(l, h, dx, q);
-    ux |= dx;
+    uint32_t q[4];
+    f8_codes_q4(x, q);
+    if (rp.flag) {   // which pairs lie on a midpoint's bracket
+      uint32_t dx, qq[4];
+      f8_codes4(l, h, dx, qq);
+      ux |= dx;
+    }
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
@@ -652,7 +581,7 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
       else pe = sq2_acc(bf16x2_sub(v[pp], rec), pe);
     }
   }
-  if (OUT) {   // uncertain pairs and exact-path rows are rewritten by the fix-ups
+  if (OUT) {   // the queued pairs and exact-path rows are rewritten by the fix-ups
     if (valid) store_unit_words(c.outw_f8 + c.elem0 / 2, uc, sw, recw);
   }
   if (!OUT || OSSE) A.f8 += (valid && !exf) ? pe + po : 0.0f;
@@ -669,9 +598,6 @@ __device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, u
     }
   }
 }
-
-// Named barrier over the 64 threads of warps 2k and 2k+1 (id 1 + k; id 0 is __syncthreads).
-__device__ __forceinline__ void pair_barrier(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
 
 __device__ __forceinline__ void fold(float& f, double& d) {
   d += (double)f;
@@ -690,10 +616,8 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
   uint32_t* qbase = reinterpret_cast<uint32_t*>(red + NWARPS * 3);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t* q_nv = qbase + warp * (2 * FAST_QCAP);
-  uint32_t* q_f8 = q_nv + FAST_QCAP;
-  uint32_t* tasks = qbase + NWARPS * 2 * FAST_QCAP + warp * FAST_TASK_CAP;
-  volatile int* qcnt = reinterpret_cast<volatile int*>(qbase + NWARPS * (2 * FAST_QCAP + FAST_TASK_CAP));   // [NWARPS][2]
+  uint32_t* q_f8 = qbase + warp * FAST_QCAP;
+  uint32_t* tasks = qbase + NWARPS * FAST_QCAP + warp * FAST_TASK_CAP;
   const uint32_t lanemask_lt = (1u << lane) - 1u;
   const int64_t n_items = L.item_prefix[L.n];
   const int64_t my_n = n_items > (int64_t)blockIdx.x ? (n_items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
@@ -722,7 +646,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
   A.nv = A.mx = A.f8 = 0.0f;
   A.dnv = A.dmx = A.df8 = 0.0;
   A.tmax = 0u;
-  A.cnt_nv = A.cnt_f8 = 0;
+  A.cnt_f8 = 0;
   int cur_t = -1, ti_proc = 0;
   auto flush_tensor = [&](int t) {   // CTA-uniform call
     const SweepDesc& d = L.t[t];
@@ -796,7 +720,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     if (NV || MX || CODES || F8) {
 #pragma unroll 1
       for (int k = 0; k < iters; ++k) {   // not unrolled: the body stays small enough for the instruction cache
-        unit_pass_a<NV, MX, F8, CODES, OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, lanemask_lt, warp_rows, q_nv, A);
+        unit_pass_a<NV, MX, F8, CODES, OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, warp_rows, A);
         if ((k & 3) == 3) {   // fp32 partials hold <= 64 squares
           fold(A.nv, A.dnv);
           fold(A.mx, A.dmx);
@@ -821,36 +745,10 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       fold(A.f8, A.df8);
     }
     __syncwarp();
-    if (F8 && (NV || CODES)) {
-      // Warps work in pairs: the even warp resolves both warps' NVFP4 queues, the odd warp
-      // both FP8 queues, so each drains one fuller batch instead of two small ones.  The
-      // pair barrier also orders the partner's code stores before any fix-up rewrite.
-      if (lane == 0) {
-        qcnt[2 * warp] = A.cnt_nv;
-        qcnt[2 * warp + 1] = A.cnt_f8;
-      }
-      pair_barrier(1 + (warp >> 1));
-      const int pw = warp ^ 1;
-      const uint32_t* pq = qbase + pw * (2 * FAST_QCAP);
-      if ((warp & 1) == 0) {
-        const int pc = qcnt[2 * pw];
-        if ((NV || CODES) && A.cnt_nv + pc)
-          A.dnv += nv_fixup_body<HW>(q_nv, A.cnt_nv, pq, pc, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
-                                     NV && (!OUT || OSSE), c.tasks, c.outw, c.h);
-      } else {
-        const int pc = qcnt[2 * pw + 1];
-        if (A.cnt_f8 + pc) A.df8 += f8_fixup_body<HW>(q_f8, A.cnt_f8, pq + FAST_QCAP, pc, c.st, lane, c.ramax, c.upr,
-                                                      c.rdiv, c.tasks, c.elem0, c.outw_f8, c.h);
-      }
-    } else {
-      if ((NV || CODES) && A.cnt_nv)
-        A.dnv += nv_fixup_body<HW>(q_nv, A.cnt_nv, q_nv, 0, c.st, lane, c.elem0, CODES ? d.nvfp4_codes : nullptr,
-                                   NV && (!OUT || OSSE), c.tasks, c.outw, c.h);
-      if (F8 && A.cnt_f8)
-        A.df8 += f8_fixup_body<HW>(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0,
-                                   c.outw_f8, c.h);
-    }
-    A.cnt_nv = A.cnt_f8 = 0;
+    if (F8 && A.cnt_f8)   // the warp's own queued FP8 units (flagged rows, exact-path rows)
+      A.df8 += f8_fixup_body<HW>(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0,
+                                 c.outw_f8, c.h);
+    A.cnt_f8 = 0;
     __syncthreads();   // stage s and the queues are free again
     if (*abort_flag) {
       if (j_abort < 0) j_abort = j;
@@ -871,7 +769,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
 size_t sweep_fast_smem_bytes() {
   return (size_t)FAST_NSTAGE * FAST_STAGE_BYTES + (FAST_NSTAGE + 1) * sizeof(uint64_t) +
          2 * FAST_MAX_ROWS * sizeof(uint32_t) + (FAST_THREADS / 32) * 3 * sizeof(double) +
-         (FAST_THREADS / 32) * (2 * FAST_QCAP + FAST_TASK_CAP + 2) * sizeof(uint32_t);
+         (FAST_THREADS / 32) * (FAST_QCAP + FAST_TASK_CAP) * sizeof(uint32_t);
 }
 
 template <bool NV, bool MX, bool F8, bool CODES, bool OUT = false, bool HW = false, bool OSSE = false>

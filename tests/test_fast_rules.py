@@ -1,0 +1,134 @@
+"""The fast sweep's division-free rounding rules against the reference's rule, on EVERY pair of
+bf16 values (group / row maximum a in [1, 2), every bf16 w with |w| <= a) — the ratios and
+roundings are the same in every binade of a inside the fast path's range [1e-8, 2^60).
+
+Reference (format_registry.py:194-233): x = fl32(w / s) with s = fl32(a / d) (d = 6 for NVFP4,
+448 for FP8 per channel), nearest point of the signed codebook with ties to the LOWER value; the
+NVFP4 export (export_native_compressed.py:114-136) takes the abs codebook with ties toward zero.
+
+Kernel rules, with r = rcp.approx(s) (within one ulp of 1/s: every r in {RN(1/s), its two
+neighbours} is tried), r_lo = RZ(r (1 - 2^-20)), r_hi = RZ(r (1 + 2^-20)) and the hardware
+conversions (round to nearest, ties to even, saturating):
+  * NVFP4 cost:    cvt_e2m1(fma(w, r, -2^-18))     (an absolute bias toward -inf)
+  * NVFP4 export:  cvt_e2m1(RZ(w r_lo))
+  * FP8 cost:      cvt_e4m3(min(RZ(w r_lo), RZ(w r_hi)))   (the lower of the two brackets)
+Why they hold: w and a have 8-bit significands, so w / (a / d) is either exactly a codebook
+midpoint m or at least ~2^-13 (relative) away from every midpoint, while the products are within
+2^-19 of it.  At an exact midpoint the reference's fl32(w / s) is m itself (a tie) whenever
+a / d is exact or m's significand is short enough; then "ties to lower" is "the bracket below".
+For NVFP4 that covers every case.  For FP8 per channel it leaves one family: rows where
+|a - 448 s| = 3 * 64 ulp(s) and s's significand is below 1.5, at midpoints with significand 21/16
+or 7/16 (the kernel flags such rows and resolves their near-midpoint pairs exactly)."""
+import numpy as np
+
+F32 = np.float32
+
+
+def _bf16_in(lo, hi):
+    b = np.arange(1 << 15, dtype=np.uint32)
+    with np.errstate(invalid="ignore"):
+        f = (b << 16).view(np.float32).astype(np.float64)
+    f = f[np.isfinite(f)]
+    return f[(f >= lo) & (f < hi)]
+
+
+def _rz32(v):
+    f = v.astype(F32).astype(np.float64)
+    return np.where(np.abs(f) > np.abs(v), np.nextafter(f.astype(F32), F32(0)).astype(np.float64), f)
+
+
+def _rne(p, mags, even, maxv):
+    a = np.abs(p)
+    i = np.clip(np.searchsorted(mags, a), 1, len(mags) - 1)
+    lo, hi = i - 1, i
+    mid = (mags[lo] + mags[hi]) / 2
+    pick = np.where(a < mid, lo, np.where(a > mid, hi, np.where(even[lo], lo, hi)))
+    pick = np.where(a >= maxv, len(mags) - 1, pick)
+    return np.where(np.signbit(p), -1.0, 1.0) * mags[pick]
+
+
+def _ties_lower(x, mags):
+    cb = np.concatenate([-mags[::-1], mags[1:]])
+    i = np.clip(np.searchsorted(cb, x), 1, len(cb) - 1)
+    lo, hi = cb[i - 1], cb[i]
+    return np.where(np.abs(hi - x) < np.abs(x - lo), hi, lo)
+
+
+def _ties_zero(x, mags):
+    a = np.abs(x)
+    i = np.clip(np.searchsorted(mags, a), 1, len(mags) - 1)
+    lo, hi = mags[i - 1], mags[i]
+    m = np.where(np.abs(hi - a) < np.abs(a - lo), hi, lo)
+    return np.where(x < 0, -1.0, 1.0) * np.minimum(m, mags[-1])
+
+
+def _reciprocals(s):
+    r0 = F32(1) / s
+    for r in (np.nextafter(r0, F32(0)), r0, np.nextafter(r0, F32(10))):
+        r = np.float64(r)
+        yield r, np.float64(_rz32(np.array([r * (1 - 2.0 ** -20)]))[0]), \
+            np.float64(_rz32(np.array([r * (1 + 2.0 ** -20)]))[0])
+
+
+E2M1 = np.array([0, .5, 1, 1.5, 2, 3, 4, 6], dtype=np.float64)
+E2M1_EVEN = np.arange(8) % 2 == 0
+
+
+def _e4m3():
+    vals = sorted({k * 2.0 ** -9 for k in range(8)} | {(1 + m / 8) * 2.0 ** (e - 7) for e in range(1, 16)
+                                                      for m in range(8)})
+    mags = np.array([v for v in vals if v <= 448], dtype=np.float64)
+    man = np.array([round(v / 2.0 ** -9) if v < 2.0 ** -6 else round((v / 2.0 ** np.floor(np.log2(v)) - 1) * 8)
+                    for v in mags])
+    return mags, man % 2 == 0
+
+
+def test_nvfp4_cost_and_export_rules_are_exact_for_every_bf16_pair():
+    ws = _bf16_in(0, 2.01)
+    ws = np.concatenate([ws, -ws])
+    bad = n = 0
+    for a in _bf16_in(1, 2):
+        w = ws[np.abs(ws) <= a]
+        s = F32(a) / F32(6)
+        x = (w.astype(F32) / s).astype(np.float64)
+        want_cost, want_exp = _ties_lower(x, E2M1), _ties_zero(x, E2M1)
+        for r, r_lo, _ in _reciprocals(s):
+            p = (w * r - 2.0 ** -18).astype(F32).astype(np.float64)       # fma, one rounding
+            bad += np.count_nonzero(_rne(p, E2M1, E2M1_EVEN, 6.0) != want_cost)
+            bad += np.count_nonzero(_rne(_rz32(w * r_lo), E2M1, E2M1_EVEN, 6.0) != want_exp)
+            n += 2 * w.size
+    assert n > 10_000_000 and bad == 0
+
+
+def fp8_row_flag(a: float) -> bool:
+    """The kernel's per-row flag (rows whose near-midpoint pairs it resolves exactly): with
+    s = fl32(a / 448), d = a - 448 s (exact as one FMA: a multiple of 64 ulp(s), at most 3 of them)
+    and s's significand: |d| >= 160 ulp(s) (i.e. 3 x 64) and significand < 1.5."""
+    s = F32(a) / F32(448)
+    d = np.float64(a) - 448.0 * np.float64(s)
+    u = np.float64(np.spacing(s))
+    sig_bits = int(np.array([s], dtype=F32).view(np.uint32)[0]) & 0x7FFFFF
+    return abs(d) >= 160 * u and sig_bits < 0x400000
+
+
+def test_fp8_channel_lower_bracket_rule_exact_outside_flagged_rows():
+    mags, even = _e4m3()
+    ws = _bf16_in(0, 2.01)
+    ws = np.concatenate([ws, -ws])
+    n = 0
+    flagged_with_misses = 0
+    for a in _bf16_in(1, 2):
+        w = ws[np.abs(ws) <= a]
+        s = F32(a) / F32(448)
+        x = (w.astype(F32) / s).astype(np.float64)
+        want = _ties_lower(x, mags)
+        miss = 0
+        for _, r_lo, r_hi in _reciprocals(s):
+            got = _rne(np.minimum(_rz32(w * r_lo), _rz32(w * r_hi)), mags, even, 448.0)
+            miss += np.count_nonzero(got != want)
+            n += w.size
+        if miss:
+            assert fp8_row_flag(a), (a, miss)
+            flagged_with_misses += 1
+    assert n > 10_000_000
+    assert flagged_with_misses > 0      # the flagged family exists: the exact resolution is needed
