@@ -254,6 +254,13 @@ int pq_nvfp4_scales(int n, const uint16_t* const* amax, const int64_t* n_groups,
                     const float* override_dev, uint8_t* const* scales,
                     float* global_div_dev, void* stream);
 
+/* compute_nvfp4_global_real (export_native_compressed.py:1045-1055) of each
+ * of `batch` [rows, cols] slices from one read of the weights:
+ * global_real[b] = max(max_g(max(amax_g, 1e-12) / 6) / 448, 1e-12) (IEEE
+ * divisions).  scratch holds batch + 1 uint32 (zeroed here); batch <= 256. */
+int pq_nvfp4_global_real(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint32_t* scratch,
+                         float* global_real, void* stream);
+
 /* One-call NVFP4 export of a [batch, rows, cols] tensor with a per-slice
  * global (batch == 1: quantize_dequantize_nvfp4; batch == E:
  * quantize_dequantize_nvfp4_packed, export_native_compressed.py:1058-1129).

@@ -33,7 +33,7 @@ EXPORTED = [
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
     "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_weighted_sse_fused_batch",
     "pq_cost_qdq_fused_sse_list", "pq_grad_sq_acc", "pq_set_wait_limit", "pq_default_wait_limit",
-    "pq_sumsq_rows_full",
+    "pq_sumsq_rows_full", "pq_nvfp4_global_real",
 ]
 
 
@@ -83,6 +83,7 @@ def load() -> ctypes.CDLL:
         "pq_nvfp4_scales": [I, ctypes.POINTER(P), ctypes.POINTER(I64), P, ctypes.POINTER(ctypes.c_int32), P,
                             ctypes.POINTER(P), P, V],
         "pq_nvfp4_pack": [P, I64, I64, I64, P, P, P, P, P, P, V],
+        "pq_nvfp4_global_real": [P, I64, I64, I64, P, P, V],
         "pq_nvfp4_pack_noalloc": [P, I64, I64, I64, P, P, P, P, V],
         "pq_mxfp8_pack": [P, I64, I64, P, P, V],
         "pq_fp8_channel_pack": [P, I64, I64, P, P, V],
@@ -469,6 +470,18 @@ def grad_sq_acc(gy: torch.Tensor, x: torch.Tensor, h: torch.Tensor, sums: torch.
 # ---------------------------------------------------------------------------
 # Export path
 # ---------------------------------------------------------------------------
+
+def nvfp4_global_real(w: torch.Tensor, batch: int = 1) -> torch.Tensor:
+    """compute_nvfp4_global_real of each of `batch` equal slices of w, from one read: fp32 [batch]."""
+    wb = as_bf16_cuda(w, "nvfp4_global_real")
+    cols = wb.shape[-1]
+    rows = wb.numel() // cols // max(batch, 1)
+    out = torch.empty(batch, dtype=torch.float32, device=wb.device)
+    scratch = torch.empty(batch + 1, dtype=torch.int32, device=wb.device)
+    _check(load().pq_nvfp4_global_real(_ptr(wb), batch, rows, cols, _ptr(scratch), _ptr(out), _stream(wb)),
+           "pq_nvfp4_global_real", f"NVFP4 group_size=16 ∤ {cols}")
+    return out
+
 
 def nvfp4_codes(w: torch.Tensor, batch: int, codes: torch.Tensor, amax: torch.Tensor, tmax: torch.Tensor):
     cols = w.shape[-1]

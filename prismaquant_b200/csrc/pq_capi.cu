@@ -560,6 +560,18 @@ int pq_nvfp4_pack(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, 
   return PQ_OK;
 }
 
+int pq_nvfp4_global_real(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint32_t* scratch,
+                         float* global_real, void* stream) {
+  if (batch < 0 || rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  if (cols % 16) return PQ_ERR_SHAPE;
+  if (batch == 0) return PQ_OK;
+  if (batch > pq::MAX_SCALE_SLICES) return PQ_ERR_LIMIT;
+  if (!scratch || !global_real || (rows > 0 && !w)) return PQ_ERR_NULL;
+  if (!aligned(w, 16) || !aligned(scratch, 4)) return PQ_ERR_ALIGN;
+  return cuda_status(pq::launch_nvfp4_global(w, rows * cols, (int)batch, scratch, global_real, num_sms_current(),
+                                             (cudaStream_t)stream));
+}
+
 int pq_mxfp8_pack(const uint16_t* w, int64_t n_rows, int64_t cols, uint8_t* q, uint8_t* scale_e8m0, void* stream) {
   if (n_rows < 0 || cols < 1) return PQ_ERR_SHAPE;
   if (cols % 32) return PQ_ERR_SHAPE;

@@ -78,6 +78,8 @@ struct ScalesLaunch {
 cudaError_t launch_nvfp4_codes(const uint16_t* w, int64_t batch, int64_t rows, int64_t cols, uint8_t* codes,
                                uint16_t* amax, uint32_t* tmax, int num_sms, cudaStream_t stream);
 cudaError_t launch_nvfp4_scales(const ScalesLaunch& L, int64_t max_groups, int num_sms, cudaStream_t stream);
+cudaError_t launch_nvfp4_global(const uint16_t* w, int64_t n_per, int n_slices, uint32_t* scratch, float* global_real,
+                                int num_sms, cudaStream_t stream);
 cudaError_t launch_mxfp8_pack(const uint16_t* w, int64_t n_elems, uint8_t* q, uint8_t* sc, int num_sms,
                               cudaStream_t stream);
 cudaError_t launch_fp8_channel_pack(const uint16_t* w, int64_t rows, int64_t cols, uint8_t* q, float* scale,

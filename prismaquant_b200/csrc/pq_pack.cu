@@ -87,6 +87,64 @@ __device__ __forceinline__ float nvfp4_global_from_tmax(uint32_t tmax_bits) {
   return fmaxf(__fdiv_rn(sg, 448.0f), 1e-12f);
 }
 
+// compute_nvfp4_global_real (export_native_compressed.py:1045-1055) of `n_slices` consecutive
+// slices of n_per bf16 values: one read of the weights.  Each block reduces its elements' bf16
+// magnitude bits (two per 32-bit max) and adds its slices' maxima into tmax[] (float bits,
+// atomic max; zeroed by the caller); the last block to finish turns every slice's maximum into
+// its global_real.  The 16-groups need not be formed: the max over groups of max(amax, 1e-12) / 6
+// is the same quotient of the slice's max (round-to-nearest is monotone).
+__global__ void __launch_bounds__(256) nvfp4_global_kernel(const uint16_t* __restrict__ w, int64_t n_per, int n_slices,
+                                                           uint32_t* tmax, unsigned int* done, float* global_real) {
+  const int64_t total = n_per * n_slices;
+  const int64_t n8 = total >> 3;   // the caller guarantees n_per % 8 == 0 and 16-byte alignment
+  const uint4* v = reinterpret_cast<const uint4*>(w);
+  __shared__ uint32_t s_max[MAX_SCALE_SLICES];
+  for (int i = threadIdx.x; i < n_slices; i += blockDim.x) s_max[i] = 0u;
+  __syncthreads();
+  const int64_t per8 = n_per >> 3;
+  int slice = -1;
+  uint32_t m = 0u;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int sl = (int)(i / per8);
+    if (sl != slice) {
+      if (slice >= 0) atomicMax(&s_max[slice], m);
+      slice = sl;
+      m = 0u;
+    }
+    const uint4 x = __ldg(v + i);
+    const uint32_t a = bf16x2_maxabs(bf16x2_maxabs(x.x, x.y), bf16x2_maxabs(x.z, x.w));
+    m = max(m, max(a & 0x7FFFu, (a >> 16) & 0x7FFFu));
+  }
+  if (slice >= 0) atomicMax(&s_max[slice], m);
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_slices; i += blockDim.x)
+    if (s_max[i]) atomicMax(&tmax[i], s_max[i] << 16);
+  __threadfence();
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) last = atomicAdd(done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < n_slices; i += blockDim.x)
+    global_real[i] = nvfp4_global_from_tmax(*(volatile uint32_t*)&tmax[i]);
+}
+
+cudaError_t launch_nvfp4_global(const uint16_t* w, int64_t n_per, int n_slices, uint32_t* scratch, float* global_real,
+                                int num_sms, cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)(n_slices + 1) * sizeof(uint32_t), stream);
+  if (e != cudaSuccess) return e;
+  const int64_t n8 = n_per * n_slices / 8;
+  int64_t blocks = (n8 + 255) / 256;
+  const int64_t cap = (int64_t)num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  nvfp4_global_kernel<<<(unsigned)blocks, 256, 0, stream>>>(w, n_per, n_slices, scratch,
+                                                            reinterpret_cast<unsigned int*>(scratch + n_slices),
+                                                            global_real);
+  return cudaGetLastError();
+}
+
 // Block scale byte of one group: e4m3(clamp(RN(RN(max(amax, 1e-12) / 6) / glob), 0, 448)), RNE
 // (export_native_compressed.py:1099-1102), by IEEE division.
 __device__ __forceinline__ uint32_t nvfp4_scale_exact(uint32_t abits, float glob) {

@@ -39,16 +39,13 @@ def _need_group(group_size: int, expected: int, fmt: str):
 
 def compute_nvfp4_global_real(weight: torch.Tensor, group_size: int = 16) -> torch.Tensor:
     """(max over 16-groups of max(amax,1e-12)/6) / 448, clamped at 1e-12; the max of
-    the rounded per-group quotients equals the quotient of the tensor amax."""
+    the rounded per-group quotients equals the quotient of the tensor amax.  A 0-d fp32
+    tensor on the weight's device, as the reference returns."""
     _need_group(group_size, 16, "NVFP4")
     rows, cols = weight.shape
     if cols % group_size:
         raise ValueError(f"NVFP4 group_size={group_size} ∤ {cols}")
-    w = _lib.as_bf16_cuda(weight, "compute_nvfp4_global_real")
-    m = w.abs().amax().float().clamp_min(1e-12)
-    # tensor / tensor is an IEEE division on CUDA (tensor / python-scalar multiplies by a reciprocal)
-    six, fp8max = torch.full_like(m, NVFP4_MAX), torch.full_like(m, FP8_E4M3_MAX)
-    return torch.div(torch.div(m, six), fp8max).clamp_min(1e-12)
+    return _lib.nvfp4_global_real(weight, 1)[0]   # one read, one kernel (pq_nvfp4_global_real)
 
 
 def quantize_dequantize_nvfp4(weight: torch.Tensor, group_size: int = 16,

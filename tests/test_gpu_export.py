@@ -244,3 +244,27 @@ def test_streaming_export_to_safetensors():
             assert torch.equal(loaded[f"{n}.weight_scale"].view(torch.uint8), s.view(torch.uint8).cpu())
             assert torch.equal(loaded[f"{n}.weight_global_scale"], g.cpu())
             assert loaded[f"{n}.input_global_scale"].tolist() == [1.0]
+
+
+def test_global_real_kernel_batched_and_joint(full_digests, monkeypatch):
+    """pq_nvfp4_global_real: per-slice globals of a stacked tensor equal the one-slice call and the
+    oracle, and the fused-sibling joint globals of the full-size q/k/v + gate/up group equal the
+    reference's (full_digests.json).  No torch reduction runs on the path (abs/amax are poisoned)."""
+    from prismaquant_b200 import _lib
+    bits = O.synthetic_weight_bits((6, 96, 256), seed=3, std=0.05, outlier_frac=0.01)
+    w = to_cuda_bf16(bits)
+    got = _lib.nvfp4_global_real(w, 6)
+    for b in range(6):
+        assert float(got[b]) == float(O.nvfp4_global_real(O.bf16_bits_to_f32(bits[b])))
+        assert float(got[b]) == float(enc.compute_nvfp4_global_real(w[b]))
+
+    def boom(*a, **k):
+        raise AssertionError("torch reduction on the global path")
+    dg = full_digests["siblings"]
+    ws = {n: to_cuda_bf16(O.synthetic_weight_bits(tuple(dg[n]["shape"]), seed=dg[n]["seed"])) for n in dg}
+    monkeypatch.setattr(torch.Tensor, "amax", boom)
+    monkeypatch.setattr(torch.Tensor, "abs", boom)
+    for group in (("q_proj", "k_proj", "v_proj"), ("gate_proj", "up_proj")):
+        joint = max(float(enc.compute_nvfp4_global_real(ws[n])) for n in group)
+        for n in group:
+            assert joint == dg[n]["joint_global_real"], n
