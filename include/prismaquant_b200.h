@@ -341,6 +341,16 @@ int pq_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm
                      const int64_t* token_idx, double* acc, void* stream);
 
 /* Housekeeping. */
+/* pq_tokennorm_dot_seg: the per-token Fisher estimate of a routed packed-expert
+ * projection in one launch (north-star form of sensitivity_probe.py:555-728's
+ * per-expert loop).  g [R, d] bf16 holds the output gradients of the R (token,
+ * expert) rows, sorted by expert; seg[r] in [0, n_seg) is row r's expert and
+ * token_idx[r] its token (NULL: xnorm is already per row).  For each expert e:
+ * acc[2e] += sum_{r in e} xnorm[token(r)] * ||g_r||^2, acc[2e+1] += its rows.
+ * Rows of one expert must be contiguous. */
+int pq_tokennorm_dot_seg(const uint16_t* g, int64_t R, int64_t d, const float* xnorm, const int64_t* token_idx,
+                         const int32_t* seg, int64_t n_seg, double* acc, void* stream);
+
 int pq_device_error(int* code);          /* reads and clears the device error word */
 
 /* Failure-detection hook (no counterpart in the reference): the iteration

@@ -33,7 +33,7 @@ EXPORTED = [
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
     "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_weighted_sse_fused_batch",
     "pq_cost_qdq_fused_sse_list", "pq_grad_sq_acc", "pq_set_wait_limit", "pq_default_wait_limit",
-    "pq_sumsq_rows_full", "pq_nvfp4_global_real",
+    "pq_sumsq_rows_full", "pq_nvfp4_global_real", "pq_tokennorm_dot_seg",
 ]
 
 
@@ -91,6 +91,7 @@ def load() -> ctypes.CDLL:
         "pq_sumsq_rows_full": [P, I64, I64, P, P, P, V],
         "pq_rownorm2": [P, I64, I64, P, V],
         "pq_tokennorm_dot": [P, I64, I64, P, P, P, V],
+        "pq_tokennorm_dot_seg": [P, I64, I64, P, P, P, I64, P, V],
         "pq_device_error": [ctypes.POINTER(ctypes.c_int)],
         "pq_set_wait_limit": [ctypes.c_uint32],
         "pq_default_wait_limit": [],
@@ -582,6 +583,22 @@ def rownorm2(x: torch.Tensor) -> torch.Tensor:
     out = torch.empty(xb.numel() // d, dtype=torch.float32, device=xb.device)
     _check(load().pq_rownorm2(_ptr(xb), out.numel(), d, _ptr(out), _stream(xb)), "pq_rownorm2")
     return out
+
+
+def tokennorm_dot_seg(g: torch.Tensor, xnorm: torch.Tensor, seg: torch.Tensor, acc: torch.Tensor,
+                      token_idx: torch.Tensor | None = None):
+    """Routed experts in one launch: rows of g [R, d] sorted by expert seg[r] (int32);
+    acc[e, 0] += sum over e's rows of xnorm[token_idx[r]] * ||g_r||^2, acc[e, 1] += row count."""
+    gb = as_bf16_cuda(g, "tokennorm_dot_seg")
+    d = gb.shape[-1]
+    R = gb.numel() // d
+    if acc.dtype != torch.float64 or not acc.is_contiguous() or acc.dim() != 2 or acc.shape[1] != 2:
+        raise TypeError("tokennorm_dot_seg: acc must be a contiguous float64 [E, 2] tensor")
+    seg = seg.to(torch.int32).contiguous()
+    if token_idx is not None:
+        token_idx = token_idx.to(torch.int64).contiguous()
+    _check(load().pq_tokennorm_dot_seg(_ptr(gb), R, d, _ptr(xnorm), _ptr(token_idx), _ptr(seg), acc.shape[0],
+                                       _ptr(acc), _stream(gb)), "pq_tokennorm_dot_seg")
 
 
 def tokennorm_dot(g: torch.Tensor, xnorm: torch.Tensor, acc: torch.Tensor, token_idx: torch.Tensor | None = None):

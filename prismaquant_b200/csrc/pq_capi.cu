@@ -623,4 +623,13 @@ int pq_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm
       pq::launch_tokennorm_dot(g, T, d, xnorm, token_idx, acc, num_sms_current(), (cudaStream_t)stream));
 }
 
+int pq_tokennorm_dot_seg(const uint16_t* g, int64_t R, int64_t d, const float* xnorm, const int64_t* token_idx,
+                         const int32_t* seg, int64_t n_seg, double* acc, void* stream) {
+  if (R < 0 || d < 1 || n_seg < 0) return PQ_ERR_SHAPE;
+  if (R == 0) return PQ_OK;
+  if (!g || !xnorm || !seg || !acc) return PQ_ERR_NULL;
+  return cuda_status(
+      pq::launch_tokennorm_seg(g, R, d, xnorm, token_idx, seg, acc, num_sms_current(), (cudaStream_t)stream));
+}
+
 }  // extern "C"

@@ -176,6 +176,42 @@ __global__ void __launch_bounds__(256) tokennorm_dot_kernel(const uint16_t* __re
   }
 }
 
+// Routed experts in one launch: rows of g are the (token, expert) pairs of one packed projection,
+// sorted by expert, row r belonging to expert seg[r]; acc[e] += (sum over e's rows of
+// xnorm[tok(r)] * ||g_r||^2, row count).  Each warp takes a contiguous run of rows and flushes its
+// running sums at every change of expert (fp64 atomics), so a run costs one atomic per expert it
+// touches.  tok == NULL: row r's norm is xnorm[r] (inputs already in row order).
+__global__ void __launch_bounds__(256) tokennorm_seg_kernel(const uint16_t* __restrict__ g, int64_t R, int64_t d,
+                                                           const float* __restrict__ xnorm,
+                                                           const int64_t* __restrict__ tok,
+                                                           const int32_t* __restrict__ seg, double* acc) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t per = (R + nw - 1) / nw;
+  const int64_t r0 = gw * per, r1 = min(R, r0 + per);
+  double a = 0.0, cnt = 0.0;
+  int cur = -1;
+  for (int64_t r = r0; r < r1; ++r) {
+    const int e = seg[r];
+    if (e != cur) {
+      if (cur >= 0 && lane == 0) {
+        atomicAdd(acc + 2 * cur, a);
+        atomicAdd(acc + 2 * cur + 1, cnt);
+      }
+      cur = e;
+      a = cnt = 0.0;
+    }
+    const double gn = row_sumsq(g + r * d, d, lane);
+    a += gn * (double)xnorm[tok != nullptr ? tok[r] : r];
+    cnt += 1.0;
+  }
+  if (cur >= 0 && lane == 0) {
+    atomicAdd(acc + 2 * cur, a);
+    atomicAdd(acc + 2 * cur + 1, cnt);
+  }
+}
+
 static inline int warp_grid(int64_t rows, int num_sms) {
   int64_t blocks = (rows + 7) / 8;
   const int64_t cap = (int64_t)num_sms * 8;
@@ -204,6 +240,16 @@ cudaError_t launch_rownorm2(const uint16_t* x, int64_t T, int64_t d, float* out,
 cudaError_t launch_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm,
                                  const int64_t* token_idx, double* acc, int num_sms, cudaStream_t stream) {
   tokennorm_dot_kernel<<<warp_grid(T, num_sms), 256, 0, stream>>>(g, T, d, xnorm, token_idx, acc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tokennorm_seg(const uint16_t* g, int64_t R, int64_t d, const float* xnorm, const int64_t* tok,
+                                 const int32_t* seg, double* acc, int num_sms, cudaStream_t stream) {
+  int64_t blocks = (R + 8 * 8 - 1) / (8 * 8);   // about eight rows per warp
+  const int64_t cap = (int64_t)num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  tokennorm_seg_kernel<<<(unsigned)blocks, 256, 0, stream>>>(g, R, d, xnorm, tok, seg, acc);
   return cudaGetLastError();
 }
 

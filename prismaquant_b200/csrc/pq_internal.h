@@ -91,6 +91,8 @@ cudaError_t launch_sumsq_rows(const uint16_t* g, int64_t rows, int64_t cols, dou
 cudaError_t launch_sumsq_rows_full(const uint16_t* g, int64_t rows, int64_t cols, double* total, float* per_row,
                                    float* h, int num_sms, cudaStream_t stream);
 cudaError_t launch_rownorm2(const uint16_t* x, int64_t T, int64_t d, float* out, int num_sms, cudaStream_t stream);
+cudaError_t launch_tokennorm_seg(const uint16_t* g, int64_t R, int64_t d, const float* xnorm, const int64_t* tok,
+                                 const int32_t* seg, double* acc, int num_sms, cudaStream_t stream);
 cudaError_t launch_tokennorm_dot(const uint16_t* g, int64_t T, int64_t d, const float* xnorm,
                                  const int64_t* token_idx, double* acc, int num_sms, cudaStream_t stream);
 

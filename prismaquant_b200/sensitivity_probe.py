@@ -161,13 +161,36 @@ def install_packed_expert_hooks(model: nn.Module, accumulator: dict, channel_acc
     return meta
 
 
+class _SegTokenNormCapture(torch.autograd.Function):
+    """Identity on the row-stacked outputs of a routed packed projection (rows grouped by expert);
+    backward adds, for every expert, sum over its rows of xnorm[token] * ||dy_row||^2 and its row
+    count into acc [E, 2], in one launch (pq_tokennorm_dot_seg), without touching the gradient.
+    `tok` empty: xnorm is already one value per row."""
+
+    @staticmethod
+    def forward(ctx, y, xnorm, tok, seg, acc):
+        ctx.save_for_backward(xnorm, tok, seg)
+        ctx.acc = acc
+        return y.view_as(y)
+
+    @staticmethod
+    def backward(ctx, gy):
+        xnorm, tok, seg = ctx.saved_tensors
+        _lib.tokennorm_dot_seg(gy.detach().reshape(-1, gy.shape[-1]), xnorm, seg, ctx.acc,
+                               token_idx=tok if tok.numel() else None)
+        return gy, None, None, None, None
+
+
 def install_routed_expert_hooks(model: nn.Module, accumulator: dict) -> dict[str, dict]:
-    """Per-token estimator for packed experts with gate_up_proj [E, 2I, H] /
-    down_proj [E, H, I] (HF Qwen3MoeExperts layout): the experts forward is
-    re-expressed as the same routed loop (token_idx per expert, act(gate)*up,
-    routing-weighted index_add) with ||x_t||^2 / ||dy_t||^2 captured around
-    each expert's two projections.  accumulator[name] is a [E, 2] float64
-    device tensor (trace, tokens) per packed parameter."""
+    """Per-token estimator for packed experts with gate_up_proj [E, 2I, H] / down_proj [E, H, I]
+    (HF Qwen3MoeExperts layout), the reference's per-expert loop (sensitivity_probe.py:555-728)
+    with its Fisher capture fused: the experts forward keeps the model's own arithmetic (one GEMM
+    per hit expert, act(gate) * up, routing-weighted index_add in expert order, so its output is
+    bit-identical), but each projection's outputs are stacked by expert and captured ONCE: the
+    forward takes ||x_t||^2 of every token (pq_rownorm2) and ||h_r||^2 of every routed row, and
+    the backward runs one pq_tokennorm_dot_seg launch per projection that adds, for each expert,
+    sum over its routed tokens of ||x_t||^2 ||g_{t,e}||^2.  accumulator[name] is a [E, 2]
+    float64 device tensor (trace, tokens) per packed parameter."""
     meta = {}
     for qname, module in model.named_modules():
         if not _is_packed_experts_module(module):
@@ -187,15 +210,29 @@ def install_routed_expert_hooks(model: nn.Module, accumulator: dict) -> dict[str
             with torch.no_grad():
                 mask = F.one_hot(top_k_index, num_classes=_m.gate_up_proj.shape[0]).permute(2, 1, 0)
                 hit = torch.greater(mask.sum(dim=(-1, -2)), 0).nonzero()
-            for e in hit.flatten().tolist():
-                top_k_pos, token_idx = torch.where(mask[e])
-                x = hidden_states[token_idx]
-                gu = _TokenNormCapture.apply(F.linear(x, _m.gate_up_proj[e]), _lib.rownorm2(x.detach()), _gu[e])
-                gate, up = gu.chunk(2, dim=-1)
-                h = _m.act_fn(gate) * up
-                out = _TokenNormCapture.apply(F.linear(h, _m.down_proj[e]), _lib.rownorm2(h.detach()), _dn[e])
-                out = out * top_k_weights[token_idx, top_k_pos, None]
-                final.index_add_(0, token_idx, out.to(final.dtype))
+            experts = hit.flatten().tolist()
+            if not experts:
+                return final
+            toks, poss = [], []
+            for e in experts:
+                p_, t_ = torch.where(mask[e])
+                poss.append(p_)
+                toks.append(t_)
+            sizes = [t.numel() for t in toks]
+            tok, pos = torch.cat(toks), torch.cat(poss)
+            seg = torch.repeat_interleave(torch.tensor(experts, dtype=torch.int32, device=tok.device),
+                                          torch.tensor(sizes, device=tok.device))
+            xn = _lib.rownorm2(hidden_states.detach())
+            gu = torch.cat([F.linear(hidden_states[t], _m.gate_up_proj[e]) for e, t in zip(experts, toks)])
+            gu = _SegTokenNormCapture.apply(gu, xn, tok, seg, _gu)
+            gate, up = gu.chunk(2, dim=-1)
+            h = _m.act_fn(gate) * up
+            hn = _lib.rownorm2(h.detach())
+            dn = torch.cat([F.linear(he, _m.down_proj[e]) for e, he in zip(experts, torch.split(h, sizes))])
+            dn = _SegTokenNormCapture.apply(dn, hn, tok.new_empty(0), seg, _dn)
+            dn = dn * top_k_weights[tok, pos, None]
+            for t_, o in zip(toks, torch.split(dn, sizes)):
+                final.index_add_(0, t_, o.to(final.dtype))
             return final
 
         module.forward = routed

@@ -303,3 +303,49 @@ def test_fisher_bridge_kernels_match_reference(n):
     assert len(calls) == x.shape[0]
     assert acc.stats[n]["n_tokens_seen"] == int(d[f"bridge16/{n}/n_tokens_seen"][0])
     assert_rel(acc.stats[n]["h_trace_raw"], float(d[f"bridge16/{n}/h_trace_raw"][0]), 1e-5, n)
+
+
+def test_tokennorm_seg_vs_oracle():
+    """pq_tokennorm_dot_seg: rows of g grouped by expert, each expert's sum of xnorm[token] *
+    ||g_r||^2 and its row count, against the per-expert oracle (rel 1e-5); empty experts stay 0."""
+    rng = np.random.default_rng(4)
+    T, d, E = 300, 768, 9
+    xb = O.synthetic_weight_bits((T, 2048), seed=5, std=1.0)
+    sizes = [37, 0, 120, 1, 64, 0, 250, 8, 40]
+    toks = [rng.choice(T, n, replace=False) for n in sizes]
+    tok = np.concatenate(toks).astype(np.int64)
+    seg = np.repeat(np.arange(E, dtype=np.int32), sizes)
+    gb = O.synthetic_weight_bits((tok.size, d), seed=6, std=0.02)
+    xn = _lib.rownorm2(to_cuda_bf16(xb))
+    acc = torch.zeros(E, 2, dtype=torch.float64, device="cuda")
+    _lib.tokennorm_dot_seg(to_cuda_bf16(gb), xn, torch.from_numpy(seg).cuda(), acc,
+                           token_idx=torch.from_numpy(tok).cuda())
+    off = 0
+    for e, n in enumerate(sizes):
+        if n == 0:
+            assert float(acc[e, 0]) == 0.0 and float(acc[e, 1]) == 0.0
+            continue
+        want = O.tokennorm_trace(xb, gb[off:off + n], token_idx=tok[off:off + n])
+        assert_rel(float(acc[e, 0]), want, 1e-5, str(e))
+        assert float(acc[e, 1]) == n
+        off += n
+
+
+def test_routed_hooks_one_launch_per_projection(monkeypatch):
+    """The routed estimator's backward is one pq_tokennorm_dot_seg launch per projection,
+    whatever the number of experts hit."""
+    from transformers import Qwen3MoeConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeSparseMoeBlock
+    cfg = Qwen3MoeConfig(hidden_size=128, moe_intermediate_size=64, num_experts=16, num_experts_per_tok=4,
+                         norm_topk_prob=True)
+    torch.manual_seed(2)
+    blk = Qwen3MoeSparseMoeBlock(cfg).cuda().to(torch.bfloat16)
+    calls = []
+    orig = _lib.tokennorm_dot_seg
+    monkeypatch.setattr(_lib, "tokennorm_dot_seg", lambda *a, **k: (calls.append(1), orig(*a, **k))[1])
+    acc = {}
+    sp.install_routed_expert_hooks(blk, acc)
+    x = torch.randn(1, 200, 128, device="cuda", dtype=torch.bfloat16)
+    blk(x).float().pow(2).sum().backward()
+    assert len(calls) == 2
+    assert float(acc["experts.gate_up_proj"][:, 1].sum()) == 200 * 4
