@@ -44,7 +44,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama8b",
                     choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b", "outerr8b", "kernels",
-                             "costtable8b"])
+                             "costtable8b", "fishermoe"])
+    ap.add_argument("--moe-tokens", type=int, default=8192, help="tokens per step of the fishermoe workload")
     ap.add_argument("--fisher-seqs", type=int, default=64, help="calibration sequences (split across ranks)")
     ap.add_argument("--fisher-batch", type=int, default=4, help="sequences per backward on each rank")
     ap.add_argument("--fisher-detail", action="store_true",
@@ -419,6 +420,90 @@ def run_kernels(a, local):
                       "clocks": clk.summary()}), flush=True)
 
 
+def run_fisher_moe(a, local):
+    """Routed packed-expert Fisher probe on one Qwen3-30B-A3B-shaped sparse MoE block (hidden 2048,
+    128 experts of intermediate 768, top-8 routing, bf16, random init): one step = forward +
+    backward of --moe-tokens tokens with the per-token estimator installed
+    (install_routed_expert_hooks: one pq_rownorm2 per projection input and one
+    pq_tokennorm_dot_seg per projection's output gradient).  Reports tokens/s and the hook
+    kernels' own time and HBM bytes (x and h read for their norms, the two output gradients read
+    once) against the measured HBM peak."""
+    import torch
+    from transformers import Qwen3MoeConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeSparseMoeBlock
+
+    from prismaquant_b200 import _lib
+    from prismaquant_b200 import sensitivity_probe as sp
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = Qwen3MoeConfig(hidden_size=2048, moe_intermediate_size=768, num_experts=128, num_experts_per_tok=8,
+                         norm_topk_prob=True)
+    torch.manual_seed(0)
+    blk = Qwen3MoeSparseMoeBlock(cfg).to(device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for p in blk.parameters():
+            p.normal_(std=0.02)
+            p.requires_grad_(False)
+    acc = {}
+    sp.install_routed_expert_hooks(blk, acc)
+    kev, kbytes = [], [0]
+    orig_rn, orig_seg = _lib.rownorm2, _lib.tokennorm_dot_seg
+
+    def timed(fn, nbytes):
+        def w(*args, **kw):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = fn(*args, **kw)
+            e1.record()
+            kev.append((e0, e1))
+            kbytes[0] += nbytes(*args, **kw)
+            return out
+        return w
+    sp._lib.rownorm2 = timed(orig_rn, lambda x: x.numel() * 2 + (x.numel() // x.shape[-1]) * 4)
+    sp._lib.tokennorm_dot_seg = timed(orig_seg, lambda g, xn, seg, acc_, token_idx=None: g.numel() * 2 + 8 * (
+        g.numel() // g.shape[-1]))
+    T = a.moe_tokens
+    gx = torch.Generator(device=dev).manual_seed(1)
+    xs = [torch.randn(1, T, 2048, device=dev, dtype=torch.bfloat16, generator=gx) for _ in range(2)]
+
+    def step(i):
+        x = xs[i % 2].clone().requires_grad_(True)
+        out = blk(x)
+        out = out[0] if isinstance(out, tuple) else out
+        out.float().pow(2).sum().backward()
+
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    kev.clear()
+    kbytes[0] = 0
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record()
+        for i in range(a.steps):
+            step(i)
+        t1.record()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    k_ms = sum(e0.elapsed_time(e1) for e0, e1 in kev)
+    hbm, peak_kind = peaks()
+    achieved = kbytes[0] / (k_ms / 1e3) / 1e9 if k_ms > 0 else 0.0
+    line = {"metric": "routed MoE Fisher probe tokens/s (one Qwen3-30B-A3B-shaped MoE block)",
+            "value": round(a.steps * T / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init N(0, 0.02^2) bf16 block, N(0, 1) hidden states",
+            "config": {"workload": "qwen3_30b_a3b_moe_block_routed_fisher", "tokens_per_step": T, "experts": 128,
+                       "top_k": 8, "hidden": 2048, "moe_intermediate": 768},
+            "hook_kernels": {"launches": len(kev), "ms_per_step": round(k_ms / a.steps, 4),
+                             "share_of_step": round(k_ms / ms, 4),
+                             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+                                          "bytes_per_step": kbytes[0] // a.steps}},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def run_costtable(a, local):
     """The reference's cost-table entry point end to end: measure_quant_cost.measure_batched_gpu
     (measure_quant_cost.py:551-685) on a random-init Llama-8B-shaped model (the 224 decoder
@@ -663,6 +748,13 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.workload == "fisher1b" and a.impl == "ours":
         return run_fisher(a, rank, world, local)
+    if a.workload == "fishermoe":
+        if a.impl == "ours" and rank == 0:
+            run_fisher_moe(a, local)
+        elif a.impl == "reference" and rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the routed MoE Fisher workload has no CPU "
+                              "reference arm (the reference's hooks run the same model on the GPU)"}))
+        return
     if a.workload == "costtable8b":
         if a.impl == "ours" and rank == 0:
             run_costtable(a, local)
