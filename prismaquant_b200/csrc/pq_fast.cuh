@@ -204,6 +204,41 @@ __device__ __forceinline__ void f8_codes4(const float (&l)[8], const float (&h)[
         "f"(h[0]), "f"(h[1]), "f"(h[2]), "f"(h[3]), "f"(h[4]), "f"(h[5]), "f"(h[6]), "f"(h[7]));
 }
 
+// E4M3 codes of two pairs (x0, x1) and (x2, x3): pair 0 in the low 16 bits, low byte = x0.
+__device__ __forceinline__ uint32_t f8_codes2(float x0, float x1, float x2, float x3) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 a, b;\n\tcvt.rn.satfinite.e4m3x2.f32 a, %2, %1;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 b, %4, %3;\n\tmov.b32 %0, {a, b};\n\t}"
+      : "=r"(r) : "f"(x0), "f"(x1), "f"(x2), "f"(x3));
+  return r;
+}
+// f16 pairs of the two code pairs packed as f8_codes2 packs them.
+__device__ __forceinline__ void f8_decode2(uint32_t c, uint32_t& q0, uint32_t& q1) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(q0), "=r"(q1) : "r"(c));
+}
+
+// The reference's E4M3 codes of four elements of a flagged FP8 row (bytes of a word), from the
+// codes of the lower bracket (cl), the upper bracket (ch) and the lower-bracket rule (cm).  An
+// element whose two bracket codes differ is an exact tie; it takes the code on the side the
+// reference's fl32 quotient falls (the upper code when `up_mask` is all ones, the lower one
+// otherwise) when `all_mask` is all ones (every tie of the row leaves its midpoint) or when its
+// lower code is subnormal (only the subnormal midpoint's ties do); every other element keeps cm.
+// Byte-wise tests without carries between bytes: a byte y <= 0x7F is nonzero iff bit 7 of
+// (y + 0x7F) | y is set.
+__device__ __forceinline__ uint32_t f8_flag_select(uint32_t cl, uint32_t ch, uint32_t cm, uint32_t all_mask,
+                                                   uint32_t up_mask) {
+  const uint32_t e = cl & 0x78787878u;                     // exponent fields
+  const uint32_t nze = (e + 0x7F7F7F7Fu) | e;              // bit 7: normal lower code
+  const uint32_t u = cl ^ ch;                              // same signs, so bytes <= 0x7F
+  const uint32_t nzu = (u + 0x7F7F7F7Fu) | u;              // bit 7: the bracket codes differ
+  const uint32_t sel = nzu & (all_mask | ~nze) & 0x80808080u;
+  const uint32_t m = (sel >> 7) * 0xFFu;
+  const uint32_t alt = (ch & up_mask) | (cl & ~up_mask);
+  return (cm & ~m) | (alt & m);
+}
+
 // One E4M3 code byte -> float32 (exact).
 __device__ __forceinline__ float e4m3x2_to_f2_lo(uint32_t c) {
   float lo, hi;

@@ -17,11 +17,19 @@
 //    pair of bf16 values (tests/test_fast_rules.py);
 //  * FP8 per channel: the code of min(RZ(w r_lo), RZ(w r_hi)), the bracket
 //    product below the quotient, the same tie rule.  It is exact except in
-//    rows where |a - 448 s| = 3 * 64 ulp(s) and s's significand is below 1.5
-//    (and rows whose max is below the 1e-8 floor): there the quotient of an
-//    exact tie can round off the midpoint.  Those rows also convert both
-//    brackets; a unit with a pair whose brackets differ is queued and
-//    resolved exactly at the end of the item (division-free, mid_side);
+//    rows where d = a - 448 s is 3 x 64 ulp(s) and s's significand is below
+//    1.5: there the exact ties (448 w / a exactly a midpoint; with 7 not
+//    dividing a's significand every such midpoint has significand 21/16, or
+//    is 7 x 2^-10) have fl32 quotients off the midpoint when the significand
+//    is below 1.125 (or, for 7 x 2^-10, below 1.5), and round up when d > 0,
+//    down when d < 0.  Those rows convert both brackets too and pick the
+//    reference's code per element in registers (f8_codes_flagged4); rows
+//    below the 1e-8 floor or near fp32 overflow take the exact path;
+//  * the item is read twice from shared memory: a pre-pass takes every
+//    unit's group maximum and minimum (kept in shared memory) and the row
+//    maxima, one table per item holds each row's FP8 scale, reciprocal
+//    brackets and flags, and then ONE pass per unit computes every format
+//    from one unpack of its values;
 //  * then exact f16 decode -> f32x2 product with the scale -> bf16x2
 //    reconstruction -> bf16x2 error -> mixed-precision square-accumulate;
 //  * MXFP8 (power-of-two scale): the E4M3 rounding is an integer rounding of
@@ -44,26 +52,41 @@ constexpr int FAST_THREADS = SWEEP_THREADS;
 // exact path (a provisional fp32 square could overflow).
 constexpr float F8_EXACT_ROW_AMAX = 1.152921504606846976e18f;  // 2^60
 
-struct RowParam {
-  float s, r_lo, r_hi, amax;
-  bool flag;   // the lower-bracket rule may differ from the reference here: resolve exactly
+// One row's FP8 per-channel parameters (shared-memory table, one entry per row of the item).
+struct RowTab {
+  float s, r_lo, r_hi;
+  uint32_t info;   // bit 0: exact-path row; 1: f7; 2: f21; 3: d > 0; bits 16-31: subnormal threshold
 };
+enum : uint32_t { RT_EXACT = 1u, RT_F7 = 2u, RT_F21 = 4u, RT_UP = 8u };
 
 // FP8 per-channel row scale from the row's max |w| (bf16 bits): s = max(amax, 1e-8) / 448
-// (div_const is exact for every normal bf16 value and for the 1e-8 floor).  flag: the row's max
-// is below the floor (s is not amax / 448), or d = amax - 448 s (exact as one FMA: a multiple of
-// 64 ulp(s) of at most 3 of them) is 3 x 64 ulp(s) and s's significand is below 1.5, the only
-// rows where an exact midpoint's fl32 quotient can round off the midpoint.
-__device__ __forceinline__ RowParam row_param(uint32_t ra_bits) {
-  RowParam p;
-  p.amax = __uint_as_float(ra_bits << 16);
-  p.s = div_const(fmaxf(p.amax, 1e-8f), 448.0f, RCP448);
-  recip_bounds(p.s, p.r_lo, p.r_hi);
-  const uint32_t sb = __float_as_uint(p.s);
+// (div_const is exact for every normal bf16 value and for the 1e-8 floor), its reciprocal
+// brackets, and where the lower-bracket rule needs help:
+//  * exact-path rows: the max is below the floor (s is not amax / 448) or near fp32 overflow;
+//  * d = amax - 448 s is exact as one FMA (a multiple of 64 ulp(s), at most 3 of them).  With
+//    |d| = 3 x 64 ulp(s), an exact tie's fl32 quotient leaves the midpoint (up when d > 0, down
+//    when d < 0) when s's significand is below 1.125 (f21: every tie of the row) or below 1.5
+//    for the subnormal midpoint 7 x 2^-10 (f7); elsewhere it is a tie;
+//  * the subnormal threshold: bf16 bits just above 2^-6 s; a unit whose smallest |w| is at or
+//    above it cannot hold a subnormal tie.
+__device__ __forceinline__ RowTab row_tab(uint32_t ra_bits) {
+  RowTab t;
+  const float amax = __uint_as_float(ra_bits << 16);
+  t.s = div_const(fmaxf(amax, 1e-8f), 448.0f, RCP448);
+  recip_bounds(t.s, t.r_lo, t.r_hi);
+  const uint32_t sb = __float_as_uint(t.s);
   const float ulp = __uint_as_float((sb & 0x7F800000u) - (23u << 23));
-  const float d = __fmaf_rn(-448.0f, p.s, p.amax);
-  p.flag = p.amax < 1e-8f || (fabsf(d) >= 160.0f * ulp && (sb & 0x7FFFFFu) < 0x400000u);
-  return p;
+  const float d = __fmaf_rn(-448.0f, t.s, amax);
+  const bool j3 = fabsf(d) >= 160.0f * ulp;
+  const uint32_t sig = sb & 0x7FFFFFu;
+  uint32_t info = 0u;
+  if (amax < 1e-8f || amax >= F8_EXACT_ROW_AMAX) info |= RT_EXACT;
+  if (j3 && sig < 0x400000u) info |= RT_F7;
+  if (j3 && sig < 0x100000u) info |= RT_F21;
+  if (d > 0.0f) info |= RT_UP;
+  const uint32_t thr = (__float_as_uint(__fmul_rn(t.s, 0.015625f)) >> 16) + 1u;   // 2^-6 s, rounded up
+  t.info = info | (min(thr, 0x7F80u) << 16);
+  return t;
 }
 
 // Loads unit u (16 bf16) from the stage into v[0..7]; lanes of a quarter-warp
@@ -108,7 +131,6 @@ __device__ __forceinline__ void unit_to_chunks(const uint32_t (&v)[8], Chunk8& c
   unpack8(make_uint4(v[4], v[5], v[6], v[7]), c1.w);
 }
 
-constexpr int FAST_QCAP = 64;            // queued FP8 units per warp
 // NVFP4 cost products are biased by this (absolute, in units of the scaled value |w / s| <= 6):
 // below 2^-13 x 0.25, the smallest distance of a non-midpoint quotient from a midpoint, and
 // above the products' own error at a midpoint (tests/test_fast_rules.py checks every bf16 pair)
@@ -125,11 +147,6 @@ __device__ __forceinline__ float sq_exact_err(float w, float r) {
 // exact path (main loop contributes nothing for it).
 __device__ __forceinline__ bool exact_unit(float a16) { return a16 < 1e-8f || a16 >= 1.152921504606846976e18f; }
 
-// NVFP4 bracket of one pair: low / high conversion codes (one byte each).
-__device__ __forceinline__ void nv_bracket(uint64_t w2, uint64_t rlo2, uint64_t rhi2, uint32_t& cl, uint32_t& ch) {
-  cl = cvt_e2m1x2(f2_mul_rz(w2, rlo2));
-  ch = cvt_e2m1x2(f2_mul_rz(w2, rhi2));
-}
 // bf16 pair with each -0.0 replaced by +0.0: the cost codebook holds only +0.0, so a value that
 // rounds to zero reconstructs as +0.0 whatever its sign.
 __device__ __forceinline__ uint32_t bf16x2_plus_zero(uint32_t r) {
@@ -189,27 +206,6 @@ __device__ __forceinline__ float f8_pair_wsq(uint32_t v, uint32_t cl, uint64_t s
   return wsq2_acc(bf16x2_sub(v, rec), h0, h1, 0.0f);
 }
 
-// FP8 pair (16-bit code pair, low byte = low element), cost rule.
-__device__ __forceinline__ uint32_t f8_resolve_pair(uint32_t vp, uint32_t cl, uint32_t ch, float s) {
-  float ql0, ql1, qh0, qh1;
-  f2_unpack(e4m3x2_to_f2(cl), ql0, ql1);
-  f2_unpack(e4m3x2_to_f2(ch), qh0, qh1);
-  const float w0 = bf16lo(vp), w1 = bf16hi(vp);
-  const uint32_t d = cl ^ ch;
-  uint32_t cx = cl;
-  if (d & 0x00FFu) {
-    bool up, dn;
-    mid_side(fabsf(w0), ql0, qh0, s, up, dn);
-    if (up || (!dn && w0 < 0.0f)) cx = (cx & 0xFF00u) | (ch & 0x00FFu);
-  }
-  if (d & 0xFF00u) {
-    bool up, dn;
-    mid_side(fabsf(w1), ql1, qh1, s, up, dn);
-    if (up || (!dn && w1 < 0.0f)) cx = (cx & 0x00FFu) | (ch & 0xFF00u);
-  }
-  return cx;
-}
-
 // Units outside the fast path's range (amax below the 1e-8 scale floor, or
 // large enough for an fp32 square to overflow): every element by IEEE
 // division and the exact tie rules.  The main loop contributed nothing.
@@ -256,94 +252,6 @@ __device__ __noinline__ double f8_exact_unit(const uint32_t* vw, float s, uint32
   return delta;
 }
 
-constexpr int FAST_TASK_CAP = 8 * 32;   // uncertain pairs of one 32-unit batch
-
-// Inclusive warp prefix sum.
-__device__ __forceinline__ int warp_incl_scan(int x, int lane) {
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(FULL, x, o);
-    if (lane >= o) x += y;
-  }
-  return x;
-}
-
-// Warp-cooperative resolution of queued FP8 units (entry = unit index), in batches of 32 units:
-// each lane finds its unit's pairs whose two bracket codes differ, a prefix sum packs them into
-// the warp's task list, and the whole warp resolves the list, so a batch costs one round per 32
-// pairs instead of one per pair of its busiest lane.  Each resolved pair adds its exact squared
-// errors minus those of the main loop's provisional code (the lower bracket's) and, in W_hat
-// launches, rewrites its reconstruction.
-// Task word: pair (bits 0-2) | unit (3-14).
-template <bool HW = false>
-__device__ __forceinline__ double f8_fixup_body(const uint32_t* q0, int c0, const uint32_t* q1, int c1, const uint4* st,
-                                               int lane, const uint32_t* ramax, int upr, uint32_t rdiv,
-                                               uint32_t* tasks, int64_t elem0, uint32_t* outw, HRef H = HRef{}) {
-  const int cnt = c0 + c1;
-  double delta = 0.0;
-  const uint32_t* words = reinterpret_cast<const uint32_t*>(st);
-  for (int base = 0; base < cnt; base += 32) {   // warp-uniform
-    const int i = base + lane;
-    uint32_t pm = 0;
-    int u = 0;
-    if (i < cnt) {
-      u = (int)(i < c0 ? q0[i] : q1[i - c0]);
-      const RowParam rp = row_param(ramax[upr == 1 ? u : (int)__umulhi((uint32_t)u, rdiv)]);
-      if (rp.amax >= F8_EXACT_ROW_AMAX) {
-        delta += f8_exact_unit(words + 8 * u, rp.s, outw ? outw + (elem0 + 16 * (int64_t)u) / 2 : nullptr,
-                               HW ? &H : nullptr, u);
-      } else {
-        const uint4 a = st[2 * u], b = st[2 * u + 1];
-        const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi);
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          const uint64_t w2 = f2_from_bf16x2(v[p]);
-          pm |= (cvt_e4m3x2(f2_mul_rz(w2, rlo2)) != cvt_e4m3x2(f2_mul_rz(w2, rhi2)) ? 1u : 0u) << p;
-        }
-      }
-    }
-    const int n = __popc(pm);
-    const int incl = warp_incl_scan(n, lane);
-    const int tot = __shfl_sync(FULL, incl, 31);
-    int off = incl - n;
-    for (uint32_t m = pm; m; m &= m - 1) tasks[off++] = (uint32_t)(__ffs(m) - 1) | ((uint32_t)u << 3);
-    __syncwarp();
-    float dl = 0.0f;
-    for (int t = lane; t < tot; t += 32) {
-      const uint32_t task = tasks[t];
-      const int p = (int)(task & 7u), uu = (int)(task >> 3);
-      const RowParam rp = row_param(ramax[upr == 1 ? uu : (int)__umulhi((uint32_t)uu, rdiv)]);
-      const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
-      const uint32_t vp = words[8 * uu + p];
-      const uint64_t w2 = f2_from_bf16x2(vp);
-      const uint64_t lo = f2_mul_rz(w2, rlo2), hi = f2_mul_rz(w2, rhi2);
-      const uint32_t cl = cvt_e4m3x2(lo), ch = cvt_e4m3x2(hi);
-      const uint32_t cp = cvt_e4m3x2(f2_min(lo, hi));   // the main loop's code
-      const uint32_t cx = f8_resolve_pair(vp, cl, ch, rp.s);
-      if (HW && cx != cp) {
-        const float h0 = H.at(uu, 2 * p), h1 = H.at(uu, 2 * p + 1);
-        dl += f8_pair_wsq(vp, cx, s2, h0, h1) - f8_pair_wsq(vp, cp, s2, h0, h1);
-      } else if (cx != cp) {
-        dl += f8_pair_sq(vp, cx, s2) - f8_pair_sq(vp, cp, s2);
-      }
-      if (outw && cx != cp) outw[(elem0 + 16 * (int64_t)uu) / 2 + p] = f8_pair_rec(cx, s2);
-    }
-    delta += (double)dl;
-    __syncwarp();
-  }
-  return delta;
-}
-
-// Out-of-line copy for the rare early flush inside the per-unit loop (the loop body stays small);
-// the end-of-item resolution inlines the body.
-template <bool HW>
-__device__ __noinline__ double f8_fixup(const uint32_t* q, int cnt, const uint4* st, int lane, const uint32_t* ramax,
-                                        int upr, uint32_t rdiv, uint32_t* tasks, int64_t elem0, uint32_t* outw,
-                                        HRef H) {
-  return f8_fixup_body<HW>(q, cnt, q, 0, st, lane, ramax, upr, rdiv, tasks, elem0, outw, H);
-}
-
 // Tensor index of item `item`, scanning forward from the previous one (items
 // of a CTA are visited in increasing order, so this is O(1) amortised).
 __device__ __forceinline__ ItemRef next_item(const SweepLaunch& L, int64_t item, int& ti) {
@@ -365,7 +273,8 @@ struct ItemCtx {
   uint8_t* codes_it;     // codes of the item's first element
   uint16_t* amax_it;     // group amax of the item's first group
   uint32_t* ramax;       // per-row max |w| (bf16 bits) of this item's rows
-  uint32_t* tasks;       // the warp's fix-up task list
+  uint32_t* ab;          // per unit: group max |w| bits | group min |w| bits << 16 (pre-pass)
+  const RowTab* rowtab;  // per row of the item: FP8 per-channel parameters
   int64_t elem0;
   // W_hat launches: each format's W_hat of the tensor as bf16 pairs, one slice per format present,
   // in format order (NVFP4, MXFP8, FP8 per channel); null otherwise
@@ -395,28 +304,54 @@ struct Accum {
   float nv, mx, f8;
   double dnv, dmx, df8;
   uint32_t tmax;
-  int cnt_f8;
 };
 
 __device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
   return c.upr == 1 ? u : (int)__umulhi((uint32_t)u, c.rdiv);   // exact for u < 4096 (host-checked)
 }
 
-// Pass A over one unit: NVFP4 cost and export codes, MXFP8 cost, and (when the
-// FP8 format is on) the unit's contribution to its row maximum.
-// HW: sums weighted by H (per element or per row).  OSSE (with OUT): the error sums as well.
+// Pre-pass over one unit: its group max and min |w| into the item's table, and (with FP8 per
+// channel) its share of the row maximum.
+template <bool F8>
+__device__ __forceinline__ void unit_prepass(const ItemCtx& c, int u, int lane, bool warp_rows) {
+  const bool valid = u < c.nunits;
+  const int uc = valid ? u : c.nunits - 1;
+  uint32_t v[8];
+  (void)load_unit(c.st, uc, true, lane, v);   // the order of the values does not matter here
+  uint32_t a16b, amin;
+  unit_absmax_min(v, a16b, amin);
+  if (valid) c.ab[uc] = a16b | (amin << 16);
+  if (F8) {
+    const int row = row_of(c, uc);
+    if (warp_rows) {   // the warp's 32 units lie in one row, all valid or all past the end
+      const uint32_t m = warp_max_u(a16b);
+      if (lane == 0 && u - lane < c.nunits) atomicMax(&c.ramax[row], m);
+    } else if (valid) {
+      atomicMax(&c.ramax[row], a16b);
+    }
+  }
+}
+
+// The one pass over a unit: NVFP4 cost and export codes, MXFP8 cost and FP8 per-channel cost from
+// one load and one unpack of its 16 values, with the group extrema of the pre-pass and the row
+// table.  HW: sums weighted by H (per element or per row).  OSSE (with OUT): the error sums too.
 template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW, bool OSSE>
-__device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, bool warp_rows, Accum& A) {
+__device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Accum& A) {
   const bool valid = u < c.nunits;
   const int uc = valid ? u : c.nunits - 1;
   uint32_t v[8];
   const bool sw = load_unit(c.st, uc, true, lane, v);
   if (OUT && c.outw_copy && valid) store_unit_words(c.outw_copy + c.elem0 / 2, uc, sw, v);
   float hv[16];
-  if (HW && (NV || MX)) load_unit_h(c.h, uc, sw, hv);
-  uint32_t a16b, amin = 0;
-  if (MX) unit_absmax_min(v, a16b, amin); else a16b = unit_absmax(v);
+  if (HW) load_unit_h(c.h, uc, sw, hv);
+  const uint32_t ab = c.ab[uc];
+  const uint32_t a16b = ab & 0xFFFFu, amin = ab >> 16;
   const float a16 = __uint_as_float(a16b << 16);
+  uint64_t w2[8];
+  if (NV || CODES || F8) {
+#pragma unroll
+    for (int p = 0; p < 8; ++p) w2[p] = f2_from_bf16x2(v[p]);
+  }
 
   if (NV || CODES) {
     const bool ex = exact_unit(a16);
@@ -431,9 +366,8 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, b
       float cc[8], l[8];
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
-        const uint64_t w2 = f2_from_bf16x2(v[4 * hf + p]);
-        if (NV) f2_unpack(f2_fma_rn(w2, r2, nb2), cc[2 * p], cc[2 * p + 1]);
-        if (CODES) f2_unpack(f2_mul_rz(w2, rlo2), l[2 * p], l[2 * p + 1]);
+        if (NV) f2_unpack(f2_fma_rn(w2[4 * hf + p], r2, nb2), cc[2 * p], cc[2 * p + 1]);
+        if (CODES) f2_unpack(f2_mul_rz(w2[4 * hf + p], rlo2), l[2 * p], l[2 * p + 1]);
       }
       if (NV) nv_cost4(cc, *reinterpret_cast<uint32_t(*)[4]>(q + 4 * hf));
       if (CODES) cw[hf] = nv_export4(l);
@@ -522,79 +456,59 @@ __device__ __forceinline__ void unit_pass_a(const ItemCtx& c, int u, int lane, b
     if (!OUT || OSSE) A.mx += valid ? part : 0.0f;
   }
 
-  if (F8) {   // row maxima for pass B
-    const int row = row_of(c, uc);
-    if (warp_rows) {   // the warp's 32 units lie in one row, all valid or all past the end
-      const uint32_t m = warp_max_u(a16b);
-      if (lane == 0 && u - lane < c.nunits) atomicMax(&c.ramax[row], m);
-    } else if (valid) {
-      atomicMax(&c.ramax[row], a16b);
-    }
-  }
-}
-
-// Pass B over one unit: FP8 per-channel cost with the completed row maximum.  The code is the
-// lower bracket's; in flagged rows (row_param) both brackets are converted too, and a unit with a
-// pair whose brackets differ is queued for the exact resolution.
-template <bool OUT, bool HW, bool OSSE>
-__device__ __forceinline__ void unit_pass_b(const ItemCtx& c, int u, int lane, uint32_t lanemask_lt, uint32_t* q_f8,
-                                            Accum& A) {
-  const bool valid = u < c.nunits;
-  const int uc = valid ? u : c.nunits - 1;
-  uint32_t v[8];
-  const bool sw = load_unit(c.st, uc, true, lane, v);
-  float hv[16];
-  if (HW) load_unit_h(c.h, uc, sw, hv);
-  const RowParam rp = row_param(c.ramax[row_of(c, uc)]);
-  const uint64_t rlo2 = f2_pack(rp.r_lo, rp.r_lo), rhi2 = f2_pack(rp.r_hi, rp.r_hi), s2 = f2_pack(rp.s, rp.s);
-  const bool exf = rp.amax >= F8_EXACT_ROW_AMAX;
-  uint32_t ux = 0;
-  float pe = 0.0f, po = 0.0f;
-  uint32_t recw[8];
+  if (F8) {
+    const RowTab rt = c.rowtab[row_of(c, uc)];
+    if (rt.info & RT_EXACT) {   // rare: the whole row by the exact path
+      if (valid)
+        A.df8 += f8_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, rt.s,
+                               OUT ? c.outw_f8 + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
+    } else {
+      const uint64_t rlo2 = f2_pack(rt.r_lo, rt.r_lo), rhi2 = f2_pack(rt.r_hi, rt.r_hi), s2 = f2_pack(rt.s, rt.s);
+      // ties may leave their midpoint: every tie in f21 rows, the subnormal midpoint's in f7 rows (only
+      // a unit holding a |w| below 2^-6 s can have one)
+      const bool flagged = (rt.info & RT_F21) || ((rt.info & RT_F7) && amin < (rt.info >> 16));
+      const uint32_t all_mask = (rt.info & RT_F21) ? 0xFFFFFFFFu : 0u;
+      const uint32_t up_mask = (rt.info & RT_UP) ? 0xFFFFFFFFu : 0u;
+      float pe = 0.0f, po = 0.0f;
+      uint32_t recw[8];
 #pragma unroll
-  for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
-    float l[8], h[8], x[8];
+      for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
+        float l[8], h[8], x[8];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const uint64_t w2 = f2_from_bf16x2(v[4 * hf + p]);
-      f2_unpack(f2_mul_rz(w2, rlo2), l[2 * p], l[2 * p + 1]);
-      f2_unpack(f2_mul_rz(w2, rhi2), h[2 * p], h[2 * p + 1]);
-      x[2 * p] = fminf(l[2 * p], h[2 * p]);
-      x[2 * p + 1] = fminf(l[2 * p + 1], h[2 * p + 1]);
-    }
-    uint32_t q[4];
-    f8_codes_q4(x, q);
-    if (rp.flag) {   // which pairs lie on a midpoint's bracket
-      uint32_t dx, qq[4];
-      f8_codes4(l, h, dx, qq);
-      ux |= dx;
-    }
+        for (int p = 0; p < 4; ++p) {
+          f2_unpack(f2_mul_rz(w2[4 * hf + p], rlo2), l[2 * p], l[2 * p + 1]);
+          f2_unpack(f2_mul_rz(w2[4 * hf + p], rhi2), h[2 * p], h[2 * p + 1]);
+          x[2 * p] = fminf(l[2 * p], h[2 * p]);
+          x[2 * p + 1] = fminf(l[2 * p + 1], h[2 * p + 1]);
+        }
+        uint32_t q[4];
+        if (!flagged) {
+          f8_codes_q4(x, q);
+        } else {
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
-      const int pp = 4 * hf + p;
-      if (OUT) recw[pp] = bf16x2_plus_zero(rec);
-      if (OUT && !OSSE) continue;
-      if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], po);
-      else if (HW) pe = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], pe);
-      else if (p & 1) po = sq2_acc(bf16x2_sub(v[pp], rec), po);
-      else pe = sq2_acc(bf16x2_sub(v[pp], rec), pe);
-    }
-  }
-  if (OUT) {   // the queued pairs and exact-path rows are rewritten by the fix-ups
-    if (valid) store_unit_words(c.outw_f8 + c.elem0 / 2, uc, sw, recw);
-  }
-  if (!OUT || OSSE) A.f8 += (valid && !exf) ? pe + po : 0.0f;
-  const bool need = valid && (ux != 0 || exf);
-  const uint32_t bal = __ballot_sync(FULL, need);
-  if (bal) {
-    if (need) q_f8[A.cnt_f8 + __popc(bal & lanemask_lt)] = (uint32_t)u;
-    A.cnt_f8 += __popc(bal);
-    if (A.cnt_f8 > FAST_QCAP - 32) {
-      __syncwarp();
-      A.df8 += f8_fixup<HW>(q_f8, A.cnt_f8, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0, c.outw_f8, c.h);
-      __syncwarp();
-      A.cnt_f8 = 0;
+          for (int k = 0; k < 2; ++k) {   // two pairs per 32-bit code word
+            const uint32_t cl = f8_codes2(l[4 * k], l[4 * k + 1], l[4 * k + 2], l[4 * k + 3]);
+            const uint32_t ch = f8_codes2(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+            const uint32_t cm = f8_codes2(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
+            f8_decode2(f8_flag_select(cl, ch, cm, all_mask, up_mask), q[2 * k], q[2 * k + 1]);
+          }
+        }
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
+          const int pp = 4 * hf + p;
+          if (OUT) recw[pp] = bf16x2_plus_zero(rec);
+          if (OUT && !OSSE) continue;
+          if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], po);
+          else if (HW) pe = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], pe);
+          else if (p & 1) po = sq2_acc(bf16x2_sub(v[pp], rec), po);
+          else pe = sq2_acc(bf16x2_sub(v[pp], rec), pe);
+        }
+      }
+      if (OUT) {
+        if (valid) store_unit_words(c.outw_f8 + c.elem0 / 2, uc, sw, recw);
+      }
+      if (!OUT || OSSE) A.f8 += valid ? pe + po : 0.0f;
     }
   }
 }
@@ -604,25 +518,25 @@ __device__ __forceinline__ void fold(float& f, double& d) {
   f = 0.0f;
 }
 
+constexpr int FAST_MAX_UNITS = FAST_STAGE_BYTES / 32;   // 16-element units per item
+
 template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW, bool OSSE>
 __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __grid_constant__ SweepLaunch L) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int NWARPS = FAST_THREADS / 32;
   uint8_t* stages = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FAST_NSTAGE * FAST_STAGE_BYTES);
+  RowTab* rowtab = reinterpret_cast<RowTab*>(smem + FAST_NSTAGE * FAST_STAGE_BYTES);   // [FAST_MAX_ROWS]
+  uint32_t* ab = reinterpret_cast<uint32_t*>(rowtab + FAST_MAX_ROWS);                   // [FAST_MAX_UNITS]
+  uint32_t* ramax = ab + FAST_MAX_UNITS;                                                // [FAST_MAX_ROWS]
+  double* red = reinterpret_cast<double*>(ramax + FAST_MAX_ROWS);                       // [NWARPS][3]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + NWARPS * 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + FAST_NSTAGE);
-  uint32_t* ramax_buf = reinterpret_cast<uint32_t*>(bars + FAST_NSTAGE + 1);   // [2][FAST_MAX_ROWS]
-  double* red = reinterpret_cast<double*>(ramax_buf + 2 * FAST_MAX_ROWS);
-  uint32_t* qbase = reinterpret_cast<uint32_t*>(red + NWARPS * 3);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t* q_f8 = qbase + warp * FAST_QCAP;
-  uint32_t* tasks = qbase + NWARPS * FAST_QCAP + warp * FAST_TASK_CAP;
-  const uint32_t lanemask_lt = (1u << lane) - 1u;
   const int64_t n_items = L.item_prefix[L.n];
   const int64_t my_n = n_items > (int64_t)blockIdx.x ? (n_items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 
-  for (int i = tid; i < 2 * FAST_MAX_ROWS; i += FAST_THREADS) ramax_buf[i] = 0u;
+  for (int i = tid; i < FAST_MAX_ROWS; i += FAST_THREADS) ramax[i] = 0u;
   if (tid == 0) {
     for (int s = 0; s < FAST_NSTAGE; ++s) mbar_init(&bars[s], 1);
     *abort_flag = 0;
@@ -646,7 +560,6 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
   A.nv = A.mx = A.f8 = 0.0f;
   A.dnv = A.dmx = A.df8 = 0.0;
   A.tmax = 0u;
-  A.cnt_f8 = 0;
   int cur_t = -1, ti_proc = 0;
   auto flush_tensor = [&](int t) {   // CTA-uniform call
     const SweepDesc& d = L.t[t];
@@ -700,8 +613,9 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     c.elem0 = it.r0 * d.cols;
     c.codes_it = CODES ? d.nvfp4_codes + c.elem0 / 2 : nullptr;
     c.amax_it = CODES ? d.nvfp4_amax + c.elem0 / 16 : nullptr;
-    c.ramax = ramax_buf + (j & 1) * FAST_MAX_ROWS;
-    c.tasks = tasks;
+    c.ramax = ramax;
+    c.ab = ab;
+    c.rowtab = rowtab;
     c.h.el = (HW && !d.h_per_row) ? d.h + c.elem0 : nullptr;
     c.h.row = (HW && d.h_per_row) ? d.h + it.r0 : nullptr;
     c.h.upr = c.upr;
@@ -717,39 +631,34 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
     const int iters = (c.nunits + FAST_THREADS - 1) / FAST_THREADS;
     const bool warp_rows = (c.upr & 31) == 0;
 
-    if (NV || MX || CODES || F8) {
+    // pre-pass: group extrema of every unit (a thread reads back only its own units) and row maxima
 #pragma unroll 1
-      for (int k = 0; k < iters; ++k) {   // not unrolled: the body stays small enough for the instruction cache
-        unit_pass_a<NV, MX, F8, CODES, OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, warp_rows, A);
-        if ((k & 3) == 3) {   // fp32 partials hold <= 64 squares
-          fold(A.nv, A.dnv);
-          fold(A.mx, A.dmx);
-        }
-      }
-      fold(A.nv, A.dnv);
-      fold(A.mx, A.dmx);
-    }
+    for (int k = 0; k < iters; ++k) unit_prepass<F8>(c, tid + k * FAST_THREADS, lane, warp_rows);
     if (F8) {
       __syncthreads();   // row maxima complete; a failed wait is visible to every thread
       if (*abort_flag) {
         if (j_abort < 0) j_abort = j;
         break;
       }
-      uint32_t* next = ramax_buf + ((j + 1) & 1) * FAST_MAX_ROWS;   // last read by item j-1
-      for (int i = tid; i < FAST_MAX_ROWS; i += FAST_THREADS) next[i] = 0u;
-#pragma unroll 1
-      for (int k = 0; k < iters; ++k) {
-        unit_pass_b<OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, lanemask_lt, q_f8, A);
-        if ((k & 3) == 3) fold(A.f8, A.df8);
+      for (int i = tid; i < (int)it.nr; i += FAST_THREADS) {
+        rowtab[i] = row_tab(ramax[i]);
+        ramax[i] = 0u;   // ready for the next item's pre-pass
       }
-      fold(A.f8, A.df8);
+      __syncthreads();   // row table complete
     }
-    __syncwarp();
-    if (F8 && A.cnt_f8)   // the warp's own queued FP8 units (flagged rows, exact-path rows)
-      A.df8 += f8_fixup_body<HW>(q_f8, A.cnt_f8, q_f8, 0, c.st, lane, c.ramax, c.upr, c.rdiv, c.tasks, c.elem0,
-                                 c.outw_f8, c.h);
-    A.cnt_f8 = 0;
-    __syncthreads();   // stage s and the queues are free again
+#pragma unroll 1
+    for (int k = 0; k < iters; ++k) {   // not unrolled: the body stays small enough for the instruction cache
+      unit_main<NV, MX, F8, CODES, OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, A);
+      if ((k & 3) == 3) {   // fp32 partials hold <= 64 squares
+        fold(A.nv, A.dnv);
+        fold(A.mx, A.dmx);
+        fold(A.f8, A.df8);
+      }
+    }
+    fold(A.nv, A.dnv);
+    fold(A.mx, A.dmx);
+    fold(A.f8, A.df8);
+    __syncthreads();   // stage s, the unit table and the row table are free again
     if (*abort_flag) {
       if (j_abort < 0) j_abort = j;
       break;
@@ -767,9 +676,9 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
 }
 
 size_t sweep_fast_smem_bytes() {
-  return (size_t)FAST_NSTAGE * FAST_STAGE_BYTES + (FAST_NSTAGE + 1) * sizeof(uint64_t) +
-         2 * FAST_MAX_ROWS * sizeof(uint32_t) + (FAST_THREADS / 32) * 3 * sizeof(double) +
-         (FAST_THREADS / 32) * (FAST_QCAP + FAST_TASK_CAP) * sizeof(uint32_t);
+  return (size_t)FAST_NSTAGE * FAST_STAGE_BYTES + FAST_MAX_ROWS * sizeof(RowTab) +
+         (FAST_MAX_UNITS + FAST_MAX_ROWS) * sizeof(uint32_t) + (FAST_THREADS / 32) * 3 * sizeof(double) +
+         (FAST_NSTAGE + 1) * sizeof(uint64_t);
 }
 
 template <bool NV, bool MX, bool F8, bool CODES, bool OUT = false, bool HW = false, bool OSSE = false>

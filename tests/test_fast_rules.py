@@ -18,7 +18,8 @@ midpoint m or at least ~2^-13 (relative) away from every midpoint, while the pro
 a / d is exact or m's significand is short enough; then "ties to lower" is "the bracket below".
 For NVFP4 that covers every case.  For FP8 per channel it leaves one family: rows where
 |a - 448 s| = 3 * 64 ulp(s) and s's significand is below 1.5, at midpoints with significand 21/16
-or 7/16 (the kernel flags such rows and resolves their near-midpoint pairs exactly)."""
+or 7/16; the kernel's row flags and per-element selection (f8_flag_select) for those rows are
+emulated here too, and the whole rule must then agree with the reference on every pair."""
 import numpy as np
 
 F32 = np.float32
@@ -132,3 +133,44 @@ def test_fp8_channel_lower_bracket_rule_exact_outside_flagged_rows():
             flagged_with_misses += 1
     assert n > 10_000_000
     assert flagged_with_misses > 0      # the flagged family exists: the exact resolution is needed
+
+
+def _e4m3_code(v, mags):
+    """E4M3 code byte of an exactly representable value (sign bit 7, magnitude index as
+    exponent/mantissa fields)."""
+    i = np.searchsorted(mags, np.abs(v))
+    e = np.where(i < 8, 0, (i - 8) // 8 + 1)
+    m = np.where(i < 8, i, (i - 8) % 8)
+    return (np.where(np.signbit(v), 0x80, 0) | (e << 3) | m).astype(np.int64)
+
+
+def test_fp8_channel_full_kernel_rule_exact_for_every_bf16_pair():
+    """The lower-bracket code, replaced in flagged rows by the flag selection, equals the
+    reference's code for every bf16 pair (row flags as row_tab computes them)."""
+    mags, even = _e4m3()
+    ws = _bf16_in(0, 2.01)
+    ws = np.concatenate([ws, -ws])
+    bad = n = 0
+    for a in _bf16_in(1, 2):
+        w = ws[np.abs(ws) <= a]
+        s = F32(a) / F32(448)
+        x = (w.astype(F32) / s).astype(np.float64)
+        want = _ties_lower(x, mags)
+        d = np.float64(a) - 448.0 * np.float64(s)
+        ulp = np.float64(np.spacing(s))
+        sig = int(np.array([s], dtype=F32).view(np.uint32)[0]) & 0x7FFFFF
+        j3 = abs(d) >= 160 * ulp
+        f7, f21, up = j3 and sig < 0x400000, j3 and sig < 0x100000, d > 0
+        for _, r_lo, r_hi in _reciprocals(s):
+            lo, hi = _rz32(w * r_lo), _rz32(w * r_hi)
+            cm = _rne(np.minimum(lo, hi), mags, even, 448.0)
+            got = cm
+            if f7:   # flagged row: the kernel's per-element selection (f8_flag_select)
+                cl, ch = _rne(lo, mags, even, 448.0), _rne(hi, mags, even, 448.0)
+                bl = _e4m3_code(cl, mags)
+                subnormal = (bl & 0x78) == 0
+                sel = (cl != ch) & (f21 | subnormal)
+                got = np.where(sel, ch if up else cl, cm)
+            bad += np.count_nonzero(got != want)
+            n += w.size
+    assert n > 10_000_000 and bad == 0
