@@ -897,6 +897,8 @@ def main():
     try:
         tr = json.loads(PROFILE_TRAFFIC.read_text())
         traffic = tr.get(wl_name)
+        if traffic is not None:   # the capture is of the whole model: this rank's share of it
+            traffic = int(traffic * my_params / params)
     except Exception:
         pass
 

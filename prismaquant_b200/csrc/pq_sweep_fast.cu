@@ -312,14 +312,14 @@ __device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
 
 // Pre-pass over one unit: its group max and min |w| into the item's table, and (with FP8 per
 // channel) its share of the row maximum.
-template <bool F8>
+template <bool MINS, bool F8>
 __device__ __forceinline__ void unit_prepass(const ItemCtx& c, int u, int lane, bool warp_rows) {
   const bool valid = u < c.nunits;
   const int uc = valid ? u : c.nunits - 1;
   uint32_t v[8];
   (void)load_unit(c.st, uc, true, lane, v);   // the order of the values does not matter here
-  uint32_t a16b, amin;
-  unit_absmax_min(v, a16b, amin);
+  uint32_t a16b, amin = 0;
+  if (MINS) unit_absmax_min(v, a16b, amin); else a16b = unit_absmax(v);
   if (valid) c.ab[uc] = a16b | (amin << 16);
   if (F8) {
     const int row = row_of(c, uc);
@@ -395,10 +395,13 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
       c.amax_it[uc] = (uint16_t)a16b;
       A.tmax = max(A.tmax, a16b);
     }
-    if (ex && valid) {   // rare: amax below the 1e-8 floor or near fp32 overflow; overwrites the unit
-      A.dnv += nv_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, a16,
-                             CODES ? c.codes_it + 8 * (int64_t)uc : nullptr, NV && (!OUT || OSSE),
-                             (OUT && NV) ? c.outw + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
+    const bool exv = ex && valid;
+    if (__any_sync(FULL, exv)) {   // rare: amax below the 1e-8 floor or near fp32 overflow; overwrites the unit
+      if (exv)
+        A.dnv += nv_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, a16,
+                               CODES ? c.codes_it + 8 * (int64_t)uc : nullptr, NV && (!OUT || OSSE),
+                               (OUT && NV) ? c.outw + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr,
+                               uc);
     }
   }
 
@@ -429,7 +432,8 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
       else pe = sq2_acc(bf16x2_sub(v[p], q), pe);
     }
     float part = pe + po;
-    if (!ok && valid) {
+    const bool slow = !ok && valid;
+    if (__any_sync(FULL, slow) && slow) {
       Chunk8 c0, c1;
       unit_to_chunks(v, c0, c1);
       uint32_t rec[8];
@@ -458,15 +462,19 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
 
   if (F8) {
     const RowTab rt = c.rowtab[row_of(c, uc)];
-    if (rt.info & RT_EXACT) {   // rare: the whole row by the exact path
-      if (valid)
+    const bool exr = (rt.info & RT_EXACT) != 0;
+    if (__any_sync(FULL, exr)) {   // rare: a row below the 1e-8 floor or near fp32 overflow, by the exact path
+      if (exr && valid)
         A.df8 += f8_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, rt.s,
                                OUT ? c.outw_f8 + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
-    } else {
+    }
+    if (!exr) {
       const uint64_t rlo2 = f2_pack(rt.r_lo, rt.r_lo), rhi2 = f2_pack(rt.r_hi, rt.r_hi), s2 = f2_pack(rt.s, rt.s);
       // ties may leave their midpoint: every tie in f21 rows, the subnormal midpoint's in f7 rows (only
       // a unit holding a |w| below 2^-6 s can have one)
       const bool flagged = (rt.info & RT_F21) || ((rt.info & RT_F7) && amin < (rt.info >> 16));
+      const bool any_flagged = __any_sync(FULL, flagged);   // warp-uniform choice of the code path
+      const uint32_t en = flagged ? 0xFFFFFFFFu : 0u;       // lanes of an unflagged row keep cm
       const uint32_t all_mask = (rt.info & RT_F21) ? 0xFFFFFFFFu : 0u;
       const uint32_t up_mask = (rt.info & RT_UP) ? 0xFFFFFFFFu : 0u;
       float pe = 0.0f, po = 0.0f;
@@ -482,7 +490,7 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
           x[2 * p + 1] = fminf(l[2 * p + 1], h[2 * p + 1]);
         }
         uint32_t q[4];
-        if (!flagged) {
+        if (!any_flagged) {
           f8_codes_q4(x, q);
         } else {
 #pragma unroll
@@ -490,7 +498,7 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
             const uint32_t cl = f8_codes2(l[4 * k], l[4 * k + 1], l[4 * k + 2], l[4 * k + 3]);
             const uint32_t ch = f8_codes2(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
             const uint32_t cm = f8_codes2(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
-            f8_decode2(f8_flag_select(cl, ch, cm, all_mask, up_mask), q[2 * k], q[2 * k + 1]);
+            f8_decode2(f8_flag_select(cl, ch, cm, all_mask, up_mask, en), q[2 * k], q[2 * k + 1]);
           }
         }
 #pragma unroll
@@ -633,7 +641,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
 
     // pre-pass: group extrema of every unit (a thread reads back only its own units) and row maxima
 #pragma unroll 1
-    for (int k = 0; k < iters; ++k) unit_prepass<F8>(c, tid + k * FAST_THREADS, lane, warp_rows);
+    for (int k = 0; k < iters; ++k) unit_prepass<MX || F8, F8>(c, tid + k * FAST_THREADS, lane, warp_rows);
     if (F8) {
       __syncthreads();   // row maxima complete; a failed wait is visible to every thread
       if (*abort_flag) {
