@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama8b",
-                    choices=["llama8b", "siblings", "linear4096", "moe30b", "fisher1b", "outerr8b", "kernels",
+                    choices=["llama8b", "siblings", "lmhead", "linear4096", "moe30b", "fisher1b", "outerr8b", "kernels",
                              "costtable8b", "fishermoe"])
     ap.add_argument("--moe-tokens", type=int, default=8192, help="tokens per step of the fishermoe workload")
     ap.add_argument("--fisher-seqs", type=int, default=64, help="calibration sequences (split across ranks)")
@@ -590,6 +590,8 @@ def workload_shapes(name):
         return S.llama_dense_linears(), "llama8b_dense_sweep_nvfp4_export"
     if name == "siblings":
         return S.fused_sibling_group(), "fused_sibling_qkv_gateup_sweep_nvfp4_export"
+    if name == "lmhead":
+        return [("lm_head", (128256, 4096))], "llama8b_lm_head_sweep_nvfp4_export"
     if name == "linear4096":
         return [("model.layers.0.self_attn.o_proj", (4096, 4096))], "single_linear_4096_sweep_nvfp4_export"
     if name == "moe30b":

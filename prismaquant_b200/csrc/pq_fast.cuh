@@ -224,17 +224,16 @@ __device__ __forceinline__ void f8_decode2(uint32_t c, uint32_t& q0, uint32_t& q
 // element whose two bracket codes differ is an exact tie; it takes the code on the side the
 // reference's fl32 quotient falls (the upper code when `up_mask` is all ones, the lower one
 // otherwise) when `all_mask` is all ones (every tie of the row leaves its midpoint) or when its
-// lower code is subnormal (only the subnormal midpoint's ties do); every other element keeps cm,
-// and so does every element when `enable` is 0 (a lane of an unflagged row).
+// lower code is subnormal (only the subnormal midpoint's ties do); every other element keeps cm.
 // Byte-wise tests without carries between bytes: a byte y <= 0x7F is nonzero iff bit 7 of
 // (y + 0x7F) | y is set.
 __device__ __forceinline__ uint32_t f8_flag_select(uint32_t cl, uint32_t ch, uint32_t cm, uint32_t all_mask,
-                                                   uint32_t up_mask, uint32_t enable) {
+                                                   uint32_t up_mask) {
   const uint32_t e = cl & 0x78787878u;                     // exponent fields
   const uint32_t nze = (e + 0x7F7F7F7Fu) | e;              // bit 7: normal lower code
   const uint32_t u = cl ^ ch;                              // same signs, so bytes <= 0x7F
   const uint32_t nzu = (u + 0x7F7F7F7Fu) | u;              // bit 7: the bracket codes differ
-  const uint32_t sel = nzu & (all_mask | ~nze) & (enable & 0x80808080u);
+  const uint32_t sel = nzu & (all_mask | ~nze) & 0x80808080u;
   const uint32_t m = (sel >> 7) * 0xFFu;
   const uint32_t alt = (ch & up_mask) | (cl & ~up_mask);
   return (cm & ~m) | (alt & m);

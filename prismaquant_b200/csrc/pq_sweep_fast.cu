@@ -395,13 +395,10 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
       c.amax_it[uc] = (uint16_t)a16b;
       A.tmax = max(A.tmax, a16b);
     }
-    const bool exv = ex && valid;
-    if (__any_sync(FULL, exv)) {   // rare: amax below the 1e-8 floor or near fp32 overflow; overwrites the unit
-      if (exv)
-        A.dnv += nv_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, a16,
-                               CODES ? c.codes_it + 8 * (int64_t)uc : nullptr, NV && (!OUT || OSSE),
-                               (OUT && NV) ? c.outw + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr,
-                               uc);
+    if (ex && valid) {   // rare: amax below the 1e-8 floor or near fp32 overflow; overwrites the unit
+      A.dnv += nv_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, a16,
+                             CODES ? c.codes_it + 8 * (int64_t)uc : nullptr, NV && (!OUT || OSSE),
+                             (OUT && NV) ? c.outw + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
     }
   }
 
@@ -432,8 +429,7 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
       else pe = sq2_acc(bf16x2_sub(v[p], q), pe);
     }
     float part = pe + po;
-    const bool slow = !ok && valid;
-    if (__any_sync(FULL, slow) && slow) {
+    if (!ok && valid) {
       Chunk8 c0, c1;
       unit_to_chunks(v, c0, c1);
       uint32_t rec[8];
@@ -462,19 +458,15 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
 
   if (F8) {
     const RowTab rt = c.rowtab[row_of(c, uc)];
-    const bool exr = (rt.info & RT_EXACT) != 0;
-    if (__any_sync(FULL, exr)) {   // rare: a row below the 1e-8 floor or near fp32 overflow, by the exact path
-      if (exr && valid)
+    if (rt.info & RT_EXACT) {   // rare: the whole row by the exact path
+      if (valid)
         A.df8 += f8_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, rt.s,
                                OUT ? c.outw_f8 + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
-    }
-    if (!exr) {
+    } else {
       const uint64_t rlo2 = f2_pack(rt.r_lo, rt.r_lo), rhi2 = f2_pack(rt.r_hi, rt.r_hi), s2 = f2_pack(rt.s, rt.s);
       // ties may leave their midpoint: every tie in f21 rows, the subnormal midpoint's in f7 rows (only
       // a unit holding a |w| below 2^-6 s can have one)
       const bool flagged = (rt.info & RT_F21) || ((rt.info & RT_F7) && amin < (rt.info >> 16));
-      const bool any_flagged = __any_sync(FULL, flagged);   // warp-uniform choice of the code path
-      const uint32_t en = flagged ? 0xFFFFFFFFu : 0u;       // lanes of an unflagged row keep cm
       const uint32_t all_mask = (rt.info & RT_F21) ? 0xFFFFFFFFu : 0u;
       const uint32_t up_mask = (rt.info & RT_UP) ? 0xFFFFFFFFu : 0u;
       float pe = 0.0f, po = 0.0f;
@@ -490,7 +482,7 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
           x[2 * p + 1] = fminf(l[2 * p + 1], h[2 * p + 1]);
         }
         uint32_t q[4];
-        if (!any_flagged) {
+        if (!flagged) {
           f8_codes_q4(x, q);
         } else {
 #pragma unroll
@@ -498,7 +490,7 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
             const uint32_t cl = f8_codes2(l[4 * k], l[4 * k + 1], l[4 * k + 2], l[4 * k + 3]);
             const uint32_t ch = f8_codes2(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
             const uint32_t cm = f8_codes2(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
-            f8_decode2(f8_flag_select(cl, ch, cm, all_mask, up_mask, en), q[2 * k], q[2 * k + 1]);
+            f8_decode2(f8_flag_select(cl, ch, cm, all_mask, up_mask), q[2 * k], q[2 * k + 1]);
           }
         }
 #pragma unroll
