@@ -237,7 +237,7 @@ def _batched_quantize(spec: fr.FormatSpec, stacked_w: torch.Tensor) -> torch.Ten
 # reference entry points
 # ---------------------------------------------------------------------------
 
-def _fused_w_hats(W: torch.Tensor, specs):
+def _fused_w_hats(W: torch.Tensor, specs, budget: int | None = None):
     """W_hat of every spec whose batched RTN is NVFP4, MXFP8 or FP8 per channel, and each W[n]'s
     squared-error sum for those specs, from one read of the stacked weight (pq_cost_qdq_fused_sse)
     when two or more of them are asked for and the extra slices fit in a quarter of the free
@@ -254,8 +254,9 @@ def _fused_w_hats(W: torch.Tensor, specs):
             by_kernel.setdefault(k, []).append(spec.name)
     if len(by_kernel) < 2:
         return {}, {}
-    free, _ = torch.cuda.mem_get_info(W.device)
-    if W.numel() * 2 * len(by_kernel) > free // 4:
+    if budget is None:
+        budget = torch.cuda.mem_get_info(W.device)[0] // 4
+    if W.numel() * 2 * len(by_kernel) > budget:
         return {}, {}
     try:
         hats, sse = _lib.cost_qdq_fused_sse(W, list(by_kernel))
@@ -267,7 +268,7 @@ def _fused_w_hats(W: torch.Tensor, specs):
     return out, mse
 
 
-def _fused_w_hats_list(ws, specs, dev: torch.device):
+def _fused_w_hats_list(ws, specs, dev: torch.device, budget: int | None = None):
     """_fused_w_hats for a chunk's weights as they are (bf16, contiguous, on `dev`, one shape),
     without stacking them first: the same read also writes the stacked weight
     (pq_cost_qdq_fused_sse_list).  Returns (W_hat dict, sums dict, stacked weight), or
@@ -288,8 +289,9 @@ def _fused_w_hats_list(ws, specs, dev: torch.device):
     if any(w.device != dev or w.dtype != torch.bfloat16 or w.dim() != 2 or w.shape != shape or
            not w.is_contiguous() for w in ws):
         return {}, {}, None
-    free, _ = torch.cuda.mem_get_info(dev)
-    if len(ws) * ws[0].numel() * 2 * (len(by_kernel) + 1) > free // 4:
+    if budget is None:
+        budget = torch.cuda.mem_get_info(dev)[0] // 4
+    if len(ws) * ws[0].numel() * 2 * (len(by_kernel) + 1) > budget:
         return {}, {}, None
     try:
         hats, W, sse = _lib.cost_qdq_fused_sse_list(ws, list(by_kernel))
@@ -367,6 +369,9 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
     # the host in between); entries are replayed in processing order, errors included.
     pending: list = []
     dev_parts: list = []
+    # memory budget for the fused W_hat slices, read once: cudaMemGetInfo waits for the device, so
+    # a query per chunk would stop the host from queueing work ahead
+    budget = torch.cuda.mem_get_info(dev)[0] // 4 if dev.type == "cuda" else 0
 
     def stash(t: torch.Tensor) -> int:
         dev_parts.append(t.detach().reshape(-1).to(torch.float64))
@@ -383,11 +388,11 @@ def measure_batched_gpu(model: nn.Module, act_cache, target_names: set[str], spe
             # stacks the weights; the reference's stack (measure_quant_cost.py:595-597) otherwise
             w_hat_pre, mse_pre, W = ({}, {}, None)
             if dtype == torch.bfloat16 and not _per_linear:
-                w_hat_pre, mse_pre, W = _fused_w_hats_list([m.weight.detach() for _, m in chunk], specs, dev)
+                w_hat_pre, mse_pre, W = _fused_w_hats_list([m.weight.detach() for _, m in chunk], specs, dev, budget)
             if W is None:
                 W = torch.stack([m.weight.detach().to(device=dev, dtype=dtype) for _, m in chunk])
                 if dtype == torch.bfloat16 and not _per_linear:
-                    w_hat_pre, mse_pre = _fused_w_hats(W, specs)
+                    w_hat_pre, mse_pre = _fused_w_hats(W, specs, budget)
             X = torch.stack([a[:rows].to(device=dev, dtype=dtype) for a in acts])
             # tensor cores with fused epilogues for bf16 operands with k % 8 == 0: y_ref (bf16) and
             # its energy once per chunk (pq_output_ref), then one GEMM per format whose epilogue
