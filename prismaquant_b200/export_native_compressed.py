@@ -24,6 +24,9 @@ import torch.nn as nn
 
 from . import _lib
 from . import measure_quant_cost as mqc
+# the checkpoint's serving configuration, at the reference's module path
+from .quantization_config import (SCHEMES as FORMAT_SCHEME, build_quantization_config,  # noqa: F401
+                                  write_config_with_quantization)
 
 FLOAT_TO_E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
 NVFP4_MAX = 6.0

@@ -21,6 +21,9 @@ Outputs:
   fisher_bridge_bf16.npz (`fisher_bridge`) FisherAccumulator at one token per
                       backward on bf16-valued inputs and gradients
   fisher_detail.npz   (`fisher_detail`) FisherAccumulator with h_detail_dir
+  qconfig_cases.json  (`qconfig`) build_quantization_config / write_config_with_quantization
+                      on recipe assignments (dense, packed and per-expert MoE, MTP, fused
+                      siblings), with the profile's answers recorded as tables
 
 Only this script touches the reference; the committed fixtures travel, the
 reference does not.
@@ -374,7 +377,115 @@ def config_fixtures():
     return out
 
 
+class _RecordingProfile:
+    """Wraps one of the reference's model profiles and records every answer the config
+    builder asks of it, so the test can replay the profile as plain tables."""
+
+    def __init__(self, inner):
+        self.inner, self.names = inner, {}
+
+    def to_vllm_internal_name(self, name):
+        self.names[name] = self.inner.to_vllm_internal_name(name)
+        return self.names[name]
+
+    def __getattr__(self, attr):
+        return getattr(self.inner, attr)
+
+
+def _qconfig_cases():
+    L = "model.layers"
+    dense = {}
+    for i in range(2):
+        dense.update({f"{L}.{i}.self_attn.q_proj": "NVFP4", f"{L}.{i}.self_attn.k_proj": "NVFP4",
+                      f"{L}.{i}.self_attn.v_proj": "NVFP4", f"{L}.{i}.self_attn.o_proj": "MXFP8",
+                      f"{L}.{i}.mlp.gate_proj": "NVFP4", f"{L}.{i}.mlp.up_proj": "NVFP4",
+                      f"{L}.{i}.mlp.down_proj": "BF16"})
+    dense[f"{L}.1.self_attn.v_proj"] = "MXFP8"          # a mixed fused group: no fused target
+    per_expert = {f"{L}.{l}.mlp.experts.{e}.{p}_proj": ("NVFP4" if l != 10 else "MXFP8")
+                  for l in (2, 10) for e in range(8) for p in ("gate", "up", "down")}
+    per_expert.update({f"{L}.3.mlp.experts.{e}.gate_proj": "MXFP8" for e in (0, 2, 5)})
+    per_expert.update({f"{L}.3.mlp.experts.{e}.up_proj": "BF16" for e in (1, 4)})
+    packed = {f"{L}.{l}.mlp.experts.{p}": f for l, f in ((0, "NVFP4"), (1, "MXFP8"), (2, "BF16"))
+              for p in ("gate_up_proj", "down_proj")}
+    packed.update({f"{L}.{l}.self_attn.q_proj": "NVFP4" for l in range(3)})
+    packed.update({"mtp.layers.0.mlp.experts.gate_up_proj": "BF16", "mtp.layers.0.mlp.experts.down_proj": "BF16"})
+    mixtral = {f"{L}.0.block_sparse_moe.experts.w{k}": "BF16" for k in (1, 2, 3)}
+    mixtral.update({f"{L}.0.self_attn.{p}_proj": "INT3" for p in "qkvo"})
+    mixtral.update({f"{L}.0.mlp.gate": "NVINT2", "lm_head": "FP8_SOURCE", "mtp.experts.down_proj": "BF16"})
+    llama_map = {"qkv_proj": ["q_proj", "k_proj", "v_proj"], "gate_up_proj": ["gate_proj", "up_proj"]}
+    qwen_map = {**llama_map, "qkv": ["qkv"], "in_proj_qkvz": ["in_proj_qkv", "in_proj_z"]}
+    return [
+        # the reference's own test scenarios (tests/test_prismaquant_export_native_compressed.py:353-520)
+        ("qwen3_5", {**{f"{L}.{i}.self_attn.k_proj": "MXFP8" for i in range(2)},
+                     **{f"{L}.{i}.mlp.experts.down_proj": "NVFP4" for i in range(5)}}, ["lm_head"], [], None),
+        ("qwen3_5", {f"{L}.0.mlp.gate_proj": "NVFP4", f"{L}.0.mlp.shared_expert_gate": "BF16"}, ["lm_head"],
+         [f"{L}.0.mlp.gate"], None),
+        ("qwen3_5", {f"{L}.0.mlp.experts.gate_up_proj": "NVFP4", f"{L}.0.mlp.experts.down_proj": "NVFP4",
+                     f"{L}.0.self_attn.q_proj": "NVFP4"}, [], [], None),
+        ("qwen3_5", {f"{L}.0.mlp.experts.gate_up_proj": "NVFP4", f"{L}.0.mlp.experts.down_proj": "NVFP4",
+                     "mtp.layers.0.mlp.experts.gate_up_proj": "BF16", "mtp.layers.0.mlp.experts.down_proj": "BF16"},
+         [], [], None),
+        ("qwen3_5", {f"{L}.0.mlp.experts.gate_up_proj": "NVFP4", f"{L}.0.mlp.experts.down_proj": "MXFP8"}, [], [], None),
+        # wider cases
+        ("qwen3_5", packed, ["lm_head", "model.embed_tokens"], [f"{L}.0.mlp.gate"], qwen_map),
+        ("qwen3_5", {**packed, f"{L}.0.linear_attn.in_proj_qkv": "MXFP8", f"{L}.0.linear_attn.in_proj_z": "MXFP8",
+                     f"{L}.1.linear_attn.in_proj_qkv": "BF16"}, [], [], qwen_map),
+        ("default", dense, ["lm_head"], [], llama_map),
+        ("default", dense, ["lm_head"], [], None),
+        ("default", {f"{L}.0.self_attn.k_proj": "BF16", f"{L}.0.mlp.up_proj": "BF16",
+                     f"{L}.0.mlp.down_proj": "NVFP4"}, [], [], llama_map),
+        ("default", per_expert, [], ["router"], None),
+        ("qwen3_5", per_expert, [], [], None),
+        ("default", packed, ["lm_head"], [], None),
+        ("default", mixtral, [], [], None),
+        ("default", {f"{L}.0.mlp.gate_proj": "MXFP8", f"{L}.0.mlp.up_proj": "NVFP4"}, [], [], None),   # size tie
+        ("default", {f"{L}.0.mlp.down_proj": "BF16"}, ["lm_head"], [], None),                        # nothing quantized
+        ("default", {f"{L}.0.mlp.down_proj": "FP8_E4M3", f"{L}.1.mlp.down_proj": "NVFP4"}, [], [], None),  # no scheme
+    ]
+
+
+def qconfig_fixtures():
+    """The reference's config builder on recipe assignments (mode `qconfig`)."""
+    import tempfile
+    from prismaquant.model_profiles import vllm_registry as vr
+    from prismaquant.model_profiles.default import DefaultProfile
+    from prismaquant.model_profiles.qwen3_5 import Qwen3_5Profile
+    out = {"build": [], "write": []}
+    real_pm = vr.packed_modules_mapping_from_class
+    for kind, assignment, passthrough, extra, mapping in _qconfig_cases():
+        prof = _RecordingProfile(Qwen3_5Profile() if kind == "qwen3_5" else DefaultProfile())
+        vr.packed_modules_mapping_from_class = (lambda _cls, m=mapping: dict(m or {}))
+        try:
+            want = enc.build_quantization_config(assignment, set(passthrough), extra, profile=prof)
+        except (RuntimeError, KeyError) as e:
+            want = {"error": type(e).__name__}
+        finally:
+            vr.packed_modules_mapping_from_class = real_pm
+        out["build"].append({"assignment": assignment, "bf16_passthrough": passthrough, "extra_ignore": extra,
+                             "packed_mapping": mapping or {}, "names": prof.names,
+                             "moe_regex": prof.per_expert_moe_regex(), "mtp_regex": prof.per_expert_mtp_regex(),
+                             "want": want})
+    # config.json: quantization_config and the pruned expert counts (the profile is detected from it)
+    src_cfg = {"architectures": ["ToyMoeForCausalLM"], "model_type": "toy_moe", "num_experts": 8,
+               "num_local_experts": 8, "hidden_size": 64, "text_config": {"n_routed_experts": 8, "vocab_size": 32}}
+    for assignment, prune in ((_qconfig_cases()[7][1], None),
+                              ({"model.layers.0.mlp.experts.gate_up_proj": "NVFP4",
+                                "model.layers.0.mlp.experts.down_proj": "NVFP4"},
+                               {"model.layers.0.mlp": {"num_experts_kept": 6}}),
+                              ({"model.layers.0.mlp.down_proj": "BF16"}, None)):
+        with tempfile.TemporaryDirectory() as src, tempfile.TemporaryDirectory() as dst:
+            Path(src, "config.json").write_text(json.dumps(src_cfg))
+            enc.write_config_with_quantization(src, Path(dst), assignment, {"lm_head"}, (), prune)
+            out["write"].append({"src_config": src_cfg, "assignment": assignment, "bf16_passthrough": ["lm_head"],
+                                 "prune_manifest": prune, "want_text": Path(dst, "config.json").read_text()})
+    return out
+
+
 def main():
+    if "qconfig" in sys.argv[1:]:         # only the quantization_config fixtures
+        with open(HERE / "qconfig_cases.json", "w") as f:
+            json.dump(qconfig_fixtures(), f, indent=1)
+        return
     if "fisher_detail" in sys.argv[1:]:   # only the per-weight Fisher fixture
         np.savez_compressed(HERE / "fisher_detail.npz", **fisher_detail())
         return
