@@ -7,7 +7,7 @@
 //  * NVFP4 cost: the code of fma(w, r, -2^-18) with r = rcp.approx(s), one
 //    hardware conversion per pair.  w and the group max a have 8-bit
 //    significands, so w / (a / 6) is either exactly an E2M1 midpoint or at
-//    least ~2^-11 (relative) away from every midpoint; at an exact midpoint
+//    least ~2^-13 (relative) away from every midpoint; at an exact midpoint
 //    the reference's fl32(w / s) IS the midpoint (a / 6 is exact unless the
 //    midpoint is 0.75, and there the scale's rounding moves the quotient by
 //    at most half an ulp of 0.75), so its nearest-with-ties-to-lower code is
@@ -22,9 +22,9 @@
 //    dividing a's significand every such midpoint has significand 21/16, or
 //    is 7 x 2^-10) have fl32 quotients off the midpoint when the significand
 //    is below 1.125 (or, for 7 x 2^-10, below 1.5), and round up when d > 0,
-//    down when d < 0.  Those rows convert both brackets too and pick the
-//    reference's code per element in registers (f8_codes_flagged4); rows
-//    below the 1e-8 floor or near fp32 overflow take the exact path;
+//    down when d < 0.  Units of those rows convert both brackets too and
+//    pick the reference's code per element in registers (f8_flag_select);
+//    rows below the 1e-8 floor or near fp32 overflow take the exact path;
 //  * the item is read twice from shared memory: a pre-pass takes every
 //    unit's group maximum and minimum (kept in shared memory) and the row
 //    maxima, one table per item holds each row's FP8 scale, reciprocal
@@ -40,7 +40,11 @@
 //    tie both neighbours are 8 ulp away (also when the upper one saturates), so
 //    the magnitude is rounded half-up whatever the reference's tie rule;
 //  * a unit or row outside the fast path's range is done by the exact path
-//    (IEEE division, the reference's tie rules).
+//    (IEEE division, the reference's tie rules).  Every format's fast
+//    arithmetic runs for every unit, and the rare units (exact path, MXFP8
+//    values in the E4M3 subnormal range, flagged FP8 rows) are redone behind
+//    one branch per unit (slow_unit), so the common path carries no other
+//    divergent branch.
 #include "pq_fast.cuh"
 #include "pq_internal.h"
 
@@ -332,9 +336,99 @@ __device__ __forceinline__ void unit_prepass(const ItemCtx& c, int u, int lane, 
   }
 }
 
+// The rare per-unit work, all behind one branch of the main pass: NVFP4 units outside the fast
+// range (nv_exact_unit), MXFP8 units with a value in the E4M3 subnormal range of their scale,
+// FP8 per-channel rows outside the fast range (f8_exact_unit) and units of flagged FP8 rows
+// (the reference's code per element from both brackets).  The main pass left nothing of these
+// in the accumulators.  W_hat words (OUT) of each format handled here are stored here.
+struct SlowSums {
+  double nv, mx, f8;
+};
+// Everything is passed by value: the caller's state stays in registers on the common path.
+template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW, bool OSSE>
+__device__ __noinline__ SlowSums slow_unit(const ItemCtx c, int uc, int lane, uint32_t which, float a16, float a32,
+                                           const RowTab rt) {
+  SlowSums A{0.0, 0.0, 0.0};
+  const uint32_t* vw = reinterpret_cast<const uint32_t*>(c.st) + 8 * uc;
+  uint32_t v[8];
+  const bool sw = load_unit(c.st, uc, true, lane, v);
+  float hv[16];
+  if (HW && (which & 6u)) load_unit_h(c.h, uc, sw, hv);
+  if ((NV || CODES) && (which & 1u))
+    A.nv += nv_exact_unit(vw, a16, CODES ? c.codes_it + 8 * (int64_t)uc : nullptr, NV && (!OUT || OSSE),
+                           (OUT && NV) ? c.outw + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
+  if (MX && (which & 2u)) {
+    Chunk8 c0, c1;
+    unit_to_chunks(v, c0, c1);
+    uint32_t rec[8], recw[8];
+    const float p0 = mxfp8_cost8(c0, a32, rec);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) recw[i] = rec[2 * i] | (rec[2 * i + 1] << 16);
+    const float p1 = mxfp8_cost8(c1, a32, rec);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) recw[4 + i] = rec[2 * i] | (rec[2 * i + 1] << 16);
+    float part = p0 + p1;
+    if (HW) {
+      part = 0.0f;
+#pragma unroll
+      for (int p = 0; p < 8; ++p) part = wsq2_acc(bf16x2_sub(v[p], recw[p]), hv[2 * p], hv[2 * p + 1], part);
+    }
+    if (OUT) {
+#pragma unroll
+      for (int p = 0; p < 8; ++p) recw[p] = bf16x2_plus_zero(recw[p]);
+      store_unit_words(c.outw_mx + c.elem0 / 2, uc, sw, recw);
+    }
+    if (!OUT || OSSE) A.mx += (double)part;
+  }
+  if (F8 && (which & 4u)) {
+    if (rt.info & RT_EXACT) {
+      A.f8 += f8_exact_unit(vw, rt.s, OUT ? c.outw_f8 + c.elem0 / 2 + 8 * (int64_t)uc : nullptr,
+                            HW ? &c.h : nullptr, uc);
+      return A;
+    }
+    const uint64_t rlo2 = f2_pack(rt.r_lo, rt.r_lo), rhi2 = f2_pack(rt.r_hi, rt.r_hi), s2 = f2_pack(rt.s, rt.s);
+    const uint32_t all_mask = (rt.info & RT_F21) ? 0xFFFFFFFFu : 0u;
+    const uint32_t up_mask = (rt.info & RT_UP) ? 0xFFFFFFFFu : 0u;
+    float part = 0.0f;
+    uint32_t recw[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {   // two pairs per 32-bit code word
+      float l[4], h[4], x[4];
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const uint64_t w2 = f2_from_bf16x2(v[2 * k + p]);
+        f2_unpack(f2_mul_rz(w2, rlo2), l[2 * p], l[2 * p + 1]);
+        f2_unpack(f2_mul_rz(w2, rhi2), h[2 * p], h[2 * p + 1]);
+        x[2 * p] = fminf(l[2 * p], h[2 * p]);
+        x[2 * p + 1] = fminf(l[2 * p + 1], h[2 * p + 1]);
+      }
+      const uint32_t cl = f8_codes2(l[0], l[1], l[2], l[3]);
+      const uint32_t ch = f8_codes2(h[0], h[1], h[2], h[3]);
+      const uint32_t cm = f8_codes2(x[0], x[1], x[2], x[3]);
+      uint32_t q[2];
+      f8_decode2(f8_flag_select(cl, ch, cm, all_mask, up_mask), q[0], q[1]);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int pp = 2 * k + p;
+        const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
+        if (OUT) recw[pp] = bf16x2_plus_zero(rec);
+        if (OUT && !OSSE) continue;
+        if (HW) part = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], part);
+        else part = sq2_acc(bf16x2_sub(v[pp], rec), part);
+      }
+    }
+    if (OUT) store_unit_words(c.outw_f8 + c.elem0 / 2, uc, sw, recw);
+    if (!OUT || OSSE) A.f8 += (double)part;
+  }
+  return A;
+}
+
 // The one pass over a unit: NVFP4 cost and export codes, MXFP8 cost and FP8 per-channel cost from
 // one load and one unpack of its 16 values, with the group extrema of the pre-pass and the row
 // table.  HW: sums weighted by H (per element or per row).  OSSE (with OUT): the error sums too.
+// Every format's fast arithmetic runs for every unit; units the fast rules do not cover are left
+// out of the sums here (their W_hat words are stored by slow_unit after these) and redone by
+// slow_unit behind a single branch.
 template <bool NV, bool MX, bool F8, bool CODES, bool OUT, bool HW, bool OSSE>
 __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Accum& A) {
   const bool valid = u < c.nunits;
@@ -352,9 +446,11 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
 #pragma unroll
     for (int p = 0; p < 8; ++p) w2[p] = f2_from_bf16x2(v[p]);
   }
+  uint32_t which = 0u;   // bit 0: NVFP4 exact unit, 1: MXFP8 exact unit, 2: FP8 exact row or flagged unit
 
   if (NV || CODES) {
     const bool ex = exact_unit(a16);
+    which |= ex ? 1u : 0u;
     const float snv = div_const(fmaxf(a16, 1e-8f), 6.0f, RCP6);
     const float r = rcp_approx(snv);
     const float rlo = __fmul_rz(r, 1.0f - 9.5367431640625e-07f);   // 1 - 2^-20
@@ -385,7 +481,7 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
         else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], rec), po);
         else pe = sq2_acc(bf16x2_sub(v[p], rec), pe);
       }
-      if (OUT) {   // exact-path units are rewritten below
+      if (OUT) {   // exact-path units are rewritten by slow_unit
         if (valid) store_unit_words(c.outw + c.elem0 / 2, uc, sw, recw);
       }
       if (!OUT || OSSE) A.nv += (valid && !ex) ? pe + po : 0.0f;
@@ -395,21 +491,18 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
       c.amax_it[uc] = (uint16_t)a16b;
       A.tmax = max(A.tmax, a16b);
     }
-    if (ex && valid) {   // rare: amax below the 1e-8 floor or near fp32 overflow; overwrites the unit
-      A.dnv += nv_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, a16,
-                             CODES ? c.codes_it + 8 * (int64_t)uc : nullptr, NV && (!OUT || OSSE),
-                             (OUT && NV) ? c.outw + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
-    }
   }
 
+  float a32 = 0.0f;
   if (MX) {
     const uint32_t a32b = max(a16b, (uint32_t)__shfl_xor_sync(FULL, a16b, 1));
-    const float a32 = __uint_as_float(a32b << 16);
+    a32 = __uint_as_float(a32b << 16);
     const int ea = (int)(a32b >> 7), ma = (int)(a32b & 0x7F);
     const int e = a32 < 1e-8f ? -35 : ea - 136 + (ma >= 31 ? 1 : 0);
     const uint32_t m448 = ((uint32_t)(e + 135) << 7) | 0x60u;   // bf16 bits of 448 * 2^e
     const uint32_t m448x2 = m448 | (m448 << 16);
     const bool ok = amin >= ((uint32_t)(e + 121) << 7);          // every |w| >= 2^(e-6): E4M3 normal range
+    which |= ok ? 0u : 2u;
     float pe = 0.0f, po = 0.0f;
     uint32_t recw[8];
 #pragma unroll
@@ -428,88 +521,58 @@ __device__ __forceinline__ void unit_main(const ItemCtx& c, int u, int lane, Acc
       else if (p & 1) po = sq2_acc(bf16x2_sub(v[p], q), po);
       else pe = sq2_acc(bf16x2_sub(v[p], q), pe);
     }
-    float part = pe + po;
-    if (!ok && valid) {
-      Chunk8 c0, c1;
-      unit_to_chunks(v, c0, c1);
-      uint32_t rec[8];
-      if (OUT || HW) {
-        const float p0 = mxfp8_cost8(c0, a32, rec);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) recw[i] = rec[2 * i] | (rec[2 * i + 1] << 16);
-        const float p1 = mxfp8_cost8(c1, a32, rec);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) recw[4 + i] = rec[2 * i] | (rec[2 * i + 1] << 16);
-        if (OSSE) part = p0 + p1;
-        if (HW) {
-          part = 0.0f;
-#pragma unroll
-          for (int p = 0; p < 8; ++p) part = wsq2_acc(bf16x2_sub(v[p], recw[p]), hv[2 * p], hv[2 * p + 1], part);
-        }
-      } else {
-        part = mxfp8_cost8(c0, a32, rec) + mxfp8_cost8(c1, a32, rec);
-      }
-    }
-    if (OUT) {
+    if (OUT) {   // units with subnormal-range values are rewritten by slow_unit
       if (valid) store_unit_words(c.outw_mx + c.elem0 / 2, uc, sw, recw);
     }
-    if (!OUT || OSSE) A.mx += valid ? part : 0.0f;
+    if (!OUT || OSSE) A.mx += (valid && ok) ? pe + po : 0.0f;
   }
 
+  RowTab rt{0.0f, 0.0f, 0.0f, 0u};
   if (F8) {
-    const RowTab rt = c.rowtab[row_of(c, uc)];
-    if (rt.info & RT_EXACT) {   // rare: the whole row by the exact path
-      if (valid)
-        A.df8 += f8_exact_unit(reinterpret_cast<const uint32_t*>(c.st) + 8 * uc, rt.s,
-                               OUT ? c.outw_f8 + c.elem0 / 2 + 8 * (int64_t)uc : nullptr, HW ? &c.h : nullptr, uc);
-    } else {
-      const uint64_t rlo2 = f2_pack(rt.r_lo, rt.r_lo), rhi2 = f2_pack(rt.r_hi, rt.r_hi), s2 = f2_pack(rt.s, rt.s);
-      // ties may leave their midpoint: every tie in f21 rows, the subnormal midpoint's in f7 rows (only
-      // a unit holding a |w| below 2^-6 s can have one)
-      const bool flagged = (rt.info & RT_F21) || ((rt.info & RT_F7) && amin < (rt.info >> 16));
-      const uint32_t all_mask = (rt.info & RT_F21) ? 0xFFFFFFFFu : 0u;
-      const uint32_t up_mask = (rt.info & RT_UP) ? 0xFFFFFFFFu : 0u;
-      float pe = 0.0f, po = 0.0f;
-      uint32_t recw[8];
+    rt = c.rowtab[row_of(c, uc)];
+    // ties may leave their midpoint: every tie in f21 rows, the subnormal midpoint's in f7 rows (only
+    // a unit holding a |w| below 2^-6 s can have one); exact-path rows are redone entirely
+    const bool other = (rt.info & (RT_EXACT | RT_F21)) || ((rt.info & RT_F7) && amin < (rt.info >> 16));
+    which |= other ? 4u : 0u;
+    const uint64_t rlo2 = f2_pack(rt.r_lo, rt.r_lo), rhi2 = f2_pack(rt.r_hi, rt.r_hi), s2 = f2_pack(rt.s, rt.s);
+    float pe = 0.0f, po = 0.0f;
+    uint32_t recw[8];
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
-        float l[8], h[8], x[8];
+    for (int hf = 0; hf < 2; ++hf) {   // four pairs per conversion block
+      float x[8];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          f2_unpack(f2_mul_rz(w2[4 * hf + p], rlo2), l[2 * p], l[2 * p + 1]);
-          f2_unpack(f2_mul_rz(w2[4 * hf + p], rhi2), h[2 * p], h[2 * p + 1]);
-          x[2 * p] = fminf(l[2 * p], h[2 * p]);
-          x[2 * p + 1] = fminf(l[2 * p + 1], h[2 * p + 1]);
-        }
-        uint32_t q[4];
-        if (!flagged) {
-          f8_codes_q4(x, q);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {   // two pairs per 32-bit code word
-            const uint32_t cl = f8_codes2(l[4 * k], l[4 * k + 1], l[4 * k + 2], l[4 * k + 3]);
-            const uint32_t ch = f8_codes2(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
-            const uint32_t cm = f8_codes2(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
-            f8_decode2(f8_flag_select(cl, ch, cm, all_mask, up_mask), q[2 * k], q[2 * k + 1]);
-          }
-        }
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
-          const int pp = 4 * hf + p;
-          if (OUT) recw[pp] = bf16x2_plus_zero(rec);
-          if (OUT && !OSSE) continue;
-          if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], po);
-          else if (HW) pe = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], pe);
-          else if (p & 1) po = sq2_acc(bf16x2_sub(v[pp], rec), po);
-          else pe = sq2_acc(bf16x2_sub(v[pp], rec), pe);
-        }
+      for (int p = 0; p < 4; ++p) {
+        float l0, l1, h0, h1;
+        f2_unpack(f2_mul_rz(w2[4 * hf + p], rlo2), l0, l1);
+        f2_unpack(f2_mul_rz(w2[4 * hf + p], rhi2), h0, h1);
+        x[2 * p] = fminf(l0, h0);
+        x[2 * p + 1] = fminf(l1, h1);
       }
-      if (OUT) {
-        if (valid) store_unit_words(c.outw_f8 + c.elem0 / 2, uc, sw, recw);
+      uint32_t q[4];
+      f8_codes_q4(x, q);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(q[p]), s2));
+        const int pp = 4 * hf + p;
+        if (OUT) recw[pp] = bf16x2_plus_zero(rec);
+        if (OUT && !OSSE) continue;
+        if (HW && (p & 1)) po = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], po);
+        else if (HW) pe = wsq2_acc(bf16x2_sub(v[pp], rec), hv[2 * pp], hv[2 * pp + 1], pe);
+        else if (p & 1) po = sq2_acc(bf16x2_sub(v[pp], rec), po);
+        else pe = sq2_acc(bf16x2_sub(v[pp], rec), pe);
       }
-      if (!OUT || OSSE) A.f8 += valid ? pe + po : 0.0f;
     }
+    if (OUT) {   // exact rows and flagged units are rewritten by slow_unit
+      if (valid) store_unit_words(c.outw_f8 + c.elem0 / 2, uc, sw, recw);
+    }
+    if (!OUT || OSSE) A.f8 += (valid && !other) ? pe + po : 0.0f;
+  }
+
+  if (valid && which) {
+    const SlowSums d = slow_unit<NV, MX, F8, CODES, OUT, HW, OSSE>(c, uc, lane, which, a16, a32, rt);
+    A.dnv += d.nv;
+    A.dmx += d.mx;
+    A.df8 += d.f8;
   }
 }
 
