@@ -709,18 +709,18 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
       }
       __syncthreads();   // row table complete
     }
+    // not unrolled: the body stays small enough for the instruction cache.  The fp32 partials
+    // hold <= 64 squares (four units); the fold sits in the outer loop, so it runs once per four
+    // units instead of as predicated instructions in every iteration
 #pragma unroll 1
-    for (int k = 0; k < iters; ++k) {   // not unrolled: the body stays small enough for the instruction cache
-      unit_main<NV, MX, F8, CODES, OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, A);
-      if ((k & 3) == 3) {   // fp32 partials hold <= 64 squares
-        fold(A.nv, A.dnv);
-        fold(A.mx, A.dmx);
-        fold(A.f8, A.df8);
-      }
+    for (int k0 = 0; k0 < iters; k0 += 4) {
+      const int k1 = min(k0 + 4, iters);
+#pragma unroll 1
+      for (int k = k0; k < k1; ++k) unit_main<NV, MX, F8, CODES, OUT, HW, OSSE>(c, tid + k * FAST_THREADS, lane, A);
+      fold(A.nv, A.dnv);
+      fold(A.mx, A.dmx);
+      fold(A.f8, A.df8);
     }
-    fold(A.nv, A.dnv);
-    fold(A.mx, A.dmx);
-    fold(A.f8, A.df8);
     __syncthreads();   // stage s, the unit table and the row table are free again
     if (*abort_flag) {
       if (j_abort < 0) j_abort = j;
