@@ -315,7 +315,9 @@ __device__ __forceinline__ int row_of(const ItemCtx& c, int u) {
 }
 
 // Pre-pass over one unit: its group max and min |w| into the item's table, and (with FP8 per
-// channel) its share of the row maximum.
+// channel, when a warp's 32 units lie in one row) the warp's share of the row maximum.  Items
+// whose rows are not a multiple of 32 units take their row maxima from the table afterwards
+// (build_row_table) instead of one shared-memory atomic per lane.
 template <bool MINS, bool F8>
 __device__ __forceinline__ void unit_prepass(const ItemCtx& c, int u, int lane, bool warp_rows) {
   const bool valid = u < c.nunits;
@@ -325,15 +327,33 @@ __device__ __forceinline__ void unit_prepass(const ItemCtx& c, int u, int lane, 
   uint32_t a16b, amin = 0;
   if (MINS) unit_absmax_min(v, a16b, amin); else a16b = unit_absmax(v);
   if (valid) c.ab[uc] = a16b | (amin << 16);
-  if (F8) {
-    const int row = row_of(c, uc);
-    if (warp_rows) {   // the warp's 32 units lie in one row, all valid or all past the end
-      const uint32_t m = warp_max_u(a16b);
-      if (lane == 0 && u - lane < c.nunits) atomicMax(&c.ramax[row], m);
-    } else if (valid) {
-      atomicMax(&c.ramax[row], a16b);
+  if (F8 && warp_rows) {   // the warp's 32 units lie in one row, all valid or all past the end
+    const uint32_t m = warp_max_u(a16b);
+    if (lane == 0 && u - lane < c.nunits) atomicMax(&c.ramax[row_of(c, uc)], m);
+  }
+}
+
+// The FP8 per-channel row table of the item: warp w takes rows w, w + NWARPS, ...; each row's
+// maximum is a warp max over its units' group maxima in the unit table, and lane k computes the
+// table entry of the warp's k-th row, so the entries of one warp are computed side by side.  Not
+// inlined: the main pass keeps its register allocation.
+template <int NWARPS>
+__device__ __noinline__ void build_row_table(const uint32_t* ab, int nr, int upr, int warp, int lane,
+                                                RowTab* rowtab) {
+  uint32_t mine = 0u;
+  int myrow = -1, k = 0;
+#pragma unroll 1
+  for (int row = warp; row < nr; row += NWARPS, ++k) {   // at most FAST_MAX_ROWS / NWARPS < 32 rows
+    const uint32_t* r = ab + (int64_t)row * upr;
+    uint32_t m = 0u;
+    for (int i = lane; i < upr; i += 32) m = max(m, r[i] & 0x7FFFu);
+    m = warp_max_u(m);   // every lane arrives here
+    if (lane == k) {
+      mine = m;
+      myrow = row;
     }
   }
+  if (myrow >= 0) rowtab[myrow] = row_tab(mine);
 }
 
 // The rare per-unit work, all behind one branch of the main pass: NVFP4 units outside the fast
@@ -703,9 +723,13 @@ __global__ void __launch_bounds__(FAST_THREADS, 1) sweep_fast_kernel(const __gri
         if (j_abort < 0) j_abort = j;
         break;
       }
-      for (int i = tid; i < (int)it.nr; i += FAST_THREADS) {
-        rowtab[i] = row_tab(ramax[i]);
-        ramax[i] = 0u;   // ready for the next item's pre-pass
+      if (warp_rows) {
+        for (int i = tid; i < (int)it.nr; i += FAST_THREADS) {
+          rowtab[i] = row_tab(ramax[i]);
+          ramax[i] = 0u;   // ready for the next item's pre-pass
+        }
+      } else {
+        build_row_table<NWARPS>(c.ab, (int)it.nr, c.upr, warp, lane, rowtab);
       }
       __syncthreads();   // row table complete
     }
