@@ -378,7 +378,12 @@ def run_kernels(a, local):
         ("cost_qdq FP8_E4M3 (W_hat)", lambda: _lib.cost_qdq(W, "FP8_E4M3"), 4 * n, "GB/s"),
     ]
     for f in ("MXFP4", "MXFP6_E3M2", "FP8_E5M2", "NVFP3", "INT4_W4A16_g128"):
-        table.append((f"xfmt2_kernel format_sse {f}", (lambda f=f: _lib.format_sse(W, f, s0)), 2 * n, "GB/s"))
+        kname = "mxsse_kernel" if f.startswith("MX") else "xfmt2_kernel"
+        table.append((f"{kname} format_sse {f}", (lambda f=f: _lib.format_sse(W, f, s0)), 2 * n, "GB/s"))
+    mx4 = ["MXFP4", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E5M2"]
+    s4 = torch.zeros(len(mx4), dtype=torch.float64, device=dev)
+    table.append(("mxsse_kernel format_sse_multi " + "+".join(mx4), lambda: _lib.format_sse_multi(W, mx4, s4),
+                  2 * n, "GB/s"))
     table += [
         ("xfmt2_kernel weighted_sse NVFP4 (predicted_dloss)", lambda: _lib.weighted_sse(W, "NVFP4", H, s0), 6 * n, "GB/s"),
         ("sweep_fast_kernel weighted NVFP4+MXFP8+FP8-channel (predicted_dloss)",

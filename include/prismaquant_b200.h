@@ -149,6 +149,18 @@ int pq_cost_qdq_fused_sse_list(const uint16_t* const* ws, int64_t batch, int64_t
 int pq_format_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, void* stream);
 
 /*
+ * pq_format_sse of nf formats over one tensor: ADDS each format's sum to
+ * sse[f] (fp64 device array of nf).  fmts is a HOST array of format ids, each
+ * one pq_format_sse accepts; every format is checked before anything runs.
+ * The MX formats among them (MXFP4, MXFP6_E3M2, MXFP6_E2M3, MXFP8_E5M2) come
+ * from one read of the weights when the rows are whole 32-element groups and w
+ * is 16-byte aligned.  Replaces the per-format loop of
+ * measure_quant_cost.py:627-632 over those formats.
+ */
+int pq_format_sse_multi(const uint16_t* w, int64_t rows, int64_t cols, const int32_t* fmts, int nf, double* sse,
+                        void* stream);
+
+/*
  * H-weighted squared error of one format over one bf16 tensor [rows, cols]:
  * ADDS sum(h * (W - qdq_fmt(W))^2) to *sse (fp64, device), the square taken
  * in fp32 and then weighted.  h is fp32, one weight per element [rows, cols]

@@ -192,12 +192,16 @@ class E8M0Thresholds:
         return np.clip(out, -127, 127)
 
     def round_log2(self, s: np.ndarray) -> np.ndarray:
-        """torch.round(torch.log2(max(s, 2^-127))).clamp(-127, 127), s normal."""
+        """torch.round(torch.log2(max(s, 2^-127))).clamp(-127, 127), s normal or +inf (a group
+        holding an infinity: log2 is inf, clamped to 127)."""
         k, m, e = self._split(s)
         if np.any(e == 0):
             raise ValueError("cost-path MX scale is never subnormal (amax >= 1e-8)")
+        if np.any(np.isnan(s)):
+            raise ValueError("NaN scale: the reference's group is NaN throughout")
         tab = np.array([self.round_first[int(i)] for i in range(-126, 128)], dtype=np.int64)
-        out = np.where(m >= tab[k + 126], k + 1, k)
+        kc = np.minimum(k, 127)
+        out = np.where(np.isinf(s), 127, np.where(m >= tab[kc + 126], kc + 1, kc))
         return np.clip(out, -127, 127)
 
 

@@ -33,7 +33,7 @@ EXPORTED = [
     "pq_format_sse", "pq_weighted_sse", "pq_output_sse", "pq_output_ref", "pq_output_err", "pq_cost_qdq_fused",
     "pq_weighted_sse_fused", "pq_cost_qdq_fused_sse", "pq_weighted_sse_fused_batch",
     "pq_cost_qdq_fused_sse_list", "pq_grad_sq_acc", "pq_set_wait_limit", "pq_default_wait_limit",
-    "pq_sumsq_rows_full", "pq_nvfp4_global_real", "pq_tokennorm_dot_seg",
+    "pq_sumsq_rows_full", "pq_nvfp4_global_real", "pq_tokennorm_dot_seg", "pq_format_sse_multi",
 ]
 
 
@@ -74,6 +74,7 @@ def load() -> ctypes.CDLL:
         "pq_weighted_sse_fused_batch": [P, I64, I64, I64, ctypes.c_uint32, P, I, P, V],
         "pq_cost_qdq_fused_sse_list": [P, I64, I64, I64, ctypes.c_uint32, P, P, V],
         "pq_format_sse": [P, I64, I64, I, P, V],
+        "pq_format_sse_multi": [P, I64, I64, P, I, P, V],
         "pq_weighted_sse": [P, I64, I64, I, P, I, P, V],
         "pq_output_sse": [P, P, P, P, I64, I64, I64, I64, P, P, P, P, V],
         "pq_output_ref": [P, P, I64, I64, I64, I64, P, P, V],
@@ -299,6 +300,21 @@ def format_sse(w: torch.Tensor, fmt: str, sse: torch.Tensor) -> None:
     cols = wb.shape[-1]
     _check(load().pq_format_sse(_ptr(wb), wb.numel() // cols, cols, FMT_IDS[fmt], _ptr(sse), _stream(wb)),
            "pq_format_sse", f"cannot reshape rows of {cols} into groups for {fmt}")
+
+
+def format_sse_multi(w: torch.Tensor, fmts: list[str], sse: torch.Tensor) -> None:
+    """format_sse of several formats: adds each format's sum into sse[f] (a contiguous fp64 device
+    vector of len(fmts)); the MX formats among them come from one read of the weights."""
+    wb = as_bf16_cuda(w, "format_sse_multi")
+    if wb.numel() == 0 or not fmts:
+        return
+    if sse.dtype != torch.float64 or not sse.is_contiguous() or sse.numel() < len(fmts):
+        raise ValueError("format_sse_multi: sse must be a contiguous fp64 vector with one entry per format")
+    cols = wb.shape[-1]
+    ids = (ctypes.c_int32 * len(fmts))(*[FMT_IDS[f] for f in fmts])
+    _check(load().pq_format_sse_multi(_ptr(wb), wb.numel() // cols, cols, ctypes.cast(ids, ctypes.c_void_p),
+                                      len(fmts), _ptr(sse), _stream(wb)),
+           "pq_format_sse_multi", f"cannot reshape rows of {cols} into groups for one of {fmts}")
 
 
 def weighted_sse(w: torch.Tensor, fmt: str, h: torch.Tensor, sse: torch.Tensor, per_row: bool = False) -> None:

@@ -216,8 +216,48 @@ int pq_format_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double
   if (fmt != PQ_FMT_BF16 && pq::xfmt_group(fmt, cols) == 0) return PQ_ERR_SHAPE;
   if (rows == 0 || fmt == PQ_FMT_BF16) return PQ_OK;
   if (!w || !sse) return PQ_ERR_NULL;
+  if (pq::mxsse_ok(w, cols, fmt))
+    return cuda_status(pq::launch_mxsse(w, rows, cols, &fmt, 1, &sse, num_sms_current(), (cudaStream_t)stream_));
   return cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse, nullptr, pq::MODE_SSE, num_sms_current(),
                                      (cudaStream_t)stream_));
+}
+
+int pq_format_sse_multi(const uint16_t* w, int64_t rows, int64_t cols, const int32_t* fmts, int nf, double* sse,
+                        void* stream_) {
+  if (nf < 0 || (nf > 0 && !fmts)) return PQ_ERR_NULL;
+  if (rows < 0 || cols < 1) return PQ_ERR_SHAPE;
+  for (int f = 0; f < nf; ++f) {   // every format checked before anything runs
+    if (fmts[f] != PQ_FMT_BF16 && !pq::xfmt_known(fmts[f])) return PQ_ERR_FORMAT;
+    if (fmts[f] != PQ_FMT_BF16 && pq::xfmt_group(fmts[f], cols) == 0) return PQ_ERR_SHAPE;
+  }
+  if (rows == 0 || nf == 0) return PQ_OK;
+  if (!w || !sse) return PQ_ERR_NULL;
+  const cudaStream_t stream = (cudaStream_t)stream_;
+  const int sms = num_sms_current();
+  int mx[8];
+  double* mx_sse[8];
+  int n_mx = 0;
+  for (int f = 0; f < nf; ++f) {
+    if (fmts[f] == PQ_FMT_BF16) continue;
+    const int fmt = fmts[f];
+    bool seen = false;   // a repeated MX format goes on its own
+    for (int i = 0; i < n_mx; ++i) seen = seen || mx[i] == fmt;
+    if (!seen && n_mx < 8 && pq::mxsse_ok(w, cols, fmt)) {   // the MX formats from one read
+      mx[n_mx] = fmt;
+      mx_sse[n_mx++] = sse + f;
+      continue;
+    }
+    if (pq::mxsse_ok(w, cols, fmt)) {
+      double* one = sse + f;
+      const int st = cuda_status(pq::launch_mxsse(w, rows, cols, &fmt, 1, &one, sms, stream));
+      if (st != PQ_OK) return st;
+      continue;
+    }
+    const int st = cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse + f, nullptr, pq::MODE_SSE, sms, stream));
+    if (st != PQ_OK) return st;
+  }
+  if (n_mx > 0) return cuda_status(pq::launch_mxsse(w, rows, cols, mx, n_mx, mx_sse, sms, stream));
+  return PQ_OK;
 }
 
 int pq_weighted_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, const float* h, int h_per_row,

@@ -19,6 +19,7 @@
 // computes the H-weighted error sum behind predicted_dloss.
 #include <type_traits>
 #include "pq_common.cuh"
+#include "pq_fast.cuh"
 #include "pq_internal.h"
 
 namespace pq {
@@ -300,6 +301,46 @@ __device__ __forceinline__ void mx_rec8(const uint4& u, const float (&wv)[8], in
   }
 }
 
+// Squared error of 8 elements of an MX group (one 16-byte word of bf16 pairs) with scale 2^es,
+// |es| <= 100, no NaN among them, on packed bf16 pairs (cost path only: at a tie both grid
+// neighbours are equally far, so the tie rule does not change the squared error):
+//  - |w| >= 2^(EMIN+es): the magnitude rounded to M mantissa bits on the bit pattern (half up; a
+//    finite bf16 half never carries into its sign bit or the other half), saturated at
+//    MAXV 2^es by a packed magnitude min;
+//  - |w| <= 2^(EMIN+es): w rounded on the grid of step 2^(EMIN+es-MS) (MS = M with subnormals,
+//    0 without, where the grid below 2^EMIN is {0, 2^EMIN}) by adding and subtracting
+//    C = 1.5 x 2^(step + 7) in bf16 arithmetic: w + C stays in C's binade, whose spacing is the
+//    step, and the subtraction is exact;
+//  - the range test is a packed subtraction 0x8000 + bits(2^(EMIN+es)) - |w| per half, whose bit
+//    15 is set iff |w| <= 2^(EMIN+es) (no borrow crosses halves), spread over the half by a
+//    sign-replicating byte permute.
+// The error w - q is exact in bf16 (q is w rounded within its binade, or the saturation value
+// one binade below a larger w, or a grid point within 2^(EMIN+es) of a subnormal-range w), so
+// its square is exact in fp32.  Returns the fp32 sum of the 8 squares.
+template <int KIND>
+__device__ __forceinline__ float mx_sse8(const uint4& u, int es) {
+  using K = XK<KIND>;
+  constexpr int MS = K::SUB ? K::M : 0;
+  constexpr uint32_t DROP = 7 - K::M;
+  constexpr uint32_t HALFUP = (1u << (DROP - 1)) * 0x00010001u;
+  constexpr uint32_t MASK = ((0xFFFFu >> DROP) << DROP) * 0x00010001u;
+  const uint32_t sat2 = ((__float_as_uint(K::MAXV) >> 16) + ((uint32_t)es << 7)) * 0x00010001u;
+  const uint32_t lo = (uint32_t)(K::EMIN + es + 127) << 7;                       // bits of 2^(EMIN+es)
+  const uint32_t thr2 = (0x8000u + lo) * 0x00010001u;
+  const uint32_t c2 = ((((uint32_t)(K::EMIN + es - MS + 7 + 127)) << 7) | 0x40u) * 0x00010001u;   // 1.5 x 2^(step+7)
+  const uint32_t words[4] = {u.x, u.y, u.z, u.w};
+  float acc = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t v = words[p];
+    const uint32_t qn = bf16x2_minabs((v + HALFUP) & MASK, sat2);
+    const uint32_t qs = bf16x2_sub(bf16x2_add(v, c2), c2);
+    const uint32_t m = prmt_sign_halves(thr2 - (v & 0x7FFF7FFFu));   // 0xFFFF where |w| <= 2^(EMIN+es)
+    acc = sq2_acc(bf16x2_sub(v, (qs & m) | (qn & ~m)), acc);
+  }
+  return acc;
+}
+
 // NaN among 8 bf16 values: a magnitude above 0x7F80 in some half
 __device__ __forceinline__ bool has_nan8(const uint4& u) {
   const uint32_t t = (((u.x & 0x7FFF7FFFu) + 0x007F007Fu) | ((u.y & 0x7FFF7FFFu) + 0x007F007Fu) |
@@ -387,9 +428,12 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
       const float scale = scale_of(a, inv);
       if (valid) {
         // an MX group in range with no NaN among the lane's 8 takes the integer reconstruction
-        if (MXK && f.mx && scale >= 0x1p-100f && scale <= 0x1p100f && !has_nan8(u))
-          do8(u, wv, r * cols + col, r, scale, inv, std::true_type{});
-        else
+        if (MXK && f.mx && scale >= 0x1p-100f && scale <= 0x1p100f && !has_nan8(u)) {
+          if (MODE == MODE_SSE && h_mode == 0)
+            acc += (double)mx_sse8<(KIND == XK_INT ? XK_E2M1 : KIND)>(u, (int)(__float_as_uint(scale) >> 23) - 127);
+          else
+            do8(u, wv, r * cols + col, r, scale, inv, std::true_type{});
+        } else
           do8(u, wv, r * cols + col, r, scale, inv, std::false_type{});
       }
     }
@@ -470,4 +514,173 @@ cudaError_t launch_xfmt(const uint16_t* w, int64_t rows, int64_t cols, int fmt, 
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Squared error of the MX formats (E8M0 scale per 32 elements) from one read of the weights,
+// unweighted (the cost path's weight_mse), any set of the five MX kinds in one launch.  Rows are
+// a multiple of 32 elements, so the tensor is one flat run of 32-element groups: a lane takes
+// 16-byte words (8 elements) and the four lanes of a group reduce its maximum magnitude with two
+// shuffles.  The group exponent, round(log2(max(amax, 1e-8) / cmax)) (format_registry.py:175-191),
+// has a closed form in the bits of the bf16 maximum: with E its unbiased exponent and m its 7
+// mantissa bits, e = E + C + (m >= T) for amax >= 1e-8 and a constant below it, per format
+// (tests/test_fast_rules.py checks C, T and the constant against the torch-derived rule for every
+// bf16 value).  Groups with e <= 100 and a finite maximum take mx_sse8; the others (an infinity or
+// NaN in the group, or a scale above 2^100) the generic per-element rule.
+
+// closed-form group exponent of each MX kind
+template <int KIND> struct MXE;
+template <> struct MXE<XK_E2M1> { static constexpr int C = -3, T = 8, FLOOR = -29; };
+template <> struct MXE<XK_E3M2> { static constexpr int C = -5, T = 31, FLOOR = -31; };
+template <> struct MXE<XK_E2M3> { static constexpr int C = -3, T = 42, FLOOR = -29; };
+template <> struct MXE<XK_E4M3> { static constexpr int C = -9, T = 31, FLOOR = -35; };
+template <> struct MXE<XK_E5M2> { static constexpr int C = -17, T = 31, FLOOR = -43; };
+constexpr uint32_t BF16_1EM8_CEIL = 0x322Cu;   // the smallest bf16 magnitude >= 1e-8f
+
+template <int KIND>
+__device__ __forceinline__ int mx_exp_closed(uint32_t ab) {   // ab: finite max |w| bits
+  using X = MXE<KIND>;
+  return ab < BF16_1EM8_CEIL ? X::FLOOR : (int)(ab >> 7) - 127 + X::C + ((ab & 0x7Fu) >= (uint32_t)X::T ? 1 : 0);
+}
+
+// The generic rule for 8 elements of a group with scale 2^e (what xfmt2_kernel does for them).
+template <int KIND>
+__device__ __forceinline__ float mx_sse8_generic(const uint4& u, int e) {
+  const float scale = pow2i(e);
+  const float inv = __frcp_rn(scale);
+  float wv[8];
+  unpack8(u, wv);
+  float part = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float x = __fmul_rn(wv[i], inv);
+    const float rec = bf16_round(__fmul_rn(xk_round<KIND>(x, 0), scale));
+    const float er = bf16_round(__fsub_rn(wv[i], rec));
+    part = __fadd_rn(part, __fmul_rn(er, er));
+  }
+  return part;
+}
+
+// max |w| bits over 8 bf16 values (integer max of the magnitude patterns: NaN above infinity
+// above every finite value, which it orders as float comparisons do)
+__device__ __forceinline__ uint32_t amax_bits8(const uint4& u) {
+  uint32_t t;
+  asm("{\n\t.reg .b32 a, b;\n\t"
+      "max.u16x2 a, %1, %2;\n\tmax.u16x2 b, %3, %4;\n\tmax.u16x2 %0, a, b;\n\t}"
+      : "=r"(t)
+      : "r"(u.x & 0x7FFF7FFFu), "r"(u.y & 0x7FFF7FFFu), "r"(u.z & 0x7FFF7FFFu), "r"(u.w & 0x7FFF7FFFu));
+  return max(t & 0xFFFFu, t >> 16);
+}
+
+// kinds present in a kind mask, in a fixed order; bit k = kind XK_E2M1 + k ... see mx_kind_bit
+__host__ __device__ constexpr int mx_kind_bit(int kind) {
+  return kind == XK_E2M1 ? 0 : kind == XK_E3M2 ? 1 : kind == XK_E2M3 ? 2 : kind == XK_E4M3 ? 3 : 4;
+}
+constexpr int MX_KIND_OF_BIT[5] = {XK_E2M1, XK_E3M2, XK_E2M3, XK_E4M3, XK_E5M2};
+
+struct MxSseLaunch {
+  double* sse[5];   // per kind bit: the format's fp64 sum (added to), null if absent
+};
+
+// one format of the set: its partial for this word, added to the fp32 accumulator
+template <uint32_t KM, int BIT>
+__device__ __forceinline__ void mx_word(const uint4& u, uint32_t ab, bool finite, float (&acc)[5]) {
+  if constexpr ((KM >> BIT) & 1u) {
+    constexpr int K = MX_KIND_OF_BIT[BIT];
+    const int e = finite ? mx_exp_closed<K>(ab) : 127;   // an infinity's group: log2 clamped at 127
+    acc[BIT] += (finite && e <= 100) ? mx_sse8<K>(u, e) : mx_sse8_generic<K>(u, e);
+  }
+}
+
+constexpr int MXSSE_UNROLL = 4;   // 16-byte words per lane in flight per pass
+
+template <uint32_t KM>
+__global__ void __launch_bounds__(256) mxsse_kernel(const uint4* __restrict__ w, int64_t nwords,
+                                                    const __grid_constant__ MxSseLaunch L) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_first = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * (32 * MXSSE_UNROLL);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * MXSSE_UNROLL;
+  double acc[5] = {0.0, 0.0, 0.0, 0.0, 0.0};
+  // warp-uniform loop: a pass covers 32 x MXSSE_UNROLL consecutive words; a 4-word group is all
+  // inside the tensor or all past its end (nwords is a multiple of 4), and words past the end
+  // are zeros, which add nothing
+  for (int64_t base = warp_first; base < nwords; base += stride) {
+    uint4 u[MXSSE_UNROLL];
+#pragma unroll
+    for (int k = 0; k < MXSSE_UNROLL; ++k) {
+      const int64_t j = base + 32 * k + lane;
+      u[k] = j < nwords ? __ldg(w + j) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float part[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};   // <= 32 exact squares each
+#pragma unroll
+    for (int k = 0; k < MXSSE_UNROLL; ++k) {
+      uint32_t ab = amax_bits8(u[k]);
+      ab = max(ab, (uint32_t)__shfl_xor_sync(FULL, ab, 1));
+      ab = max(ab, (uint32_t)__shfl_xor_sync(FULL, ab, 2));
+      const bool finite = ab < 0x7F80u;
+      mx_word<KM, 0>(u[k], ab, finite, part);
+      mx_word<KM, 1>(u[k], ab, finite, part);
+      mx_word<KM, 2>(u[k], ab, finite, part);
+      mx_word<KM, 3>(u[k], ab, finite, part);
+      mx_word<KM, 4>(u[k], ab, finite, part);
+    }
+#pragma unroll
+    for (int f = 0; f < 5; ++f)
+      if ((KM >> f) & 1u) acc[f] += (double)part[f];
+  }
+#pragma unroll
+  for (int f = 0; f < 5; ++f) {
+    if (!((KM >> f) & 1u)) continue;
+    const double v = warp_sum_d(acc[f]);
+    if (lane == 0 && v != 0.0) atomicAdd(L.sse[f], v);
+  }
+}
+
+// MX kind of a format, false if it is not an MX format of this kernel
+__host__ __device__ inline bool mx_kind_of(int fmt, int& kind) {
+  switch (fmt) {
+    case PQ_FMT_MXFP4: kind = XK_E2M1; return true;
+    case PQ_FMT_MXFP6_E3M2: kind = XK_E3M2; return true;
+    case PQ_FMT_MXFP6_E2M3: kind = XK_E2M3; return true;
+    case PQ_FMT_MXFP8: kind = XK_E4M3; return true;
+    case PQ_FMT_MXFP8_E5M2: kind = XK_E5M2; return true;
+    default: return false;
+  }
+}
+
+// The one-read path applies: the format is an MX format of mxsse_kernel, rows are a whole number
+// of 32-element groups, and the weights start on a 16-byte boundary.
+bool mxsse_ok(const uint16_t* w, int64_t cols, int fmt) {
+  int kind;
+  return mx_kind_of(fmt, kind) && cols % 32 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+}
+
+// fmts: distinct MX formats, each mxsse_ok; sse[f] receives format f's sum
+cudaError_t launch_mxsse(const uint16_t* w, int64_t rows, int64_t cols, const int* fmts, int nf,
+                         double* const* sse, int num_sms, cudaStream_t stream) {
+  MxSseLaunch L{};
+  uint32_t km = 0;
+  for (int f = 0; f < nf; ++f) {
+    int kind = 0;
+    mx_kind_of(fmts[f], kind);
+    const int bit = mx_kind_bit(kind);
+    km |= 1u << bit;
+    L.sse[bit] = sse[f];
+  }
+  const int64_t nwords = rows * cols / 8;
+  int64_t blocks = (nwords + 256 * MXSSE_UNROLL - 1) / (256 * MXSSE_UNROLL);
+  if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
+  if (blocks < 1) blocks = 1;
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  switch (km) {
+#define PQ_MX_CASE(M) \
+    case M: mxsse_kernel<M><<<(unsigned)blocks, 256, 0, stream>>>(w4, nwords, L); break;
+    PQ_MX_CASE(1) PQ_MX_CASE(2) PQ_MX_CASE(3) PQ_MX_CASE(4) PQ_MX_CASE(5) PQ_MX_CASE(6) PQ_MX_CASE(7)
+    PQ_MX_CASE(8) PQ_MX_CASE(9) PQ_MX_CASE(10) PQ_MX_CASE(11) PQ_MX_CASE(12) PQ_MX_CASE(13) PQ_MX_CASE(14)
+    PQ_MX_CASE(15) PQ_MX_CASE(16) PQ_MX_CASE(17) PQ_MX_CASE(18) PQ_MX_CASE(19) PQ_MX_CASE(20) PQ_MX_CASE(21)
+    PQ_MX_CASE(22) PQ_MX_CASE(23) PQ_MX_CASE(24) PQ_MX_CASE(25) PQ_MX_CASE(26) PQ_MX_CASE(27) PQ_MX_CASE(28)
+    PQ_MX_CASE(29) PQ_MX_CASE(30) PQ_MX_CASE(31)
+#undef PQ_MX_CASE
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
 }  // namespace pq

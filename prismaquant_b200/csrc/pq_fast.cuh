@@ -258,6 +258,19 @@ __device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
   asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+// Each 16-bit half set to all ones where its bit 15 is set, else zero: PTX prmt in its generic
+// mode, where a selector nibble with bit 3 set replicates the sign bit of the chosen byte
+// (bytes 1 and 3 here).  (CUDA's __byte_perm reads only the low 3 bits of each nibble.)
+__device__ __forceinline__ uint32_t prmt_sign_halves(uint32_t x) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, 0, 0xBB99;" : "=r"(d) : "r"(x));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 // max(|a|, |b|) per half (sign = sign(a) ^ sign(b)); on magnitudes it is the magnitude max.
 __device__ __forceinline__ uint32_t bf16x2_maxabs(uint32_t a, uint32_t b) {
   uint32_t d;

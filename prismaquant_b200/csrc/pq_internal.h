@@ -47,6 +47,9 @@ static_assert(sizeof(SweepLaunch) <= 32764, "a SweepLaunch is passed as one kern
 size_t sweep_smem_bytes();
 size_t sweep_fast_smem_bytes();
 int64_t xfmt_group(int fmt, int64_t cols);
+bool mxsse_ok(const uint16_t* w, int64_t cols, int fmt);
+cudaError_t launch_mxsse(const uint16_t* w, int64_t rows, int64_t cols, const int* fmts, int nf,
+                         double* const* sse, int num_sms, cudaStream_t stream);
 cudaError_t launch_xfmt(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, uint16_t* out,
                         int mode, int num_sms, cudaStream_t stream, const float* h = nullptr, int h_mode = 0);
 cudaError_t launch_sweep_fast(const SweepLaunch& L, int grid, uint32_t key, cudaStream_t stream);

@@ -191,10 +191,13 @@ def sweep_weight_mse(named_weights, specs: list[fr.FormatSpec],
     sse, errors = sweep_sse_async(weights, [_as_kernel_spec(s, kf[s.name]) for s in fused])
     ext_sse = torch.zeros(len(weights), max(len(ext), 1), dtype=torch.float64, device=weights[0].device)
     for i, w in enumerate(weights):
+        bad = {s.name: shape_error(kf[s.name], w.shape[-1]) for s in ext}
+        if ext and not any(bad.values()):   # the MX formats among them from one read
+            _lib.format_sse_multi(w, [kf[s.name] for s in ext], ext_sse[i])
+            continue
         for j, s in enumerate(ext):
-            e = shape_error(kf[s.name], w.shape[-1])
-            if e:
-                errors[i][s.name] = e
+            if bad[s.name]:
+                errors[i][s.name] = bad[s.name]
             else:
                 _lib.format_sse(w, kf[s.name], ext_sse[i, j])
     host, ext_host = sse.cpu().tolist(), ext_sse.cpu().tolist()   # the device->host copies

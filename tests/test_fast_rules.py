@@ -174,3 +174,91 @@ def test_fp8_channel_full_kernel_rule_exact_for_every_bf16_pair():
             bad += np.count_nonzero(got != want)
             n += w.size
     assert n > 10_000_000 and bad == 0
+
+
+# MX formats of the codebook kernel's packed squared-error path (mx_sse8): kind -> (M, EMIN,
+# subnormals, MAXV), as in the codebook kernel's table of kinds
+MX_KINDS = {"E2M1": (1, 0, True, 6.0), "E3M2": (2, -3, False, 28.0), "E2M3": (3, -1, False, 7.5),
+            "E4M3": (3, -6, True, 448.0), "E5M2": (2, -14, True, 114688.0)}
+
+
+def _mx_grid(M, EMIN, sub, maxv):
+    """Non-negative grid points of the format (the reference's codebook magnitudes)."""
+    pts = {0.0}
+    e = EMIN
+    while True:
+        for k in range(1 << M):
+            v = (1 + k / (1 << M)) * 2.0 ** e
+            if v <= maxv:
+                pts.add(v)
+        if 2.0 ** e > maxv:
+            break
+        e += 1
+    if sub:
+        pts |= {k / (1 << M) * 2.0 ** EMIN for k in range(1 << M)}
+    return np.array(sorted(pts))
+
+
+def _mx_sse8_emulated(bits, es, M, EMIN, sub, maxv):
+    """The packed path's grid point for each bf16 pattern (int arithmetic as the kernel does it;
+    the bf16 add/subtract of C as its exact value: w rounded to the step, ties to the even
+    multiple)."""
+    MS = M if sub else 0
+    drop = 7 - M
+    mag = bits.astype(np.int64) & 0x7FFF
+    sign = np.where(bits & 0x8000, -1.0, 1.0)
+    qn_mag = (mag + (1 << (drop - 1))) & ((0xFFFF >> drop) << drop)
+    sat = (int(np.array([maxv], dtype=np.float32).view(np.uint32)[0]) >> 16) + (es << 7)
+    qn_mag = np.minimum(qn_mag, sat)
+    qn = sign * ((qn_mag << 16).astype(np.uint32).view(np.float32).astype(np.float64))
+    w = ((bits.astype(np.uint32) << 16).view(np.float32)).astype(np.float64)
+    step = 2.0 ** (EMIN + es - MS)
+    qs = np.round(w / step) * step                                   # numpy rounds half to even
+    lo = (EMIN + es + 127) << 7
+    d = 0x8000 + lo - mag                    # one half of the packed subtraction: never negative,
+    assert (d > 0).all()                     # so no borrow reaches the other half
+    return w, np.where(d & 0x8000, qs, qn)   # bit 15 (spread over the half by the byte permute)
+
+
+def test_mx_packed_cost_rounding_matches_the_codebook_rule():
+    """mx_sse8's grid point gives the reference's squared error for every finite bf16 w, every
+    MX kind the codebook kernel serves, at scales 2^es across its fast range (|es| <= 100)."""
+    b = np.arange(1 << 16, dtype=np.uint32)
+    with np.errstate(invalid="ignore"):
+        f = (b << 16).view(np.float32)
+    bits = b[np.isfinite(f)].astype(np.uint16)
+    for name, (M, EMIN, sub, maxv) in MX_KINDS.items():
+        grid = _mx_grid(M, EMIN, sub, maxv)
+        for es in (-100, -40, -7, -1, 0, 3, 20, 100):
+            w, q = _mx_sse8_emulated(bits, es, M, EMIN, sub, maxv)
+            x = np.abs(w) / 2.0 ** es
+            i = np.clip(np.searchsorted(grid, x), 1, len(grid) - 1)
+            lo_, hi_ = grid[i - 1], grid[i]
+            ref = np.where(hi_ - x < x - lo_, hi_, lo_)          # nearest, ties to the lower magnitude
+            ref = np.where(x >= grid[-1], grid[-1], ref) * 2.0 ** es
+            ok = np.abs(np.abs(w - q) - np.abs(np.abs(w) - ref)) == 0
+            assert ok.all(), (name, es, w[~ok][:5], q[~ok][:5], ref[~ok][:5])
+
+
+def test_mx_group_exponent_closed_form_matches_the_torch_rule():
+    """mxsse_kernel's closed form e = E + C + (m >= T) (FLOOR below 1e-8) against
+    round(log2(max(max(amax, 1e-8) / cmax, 2^-127))) with the torch-derived thresholds, for every
+    finite bf16 amax and each MX kind; the constants are read from the kernel source."""
+    import re
+    from pathlib import Path
+    from oracle import pq_oracle as O
+    src = (Path(__file__).resolve().parent.parent / "prismaquant_b200" / "csrc" / "pq_codebook.cu").read_text()
+    consts = {k: tuple(int(x) for x in v) for k, *v in
+              re.findall(r"struct MXE<XK_(\w+)> \{ static constexpr int C = (-?\d+), T = (\d+), FLOOR = (-?\d+); \}", src)}
+    ceil_1em8 = int(re.search(r"BF16_1EM8_CEIL = 0x([0-9A-Fa-f]+)u", src).group(1), 16)
+    assert set(consts) == set(MX_KINDS)
+    assert (np.array([ceil_1em8 << 16], dtype=np.uint32).view(F32)[0] >= F32(1e-8) >
+            np.array([(ceil_1em8 - 1) << 16], dtype=np.uint32).view(F32)[0])
+    b = np.arange(0x7F80, dtype=np.uint32)               # every finite bf16 magnitude
+    a = (b << 16).view(F32)
+    for kind, (C, T, FLOOR) in consts.items():
+        cmax = F32(MX_KINDS[kind][3])
+        s = np.maximum((np.maximum(a, F32(1e-8)) / cmax).astype(F32), F32(2.0 ** -127))
+        want = O.e8m0().round_log2(s)
+        got = np.where(b < ceil_1em8, FLOOR, (b >> 7).astype(np.int64) - 127 + C + ((b & 0x7F) >= T))
+        assert np.array_equal(got, want), kind

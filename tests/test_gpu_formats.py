@@ -149,3 +149,76 @@ def test_misaligned_view_takes_the_scalar_kernel_with_equal_results(fmt):
     _lib.format_sse(w, fmt, s1)
     _lib.format_sse(wm, fmt, s2)
     assert s1.item() == pytest.approx(s2.item(), rel=1e-6)   # fp32 partials of 8 vs 64 squares
+
+
+MX_EXT = ["MXFP4", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E5M2"]
+
+
+def _oracle_sse(bits, fmt):
+    err = O.bf16_round((O.bf16_bits_to_f32(bits) - O.cost_qdq_f32(bits, fmt)).astype(np.float32))
+    with np.errstate(over="ignore", invalid="ignore"):
+        return float((err * err).astype(np.float32).astype(np.float64).sum())
+
+
+def _special_rows(kind):
+    """Rows of 32-element groups that leave the packed path: tiny scales (group exponents below
+    -100, whose squares underflow), all-zero groups (the 1e-8 floor) and bf16 subnormals beside
+    ordinary groups ("tiny"); a group with an exponent above 100, whose squared error overflows
+    fp32 as the reference's does ("huge"); an infinity in a group, whose error is inf - inf
+    ("inf")."""
+    rng = np.random.default_rng(7)
+    f = O.bf16_bits_to_f32(O.synthetic_weight_bits((16, 64), seed=9, outlier_frac=0.0)).astype(np.float32)
+    f[1, 32:] *= np.float32(2.0 ** -110)
+    f[2, :32] = 0.0
+    f[5, :] = rng.standard_normal(64).astype(np.float32) * np.float32(2.0 ** -126)
+    if kind == "huge":
+        f[0, :32] *= np.float32(2.0 ** 120)
+    if kind == "inf":
+        f[3, 5] = np.inf
+    return O.f32_to_bf16_bits(f)
+
+
+@pytest.mark.parametrize("kind", ["tiny", "huge", "inf"])
+def test_mx_multi_format_sse_special_groups(kind):
+    """Groups outside the packed path's range, subnormals, overflowing squares and infinities: the
+    oracle's sums, inf and NaN included (the MX formats from one read, the rest one by one)."""
+    import warnings
+    from prismaquant_b200 import _lib
+    bits = _special_rows(kind)
+    fmts = MX_EXT + ["INT3", "BF16", "FP8_E5M2"]
+    out = torch.zeros(len(fmts), dtype=torch.float64, device="cuda")
+    _lib.format_sse_multi(to_cuda_bf16(bits), fmts, out)
+    got = out.cpu().numpy()
+    for i, fmt in enumerate(fmts):
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            want = 0.0 if fmt == "BF16" else _oracle_sse(bits, fmt)
+        if np.isnan(want):
+            assert np.isnan(got[i]), (fmt, got[i])
+        elif np.isinf(want):
+            assert got[i] == want, (fmt, got[i])
+        else:
+            assert got[i] == pytest.approx(want, rel=1e-5, abs=1e-30), fmt
+
+
+def test_mx_multi_format_sse_rejects_before_running():
+    """A format that cannot group the rows fails the whole call and adds nothing."""
+    from prismaquant_b200 import _lib
+    w = to_cuda_bf16(O.synthetic_weight_bits((4, 40), seed=2))
+    out = torch.zeros(2, dtype=torch.float64, device="cuda")
+    with pytest.raises(ValueError):
+        _lib.format_sse_multi(w, ["FP8_E5M2", "MXFP4"], out)
+    assert (out == 0).all()
+
+
+def test_mx_multi_format_sse_repeated_and_mixed_formats():
+    """A repeated MX format is scored on its own, a non-MX one by the codebook kernel; every entry
+    equals the oracle's sum for its format."""
+    from prismaquant_b200 import _lib
+    bits = O.synthetic_weight_bits((64, 96), seed=4, outlier_frac=0.01)
+    w = to_cuda_bf16(bits)
+    fmts = ["MXFP4", "MXFP4", "MXFP6_E2M3", "NVFP3", "MXFP8_E5M2", "MXFP6_E3M2"]
+    out = torch.zeros(len(fmts), dtype=torch.float64, device="cuda")
+    _lib.format_sse_multi(w, fmts, out)
+    for i, f in enumerate(fmts):
+        assert out[i].item() == pytest.approx(_oracle_sse(bits, f), rel=1e-5, abs=1e-30), f
