@@ -218,6 +218,8 @@ int pq_format_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double
   if (!w || !sse) return PQ_ERR_NULL;
   if (pq::mxsse_ok(w, cols, fmt))
     return cuda_status(pq::launch_mxsse(w, rows, cols, &fmt, 1, &sse, num_sms_current(), (cudaStream_t)stream_));
+  if (pq::intsse_ok(w, cols, fmt))
+    return cuda_status(pq::launch_intsse(w, rows, cols, fmt, sse, num_sms_current(), (cudaStream_t)stream_));
   return cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse, nullptr, pq::MODE_SSE, num_sms_current(),
                                      (cudaStream_t)stream_));
 }
@@ -253,7 +255,9 @@ int pq_format_sse_multi(const uint16_t* w, int64_t rows, int64_t cols, const int
       if (st != PQ_OK) return st;
       continue;
     }
-    const int st = cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse + f, nullptr, pq::MODE_SSE, sms, stream));
+    const int st = pq::intsse_ok(w, cols, fmt)
+                       ? cuda_status(pq::launch_intsse(w, rows, cols, fmt, sse + f, sms, stream))
+                       : cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse + f, nullptr, pq::MODE_SSE, sms, stream));
     if (st != PQ_OK) return st;
   }
   if (n_mx > 0) return cuda_status(pq::launch_mxsse(w, rows, cols, mx, n_mx, mx_sse, sms, stream));

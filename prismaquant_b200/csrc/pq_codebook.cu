@@ -683,4 +683,91 @@ cudaError_t launch_mxsse(const uint16_t* w, int64_t rows, int64_t cols, const in
   }
   return cudaGetLastError();
 }
+// ---------------------------------------------------------------------------
+// Squared error of the grouped symmetric integer formats (INT2 / INT3 in groups of 16, INT4 in
+// groups of 128; format_registry.py:147-172): s = fl32(max(amax, 1e-8) / L), q = round half even
+// (fl32(w / s)) clamped to [-L-1, L], W_hat = bf16(q s).  The quotient comes from the product
+// p = RN(w r), r = RN(1 / s): |p - w / s| and |fl32(w / s) - w / s| are below 2^-22 |w / s|, so
+// unless p lies within 2^-19 |M| of a midpoint M = k + 1/2 (the nearest one is floor(p) + 1/2),
+// p and fl32(w / s) round to the same integer.  The elements within that distance (every exact
+// tie among them) take IEEE division; they are about 1e-4 of bf16 data.  Rows are a multiple of
+// the group, so the tensor is one flat run of groups; LANES = group / 8 lanes reduce a group's
+// maximum.  Groups with an infinity or NaN take IEEE division throughout.
+template <int L>
+__device__ __forceinline__ float int_err_sq(float w, float s, float r, bool exact) {
+  const float p = __fmul_rn(w, r);
+  const float mid = floorf(p) + 0.5f;
+  float x = p;
+  if (exact || fabsf(p - mid) <= fabsf(mid) * 0x1p-19f) x = __fdiv_rn(w, s);   // rare
+  const float q = fminf(fmaxf(rintf(x), (float)(-L - 1)), (float)L);
+  const float e = bf16_round(__fsub_rn(w, bf16_round(__fmul_rn(q, s))));
+  return __fmul_rn(e, e);   // the reference squares in fp32
+}
+
+template <int L, int LANES>
+__global__ void __launch_bounds__(256) intsse_kernel(const uint4* __restrict__ w, int64_t nwords, double* sse) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_first = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * (32 * MXSSE_UNROLL);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * MXSSE_UNROLL;
+  double acc = 0.0;
+  for (int64_t base = warp_first; base < nwords; base += stride) {   // warp-uniform
+    uint4 u[MXSSE_UNROLL];
+#pragma unroll
+    for (int k = 0; k < MXSSE_UNROLL; ++k) {
+      const int64_t j = base + 32 * k + lane;
+      u[k] = j < nwords ? __ldg(w + j) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float part = 0.0f;
+#pragma unroll
+    for (int k = 0; k < MXSSE_UNROLL; ++k) {
+      uint32_t ab = amax_bits8(u[k]);
+#pragma unroll
+      for (int o = 1; o < LANES; o <<= 1) ab = max(ab, (uint32_t)__shfl_xor_sync(FULL, ab, o));
+      const bool finite = ab < 0x7F80u;
+      const float s = __fdiv_rn(fmaxf(__uint_as_float(ab << 16), 1e-8f), (float)L);
+      const float r = __frcp_rn(s);
+      float wv[8];
+      unpack8(u[k], wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) part = __fadd_rn(part, int_err_sq<L>(wv[i], s, r, !finite));
+    }
+    acc += (double)part;   // fp32 partials of 32 exact squares
+  }
+  const double v = warp_sum_d(acc);
+  if (lane == 0 && v != 0.0) atomicAdd(sse, v);
+}
+
+// levels L and group length of a grouped integer format of intsse_kernel (0 if it is not one)
+__host__ __device__ inline int int_group_of(int fmt, int& L) {
+  switch (fmt) {
+    case PQ_FMT_INT2: L = 1; return 16;
+    case PQ_FMT_INT3: L = 3; return 16;
+    case PQ_FMT_INT4_G128: L = 7; return 128;
+    default: return 0;
+  }
+}
+
+bool intsse_ok(const uint16_t* w, int64_t cols, int fmt) {
+  int L;
+  const int g = int_group_of(fmt, L);
+  return g > 0 && cols > g && cols % g == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+}
+
+cudaError_t launch_intsse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, int num_sms,
+                          cudaStream_t stream) {
+  int L = 0;
+  int_group_of(fmt, L);
+  const int64_t nwords = rows * cols / 8;
+  int64_t blocks = (nwords + 256 * MXSSE_UNROLL - 1) / (256 * MXSSE_UNROLL);
+  if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
+  if (blocks < 1) blocks = 1;
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  switch (fmt) {
+    case PQ_FMT_INT2: intsse_kernel<1, 2><<<(unsigned)blocks, 256, 0, stream>>>(w4, nwords, sse); break;
+    case PQ_FMT_INT3: intsse_kernel<3, 2><<<(unsigned)blocks, 256, 0, stream>>>(w4, nwords, sse); break;
+    default: intsse_kernel<7, 16><<<(unsigned)blocks, 256, 0, stream>>>(w4, nwords, sse); break;
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace pq

@@ -48,6 +48,9 @@ size_t sweep_smem_bytes();
 size_t sweep_fast_smem_bytes();
 int64_t xfmt_group(int fmt, int64_t cols);
 bool mxsse_ok(const uint16_t* w, int64_t cols, int fmt);
+bool intsse_ok(const uint16_t* w, int64_t cols, int fmt);
+cudaError_t launch_intsse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, int num_sms,
+                          cudaStream_t stream);
 cudaError_t launch_mxsse(const uint16_t* w, int64_t rows, int64_t cols, const int* fmts, int nf,
                          double* const* sse, int num_sms, cudaStream_t stream);
 cudaError_t launch_xfmt(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, uint16_t* out,

@@ -222,3 +222,41 @@ def test_mx_multi_format_sse_repeated_and_mixed_formats():
     _lib.format_sse_multi(w, fmts, out)
     for i, f in enumerate(fmts):
         assert out[i].item() == pytest.approx(_oracle_sse(bits, f), rel=1e-5, abs=1e-30), f
+
+
+INT_GROUPED = ["INT2", "INT3", "INT4_W4A16_g128"]
+
+
+def _int_tie_rows():
+    """Rows whose quotients w / s sit exactly on half-integers (round half even decides) next to
+    rows with inexact scales: each group's maximum is L (s = 1) or L x 2^k with odd multiples of
+    s / 2 around it, and groups with maximum 1 (s = fl32(1 / L))."""
+    rng = np.random.default_rng(3)
+    rows = []
+    for L in (1, 3, 7):
+        for k in (-3, 0, 5):
+            half = (rng.integers(-L, L, size=256) + 0.5) * 2.0 ** k   # |x| <= L - 1/2: ties
+            half[::16] = L * 2.0 ** k        # the group maximum
+            rows.append(half)
+        rows.append(rng.uniform(-1, 1, size=256))
+    f = np.clip(np.array(rows, dtype=np.float32), -1e30, 1e30)
+    return O.f32_to_bf16_bits(f)
+
+
+@pytest.mark.parametrize("fmt", INT_GROUPED)
+@pytest.mark.parametrize("case", ["every_bf16", "ties"])
+def test_int_grouped_sse_matches_oracle(fmt, case):
+    """The grouped integer formats' squared error (product with exact fallback near midpoints)
+    against the oracle, and against the codebook kernel's IEEE division (the weighted sum with
+    unit weights)."""
+    from prismaquant_b200 import _lib
+    bits = _all_bf16_rows(256) if case == "every_bf16" else _int_tie_rows()
+    w = to_cuda_bf16(bits)
+    got = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.format_sse(w, fmt, got)
+    ref = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.weighted_sse(w, fmt, torch.ones(bits.size, dtype=torch.float32, device="cuda"), ref)
+    want = _oracle_sse(bits, fmt)
+    assert got.item() == pytest.approx(want, rel=1e-5, abs=1e-30), fmt
+    # fp32 partials of 32 squares here, of 8 there: the sums agree to fp32 rounding
+    assert got.item() == pytest.approx(ref.item(), rel=1e-6, abs=1e-30), fmt
