@@ -686,13 +686,13 @@ cudaError_t launch_mxsse(const uint16_t* w, int64_t rows, int64_t cols, const in
 // ---------------------------------------------------------------------------
 // Squared error of the grouped symmetric integer formats (INT2 / INT3 in groups of 16, INT4 in
 // groups of 128; format_registry.py:147-172): s = fl32(max(amax, 1e-8) / L), q = round half even
-// (fl32(w / s)) clamped to [-L-1, L], W_hat = bf16(q s).  The quotient comes from the product
-// p = RN(w r), r = RN(1 / s): |p - w / s| and |fl32(w / s) - w / s| are below 2^-22 |w / s|, so
-// unless p lies within 2^-19 |M| of a midpoint M = k + 1/2 (the nearest one is floor(p) + 1/2),
-// p and fl32(w / s) round to the same integer.  The elements within that distance (every exact
-// tie among them) take IEEE division; they are about 1e-4 of bf16 data.  Rows are a multiple of
-// the group, so the tensor is one flat run of groups; LANES = group / 8 lanes reduce a group's
-// maximum.  Groups with an infinity or NaN take IEEE division throughout.
+// (fl32(w / s)) clamped to [-L-1, L], W_hat = bf16(q s).  The integer comes from a reciprocal
+// bracket, two products per pair of elements (int_sse_word); words where the bracket straddles a
+// half-integer (every exact tie among them) are redone by IEEE division, about 1e-4 of bf16 data.
+// Rows are a multiple of the group, so the tensor is one flat run of groups; LANES = group / 8
+// lanes reduce a group's maximum.  Groups with an infinity or NaN take IEEE division throughout
+// (int_err_sq, which alone takes the product p = RN(w r) when p lies further than 2^-19 |M| from
+// the nearest midpoint M = floor(p) + 1/2).
 template <int L>
 __device__ __forceinline__ float int_err_sq(float w, float s, float r, bool exact) {
   const float p = __fmul_rn(w, r);
@@ -702,6 +702,40 @@ __device__ __forceinline__ float int_err_sq(float w, float s, float r, bool exac
   const float q = fminf(fmaxf(rintf(x), (float)(-L - 1)), (float)L);
   const float e = bf16_round(__fsub_rn(w, bf16_round(__fmul_rn(q, s))));
   return __fmul_rn(e, e);   // the reference squares in fp32
+}
+
+// The 8 elements of one 16-byte word in float32 pairs: the two bracket products p_lo = RN(w r_lo)
+// and p_hi = RN(w r_hi), r_lo / r_hi RN(1/s) (1 -+ 2^-19) rounded, hold fl32(w / s) strictly
+// between them; each is rounded half even to an integer by adding and subtracting 1.5 x 2^23.
+// Where the two integers agree no half-integer lies between the products (one exactly on a
+// half-integer rounds toward the other side's integer or to the same one), so that integer is
+// the reference's; it is never outside [-L, L] here (|w| <= amax).  A word with a pair that
+// disagrees (an exact tie among them) is redone by IEEE division.  Returns the fp32 sum of the
+// 8 exact squares.
+template <int L>
+__device__ __forceinline__ float int_sse_word(const uint4& u, float s, float r_lo, float r_hi) {
+  const uint64_t lo2 = f2_pack(r_lo, r_lo), hi2 = f2_pack(r_hi, r_hi), s2 = f2_pack(s, s);
+  const uint64_t m2 = f2_pack(12582912.0f, 12582912.0f), nm2 = f2_pack(-12582912.0f, -12582912.0f);   // 1.5 x 2^23
+  const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+  float acc = 0.0f;
+  bool split = false;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint64_t w2 = f2_from_bf16x2(v[p]);
+    const uint64_t ql = f2_add_rn(f2_add_rn(f2_mul_rn(w2, lo2), m2), nm2);
+    const uint64_t qh = f2_add_rn(f2_add_rn(f2_mul_rn(w2, hi2), m2), nm2);
+    split = split || ql != qh;
+    acc = sq2_acc(bf16x2_sub(v[p], f2_to_bf16x2(f2_mul_rn(ql, s2))), acc);
+  }
+  if (split) {   // rare
+    const float r = __frcp_rn(s);
+    float wv[8];
+    unpack8(u, wv);
+    acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, int_err_sq<L>(wv[i], s, r, true));
+  }
+  return acc;
 }
 
 template <int L, int LANES>
@@ -725,11 +759,15 @@ __global__ void __launch_bounds__(256) intsse_kernel(const uint4* __restrict__ w
       for (int o = 1; o < LANES; o <<= 1) ab = max(ab, (uint32_t)__shfl_xor_sync(FULL, ab, o));
       const bool finite = ab < 0x7F80u;
       const float s = __fdiv_rn(fmaxf(__uint_as_float(ab << 16), 1e-8f), (float)L);
-      const float r = __frcp_rn(s);
-      float wv[8];
-      unpack8(u[k], wv);
+      if (finite) {
+        const float r = __frcp_rn(s);
+        part += int_sse_word<L>(u[k], s, __fmul_rn(r, 1.0f - 0x1p-19f), __fmul_rn(r, 1.0f + 0x1p-19f));
+      } else {   // an infinity or NaN in the group
+        float wv[8];
+        unpack8(u[k], wv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) part = __fadd_rn(part, int_err_sq<L>(wv[i], s, r, !finite));
+        for (int i = 0; i < 8; ++i) part = __fadd_rn(part, int_err_sq<L>(wv[i], s, 0.0f, true));
+      }
     }
     acc += (double)part;   // fp32 partials of 32 exact squares
   }

@@ -50,6 +50,11 @@ __device__ __forceinline__ uint64_t f2_mul_rn(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint64_t f2_add_rn(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ uint64_t f2_fma_rn(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
