@@ -616,14 +616,55 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and clock-event reasons of the rank's GPU during the timed region: read-only NVML
+    queries, one sample when the region opens, one when it closes and one every 2 ms between
+    (short regions still get samples); nvidia-smi at 200 ms when NVML cannot be loaded."""
+
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
-        self.samples = []
+        self.samples = []   # (sm_mhz, max_mhz, {reason, ...})
         self.proc = None
+        self.nvml = None
+        self.stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:   # the CUDA device's PCI address, so the two orderings cannot disagree
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _sample_nvml(self):
+        nv, h = self.nvml
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        masks = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                             float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)),
+                             {n for n, m in zip(self.NAMES, masks) if bits & m}))
+
+    def _poll(self):
+        while not self.stop.wait(0.002):
+            try:
+                self._sample_nvml()
+            except Exception:
+                return
 
     def __enter__(self):
+        try:
+            self.nvml = self._nvml_handle()
+            self._sample_nvml()
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -640,10 +681,18 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.samples.append(parts)
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                self.samples.append((float(parts[1]), float(parts[2]) if parts[2].replace(".", "").isdigit() else 0.0,
+                                     {n for n, v in zip(self.NAMES, parts[5:9]) if v.lower() == "active"}))
 
     def __exit__(self, *a):
+        if self.nvml is not None:
+            self.stop.set()
+            self.t.join(timeout=5)
+            try:
+                self._sample_nvml()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -654,12 +703,10 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for s in self.samples for n, v in zip(names, s[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples),
+                "reasons": sorted(set().union(*(s[2] for s in self.samples))), "samples": len(self.samples),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------

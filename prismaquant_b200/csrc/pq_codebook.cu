@@ -740,6 +740,7 @@ __device__ __forceinline__ float int_sse_word(const uint4& u, float s, float r_l
 
 template <int L, int LANES>
 __global__ void __launch_bounds__(256) intsse_kernel(const uint4* __restrict__ w, int64_t nwords, double* sse) {
+  static_assert(L == 1 || L == 3 || L == 7, "div_const is checked for these divisors");
   const int lane = threadIdx.x & 31;
   const int64_t warp_first = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * (32 * MXSSE_UNROLL);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * MXSSE_UNROLL;
@@ -758,11 +759,15 @@ __global__ void __launch_bounds__(256) intsse_kernel(const uint4* __restrict__ w
 #pragma unroll
       for (int o = 1; o < LANES; o <<= 1) ab = max(ab, (uint32_t)__shfl_xor_sync(FULL, ab, o));
       const bool finite = ab < 0x7F80u;
-      const float s = __fdiv_rn(fmaxf(__uint_as_float(ab << 16), 1e-8f), (float)L);
+      const float am = fmaxf(__uint_as_float(ab << 16), 1e-8f);
       if (finite) {
-        const float r = __frcp_rn(s);
+        // s = RN(am / L) (div_const is IEEE division for every normal bf16 and the floor); the
+        // bracket tolerates a reciprocal within one ulp
+        const float s = L == 1 ? am : div_const(am, (float)L, L == 3 ? RCP3 : RCP7);
+        const float r = rcp_approx(s);
         part += int_sse_word<L>(u[k], s, __fmul_rn(r, 1.0f - 0x1p-19f), __fmul_rn(r, 1.0f + 0x1p-19f));
       } else {   // an infinity or NaN in the group
+        const float s = __fdiv_rn(am, (float)L);
         float wv[8];
         unpack8(u[k], wv);
 #pragma unroll

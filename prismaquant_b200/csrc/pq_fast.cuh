@@ -301,10 +301,13 @@ __device__ __forceinline__ float rcp_approx(float x) {
 
 constexpr float RCP6 = 0.16666667163372039794921875f;   // RN(1/6)
 constexpr float RCP448 = 0x1.24924ap-9f;                // RN(1/448)
+constexpr float RCP3 = 0x1.555556p-2f;                  // RN(1/3)
+constexpr float RCP7 = 0x1.24924ap-3f;                  // RN(1/7)
 
-// RN(a / d) for a normal bf16 value a and d in {6, 448}, with rd = RN(1/d):
+// RN(a / d) for a normal bf16 value a and d in {3, 6, 7, 448}, with rd = RN(1/d):
 // product plus one remainder correction (Markstein); checked exhaustively
-// against IEEE division over all normal bf16 inputs and the floors 1e-8 and 1e-12.
+// against IEEE division over all normal bf16 inputs and the floors 1e-8 and 1e-12
+// (tests/test_fast_rules.py).
 __device__ __forceinline__ float div_const(float a, float d, float rd) {
   const float q = __fmul_rn(a, rd);
   const float r = __fmaf_rn(-q, d, a);

@@ -262,3 +262,29 @@ def test_mx_group_exponent_closed_form_matches_the_torch_rule():
         want = O.e8m0().round_log2(s)
         got = np.where(b < ceil_1em8, FLOOR, (b >> 7).astype(np.int64) - 127 + C + ((b & 0x7F) >= T))
         assert np.array_equal(got, want), kind
+
+
+def _rn32(x):
+    """Round a Fraction to the nearest float32, ties to even (exactly)."""
+    from fractions import Fraction as Fr
+    if x == 0:
+        return F32(0)
+    f = F32(float(x))
+    cands = [np.nextafter(f, F32(-np.inf)), f, np.nextafter(f, F32(np.inf))]
+    return min(cands, key=lambda c: (abs(Fr(float(c)) - x), int(np.array([c], F32).view(np.uint32)[0]) & 1))
+
+
+def test_div_const_is_ieee_division_for_every_bf16_value():
+    """div_const (q = RN(a rd), r = fma(-q, d, a), RN(q + r rd) with rd = RN(1/d)) equals IEEE
+    division for every normal bf16 a and the 1e-8 / 1e-12 floors, for the divisors the kernels
+    use it with: 6 (NVFP4 group scale), 448 (FP8 row scale), 3 and 7 (INT3 / INT4 group scales)."""
+    from fractions import Fraction as Fr
+    b = np.arange(0x0080, 0x7F80, dtype=np.uint32)
+    vals = list((b << 16).view(F32)) + [F32(1e-8), F32(1e-12)]
+    for d in (3, 6, 7, 448):
+        rd = _rn32(Fr(1, d))
+        for a in vals:
+            q = F32(a) * rd
+            r = _rn32(Fr(float(a)) - Fr(float(q)) * d)
+            got = _rn32(Fr(float(r)) * Fr(float(rd)) + Fr(float(q)))
+            assert got == _rn32(Fr(float(a)) / d), (d, a)
