@@ -914,9 +914,12 @@ def main():
             sweep_ms.append((e0, e1))
         else:
             plan.launch_sweep()
-        if plan.export:
-            plan.launch_scales()
-        return gather()
+        if not plan.export:
+            return gather()
+        side = plan.launch_scales_side()   # the scale pass overlaps the cost-table gather
+        out = gather()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        return out
 
     for _ in range(a.warmup):
         step(False)

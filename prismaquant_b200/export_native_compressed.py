@@ -388,14 +388,37 @@ class SweepExportPlan:
             _lib._check(lib.pq_nvfp4_scales(n, A, G, ctypes.c_void_p(tptr), Q, None, S, ctypes.c_void_p(gptr),
                                             stream), "pq_nvfp4_scales")
 
-    def run(self):
+    def launch_scales_side(self):
+        """The NVFP4 scale pass on the plan's side stream, after what the current stream has
+        enqueued (the sweep); returns that stream, which the current stream must wait on before
+        the scales and globals are read.  Work enqueued on the current stream meanwhile (the
+        cost-table all-gather) overlaps the scale pass."""
+        cur = torch.cuda.current_stream(self.device)
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._side.wait_stream(cur)
+        with torch.cuda.stream(self._side):
+            self.launch_scales()
+        return self._side
+
+    def run(self, then=None):
+        """Sweep, then the NVFP4 scale pass.  With `then` (a callable, e.g. the all-gather of the
+        cost table) the scale pass runs on a side stream while `then()` is enqueued on the current
+        one, which waits for the scale pass before returning; returns `then()`'s result, else the
+        per-tensor sums."""
         self.sse.zero_()
         if self.export:
             self.tmax.zero_()
         self.launch_sweep()
-        if self.export:
-            self.launch_scales()
-        return self.sse
+        if then is None:
+            if self.export:
+                self.launch_scales()
+            return self.sse
+        side = self.launch_scales_side() if self.export else None
+        out = then()
+        if side is not None:
+            torch.cuda.current_stream(self.device).wait_stream(side)
+        return out
 
     def costs(self) -> dict:
         host = self.sse.cpu().tolist()

@@ -208,6 +208,25 @@ def test_streaming_sweep_export_equals_resident():
             assert torch.equal(hg, g.cpu())
 
 
+def test_plan_run_with_overlapped_collective_equals_run():
+    """SweepExportPlan.run(then=...): the scale pass on a side stream while `then` is enqueued on
+    the current one gives run()'s packed bytes, globals and sums, and returns `then`'s result."""
+    shapes = {"model.layers.0.self_attn.q_proj": (256, 512), "model.layers.0.self_attn.k_proj": (64, 512),
+              "model.layers.0.self_attn.v_proj": (64, 512), "model.layers.0.mlp.down_proj": (512, 384)}
+    ws = {n: to_cuda_bf16(O.synthetic_weight_bits(s, seed=90 + i, outlier_frac=0.01)) for i, (n, s) in enumerate(shapes.items())}
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3", "BF16")]
+    plan = enc.SweepExportPlan(ws, specs)
+    plan.run()
+    want = [(c.clone(), s.view(torch.uint8).clone(), g.clone()) for c, s, g in plan.outputs]
+    want_sse = plan.sse.clone()
+    for _ in range(2):
+        got = plan.run(then=lambda: plan.sse.clone())
+        torch.cuda.synchronize()
+        assert torch.equal(got, want_sse) and torch.equal(plan.sse, want_sse)
+        for (c, s, g), (wc, ws_, wg) in zip(plan.outputs, want):
+            assert torch.equal(c, wc) and torch.equal(s.view(torch.uint8), ws_) and torch.equal(g, wg)
+
+
 def test_streaming_export_to_safetensors():
     """export_to streams every chunk's NVFP4 entries into IncrementalSafetensorsWriter shards while
     later chunks are on the GPU; the checkpoint on disk holds the resident path's bytes under the
