@@ -743,11 +743,13 @@ def make_pool():
 
 # ---------------------------------------------------------------------------
 
-def result_digest(plan, mine, table, n_units, world, strong, dev):
+def result_digest(plan, mine, first, table, n_units, world, strong, dev):
     """A checksum of the run's outputs, outside the timed region: per unit an integer checksum of
-    its NVFP4 codes, block scales and global (64-bit word sums, exact and order-free), gathered in
-    unit order and hashed; and the cost table's weight MSE averaged over all weights per format.
-    The codes digest is the same at every N of a strong-scaling run (the same model)."""
+    its NVFP4 codes, block scales and global (64-bit word sums, exact and order-free, so the row
+    blocks of a unit cut into pieces add up to the whole unit's; the global counted by the first
+    block only), gathered in unit order and hashed; and the cost table's weight MSE averaged over
+    all weights per format.  The codes digest is the same at every N of a strong-scaling run (the
+    same model).  mine / first: each plan entry's unit and whether it starts at row 0."""
     import hashlib
 
     import torch
@@ -762,7 +764,7 @@ def result_digest(plan, mine, table, n_units, world, strong, dev):
                 if pad:
                     b = torch.cat([b, torch.zeros(pad, dtype=torch.uint8, device=dev)])
                 v = b.view(torch.int64)
-                cs[j, k] = v.sum() + (v * 0x9E3779B97F4A7C1).sum()
+                cs[j, k] = v.sum() + (v * 0x9E3779B97F4A7C1).sum() if (k < 2 or first[j]) else 0
     numel = float(sum(plan.numel))
     if world > 1:
         caps = torch.tensor([n_local], device=dev)
@@ -782,10 +784,15 @@ def result_digest(plan, mine, table, n_units, world, strong, dev):
         numel = float(total.item())
     else:
         rows = list(zip(mine, cs[:n_local].cpu().tolist()))
-    h = hashlib.sha256()
+    agg: dict[int, list[int]] = {}   # a unit's pieces add up (64-bit wrap-around, as the sums on the device)
     for uid, vals in rows:
-        h.update(int(uid).to_bytes(8, "little", signed=True))
-        for v in vals:
+        acc = agg.setdefault(int(uid), [0, 0, 0])
+        for k, v in enumerate(vals):
+            acc[k] = ((acc[k] + int(v) + (1 << 63)) % (1 << 64)) - (1 << 63)
+    h = hashlib.sha256()
+    for uid in sorted(agg):
+        h.update(uid.to_bytes(8, "little", signed=True))
+        for v in agg[uid]:
             h.update(int(v).to_bytes(8, "little", signed=True))
     sse = table.double().sum(dim=0).cpu().tolist()
     return {"nvfp4_export_sha256_16": h.hexdigest()[:16] if plan.export else None,
@@ -879,15 +886,38 @@ def main():
     specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3", "BF16")]
     strong = world > 1 and a.scaling in ("auto", "strong")
     n_units = len(shapes)
-    if strong:   # one model: this rank's units only, the same per-name seeds at every N
-        sizes = [int(__import__("math").prod(sh)) for _, sh in shapes]
-        owner = D.partition_units(sizes, world, [enc.sibling_group_key(n) for n, _ in shapes])
-        mine = [i for i in range(n_units) if owner[i] == rank]
+    split_slots = split_ids = None
+    n_split = 0
+    if strong:   # one model: this rank's pieces only, the same per-name seeds at every N
+        pieces, owner = D.plan_pieces(shapes, world, [enc.sibling_group_key(n) for n, _ in shapes])
+        mine_p = [i for i in range(len(pieces)) if owner[i] == rank]
         cap = D.max_units_per_rank(owner, world)
-        weights = S.cuda_weights([shapes[i] for i in mine], dev, base_seed=0)
-        my_params = sum(sizes[i] for i in mine)
+        n_pieces = [0] * n_units
+        for u, _, _ in pieces:
+            n_pieces[u] += 1
+        split_of = {}
+        for u in range(n_units):
+            if n_pieces[u] > 1:
+                split_of[u] = len(split_of)
+        n_split = len(split_of)
+        weights, mine, first, slots, sids = {}, [], [], [], []
+        for j, i in enumerate(mine_p):   # a row block of a unit cut into pieces: generate the unit, keep the rows
+            u, r0, r1 = pieces[i]
+            name, sh = shapes[u]
+            w = S.cuda_weights([(name, sh)], dev, base_seed=0)[name]
+            whole = r0 == 0 and r1 == sh[0]
+            weights[name if whole else f"{name}[{r0}:{r1}]"] = w if whole else w[r0:r1].contiguous()
+            mine.append(u)
+            first.append(r0 == 0)
+            if u in split_of:
+                slots.append(j)
+                sids.append(split_of[u])
+        split_slots = torch.tensor(slots, dtype=torch.int64, device=dev)
+        split_ids = torch.tensor(sids, dtype=torch.int64, device=dev)
+        my_params = sum(w.numel() for w in weights.values())
     else:
         mine = list(range(n_units))
+        first = [True] * n_units
         weights = S.cuda_weights(shapes, dev, base_seed=1_000_003 * rank)
         my_params = params
     plan = enc.SweepExportPlan(weights, specs, export_nvfp4=a.workload != "moe30b")
@@ -916,6 +946,8 @@ def main():
             plan.launch_sweep()
         if not plan.export:
             return gather()
+        if n_split:   # units cut into row blocks: their NVFP4 maximum over all ranks first
+            D.reduce_split_tmax(plan.tmax, split_slots, split_ids, n_split)
         side = plan.launch_scales_side()   # the scale pass overlaps the cost-table gather
         out = gather()
         torch.cuda.current_stream(dev).wait_stream(side)
@@ -945,7 +977,7 @@ def main():
     bytes_w = 2.0 * params                       # one model
     job_bytes = bytes_w if strong else world * bytes_w
     value = job_bytes * a.steps / (ms_max / 1e3) / 1e9
-    digest = result_digest(plan, mine, gather(), n_units, world, strong, dev)
+    digest = result_digest(plan, mine, first, gather(), n_units, world, strong, dev)
 
     # dominant kernel roofline: fused sweep + NVFP4 codes; reads 2 B/param, writes 0.5 B/param of codes
     alg_bytes = my_params * (2.0 + (0.5 if plan.export else 0.0))

@@ -6,8 +6,12 @@ into per-shard pickles merged on disk (incremental_measure_quant_cost.py:73-99,
   * `partition_units` assigns whole units (Linears, expert tensors; fused
     siblings as one unit so their joint NVFP4 global needs no communication)
     to ranks, greedy by bytes (largest first onto the least-loaded rank);
+  * `plan_pieces` does the same after cutting a 2-D unit larger than a rank's
+    share (total / world) outside any sibling group (lm_head at large N) into
+    row blocks; the blocks' NVFP4 maxima meet in ONE all_reduce(MAX)
+    (`reduce_split_tmax`) before the scale pass;
   * `all_gather_costs` assembles the cost table with ONE all_gather of
-    fixed-size float64 records (sse per format + element count) per unit;
+    fixed-size float64 records (sse per format) per piece, summed by unit;
   * `all_reduce_traces` sums the per-Linear Fisher (raw trace, tokens) buffer
     across data-parallel ranks with ONE all_reduce.
 Nothing else crosses GPUs: weights and packed outputs stay on their rank.
@@ -15,6 +19,7 @@ Nothing else crosses GPUs: weights and packed outputs stay on their rank.
 from __future__ import annotations
 
 import heapq
+import math
 
 import torch
 import torch.distributed as dist
@@ -38,6 +43,44 @@ def partition_units(sizes: list[int], world: int, group_keys: list[str | None] |
     return rank
 
 
+def plan_pieces(shapes, world: int, group_keys: list[str | None] | None = None):
+    """Pieces of a model for `world` ranks and the rank of each: ([(unit, r0, r1)], [rank]).
+    A unit is one piece, rows [0, rows), except a 2-D unit outside any sibling group whose size
+    exceeds the per-rank share (total / world): it is cut into ceil(size / share) row blocks of
+    near-equal height.  Pieces go to ranks as partition_units assigns units (siblings together,
+    greedy by bytes).  shapes: [(name, shape)]."""
+    keys = group_keys or [None] * len(shapes)
+    sizes = [int(math.prod(sh)) for _, sh in shapes]
+    share = sum(sizes) / max(world, 1)
+    pieces, psizes, pkeys = [], [], []
+    for u, ((_, sh), size, key) in enumerate(zip(shapes, sizes, keys)):
+        rows = sh[0] if len(sh) == 2 else None
+        k = math.ceil(size / share) if (world > 1 and key is None and rows and size > share) else 1
+        k = min(k, rows or 1)
+        for b in range(k):
+            r0 = (rows or 0) * b // k if rows else 0
+            r1 = (rows or 0) * (b + 1) // k if rows else (sh[0] if sh else 0)
+            pieces.append((u, r0, r1))
+            psizes.append(size * (r1 - r0) // max(sh[0], 1) if sh else size)
+            pkeys.append(key)
+    return pieces, partition_units(psizes, world, pkeys)
+
+
+def reduce_split_tmax(tmax: torch.Tensor, slots: torch.Tensor, split_ids: torch.Tensor, n_split: int,
+                      group=None) -> None:
+    """The NVFP4 maxima of units cut into pieces, across ranks: `tmax` holds this rank's per-piece
+    maxima (int32 bit patterns of non-negative floats, which order as the floats do), `slots` the
+    positions of its pieces of split units and `split_ids` their split-unit numbers.  After ONE
+    all_reduce(MAX) every piece of a split unit holds the unit's maximum (collective: every rank
+    calls it, with empty slots if it holds no such piece)."""
+    buf = torch.zeros(max(n_split, 1), dtype=torch.int32, device=tmax.device)
+    if slots.numel():
+        buf.scatter_reduce_(0, split_ids, tmax.index_select(0, slots), reduce="amax")
+    dist.all_reduce(buf, op=dist.ReduceOp.MAX, group=group)
+    if slots.numel():
+        tmax.index_copy_(0, slots, buf.index_select(0, split_ids))
+
+
 def max_units_per_rank(ranks: list[int], world: int) -> int:
     return max([ranks.count(r) for r in range(world)] + [0])
 
@@ -46,9 +89,10 @@ def all_gather_costs(local_ids: torch.Tensor, local_sse: torch.Tensor, n_units: 
                      group=None) -> torch.Tensor:
     """Gather [n_local, 4] sse records from every rank into a [n_units, 4] table.
 
-    Every rank pads its records to `cap` (the largest per-rank unit count,
+    Every rank pads its records to `cap` (the largest per-rank record count,
     known to all ranks from the partition) and tags each with its unit id,
-    so the table is assembled by index after ONE all_gather."""
+    so the table is assembled by index after ONE all_gather; records of the
+    pieces of one unit add up."""
     world = dist.get_world_size(group)
     dev = local_sse.device
     rec = torch.full((cap, 5), -1.0, dtype=torch.float64, device=dev)
@@ -60,7 +104,7 @@ def all_gather_costs(local_ids: torch.Tensor, local_sse: torch.Tensor, n_units: 
     ids = out[:, 0].long()
     ids = torch.where(ids >= 0, ids, torch.full_like(ids, n_units))
     table = torch.zeros(n_units + 1, 4, dtype=torch.float64, device=dev)
-    table.index_copy_(0, ids, out[:, 1:])
+    table.index_add_(0, ids, out[:, 1:])
     return table[:n_units]
 
 

@@ -401,15 +401,18 @@ class SweepExportPlan:
             self.launch_scales()
         return self._side
 
-    def run(self, then=None):
+    def run(self, then=None, between=None):
         """Sweep, then the NVFP4 scale pass.  With `then` (a callable, e.g. the all-gather of the
         cost table) the scale pass runs on a side stream while `then()` is enqueued on the current
         one, which waits for the scale pass before returning; returns `then()`'s result, else the
-        per-tensor sums."""
+        per-tensor sums.  `between` runs after the sweep and before the scale pass (e.g.
+        distributed.reduce_split_tmax for tensors cut into row blocks across ranks)."""
         self.sse.zero_()
         if self.export:
             self.tmax.zero_()
         self.launch_sweep()
+        if between is not None:
+            between()
         if then is None:
             if self.export:
                 self.launch_scales()

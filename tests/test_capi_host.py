@@ -496,3 +496,78 @@ def test_installed_cost_entry_keeps_reference_path_off_cuda():
     assert w(None, None, set(), [Spec("NVFP4"), Spec("MXFP8")], "cuda", None, chunk_size=8) == "b200"
     assert calls[-1] == ("ours", "cuda", 8, ["NVFP4", "MXFP8"])
     assert w(None, None, set(), [Spec("MY_CUSTOM_FORMAT")], "cuda:0", None) == "ref"
+
+
+def test_plan_pieces_cuts_units_larger_than_a_share():
+    """plan_pieces: every unit's rows covered once, in order; only 2-D units outside sibling groups
+    and larger than total / world are cut, into ceil(size / share) near-equal row blocks; siblings
+    stay together; one rank keeps everything whole."""
+    from prismaquant_b200 import distributed as D
+    from prismaquant_b200 import export_native_compressed as enc
+    shapes = [("lm_head", (128256, 4096)), ("model.layers.0.self_attn.q_proj", (4096, 4096)),
+              ("model.layers.0.self_attn.k_proj", (1024, 4096)), ("model.layers.0.self_attn.v_proj", (1024, 4096)),
+              ("model.layers.0.mlp.experts.gate_up_proj", (128, 1536, 2048))]
+    keys = [enc.sibling_group_key(n) for n, _ in shapes]
+    for world in (1, 2, 4, 8, 16):
+        pieces, ranks = D.plan_pieces(shapes, world, keys)
+        assert len(ranks) == len(pieces)
+        sizes = [int(np.prod(sh)) for _, sh in shapes]
+        share = sum(sizes) / world
+        for u, (name, sh) in enumerate(shapes):
+            mine = [(r0, r1) for uu, r0, r1 in pieces if uu == u]
+            assert mine[0][0] == 0 and mine[-1][1] == sh[0]
+            assert all(a[1] == b[0] for a, b in zip(mine, mine[1:]))
+            cut = world > 1 and keys[u] is None and len(sh) == 2 and sizes[u] > share
+            assert len(mine) == (int(np.ceil(sizes[u] / share)) if cut else 1), (world, name)
+        for k in {x for x in keys if x}:
+            assert len({r for (u, _, _), r in zip(pieces, ranks) if keys[u] == k}) == 1
+    assert D.plan_pieces(shapes, 1, keys)[0] == [(u, 0, sh[0]) for u, (_, sh) in enumerate(shapes)]
+
+
+def _gloo_split_worker(rank, world, port, q):
+    import os
+    import torch
+    import torch.distributed as dist
+    from prismaquant_b200 import distributed as D
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # unit 0 cut in two (one block per rank), unit 1 whole on rank 0, unit 2 cut in two with
+        # both blocks on rank 1
+        pieces = {0: [(0, 0), (2, 0), (1, None)], 1: [(0, 1), (2, 1), (2, 1)]}[rank]
+        ids = torch.tensor([u for u, _ in pieces])
+        sse = torch.stack([torch.full((4,), 1.0 + u + 10 * rank, dtype=torch.float64) for u, _ in pieces])
+        table = D.all_gather_costs(ids, sse, 3, 3)
+        tmax = torch.tensor([100 + 7 * rank + j for j in range(len(pieces))], dtype=torch.int32)
+        slots = torch.tensor([j for j, (_, s) in enumerate(pieces) if s is not None])
+        sids = torch.tensor([{0: 0, 2: 1}[u] for u, s in pieces if s is not None])
+        D.reduce_split_tmax(tmax, slots, sids, 2)
+        q.put((rank, table.tolist(), tmax.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_split_units():
+    """Row blocks of one unit on two ranks (or twice on one): the gathered sums add up per unit,
+    and reduce_split_tmax leaves every block of a split unit holding the unit's maximum."""
+    import multiprocessing as mp
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_split_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (t, m)) for r, t, m in (q.get(timeout=120) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = [[1.0 + 11.0] * 4, [2.0] * 4, [3.0 + 13.0 + 13.0] * 4]   # unit 2: one block on rank 0, two on rank 1
+    for r in (0, 1):
+        assert res[r][0] == want
+    # unit 0: max(100, 107) on both; unit 2: max(101, 108, 109) on both; unit 1 untouched
+    assert res[0][1] == [107, 109, 102]
+    assert res[1][1] == [107, 109, 109]
