@@ -166,9 +166,13 @@ __device__ __forceinline__ uint32_t e4m3_rne_pick(float a, float s, uint32_t lo,
 // clamp does).  Equal codes are the reference's code; where they differ (a
 // quotient within ~2^-20 of an E4M3 midpoint) mid_side decides the side exactly.
 __device__ __forceinline__ uint32_t nvfp4_scale_pair(uint32_t a2, float glob, uint64_t rlo2, uint64_t rhi2) {
-  const float sg0 = div_const(fmaxf(__uint_as_float(a2 << 16), 1e-12f), 6.0f, RCP6);
-  const float sg1 = div_const(fmaxf(__uint_as_float(a2 & 0xFFFF0000u), 1e-12f), 6.0f, RCP6);
-  const uint64_t sg2 = f2_pack(sg0, sg1);
+  // div_const on the pair in float32x2 arithmetic (the same three roundings per element)
+  const uint64_t a = f2_pack(fmaxf(__uint_as_float(a2 << 16), 1e-12f), fmaxf(__uint_as_float(a2 & 0xFFFF0000u), 1e-12f));
+  const uint64_t rd2 = f2_pack(RCP6, RCP6), nd2 = f2_pack(-6.0f, -6.0f);
+  const uint64_t q = f2_mul_rn(a, rd2);
+  const uint64_t sg2 = f2_fma_rn(f2_fma_rn(q, nd2, a), rd2, q);
+  float sg0, sg1;
+  f2_unpack(sg2, sg0, sg1);
   const uint32_t lo = cvt_e4m3x2(f2_mul_rz(sg2, rlo2));
   const uint32_t hi = cvt_e4m3x2(f2_mul_rz(sg2, rhi2));
   if (lo == hi) return lo;
