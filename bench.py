@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--scaling", default="auto", choices=["auto", "strong", "weak"],
                     help="N > 1: strong = one model sharded across the ranks by whole units (fused siblings "
                          "kept together), weak = one model instance per rank; auto = strong")
+    ap.add_argument("--pipeline-chunks", type=int, default=1,
+                    help="sweep launches per step, each chunk's NVFP4 scale pass overlapping the next chunk")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -920,7 +922,7 @@ def main():
         first = [True] * n_units
         weights = S.cuda_weights(shapes, dev, base_seed=1_000_003 * rank)
         my_params = params
-    plan = enc.SweepExportPlan(weights, specs, export_nvfp4=a.workload != "moe30b")
+    plan = enc.SweepExportPlan(weights, specs, export_nvfp4=a.workload != "moe30b", pipeline_chunks=a.pipeline_chunks)
     my_ids = torch.tensor(mine, dtype=torch.int64, device=dev)
 
     def gather():
@@ -936,21 +938,21 @@ def main():
         plan.sse.zero_()
         if plan.export:
             plan.tmax.zero_()
-        if timed:
+        if timed:   # the sweep's device time: its launches on this stream, between two events
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
+        if n_split:   # units cut into row blocks: the whole sweep, their NVFP4 maximum over all ranks, scales
             plan.launch_sweep()
+            D.reduce_split_tmax(plan.tmax, split_slots, split_ids, n_split)
+            side = plan.launch_scales_side()
+        else:   # each chunk's scale pass on a side stream while the next chunk is swept
+            side = plan.launch_pipelined()
+        if timed:
             e1.record()
             sweep_ms.append((e0, e1))
-        else:
-            plan.launch_sweep()
-        if not plan.export:
-            return gather()
-        if n_split:   # units cut into row blocks: their NVFP4 maximum over all ranks first
-            D.reduce_split_tmax(plan.tmax, split_slots, split_ids, n_split)
-        side = plan.launch_scales_side()   # the scale pass overlaps the cost-table gather
-        out = gather()
-        torch.cuda.current_stream(dev).wait_stream(side)
+        out = gather()   # overlaps the last chunk's scale pass
+        if side is not None:
+            torch.cuda.current_stream(dev).wait_stream(side)
         return out
 
     for _ in range(a.warmup):
@@ -1049,7 +1051,7 @@ def main():
                          "kernel": "sweep_fast_kernel (fused sweep + NVFP4 codes)",
                          "kernel_ms": round(kern_ms, 4), "algorithmic_bytes_per_launch": alg_bytes},
             "clocks": clk.summary(),
-            "gpu_launches": a.steps * (2 if plan.export else 1),
+            "gpu_launches": a.steps * (len(plan.chunks) * (2 if plan.export else 1)),   # sweep + scale per chunk
             "e2e": e2e,
             "cpu_baseline": cpu,
         }

@@ -571,3 +571,27 @@ def test_gloo_two_ranks_split_units():
     # unit 0: max(100, 107) on both; unit 2: max(101, 108, 109) on both; unit 1 untouched
     assert res[0][1] == [107, 109, 102]
     assert res[1][1] == [107, 109, 109]
+
+
+def test_plan_chunks_keep_sibling_groups_whole():
+    """SweepExportPlan's chunks: cover the tensors in order, at most 256 each, about equal bytes,
+    and never put a cut between two members of one fused-sibling group, even when the members
+    are not adjacent in the list."""
+    from prismaquant_b200 import export_native_compressed as enc
+    names = []
+    for l in range(40):
+        names += [f"model.layers.{l}.self_attn.{p}_proj" for p in ("q", "o", "k", "v")]   # o between siblings
+        names += [f"model.layers.{l}.mlp.{p}_proj" for p in ("gate", "down", "up")]
+    sizes = [4096 * 4096 if n.endswith(("q_proj", "o_proj")) else 1024 * 4096 if n.endswith(("k_proj", "v_proj"))
+             else 14336 * 4096 for n in names]
+    keys = [enc.sibling_group_key(n) for n in names]
+    for target in (1, 2, 4, 7):
+        chunks = enc._plan_chunks(sizes, keys, target)
+        assert chunks[0][0] == 0 and chunks[-1][1] == len(names)
+        assert all(a[1] == b[0] for a, b in zip(chunks, chunks[1:]))
+        assert all(b - a <= 256 for a, b in chunks)
+        where = {i: c for c, (a, b) in enumerate(chunks) for i in range(a, b)}
+        for k in {x for x in keys if x}:
+            assert len({where[i] for i, kk in enumerate(keys) if kk == k}) == 1, (target, k)
+        if target > 1 and len(names) <= 256 * target:
+            assert len(chunks) >= min(target, 2)

@@ -287,3 +287,26 @@ def test_global_real_kernel_batched_and_joint(full_digests, monkeypatch):
         joint = max(float(enc.compute_nvfp4_global_real(ws[n])) for n in group)
         for n in group:
             assert joint == dg[n]["joint_global_real"], n
+
+
+def test_pipelined_plan_equals_one_chunk():
+    """A plan swept and scaled in several chunks (scale passes on a side stream) gives the packed
+    bytes, globals (fused-sibling joint ones included) and sums of a one-chunk plan."""
+    shapes = {}
+    for l in range(3):
+        for p, sh in (("self_attn.q_proj", (256, 512)), ("self_attn.k_proj", (64, 512)), ("self_attn.v_proj", (64, 512)),
+                      ("self_attn.o_proj", (512, 256)), ("mlp.gate_proj", (384, 512)), ("mlp.up_proj", (384, 512)),
+                      ("mlp.down_proj", (512, 384))):
+            shapes[f"model.layers.{l}.{p}"] = sh
+    ws = {n: to_cuda_bf16(O.synthetic_weight_bits(s, seed=70 + i, outlier_frac=0.01)) for i, (n, s) in enumerate(shapes.items())}
+    specs = [fr.get_format(f) for f in ("NVFP4", "MXFP8", "FP8_E4M3", "BF16")]
+    one = enc.SweepExportPlan(ws, specs, pipeline_chunks=1)
+    many = enc.SweepExportPlan(ws, specs, pipeline_chunks=4)
+    assert len(one.chunks) == 1 and len(many.chunks) > 2
+    one.run()
+    for _ in range(2):
+        many.run()
+        torch.cuda.synchronize()
+        assert torch.allclose(many.sse, one.sse, rtol=1e-12, atol=0.0)   # fp64 atomics: order may differ
+        for (c, s, g), (c1, s1, g1) in zip(many.outputs, one.outputs):
+            assert torch.equal(c, c1) and torch.equal(s.view(torch.uint8), s1.view(torch.uint8)) and torch.equal(g, g1)
