@@ -378,6 +378,8 @@ def run_kernels(a, local):
         ("cost_qdq NVFP4 (W_hat)", lambda: _lib.cost_qdq(W, "NVFP4"), 4 * n, "GB/s"),
         ("cost_qdq MXFP8 (W_hat)", lambda: _lib.cost_qdq(W, "MXFP8"), 4 * n, "GB/s"),
         ("cost_qdq FP8_E4M3 (W_hat)", lambda: _lib.cost_qdq(W, "FP8_E4M3"), 4 * n, "GB/s"),
+        ("xfmt2_kernel cost_qdq MXFP4 (W_hat)", lambda: _lib.cost_qdq(W, "MXFP4"), 4 * n, "GB/s"),
+        ("xfmt2_kernel cost_qdq MXFP6_E3M2 (W_hat)", lambda: _lib.cost_qdq(W, "MXFP6_E3M2"), 4 * n, "GB/s"),
     ]
     for f in ("MXFP4", "MXFP6_E3M2", "FP8_E5M2", "NVFP3", "INT3", "INT4_W4A16_g128"):
         kname = "mxsse_kernel" if f.startswith("MX") else "intsse_kernel" if f.startswith("INT") else "xfmt2_kernel"

@@ -341,6 +341,45 @@ __device__ __forceinline__ float mx_sse8(const uint4& u, int es) {
   return acc;
 }
 
+// W_hat of 8 elements of an MX group (one 16-byte word of bf16 pairs) with scale 2^es, |es| <= 90,
+// no NaN among them, as four bf16 pairs: the grid points of mx_rec8 with the reference's tie rule
+// (ties to the lower signed value, +0 for a negative w that rounds to zero), two per step:
+//  - |w| >= 2^(EMIN+es): the magnitude rounded to M mantissa bits on the bit pattern with the
+//    sign-dependent tie increment of mx_rec8, saturated at MAXV 2^es by a packed unsigned min,
+//    the sign put back;
+//  - |w| <= 2^(EMIN+es): w - eps rounded to a multiple of step = 2^(EMIN+es-MS) by adding and
+//    subtracting c = 1.5 x 2^(step+23) in float32 pairs, eps = step x 2^-11.  Where w can reach
+//    a half-step, w and eps are multiples of step x 2^-11 below 8 step, so w - eps is exact; a
+//    bf16 w that is not a tie lies at least step x 2^-8 from the half-step, so it stays on its
+//    side, and a tie moves to the lower neighbour; a zero result is c - c = +0.  |es| <= 90
+//    keeps c and eps normal float32 numbers;
+//  - the range mask is mx_sse8's packed subtraction (both sides agree at |w| = 2^(EMIN+es)).
+template <int KIND>
+__device__ __forceinline__ void mx_qdq8(const uint4& u, int es, uint32_t (&o)[4]) {
+  using K = XK<KIND>;
+  constexpr int MS = K::SUB ? K::M : 0;
+  constexpr uint32_t DROP = 7 - K::M;
+  constexpr uint32_t HALF = ((1u << (DROP - 1)) - 1u) * 0x00010001u;
+  constexpr uint32_t MASK = ((0xFFFFu >> DROP) << DROP) * 0x00010001u;
+  const uint32_t sat2 = ((__float_as_uint(K::MAXV) >> 16) + ((uint32_t)es << 7)) * 0x00010001u;
+  const uint32_t thr2 = (0x8000u + ((uint32_t)(K::EMIN + es + 127) << 7)) * 0x00010001u;
+  const int sexp = K::EMIN + es - MS;
+  const float c = __uint_as_float(((uint32_t)(sexp + 23 + 127) << 23) | 0x400000u);
+  const float eps = __uint_as_float((uint32_t)(sexp - 11 + 127) << 23);
+  const uint64_t c2 = f2_pack(c, c), nc2 = f2_pack(-c, -c), neps2 = f2_pack(-eps, -eps);
+  const uint32_t words[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t v = words[p];
+    const uint32_t neg = (v >> 15) & 0x00010001u;
+    const uint32_t qn = __vminu2(((v & 0x7FFF7FFFu) + HALF + neg) & MASK, sat2) | (v & 0x80008000u);
+    const uint64_t t = f2_add_rn(f2_add_rn(f2_add_rn(f2_from_bf16x2(v), neps2), c2), nc2);
+    const uint32_t qs = f2_to_bf16x2(t);
+    const uint32_t m = prmt_sign_halves(thr2 - (v & 0x7FFF7FFFu));   // 0xFFFF where |w| <= 2^(EMIN+es)
+    o[p] = (qs & m) | (qn & ~m);
+  }
+}
+
 // NaN among 8 bf16 values: a magnitude above 0x7F80 in some half
 __device__ __forceinline__ bool has_nan8(const uint4& u) {
   const uint32_t t = (((u.x & 0x7FFF7FFFu) + 0x007F007Fu) | ((u.y & 0x7FFF7FFFu) + 0x007F007Fu) |
@@ -429,9 +468,14 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
       if (valid) {
         // an MX group in range with no NaN among the lane's 8 takes the integer reconstruction
         if (MXK && f.mx && scale >= 0x1p-100f && scale <= 0x1p100f && !has_nan8(u)) {
+          const int es = (int)(__float_as_uint(scale) >> 23) - 127;
           if (MODE == MODE_SSE && h_mode == 0)
-            acc += (double)mx_sse8<(KIND == XK_INT ? XK_E2M1 : KIND)>(u, (int)(__float_as_uint(scale) >> 23) - 127);
-          else
+            acc += (double)mx_sse8<(KIND == XK_INT ? XK_E2M1 : KIND)>(u, es);
+          else if (MODE == MODE_QDQ && es >= -90 && es <= 90) {
+            uint32_t o[4];
+            mx_qdq8<(KIND == XK_INT ? XK_E2M1 : KIND)>(u, es, o);
+            *reinterpret_cast<uint4*>(out + r * cols + col) = make_uint4(o[0], o[1], o[2], o[3]);
+          } else
             do8(u, wv, r * cols + col, r, scale, inv, std::true_type{});
         } else
           do8(u, wv, r * cols + col, r, scale, inv, std::false_type{});

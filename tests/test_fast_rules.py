@@ -288,3 +288,50 @@ def test_div_const_is_ieee_division_for_every_bf16_value():
             r = _rn32(Fr(float(a)) - Fr(float(q)) * d)
             got = _rn32(Fr(float(r)) * Fr(float(rd)) + Fr(float(q)))
             assert got == _rn32(Fr(float(a)) / d), (d, a)
+
+
+def _mx_qdq8_emulated(bits, es, M, EMIN, sub, maxv):
+    """mx_qdq8's output bf16 pattern for each bf16 pattern: the integer half as the kernel does it,
+    the float32 pair arithmetic (w - eps + c - c, round to nearest even) in numpy float32."""
+    MS = M if sub else 0
+    drop = 7 - M
+    b = bits.astype(np.int64)
+    mag = b & 0x7FFF
+    neg = (b >> 15) & 1
+    sat = (int(np.array([maxv], dtype=F32).view(np.uint32)[0]) >> 16) + (es << 7)
+    qn = np.minimum((mag + ((1 << (drop - 1)) - 1) + neg) & ((0xFFFF >> drop) << drop), sat) | (b & 0x8000)
+    sexp = EMIN + es - MS
+    c = np.array([((sexp + 23 + 127) << 23) | 0x400000], dtype=np.uint32).view(F32)[0]
+    eps = np.array([(sexp - 11 + 127) << 23], dtype=np.uint32).view(F32)[0]
+    w = (bits.astype(np.uint32) << 16).view(F32)
+    t = ((w + (-eps)) + c) + (-c)                 # numpy float32 arithmetic rounds to nearest even
+    tb = t.view(np.uint32)
+    qs = (tb >> 16).astype(np.int64)
+    d = 0x8000 + ((EMIN + es + 127) << 7) - mag
+    small = (d & 0x8000) != 0
+    assert ((tb[small] & 0xFFFF) == 0).all()      # every selected result is a bf16: the cvt is exact
+    return np.where(small, qs, qn)
+
+
+def test_mx_packed_w_hat_rounding_matches_the_codebook_rule():
+    """mx_qdq8 (the MX W_hat of the codebook kernel's grouped fast path) gives the reference's
+    bf16 pattern for every finite bf16 w, every MX kind, at scales 2^es across its range
+    (|es| <= 90): the nearest grid point with ties to the lower signed value, saturated at MAXV,
+    +0 for a negative w that rounds to zero."""
+    b = np.arange(1 << 16, dtype=np.uint32)
+    with np.errstate(invalid="ignore"):
+        f = (b << 16).view(F32)
+    bits = b[np.isfinite(f)].astype(np.uint16)
+    w = ((bits.astype(np.uint32) << 16).view(F32)).astype(np.float64)
+    for name, (M, EMIN, sub, maxv) in MX_KINDS.items():
+        grid = _mx_grid(M, EMIN, sub, maxv)
+        for es in (-90, -40, -7, -1, 0, 3, 20, 90):
+            got = _mx_qdq8_emulated(bits, es, M, EMIN, sub, maxv)
+            x = w / 2.0 ** es
+            near = np.abs(x) <= 1.5 * maxv            # beyond, float64 distances could tie falsely
+            ref = np.where(np.abs(x) >= maxv, np.sign(x) * maxv, _ties_lower(np.where(near, x, 0.0), grid))
+            ref = ref * 2.0 ** es + 0.0                # + 0.0: a negative w that rounds to zero gives +0
+            want = (ref.astype(F32).view(np.uint32) >> 16).astype(np.int64)
+            assert (ref.astype(F32).astype(np.float64) == ref).all()
+            ok = got == want
+            assert ok.all(), (name, es, bits[~ok][:5], got[~ok][:5], want[~ok][:5])

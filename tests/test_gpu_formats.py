@@ -260,3 +260,25 @@ def test_int_grouped_sse_matches_oracle(fmt, case):
     assert got.item() == pytest.approx(want, rel=1e-5, abs=1e-30), fmt
     # fp32 partials of 32 squares here, of 8 there: the sums agree to fp32 rounding
     assert got.item() == pytest.approx(ref.item(), rel=1e-6, abs=1e-30), fmt
+
+
+@pytest.mark.parametrize("fmt", MX_EXT)
+def test_mx_w_hat_across_the_group_exponent_range(fmt):
+    """W_hat of 32-element groups whose scales run from 2^-110 to 2^112 (the packed pair path
+    serves group exponents within +-90, the per-element path the rest), with ties to the lower
+    value planted in every group, the special rows (tiny, huge, an infinity) beside them:
+    bit-exact against the oracle."""
+    from prismaquant_b200 import _lib
+    rng = np.random.default_rng(11)
+    shifts = np.arange(-110, 114, 2)
+    f = rng.standard_normal((shifts.size, 32)).astype(np.float32)
+    f[:, :8] = np.array([0.25, -0.25, 0.75, -0.75, 1.25, -1.25, 3.5, -3.5], np.float32)   # grid midpoints
+    f[:, 8] = 6.0                                                   # the group's maximum
+    f = f * np.float32(2.0) ** shifts[:, None].astype(np.float32)
+    bits = np.concatenate([O.f32_to_bf16_bits(f).reshape(-1, 64)] +
+                          [_special_rows(k) for k in ("tiny", "huge", "inf")])
+    got = bits_of(_lib.cost_qdq(to_cuda_bf16(bits), fmt))
+    with np.errstate(all="ignore"):
+        want = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt))
+    bad = np.nonzero(got != want)
+    assert bad[0].size == 0, (fmt, got[bad][:5], want[bad][:5], bits[bad][:5])
