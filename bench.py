@@ -380,9 +380,11 @@ def run_kernels(a, local):
         ("cost_qdq FP8_E4M3 (W_hat)", lambda: _lib.cost_qdq(W, "FP8_E4M3"), 4 * n, "GB/s"),
         ("xfmt2_kernel cost_qdq MXFP4 (W_hat)", lambda: _lib.cost_qdq(W, "MXFP4"), 4 * n, "GB/s"),
         ("xfmt2_kernel cost_qdq MXFP6_E3M2 (W_hat)", lambda: _lib.cost_qdq(W, "MXFP6_E3M2"), 4 * n, "GB/s"),
+        ("xfmt2_kernel cost_qdq NVFP3 (W_hat)", lambda: _lib.cost_qdq(W, "NVFP3"), 4 * n, "GB/s"),
     ]
     for f in ("MXFP4", "MXFP6_E3M2", "FP8_E5M2", "NVFP3", "INT3", "INT4_W4A16_g128"):
-        kname = "mxsse_kernel" if f.startswith("MX") else "intsse_kernel" if f.startswith("INT") else "xfmt2_kernel"
+        kname = ("mxsse_kernel" if f.startswith("MX") else "intsse_kernel" if f.startswith("INT") else
+                 "fp3sse_kernel" if f == "NVFP3" else "xfmt2_kernel")
         table.append((f"{kname} format_sse {f}", (lambda f=f: _lib.format_sse(W, f, s0)), 2 * n, "GB/s"))
     mx4 = ["MXFP4", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E5M2"]
     s4 = torch.zeros(len(mx4), dtype=torch.float64, device=dev)

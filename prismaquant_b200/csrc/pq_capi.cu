@@ -220,6 +220,8 @@ int pq_format_sse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double
     return cuda_status(pq::launch_mxsse(w, rows, cols, &fmt, 1, &sse, num_sms_current(), (cudaStream_t)stream_));
   if (pq::intsse_ok(w, cols, fmt))
     return cuda_status(pq::launch_intsse(w, rows, cols, fmt, sse, num_sms_current(), (cudaStream_t)stream_));
+  if (pq::fp3sse_ok(w, cols, fmt))
+    return cuda_status(pq::launch_fp3sse(w, rows, cols, sse, num_sms_current(), (cudaStream_t)stream_));
   return cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse, nullptr, pq::MODE_SSE, num_sms_current(),
                                      (cudaStream_t)stream_));
 }
@@ -257,6 +259,8 @@ int pq_format_sse_multi(const uint16_t* w, int64_t rows, int64_t cols, const int
     }
     const int st = pq::intsse_ok(w, cols, fmt)
                        ? cuda_status(pq::launch_intsse(w, rows, cols, fmt, sse + f, sms, stream))
+                   : pq::fp3sse_ok(w, cols, fmt)
+                       ? cuda_status(pq::launch_fp3sse(w, rows, cols, sse + f, sms, stream))
                        : cuda_status(pq::launch_xfmt(w, rows, cols, fmt, sse + f, nullptr, pq::MODE_SSE, sms, stream));
     if (st != PQ_OK) return st;
   }

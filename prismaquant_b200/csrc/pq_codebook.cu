@@ -106,7 +106,7 @@ __device__ __forceinline__ float xfmt_rec(const XFmt& f, const float* cb, int nc
   float q;
   if (f.is_int) {
     const float lv = (float)((1 << (f.bits - 1)) - 1);
-    q = fminf(fmaxf(rintf(x), -lv - 1.0f), lv);
+    q = x != x ? x : fminf(fmaxf(rintf(x), -lv - 1.0f), lv);   // torch.clamp keeps a NaN
   } else {
     int lo = 0, hi = ncb;   // first entry >= x (torch.bucketize, right=False)
     while (lo < hi) {
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(256) xfmt_kernel(const uint16_t* __restrict__ 
   float part = 0.0f;
   int nsq = 0;
   auto emit = [&](int64_t idx, float wi, float r) {
-    if (MODE == MODE_QDQ) out[idx] = (uint16_t)(__float_as_uint(r) >> 16);
+    if (MODE == MODE_QDQ) out[idx] = (uint16_t)bf16_bits_torch(r);
     const float e = bf16_round(__fsub_rn(wi, r));
     const float e2 = __fmul_rn(e, e);   // the reference squares in fp32, then weights
     part = h_mode == 0 ? __fadd_rn(part, e2)
@@ -241,7 +241,7 @@ template <int KIND>
 __device__ __forceinline__ float xk_round(float x, int bits) {
   if constexpr (KIND == XK_INT) {
     const float lv = (float)((1 << (bits - 1)) - 1);
-    return fminf(fmaxf(rintf(x), -lv - 1.0f), lv);
+    return x != x ? x : fminf(fmaxf(rintf(x), -lv - 1.0f), lv);   // torch.clamp keeps a NaN
   } else {
     using K = XK<KIND>;
     const float a = fabsf(x);
@@ -380,6 +380,109 @@ __device__ __forceinline__ void mx_qdq8(const uint4& u, int es, uint32_t (&o)[4]
   }
 }
 
+// NVFP3 (the E2M0 codebook {0, 1/4, 1/2, 1, 2} with a real scale per 16 elements;
+// format_registry.py:264-272, 505-514) without division.  s = fl32(a / 2) with
+// a = max(amax, 1e-8) is a / 2 exactly, so the nearest codebook point of fl32(w / s) is decided by
+// comparing |w| with the midpoints times s: a/16, 3a/16, 3a/8 and 3a/4.  For a bf16 a
+// (amax >= 1e-8) the quotient 2w/a is either exactly such a midpoint or at least 2^-13 (relative)
+// away from it, so fl32 rounding never moves it across or onto one, and the exact comparisons are
+// the reference's.  On bf16 bit patterns, |w| > t is
+// bits(|w|) > bits(RD(t)), and |w| >= t is bits(|w|) + 1 > bits(t) when t is a bf16, else
+// bits(|w|) > bits(RD(t)); a/16 is always a bf16, the three 3a thresholds are together or not.
+// Ties go to the lower signed value: up in magnitude (>=) for a negative w, down (>) for a
+// positive one.  The level gives |W_hat| = 0, a/8, a/4, a/2 or a (bf16 values); the error
+// |w| - |W_hat| has the reference's square.  Used by fp3sse_kernel (squared error) and by
+// xfmt2_kernel (W_hat) for groups whose maximum is at least 1e-8 and below 2^126 (so that 3a
+// is finite).
+constexpr uint32_t BF16_1EM8_CEIL = 0x322Cu;   // the smallest bf16 magnitude >= 1e-8f
+constexpr uint32_t FP3_FAST_CEIL = 0x7E80u;    // group maxima below 2^126 keep 3a finite
+
+struct Fp3Group {
+  uint32_t k[4];   // 0x7FFF - bits(RD(threshold k)) per half: bit 15 of mag' + k[i] is mag' > RD
+  uint32_t ex;     // 0x00010001 where the 3a thresholds are bf16 values, else 0
+  uint32_t r[4];   // |W_hat| bits per half at levels 1..4: a/8, a/4, a/2, a
+};
+
+__device__ __forceinline__ Fp3Group fp3_group(uint32_t ab) {   // ab: bits of amax, 1e-8 <= amax < 2^126
+  const uint32_t t3 = __float_as_uint(__uint_as_float(ab << 16) * 3.0f);   // 3a, exact in float32
+  const uint32_t rd3 = t3 >> 16;
+  Fp3Group g;
+  g.k[0] = (0x7FFFu - (ab - 4u * 0x80u)) * 0x00010001u;
+  g.k[1] = (0x7FFFu - (rd3 - 4u * 0x80u)) * 0x00010001u;
+  g.k[2] = (0x7FFFu - (rd3 - 3u * 0x80u)) * 0x00010001u;
+  g.k[3] = (0x7FFFu - (rd3 - 2u * 0x80u)) * 0x00010001u;
+  g.ex = (t3 & 0xFFFFu) == 0u ? 0x00010001u : 0u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) g.r[j] = (ab - (uint32_t)(3 - j) * 0x80u) * 0x00010001u;
+  return g;
+}
+
+// W_hat bits of the two halves of a bf16 pair word: magnitudes, or with w's sign (+0 at level 0)
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t fp3_rec2(uint32_t v, const Fp3Group& g) {
+  const uint32_t mag = v & 0x7FFF7FFFu;
+  const uint32_t neg = (v >> 15) & 0x00010001u;
+  const uint32_t m0 = prmt_sign_halves(mag + neg + g.k[0]);
+  const uint32_t mge = mag + (neg & g.ex);
+  const uint32_t m1 = prmt_sign_halves(mge + g.k[1]);
+  const uint32_t m2 = prmt_sign_halves(mge + g.k[2]);
+  const uint32_t m3 = prmt_sign_halves(mge + g.k[3]);
+  uint32_t r = (g.r[1] & m1) | (g.r[0] & ~m1);
+  r = (g.r[2] & m2) | (r & ~m2);
+  r = (g.r[3] & m3) | (r & ~m3);
+  return SIGNED ? (r | (v & 0x80008000u)) & m0 : r & m0;
+}
+
+// FP8_E5M2 (format_registry.py:291-300, 466-473: one real scale per row, s = fl32(a / 114688),
+// a codebook with exponent 31 kept finite, so up to 1.75 x 2^16) without division, two elements
+// per step.  The quotient's half x/2 = w / (2s) is bracketed between RZ(w r_lo / 2) and
+// RZ(w r_hi / 2) with the widened reciprocal bounds of the fast sweep (pq_fast.cuh), and both are
+// converted by the hardware E5M2 conversion (round to nearest even, saturating at 57344).  Where
+// the two codes agree, no codebook midpoint lies strictly between the brackets, fl32(w / s) lies
+// strictly inside them, so the reference's nearest point (ties to the lower value) of fl32(w / s)
+// is that code times 2: above 2^-13 the hardware grid of x/2, doubled, is the reference's grid of
+// x (the 2^16 binade included), and saturation agrees.  A word with a pair whose codes differ (an
+// element within 2^-20 of a midpoint, exact ties among them), or with a nonzero |w| at or below
+// RU(s 2^-12) (x/2 in the hardware's subnormal range, where the grids part), or a NaN, is redone
+// by the exact rule.  W_hat = bf16(fl32((x/2 code) (2s))), the error bf16(w - W_hat); a w of zero
+// gives W_hat +0 as the reference's codebook zero does.
+struct E5m2Row {
+  uint64_t rlo2, rhi2, s2;   // r_lo / 2, r_hi / 2 and 2s, in both halves of a float32 pair
+  uint32_t tiny2;            // 0x8000 + bits(RU(s 2^-12)) per half
+};
+
+__device__ __forceinline__ E5m2Row e5m2_row(float s) {   // s: a positive normal scale
+  float rl, rh;
+  recip_bounds(s, rl, rh);
+  E5m2Row q;
+  q.rlo2 = f2_pack(0.5f * rl, 0.5f * rl);
+  q.rhi2 = f2_pack(0.5f * rh, 0.5f * rh);
+  q.s2 = f2_pack(2.0f * s, 2.0f * s);
+  q.tiny2 = (0x8000u + (__float_as_uint(s * 0x1p-12f) >> 16) + 1u) * 0x00010001u;
+  return q;
+}
+
+// 8 elements: W_hat words and the fp32 sum of the 8 exact squares; false if the word needs the
+// exact rule
+__device__ __forceinline__ bool e5m2_word(const uint4& u, const E5m2Row& q, uint32_t (&o)[4], float& part) {
+  const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+  uint32_t bad = 0u;
+  float acc = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint64_t w2 = f2_from_bf16x2(v[p]);
+    const uint32_t cl = cvt_e5m2x2(f2_mul_rz(w2, q.rlo2));
+    const uint32_t ch = cvt_e5m2x2(f2_mul_rz(w2, q.rhi2));
+    const uint32_t mag = v[p] & 0x7FFF7FFFu;
+    bad |= (cl ^ ch) | ((q.tiny2 - mag) & (mag + 0x7FFF7FFFu) & 0x80008000u);   // differ, or 0 < |w| <= RU
+    const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(__byte_perm(cl, 0u, 0x1404u)), q.s2));
+    o[p] = rec & (prmt_sign_halves(mag + 0x7FFF7FFFu) | 0x7FFF7FFFu);   // -0 -> +0 where w = +-0
+    acc = sq2_acc(bf16x2_sub(v[p], rec), acc);
+  }
+  part = acc;
+  return bad == 0u;
+}
+
 // NaN among 8 bf16 values: a magnitude above 0x7F80 in some half
 __device__ __forceinline__ bool has_nan8(const uint4& u) {
   const uint32_t t = (((u.x & 0x7FFF7FFFu) + 0x007F007Fu) | ((u.y & 0x7FFF7FFFu) + 0x007F007Fu) |
@@ -441,7 +544,7 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
       const float e2 = __fmul_rn(e, e);   // the reference squares in fp32, then weights
       part = h_mode == 0 ? __fadd_rn(part, e2) : fmaf(hv[i], e2, part);
       if (MODE == MODE_QDQ) {
-        const uint32_t b = __float_as_uint(rec) >> 16;
+        const uint32_t b = FAST ? __float_as_uint(rec) >> 16 : bf16_bits_torch(rec);   // NaN: 0 x inf
         o[i >> 1] = (i & 1) ? (o[i >> 1] | (b << 16)) : b;
       }
     }
@@ -477,6 +580,13 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
             *reinterpret_cast<uint4*>(out + r * cols + col) = make_uint4(o[0], o[1], o[2], o[3]);
           } else
             do8(u, wv, r * cols + col, r, scale, inv, std::true_type{});
+        } else if (KIND == XK_E2M0 && MODE == MODE_QDQ && (__float_as_uint(a) >> 16) >= BF16_1EM8_CEIL &&
+                   (__float_as_uint(a) >> 16) < FP3_FAST_CEIL && !has_nan8(u)) {
+          // NVFP3 with a group maximum in [1e-8, 2^126): the comparisons of fp3sse_kernel
+          const Fp3Group g3 = fp3_group(__float_as_uint(a) >> 16);
+          const uint4 o = make_uint4(fp3_rec2<true>(u.x, g3), fp3_rec2<true>(u.y, g3), fp3_rec2<true>(u.z, g3),
+                                     fp3_rec2<true>(u.w, g3));
+          *reinterpret_cast<uint4*>(out + r * cols + col) = o;
         } else
           do8(u, wv, r * cols + col, r, scale, inv, std::false_type{});
       }
@@ -494,6 +604,28 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
       a = __uint_as_float(warp_max_u(__float_as_uint(a)));
       float inv;
       const float scale = scale_of(a, inv);
+      if constexpr (KIND == XK_E5M2) {
+        // FP8_E5M2 by the bracket (e5m2_word) where the scale is a normal number, unweighted
+        if (!f.mx && h_mode == 0 && scale >= 0x1p-126f && scale <= 0x1p120f) {
+          const E5m2Row q = e5m2_row(scale);
+          for (int64_t col = lane * 8; col < cols; col += 256) {
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + col));
+            uint32_t o[4];
+            float part;
+            if (!has_nan8(u) && e5m2_word(u, q, o, part)) {
+              if (MODE == MODE_QDQ)
+                *reinterpret_cast<uint4*>(out + r * cols + col) = make_uint4(o[0], o[1], o[2], o[3]);
+              else
+                acc += (double)part;
+            } else {   // rare: a near-midpoint element, a tiny one or a NaN
+              float wv[8];
+              unpack8(u, wv);
+              do8(u, wv, r * cols + col, r, scale, inv, std::false_type{});
+            }
+          }
+          continue;
+        }
+      }
       for (int64_t col = lane * 8; col < cols; col += 256) {
         float wv[8];
         const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + col));
@@ -577,7 +709,6 @@ template <> struct MXE<XK_E3M2> { static constexpr int C = -5, T = 31, FLOOR = -
 template <> struct MXE<XK_E2M3> { static constexpr int C = -3, T = 42, FLOOR = -29; };
 template <> struct MXE<XK_E4M3> { static constexpr int C = -9, T = 31, FLOOR = -35; };
 template <> struct MXE<XK_E5M2> { static constexpr int C = -17, T = 31, FLOOR = -43; };
-constexpr uint32_t BF16_1EM8_CEIL = 0x322Cu;   // the smallest bf16 magnitude >= 1e-8f
 
 template <int KIND>
 __device__ __forceinline__ int mx_exp_closed(uint32_t ab) {   // ab: finite max |w| bits
@@ -743,7 +874,7 @@ __device__ __forceinline__ float int_err_sq(float w, float s, float r, bool exac
   const float mid = floorf(p) + 0.5f;
   float x = p;
   if (exact || fabsf(p - mid) <= fabsf(mid) * 0x1p-19f) x = __fdiv_rn(w, s);   // rare
-  const float q = fminf(fmaxf(rintf(x), (float)(-L - 1)), (float)L);
+  const float q = x != x ? x : fminf(fmaxf(rintf(x), (float)(-L - 1)), (float)L);   // torch.clamp keeps a NaN
   const float e = bf16_round(__fsub_rn(w, bf16_round(__fmul_rn(q, s))));
   return __fmul_rn(e, e);   // the reference squares in fp32
 }
@@ -854,6 +985,76 @@ cudaError_t launch_intsse(const uint16_t* w, int64_t rows, int64_t cols, int fmt
     case PQ_FMT_INT3: intsse_kernel<3, 2><<<(unsigned)blocks, 256, 0, stream>>>(w4, nwords, sse); break;
     default: intsse_kernel<7, 16><<<(unsigned)blocks, 256, 0, stream>>>(w4, nwords, sse); break;
   }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Squared error of NVFP3 from one read, flat over the tensor's groups like intsse_kernel, with the
+// comparisons of fp3_group / fp3_rec2.  Groups whose maximum is below 1e-8 (all zeros excepted,
+// which add nothing), at least 2^126 or not finite take the per-element rule.
+
+__device__ __forceinline__ float fp3_sse8(const uint4& u, const Fp3Group& g) {
+  const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+  float acc = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) acc = sq2_acc(bf16x2_sub(v[p] & 0x7FFF7FFFu, fp3_rec2<false>(v[p], g)), acc);
+  return acc;
+}
+
+// the per-element rule for 8 elements of a group with maximum bits ab (xfmt2_kernel's arithmetic)
+__device__ __forceinline__ float fp3_sse8_generic(const uint4& u, uint32_t ab) {
+  const float s = __fdiv_rn(fmaxf(__uint_as_float(ab << 16), 1e-8f), 2.0f);
+  float wv[8];
+  unpack8(u, wv);
+  float part = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float rec = bf16_round(__fmul_rn(xk_round<XK_E2M0>(__fdiv_rn(wv[i], s), 0), s));
+    const float e = bf16_round(__fsub_rn(wv[i], rec));
+    part = __fadd_rn(part, __fmul_rn(e, e));
+  }
+  return part;
+}
+
+__global__ void __launch_bounds__(256) fp3sse_kernel(const uint4* __restrict__ w, int64_t nwords, double* sse) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_first = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * (32 * MXSSE_UNROLL);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * MXSSE_UNROLL;
+  double acc = 0.0;
+  for (int64_t base = warp_first; base < nwords; base += stride) {   // warp-uniform
+    uint4 u[MXSSE_UNROLL];
+#pragma unroll
+    for (int k = 0; k < MXSSE_UNROLL; ++k) {
+      const int64_t j = base + 32 * k + lane;
+      u[k] = j < nwords ? __ldg(w + j) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float part = 0.0f;
+#pragma unroll
+    for (int k = 0; k < MXSSE_UNROLL; ++k) {
+      uint32_t ab = amax_bits8(u[k]);
+      ab = max(ab, (uint32_t)__shfl_xor_sync(FULL, ab, 1));   // the two lanes of a 16-element group
+      if (ab >= BF16_1EM8_CEIL && ab < FP3_FAST_CEIL)
+        part += fp3_sse8(u[k], fp3_group(ab));
+      else if (ab != 0u)   // rare: a maximum below 1e-8 or at least 2^126, an infinity or a NaN
+        part += fp3_sse8_generic(u[k], ab);
+    }
+    acc += (double)part;   // fp32 partials of 32 exact squares
+  }
+  const double v = warp_sum_d(acc);
+  if (lane == 0 && v != 0.0) atomicAdd(sse, v);
+}
+
+bool fp3sse_ok(const uint16_t* w, int64_t cols, int fmt) {
+  return fmt == PQ_FMT_NVFP3 && cols % 16 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+}
+
+cudaError_t launch_fp3sse(const uint16_t* w, int64_t rows, int64_t cols, double* sse, int num_sms,
+                          cudaStream_t stream) {
+  const int64_t nwords = rows * cols / 8;
+  int64_t blocks = (nwords + 256 * MXSSE_UNROLL - 1) / (256 * MXSSE_UNROLL);
+  if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
+  if (blocks < 1) blocks = 1;
+  fp3sse_kernel<<<(unsigned)blocks, 256, 0, stream>>>(reinterpret_cast<const uint4*>(w), nwords, sse);
   return cudaGetLastError();
 }
 

@@ -35,6 +35,9 @@ __device__ __forceinline__ uint32_t bf16_bits(float x) {
   return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// bf16 bits of a value that is already a bf16, NaN written as 0x7FC0 (torch's float -> bf16 NaN;
+// the hardware conversion writes 0x7FFF)
+__device__ __forceinline__ uint32_t bf16_bits_torch(float r) { return r != r ? 0x7FC0u : __float_as_uint(r) >> 16; }
 
 __device__ __forceinline__ void unpack8(const uint4& v, float (&w)[8]) {
   w[0] = bf16lo(v.x); w[1] = bf16hi(v.x);

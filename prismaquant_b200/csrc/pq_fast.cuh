@@ -84,6 +84,14 @@ __device__ __forceinline__ uint32_t cvt_e4m3x2(uint64_t x) {
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// FP8 E5M2 pair, round-to-nearest-even, saturating at 57344: low byte = lo.
+__device__ __forceinline__ uint32_t cvt_e5m2x2(uint64_t x) {
+  float lo, hi;
+  f2_unpack(x, lo, hi);
+  uint16_t r;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
 // Code pair -> float32 pair (exact: both formats embed in f16).
 __device__ __forceinline__ uint64_t e2m1x2_to_f2(uint32_t c) {
   uint32_t h;

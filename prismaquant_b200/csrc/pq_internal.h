@@ -49,6 +49,9 @@ size_t sweep_fast_smem_bytes();
 int64_t xfmt_group(int fmt, int64_t cols);
 bool mxsse_ok(const uint16_t* w, int64_t cols, int fmt);
 bool intsse_ok(const uint16_t* w, int64_t cols, int fmt);
+bool fp3sse_ok(const uint16_t* w, int64_t cols, int fmt);
+cudaError_t launch_fp3sse(const uint16_t* w, int64_t rows, int64_t cols, double* sse, int num_sms,
+                          cudaStream_t stream);
 cudaError_t launch_intsse(const uint16_t* w, int64_t rows, int64_t cols, int fmt, double* sse, int num_sms,
                           cudaStream_t stream);
 cudaError_t launch_mxsse(const uint16_t* w, int64_t rows, int64_t cols, const int* fmts, int nf,

@@ -335,3 +335,125 @@ def test_mx_packed_w_hat_rounding_matches_the_codebook_rule():
             assert (ref.astype(F32).astype(np.float64) == ref).all()
             ok = got == want
             assert ok.all(), (name, es, bits[~ok][:5], got[~ok][:5], want[~ok][:5])
+
+
+def _fp3_err_sq_kernel(wbits, abits):
+    """fp3_rec2 / fp3_sse8 of the codebook kernel, emulated on the bit patterns: the squared
+    bf16 error of each w in a group whose maximum has bits abits."""
+    from oracle import pq_oracle as O
+    ab = int(abits)
+    t3 = int(np.array([np.float32((np.uint32(ab) << 16).view(F32) * F32(3.0))], F32).view(np.uint32)[0])
+    rd3, ex = t3 >> 16, int((t3 & 0xFFFF) == 0)
+    thr = [ab - 4 * 0x80, rd3 - 4 * 0x80, rd3 - 3 * 0x80, rd3 - 2 * 0x80]
+    w = wbits.astype(np.int64)
+    mag, neg = w & 0x7FFF, (w >> 15) & 1
+    lvl = np.zeros(w.shape, np.int64)
+    for k, t in enumerate(thr):
+        mk = mag + (neg if k == 0 else neg * ex)
+        lvl += ((mk + 0x7FFF - t) >> 15) & 1
+    rec = np.where(lvl == 0, 0, ab - (4 - lvl) * 0x80)
+    f = lambda b: (b.astype(np.uint32) << 16).view(F32).astype(np.float64)
+    d = f(mag) - f(rec)
+    assert (d.astype(F32).astype(np.float64) == d).all()   # exact in float32: one rounding, to bf16
+    e = O.bf16_round(d.astype(F32))
+    w_hat = np.where(lvl == 0, 0, rec | (neg << 15))        # signed W_hat bits, +0 at level 0
+    return w_hat, (e.astype(F32) * e.astype(F32)).astype(F32)
+
+
+def _fp3_err_sq_reference(wbits, abits):
+    """format_registry.py:194-233 for NVFP3: s = fl32(a / 2), x = fl32(w / s), bucketize into the
+    signed E2M0 codebook, the upper neighbour only when strictly closer in float32,
+    W_hat = bf16(q s), error bf16(w - W_hat), squared in float32."""
+    from oracle import pq_oracle as O
+    cb = np.array([-2, -1, -0.5, -0.25, 0, 0.25, 0.5, 1, 2], F32)
+    a = (np.uint32(abits) << 16).view(F32)
+    s = F32(a) / F32(2.0)
+    w = (wbits.astype(np.uint32) << 16).view(F32)
+    x = (w / s).astype(F32)
+    i = np.searchsorted(cb, x, side="left")
+    lo, hi = cb[np.maximum(i - 1, 0)], cb[np.minimum(i, cb.size - 1)]
+    q = np.where(np.abs(hi - x) < np.abs(x - lo), hi, lo)
+    rec = O.bf16_round((q * s).astype(F32))
+    e = O.bf16_round((w - rec).astype(F32))
+    return O.f32_to_bf16_bits(rec).astype(np.int64), (e * e).astype(F32)
+
+
+def test_nvfp3_threshold_rule_matches_the_codebook_rule():
+    """fp3sse_kernel's comparisons on bf16 bit patterns give the reference's W_hat and squared
+    error for every finite bf16 w with |w| <= a and every group maximum a in [1, 2), and for
+    maxima in the binades of 1e-8, 2^-60, 2^100 and 2^125 (the thresholds move with a's
+    exponent; from 2^126 up, where 3a would overflow, the kernel takes the per-element rule).  The
+    squared error alone cannot see the tie rule (a tie of fl32(w / s) is an exact tie here, both
+    neighbours equally far), so W_hat is compared too."""
+    b = np.arange(1 << 16, dtype=np.uint32)
+    with np.errstate(invalid="ignore"):
+        fin = b[np.isfinite((b << 16).view(F32))]
+    import re
+    from pathlib import Path
+    src = (Path(__file__).resolve().parent.parent / "prismaquant_b200" / "csrc" / "pq_codebook.cu").read_text()
+    lo = int(re.search(r"BF16_1EM8_CEIL = 0x([0-9A-Fa-f]+)u", src).group(1), 16)
+    hi = int(re.search(r"FP3_FAST_CEIL = 0x([0-9A-Fa-f]+)u", src).group(1), 16)
+    assert hi == 0x7E80                                    # 2^126: 3a stays finite below it
+    binades = [0x3F80, 0x3200, 0x2180, 0x7180, 0x7E00]   # 1, 2^-27 (holds 1e-8), 2^-60, 2^100, 2^125
+    for base in binades:
+        for ab in range(base, base + 0x80):
+            if ab < lo or ab >= hi:                        # the per-element path
+                continue
+            wb = fin[(fin & 0x7FFF) <= ab].astype(np.uint16)
+            with np.errstate(over="ignore"):               # squares of errors near 2^100
+                got, want = _fp3_err_sq_kernel(wb, ab), _fp3_err_sq_reference(wb, ab)
+            for g, r in zip(got, want):
+                bad = g != r
+                assert not bad.any(), (hex(ab), wb[bad][:5], g[bad][:5], r[bad][:5])
+
+
+def _e5m2_standard_mags():
+    """Non-negative values of the hardware E5M2 format (finite, up to 57344), ascending."""
+    m = [k / 4 * 2.0 ** -14 for k in range(4)]
+    m += [(1 + k / 4) * 2.0 ** (e - 15) for e in range(1, 31) for k in range(4)]
+    return np.array(m)
+
+
+def test_fp8_e5m2_bracket_rule_matches_the_codebook_rule():
+    """e5m2_word of the codebook kernel: for a row maximum a (every bf16 a in [1, 2), and binades
+    of 2^-30 and 2^40) and every finite bf16 w with |w| <= a, with r any of RN(1/s) and its two
+    neighbours (rcp.approx is within one ulp), the hardware conversions (round to nearest even,
+    saturating) of RZ(w r_lo / 2) and RZ(w r_hi / 2), where they agree and the word is not
+    flagged tiny, give the reference's W_hat bf16(q s) (nearest codebook point of fl32(w / s),
+    ties to the lower value, codebook exponent 31 finite)."""
+    from oracle import pq_oracle as O
+    mags = _e5m2_standard_mags()
+    even = (np.arange(mags.size) % 2) == 0
+    cb = O.CODEBOOKS["fp8_e5m2"].astype(np.float64)
+    b = np.arange(1 << 16, dtype=np.uint32)
+    with np.errstate(invalid="ignore"):
+        fin = b[np.isfinite((b << 16).view(F32))]
+    checked = fast = 0
+    for base in (0x3F80, 0x3080, 0x53 << 8):
+        for ab in range(base, base + 0x80, 3 if base != 0x3F80 else 1):
+            a = (np.uint32(ab) << 16).view(F32)
+            s = F32(max(a, F32(1e-8)) / F32(114688.0))
+            wb = fin[(fin & 0x7FFF) <= ab]
+            w = (wb << 16).view(F32)
+            x = (w / s).astype(F32).astype(np.float64)
+            ref = _ties_lower(x, cb[cb >= 0])
+            ref = np.where(np.abs(x) >= 114688.0, np.sign(x) * 114688.0, ref)
+            want = O.f32_to_bf16_bits((ref * np.float64(s)).astype(F32))
+            want = np.where(want == 0x8000, 0, want)
+            tiny_t = ((int(np.array([s * F32(2.0 ** -12)], F32).view(np.uint32)[0]) >> 16) + 1)
+            mag = wb & 0x7FFF
+            tiny = (mag > 0) & (mag <= tiny_t)
+            r0 = F32(1.0) / s
+            for r in (np.nextafter(r0, F32(0)), r0, np.nextafter(r0, F32(np.inf))):
+                r_lo = _rz32(np.array([np.float64(r) * (1 - 2.0 ** -20)]))[0] * 0.5
+                r_hi = _rz32(np.array([np.float64(r) * (1 + 2.0 ** -20)]))[0] * 0.5
+                cl = _rne(_rz32(w.astype(np.float64) * r_lo), mags, even, 57344.0)
+                ch = _rne(_rz32(w.astype(np.float64) * r_hi), mags, even, 57344.0)
+                ok = (cl == ch) & ~tiny
+                rec = O.f32_to_bf16_bits((cl * np.float64(F32(2.0) * s)).astype(F32))   # fl32(code x 2s)
+                got = np.where(rec == 0x8000, 0, rec)
+                bad = ok & (got != want)
+                assert not bad.any(), (hex(ab), wb[bad][:5], got[bad][:5], want[bad][:5])
+                checked += int((mag > tiny_t).sum())
+                fast += int((ok & (mag > tiny_t)).sum())
+    assert fast > 0.99 * checked                       # beside tiny elements, the exact rule is rare

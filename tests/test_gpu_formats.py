@@ -185,7 +185,7 @@ def test_mx_multi_format_sse_special_groups(kind):
     import warnings
     from prismaquant_b200 import _lib
     bits = _special_rows(kind)
-    fmts = MX_EXT + ["INT3", "BF16", "FP8_E5M2"]
+    fmts = MX_EXT + ["INT3", "BF16", "FP8_E5M2", "NVFP3"]
     out = torch.zeros(len(fmts), dtype=torch.float64, device="cuda")
     _lib.format_sse_multi(to_cuda_bf16(bits), fmts, out)
     got = out.cpu().numpy()
@@ -280,5 +280,126 @@ def test_mx_w_hat_across_the_group_exponent_range(fmt):
     got = bits_of(_lib.cost_qdq(to_cuda_bf16(bits), fmt))
     with np.errstate(all="ignore"):
         want = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt))
+    bad = np.nonzero(got != want)
+    assert bad[0].size == 0, (fmt, got[bad][:5], want[bad][:5], bits[bad][:5])
+
+
+def _moderate_bf16_rows(cols):
+    """Every bf16 value of magnitude below 2^60 (squares stay finite), randomly grouped."""
+    allv = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    keep = allv[(allv & 0x7FFF) < 0x5D80]
+    keep = np.random.default_rng(cols + 1).permutation(keep)
+    return keep[: (keep.size // cols) * cols].reshape(-1, cols)
+
+
+def _nvfp3_threshold_rows():
+    """16-element groups around NVFP3's decision points: group maxima a with 3a a bf16 (exact ties
+    possible) and not, each group holding a, the bf16 values next to a/16, 3a/16, 3a/8 and 3a/4
+    (on them where they are bf16 values) with both signs; beside them all-zero groups and groups
+    whose maximum is below 1e-8."""
+    groups = []
+    for a0 in (1.0, 1.25, 1.5, 1.0078125, 1.3359375, 1.9921875):
+        for k in (-20, 0, 7):
+            a = np.float32(a0 * 2.0 ** k)
+            near = []
+            for t in (a / 16, 3 * np.float64(a) / 16, 3 * np.float64(a) / 8, 3 * np.float64(a) / 4):
+                b = int(O.f32_to_bf16_bits(np.array([t], np.float32))[0])   # nearest bf16, its neighbours
+                near += [b, b + 1, b - 1]
+            vals = O.bf16_bits_to_f32(np.array(near, np.uint16))
+            for sign in (1, -1):
+                g = np.zeros(16, np.float32)
+                g[0] = a
+                g[1:1 + vals.size] = sign * vals[:15]
+                groups.append(g)
+    groups.append(np.linspace(-9e-9, 9e-9, 16).astype(np.float32))
+    while len(groups) % 4:
+        groups.append(np.zeros(16, np.float32))
+    return O.f32_to_bf16_bits(np.concatenate(groups).reshape(-1, 64))
+
+
+@pytest.mark.parametrize("case", ["every_bf16", "moderate_bf16", "thresholds", "tiny", "huge", "inf"])
+def test_nvfp3_sse_and_w_hat_match_oracle(case):
+    """NVFP3's squared error (fp3sse_kernel) and W_hat (the codebook kernel's comparison path)
+    against the oracle, the error sum also against the codebook kernel's division rule (the
+    weighted sum with unit weights)."""
+    import warnings
+    from prismaquant_b200 import _lib
+    bits = {"every_bf16": lambda: _all_bf16_rows(256), "moderate_bf16": lambda: _moderate_bf16_rows(256),
+            "thresholds": _nvfp3_threshold_rows}.get(case, lambda: _special_rows(case))()
+    w = to_cuda_bf16(bits)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        want_sse = _oracle_sse(bits, "NVFP3")
+        want_hat = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, "NVFP3"))
+    got = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.format_sse(w, "NVFP3", got)
+    ref = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.weighted_sse(w, "NVFP3", torch.ones(bits.size, dtype=torch.float32, device="cuda"), ref)
+    if np.isnan(want_sse) or np.isinf(want_sse):
+        assert got.item() == want_sse or (np.isnan(want_sse) and np.isnan(got.item())), (got.item(), want_sse)
+    else:
+        assert got.item() == pytest.approx(want_sse, rel=1e-5, abs=1e-30)
+        assert got.item() == pytest.approx(ref.item(), rel=1e-6, abs=1e-30)
+    hat = bits_of(_lib.cost_qdq(w, "NVFP3"))
+    bad = np.nonzero(hat != want_hat)
+    assert bad[0].size == 0, (hat[bad][:5], want_hat[bad][:5], bits[bad][:5])
+
+
+def _e5m2_rows():
+    """Rows for FP8_E5M2's bracket path: maxima with significand 1.75 (s a power of two, so w / s
+    is exact and every codebook midpoint among the elements is an exact tie), others with inexact
+    scales; elements on and next to midpoints, +-0, values far below the maximum (the exact rule)
+    and values near it (saturation)."""
+    rng = np.random.default_rng(5)
+    rows = []
+    for amax in (1.75, 1.75 * 2.0 ** -9, 1.0078125, 1.5, 1.75 * 2.0 ** 20):
+        s = np.float64(np.float32(np.float32(amax) / np.float32(114688.0)))
+        for _ in range(3):
+            k = rng.integers(-14, 16, size=256)
+            mid = (1 + (2 * rng.integers(0, 4, size=256) + 1) / 8) * 2.0 ** k * s      # midpoints x s
+            row = np.where(rng.random(256) < 0.5, mid, rng.standard_normal(256) * amax / 3)
+            row = np.clip(row, -amax, amax) * np.where(rng.random(256) < 0.5, -1, 1)
+            row[:4] = [amax, -amax, 0.0, -0.0]
+            row[4:8] = np.array([2.0 ** -40, -2.0 ** -40, 2.0 ** -20, 1e-30]) * amax
+            row[8] = 0.97 * amax
+            rows.append(row)
+    return O.f32_to_bf16_bits(np.array(rows, np.float32))
+
+
+def test_fp8_e5m2_bracket_path_matches_oracle():
+    """FP8_E5M2's W_hat (bit-exact) and squared error (rel 1e-5) against the oracle on rows with
+    exact ties, zeros of both signs and elements on the exact rule, the error also against the
+    codebook kernel's per-element rule (the weighted sum with unit weights)."""
+    from prismaquant_b200 import _lib
+    bits = _e5m2_rows()
+    w = to_cuda_bf16(bits)
+    hat = bits_of(_lib.cost_qdq(w, "FP8_E5M2"))
+    want = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, "FP8_E5M2"))
+    bad = np.nonzero(hat != want)
+    assert bad[0].size == 0, (hat[bad][:5], want[bad][:5], bits[bad][:5])
+    got = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.format_sse(w, "FP8_E5M2", got)
+    ref = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.weighted_sse(w, "FP8_E5M2", torch.ones(bits.size, dtype=torch.float32, device="cuda"), ref)
+    assert got.item() == pytest.approx(_oracle_sse(bits, "FP8_E5M2"), rel=1e-5, abs=1e-30)
+    assert got.item() == pytest.approx(ref.item(), rel=1e-6, abs=1e-30)
+
+
+@pytest.mark.parametrize("kind", ["tiny", "huge", "inf"])
+@pytest.mark.parametrize("fmt", EXT_FMTS[:-1] + ["FP8_E4M3_G128"])
+def test_w_hat_of_special_groups_matches_oracle(fmt, kind):
+    """W_hat of groups with tiny scales, bf16 subnormals, all zeros, overflowing scales and an
+    infinity, for every format of the codebook kernel: bit-exact against the oracle (a NaN
+    reconstruction, 0 x an infinite scale, is written 0x7FC0 as torch writes it)."""
+    import warnings
+    from prismaquant_b200 import _lib
+    bits = _special_rows(kind).reshape(8, 128)
+    got = bits_of(_lib.cost_qdq(to_cuda_bf16(bits), fmt))
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        if fmt == "FP8_E4M3_G128":
+            want = O.f32_to_bf16_bits(O.codebook_qdq_f32(bits, "fp8_e4m3", 128, False))
+        else:
+            want = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt))
     bad = np.nonzero(got != want)
     assert bad[0].size == 0, (fmt, got[bad][:5], want[bad][:5], bits[bad][:5])
