@@ -483,6 +483,46 @@ __device__ __forceinline__ bool e5m2_word(const uint4& u, const E5m2Row& q, uint
   return bad == 0u;
 }
 
+// Row-wise symmetric integer formats (INT8_W8A16, and any integer format whose group is a whole
+// row; format_registry.py:147-172: s = fl32(max(a, 1e-8) / L), q = round half even (fl32(w / s))
+// clamped to [-L-1, L], W_hat = bf16(q s)) without division per element: the reciprocal bracket
+// of intsse_kernel, RN(w RN(r (1 -+ 2^-19))) with r = rcp.approx(s), each rounded half even to
+// an integer by adding and subtracting 1.5 x 2^23 in float32 pairs.  Where the two integers agree
+// no half-integer lies between the products, which hold fl32(w / s) strictly between them, so
+// that integer is the reference's (|w| <= a keeps it within [-L, L]).  W_hat takes w's sign, as
+// torch.round gives -0.0 for a negative w that rounds to zero.  A word with a pair that
+// disagrees (an exact tie among them) or a NaN takes the exact rule.
+struct IntRow {
+  uint64_t lo2, hi2, s2;   // the two bracket reciprocals and s, in both halves of a float32 pair
+};
+
+__device__ __forceinline__ IntRow int_row(float s) {   // s: a positive normal scale
+  const float r = rcp_approx(s);
+  const float lo = __fmul_rn(r, 1.0f - 0x1p-19f), hi = __fmul_rn(r, 1.0f + 0x1p-19f);
+  return {f2_pack(lo, lo), f2_pack(hi, hi), f2_pack(s, s)};
+}
+
+// 8 elements: W_hat words and the fp32 sum of the 8 exact squares; false if the word needs the
+// exact rule
+__device__ __forceinline__ bool int_word(const uint4& u, const IntRow& q, uint32_t (&o)[4], float& part) {
+  const uint64_t m2 = f2_pack(12582912.0f, 12582912.0f), nm2 = f2_pack(-12582912.0f, -12582912.0f);   // 1.5 x 2^23
+  const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+  bool split = false;
+  float acc = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint64_t w2 = f2_from_bf16x2(v[p]);
+    const uint64_t ql = f2_add_rn(f2_add_rn(f2_mul_rn(w2, q.lo2), m2), nm2);
+    const uint64_t qh = f2_add_rn(f2_add_rn(f2_mul_rn(w2, q.hi2), m2), nm2);
+    split = split || ql != qh;
+    const uint32_t rec = f2_to_bf16x2(f2_mul_rn(ql, q.s2));
+    o[p] = rec | (v[p] & 0x80008000u);   // q = 0 keeps w's sign; q != 0 has it already
+    acc = sq2_acc(bf16x2_sub(v[p], rec), acc);
+  }
+  part = acc;
+  return !split;
+}
+
 // NaN among 8 bf16 values: a magnitude above 0x7F80 in some half
 __device__ __forceinline__ bool has_nan8(const uint4& u) {
   const uint32_t t = (((u.x & 0x7FFF7FFFu) + 0x007F007Fu) | ((u.y & 0x7FFF7FFFu) + 0x007F007Fu) |
@@ -604,15 +644,21 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
       a = __uint_as_float(warp_max_u(__float_as_uint(a)));
       float inv;
       const float scale = scale_of(a, inv);
-      if constexpr (KIND == XK_E5M2) {
-        // FP8_E5M2 by the bracket (e5m2_word) where the scale is a normal number, unweighted
+      if constexpr (KIND == XK_E5M2 || KIND == XK_INT) {
+        // FP8_E5M2 (e5m2_word) and the integer formats (int_word) by their brackets where the
+        // scale is a normal number, unweighted
         if (!f.mx && h_mode == 0 && scale >= 0x1p-126f && scale <= 0x1p120f) {
-          const E5m2Row q = e5m2_row(scale);
+          E5m2Row qe{};
+          IntRow qi{};
+          if constexpr (KIND == XK_E5M2) qe = e5m2_row(scale); else qi = int_row(scale);
           for (int64_t col = lane * 8; col < cols; col += 256) {
             const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + col));
             uint32_t o[4];
             float part;
-            if (!has_nan8(u) && e5m2_word(u, q, o, part)) {
+            bool fast;
+            if constexpr (KIND == XK_E5M2) fast = !has_nan8(u) && e5m2_word(u, qe, o, part);
+            else fast = !has_nan8(u) && int_word(u, qi, o, part);
+            if (fast) {
               if (MODE == MODE_QDQ)
                 *reinterpret_cast<uint4*>(out + r * cols + col) = make_uint4(o[0], o[1], o[2], o[3]);
               else

@@ -457,3 +457,39 @@ def test_fp8_e5m2_bracket_rule_matches_the_codebook_rule():
                 checked += int((mag > tiny_t).sum())
                 fast += int((ok & (mag > tiny_t)).sum())
     assert fast > 0.99 * checked                       # beside tiny elements, the exact rule is rare
+
+
+def test_integer_row_bracket_matches_the_reference_rule():
+    """int_word of the codebook kernel's row path: for L = 127 (INT8_W8A16) and L = 1, 3, 7, row
+    maxima a across [1, 2) and two more binades, every finite bf16 w with |w| <= a, and r any of
+    RN(1/s) and its two neighbours, the products RN(w RN(r (1 -+ 2^-19))) rounded half even, where
+    they agree, give the reference's W_hat: bf16(q s), q = round half even of fl32(w / s),
+    -0 for a negative w that rounds to zero (format_registry.py:147-172)."""
+    from oracle import pq_oracle as O
+    b = np.arange(1 << 16, dtype=np.uint32)
+    with np.errstate(invalid="ignore"):
+        fin = b[np.isfinite((b << 16).view(F32))]
+    checked = fast = 0
+    for L in (127, 1, 3, 7):
+        for base in (0x3F80, 0x2F00, 0x5500):
+            for ab in range(base, base + 0x80, 1 if (L == 127 and base == 0x3F80) else 9):
+                a = (np.uint32(ab) << 16).view(F32)
+                s = F32(max(a, F32(1e-8)) / F32(L))
+                wb = fin[(fin & 0x7FFF) <= ab]
+                w = (wb << 16).view(F32)
+                q_ref = np.clip(np.rint((w / s).astype(F32)), -L - 1, L).astype(F32)
+                want = O.f32_to_bf16_bits((q_ref * s).astype(F32))
+                r0 = F32(1.0) / s
+                for r in (np.nextafter(r0, F32(0)), r0, np.nextafter(r0, F32(np.inf))):
+                    lo, hi = F32(r * F32(1 - 2.0 ** -19)), F32(r * F32(1 + 2.0 ** -19))
+                    m = F32(1.5 * 2.0 ** 23)                           # the kernel's magic add: half
+                    ql = ((w * lo).astype(F32) + m) - m                # even, and +0 for a small w < 0
+                    qh = ((w * hi).astype(F32) + m) - m
+                    ok = ql == qh
+                    rec = O.f32_to_bf16_bits((ql * s).astype(F32)).astype(np.uint32) | (wb & 0x8000)
+                    bad = ok & (rec != want)
+                    assert not bad.any(), (L, hex(ab), wb[bad][:5], rec[bad][:5], want[bad][:5])
+                    big = (wb & 0x7FFF) > ab - 0x600                   # within 2^-12 of the maximum
+                    checked += int(big.sum())
+                    fast += int((ok & big).sum())
+    assert fast > 0.99 * checked                                       # the exact rule is rare

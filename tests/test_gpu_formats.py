@@ -403,3 +403,38 @@ def test_w_hat_of_special_groups_matches_oracle(fmt, kind):
             want = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt))
     bad = np.nonzero(got != want)
     assert bad[0].size == 0, (fmt, got[bad][:5], want[bad][:5], bits[bad][:5])
+
+
+def _int8_tie_rows():
+    """Rows for the integer row path: maxima 127 x 2^k (s = 2^k, so elements at half-integer
+    multiples of s are exact ties) beside rows with inexact scales, negative values that round
+    to zero, and +-0."""
+    rng = np.random.default_rng(8)
+    rows = []
+    for k in (-9, 0, 6):
+        half = (rng.integers(-127, 127, size=512) + 0.5) * 2.0 ** k
+        half[0] = 127 * 2.0 ** k
+        half[1:5] = np.array([-0.3, -0.5, 0.5, -0.0]) * 2.0 ** k
+        rows.append(half)
+        rows.append(rng.standard_normal(512) * 2.0 ** k)
+    return O.f32_to_bf16_bits(np.array(rows, dtype=np.float32))
+
+
+@pytest.mark.parametrize("fmt,cols", [("INT8_W8A16", 512), ("INT3", 16), ("INT4_W4A16_g128", 128)])
+def test_integer_row_path_matches_oracle(fmt, cols):
+    """The row path's integer bracket (INT8_W8A16, and INT3 / INT4 rows one group long): W_hat
+    bit-exact and the squared error within 1e-5 of the oracle, on exact ties, values that round
+    to -0 and ordinary rows; the error also against the per-element rule (unit weights)."""
+    from prismaquant_b200 import _lib
+    bits = _int8_tie_rows().reshape(-1, cols)
+    w = to_cuda_bf16(bits)
+    hat = bits_of(_lib.cost_qdq(w, fmt))
+    want = O.f32_to_bf16_bits(O.cost_qdq_f32(bits, fmt))
+    bad = np.nonzero(hat != want)
+    assert bad[0].size == 0, (fmt, hat[bad][:5], want[bad][:5], bits[bad][:5])
+    got = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.format_sse(w, fmt, got)
+    ref = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.weighted_sse(w, fmt, torch.ones(bits.size, dtype=torch.float32, device="cuda"), ref)
+    assert got.item() == pytest.approx(_oracle_sse(bits, fmt), rel=1e-5, abs=1e-30)
+    assert got.item() == pytest.approx(ref.item(), rel=1e-6, abs=1e-30)
