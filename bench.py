@@ -382,7 +382,7 @@ def run_kernels(a, local):
         ("xfmt2_kernel cost_qdq MXFP6_E3M2 (W_hat)", lambda: _lib.cost_qdq(W, "MXFP6_E3M2"), 4 * n, "GB/s"),
         ("xfmt2_kernel cost_qdq NVFP3 (W_hat)", lambda: _lib.cost_qdq(W, "NVFP3"), 4 * n, "GB/s"),
     ]
-    for f in ("MXFP4", "MXFP6_E3M2", "FP8_E5M2", "NVFP3", "INT3", "INT4_W4A16_g128", "INT8_W8A16"):
+    for f in ("MXFP4", "MXFP6_E3M2", "FP8_E5M2", "NVFP3", "INT3", "INT4_W4A16_g128", "INT8_W8A16", "FP8_E4M3_G128"):
         kname = ("mxsse_kernel" if f.startswith("MX") else "fp3sse_kernel" if f == "NVFP3" else
                  "intsse_kernel" if f in ("INT2", "INT3", "INT4_W4A16_g128") else "xfmt2_kernel")
         table.append((f"{kname} format_sse {f}", (lambda f=f: _lib.format_sse(W, f, s0)), 2 * n, "GB/s"))

@@ -483,6 +483,52 @@ __device__ __forceinline__ bool e5m2_word(const uint4& u, const E5m2Row& q, uint
   return bad == 0u;
 }
 
+// E4M3 with a real scale per group (FP8_E4M3_G128, the batched form of FP8_SOURCE;
+// measure_quant_cost.py:516-548 with format_registry.py:194-233): the codebook is the hardware
+// E4M3 grid up to 448, so the bracket of the fast sweep decides each pair: RZ(w r_lo) and
+// RZ(w r_hi) hold fl32(w / s) strictly between them, and where their hardware conversions (round
+// to nearest even, saturating at 448) agree no midpoint lies between them, so the code is the
+// reference's nearest point of fl32(w / s) whatever its tie rule.  A word with a pair that
+// disagrees (exact ties among them) or a NaN takes the exact rule.  W_hat = bf16(fl32(q s)), +0
+// where q is zero, as the reference's codebook zero gives.
+__device__ __forceinline__ bool e4m3g_word(const uint4& u, uint64_t lo2, uint64_t hi2, uint64_t s2, uint32_t (&o)[4],
+                                           float& part) {
+  const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+  uint32_t dx = 0u;
+  float acc = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint64_t w2 = f2_from_bf16x2(v[p]);
+    const uint32_t cl = cvt_e4m3x2(f2_mul_rz(w2, lo2));
+    dx |= cl ^ cvt_e4m3x2(f2_mul_rz(w2, hi2));
+    const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(cl), s2));
+    o[p] = rec & (prmt_sign_halves((rec & 0x7FFF7FFFu) + 0x7FFF7FFFu) | 0x7FFF7FFFu);   // -0 -> +0
+    acc = sq2_acc(bf16x2_sub(v[p], rec), acc);
+  }
+  part = acc;
+  return dx == 0u;
+}
+
+// The same groups outside the flagged family of the fast sweep's FP8 rows (row_tab in
+// pq_sweep_fast.cu): with 1e-8 <= a < 2^60 and not (|a - 448 s| >= 160 ulp(s) and s's significand
+// below 1.5), the conversion of the lower bracket min(RZ(w r_lo), RZ(w r_hi)) is the reference's
+// code, exact ties included (tests/test_fast_rules.py checks the rule for every pair of bf16
+// values), so no word needs the exact rule.
+__device__ __forceinline__ void e4m3g_lower_word(const uint4& u, uint64_t lo2, uint64_t hi2, uint64_t s2,
+                                                 uint32_t (&o)[4], float& part) {
+  const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+  float acc = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint64_t w2 = f2_from_bf16x2(v[p]);
+    const uint32_t c = cvt_e4m3x2(f2_min(f2_mul_rz(w2, lo2), f2_mul_rz(w2, hi2)));
+    const uint32_t rec = f2_to_bf16x2(f2_mul_rn(e4m3x2_to_f2(c), s2));
+    o[p] = rec & (prmt_sign_halves((rec & 0x7FFF7FFFu) + 0x7FFF7FFFu) | 0x7FFF7FFFu);   // -0 -> +0
+    acc = sq2_acc(bf16x2_sub(v[p], rec), acc);
+  }
+  part = acc;
+}
+
 // Row-wise symmetric integer formats (INT8_W8A16, and any integer format whose group is a whole
 // row; format_registry.py:147-172: s = fl32(max(a, 1e-8) / L), q = round half even (fl32(w / s))
 // clamped to [-L-1, L], W_hat = bf16(q s)) without division per element: the reciprocal bracket
@@ -620,6 +666,29 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
             *reinterpret_cast<uint4*>(out + r * cols + col) = make_uint4(o[0], o[1], o[2], o[3]);
           } else
             do8(u, wv, r * cols + col, r, scale, inv, std::true_type{});
+        } else if (KIND == XK_E4M3 && !f.mx && h_mode == 0 && a >= 1e-8f && a < F8_EXACT_ROW_AMAX &&
+                   !has_nan8(u)) {
+          // E4M3 with real group scales (FP8_E4M3_G128): the lower-bracket rule, or the bracket of
+          // e4m3g_word in groups of the flagged family
+          float rl, rh;
+          recip_bounds(scale, rl, rh);
+          const uint32_t sb = __float_as_uint(scale);
+          const float ulp = __uint_as_float((sb & 0x7F800000u) - (23u << 23));
+          const bool flagged = fabsf(__fmaf_rn(-448.0f, scale, a)) >= 160.0f * ulp && (sb & 0x7FFFFFu) < 0x400000u;
+          const uint64_t lo2 = f2_pack(rl, rl), hi2 = f2_pack(rh, rh), s2 = f2_pack(scale, scale);
+          uint32_t o[4];
+          float part;
+          bool fast = true;
+          if (flagged) fast = e4m3g_word(u, lo2, hi2, s2, o, part);
+          else e4m3g_lower_word(u, lo2, hi2, s2, o, part);
+          if (fast) {
+            if (MODE == MODE_QDQ)
+              *reinterpret_cast<uint4*>(out + r * cols + col) = make_uint4(o[0], o[1], o[2], o[3]);
+            else
+              acc += (double)part;
+          } else {
+            do8(u, wv, r * cols + col, r, scale, inv, std::false_type{});
+          }
         } else if (KIND == XK_E2M0 && MODE == MODE_QDQ && (__float_as_uint(a) >> 16) >= BF16_1EM8_CEIL &&
                    (__float_as_uint(a) >> 16) < FP3_FAST_CEIL && !has_nan8(u)) {
           // NVFP3 with a group maximum in [1e-8, 2^126): the comparisons of fp3sse_kernel

@@ -493,3 +493,51 @@ def test_integer_row_bracket_matches_the_reference_rule():
                     checked += int(big.sum())
                     fast += int((ok & big).sum())
     assert fast > 0.99 * checked                                       # the exact rule is rare
+
+
+def test_fp8_e4m3_group_bracket_matches_the_codebook_rule():
+    """e4m3g_word (FP8_E4M3_G128 on the codebook kernel): for group maxima a across [1, 2) and two
+    more binades, every finite bf16 w with |w| <= a, and r any of RN(1/s) and its two neighbours,
+    the hardware conversions of RZ(w r_lo) and RZ(w r_hi), where they agree, give the reference's
+    W_hat bf16(q s) (nearest E4M3 point of fl32(w / s), ties to the lower value, +0 for zero);
+    outside the flagged family (fp8_row_flag) the lower bracket's conversion gives it for every
+    w (e4m3g_lower_word)."""
+    from oracle import pq_oracle as O
+    cb = O.CODEBOOKS["fp8_e4m3"].astype(np.float64)
+    mags = cb[cb >= 0]
+    even = (np.arange(mags.size) % 2) == 0
+    b = np.arange(1 << 16, dtype=np.uint32)
+    with np.errstate(invalid="ignore"):
+        fin = b[np.isfinite((b << 16).view(F32))]
+    checked = fast = 0
+    for base in (0x3F80, 0x3080, 0x5300):
+        for ab in range(base, base + 0x80, 1 if base == 0x3F80 else 5):
+            a = (np.uint32(ab) << 16).view(F32)
+            s = F32(max(a, F32(1e-8)) / F32(448.0))
+            wb = fin[(fin & 0x7FFF) <= ab]
+            w = (wb << 16).view(F32)
+            x = (w / s).astype(F32).astype(np.float64)
+            ref = np.where(np.abs(x) >= 448.0, np.sign(x) * 448.0, _ties_lower(x, mags))
+            want = O.f32_to_bf16_bits((ref * np.float64(s)).astype(F32))
+            want = np.where(want == 0x8000, 0, want)
+            r0 = F32(1.0) / s
+            for r in (np.nextafter(r0, F32(0)), r0, np.nextafter(r0, F32(np.inf))):
+                r_lo = _rz32(np.array([np.float64(r) * (1 - 2.0 ** -20)]))[0]
+                r_hi = _rz32(np.array([np.float64(r) * (1 + 2.0 ** -20)]))[0]
+                cl = _rne(_rz32(w.astype(np.float64) * r_lo), mags, even, 448.0)
+                ch = _rne(_rz32(w.astype(np.float64) * r_hi), mags, even, 448.0)
+                ok = cl == ch
+                rec = O.f32_to_bf16_bits((cl * np.float64(s)).astype(F32))
+                got = np.where(rec == 0x8000, 0, rec)                    # -0 -> +0
+                bad = ok & (got != want)
+                assert not bad.any(), (hex(ab), wb[bad][:5], got[bad][:5], want[bad][:5])
+                if not fp8_row_flag(a):                                  # e4m3g_lower_word: every w
+                    cm = _rne(np.minimum(_rz32(w.astype(np.float64) * r_lo),
+                                         _rz32(w.astype(np.float64) * r_hi)), mags, even, 448.0)
+                    low = O.f32_to_bf16_bits((cm * np.float64(s)).astype(F32))
+                    low = np.where(low == 0x8000, 0, low)
+                    assert (low == want).all(), (hex(ab), wb[low != want][:5])
+                big = (wb & 0x7FFF) > ab - 0x600
+                checked += int(big.sum())
+                fast += int((ok & big).sum())
+    assert fast > 0.99 * checked

@@ -310,3 +310,28 @@ def test_pipelined_plan_equals_one_chunk():
         assert torch.allclose(many.sse, one.sse, rtol=1e-12, atol=0.0)   # fp64 atomics: order may differ
         for (c, s, g), (c1, s1, g1) in zip(many.outputs, one.outputs):
             assert torch.equal(c, c1) and torch.equal(s.view(torch.uint8), s1.view(torch.uint8)) and torch.equal(g, g1)
+
+
+def test_fp8_channel_export_ties_and_every_bf16_value():
+    """The FP8 per-channel export against the oracle: rows whose maximum has a significand that
+    is a multiple of 7 (s = a / 448 exact, so E4M3 midpoints among the quotients are exact ties,
+    which round to even), 1.75 x 2^k (s a power of two), and others, each row holding 4095 bf16
+    magnitudes drawn from all those up to its maximum, with random signs."""
+    rng = np.random.default_rng(12)
+    b = np.arange(1 << 15, dtype=np.uint32)
+    mags = b[b < 0x7F80]
+    rows = []
+    for sig in (1.75, 1.3125, 1.09375, 1.0, 1.5390625, 1.9921875):     # 224, 168, 140: multiples of 7
+        for k in (-30, -1, 0, 9):
+            a_bits = int(O.f32_to_bf16_bits(np.array([sig * 2.0 ** k], np.float32))[0])
+            pool = mags[mags <= a_bits]
+            row = rng.choice(pool, size=4095, replace=pool.size < 4095).astype(np.uint32)
+            row |= rng.integers(0, 2, size=4095).astype(np.uint32) << 15
+            rows.append(np.concatenate([[a_bits], row]).astype(np.uint16))
+    bits = np.array(rows)
+    q, sc = enc.quantize_dequantize_fp8_dynamic(to_cuda_bf16(bits))
+    rq, rsc = O.fp8_dynamic_pack(O.bf16_bits_to_f32(bits))
+    np.testing.assert_array_equal(f32(sc), rsc)
+    got = u8_of(q)
+    bad = np.nonzero(got != rq)
+    assert bad[0].size == 0, (got[bad][:5], rq[bad][:5], bits[bad][:5])

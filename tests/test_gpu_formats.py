@@ -438,3 +438,37 @@ def test_integer_row_path_matches_oracle(fmt, cols):
     _lib.weighted_sse(w, fmt, torch.ones(bits.size, dtype=torch.float32, device="cuda"), ref)
     assert got.item() == pytest.approx(_oracle_sse(bits, fmt), rel=1e-5, abs=1e-30)
     assert got.item() == pytest.approx(ref.item(), rel=1e-6, abs=1e-30)
+
+
+def test_fp8_e4m3_g128_bracket_path_matches_oracle():
+    """FP8_E4M3_G128 (real scale per 128 elements) on the codebook kernel's bracket: groups whose
+    maxima have significands that are multiples of 7 (exact scales, so E4M3 midpoints among the
+    quotients are exact ties, taken by the exact rule), signed zeros and values that round to
+    zero; W_hat bit-exact, squared error within 1e-5 of the oracle and 1e-6 of the per-element
+    rule (unit weights)."""
+    from prismaquant_b200 import _lib
+    rng = np.random.default_rng(14)
+    b = np.arange(1 << 15, dtype=np.uint32)
+    mags = b[b < 0x7F80]
+    groups = []
+    for sig in (1.75, 1.3125, 1.09375, 1.0, 1.5390625):
+        for k in (-20, 0, 11):
+            a_bits = int(O.f32_to_bf16_bits(np.array([sig * 2.0 ** k], np.float32))[0])
+            pool = mags[mags <= a_bits]
+            g = rng.choice(pool[pool > a_bits - 0x500], size=127).astype(np.uint32)
+            g |= rng.integers(0, 2, size=127).astype(np.uint32) << 15
+            g[:3] = [0, 0x8000, 0x8000 | (a_bits - 0x500)]
+            groups.append(np.concatenate([[a_bits], g]).astype(np.uint16))
+    bits = np.array(groups).reshape(-1, 384)                     # three groups a row
+    w = to_cuda_bf16(bits)
+    hat = bits_of(_lib.cost_qdq(w, "FP8_E4M3_G128"))
+    want = O.f32_to_bf16_bits(O.codebook_qdq_f32(bits, "fp8_e4m3", 128, False))
+    bad = np.nonzero(hat != want)
+    assert bad[0].size == 0, (hat[bad][:5], want[bad][:5], bits[bad][:5])
+    err = O.bf16_round((O.bf16_bits_to_f32(bits) - O.codebook_qdq_f32(bits, "fp8_e4m3", 128, False)).astype(np.float32))
+    got = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.format_sse(w, "FP8_E4M3_G128", got)
+    ref = torch.zeros((), dtype=torch.float64, device="cuda")
+    _lib.weighted_sse(w, "FP8_E4M3_G128", torch.ones(bits.size, dtype=torch.float32, device="cuda"), ref)
+    assert got.item() == pytest.approx(float((err * err).astype(np.float32).astype(np.float64).sum()), rel=1e-5)
+    assert got.item() == pytest.approx(ref.item(), rel=1e-6)
