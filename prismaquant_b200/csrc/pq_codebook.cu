@@ -441,10 +441,11 @@ __device__ __forceinline__ uint32_t fp3_rec2(uint32_t v, const Fp3Group& g) {
 // the two codes agree, no codebook midpoint lies strictly between the brackets, fl32(w / s) lies
 // strictly inside them, so the reference's nearest point (ties to the lower value) of fl32(w / s)
 // is that code times 2: above 2^-13 the hardware grid of x/2, doubled, is the reference's grid of
-// x (the 2^16 binade included), and saturation agrees.  A word with a pair whose codes differ (an
-// element within 2^-20 of a midpoint, exact ties among them), or with a nonzero |w| at or below
-// RU(s 2^-12) (x/2 in the hardware's subnormal range, where the grids part), or a NaN, is redone
-// by the exact rule.  W_hat = bf16(fl32((x/2 code) (2s))), the error bf16(w - W_hat); a w of zero
+// x (the 2^16 binade included), and saturation agrees.  With a row maximum of at least 1e-8 the
+// lower bracket alone decides (e5m2_word<true>); below it, a word with a pair whose codes differ
+// (an element within 2^-20 of a midpoint, exact ties among them) is redone by the exact rule, and
+// in both a word with a nonzero |w| at or below RU(s 2^-12) (x/2 in the hardware's subnormal
+// range, where the grids part) or a NaN is.  W_hat = bf16(fl32((x/2 code) (2s))), the error bf16(w - W_hat); a w of zero
 // gives W_hat +0 as the reference's codebook zero does.
 struct E5m2Row {
   uint64_t rlo2, rhi2, s2;   // r_lo / 2, r_hi / 2 and 2s, in both halves of a float32 pair
@@ -463,7 +464,12 @@ __device__ __forceinline__ E5m2Row e5m2_row(float s) {   // s: a positive normal
 }
 
 // 8 elements: W_hat words and the fp32 sum of the 8 exact squares; false if the word needs the
-// exact rule
+// exact rule.  LOWER: convert the lower bracket min(RZ(w r_lo / 2), RZ(w r_hi / 2)) alone, which
+// is the reference's point of fl32(w / s) for every element above the tiny bound, exact ties
+// included, when the row maximum is a bf16 of at least 1e-8 (tests/test_fast_rules.py checks it
+// for every bf16 w under every maximum of four binades and each of rcp.approx's results); only
+// tiny elements then need the exact rule.
+template <bool LOWER>
 __device__ __forceinline__ bool e5m2_word(const uint4& u, const E5m2Row& q, uint32_t (&o)[4], float& part) {
   const uint32_t v[4] = {u.x, u.y, u.z, u.w};
   uint32_t bad = 0u;
@@ -471,10 +477,15 @@ __device__ __forceinline__ bool e5m2_word(const uint4& u, const E5m2Row& q, uint
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
     const uint64_t w2 = f2_from_bf16x2(v[p]);
-    const uint32_t cl = cvt_e5m2x2(f2_mul_rz(w2, q.rlo2));
-    const uint32_t ch = cvt_e5m2x2(f2_mul_rz(w2, q.rhi2));
+    uint32_t cl;
+    if constexpr (LOWER) {
+      cl = cvt_e5m2x2(f2_min(f2_mul_rz(w2, q.rlo2), f2_mul_rz(w2, q.rhi2)));
+    } else {
+      cl = cvt_e5m2x2(f2_mul_rz(w2, q.rlo2));
+      bad |= cl ^ cvt_e5m2x2(f2_mul_rz(w2, q.rhi2));   // the two codes differ
+    }
     const uint32_t mag = v[p] & 0x7FFF7FFFu;
-    bad |= (cl ^ ch) | ((q.tiny2 - mag) & (mag + 0x7FFF7FFFu) & 0x80008000u);   // differ, or 0 < |w| <= RU
+    bad |= (q.tiny2 - mag) & (mag + 0x7FFF7FFFu) & 0x80008000u;   // 0 < |w| <= RU(s 2^-12)
     const uint32_t rec = f2_to_bf16x2(f2_mul_rn(f16x2_to_f2(__byte_perm(cl, 0u, 0x1404u)), q.s2));
     o[p] = rec & (prmt_sign_halves(mag + 0x7FFF7FFFu) | 0x7FFF7FFFu);   // -0 -> +0 where w = +-0
     acc = sq2_acc(bf16x2_sub(v[p], rec), acc);
@@ -725,7 +736,8 @@ __global__ void __launch_bounds__(256) xfmt2_kernel(const uint16_t* __restrict__
             uint32_t o[4];
             float part;
             bool fast;
-            if constexpr (KIND == XK_E5M2) fast = !has_nan8(u) && e5m2_word(u, qe, o, part);
+            if constexpr (KIND == XK_E5M2)
+              fast = !has_nan8(u) && (a >= 1e-8f ? e5m2_word<true>(u, qe, o, part) : e5m2_word<false>(u, qe, o, part));
             else fast = !has_nan8(u) && int_word(u, qi, o, part);
             if (fast) {
               if (MODE == MODE_QDQ)

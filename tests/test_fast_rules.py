@@ -416,11 +416,13 @@ def _e5m2_standard_mags():
 
 def test_fp8_e5m2_bracket_rule_matches_the_codebook_rule():
     """e5m2_word of the codebook kernel: for a row maximum a (every bf16 a in [1, 2), and binades
-    of 2^-30 and 2^40) and every finite bf16 w with |w| <= a, with r any of RN(1/s) and its two
-    neighbours (rcp.approx is within one ulp), the hardware conversions (round to nearest even,
-    saturating) of RZ(w r_lo / 2) and RZ(w r_hi / 2), where they agree and the word is not
-    flagged tiny, give the reference's W_hat bf16(q s) (nearest codebook point of fl32(w / s),
-    ties to the lower value, codebook exponent 31 finite)."""
+    of 2^-27 (from 1e-8 up), 2^39 and 2^97) and every finite bf16 w with |w| <= a, with r any of
+    RN(1/s) and its two neighbours (rcp.approx is within one ulp), the hardware conversions (round
+    to nearest even, saturating) of RZ(w r_lo / 2) and RZ(w r_hi / 2), where they agree and the
+    word is not flagged tiny, give the reference's W_hat bf16(q s) (nearest codebook point of
+    fl32(w / s), ties to the lower value, codebook exponent 31 finite); and the conversion of the
+    lower of the two alone gives it for every element that is not tiny (e5m2_word<true>, row
+    maxima of at least 1e-8)."""
     from oracle import pq_oracle as O
     mags = _e5m2_standard_mags()
     even = (np.arange(mags.size) % 2) == 0
@@ -429,8 +431,10 @@ def test_fp8_e5m2_bracket_rule_matches_the_codebook_rule():
     with np.errstate(invalid="ignore"):
         fin = b[np.isfinite((b << 16).view(F32))]
     checked = fast = 0
-    for base in (0x3F80, 0x3080, 0x53 << 8):
+    for base in (0x3F80, 0x3200, 0x53 << 8, 0x7000):
         for ab in range(base, base + 0x80, 3 if base != 0x3F80 else 1):
+            if ab < 0x322C:                                # below 1e-8: agree-or-exact only
+                continue
             a = (np.uint32(ab) << 16).view(F32)
             s = F32(max(a, F32(1e-8)) / F32(114688.0))
             wb = fin[(fin & 0x7FFF) <= ab]
@@ -454,6 +458,13 @@ def test_fp8_e5m2_bracket_rule_matches_the_codebook_rule():
                 got = np.where(rec == 0x8000, 0, rec)
                 bad = ok & (got != want)
                 assert not bad.any(), (hex(ab), wb[bad][:5], got[bad][:5], want[bad][:5])
+                # e5m2_word<true> (row maximum >= 1e-8): the lower bracket alone, every non-tiny w
+                cm = _rne(np.minimum(_rz32(w.astype(np.float64) * r_lo), _rz32(w.astype(np.float64) * r_hi)),
+                          mags, even, 57344.0)
+                low = O.f32_to_bf16_bits((cm * np.float64(F32(2.0) * s)).astype(F32))
+                low = np.where(low == 0x8000, 0, low)
+                bad = ~tiny & (mag > 0) & (low != want)
+                assert not bad.any(), ("lower", hex(ab), wb[bad][:5], low[bad][:5], want[bad][:5])
                 checked += int((mag > tiny_t).sum())
                 fast += int((ok & (mag > tiny_t)).sum())
     assert fast > 0.99 * checked                       # beside tiny elements, the exact rule is rare
